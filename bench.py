@@ -1,0 +1,388 @@
+#!/usr/bin/env python
+"""Benchmark of the ragged paged-attention decode path on B200.
+
+Workload (default): Llama-3.2-1B-shaped paged decode, bfloat16 -- 16 layers,
+32 query heads, 8 KV heads, head_dim 64, block size 16, 64 sequences with
+context lengths uniform in [512, 4096] (seed 0), Q/K/V ~ N(0, 1), block ids a
+seeded random permutation of the pool.  One step = one decode token for every
+sequence: pack the step on the GPU, then per layer append the new K/V and run
+paged attention.  Contexts grow by one token per step.  Every layer reads a
+different ~300 MB pool, larger than the 126 MB L2, so no flush is needed.
+
+With --gpus N (torchrun, one process per GPU) each rank holds 8/N KV heads
+(and the matching 32/N query heads) of a batch of 64*N sequences -- fixed
+work per GPU -- and the attention outputs are all-gathered over NCCL after
+every layer.
+
+Prints one JSON line (rank 0).  --impl reference times the CPU oracle (the
+reference's per-row algorithm restated) on the host cores instead.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+CFG = dict(name="llama3.2-1b-decode", layers=16, hq=32, hkv=8, d=64, bs=16, seqs=64, ctx_lo=512, ctx_hi=4096,
+           dtype="bf16", seed=0)
+METRIC = "paged-attn decode tok/s (1B shape, 16 layers)"
+
+
+def _args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=300)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--e2e-steps", type=int, default=50)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def _ctx_lens(n, seed):
+    rng = np.random.default_rng(seed)
+    return rng.integers(CFG["ctx_lo"], CFG["ctx_hi"] + 1, size=n).tolist()
+
+
+# ---------------------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.t.join(timeout=2)
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for nm, val in zip(names, parts[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def _peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+# ---------------------------------------------------------------------------- CPU baseline (oracle)
+class CpuOracleDecode:
+    """The reference algorithm on the host: per-row get -> append -> cat -> matmul -> softmax -> matmul.
+
+    One call of ``layer()`` is one layer of decode for the first ``n_sample``
+    sequences of the workload (grouped-query heads restated by repeating the
+    KV heads, as the reference has a single head count).  ``pos`` is held so
+    every call sees the same contexts.
+    """
+
+    def __init__(self, n_sample: int = 8, threads: int | None = None):
+        from oracle.paged import OracleStore
+
+        if threads:
+            torch.set_num_threads(threads)
+        self.n = n_sample
+        self.ctx = _ctx_lens(CFG["seqs"], CFG["seed"])[:n_sample]
+        H, D, bs = CFG["hkv"], CFG["d"], CFG["bs"]
+        st = OracleStore(2, max(self.ctx) + 64, H, D, batch_size=n_sample, dtype=torch.bfloat16,
+                         block_size=bs, prefix=False)
+        g = torch.Generator().manual_seed(1)
+        for s, c in enumerate(self.ctx):  # fill contexts block-wise (not timed)
+            st.tables[s].ensure(c)
+            kk = torch.randn(c, H, D, generator=g).to(torch.bfloat16)
+            vv = torch.randn(c, H, D, generator=g).to(torch.bfloat16)
+            for i, b in enumerate(st.tables[s].blocks):
+                n = min(bs, c - i * bs)
+                st.k[0][b, :n] = kk[i * bs: i * bs + n]
+                st.v[0][b, :n] = vv[i * bs: i * bs + n]
+            st.pos[s] = c
+        self.store = st
+        self.q = torch.randn(n_sample, 1, CFG["hq"] * D, generator=g).to(torch.bfloat16)
+        self.k = torch.randn(n_sample, 1, H * D, generator=g).to(torch.bfloat16)
+
+    def layer(self) -> float:
+        from oracle.attention import forward_with_cache
+
+        t0 = time.perf_counter()
+        forward_with_cache(self.store, 0, self.q, self.k, self.k, CFG["hq"])  # layer 0 of 2: pos held
+        return time.perf_counter() - t0
+
+    def describe(self, calls: int, seconds: float) -> str:
+        return (f"{self.n} of {CFG['seqs']} sequences (mean ctx {sum(self.ctx) / self.n:.0f}), one layer x "
+                f"{calls} calls in {seconds:.1f} s, scaled to {CFG['layers']} layers")
+
+    def rate(self, t_layer: float) -> float:
+        return self.n / (CFG["layers"] * t_layer)
+
+
+def cpu_decode_rate(seconds: float, threads: int | None = None):
+    cpu = CpuOracleDecode(threads=threads)
+    times = []
+    while sum(times) < seconds:
+        times.append(cpu.layer())
+    t = sum(times) / len(times)
+    return {"value": cpu.rate(t), "unit": "tok/s", "cores": torch.get_num_threads(),
+            "sample": cpu.describe(len(times), sum(times))}
+
+
+# ---------------------------------------------------------------------------- our arm
+def run_ours(args):
+    from nifre_b200 import Attention, PagedKVCache
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    if CFG["hkv"] % world:
+        raise SystemExit(f"--gpus {world} must divide {CFG['hkv']} KV heads")
+    L, D, bs = CFG["layers"], CFG["d"], CFG["bs"]
+    hkv, hq = CFG["hkv"] // world, CFG["hq"] // world
+    B = CFG["seqs"] * world
+    ctx = _ctx_lens(B, CFG["seed"])
+    steps_total = args.warmup + args.steps + args.e2e_steps + 2
+    max_seq = CFG["ctx_hi"] + steps_total + 16
+    dt = torch.bfloat16
+    cache = PagedKVCache(L, max_seq, hkv, D, device=dev, dtype=dt, block_size=bs, enable_prefix_cache=False)
+    cache.init_batch(B)
+    g = torch.Generator().manual_seed(CFG["seed"])
+    cache.block_allocator.set_free_order(torch.randperm(cache.num_blocks, generator=g).tolist())
+    # fill the contexts (N(0,1) keys and values) through the append path, layer by layer
+    T0 = sum(ctx)
+    plan = cache.plan(list(range(B)), ctx, np.cumsum([0] + ctx[:-1]).tolist())
+    gd = torch.Generator(device=dev).manual_seed(CFG["seed"] + rank)
+    kfill = torch.empty(T0, hkv * D, device=dev, dtype=dt)
+    vfill = torch.empty_like(kfill)
+    for layer in range(L):
+        kfill.normal_(generator=gd)
+        vfill.normal_(generator=gd)
+        cache.append_step(layer, kfill, vfill, plan)
+    del kfill, vfill
+    q_all = torch.randn(L, B, hq * D, device=dev, dtype=dt, generator=gd)
+    k_all = torch.randn(L, B, hkv * D, device=dev, dtype=dt, generator=gd)
+    v_all = torch.randn(L, B, hkv * D, device=dev, dtype=dt, generator=gd)
+    out_loc = torch.empty(L, B, hq * D, device=dev, dtype=dt)
+    gathered = torch.empty(world, B, hq * D, device=dev, dtype=dt) if world > 1 else None
+    slots, ones, rows = list(range(B)), [1] * B, list(range(B))
+    stream = torch.cuda.current_stream(dev)
+    att_events = []
+
+    def step(record=False):
+        p = cache.plan(slots, ones, rows)
+        for layer in range(L):
+            cache.append_step(layer, k_all[layer], v_all[layer], p)
+            if record:
+                e0 = torch.cuda.Event(enable_timing=True)
+                e1 = torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+            cache.attention_step(layer, q_all[layer], p, out_loc[layer])
+            if record:
+                e1.record(stream)
+                att_events.append((e0, e1, p))
+            if world > 1:
+                dist.all_gather_into_tensor(gathered, out_loc[layer])
+                # heads of rank r are query heads [r*hq, (r+1)*hq): (N, B, hq*D) -> (B, N*hq*D)
+                gathered.permute(1, 0, 2).reshape(B, world * hq * D)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    cache.check_status()
+    if world > 1:
+        dist.barrier()
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.25)
+    torch.cuda.synchronize()
+    e_start = torch.cuda.Event(enable_timing=True)
+    e_end = torch.cuda.Event(enable_timing=True)
+    e_start.record(stream)
+    for _ in range(args.steps):
+        step(record=True)
+    e_end.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = e_start.elapsed_time(e_end)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    cache.check_status()
+    # attention kernel: algorithmic bytes per launch / event duration
+    att_ms = [a.elapsed_time(b) for a, b, _ in att_events]
+    att_bytes = []
+    for _, _, p in att_events:
+        kv = int(p.kv_lens.sum())
+        nblk = int(((p.kv_lens + bs - 1) // bs).sum())
+        att_bytes.append(kv * hkv * D * 2 * 2 + 2 * B * hq * D * 2 + 4 * nblk + 16 * B)
+    att_avg_ms = sum(att_ms) / len(att_ms)
+    achieved = (sum(att_bytes) / len(att_bytes)) / (att_avg_ms * 1e-3) / 1e9
+    peak, peak_kind = _peaks()
+
+    # e2e through the public drop-in API with host buffers
+    e2e = None
+    if args.e2e_steps > 0:
+        attn = Attention(hq, D)
+        hq_host = torch.empty(L, B, 1, hq * D, dtype=dt).pin_memory()
+        hk_host = torch.empty(L, B, 1, hkv * D, dtype=dt).pin_memory()
+        hv_host = torch.empty_like(hk_host).pin_memory()
+        ho_host = torch.empty(L, B, 1, hq * D, dtype=dt).pin_memory()
+        hq_host.copy_(q_all.view(L, B, 1, -1).cpu())
+        hk_host.copy_(k_all.view(L, B, 1, -1).cpu())
+        hv_host.copy_(v_all.view(L, B, 1, -1).cpu())
+
+        def e2e_step():
+            for layer in range(L):
+                qd = hq_host[layer].to(dev, non_blocking=True)
+                kd = hk_host[layer].to(dev, non_blocking=True)
+                vd = hv_host[layer].to(dev, non_blocking=True)
+                o = attn(qd, kd, vd, kv_cache=cache, layer_id=layer, cache_batch_indices=slots)
+                if world > 1:
+                    dist.all_gather_into_tensor(gathered, o.view(B, -1))
+                    o = gathered.permute(1, 0, 2).reshape(B, 1, world * hq * D)
+                    ho_host[layer].copy_(o[:, :, : hq * D], non_blocking=True)
+                else:
+                    ho_host[layer].copy_(o, non_blocking=True)
+
+        e2e_step()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(args.e2e_steps - 1):
+            e2e_step()
+        b.record(stream)
+        torch.cuda.synchronize()
+        ems = a.elapsed_time(b)
+        if world > 1:
+            t = torch.tensor([ems], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ems = float(t.item())
+        cache.check_status()
+        n_e2e = args.e2e_steps - 1
+        e2e = {"value": B * n_e2e / (ems * 1e-3), "unit": "tok/s",
+               "h2d_bytes_per_step": L * B * (hq + 2 * hkv) * D * 2,
+               "d2h_bytes_per_step": L * B * hq * D * 2,
+               "ms_per_step": ems / n_e2e, "path": "nifre_b200.Attention.forward per layer, pinned host q/k/v"}
+
+    if rank == 0:
+        cpu = None
+        if not args.no_cpu_baseline:
+            cpu = cpu_decode_rate(12.0)
+            cpu["kind"] = "port"
+        line = {
+            "metric": METRIC, "value": B * args.steps / (ms * 1e-3), "unit": "tok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1) Q/K/V, random block permutation)",
+            "config": {"workload": CFG["name"], "layers": L, "q_heads": CFG["hq"], "kv_heads": CFG["hkv"],
+                       "head_dim": D, "block_size": bs, "seqs_per_gpu_x_heads": f"{B} seqs x {hkv} kv heads",
+                       "global_batch": B, "ctx": f"U[{CFG['ctx_lo']},{CFG['ctx_hi']}] + step",
+                       "parallelism": f"kv-head shard x{world}" if world > 1 else "single GPU",
+                       "l2": "inputs larger than L2 (each layer reads a distinct ~300 MB pool)"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": None, "kernel": "nf_paged_attention",
+                         "peak_source": peak_kind, "avg_launch_us": att_avg_ms * 1e3},
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "gpu_launches": args.steps * (1 + 2 * L),
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_reference(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    cpu = CpuOracleDecode(threads=threads)
+    for _ in range(args.warmup):
+        cpu.layer()
+    times = [cpu.layer() for _ in range(args.steps)]
+    v = cpu.rate(sum(times) / len(times))
+    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": CFG["name"], "layers": CFG["layers"], "q_heads": CFG["hq"],
+                       "kv_heads": CFG["hkv"], "head_dim": CFG["d"], "block_size": CFG["bs"]},
+            "cpu_baseline": {"value": v, "unit": "tok/s", "cores": torch.get_num_threads(), "kind": "port",
+                             "sample": cpu.describe(len(times), sum(times)) + "; each step = one such call"},
+            "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = _args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

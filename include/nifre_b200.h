@@ -1,0 +1,148 @@
+/*
+ * nifre_b200 -- C ABI of the B200 (sm_100a) ragged paged-attention path.
+ *
+ * Everything here is plain C: raw device pointers borrowed from the caller,
+ * sizes in elements unless a name says bytes, a CUDA stream passed as void*,
+ * int status returns (0 = ok) with the message of the last failure of the
+ * calling thread in nf_last_error().  The library allocates no device memory:
+ * every buffer, workspace included, belongs to the caller.
+ *
+ * Reference interfaces replaced (jyotilakra92/nifre, src/inference/):
+ *   nf_pack_step        -> the per-row host loops that build a step's batch:
+ *                          batching.py:8-19 (left padding + input_lens),
+ *                          model_runner.py:39-50,73-75 (chunk slicing, slots),
+ *                          gpt.py:108-126 (positions from kv_cache.pos),
+ *                          paged_kv_cache.py:107-121 (per-token resolve of the
+ *                          destination slot), block_table.py:36-40 (resolve).
+ *   nf_kv_append        -> PagedKVCache.append, paged_kv_cache.py:107-121
+ *                          (scatter of the new K/V rows; pos advance on the
+ *                          last layer, :120-121).
+ *   nf_paged_attention  -> Attention._forward_with_cache(_row),
+ *                          attention.py:77-142 (get -> cat -> q@k^T ->
+ *                          causal mask -> softmax(/sqrt(D)) -> @v), reading K/V
+ *                          in place from the block pool instead of the
+ *                          PagedKVCache.get gather, paged_kv_cache.py:123-142.
+ *
+ * Pool layout (unchanged from paged_kv_cache.py:72-85): per layer one K and
+ * one V tensor of shape (num_blocks, block_size, num_kv_heads, head_dim),
+ * row-major.  Token t of a sequence lives in row
+ *     slot = block_table[t / block_size] * block_size + t % block_size.
+ */
+#ifndef NIFRE_B200_H
+#define NIFRE_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* element types */
+#define NF_F32 0
+#define NF_F16 1
+#define NF_BF16 2
+
+/* return codes */
+#define NF_OK 0
+#define NF_EINVAL 1       /* bad argument (host-side check, nothing launched) */
+#define NF_ECUDA 2        /* a CUDA runtime call failed */
+#define NF_EUNSUPPORTED 3 /* shape/type combination without a kernel */
+
+/* bits of the device status word kernels may set (never a trap) */
+#define NF_STATUS_BAD_BLOCK 1   /* block id or logical block out of range: access skipped */
+#define NF_STATUS_UNIT_OVERFLOW 2 /* more work units than the caller's workspace holds */
+#define NF_STATUS_WAIT_TIMEOUT 4  /* a pipeline wait gave up after its time limit */
+#define NF_STATUS_BAD_SLOT 8    /* cache slot out of range: entry skipped */
+
+/* Record layouts (int32) of the step descriptor the host uploads. */
+#define NF_SEQ_FIELDS 4   /* slot, q_start (row of the first new token), q_len, ctx_before */
+#define NF_PATCH_FIELDS 3 /* slot, logical block index, physical block id */
+#define NF_ITEM_FIELDS 4  /* slot, q_row, kv_len, unit_base */
+#define NF_UNIT_FIELDS 2  /* item, split index */
+
+/* Message of the last failed call on this thread ("" if none). */
+const char* nf_last_error(void);
+
+/* ABI revision of this header; bumped on any signature change. */
+int nf_abi_version(void);
+
+/*
+ * nf_pack_step: expand one step's ragged batch on the device.
+ *
+ * seqs[n_seqs][4]      (device) slot, q_start, q_len, ctx_before of each
+ *                      sequence in the step, in the order the reference
+ *                      processes rows (prefill rows first, then decode rows).
+ * patches[n_patches][3](device) block-table writes applied first:
+ *                      block_tables[slot][logical] = physical.
+ * block_tables         (device, in/out) int32 [num_slots][max_blocks_per_seq].
+ * Outputs, one entry per new token t (n_tokens = sum of q_len):
+ *   slot_mapping[t]    destination pool row of token t,
+ *   src_rows[t]        row of token t in the caller's q/k/v tensors,
+ *   positions[t]       absolute position (int64, may be NULL),
+ *   items[t][4]        attention work item of the query at token t,
+ * and the split-K work list units[max_units][2] of key ranges of
+ * split_tokens keys; counts[0] = n_tokens, counts[1] = number of units.
+ */
+int nf_pack_step(const int32_t* seqs, int32_t n_seqs,
+                 const int32_t* patches, int32_t n_patches,
+                 int32_t* block_tables, int32_t num_slots, int32_t max_blocks_per_seq,
+                 int32_t block_size, int32_t num_blocks, int32_t split_tokens,
+                 int32_t* slot_mapping, int32_t* src_rows, int64_t* positions,
+                 int32_t* items, int32_t* units, int32_t* counts,
+                 int32_t n_tokens, int32_t max_units,
+                 int32_t* status, void* stream);
+
+/*
+ * nf_kv_append: pool[slot_mapping[t]] = new[src_rows[t]] for K and V.
+ * pool_rows = num_blocks * block_size (rows outside it are skipped and flagged).
+ * Each pool row holds num_kv_heads*head_dim elements of pool_dtype; source
+ * rows start every src_row_stride elements (so a head slice of a wider
+ * projection can be passed with an offset pointer).  Values are converted to
+ * the pool dtype with round-to-nearest-even, as torch's copy does.
+ * If pos_out (int64 [num_slots]) is not NULL the kernel also sets
+ * pos_out[slot] = ctx_before + q_len for each of the n_seqs records in seqs:
+ * the reference advances pos only on the last layer (paged_kv_cache.py:120-121).
+ */
+int nf_kv_append(void* k_pool, void* v_pool, int32_t pool_dtype, int64_t pool_rows,
+                 const void* k_new, const void* v_new, int32_t src_dtype,
+                 int64_t k_src_row_stride, int64_t v_src_row_stride,
+                 const int32_t* slot_mapping, const int32_t* src_rows, int32_t n_tokens,
+                 int32_t num_kv_heads, int32_t head_dim,
+                 const int32_t* seqs, int32_t n_seqs, int64_t* pos_out,
+                 int32_t* status, void* stream);
+
+/*
+ * nf_attention_workspace: sizes of the caller-owned split-K workspace for
+ * nf_paged_attention (float partials and int32 counters).  Counters must be
+ * zeroed once when allocated; the kernel leaves them zero when it returns.
+ */
+int nf_attention_workspace(int32_t max_units, int32_t max_items, int32_t num_q_heads,
+                           int32_t num_kv_heads, int32_t head_dim, int32_t dtype,
+                           int64_t* partial_floats, int64_t* counter_ints);
+
+/*
+ * nf_paged_attention: out[q_row] = softmax(q[q_row] k^T * scale) v over keys
+ * [0, kv_len) of the item's sequence, for every work item produced by
+ * nf_pack_step, with query head j reading KV head j / (num_q_heads/num_kv_heads).
+ * q/out rows hold num_q_heads*head_dim elements of `dtype` (the pool dtype);
+ * rows start every q_row_stride / out_row_stride elements.  Work is split
+ * into units of split_tokens keys; partial results go to ws_partials and are
+ * merged by the last unit of each item to finish (no extra launch).
+ */
+int nf_paged_attention(void* out, int64_t out_row_stride,
+                       const void* q, int64_t q_row_stride,
+                       const void* k_pool, const void* v_pool, int32_t dtype,
+                       int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                       int32_t block_size, int32_t num_blocks,
+                       const int32_t* block_tables, int32_t max_blocks_per_seq,
+                       const int32_t* items, const int32_t* units, const int32_t* counts,
+                       int32_t max_items, int32_t max_units, int32_t split_tokens, float scale,
+                       float* ws_partials, int64_t ws_partial_floats,
+                       int32_t* ws_counters, int64_t ws_counter_ints,
+                       int32_t* status, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NIFRE_B200_H */

@@ -1,0 +1,103 @@
+"""ctypes binding of ``libnifre_b200.so`` (the C ABI declared in include/nifre_b200.h).
+
+The library is built in-tree by ``nifre_b200.build``.  There is no fallback:
+if the shared object is missing or a CUDA device is absent, every entry point
+raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+import torch
+
+LIB_PATH = Path(__file__).resolve().parent / "libnifre_b200.so"
+
+NF_F32, NF_F16, NF_BF16 = 0, 1, 2
+NF_STATUS_BAD_BLOCK = 1
+NF_STATUS_UNIT_OVERFLOW = 2
+NF_STATUS_WAIT_TIMEOUT = 4
+NF_STATUS_BAD_SLOT = 8
+
+SEQ_FIELDS, PATCH_FIELDS, ITEM_FIELDS, UNIT_FIELDS = 4, 3, 4, 2
+
+_DTYPE_CODE = {torch.float32: NF_F32, torch.float16: NF_F16, torch.bfloat16: NF_BF16}
+
+EXPORTS = ("nf_last_error", "nf_abi_version", "nf_pack_step", "nf_kv_append",
+           "nf_attention_workspace", "nf_paged_attention")
+
+_P = ctypes.c_void_p
+_I32 = ctypes.c_int32
+_I64 = ctypes.c_int64
+
+_SIGNATURES = {
+    "nf_last_error": ([], ctypes.c_char_p),
+    "nf_abi_version": ([], ctypes.c_int),
+    "nf_pack_step": ([_P, _I32, _P, _I32, _P, _I32, _I32, _I32, _I32, _I32,
+                      _P, _P, _P, _P, _P, _P, _I32, _I32, _P, _P], ctypes.c_int),
+    "nf_kv_append": ([_P, _P, _I32, _I64, _P, _P, _I32, _I64, _I64, _P, _P, _I32,
+                      _I32, _I32, _P, _I32, _P, _P, _P], ctypes.c_int),
+    "nf_attention_workspace": ([_I32, _I32, _I32, _I32, _I32, _I32,
+                                ctypes.POINTER(_I64), ctypes.POINTER(_I64)], ctypes.c_int),
+    "nf_paged_attention": ([_P, _I64, _P, _I64, _P, _P, _I32, _I32, _I32, _I32, _I32, _I32,
+                            _P, _I32, _P, _P, _P, _I32, _I32, _I32, ctypes.c_float,
+                            _P, _I64, _P, _I64, _P, _P], ctypes.c_int),
+}
+
+
+class NifreError(RuntimeError):
+    """A C-ABI call of libnifre_b200 returned an error."""
+
+
+_lib = None
+
+
+def load() -> ctypes.CDLL:
+    """Load the shared library once; raise if it has not been built."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise NifreError(
+                f"{LIB_PATH.name} is missing: build it with `python -m nifre_b200.build` "
+                "(the CUDA path has no CPU fallback)")
+        lib = ctypes.CDLL(str(LIB_PATH))
+        for name, (args, res) in _SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.argtypes = args
+            fn.restype = res
+        _lib = lib
+    return _lib
+
+
+def check(rc: int, what: str) -> None:
+    if rc != 0:
+        msg = load().nf_last_error().decode(errors="replace")
+        raise NifreError(f"{what} failed (code {rc}): {msg}")
+
+
+def dtype_code(dtype: torch.dtype) -> int:
+    try:
+        return _DTYPE_CODE[dtype]
+    except KeyError as exc:
+        raise ValueError(f"unsupported dtype {dtype}") from exc
+
+
+def ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def stream_handle(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def require_cuda(t: torch.Tensor, name: str) -> None:
+    if not t.is_cuda:
+        raise NifreError(f"{name} must be a CUDA tensor: nifre_b200 has no CPU path")
+
+
+def workspace_sizes(max_units: int, max_items: int, hq: int, hkv: int, d: int, dtype: torch.dtype):
+    pf, ci = _I64(0), _I64(0)
+    check(load().nf_attention_workspace(max_units, max_items, hq, hkv, d, dtype_code(dtype),
+                                        ctypes.byref(pf), ctypes.byref(ci)), "nf_attention_workspace")
+    return pf.value, ci.value

@@ -1,0 +1,132 @@
+"""Model-agnostic attention over the B200 paged KV cache (drop-in for nifre's Attention).
+
+Same constructor and ``forward(q, k, v, kv_cache=None, layer_id=None,
+input_lens=None, cache_batch_indices=None)`` contract as jyotilakra92/nifre
+``src/inference/attention.py:16-152``:
+
+* ``q``/``k``/``v`` are projected ``(batch, seq, heads * head_dim)`` tensors;
+  ``k``/``v`` may carry fewer (KV) heads than ``q`` (grouped-query attention,
+  query head ``j`` reads KV head ``j // (Hq / Hkv)``);
+* with a cache, each row appends its new K/V and attends causally over
+  ``past + new`` with the query at absolute position ``past_len + i``
+  (``attention.py:77-152``); a left-padded prefill row uses its last
+  ``input_lens[i]`` tokens and its padding rows of the output stay zero
+  (``:79-93``); ``pos`` advances after the last layer;
+* without a cache it is full causal attention (``:59-75``);
+* a missing ``layer_id`` with a cache raises ValueError (``:45-46``).
+
+All rows of a call go through one ``nf_kv_append`` and one
+``nf_paged_attention`` launch; the batch metadata is packed once per forward
+(first layer) and reused by the other layers.  ``input_lens`` given as a CUDA
+tensor costs one device->host read per forward (the reference reads it with
+``.item()`` per row); pass a list or CPU tensor to avoid it.
+"""
+
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import torch
+from torch import nn
+
+from nifre_b200 import _lib
+from nifre_b200.paged_kv_cache import PagedKVCache
+
+
+class Attention(nn.Module):
+    def __init__(self, num_heads, head_dim, layer_id=None, dropout=0.0):
+        super().__init__()
+        self.num_heads = num_heads
+        self.head_dim = head_dim
+        self.d_out = num_heads * head_dim
+        self.layer_id = layer_id
+        self.dropout = nn.Dropout(dropout)
+
+    def forward(self, q, k, v, kv_cache=None, layer_id=None, input_lens=None, cache_batch_indices=None):
+        lid = layer_id if layer_id is not None else self.layer_id
+        if kv_cache is None:
+            return self._forward_full_causal(q, k, v)
+        if lid is None:
+            raise ValueError("layer_id is required when kv_cache is set")
+        if not isinstance(kv_cache, PagedKVCache):
+            raise TypeError("nifre_b200.Attention runs on nifre_b200.PagedKVCache (or KVCache)")
+        return self._forward_with_cache(q, k, v, kv_cache, lid, input_lens, cache_batch_indices)
+
+    # ------------------------------------------------------------------ cached path
+    def _forward_with_cache(self, q, k, v, cache: PagedKVCache, layer_id, input_lens, cache_batch_indices):
+        B, T, _ = q.shape
+        slots = list(range(B)) if cache_batch_indices is None else [int(s) for s in cache_batch_indices]
+        if input_lens is not None and T > 1:
+            lens = input_lens.tolist() if torch.is_tensor(input_lens) else [int(x) for x in input_lens]
+        else:
+            lens = [T] * B
+        key = (tuple(slots), tuple(lens), T)
+        plan = cache._plan
+        if plan is None or plan.key != key or plan.closed:
+            starts = [i * T + (T - n) for i, n in enumerate(lens)]
+            plan = cache.plan(slots, lens, starts)
+            plan.key = key
+        q2 = q.reshape(B * T, q.shape[-1])
+        k2 = k.reshape(B * T, k.shape[-1])
+        v2 = v.reshape(B * T, v.shape[-1])
+        if k2.stride(1) != 1:
+            k2 = k2.contiguous()
+        if v2.stride(1) != 1:
+            v2 = v2.contiguous()
+        qk = q2 if q2.dtype == cache.dtype and q2.stride(1) == 1 else q2.to(cache.dtype).contiguous()
+        out = torch.zeros((B * T, q.shape[-1]), dtype=cache.dtype, device=q.device)
+        cache.append_step(layer_id, k2, v2, plan)
+        cache.attention_step(layer_id, qk, plan, out, scale=1.0 / math.sqrt(self.head_dim))
+        return out.view(B, T, -1).to(q.dtype)
+
+    # ------------------------------------------------------------------ no-cache path
+    def _forward_full_causal(self, q, k, v):
+        """Full causal attention through the same kernels: each row's K/V is a one-block pool."""
+        return causal_attention(q, k, v, self.head_dim)
+
+
+def causal_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, head_dim: int) -> torch.Tensor:
+    """Causal attention over (B, T, H*D) tensors without a cache (attention.py:59-75).
+
+    Row b of ``k``/``v`` is used in place as block b of a pool whose block
+    size is T, with the identity block table; every query i of row b is a
+    work item over keys [0, i].
+    """
+    _lib.require_cuda(q, "q")
+    B, T, hqd = q.shape
+    dtype = q.dtype
+    k = k.to(dtype).contiguous()
+    v = v.to(dtype).contiguous()
+    q = q.contiguous()
+    hkv = k.shape[-1] // head_dim
+    hq = hqd // head_dim
+    dev = q.device
+    n_tok = B * T
+    split = 128 * max(1, math.ceil(T / 128))
+    max_units = n_tok  # one unit per query: kv_len <= T <= split
+    seqs = np.stack([np.arange(B), np.arange(B) * T, np.full(B, T), np.zeros(B)], 1).astype(np.int32)
+    seqs_d = torch.from_numpy(seqs.reshape(-1)).to(dev)
+    bt = torch.arange(B, dtype=torch.int32, device=dev).view(B, 1)
+    slot_mapping = torch.empty(n_tok, dtype=torch.int32, device=dev)
+    src_rows = torch.empty_like(slot_mapping)
+    items = torch.empty(4 * n_tok, dtype=torch.int32, device=dev)
+    units = torch.empty(2 * max_units, dtype=torch.int32, device=dev)
+    counts = torch.empty(2, dtype=torch.int32, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    stream = _lib.stream_handle(dev)
+    lib = _lib.load()
+    _lib.check(lib.nf_pack_step(seqs_d.data_ptr(), B, None, 0, bt.data_ptr(), B, 1, T, B, split,
+                                slot_mapping.data_ptr(), src_rows.data_ptr(), None, items.data_ptr(),
+                                units.data_ptr(), counts.data_ptr(), n_tok, max_units, status.data_ptr(),
+                                stream), "nf_pack_step")
+    pf, ci = _lib.workspace_sizes(max_units, n_tok, hq, hkv, head_dim, dtype)
+    ws = torch.empty(max(pf, 1), dtype=torch.float32, device=dev)
+    cnt = torch.zeros(max(ci, 1), dtype=torch.int32, device=dev)
+    out = torch.empty_like(q)
+    _lib.check(lib.nf_paged_attention(
+        out.data_ptr(), hqd, q.data_ptr(), hqd, k.data_ptr(), v.data_ptr(), _lib.dtype_code(dtype),
+        hq, hkv, head_dim, T, B, bt.data_ptr(), 1, items.data_ptr(), units.data_ptr(), counts.data_ptr(),
+        n_tok, max_units, split, 1.0 / math.sqrt(head_dim), ws.data_ptr(), ws.numel(), cnt.data_ptr(),
+        cnt.numel(), status.data_ptr(), stream), "nf_paged_attention")
+    return out

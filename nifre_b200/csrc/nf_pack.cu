@@ -1,0 +1,194 @@
+// GPU-side packing of one step's ragged batch.
+//
+// Replaces the per-row / per-token host loops of the reference step
+// (jyotilakra92/nifre src/inference/): batching.py:8-19 (left padding),
+// model_runner.py:39-50,73-75 (chunk slicing and slot lists),
+// models/gpt.py:108-126 (positions read back from kv_cache.pos),
+// paged_kv_cache.py:107-121 + block_table.py:36-40 (per-token resolve).
+// One CTA does the whole step: a step holds at most a few thousand tokens
+// (the reference token budget is 2048 by default, 4096 at most in the
+// auto-tuner's range), which one CTA scans in a few microseconds, and a
+// single launch keeps the per-step host work to one upload.
+#include "nf_common.cuh"
+#include "nf_internal.h"
+
+namespace nf {
+
+struct PackParams {
+  const int* seqs;
+  int n_seqs;
+  const int* patches;
+  int n_patches;
+  int* bt;
+  int num_slots, max_blocks, bs, num_blocks, split;
+  int* slot_mapping;
+  int* src_rows;
+  long long* positions;
+  int* items;
+  int* units;
+  int* counts;
+  int n_tokens, max_units;
+  int* status;
+};
+
+constexpr int kPackThreads = 1024;
+
+// Exclusive scan, in place, of a[i * stride] for i < n by one CTA.
+// Returns the total to every thread.
+__device__ int cta_exclusive_scan(int* a, int n, int stride) {
+  __shared__ int warp_tot[32];
+  __shared__ int carry_sh;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (tid == 0) carry_sh = 0;
+  __syncthreads();
+  for (int base = 0; base < n; base += kPackThreads) {
+    const int i = base + tid;
+    const int x = (i < n) ? a[(long long)i * stride] : 0;
+    int incl = x;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      int y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    if (lane == 31) warp_tot[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+      int w = warp_tot[lane];
+      int wi = w;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        int y = __shfl_up_sync(0xffffffffu, wi, o);
+        if (lane >= o) wi += y;
+      }
+      warp_tot[lane] = wi - w;  // exclusive prefix of warp totals
+    }
+    __syncthreads();
+    const int carry = carry_sh;
+    const int excl = carry + warp_tot[warp] + incl - x;
+    if (i < n) a[(long long)i * stride] = excl;
+    __syncthreads();
+    if (tid == kPackThreads - 1) carry_sh = excl + x;
+    __syncthreads();
+  }
+  return carry_sh;
+}
+
+__global__ void __launch_bounds__(kPackThreads) pack_kernel(const PackParams p) {
+  extern __shared__ int cu[];  // n_seqs + 1 query offsets
+  const int tid = threadIdx.x;
+
+  // 1. block-table writes recorded by the host allocator for this step.
+  for (int i = tid; i < p.n_patches; i += kPackThreads) {
+    const int slot = p.patches[3 * i], lb = p.patches[3 * i + 1], phys = p.patches[3 * i + 2];
+    if (slot < 0 || slot >= p.num_slots || lb < 0 || lb >= p.max_blocks || phys < 0 || phys >= p.num_blocks) {
+      atomicOr(p.status, NF_STATUS_BAD_BLOCK);
+      continue;
+    }
+    p.bt[(long long)slot * p.max_blocks + lb] = phys;
+  }
+  // 2. query offsets: scan of q_len.
+  for (int s = tid; s < p.n_seqs; s += kPackThreads) cu[s] = p.seqs[4 * s + 2];
+  __syncthreads();
+  const int total = cta_exclusive_scan(cu, p.n_seqs, 1);
+  if (tid == 0) cu[p.n_seqs] = total;
+  __syncthreads();
+  const int T = min(total, p.n_tokens);
+  if (total != p.n_tokens && tid == 0) atomicOr(p.status, NF_STATUS_UNIT_OVERFLOW);
+
+  // 3. per-token expansion: slot mapping, source row, position, work item.
+  for (int t = tid; t < T; t += kPackThreads) {
+    int lo = 0, hi = p.n_seqs - 1;  // last s with cu[s] <= t
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (cu[mid] <= t) lo = mid; else hi = mid - 1;
+    }
+    const int s = lo, i = t - cu[s];
+    int slot = p.seqs[4 * s];
+    const int q_start = p.seqs[4 * s + 1], ctx_before = p.seqs[4 * s + 3];
+    if (slot < 0 || slot >= p.num_slots) {
+      atomicOr(p.status, NF_STATUS_BAD_SLOT);
+      slot = 0;
+    }
+    const int pos = ctx_before + i;
+    const int lb = pos / p.bs;
+    int phys = (lb < p.max_blocks) ? p.bt[(long long)slot * p.max_blocks + lb] : -1;
+    if (phys < 0 || phys >= p.num_blocks) {
+      atomicOr(p.status, NF_STATUS_BAD_BLOCK);
+      phys = 0;
+    }
+    p.slot_mapping[t] = phys * p.bs + pos % p.bs;
+    p.src_rows[t] = q_start + i;
+    if (p.positions) p.positions[t] = pos;
+    const int kv_len = pos + 1;  // query at pos sees keys 0..pos (attention.py:144-152)
+    int4 it;
+    it.x = slot;
+    it.y = q_start + i;
+    it.z = kv_len;
+    it.w = (kv_len + p.split - 1) / p.split;  // number of splits; scanned below
+    reinterpret_cast<int4*>(p.items)[t] = it;
+  }
+  __syncthreads();
+  // 4. unit base of each item: scan of the split counts.
+  const int n_units = cta_exclusive_scan(p.items + 3, T, 4);
+  // 5. the unit list, one (item, split) per key range.
+  for (int t = tid; t < T; t += kPackThreads) {
+    const int4 it = reinterpret_cast<const int4*>(p.items)[t];
+    const int n = (it.z + p.split - 1) / p.split;
+    for (int j = 0; j < n; ++j) {
+      const int u = it.w + j;
+      if (u < p.max_units) {
+        p.units[2 * u] = t;
+        p.units[2 * u + 1] = j;
+      }
+    }
+  }
+  if (tid == 0) {
+    if (n_units > p.max_units) atomicOr(p.status, NF_STATUS_UNIT_OVERFLOW);
+    p.counts[0] = T;
+    p.counts[1] = min(n_units, p.max_units);
+  }
+}
+
+}  // namespace nf
+
+extern "C" int nf_pack_step(const int32_t* seqs, int32_t n_seqs, const int32_t* patches, int32_t n_patches,
+                            int32_t* block_tables, int32_t num_slots, int32_t max_blocks_per_seq,
+                            int32_t block_size, int32_t num_blocks, int32_t split_tokens,
+                            int32_t* slot_mapping, int32_t* src_rows, int64_t* positions, int32_t* items,
+                            int32_t* units, int32_t* counts, int32_t n_tokens, int32_t max_units,
+                            int32_t* status, void* stream) {
+  using namespace nf;
+  if (n_seqs <= 0 || n_tokens <= 0) return fail(NF_EINVAL, "nf_pack_step: empty step (n_seqs=%d, n_tokens=%d)", n_seqs, n_tokens);
+  if (!seqs || !block_tables || !slot_mapping || !src_rows || !items || !units || !counts || !status)
+    return fail(NF_EINVAL, "nf_pack_step: null pointer argument");
+  if (n_patches > 0 && !patches) return fail(NF_EINVAL, "nf_pack_step: patches is null");
+  if (block_size <= 0 || split_tokens <= 0 || num_slots <= 0 || max_blocks_per_seq <= 0 || num_blocks <= 0)
+    return fail(NF_EINVAL, "nf_pack_step: sizes must be positive");
+  if (max_units <= 0) return fail(NF_EINVAL, "nf_pack_step: max_units must be positive");
+  if ((reinterpret_cast<uintptr_t>(items) & 15) != 0) return fail(NF_EINVAL, "nf_pack_step: items must be 16-byte aligned");
+  const size_t smem = sizeof(int) * (size_t)(n_seqs + 1);
+  if (smem > 200 * 1024) return fail(NF_EINVAL, "nf_pack_step: too many sequences (%d)", n_seqs);
+  if (smem > 48 * 1024) cudaFuncSetAttribute(pack_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  PackParams p;
+  p.seqs = seqs;
+  p.n_seqs = n_seqs;
+  p.patches = patches;
+  p.n_patches = n_patches;
+  p.bt = block_tables;
+  p.num_slots = num_slots;
+  p.max_blocks = max_blocks_per_seq;
+  p.bs = block_size;
+  p.num_blocks = num_blocks;
+  p.split = split_tokens;
+  p.slot_mapping = slot_mapping;
+  p.src_rows = src_rows;
+  p.positions = reinterpret_cast<long long*>(positions);
+  p.items = items;
+  p.units = units;
+  p.counts = counts;
+  p.n_tokens = n_tokens;
+  p.max_units = max_units;
+  p.status = status;
+  pack_kernel<<<1, kPackThreads, smem, static_cast<cudaStream_t>(stream)>>>(p);
+  return check_launch("nf_pack_step");
+}

@@ -1,0 +1,377 @@
+"""Paged KV cache on B200 HBM (drop-in for nifre's PagedKVCache).
+
+Public API and attributes follow jyotilakra92/nifre
+``src/inference/paged_kv_cache.py:8-169`` (``init_batch``, ``append``, ``get``,
+``length``, ``lengths``, ``reset_slot``, ``free``, ``try_load_prefix``,
+``register_prefix``, ``pos``, ``k``, ``v``, ``block_tables``,
+``block_allocator``, ``prefix_cache``, ``num_blocks`` ...), so the engine, the
+model runner and the observability probe keep working unchanged.  The pools
+keep the reference layout ``(num_blocks, block_size, n_heads, head_dim)`` per
+layer, with ``n_heads`` the number of KV heads stored (grouped-query models
+store fewer KV heads than they have query heads).
+
+What changes is where the work happens:
+
+* block allocation stays on the host (``BlockAllocator``/``BlockTable``, same
+  ids as the reference), but a step's allocations are collected into a
+  *step plan*: one int32 upload (sequence records + block-table patches) and
+  one ``nf_pack_step`` launch compute every token's destination row, source
+  row, position and the split-K work list on the GPU;
+* ``append`` is one ``nf_kv_append`` launch for all sequences of the step;
+* attention reads K/V in place from the pools (``nf_paged_attention``); the
+  ``get`` gather is kept for API compatibility only.
+
+``pos`` stays a device int64 tensor like the reference; a host copy drives
+planning so no step ever reads it back.  As in the reference, ``pos``
+advances only when the last layer of a step has appended
+(``paged_kv_cache.py:120-121``).
+"""
+
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import torch
+
+from nifre_b200 import _lib
+from nifre_b200.block_allocator import BlockAllocator
+from nifre_b200.block_table import BlockTable
+from nifre_b200.prefix_cache import PrefixCache
+
+
+class _DeviceBuffer:
+    """Grow-only device buffer reused across steps (stream-ordered reuse)."""
+
+    def __init__(self, dtype: torch.dtype, device, zero: bool = False):
+        self.dtype, self.device, self.zero = dtype, device, zero
+        self.t: torch.Tensor | None = None
+
+    def get(self, n: int) -> torch.Tensor:
+        if self.t is None or self.t.numel() < n:
+            cap = max(n, int((self.t.numel() if self.t is not None else 0) * 1.5), 64)
+            alloc = torch.zeros if self.zero else torch.empty
+            self.t = alloc(cap, dtype=self.dtype, device=self.device)
+        return self.t
+
+
+class StepPlan:
+    """Device metadata of one forward pass over a ragged batch.
+
+    Valid for every layer of that forward; ``PagedKVCache`` closes it when the
+    last layer has appended.
+    """
+
+    def __init__(self, slots, q_lens, q_starts, ctx_before, split, max_units):
+        self.slots = slots
+        self.q_lens = q_lens
+        self.q_starts = q_starts
+        self.ctx_before = ctx_before
+        self.n_seqs = len(slots)
+        self.n_tokens = int(q_lens.sum())
+        self.rows_needed = int((q_starts + q_lens).max())
+        self.split = split
+        self.max_units = max_units
+        self.key = None
+        self.closed = False
+        # device views, filled by PagedKVCache.plan
+        self.seqs = self.slot_mapping = self.src_rows = self.items = self.units = self.counts = None
+        self.positions = None
+
+    @property
+    def kv_lens(self) -> np.ndarray:
+        return self.ctx_before + self.q_lens
+
+
+class PagedKVCache:
+    def __init__(self, num_layers: int, max_seq_len: int, n_heads: int, head_dim: int,
+                 device="cuda", dtype: torch.dtype = torch.float16, block_size: int = 16,
+                 enable_prefix_cache: bool = True, prefix_cache_max_entries: int = 1024,
+                 num_blocks: int | None = None) -> None:
+        if block_size <= 0:
+            raise ValueError(f"block_size must be positive, got {block_size}")
+        self.num_layers = num_layers
+        self.max_seq_len = max_seq_len
+        self.n_heads = n_heads
+        self.head_dim = head_dim
+        self.device = torch.device(device)
+        self.dtype = dtype
+        self.block_size = block_size
+        self.enable_prefix_cache = enable_prefix_cache
+        self.prefix_cache_max_entries = prefix_cache_max_entries
+        self._num_blocks_override = num_blocks
+        self.batch_size = 0
+        self.num_blocks = 0
+        self.pos = None
+        self.k = None
+        self.v = None
+        self.block_allocator: BlockAllocator | None = None
+        self.block_tables: list[BlockTable] = []
+        self.prefix_cache: PrefixCache | None = None
+        self._plan: StepPlan | None = None
+
+    # ------------------------------------------------------------------ setup
+    def init_batch(self, batch_size: int) -> None:
+        _lib.load()
+        if self.device.type != "cuda":
+            raise _lib.NifreError("PagedKVCache needs a CUDA device: nifre_b200 has no CPU path")
+        self.batch_size = batch_size
+        self.pos = torch.zeros(batch_size, dtype=torch.long, device=self.device)
+        self.pos_host = np.zeros(batch_size, dtype=np.int64)
+        self.max_blocks_per_seq = (self.max_seq_len + self.block_size - 1) // self.block_size
+        self.num_blocks = (self._num_blocks_override if self._num_blocks_override is not None
+                           else self.max_blocks_per_seq * batch_size)
+        self.block_allocator = BlockAllocator(self.num_blocks)
+        self.block_tables = [BlockTable(self.block_allocator, self.block_size) for _ in range(batch_size)]
+        self.prefix_cache = (PrefixCache(self.block_allocator, self.block_size,
+                                         max_entries=self.prefix_cache_max_entries)
+                             if self.enable_prefix_cache else None)
+        shape = (self.num_layers, self.num_blocks, self.block_size, self.n_heads, self.head_dim)
+        self._k_all = torch.empty(shape, device=self.device, dtype=self.dtype)
+        self._v_all = torch.empty(shape, device=self.device, dtype=self.dtype)
+        self.k = list(self._k_all.unbind(0))
+        self.v = list(self._v_all.unbind(0))
+        self.bt_dev = torch.zeros((batch_size, self.max_blocks_per_seq), dtype=torch.int32, device=self.device)
+        self._synced = [(-1, 0)] * batch_size  # (table epoch, entries mirrored on the device)
+        self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self._meta = _DeviceBuffer(torch.int32, self.device)
+        self._pos_buf = _DeviceBuffer(torch.int64, self.device)
+        self._ws_partials = _DeviceBuffer(torch.float32, self.device)
+        self._ws_counters = _DeviceBuffer(torch.int32, self.device, zero=True)
+        self._plan = None
+
+    def free(self) -> None:
+        self.batch_size = 0
+        self.num_blocks = 0
+        self.pos = None
+        self.k = None
+        self.v = None
+        self.block_allocator = None
+        self.block_tables = []
+        self.prefix_cache = None
+        self._plan = None
+        self._k_all = self._v_all = None
+
+    # ------------------------------------------------------------------ reference API
+    def try_load_prefix(self, batch_idx: int, token_ids: list[int]) -> int:
+        if self.prefix_cache is None:
+            return 0
+        num_tokens, blocks = self.prefix_cache.lookup(token_ids)
+        if num_tokens == 0:
+            return 0
+        self.block_tables[batch_idx].import_blocks(blocks)
+        self._set_pos(batch_idx, num_tokens)
+        return num_tokens
+
+    def register_prefix(self, batch_idx: int, token_ids: list[int]) -> None:
+        if self.prefix_cache is None:
+            return
+        self.prefix_cache.insert(token_ids, self.block_tables[batch_idx].physical_blocks())
+
+    def append(self, batch_idx: int, layer_id: int, key: torch.Tensor, value: torch.Tensor) -> None:
+        """Append ``key``/``value`` (n, H, D) of one sequence (reference per-row API)."""
+        n = key.shape[0]
+        plan = self.plan([batch_idx], [n], [0])
+        self.append_step(layer_id, key.reshape(n, -1), value.reshape(n, -1), plan)
+
+    def get(self, batch_idx: int, layer_id: int) -> tuple[torch.Tensor, torch.Tensor]:
+        pos = int(self.pos_host[batch_idx])
+        if pos == 0:
+            empty = torch.empty(0, self.n_heads, self.head_dim, device=self.device, dtype=self.dtype)
+            return empty, empty.clone()
+        nb = (pos + self.block_size - 1) // self.block_size
+        idx = torch.tensor(self.block_tables[batch_idx].physical_blocks()[:nb], device=self.device)
+        k = self.k[layer_id].index_select(0, idx).reshape(-1, self.n_heads, self.head_dim)[:pos]
+        v = self.v[layer_id].index_select(0, idx).reshape(-1, self.n_heads, self.head_dim)[:pos]
+        return k, v
+
+    def length(self, batch_idx: int) -> int:
+        return int(self.pos_host[batch_idx])
+
+    def lengths(self) -> torch.Tensor:
+        return self.pos.clone()
+
+    def reset_slot(self, batch_idx: int) -> None:
+        self.block_tables[batch_idx].clear()
+        self._set_pos(batch_idx, 0)
+
+    @property
+    def allocated_blocks(self) -> int:
+        return 0 if self.block_allocator is None else self.block_allocator.allocated_count
+
+    def _set_pos(self, slot: int, value: int) -> None:
+        self.pos_host[slot] = value
+        self.pos[slot] = value
+
+    # ------------------------------------------------------------------ step planning
+    def split_for(self, total_keys: int, units_per_sm: int = 4) -> int:
+        """Keys per split-K unit: ~units_per_sm units per SM, a multiple of 128."""
+        sms = torch.cuda.get_device_properties(self.device).multi_processor_count
+        s = total_keys / max(1, units_per_sm * sms)
+        return max(128, int(math.ceil(s / 128.0)) * 128)
+
+    def plan(self, slots, q_lens, q_starts, split: int | None = None) -> StepPlan:
+        """Allocate blocks for a step and pack its metadata on the GPU.
+
+        ``slots[i]`` gets ``q_lens[i]`` new tokens whose rows in the caller's
+        q/k/v tensors start at ``q_starts[i]``.  Allocation happens in list
+        order, like the reference's row loop (paged_kv_cache.py:110-111).
+        Raises before any launch on an over-long sequence or an exhausted pool.
+        """
+        slots = np.asarray(slots, dtype=np.int64)
+        q_lens = np.asarray(q_lens, dtype=np.int64)
+        q_starts = np.asarray(q_starts, dtype=np.int64)
+        if slots.size == 0:
+            raise ValueError("a step needs at least one sequence")
+        if (q_lens <= 0).any():
+            raise ValueError("every sequence of a step needs at least one new token")
+        if len(q_lens) != len(slots) or len(q_starts) != len(slots):
+            raise ValueError("slots, q_lens and q_starts must have the same length")
+        if (q_starts < 0).any():
+            raise ValueError("q_starts must be non-negative")
+        if slots.min() < 0 or slots.max() >= self.batch_size:
+            raise IndexError(f"cache slot out of range [0, {self.batch_size})")
+        if len(np.unique(slots)) != len(slots):
+            raise ValueError("a slot may appear only once per step")
+        ctx = self.pos_host[slots]
+        over = ctx + q_lens > self.max_seq_len
+        if over.any():
+            i = int(np.argmax(over))
+            raise AssertionError(
+                f"slot {int(slots[i])}: {int(ctx[i])} + {int(q_lens[i])} tokens exceed max_seq_len {self.max_seq_len}")
+        for s, c, n in zip(slots.tolist(), ctx.tolist(), q_lens.tolist()):
+            self.block_tables[s].ensure_capacity(c + n)
+        patches = []
+        for s in slots.tolist():
+            tab = self.block_tables[s]
+            epoch, done = self._synced[s]
+            if epoch != tab.epoch:
+                done = 0
+            blocks = tab._physical_blocks
+            if len(blocks) > done:
+                for lb in range(done, len(blocks)):
+                    patches.append((s, lb, blocks[lb]))
+            self._synced[s] = (tab.epoch, len(blocks))
+        S, P = len(slots), len(patches)
+        T = int(q_lens.sum())
+        # every query token is one work item attending over keys [0, ctx + i]
+        kv = np.repeat(ctx + 1, q_lens) + (np.arange(T) - np.repeat(np.cumsum(q_lens) - q_lens, q_lens))
+        if split is None:
+            split = self.split_for(int(kv.sum()))
+        max_units = int(((kv + split - 1) // split).sum())
+
+        host = np.empty(S * 4 + P * 3, dtype=np.int32)
+        host[: S * 4] = np.stack([slots, q_starts, q_lens, ctx], axis=1).reshape(-1)
+        if P:
+            host[S * 4:] = np.asarray(patches, dtype=np.int32).reshape(-1)
+        off_slot = _align4(S * 4 + P * 3)
+        off_src = off_slot + T
+        off_items = _align4(off_src + T)
+        off_units = off_items + 4 * T
+        off_counts = off_units + 2 * max_units
+        meta = self._meta.get(off_counts + 4)
+        meta[: host.size].copy_(torch.from_numpy(host).pin_memory(), non_blocking=True)
+        pos_dev = self._pos_buf.get(T)
+
+        plan = StepPlan(slots, q_lens, q_starts, ctx, split, max_units)
+        plan.seqs = meta[: S * 4]
+        plan.slot_mapping = meta[off_slot: off_slot + T]
+        plan.src_rows = meta[off_src: off_src + T]
+        plan.items = meta[off_items: off_items + 4 * T]
+        plan.units = meta[off_units: off_units + 2 * max_units]
+        plan.counts = meta[off_counts: off_counts + 2]
+        plan.positions = pos_dev[:T]
+        lib = _lib.load()
+        _lib.check(lib.nf_pack_step(
+            meta.data_ptr(), S, meta.data_ptr() + 4 * S * 4 if P else None, P,
+            self.bt_dev.data_ptr(), self.batch_size, self.max_blocks_per_seq, self.block_size,
+            self.num_blocks, split, plan.slot_mapping.data_ptr(), plan.src_rows.data_ptr(),
+            plan.positions.data_ptr(), plan.items.data_ptr(), plan.units.data_ptr(), plan.counts.data_ptr(),
+            T, max_units, self.status.data_ptr(), _lib.stream_handle(self.device)), "nf_pack_step")
+        self._plan = plan
+        return plan
+
+    def _close(self, plan: StepPlan) -> None:
+        self.pos_host[plan.slots] = plan.ctx_before + plan.q_lens
+        plan.closed = True
+        if self._plan is plan:
+            self._plan = None
+
+    # ------------------------------------------------------------------ per-layer kernels
+    def append_step(self, layer_id: int, key: torch.Tensor, value: torch.Tensor, plan: StepPlan) -> None:
+        """Scatter the step's new K/V rows (rows of ``key``/``value``: n_rows x H*D) into layer ``layer_id``."""
+        if plan.closed:
+            raise RuntimeError("step plan already closed")
+        _lib.require_cuda(key, "key")
+        for name, t in (("key", key), ("value", value)):
+            if t.dim() != 2 or t.shape[1] != self.n_heads * self.head_dim or t.stride(1) != 1:
+                raise ValueError(f"{name} must be (rows, {self.n_heads * self.head_dim}) with unit column stride")
+        if key.shape[0] < plan.rows_needed or value.shape[0] < plan.rows_needed:
+            raise ValueError(f"key/value have {key.shape[0]} rows, the step uses rows up to {plan.rows_needed}")
+        if not 0 <= layer_id < self.num_layers:
+            raise IndexError(f"layer_id {layer_id} out of range [0, {self.num_layers})")
+        last = layer_id == self.num_layers - 1
+        lib = _lib.load()
+        _lib.check(lib.nf_kv_append(
+            self.k[layer_id].data_ptr(), self.v[layer_id].data_ptr(), _lib.dtype_code(self.dtype),
+            self.num_blocks * self.block_size, key.data_ptr(), value.data_ptr(), _lib.dtype_code(key.dtype),
+            key.stride(0), value.stride(0), plan.slot_mapping.data_ptr(), plan.src_rows.data_ptr(),
+            plan.n_tokens, self.n_heads, self.head_dim, plan.seqs.data_ptr(), plan.n_seqs,
+            self.pos.data_ptr() if last else None, self.status.data_ptr(),
+            _lib.stream_handle(self.device)), "nf_kv_append")
+        if last:
+            self._close(plan)
+
+    def attention_step(self, layer_id: int, q: torch.Tensor, plan: StepPlan, out: torch.Tensor,
+                       scale: float | None = None) -> torch.Tensor:
+        """out[row] = attention of q[row] over the cached keys of its sequence, for the step's rows.
+
+        ``q``/``out``: (rows, Hq*D) in the pool dtype with unit column stride.
+        Rows not in the step are left untouched.
+        """
+        _lib.require_cuda(q, "q")
+        D = self.head_dim
+        if q.dim() != 2 or q.shape[1] % (self.n_heads * D) != 0 or q.stride(1) != 1:
+            raise ValueError(f"q must be (rows, Hq*{D}) with Hq a multiple of {self.n_heads}")
+        if out.shape != q.shape or out.stride(1) != 1:
+            raise ValueError("out must have q's shape")
+        if q.dtype != self.dtype or out.dtype != self.dtype:
+            raise ValueError(f"q/out dtype must be the cache dtype {self.dtype}")
+        if q.shape[0] < plan.rows_needed:
+            raise ValueError(f"q has {q.shape[0]} rows, the step uses rows up to {plan.rows_needed}")
+        if not 0 <= layer_id < self.num_layers:
+            raise IndexError(f"layer_id {layer_id} out of range [0, {self.num_layers})")
+        hq = q.shape[1] // D
+        max_items = plan.n_tokens
+        pf, ci = _lib.workspace_sizes(plan.max_units, max_items, hq, self.n_heads, D, self.dtype)
+        ws = self._ws_partials.get(pf)
+        cnt = self._ws_counters.get(ci)
+        if scale is None:
+            scale = 1.0 / math.sqrt(D)
+        lib = _lib.load()
+        _lib.check(lib.nf_paged_attention(
+            out.data_ptr(), out.stride(0), q.data_ptr(), q.stride(0),
+            self.k[layer_id].data_ptr(), self.v[layer_id].data_ptr(), _lib.dtype_code(self.dtype),
+            hq, self.n_heads, D, self.block_size, self.num_blocks, self.bt_dev.data_ptr(),
+            self.max_blocks_per_seq, plan.items.data_ptr(), plan.units.data_ptr(), plan.counts.data_ptr(),
+            max_items, plan.max_units, plan.split, float(scale), ws.data_ptr(), ws.numel(),
+            cnt.data_ptr(), cnt.numel(), self.status.data_ptr(), _lib.stream_handle(self.device)),
+            "nf_paged_attention")
+        return out
+
+    # ------------------------------------------------------------------ diagnostics
+    def check_status(self) -> None:
+        """Raise if any kernel flagged a problem (reads the device status word: synchronises)."""
+        st = int(self.status.item())
+        if st:
+            self.status.zero_()
+            raise _lib.NifreError(f"device status {st:#x} (bad block={st & 1}, unit overflow={st >> 1 & 1}, "
+                                  f"wait timeout={st >> 2 & 1}, bad slot={st >> 3 & 1})")
+
+    def device_block_table(self, slot: int, n: int | None = None) -> list[int]:
+        row = self.bt_dev[slot].tolist()
+        return row[: len(self.block_tables[slot]) if n is None else n]
+
+
+def _align4(n: int) -> int:
+    return (n + 3) & ~3
