@@ -50,7 +50,11 @@ def _args():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--e2e-steps", type=int, default=50)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    return ap.parse_args()
+    ap.add_argument("--layers", type=int, default=None, help="fewer layers (profiling a small case)")
+    a = ap.parse_args()
+    if a.layers:
+        CFG["layers"] = a.layers
+    return a
 
 
 def _ctx_lens(n, seed):

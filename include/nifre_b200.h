@@ -58,7 +58,7 @@ extern "C" {
 #define NF_SEQ_FIELDS 4   /* slot, q_start (row of the first new token), q_len, ctx_before */
 #define NF_PATCH_FIELDS 3 /* slot, logical block index, physical block id */
 #define NF_ITEM_FIELDS 4  /* slot, q_row, kv_len, unit_base */
-#define NF_UNIT_FIELDS 2  /* item, split index */
+#define NF_UNIT_FIELDS 8  /* item, slot, q_row, kv_len, key_begin, key_end, unit_base, n_splits */
 
 /* Message of the last failed call on this thread ("" if none). */
 const char* nf_last_error(void);
@@ -80,8 +80,10 @@ int nf_abi_version(void);
  *   src_rows[t]        row of token t in the caller's q/k/v tensors,
  *   positions[t]       absolute position (int64, may be NULL),
  *   items[t][4]        attention work item of the query at token t,
- * and the split-K work list units[max_units][2] of key ranges of
- * split_tokens keys; counts[0] = n_tokens, counts[1] = number of units.
+ * and the split-K work list units[max_units][8] (16-byte aligned) of key
+ * ranges [key_begin, key_end) of at most split_tokens keys, each record
+ * self-contained so a kernel needs one read per unit;
+ * counts[0] = n_tokens, counts[1] = number of units.
  */
 int nf_pack_step(const int32_t* seqs, int32_t n_seqs,
                  const int32_t* patches, int32_t n_patches,

@@ -20,7 +20,7 @@ NF_STATUS_UNIT_OVERFLOW = 2
 NF_STATUS_WAIT_TIMEOUT = 4
 NF_STATUS_BAD_SLOT = 8
 
-SEQ_FIELDS, PATCH_FIELDS, ITEM_FIELDS, UNIT_FIELDS = 4, 3, 4, 2
+SEQ_FIELDS, PATCH_FIELDS, ITEM_FIELDS, UNIT_FIELDS = 4, 3, 4, 8
 
 _DTYPE_CODE = {torch.float32: NF_F32, torch.float16: NF_F16, torch.bfloat16: NF_BF16}
 

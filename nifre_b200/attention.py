@@ -111,7 +111,7 @@ def causal_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, head_dim
     slot_mapping = torch.empty(n_tok, dtype=torch.int32, device=dev)
     src_rows = torch.empty_like(slot_mapping)
     items = torch.empty(4 * n_tok, dtype=torch.int32, device=dev)
-    units = torch.empty(2 * max_units, dtype=torch.int32, device=dev)
+    units = torch.empty(_lib.UNIT_FIELDS * max_units, dtype=torch.int32, device=dev)
     counts = torch.empty(2, dtype=torch.int32, device=dev)
     status = torch.zeros(1, dtype=torch.int32, device=dev)
     stream = _lib.stream_handle(dev)

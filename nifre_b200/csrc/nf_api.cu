@@ -54,4 +54,4 @@ size_t dtype_size(int dtype) {
 
 extern "C" const char* nf_last_error(void) { return nf::g_err; }
 
-extern "C" int nf_abi_version(void) { return 1; }
+extern "C" int nf_abi_version(void) { return 2; }

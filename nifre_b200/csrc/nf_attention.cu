@@ -8,32 +8,38 @@
 // (paged_kv_cache.py:72-85 layout) instead of PagedKVCache.get's gather and
 // torch.cat (paged_kv_cache.py:123-142, attention.py:121-127).
 //
-// Work decomposition.  nf_pack_step emits one work item per query token
-// (slot, query row, kv_len) and cuts each item's keys into units of
-// `split` keys.  A persistent grid (one CTA per SM) walks the units; each
-// CTA covers a group of HG KV heads, so every staged key row is one
-// contiguous run of HG*D elements of the pool.
+// Work.  nf_pack_step emits one item per query token and cuts its keys into
+// units of at most `split` keys, each described by one 32-byte record.  A
+// work item of this kernel is (unit, KV head).  Every warp is an independent
+// worker: it takes the next work item from a queue (one atomic in the
+// caller's workspace), so fast warps simply take more items and the grid
+// finishes together whatever the mix of context lengths.  The next item is
+// requested two tiles before the current one's loads end and its record is
+// prefetched, so taking work costs no stall.
 //
-// Inside a CTA (warp specialised):
-//   * warp W (producer): for each stage of R = 16*SUB keys, looks up the
-//     block table and issues one TMA bulk copy (cp.async.bulk) per K row and
-//     per V row into a padded shared-memory row (pitch = HG*D*size + 16 so the
-//     fragment loads below hit 8 distinct bank groups); completion is counted
-//     in bytes on the stage's "full" mbarrier.
-//   * warps 0..W-1 (consumers): warp w owns KV head (w % HG) of the group and
-//     the 16-key sub-tile (w / HG) of each stage.  For 16-bit pools, the
-//     scores S^T = K Q^T (16 keys x 8 query heads of the group) and the output
-//     O^T += V^T P^T (D x 8) are mma.sync m16n8k16 tiles: GQA groups of up to
-//     8 query heads share one K/V read.  The probabilities go from the S^T
-//     accumulator layout to the B-operand layout with two movmatrix
-//     transposes.  For float32 pools the same stages are consumed with
-//     CUDA-core FMAs (the reference's float32 model must keep full precision).
-//   * split-K merge: a unit whose item has more than one partial writes
-//     (m, l, acc) to the caller's workspace; the last warp to finish an
-//     (item, KV head) -- counted with one atomic per warp -- merges all
-//     partials and writes the output.  There is no second launch and no
-//     cross-warp barrier; every wait in the kernel is an mbarrier wait with a
-//     time limit.
+// Staging.  Every warp runs its own pipeline: a ring of `stages` shared-memory
+// slots, each holding the K rows and V rows (one head, head_dim elements each)
+// of one tile of keys, filled with 16-byte cp.async copies.  A key tile is a
+// gather: with 16-token blocks its rows come from blocks scattered over the
+// pool and one head's row is only head_dim*2 bytes, so many small independent
+// copies keep HBM busy where a few large copies issued by one thread cannot.
+// The load cursor runs stages-1 tiles ahead of the compute cursor and crosses
+// unit boundaries; unit records travel from the loader to the compute side
+// through a small per-warp FIFO in shared memory.  Rows are XOR-swizzled in
+// 16-byte chunks (chunk c of row r at c ^ (r & 7)) so the ldmatrix fragment
+// loads are free of bank conflicts.  No warp ever waits on another warp: the
+// only waits are cp.async.wait_group on the warp's own copies.
+//
+// Compute.  For 16-bit pools the scores S^T = K Q^T (keys x 8 query heads of
+// the group) and the output O^T += V^T P^T (head_dim x 8) are mma.sync
+// m16n8k16 tiles: a GQA group of up to 8 query heads shares one K/V read.
+// Probabilities go from the S^T accumulator layout to the B-operand layout
+// with movmatrix transposes.  Float32 pools use CUDA-core FMAs (the
+// reference's float32 model keeps full precision).
+//
+// Split-K merge.  A unit whose item has more than one part writes (acc, m, l)
+// to the caller's workspace; the last warp to finish an (item, KV head) --
+// counted with one atomic -- merges all parts and writes the output.
 #include <math.h>
 
 #include "nf_common.cuh"
@@ -51,114 +57,329 @@ struct AttnParams {
   int Hq, Hkv, D, G, bs, num_blocks;
   const int* bt;
   int max_blocks;
-  const int* items;
   const int* units;
   const int* counts;
   int max_units, split;
   float scale_log2;
-  float* ws;
-  int* cnt;
+  float* ws;    // partials [max_units][Hq][D + 4]: acc[D], m, l, pad
+  int* cnt;     // parts finished per (item, KV head)
+  int* queue;   // {next work item, warps finished}; zero between launches
   int* status;
   // launch plan
-  int HG, SUB, W, n_hg, stages, R, pitch, row_bytes, stage_bytes;
+  int W, stages, head_bytes, stage_bytes, swz, tile, bs16, q_smem;
 };
 
-constexpr int kBarrierBytes = 256;  // full[8] + empty[8] mbarriers
-constexpr int kMaxStages = 8;
 constexpr float kNegInf = -INFINITY;
+constexpr int kFifo = 8;        // unit records in flight between loader and compute
+constexpr int kFifoInts = 16;   // ints per record
+constexpr int kFifoBytes = kFifo * kFifoInts * 4;
 
-__device__ __forceinline__ uint32_t full_bar(unsigned char* smem, int s) { return smem_u32(smem) + 8 * s; }
-__device__ __forceinline__ uint32_t empty_bar(unsigned char* smem, int s) { return smem_u32(smem) + 64 + 8 * s; }
-
-// ---------------------------------------------------------------- producer
-template <typename T>
-__device__ void producer_loop(const AttnParams& p, unsigned char* smem, int total) {
-  const int lane = threadIdx.x & 31;
-  const uint32_t tx_bytes = 2u * p.R * p.row_bytes;
-  const uint32_t stage0 = smem_u32(smem) + kBarrierBytes;
-  int k = 0;
-  bool ok = true;
-  for (int v = blockIdx.x; v < total && ok; v += gridDim.x) {
-    const int u = v / p.n_hg, hg = v % p.n_hg;
-    const int item = p.units[2 * u], split = p.units[2 * u + 1];
-    const int slot = p.items[4 * item], kv_len = p.items[4 * item + 2];
-    const int t0 = split * p.split, t1 = min(t0 + p.split, kv_len);
-    const int* btrow = p.bt + (long long)slot * p.max_blocks;
-    const long long head_off = (long long)hg * p.HG * p.D;
-    for (int t = t0; t < t1; t += p.R, ++k) {
-      const int s = k % p.stages, round = k / p.stages;
-      if (!mbar_wait(empty_bar(smem, s), (round & 1) ^ 1, p.status)) {
-        ok = false;
-        break;
-      }
-      if (lane == 0) mbar_arrive_expect_tx(full_bar(smem, s), tx_bytes);
-      __syncwarp();
-      const uint32_t sbase = stage0 + s * p.stage_bytes;
-      for (int i = lane; i < 2 * p.R; i += 32) {
-        const int kv = i >= p.R;
-        const int r = kv ? i - p.R : i;
-        const int tok = min(t + r, t1 - 1);  // rows past the end repeat the last key (masked)
-        const int lb = tok / p.bs;
-        int phys = lb < p.max_blocks ? btrow[lb] : -1;
-        if (phys < 0 || phys >= p.num_blocks) {
-          atomicOr(p.status, NF_STATUS_BAD_BLOCK);
-          phys = 0;
-        }
-        const long long row = (long long)phys * p.bs + tok % p.bs;
-        const T* src = reinterpret_cast<const T*>(kv ? p.vp : p.kp) + row * p.Hkv * p.D + head_off;
-        bulk_g2s(sbase + (kv * p.R + r) * p.pitch, src, p.row_bytes, full_bar(smem, s));
-      }
-    }
-  }
-  if (!ok) {
-    // leave no bulk copy in flight into this CTA's shared memory
-    for (int j = max(0, k - p.stages); j < k; ++j) mbar_wait(full_bar(smem, j % p.stages), (j / p.stages) & 1, p.status);
-  }
+// Byte offset of 16-byte chunk c of row r inside a tile (rows of head_bytes).
+__device__ __forceinline__ int tile_off(int r, int c, int head_bytes, int swz) {
+  const int pc = swz ? ((c & ~7) | ((c & 7) ^ (r & 7))) : c;
+  return r * head_bytes + pc * 16;
 }
 
-// ---------------------------------------------------------------- shared epilogue
-// Writes one query head's result for this warp's part of a unit.  `acc(d)`
-// returns the unnormalised accumulator of element d held by this lane (the
-// caller only calls for elements it owns).
-struct UnitCtx {
-  int u, item, q_row, kv_len, unit_base, nparts, kvh, sub;
+// One work item as both cursors see it.
+struct Work {
+  int w;  // work item index; < 0 marks the end of this warp's work
+  int u, item, slot, q_row, t0, t1, unit_base, nparts, kvh;
 };
 
-// Merge of all partials of (item, kvh) by the last warp to finish.
+// ---------------------------------------------------------------- load cursor
+struct Loader {
+  Work c;          // work item being loaded (c.w < 0: exhausted)
+  int t;           // first key of the next tile to load
+  int lb, off;     // its logical block and offset in that block
+  int total;       // number of work items
+  int pending;     // lane 0: queue ticket requested, not yet read
+  int nstate;      // 0: next not requested yet, 1: ticket pending, 2: next record fetched
+  int nw;          // next work item
+  int4 na, nb;     // its unit record
+  int fifo_w;      // FIFO write index
+};
+
+__device__ __forceinline__ void request_next(const AttnParams& p, Loader& L) {
+  if ((threadIdx.x & 31) == 0) L.pending = atomicAdd(p.queue, 1);
+  L.nstate = 1;
+}
+
+// Turn the pending ticket into the next item and start fetching its record.
+__device__ __forceinline__ void resolve_next(const AttnParams& p, Loader& L) {
+  L.nw = __shfl_sync(0xffffffffu, L.pending, 0);
+  if (L.nw < L.total) {
+    const int4* rec = reinterpret_cast<const int4*>(p.units) + 2 * (L.nw / p.Hkv);
+    L.na = __ldg(rec);
+    L.nb = __ldg(rec + 1);
+  }
+  L.nstate = 2;
+}
+
+__device__ __forceinline__ void fifo_push(unsigned char* fifo, Loader& L) {
+  if ((threadIdx.x & 31) == 0) {
+    int* e = reinterpret_cast<int*>(fifo) + (L.fifo_w % kFifo) * kFifoInts;
+    const Work& c = L.c;
+    e[0] = c.w; e[1] = c.u; e[2] = c.item; e[3] = c.slot; e[4] = c.q_row;
+    e[5] = c.t0; e[6] = c.t1; e[7] = c.unit_base; e[8] = c.nparts; e[9] = c.kvh;
+  }
+  ++L.fifo_w;
+  __syncwarp();
+}
+
+// Make the prefetched item current (or mark the loader exhausted) and queue
+// its record for the compute side.
+__device__ __forceinline__ void loader_enter(const AttnParams& p, Loader& L, unsigned char* fifo) {
+  if (L.nstate == 1) resolve_next(p, L);
+  if (L.nw >= L.total) {
+    L.c.w = -1;
+    fifo_push(fifo, L);
+    return;
+  }
+  Work& c = L.c;
+  c.w = L.nw;
+  c.u = L.nw / p.Hkv;
+  c.kvh = L.nw - c.u * p.Hkv;
+  c.item = L.na.x;
+  c.slot = L.na.y;
+  c.q_row = L.na.z;
+  c.t0 = L.nb.x;
+  c.t1 = L.nb.y;
+  c.unit_base = L.nb.z;
+  c.nparts = L.nb.w;
+  L.t = c.t0;
+  L.lb = c.t0 / p.bs;
+  L.off = c.t0 - L.lb * p.bs;
+  // pull the unit's block-table entries into L1 ahead of the tile loads
+  {
+    const int* btrow = p.bt + (long long)c.slot * p.max_blocks;
+    const int lb_end = min((c.t1 - 1) / p.bs, p.max_blocks - 1);
+    const int lane = threadIdx.x & 31;
+    for (int lbx = L.lb + 32 * lane; lbx <= lb_end; lbx += 32 * 32)
+      asm volatile("prefetch.global.L1 [%0];" ::"l"(btrow + lbx));
+  }
+  fifo_push(fifo, L);
+  L.nstate = 0;
+  // a one- or two-tile unit needs its successor right away
+  if (c.t1 - c.t0 <= 2 * p.tile) request_next(p, L);
+}
+
+__device__ __forceinline__ void loader_init(const AttnParams& p, Loader& L, unsigned char* fifo, int total) {
+  L.total = total;
+  L.fifo_w = 0;
+  L.pending = 0;
+  request_next(p, L);
+  resolve_next(p, L);
+  loader_enter(p, L, fifo);
+}
+
+// Advance by one tile.  The next work item is requested two tiles before the
+// current unit's loads end (late enough that a warp never holds work another
+// warp could start, early enough to hide the atomic) and its ticket is read
+// one tile later.
+__device__ __forceinline__ void loader_next(const AttnParams& p, Loader& L, unsigned char* fifo) {
+  L.t += p.tile;
+  L.off += p.tile;
+  while (L.off >= p.bs) {
+    L.off -= p.bs;
+    ++L.lb;
+  }
+  if (L.nstate == 1) resolve_next(p, L);
+  if (L.nstate == 0 && L.t + 2 * p.tile >= L.c.t1) request_next(p, L);
+  if (L.t >= L.c.t1) loader_enter(p, L, fifo);
+}
+
+__device__ __forceinline__ Work fifo_pop(const unsigned char* fifo, int& r) {
+  __syncwarp();
+  const int* e = reinterpret_cast<const int*>(fifo) + (r % kFifo) * kFifoInts;
+  ++r;
+  Work c;
+  c.w = e[0]; c.u = e[1]; c.item = e[2]; c.slot = e[3]; c.q_row = e[4];
+  c.t0 = e[5]; c.t1 = e[6]; c.unit_base = e[7]; c.nparts = e[8]; c.kvh = e[9];
+  return c;
+}
+
+__device__ __forceinline__ int checked_block(const AttnParams& p, const int* btrow, int lb) {
+  int phys = lb < p.max_blocks ? __ldg(btrow + lb) : -1;
+  if (phys < 0 || phys >= p.num_blocks) {
+    atomicOr(p.status, NF_STATUS_BAD_BLOCK);
+    phys = 0;
+  }
+  return phys;
+}
+
+// With the first tile of a unit, bring the group's query rows along (G rows
+// of head_bytes after the K and V tiles of the slot).
 template <typename T>
-__device__ void merge_partials(const AttnParams& p, const UnitCtx& c) {
+__device__ __forceinline__ void stage_query(const AttnParams& p, const Loader& L, uint32_t slot_base) {
+  if (!p.q_smem || L.t != L.c.t0) return;
   const int lane = threadIdx.x & 31;
-  const int DP = p.D + 2;
-  for (int n = 0; n < p.G; ++n) {
-    const int qh = c.kvh * p.G + n;
-    float M = kNegInf;
-    for (int j = 0; j < c.nparts; ++j) {
-      const float* pb = p.ws + ((long long)(c.unit_base * p.SUB + j) * p.Hq + qh) * DP;
-      M = fmaxf(M, __ldcg(pb + p.D));
+  const char* qrow = p.q + ((long long)L.c.q_row * p.q_stride + (long long)L.c.kvh * p.G * p.D) * (long long)sizeof(T);
+  const uint32_t qs = slot_base + 2 * p.tile * p.head_bytes;
+  for (int idx = lane; idx < p.G * (p.head_bytes >> 4); idx += 32) cp_async16(qs + idx * 16, qrow + idx * 16);
+}
+
+// Copies of the loader's current tile into ring slot `slot_base`: any block
+// size and row length, one block-table read per row.
+template <typename T>
+__device__ __forceinline__ void issue_tile(const AttnParams& p, const Loader& L, uint32_t slot_base) {
+  const int lane = threadIdx.x & 31;
+  const int cpr = p.head_bytes >> 4;  // 16-byte chunks per row
+  const int* btrow = p.bt + (long long)L.c.slot * p.max_blocks;
+  const int last = L.c.t1 - 1 - L.t;  // rows past the end repeat the last key (masked later)
+  const size_t head_off = (size_t)L.c.kvh * p.D;
+  for (int idx = lane; idx < p.tile * cpr; idx += 32) {
+    const int r = idx / cpr, ch = idx - r * cpr;
+    int off = L.off + min(r, last), lb = L.lb;
+    while (off >= p.bs) {
+      off -= p.bs;
+      ++lb;
     }
-    float L = 0.f;
-    for (int j = 0; j < c.nparts; ++j) {
-      const float* pb = p.ws + ((long long)(c.unit_base * p.SUB + j) * p.Hq + qh) * DP;
-      const float mj = __ldcg(pb + p.D);
-      if (mj != kNegInf) L += __ldcg(pb + p.D + 1) * ex2(mj - M);
+    const int phys = checked_block(p, btrow, lb);
+    const size_t row = ((size_t)phys * p.bs + off) * p.Hkv * p.D + head_off;
+    const uint32_t dst = slot_base + tile_off(r, ch, p.head_bytes, p.swz);
+    cp_async16(dst, reinterpret_cast<const char*>(reinterpret_cast<const T*>(p.kp) + row) + ch * 16);
+    cp_async16(dst + p.tile * p.head_bytes, reinterpret_cast<const char*>(reinterpret_cast<const T*>(p.vp) + row) + ch * 16);
+  }
+  stage_query<T>(p, L, slot_base);
+}
+
+// Per-lane constants of the fast tile copy: the lane's 16-byte chunk of a
+// row, its first row, and the swizzled destination offsets, which repeat
+// every 8/RP rows.
+template <int TILE, int HB>
+struct LaneCopy {
+  static constexpr int CPR = HB / 16;              // 16-byte chunks per row
+  static constexpr int LPR = CPR < 32 ? CPR : 32;  // lanes per row
+  static constexpr int RP = 32 / LPR;              // rows per pass
+  static constexpr int CPL = CPR / LPR;            // chunks per lane per row
+  static constexpr int NPAT = RP >= 8 ? 1 : 8 / RP;
+  int src;          // byte offset within a pool row run: rg * row_stride + chunk * 16
+  int dst[NPAT][CPL];
+  __device__ __forceinline__ void init(int row_stride) {
+    const int lane = threadIdx.x & 31;
+    const int c0 = lane % LPR, rg = lane / LPR;
+    src = rg * row_stride + c0 * 16;
+#pragma unroll
+    for (int q = 0; q < NPAT; ++q)
+#pragma unroll
+      for (int cc = 0; cc < CPL; ++cc) dst[q][cc] = tile_off(rg + RP * q, c0 + LPR * cc, HB, 1) - (RP * q) * HB;
+  }
+};
+
+// Same copies with compile-time geometry: TILE keys, HB-byte head rows.  When
+// the block size is a multiple of 16 each 16-key half of the tile is one run
+// of consecutive pool rows: a full tile costs at most two block-table reads
+// (L1 hits, prefetched when the unit was entered) and one add per copy.
+template <typename T, int TILE, int HB>
+__device__ __forceinline__ void issue_tile_fast(const AttnParams& p, const Loader& L, const LaneCopy<TILE, HB>& lc,
+                                                uint32_t slot_base) {
+  using LC = LaneCopy<TILE, HB>;
+  if (!p.bs16 || L.c.t1 - L.t < TILE) {  // other block sizes and the tail tile of a unit
+    issue_tile<T>(p, L, slot_base);
+    return;
+  }
+  const int* btrow = p.bt + (long long)L.c.slot * p.max_blocks;
+  const long long rs = (long long)p.Hkv * HB;  // pool row stride, bytes
+  const char* kbase[TILE / 16];
+  const char* vbase[TILE / 16];
+#pragma unroll
+  for (int h = 0; h < TILE / 16; ++h) {
+    int off = L.off + 16 * h, lb = L.lb;
+    if (off >= p.bs) {  // off and bs are multiples of 16: at most one block further
+      off -= p.bs;
+      ++lb;
     }
-    const float inv = L > 0.f ? 1.f / L : 0.f;
-    T* o = reinterpret_cast<T*>(p.out) + (long long)c.q_row * p.out_stride + (long long)qh * p.D;
-    for (int d = lane; d < p.D; d += 32) {
-      float a = 0.f;
-      for (int j = 0; j < c.nparts; ++j) {
-        const float* pb = p.ws + ((long long)(c.unit_base * p.SUB + j) * p.Hq + qh) * DP;
-        const float mj = __ldcg(pb + p.D);
-        if (mj != kNegInf) a += __ldcg(pb + d) * ex2(mj - M);
+    const long long o = ((long long)checked_block(p, btrow, lb) * p.bs + off) * rs + (long long)L.c.kvh * HB + lc.src;
+    kbase[h] = p.kp + o;
+    vbase[h] = p.vp + o;
+  }
+#pragma unroll
+  for (int j = 0; j < TILE / LC::RP; ++j) {
+    const int r0 = LC::RP * j;  // first row of this pass (compile time)
+    const int h = r0 >> 4;
+    const int rrow = (r0 & 15) * (int)rs;
+#pragma unroll
+    for (int cc = 0; cc < LC::CPL; ++cc) {
+      const uint32_t dst = slot_base + lc.dst[j % LC::NPAT][cc] + r0 * HB;
+      cp_async16(dst, kbase[h] + rrow + LC::LPR * cc * 16);
+      cp_async16(dst + TILE * HB, vbase[h] + rrow + LC::LPR * cc * 16);
+    }
+  }
+  stage_query<T>(p, L, slot_base);
+}
+
+// ---------------------------------------------------------------- split-K merge
+// Merges the nparts (acc, m, l) records of one (item, KV head) into the
+// output.  Warp-parallel: lanes read the parts' maxima and sums for all heads
+// of the group at once, then every lane accumulates its float4 chunks of the
+// output with four parts' loads in flight.
+template <typename T>
+__device__ void merge_partials(const AttnParams& p, const Work& c) {
+  const int lane = threadIdx.x & 31;
+  const int D = p.D, DP = D + 4, G = p.G;
+  const float* part0 = p.ws + ((long long)c.unit_base * p.Hq + (long long)c.kvh * G) * DP;
+  const long long ps = (long long)p.Hq * DP;  // between consecutive parts
+  const int GP = G <= 1 ? 1 : G <= 2 ? 2 : G <= 4 ? 4 : 8;  // heads rounded up to a power of two
+  const int n = lane % GP, jj = lane / GP, PP = 32 / GP;
+  float mx = kNegInf;
+  if (n < G)
+    for (int j = jj; j < c.nparts; j += PP) mx = fmaxf(mx, __ldcg(part0 + j * ps + n * DP + D));
+  for (int o_ = GP; o_ < 32; o_ <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o_));
+  float sm = 0.f;
+  if (n < G)
+    for (int j = jj; j < c.nparts; j += PP) {
+      const float* pb = part0 + j * ps + n * DP;
+      const float mj = __ldcg(pb + D);
+      if (mj != kNegInf) sm += __ldcg(pb + D + 1) * ex2(mj - mx);
+    }
+  for (int o_ = GP; o_ < 32; o_ <<= 1) sm += __shfl_xor_sync(0xffffffffu, sm, o_);
+  // lane n (< GP) now holds head n's max and normaliser
+  T* o = reinterpret_cast<T*>(p.out) + (long long)c.q_row * p.out_stride + (long long)c.kvh * G * D;
+  const int D4 = D >> 2, GD4 = G * D4;
+  for (int e0 = 0; e0 < GD4; e0 += 32) {
+    const int e = min(e0 + lane, GD4 - 1);
+    const int hn = e / D4, d = (e - hn * D4) * 4;
+    const float Mn = __shfl_sync(0xffffffffu, mx, hn);
+    const float Ln = __shfl_sync(0xffffffffu, sm, hn);
+    if (e0 + lane < GD4) {
+      const float* pe = part0 + hn * DP;
+      float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+      int j = 0;
+      for (; j + 4 <= c.nparts; j += 4) {
+        float4 x[4];
+        float mm[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          x[u] = __ldcg(reinterpret_cast<const float4*>(pe + (j + u) * ps + d));
+          mm[u] = __ldcg(pe + (j + u) * ps + D);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const float wgt = mm[u] == kNegInf ? 0.f : ex2(mm[u] - Mn);
+          a.x += x[u].x * wgt; a.y += x[u].y * wgt; a.z += x[u].z * wgt; a.w += x[u].w * wgt;
+        }
       }
-      o[d] = Elem<T>::from_f(a * inv);
+      for (; j < c.nparts; ++j) {
+        const float mj = __ldcg(pe + j * ps + D);
+        if (mj != kNegInf) {
+          const float4 x = __ldcg(reinterpret_cast<const float4*>(pe + j * ps + d));
+          const float wgt = ex2(mj - Mn);
+          a.x += x.x * wgt; a.y += x.y * wgt; a.z += x.z * wgt; a.w += x.w * wgt;
+        }
+      }
+      const float inv = Ln > 0.f ? 1.f / Ln : 0.f;
+      T* od = o + hn * D + d;
+      od[0] = Elem<T>::from_f(a.x * inv);
+      od[1] = Elem<T>::from_f(a.y * inv);
+      od[2] = Elem<T>::from_f(a.z * inv);
+      od[3] = Elem<T>::from_f(a.w * inv);
     }
   }
 }
 
-// After this warp wrote its partial: count it; the last one merges.
+// After this warp wrote its part: count it; the last part merges.
 template <typename T>
-__device__ void finish_partial(const AttnParams& p, const UnitCtx& c) {
+__device__ void finish_partial(const AttnParams& p, const Work& c) {
   __threadfence();
   __syncwarp();
   int last = 0;
@@ -172,44 +393,56 @@ __device__ void finish_partial(const AttnParams& p, const UnitCtx& c) {
   }
 }
 
-// ---------------------------------------------------------------- consumers
-__device__ __forceinline__ UnitCtx unit_ctx(const AttnParams& p, int v, int warp) {
-  UnitCtx c;
-  c.u = v / p.n_hg;
-  const int hg = v % p.n_hg;
-  c.item = p.units[2 * c.u];
-  c.q_row = p.items[4 * c.item + 1];
-  c.kv_len = p.items[4 * c.item + 2];
-  c.unit_base = p.items[4 * c.item + 3];
-  c.nparts = ((c.kv_len + p.split - 1) / p.split) * p.SUB;
-  c.kvh = hg * p.HG + warp % p.HG;
-  c.sub = warp / p.HG;
-  return c;
+// The last warp of the grid to run out of work resets the queue for the next launch.
+__device__ __forceinline__ void retire_warp(const AttnParams& p) {
+  if ((threadIdx.x & 31) == 0) {
+    __threadfence();
+    if (atomicAdd(p.queue + 1, 1) == (int)(gridDim.x * p.W) - 1) {
+      p.queue[0] = 0;
+      p.queue[1] = 0;
+      __threadfence();
+    }
+  }
 }
 
-// 16-bit pools: tensor-core tiles.  D_ is the head dimension (64 or 128).
-template <typename T, int D_>
-__device__ void consumer_mma(const AttnParams& p, unsigned char* smem, int total) {
+// ---------------------------------------------------------------- 16-bit pools: tensor-core tiles
+// D_: head dim (64 or 128).  MT: 16-key m-tiles per warp tile (TILE = 16*MT keys).
+template <typename T, int D_, int MT>
+__device__ void warp_mma(const AttnParams& p, uint32_t ring, unsigned char* fifo, int total) {
   constexpr int KS = D_ / 16;  // k-steps of S^T and m-tiles of O^T
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint32_t stage0 = smem_u32(smem) + kBarrierBytes;
-  const int n0 = 2 * (lane & 3);       // query heads of this lane's accumulator columns
-  const int tq = lane >> 2;            // key row / d row of this lane in a fragment
-  int k = 0;
-  for (int v = blockIdx.x; v < total; v += gridDim.x) {
-    const UnitCtx c = unit_ctx(p, v, warp);
-    const int split = p.units[2 * c.u + 1];
-    const int t0 = split * p.split, t1 = min(t0 + p.split, c.kv_len);
-    // Q^T as the B operand: column n = query head tq of the group.
+  constexpr int HB = D_ * 2;   // bytes of one head row
+  constexpr int TILE = 16 * MT;
+  const int lane = threadIdx.x & 31;
+  const int n0 = 2 * (lane & 3);  // query heads of this lane's accumulator columns
+  const int tq = lane >> 2;       // key row / d row of this lane in a fragment
+  const bool has = tq < p.G;      // lane's B-operand column is a real query head
+  const int S = p.stages;
+  LaneCopy<TILE, HB> lc;
+  lc.init(p.Hkv * HB);
+  Loader L;
+  loader_init(p, L, fifo, total);
+  for (int s = 0; s < S - 1; ++s) {
+    if (L.c.w >= 0) {
+      issue_tile_fast<T, TILE, HB>(p, L, lc, ring + s * p.stage_bytes);
+      loader_next(p, L, fifo);
+    }
+    cp_async_commit();
+  }
+  // fragment addressing (rows this lane supplies to ldmatrix, before the swizzle)
+  const int kr = (lane & 7) + ((lane >> 3) & 1) * 8, kc = lane >> 4;        // K: row, chunk parity
+  const int vr = (lane & 7) + ((lane >> 4) & 1) * 8, vc = (lane >> 3) & 1;  // V: row, chunk parity
+  int k = 0, fr = 0;
+  while (true) {
+    const Work c = fifo_pop(fifo, fr);
+    if (c.w < 0) break;
     uint32_t qf[KS][2];
-    {
+    if (!p.q_smem) {
       const T* qp = reinterpret_cast<const T*>(p.q) + (long long)c.q_row * p.q_stride +
                     (long long)(c.kvh * p.G + tq) * D_ + n0;
-      const bool has = tq < p.G;
 #pragma unroll
       for (int ks = 0; ks < KS; ++ks) {
-        qf[ks][0] = has ? *reinterpret_cast<const uint32_t*>(qp + ks * 16) : 0u;
-        qf[ks][1] = has ? *reinterpret_cast<const uint32_t*>(qp + ks * 16 + 8) : 0u;
+        qf[ks][0] = has ? __ldg(reinterpret_cast<const uint32_t*>(qp + ks * 16)) : 0u;
+        qf[ks][1] = has ? __ldg(reinterpret_cast<const uint32_t*>(qp + ks * 16 + 8)) : 0u;
       }
     }
     float m0 = kNegInf, m1 = kNegInf, l0 = 0.f, l1 = 0.f;
@@ -217,70 +450,90 @@ __device__ void consumer_mma(const AttnParams& p, unsigned char* smem, int total
 #pragma unroll
     for (int i = 0; i < KS; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
 
-    for (int t = t0; t < t1; t += p.R, ++k) {
-      const int s = k % p.stages, round = k / p.stages;
-      if (!mbar_wait(full_bar(smem, s), round & 1, p.status)) return;
-      const int tb = t + c.sub * 16;
-      if (tb < t1) {
-        const uint32_t kbase = stage0 + s * p.stage_bytes + (c.sub * 16) * p.pitch + (warp % p.HG) * D_ * 2;
-        const uint32_t vbase = kbase + p.R * p.pitch;
-        // S^T = K Q^T : 16 keys x 8 query heads
-        float sc[4] = {0.f, 0.f, 0.f, 0.f};
-        {
-          const int r = (lane & 7) + ((lane >> 3) & 1) * 8;  // key row supplied by this lane
-          const int cb = (lane >> 4) * 8;                       // column half
-          const uint32_t a_addr = kbase + r * p.pitch + cb * 2;
+    for (int tb = c.t0; tb < c.t1; tb += TILE, ++k) {
+      cp_async_wait(S - 2);
+      __syncwarp();
+      if (L.c.w >= 0) {
+        issue_tile_fast<T, TILE, HB>(p, L, lc, ring + ((k + S - 1) % S) * p.stage_bytes);
+        loader_next(p, L, fifo);
+      }
+      cp_async_commit();
+      const uint32_t kb = ring + (k % S) * p.stage_bytes;
+      const uint32_t vb = kb + TILE * HB;
+      if (p.q_smem && tb == c.t0) {
+        // Q^T as the B operand, staged with this unit's first tile: column n = query head tq
+        const uint32_t qs = kb + 2 * TILE * HB + tq * HB + n0 * 2;
 #pragma unroll
-          for (int ks = 0; ks < KS; ++ks) {
-            uint32_t a0, a1, a2, a3;
-            ldsm_x4(a_addr + ks * 32, a0, a1, a2, a3);
-            mma16816<T>(sc, a0, a1, a2, a3, qf[ks][0], qf[ks][1]);
-          }
-        }
-        const bool v0 = tb + tq < t1, v1 = tb + tq + 8 < t1;
-        const float x0 = v0 ? sc[0] * p.scale_log2 : kNegInf;
-        const float x1 = v0 ? sc[1] * p.scale_log2 : kNegInf;
-        const float x2 = v1 ? sc[2] * p.scale_log2 : kNegInf;
-        const float x3 = v1 ? sc[3] * p.scale_log2 : kNegInf;
-        float mx0 = fmaxf(x0, x2), mx1 = fmaxf(x1, x3);
-#pragma unroll
-        for (int o_ = 4; o_ < 32; o_ <<= 1) {
-          mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o_));
-          mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o_));
-        }
-        const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
-        const float b0 = mn0 == kNegInf ? 0.f : mn0, b1 = mn1 == kNegInf ? 0.f : mn1;
-        const float al0 = ex2(m0 - b0), al1 = ex2(m1 - b1);
-        const float p0 = ex2(x0 - b0), p1 = ex2(x1 - b1), p2 = ex2(x2 - b0), p3 = ex2(x3 - b1);
-        l0 = l0 * al0 + p0 + p2;
-        l1 = l1 * al1 + p1 + p3;
-        m0 = mn0;
-        m1 = mn1;
-#pragma unroll
-        for (int i = 0; i < KS; ++i) {
-          o[i][0] *= al0;
-          o[i][1] *= al1;
-          o[i][2] *= al0;
-          o[i][3] *= al1;
-        }
-        // P^T (keys x heads) as the B operand: transpose the two 8x8 halves.
-        const uint32_t pb0 = movmatrix_t(pack2<T>(p0, p1));
-        const uint32_t pb1 = movmatrix_t(pack2<T>(p2, p3));
-        // O^T += V^T P^T
-        {
-          const int r = (lane & 7) + ((lane >> 4) & 1) * 8;  // key row supplied by this lane
-          const int cb = ((lane >> 3) & 1) * 8;               // d offset within the m-tile
-          const uint32_t a_addr = vbase + r * p.pitch + cb * 2;
-#pragma unroll
-          for (int i = 0; i < KS; ++i) {
-            uint32_t a0, a1, a2, a3;
-            ldsm_x4_t(a_addr + i * 32, a0, a1, a2, a3);
-            mma16816<T>(o[i], a0, a1, a2, a3, pb0, pb1);
-          }
+        for (int ks = 0; ks < KS; ++ks) {
+          qf[ks][0] = has ? lds32(qs + ks * 32) : 0u;
+          qf[ks][1] = has ? lds32(qs + ks * 32 + 16) : 0u;
         }
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(empty_bar(smem, s));
+      // S^T = K Q^T : TILE keys x 8 query heads (MT independent accumulator chains)
+      float sc[MT][4];
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt) sc[mt][0] = sc[mt][1] = sc[mt][2] = sc[mt][3] = 0.f;
+#pragma unroll
+      for (int ks = 0; ks < KS; ++ks) {
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt) {
+          uint32_t a0, a1, a2, a3;
+          ldsm_x4(kb + tile_off(16 * mt + kr, 2 * ks + kc, HB, 1), a0, a1, a2, a3);
+          mma16816<T>(sc[mt], a0, a1, a2, a3, qf[ks][0], qf[ks][1]);
+        }
+      }
+      float x[MT][4];
+      float mx0 = kNegInf, mx1 = kNegInf;
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt) {
+        const bool v0 = tb + 16 * mt + tq < c.t1, v1 = tb + 16 * mt + tq + 8 < c.t1;
+        x[mt][0] = v0 ? sc[mt][0] * p.scale_log2 : kNegInf;
+        x[mt][1] = v0 ? sc[mt][1] * p.scale_log2 : kNegInf;
+        x[mt][2] = v1 ? sc[mt][2] * p.scale_log2 : kNegInf;
+        x[mt][3] = v1 ? sc[mt][3] * p.scale_log2 : kNegInf;
+        mx0 = fmaxf(mx0, fmaxf(x[mt][0], x[mt][2]));
+        mx1 = fmaxf(mx1, fmaxf(x[mt][1], x[mt][3]));
+      }
+#pragma unroll
+      for (int o_ = 4; o_ < 32; o_ <<= 1) {
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o_));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o_));
+      }
+      const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+      const float b0 = mn0 == kNegInf ? 0.f : mn0, b1 = mn1 == kNegInf ? 0.f : mn1;
+      const float al0 = ex2(m0 - b0), al1 = ex2(m1 - b1);
+      m0 = mn0;
+      m1 = mn1;
+      l0 *= al0;
+      l1 *= al1;
+      uint32_t pb[MT][2];
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt) {
+        const float p0 = ex2(x[mt][0] - b0), p1 = ex2(x[mt][1] - b1);
+        const float p2 = ex2(x[mt][2] - b0), p3 = ex2(x[mt][3] - b1);
+        l0 += p0 + p2;
+        l1 += p1 + p3;
+        // P^T (keys x heads) as the B operand: transpose the two 8x8 halves
+        pb[mt][0] = movmatrix_t(pack2<T>(p0, p1));
+        pb[mt][1] = movmatrix_t(pack2<T>(p2, p3));
+      }
+#pragma unroll
+      for (int i = 0; i < KS; ++i) {
+        o[i][0] *= al0;
+        o[i][1] *= al1;
+        o[i][2] *= al0;
+        o[i][3] *= al1;
+      }
+      // O^T += V^T P^T
+#pragma unroll
+      for (int i = 0; i < KS; ++i) {
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt) {
+          uint32_t a0, a1, a2, a3;
+          ldsm_x4_t(vb + tile_off(16 * mt + vr, 2 * i + vc, HB, 1), a0, a1, a2, a3);
+          mma16816<T>(o[i], a0, a1, a2, a3, pb[mt][0], pb[mt][1]);
+        }
+      }
     }
     // row sums: lanes sharing lane&3 hold the same query heads
 #pragma unroll
@@ -305,8 +558,8 @@ __device__ void consumer_mma(const AttnParams& p, unsigned char* smem, int total
         }
       }
     } else {
-      const int DP = D_ + 2;
-      float* wb = p.ws + ((long long)(c.u * p.SUB + c.sub) * p.Hq + c.kvh * p.G) * DP;
+      const int DP = D_ + 4;
+      float* wb = p.ws + ((long long)c.u * p.Hq + c.kvh * p.G) * DP;
 #pragma unroll
       for (int i = 0; i < KS; ++i) {
         const int d = 16 * i + tq;
@@ -332,19 +585,32 @@ __device__ void consumer_mma(const AttnParams& p, unsigned char* smem, int total
       finish_partial<T>(p, c);
     }
   }
+  cp_async_wait(0);
+  retire_warp(p);
 }
 
-// Any dtype, any head_dim <= 32*DPL, up to 8 query heads per KV head:
-// CUDA-core FMAs, lanes split the head dimension.
+// ---------------------------------------------------------------- any dtype: CUDA-core path
+// Any head_dim <= 32*DPL, up to 8 query heads per KV head; lanes split the
+// head dimension.  Same pipeline and queue as the tensor-core path.
 template <typename T, int DPL>
-__device__ void consumer_simt(const AttnParams& p, unsigned char* smem, int total) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  unsigned char* stage0 = smem + kBarrierBytes;
-  int k = 0;
-  for (int v = blockIdx.x; v < total; v += gridDim.x) {
-    const UnitCtx c = unit_ctx(p, v, warp);
-    const int split = p.units[2 * c.u + 1];
-    const int t0 = split * p.split, t1 = min(t0 + p.split, c.kv_len);
+__device__ void warp_simt(const AttnParams& p, uint32_t ring, unsigned char* ring_ptr, unsigned char* fifo,
+                          int total) {
+  const int lane = threadIdx.x & 31;
+  const int S = p.stages;
+  const int HB = p.head_bytes;
+  Loader L;
+  loader_init(p, L, fifo, total);
+  for (int s = 0; s < S - 1; ++s) {
+    if (L.c.w >= 0) {
+      issue_tile<T>(p, L, ring + s * p.stage_bytes);
+      loader_next(p, L, fifo);
+    }
+    cp_async_commit();
+  }
+  int k = 0, fr = 0;
+  while (true) {
+    const Work c = fifo_pop(fifo, fr);
+    if (c.w < 0) break;
     float qv[8][DPL], acc[8][DPL], m[8], l[8];
     const T* qp = reinterpret_cast<const T*>(p.q) + (long long)c.q_row * p.q_stride + (long long)(c.kvh * p.G) * p.D;
 #pragma unroll
@@ -358,22 +624,26 @@ __device__ void consumer_simt(const AttnParams& p, unsigned char* smem, int tota
         acc[n][i] = 0.f;
       }
     }
-    for (int t = t0; t < t1; t += p.R, ++k) {
-      const int s = k % p.stages, round = k / p.stages;
-      if (!mbar_wait(full_bar(smem, s), round & 1, p.status)) return;
-      const int tb = t + c.sub * 16;
-      const int nv = min(16, t1 - tb);
-      const unsigned char* kb = stage0 + s * p.stage_bytes + (c.sub * 16) * p.pitch + (warp % p.HG) * p.D * sizeof(T);
-      const unsigned char* vb = kb + p.R * p.pitch;
+    for (int tb = c.t0; tb < c.t1; tb += p.tile, ++k) {
+      cp_async_wait(S - 2);
+      __syncwarp();
+      if (L.c.w >= 0) {
+        issue_tile<T>(p, L, ring + ((k + S - 1) % S) * p.stage_bytes);
+        loader_next(p, L, fifo);
+      }
+      cp_async_commit();
+      const unsigned char* kb = ring_ptr + (k % S) * p.stage_bytes;
+      const unsigned char* vb = kb + p.tile * HB;
+      const int nv = min(p.tile, c.t1 - tb);
       for (int j = 0; j < nv; ++j) {
-        const T* kr = reinterpret_cast<const T*>(kb + j * p.pitch);
-        const T* vr = reinterpret_cast<const T*>(vb + j * p.pitch);
         float kk[DPL], vv[DPL];
 #pragma unroll
         for (int i = 0; i < DPL; ++i) {
           const int d = lane + 32 * i;
-          kk[i] = d < p.D ? Elem<T>::to_f(kr[d]) : 0.f;
-          vv[i] = d < p.D ? Elem<T>::to_f(vr[d]) : 0.f;
+          const int byte = d * (int)sizeof(T);
+          const int off = tile_off(j, byte >> 4, HB, p.swz) + (byte & 15);
+          kk[i] = d < p.D ? Elem<T>::to_f(*reinterpret_cast<const T*>(kb + off)) : 0.f;
+          vv[i] = d < p.D ? Elem<T>::to_f(*reinterpret_cast<const T*>(vb + off)) : 0.f;
         }
 #pragma unroll
         for (int n = 0; n < 8; ++n) {
@@ -392,8 +662,6 @@ __device__ void consumer_simt(const AttnParams& p, unsigned char* smem, int tota
           }
         }
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(empty_bar(smem, s));
     }
     if (c.nparts == 1) {
       T* ob = reinterpret_cast<T*>(p.out) + (long long)c.q_row * p.out_stride + (long long)(c.kvh * p.G) * p.D;
@@ -409,8 +677,8 @@ __device__ void consumer_simt(const AttnParams& p, unsigned char* smem, int tota
         }
       }
     } else {
-      const int DP = p.D + 2;
-      float* wb = p.ws + ((long long)(c.u * p.SUB + c.sub) * p.Hq + c.kvh * p.G) * DP;
+      const int DP = p.D + 4;
+      float* wb = p.ws + ((long long)c.u * p.Hq + c.kvh * p.G) * DP;
 #pragma unroll
       for (int n = 0; n < 8; ++n) {
         if (n < p.G) {
@@ -428,41 +696,32 @@ __device__ void consumer_simt(const AttnParams& p, unsigned char* smem, int tota
       finish_partial<T>(p, c);
     }
   }
+  cp_async_wait(0);
+  retire_warp(p);
 }
 
 // ---------------------------------------------------------------- kernel
-template <typename T, int D_, bool MMA, int DPL>
-__global__ void __launch_bounds__(288, 1) paged_attention_kernel(const AttnParams p) {
+template <typename T, int D_, int MT, bool MMA, int DPL>
+__global__ void __launch_bounds__(256) paged_attention_kernel(const AttnParams p) {
   extern __shared__ __align__(128) unsigned char smem[];
   const int warp = threadIdx.x >> 5;
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < p.stages; ++s) {
-      mbar_init(full_bar(smem, s), 1);
-      mbar_init(empty_bar(smem, s), p.W);
-    }
-    fence_mbar_init();
-  }
-  __syncthreads();
-  const int n_units = min(p.counts[1], p.max_units);
-  const int total = n_units * p.n_hg;
-  if (warp == p.W) {
-    producer_loop<T>(p, smem, total);
-  } else if (warp < p.W) {
-    if constexpr (MMA) consumer_mma<T, D_>(p, smem, total);
-    else consumer_simt<T, DPL>(p, smem, total);
-  }
+  const int n_units = min(__ldg(p.counts + 1), p.max_units);
+  const int total = n_units * p.Hkv;
+  unsigned char* ring_ptr = smem + (size_t)warp * p.stages * p.stage_bytes;
+  unsigned char* fifo = smem + (size_t)p.W * p.stages * p.stage_bytes + warp * kFifoBytes;
+  const uint32_t ring = smem_u32(ring_ptr);
+  if constexpr (MMA) warp_mma<T, D_, MT>(p, ring, fifo, total);
+  else warp_simt<T, DPL>(p, ring, ring_ptr, fifo, total);
 }
 
 // ---------------------------------------------------------------- host plan
 struct Plan {
-  int HG, SUB, W, n_hg, stages, R, pitch, row_bytes, stage_bytes, smem;
-  bool mma;
+  int W, stages, head_bytes, stage_bytes, smem, swz, tile;
+  bool mma, q_smem;
   int dpl;
 };
 
-constexpr int kSmemBudget = 227 * 1024;
-
-static int make_plan(int dtype, int Hq, int Hkv, int D, Plan& pl) {
+static int make_plan(int dtype, int Hq, int Hkv, int D, bool q_smem_ok, Plan& pl) {
   const size_t es = dtype_size(dtype);
   if (!es) return fail(NF_EINVAL, "nf_paged_attention: bad dtype %d", dtype);
   if (Hq <= 0 || Hkv <= 0 || D <= 0 || Hq % Hkv != 0)
@@ -470,61 +729,70 @@ static int make_plan(int dtype, int Hq, int Hkv, int D, Plan& pl) {
   const int G = Hq / Hkv;
   if (G > 8) return fail(NF_EUNSUPPORTED, "nf_paged_attention: more than 8 query heads per KV head (%d)", G);
   if (D > 256) return fail(NF_EUNSUPPORTED, "nf_paged_attention: head_dim %d > 256", D);
+  pl.head_bytes = D * (int)es;
+  if (pl.head_bytes % 16) return fail(NF_EUNSUPPORTED, "nf_paged_attention: a head row of %d bytes is not a multiple of 16", pl.head_bytes);
+  if (D % 4) return fail(NF_EUNSUPPORTED, "nf_paged_attention: head_dim %d is not a multiple of 4", D);
   pl.mma = (dtype != NF_F32) && (D == 64 || D == 128);
+  pl.q_smem = pl.mma && q_smem_ok;
   pl.dpl = D <= 32 ? 1 : D <= 64 ? 2 : D <= 128 ? 4 : 8;
-  // Pick the head group (HG KV heads per CTA, rows contiguous in the pool) and
-  // the number of 16-key sub-tiles per stage (SUB) with the most consumer
-  // warps (W = HG * SUB <= 8) whose stage still fits three times in shared
-  // memory (twice as a last resort).
-  pl.HG = 0;
-  for (int need = 3; need >= 2 && !pl.HG; --need) {
-    for (int w = 8; w >= 1 && !pl.HG; w >>= 1) {
-      for (int hg = (Hkv < 8 ? Hkv : 8); hg >= 1; --hg) {
-        if (Hkv % hg || (hg * D * (int)es) % 16) continue;
-        const int sub = w / hg > 0 ? w / hg : 1;
-        if (hg * sub > 8) continue;
-        const int pitch = hg * D * (int)es + 16;
-        const int stage = 2 * 16 * sub * pitch;
-        if ((kSmemBudget - kBarrierBytes) / stage < need) continue;
-        pl.HG = hg;
-        pl.SUB = sub;
-        break;
-      }
+  pl.swz = pl.head_bytes % 128 == 0;
+  // warp tiles of about 4 KB of keys: 32 keys of 128-byte rows, else 16
+  pl.tile = (pl.mma && D == 64) ? 32 : 16;
+  pl.stage_bytes = (2 * pl.tile + (pl.q_smem ? G : 0)) * pl.head_bytes;  // K tile, V tile, query rows
+  // Warps per CTA and ring depth: the most warps resident per SM with >= 3
+  // slots per warp (each warp keeps two tiles in flight); ties go to fewer,
+  // larger CTAs.  Two slots only as a last resort.
+  const int kSmemSM = 228 * 1024, kSmemCTA = 227 * 1024, kReserve = 1024;
+  int best = 0;
+  pl.W = 0;
+  for (int min_st = 3; min_st >= 2 && !pl.W; --min_st) {
+    for (int w = 8; w >= 1; w >>= 1) {
+      const int per_warp = min_st * pl.stage_bytes + kFifoBytes;
+      if (w * per_warp > kSmemCTA) continue;
+      int ctas = kSmemSM / (w * per_warp + kReserve);
+      if (ctas * w > 64) ctas = 64 / w;
+      if (ctas < 1 || ctas * w <= best) continue;
+      best = ctas * w;
+      pl.W = w;
+      int st = ((kSmemSM / ctas - kReserve) / w - kFifoBytes) / pl.stage_bytes;
+      if (w * (st * pl.stage_bytes + kFifoBytes) > kSmemCTA) st = (kSmemCTA / w - kFifoBytes) / pl.stage_bytes;
+      pl.stages = st > 8 ? 8 : st;
     }
   }
-  if (!pl.HG) return fail(NF_EUNSUPPORTED, "nf_paged_attention: no stage layout fits for %d KV heads x %d elements", Hkv, D);
-  pl.W = pl.HG * pl.SUB;
-  pl.n_hg = Hkv / pl.HG;
-  pl.R = 16 * pl.SUB;
-  pl.row_bytes = pl.HG * D * (int)es;
-  pl.pitch = pl.row_bytes + 16;
-  pl.stage_bytes = 2 * pl.R * pl.pitch;
-  pl.stages = (kSmemBudget - kBarrierBytes) / pl.stage_bytes;
-  if (pl.stages > kMaxStages) pl.stages = kMaxStages;
-  pl.smem = kBarrierBytes + pl.stages * pl.stage_bytes;
+  if (!pl.W) return fail(NF_EUNSUPPORTED, "nf_paged_attention: head rows of %d bytes do not fit the pipeline", pl.head_bytes);
+  pl.smem = pl.W * (pl.stages * pl.stage_bytes + kFifoBytes);
   return ok();
 }
 
-template <typename T, int D_, bool MMA, int DPL>
-static int launch_attn(const AttnParams& p, const Plan& pl, int grid, cudaStream_t st) {
-  auto kern = paged_attention_kernel<T, D_, MMA, DPL>;
+template <typename T, int D_, int MT, bool MMA, int DPL>
+static int launch_attn(const AttnParams& p, const Plan& pl, long long want, cudaStream_t st) {
+  auto kern = paged_attention_kernel<T, D_, MT, MMA, DPL>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, pl.smem);
   if (e != cudaSuccess) return fail(NF_ECUDA, "nf_paged_attention: smem attribute: %s", cudaGetErrorString(e));
-  kern<<<grid, (pl.W + 1) * 32, pl.smem, st>>>(p);
+  int per_sm = 1;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, pl.W * 32, pl.smem) != cudaSuccess || per_sm < 1)
+    per_sm = 1;
+  long long grid = (long long)sm_count() * per_sm;
+  const long long need = (want + pl.W - 1) / pl.W;  // no more warps than work items
+  if (need < grid) grid = need;
+  if (grid < 1) grid = 1;
+  kern<<<(int)grid, pl.W * 32, pl.smem, st>>>(p);
   return check_launch("nf_paged_attention");
 }
 
 template <typename T>
-static int dispatch_attn(const AttnParams& p, const Plan& pl, int grid, cudaStream_t st) {
+static int dispatch_attn(const AttnParams& p, const Plan& pl, long long want, cudaStream_t st) {
   if constexpr (!std::is_same<T, float>::value) {
-    if (pl.mma && p.D == 64) return launch_attn<T, 64, true, 2>(p, pl, grid, st);
-    if (pl.mma && p.D == 128) return launch_attn<T, 128, true, 4>(p, pl, grid, st);
+    if (pl.mma && p.D == 64)
+      return pl.tile == 32 ? launch_attn<T, 64, 2, true, 2>(p, pl, want, st) : launch_attn<T, 64, 1, true, 2>(p, pl, want, st);
+    if (pl.mma && p.D == 128)
+      return pl.tile == 32 ? launch_attn<T, 128, 2, true, 4>(p, pl, want, st) : launch_attn<T, 128, 1, true, 4>(p, pl, want, st);
   }
   switch (pl.dpl) {
-    case 1: return launch_attn<T, 0, false, 1>(p, pl, grid, st);
-    case 2: return launch_attn<T, 0, false, 2>(p, pl, grid, st);
-    case 4: return launch_attn<T, 0, false, 4>(p, pl, grid, st);
-    default: return launch_attn<T, 0, false, 8>(p, pl, grid, st);
+    case 1: return launch_attn<T, 0, 1, false, 1>(p, pl, want, st);
+    case 2: return launch_attn<T, 0, 1, false, 2>(p, pl, want, st);
+    case 4: return launch_attn<T, 0, 1, false, 4>(p, pl, want, st);
+    default: return launch_attn<T, 0, 1, false, 8>(p, pl, want, st);
   }
 }
 
@@ -535,12 +803,12 @@ extern "C" int nf_attention_workspace(int32_t max_units, int32_t max_items, int3
                                       int64_t* partial_floats, int64_t* counter_ints) {
   using namespace nf;
   Plan pl;
-  int rc = make_plan(dtype, num_q_heads, num_kv_heads, head_dim, pl);
+  int rc = make_plan(dtype, num_q_heads, num_kv_heads, head_dim, true, pl);
   if (rc) return rc;
   if (max_units <= 0 || max_items <= 0 || !partial_floats || !counter_ints)
     return fail(NF_EINVAL, "nf_attention_workspace: bad arguments");
-  *partial_floats = (int64_t)max_units * pl.SUB * num_q_heads * (head_dim + 2);
-  *counter_ints = (int64_t)max_items * num_kv_heads;
+  *partial_floats = (int64_t)max_units * num_q_heads * (head_dim + 4);
+  *counter_ints = (int64_t)max_items * num_kv_heads + 2;
   return ok();
 }
 
@@ -552,23 +820,27 @@ extern "C" int nf_paged_attention(void* out, int64_t out_row_stride, const void*
                                   int32_t split_tokens, float scale, float* ws_partials, int64_t ws_partial_floats,
                                   int32_t* ws_counters, int64_t ws_counter_ints, int32_t* status, void* stream) {
   using namespace nf;
+  (void)items;  // unit records are self-contained; the argument stays for ABI stability
+  const size_t es = dtype_size(dtype);
+  auto al = [](const void* ptr, size_t a) { return (reinterpret_cast<uintptr_t>(ptr) % a) == 0; };
+  const bool q_smem_ok = es && al(q, 16) && (q_row_stride * (int64_t)es) % 16 == 0;
   Plan pl;
-  int rc = make_plan(dtype, num_q_heads, num_kv_heads, head_dim, pl);
+  int rc = make_plan(dtype, num_q_heads, num_kv_heads, head_dim, q_smem_ok, pl);
   if (rc) return rc;
-  if (!out || !q || !k_pool || !v_pool || !block_tables || !items || !units || !counts || !status)
+  if (!out || !q || !k_pool || !v_pool || !block_tables || !units || !counts || !status)
     return fail(NF_EINVAL, "nf_paged_attention: null pointer argument");
   if (block_size <= 0 || num_blocks <= 0 || max_blocks_per_seq <= 0 || max_units <= 0 || max_items <= 0)
     return fail(NF_EINVAL, "nf_paged_attention: sizes must be positive");
-  if (split_tokens <= 0 || split_tokens % pl.R != 0)
-    return fail(NF_EINVAL, "nf_paged_attention: split_tokens (%d) must be a positive multiple of %d", split_tokens, pl.R);
-  const int64_t need_p = (int64_t)max_units * pl.SUB * num_q_heads * (head_dim + 2);
-  const int64_t need_c = (int64_t)max_items * num_kv_heads;
+  if (split_tokens <= 0 || split_tokens % 16 != 0)
+    return fail(NF_EINVAL, "nf_paged_attention: split_tokens (%d) must be a positive multiple of 16", split_tokens);
+  const int64_t need_p = (int64_t)max_units * num_q_heads * (head_dim + 4);
+  const int64_t need_c = (int64_t)max_items * num_kv_heads + 2;
   if (!ws_partials || ws_partial_floats < need_p || !ws_counters || ws_counter_ints < need_c)
     return fail(NF_EINVAL, "nf_paged_attention: workspace too small (need %lld floats, %lld counters)",
                 (long long)need_p, (long long)need_c);
-  const size_t es = dtype_size(dtype);
-  auto al = [](const void* ptr, size_t a) { return (reinterpret_cast<uintptr_t>(ptr) % a) == 0; };
   if (!al(k_pool, 16) || !al(v_pool, 16)) return fail(NF_EINVAL, "nf_paged_attention: pools must be 16-byte aligned");
+  if (!al(units, 16)) return fail(NF_EINVAL, "nf_paged_attention: units must be 16-byte aligned");
+  if (!al(ws_partials, 16)) return fail(NF_EINVAL, "nf_paged_attention: partials must be 16-byte aligned");
   if (pl.mma && (!al(q, 4) || (q_row_stride * (int64_t)es) % 4 != 0))
     return fail(NF_EINVAL, "nf_paged_attention: q rows must be 4-byte aligned");
   AttnParams p;
@@ -586,7 +858,6 @@ extern "C" int nf_paged_attention(void* out, int64_t out_row_stride, const void*
   p.num_blocks = num_blocks;
   p.bt = block_tables;
   p.max_blocks = max_blocks_per_seq;
-  p.items = items;
   p.units = units;
   p.counts = counts;
   p.max_units = max_units;
@@ -594,25 +865,22 @@ extern "C" int nf_paged_attention(void* out, int64_t out_row_stride, const void*
   p.scale_log2 = scale * 1.4426950408889634f;
   p.ws = ws_partials;
   p.cnt = ws_counters;
+  p.queue = ws_counters + (int64_t)max_items * num_kv_heads;
   p.status = status;
-  p.HG = pl.HG;
-  p.SUB = pl.SUB;
   p.W = pl.W;
-  p.n_hg = pl.n_hg;
   p.stages = pl.stages;
-  p.R = pl.R;
-  p.pitch = pl.pitch;
-  p.row_bytes = pl.row_bytes;
+  p.head_bytes = pl.head_bytes;
   p.stage_bytes = pl.stage_bytes;
-  long long want = (long long)max_units * pl.n_hg;
-  int grid = sm_count();
-  if (want < grid) grid = (int)want;
-  if (grid < 1) grid = 1;
+  p.swz = pl.swz;
+  p.tile = pl.tile;
+  p.bs16 = block_size % 16 == 0;
+  p.q_smem = pl.q_smem;
+  const long long want = (long long)max_units * num_kv_heads;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   switch (dtype) {
-    case NF_F32: return dispatch_attn<float>(p, pl, grid, st);
-    case NF_F16: return dispatch_attn<__half>(p, pl, grid, st);
-    case NF_BF16: return dispatch_attn<__nv_bfloat16>(p, pl, grid, st);
+    case NF_F32: return dispatch_attn<float>(p, pl, want, st);
+    case NF_F16: return dispatch_attn<__half>(p, pl, want, st);
+    case NF_BF16: return dispatch_attn<__nv_bfloat16>(p, pl, want, st);
   }
   return fail(NF_EINVAL, "nf_paged_attention: bad dtype %d", dtype);
 }

@@ -130,15 +130,16 @@ __global__ void __launch_bounds__(kPackThreads) pack_kernel(const PackParams p) 
   __syncthreads();
   // 4. unit base of each item: scan of the split counts.
   const int n_units = cta_exclusive_scan(p.items + 3, T, 4);
-  // 5. the unit list, one (item, split) per key range.
+  // 5. the unit list: one self-contained record per key range of an item.
   for (int t = tid; t < T; t += kPackThreads) {
     const int4 it = reinterpret_cast<const int4*>(p.items)[t];
     const int n = (it.z + p.split - 1) / p.split;
     for (int j = 0; j < n; ++j) {
       const int u = it.w + j;
       if (u < p.max_units) {
-        p.units[2 * u] = t;
-        p.units[2 * u + 1] = j;
+        int4* rec = reinterpret_cast<int4*>(p.units) + 2 * u;
+        rec[0] = make_int4(t, it.x, it.y, it.z);
+        rec[1] = make_int4(j * p.split, min((j + 1) * p.split, it.z), it.w, n);
       }
     }
   }
@@ -165,7 +166,8 @@ extern "C" int nf_pack_step(const int32_t* seqs, int32_t n_seqs, const int32_t* 
   if (block_size <= 0 || split_tokens <= 0 || num_slots <= 0 || max_blocks_per_seq <= 0 || num_blocks <= 0)
     return fail(NF_EINVAL, "nf_pack_step: sizes must be positive");
   if (max_units <= 0) return fail(NF_EINVAL, "nf_pack_step: max_units must be positive");
-  if ((reinterpret_cast<uintptr_t>(items) & 15) != 0) return fail(NF_EINVAL, "nf_pack_step: items must be 16-byte aligned");
+  if ((reinterpret_cast<uintptr_t>(items) & 15) != 0 || (reinterpret_cast<uintptr_t>(units) & 15) != 0)
+    return fail(NF_EINVAL, "nf_pack_step: items and units must be 16-byte aligned");
   const size_t smem = sizeof(int) * (size_t)(n_seqs + 1);
   if (smem > 200 * 1024) return fail(NF_EINVAL, "nf_pack_step: too many sequences (%d)", n_seqs);
   if (smem > 48 * 1024) cudaFuncSetAttribute(pack_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);

@@ -268,7 +268,7 @@ class PagedKVCache:
         off_src = off_slot + T
         off_items = _align4(off_src + T)
         off_units = off_items + 4 * T
-        off_counts = off_units + 2 * max_units
+        off_counts = off_units + _lib.UNIT_FIELDS * max_units
         meta = self._meta.get(off_counts + 4)
         meta[: host.size].copy_(torch.from_numpy(host).pin_memory(), non_blocking=True)
         pos_dev = self._pos_buf.get(T)
@@ -278,7 +278,7 @@ class PagedKVCache:
         plan.slot_mapping = meta[off_slot: off_slot + T]
         plan.src_rows = meta[off_src: off_src + T]
         plan.items = meta[off_items: off_items + 4 * T]
-        plan.units = meta[off_units: off_units + 2 * max_units]
+        plan.units = meta[off_units: off_units + _lib.UNIT_FIELDS * max_units]
         plan.counts = meta[off_counts: off_counts + 2]
         plan.positions = pos_dev[:T]
         lib = _lib.load()

@@ -199,7 +199,7 @@ def test_library_exports_every_declared_symbol():
     for s in syms:
         assert hasattr(lib, s), s
     assert set(_lib.EXPORTS) <= set(syms)
-    assert _lib.load().nf_abi_version() == 1
+    assert _lib.load().nf_abi_version() == 2
 
 
 def test_workspace_sizing_and_argument_errors():
@@ -207,9 +207,9 @@ def test_workspace_sizing_and_argument_errors():
     from nifre_b200 import _lib
     import torch
     pf, ci = _lib.workspace_sizes(100, 64, 32, 8, 64, torch.bfloat16)
-    assert pf == 100 * 1 * 32 * 66 and ci == 64 * 8
-    pf, ci = _lib.workspace_sizes(10, 4, 8, 1, 128, torch.bfloat16)  # one KV head: 8 sub-tiles per stage
-    assert pf == 10 * 8 * 8 * 130
+    assert pf == 100 * 32 * 68 and ci == 64 * 8 + 2  # (acc, m, l, pad) per part; counters + work queue
+    pf, ci = _lib.workspace_sizes(10, 4, 8, 1, 128, torch.bfloat16)
+    assert pf == 10 * 8 * 132 and ci == 4 + 2
     with pytest.raises(_lib.NifreError, match="multiple of num_kv_heads"):
         _lib.workspace_sizes(1, 1, 6, 4, 64, torch.bfloat16)
     with pytest.raises(_lib.NifreError, match="more than 8"):
