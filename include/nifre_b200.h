@@ -143,6 +143,36 @@ int nf_paged_attention(void* out, int64_t out_row_stride,
                        int32_t* ws_counters, int64_t ws_counter_ints,
                        int32_t* status, void* stream);
 
+/*
+ * nf_paged_attention_noalloc: nf_paged_attention without a caller workspace.
+ * This entry point has no counterpart in the reference.  It is for callers
+ * that cannot allocate device memory themselves -- for example a host binding
+ * that only borrows the tensors of another runtime, or a server whose device
+ * memory is entirely reserved by its own pool -- and so cannot pass
+ * ws_partials / ws_counters.  The split-K scratch is instead a buffer of
+ * NF_NOALLOC_SCRATCH_BYTES compiled into this library (every GPU that loads
+ * the library holds it until the process exits).  The call allocates
+ * nothing: the first call on a device looks up that buffer's device address
+ * (so make that first call before any stream capture), and every call clears
+ * the buffer's counters with cudaMemsetAsync on `stream`.  A step whose
+ * scratch (max_units * num_q_heads * (head_dim + 4) floats, rounded up to
+ * 256 bytes, plus max_items * num_kv_heads + 2 ints) exceeds the buffer is
+ * rejected with NF_EINVAL.  All calls share the one buffer: calls that
+ * overlap on the GPU (other streams, other threads) race and give wrong
+ * results.  Arguments and results are otherwise those of nf_paged_attention.
+ */
+#define NF_NOALLOC_SCRATCH_BYTES (16u << 20)
+
+int nf_paged_attention_noalloc(void* out, int64_t out_row_stride,
+                               const void* q, int64_t q_row_stride,
+                               const void* k_pool, const void* v_pool, int32_t dtype,
+                               int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                               int32_t block_size, int32_t num_blocks,
+                               const int32_t* block_tables, int32_t max_blocks_per_seq,
+                               const int32_t* items, const int32_t* units, const int32_t* counts,
+                               int32_t max_items, int32_t max_units, int32_t split_tokens, float scale,
+                               int32_t* status, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -25,7 +25,7 @@ SEQ_FIELDS, PATCH_FIELDS, ITEM_FIELDS, UNIT_FIELDS = 4, 3, 4, 8
 _DTYPE_CODE = {torch.float32: NF_F32, torch.float16: NF_F16, torch.bfloat16: NF_BF16}
 
 EXPORTS = ("nf_last_error", "nf_abi_version", "nf_pack_step", "nf_kv_append",
-           "nf_attention_workspace", "nf_paged_attention")
+           "nf_attention_workspace", "nf_paged_attention", "nf_paged_attention_noalloc")
 
 _P = ctypes.c_void_p
 _I32 = ctypes.c_int32
@@ -43,6 +43,9 @@ _SIGNATURES = {
     "nf_paged_attention": ([_P, _I64, _P, _I64, _P, _P, _I32, _I32, _I32, _I32, _I32, _I32,
                             _P, _I32, _P, _P, _P, _I32, _I32, _I32, ctypes.c_float,
                             _P, _I64, _P, _I64, _P, _P], ctypes.c_int),
+    "nf_paged_attention_noalloc": ([_P, _I64, _P, _I64, _P, _P, _I32, _I32, _I32, _I32, _I32, _I32,
+                                    _P, _I32, _P, _P, _P, _I32, _I32, _I32, ctypes.c_float,
+                                    _P, _P], ctypes.c_int),
 }
 
 

@@ -884,3 +884,59 @@ extern "C" int nf_paged_attention(void* out, int64_t out_row_stride, const void*
   }
   return fail(NF_EINVAL, "nf_paged_attention: bad dtype %d", dtype);
 }
+
+// ---------------------------------------------------------------- allocation-free variant
+// Scratch for nf_paged_attention_noalloc: split-K partials followed by the
+// part counters and the work queue.  It lives in this library's image, so
+// every GPU that loads the library keeps these bytes until the process ends.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[NF_NOALLOC_SCRATCH_BYTES];
+
+namespace nf {
+// Device address of g_noalloc_scratch per device, looked up on the first call
+// made with that device current (host code cannot use the symbol itself: on
+// the host it names a stand-in, not device memory).
+static void* g_noalloc_ptr[64] = {nullptr};
+}  // namespace nf
+
+extern "C" int nf_paged_attention_noalloc(void* out, int64_t out_row_stride, const void* q, int64_t q_row_stride,
+                                          const void* k_pool, const void* v_pool, int32_t dtype,
+                                          int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                                          int32_t block_size, int32_t num_blocks, const int32_t* block_tables,
+                                          int32_t max_blocks_per_seq, const int32_t* items, const int32_t* units,
+                                          const int32_t* counts, int32_t max_items, int32_t max_units,
+                                          int32_t split_tokens, float scale, int32_t* status, void* stream) {
+  using namespace nf;
+  if (max_units <= 0 || max_items <= 0 || num_q_heads <= 0 || num_kv_heads <= 0 || head_dim <= 0)
+    return fail(NF_EINVAL, "nf_paged_attention_noalloc: sizes must be positive");
+  const int64_t part_floats = (int64_t)max_units * num_q_heads * (head_dim + 4);
+  const int64_t cnt_ints = (int64_t)max_items * num_kv_heads + 2;
+  const int64_t part_bytes = ((part_floats * 4 + 255) / 256) * 256;
+  const int64_t need = part_bytes + cnt_ints * 4;
+  if (need > (int64_t)NF_NOALLOC_SCRATCH_BYTES)
+    return fail(NF_EINVAL,
+                "nf_paged_attention_noalloc: this step needs %lld bytes of scratch, the built-in buffer holds %lld "
+                "(use nf_paged_attention with a caller-owned workspace, or a larger split_tokens)",
+                (long long)need, (long long)NF_NOALLOC_SCRATCH_BYTES);
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(NF_ECUDA, "nf_paged_attention_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= 64) return fail(NF_EUNSUPPORTED, "nf_paged_attention_noalloc: device index %d", dev);
+  if (!g_noalloc_ptr[dev]) {
+    void* ptr = nullptr;
+    e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (e != cudaSuccess || !ptr)
+      return fail(NF_ECUDA, "nf_paged_attention_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+    g_noalloc_ptr[dev] = ptr;
+  }
+  unsigned char* base = static_cast<unsigned char*>(g_noalloc_ptr[dev]);
+  float* partials = reinterpret_cast<float*>(base);
+  int32_t* counters = reinterpret_cast<int32_t*>(base + part_bytes);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // counters and the work queue must start at zero; the partials need no clearing
+  e = cudaMemsetAsync(counters, 0, cnt_ints * 4, st);
+  if (e != cudaSuccess) return fail(NF_ECUDA, "nf_paged_attention_noalloc: clearing counters: %s", cudaGetErrorString(e));
+  return nf_paged_attention(out, out_row_stride, q, q_row_stride, k_pool, v_pool, dtype, num_q_heads, num_kv_heads,
+                            head_dim, block_size, num_blocks, block_tables, max_blocks_per_seq, items, units, counts,
+                            max_items, max_units, split_tokens, scale, partials, part_floats, counters, cnt_ints,
+                            status, stream);
+}
