@@ -283,6 +283,8 @@ def run_ours(args):
         kv = int(p.kv_lens.sum())
         nblk = int(((p.kv_lens + bs - 1) // bs).sum())
         att_bytes.append(kv * hkv * D * 2 * 2 + 2 * B * hq * D * 2 + 4 * nblk + 16 * B)
+    from nifre_b200 import _lib
+    att_path = _lib.load().nf_last_attention_path()
     att_avg_ms = sum(att_ms) / len(att_ms)
     achieved = (sum(att_bytes) / len(att_bytes)) / (att_avg_ms * 1e-3) / 1e9
     peak, peak_kind = _peaks()
@@ -355,6 +357,8 @@ def run_ours(args):
                          "traffic": ATTN_TRAFFIC_RATIO * sum(att_bytes) / len(att_bytes),
                          "traffic_source": "ncu capture of the 1-layer case, scaled by keys read",
                          "kernel": "nf_paged_attention",
+                         "kernel_path": {0: "per-warp cp.async", 1: "tensor map, one copy per block",
+                                         2: "tensor map, one copy per head"}.get(att_path, str(att_path)),
                          "peak_source": peak_kind, "avg_launch_us": att_avg_ms * 1e3},
             "cpu_baseline": cpu,
             "e2e": e2e,

@@ -67,6 +67,15 @@ const char* nf_last_error(void);
 int nf_abi_version(void);
 
 /*
+ * Which kernel the last nf_paged_attention call of this thread launched:
+ * 0 = per-warp cp.async staging (any dtype and shape),
+ * 1 = tensor-map (TMA) staging, one copy per 16-token block for all heads of
+ *     a CTA, 2 = tensor-map staging with one copy per head; -1 = none yet.
+ * A diagnostic with no counterpart in the reference.
+ */
+int nf_last_attention_path(void);
+
+/*
  * nf_pack_step: expand one step's ragged batch on the device.
  *
  * seqs[n_seqs][4]      (device) slot, q_start, q_len, ctx_before of each

@@ -25,7 +25,8 @@ SEQ_FIELDS, PATCH_FIELDS, ITEM_FIELDS, UNIT_FIELDS = 4, 3, 4, 8
 _DTYPE_CODE = {torch.float32: NF_F32, torch.float16: NF_F16, torch.bfloat16: NF_BF16}
 
 EXPORTS = ("nf_last_error", "nf_abi_version", "nf_pack_step", "nf_kv_append",
-           "nf_attention_workspace", "nf_paged_attention", "nf_paged_attention_noalloc")
+           "nf_attention_workspace", "nf_paged_attention", "nf_paged_attention_noalloc",
+           "nf_last_attention_path")
 
 _P = ctypes.c_void_p
 _I32 = ctypes.c_int32
@@ -34,6 +35,7 @@ _I64 = ctypes.c_int64
 _SIGNATURES = {
     "nf_last_error": ([], ctypes.c_char_p),
     "nf_abi_version": ([], ctypes.c_int),
+    "nf_last_attention_path": ([], ctypes.c_int),
     "nf_pack_step": ([_P, _I32, _P, _I32, _P, _I32, _I32, _I32, _I32, _I32,
                       _P, _P, _P, _P, _P, _P, _I32, _I32, _P, _P], ctypes.c_int),
     "nf_kv_append": ([_P, _P, _I32, _I64, _P, _P, _I32, _I64, _I64, _P, _P, _I32,

@@ -8,6 +8,9 @@
 namespace nf {
 
 static thread_local char g_err[512] = "";
+static thread_local int g_attention_path = -1;
+
+void set_attention_path(int path) { g_attention_path = path; }
 
 int fail(int code, const char* fmt, ...) {
   va_list ap;
@@ -54,4 +57,6 @@ size_t dtype_size(int dtype) {
 
 extern "C" const char* nf_last_error(void) { return nf::g_err; }
 
-extern "C" int nf_abi_version(void) { return 2; }
+extern "C" int nf_abi_version(void) { return 3; }
+
+extern "C" int nf_last_attention_path(void) { return nf::g_attention_path; }

@@ -1,0 +1,389 @@
+// Paged attention with tensor-map (TMA) staging of whole key blocks.
+//
+// Same computation and work records as nf_attention.cu (see there for the
+// reference mapping: attention.py:106-152 over the paged_kv_cache.py pools);
+// this file only changes how keys reach shared memory, for 16-bit pools with
+// head_dim 64 or 128 and a block size that is a multiple of 16.
+//
+// A CTA owns HG KV heads.  Its producer warp takes (unit, head group) work
+// items from the queue and, for each 16-key step of a unit, issues one TMA
+// tensor copy for K and one for V: the box is 16 tokens of one block x HG
+// heads x head_dim, read through a tensor map whose dimensions are
+// (head_dim, token in block, head, block) -- strides 2 B, Hkv*D*2, D*2,
+// bs*Hkv*D*2 -- so the copy lands head-major: for every head, 16 rows of
+// 128 bytes (two such halves for head_dim 128) with the hardware 128-byte
+// swizzle, which is the bank-conflict-free layout the ldmatrix fragment
+// loads expect.  Two requests move 16 KB (head_dim 64, 8 heads) where
+// per-row copies needed 256 instructions per lane-set.  If the driver refuses
+// that permuted-stride map, a map with increasing strides and one box per
+// head (and per 64-element half of the head) gives the same layout.
+//
+// Consumer warp h computes KV head h of the group exactly as the per-warp
+// path does (mma.sync S^T = K Q^T, online softmax, O^T += V^T P^T, split-K
+// parts and merge).  Every wait is an mbarrier wait with a time limit: a wait
+// that runs out sets NF_STATUS_WAIT_TIMEOUT and the warp leaves its loop.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include "nf_attn_common.cuh"
+#include "nf_internal.h"
+
+namespace nf {
+
+constexpr int kTmaHeader = 1024;  // mbarriers (full[8] at 0, empty[8] at 64) + step records at 128
+constexpr int kTmaMaxStages = 8;
+
+struct StepRec {  // one 16-key step as the producer describes it to the consumers
+  int u, item, q_row, t0, t1, unit_base, nsplits, hg, t, first, last, pad[5];
+};
+
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2, int c3,
+                                            uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], "
+      "[%6];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_5d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2, int c3,
+                                            int c4, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5, "
+      "%6}], [%7];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4), "r"(bar)
+      : "memory");
+}
+
+// Byte offset of key row r, 16-byte chunk c, in one head's staged tile:
+// [d_hi][16 rows][128 B], chunks XOR-swizzled by the row (the TMA 128B mode).
+__device__ __forceinline__ int tma_off(int r, int c) {
+  return (c >> 3) * 2048 + r * 128 + (((c & 7) ^ (r & 7)) << 4);
+}
+
+template <typename T, int D_>
+__device__ void tma_producer(const AttnParams& p, const CUtensorMap* tk, const CUtensorMap* tv, unsigned char* base,
+                             int total, int box_bytes, int q_bytes) {
+  constexpr int NDH = D_ / 64;  // 64-element halves of a head row
+  const uint32_t hdr = smem_u32(base);
+  auto full = [&](int s) { return hdr + 8 * s; };
+  auto empty = [&](int s) { return hdr + 64 + 8 * s; };
+  StepRec* recs = reinterpret_cast<StepRec*>(base + 128);
+  const uint32_t stage0 = hdr + kTmaHeader;
+  const int S = p.stages;
+  int k = 0;
+  bool ok = true;
+  while (ok) {
+    const int w = atomicAdd(p.queue, 1);
+    if (w >= total) break;
+    const int u = w / p.n_hg, hg = w - u * p.n_hg;
+    const int4 ra = __ldg(reinterpret_cast<const int4*>(p.units) + 2 * u);
+    const int4 rb = __ldg(reinterpret_cast<const int4*>(p.units) + 2 * u + 1);
+    const int* btrow = p.bt + (long long)ra.y * p.max_blocks;
+    const int h0 = hg * p.HG;
+    for (int t = rb.x; t < rb.y; t += 16, ++k) {
+      const int s = k % S, round = k / S;
+      if (!mbar_wait(empty(s), (round & 1) ^ 1, p.status)) {
+        ok = false;
+        break;
+      }
+      StepRec& r = recs[s];
+      r.u = u; r.item = ra.x; r.q_row = ra.z; r.t0 = rb.x; r.t1 = rb.y; r.unit_base = rb.z;
+      r.nsplits = rb.w; r.hg = hg; r.t = t; r.first = t == rb.x; r.last = t + 16 >= rb.y;
+      const int lb = t / p.bs, off = t - lb * p.bs;
+      const int phys = checked_block(p, btrow, lb);
+      const uint32_t sb = stage0 + s * p.stage_bytes;
+      mbar_arrive_expect_tx(full(s), 2 * box_bytes + (r.first ? q_bytes : 0));
+      if (p.swz) {  // permuted-stride map: one box = 16 tokens x HG heads
+        if constexpr (D_ == 64) {
+          tma_load_4d(sb, tk, 0, off, h0, phys, full(s));
+          tma_load_4d(sb + box_bytes, tv, 0, off, h0, phys, full(s));
+        } else {
+          tma_load_5d(sb, tk, 0, off, 0, h0, phys, full(s));
+          tma_load_5d(sb + box_bytes, tv, 0, off, 0, h0, phys, full(s));
+        }
+      } else {  // increasing-stride map: one box per head (and per half of a 128-wide head)
+        for (int h = 0; h < p.HG; ++h)
+#pragma unroll
+          for (int dh = 0; dh < NDH; ++dh) {
+            const uint32_t d = sb + (h * NDH + dh) * 2048;
+            if constexpr (D_ == 64) {
+              tma_load_4d(d, tk, 0, h0 + h, off, phys, full(s));
+              tma_load_4d(d + box_bytes, tv, 0, h0 + h, off, phys, full(s));
+            } else {
+              tma_load_5d(d, tk, 0, dh, h0 + h, off, phys, full(s));
+              tma_load_5d(d + box_bytes, tv, 0, dh, h0 + h, off, phys, full(s));
+            }
+          }
+      }
+      if (r.first) {
+        const char* qrow = p.q + ((long long)ra.z * p.q_stride + (long long)h0 * p.G * p.D) * (long long)sizeof(T);
+        bulk_g2s(sb + 2 * box_bytes, qrow, q_bytes, full(s));
+      }
+    }
+  }
+  if (ok) {
+    // end of work: a record with u = -1, published by a plain arrive
+    const int s = k % S, round = k / S;
+    if (mbar_wait(empty(s), (round & 1) ^ 1, p.status)) {
+      recs[s].u = -1;
+      mbar_arrive(full(s));
+      retire_worker(p, gridDim.x);
+      return;
+    }
+  }
+  // a wait ran out: leave no copy in flight into this CTA's shared memory
+  for (int j = max(0, k - S); j < k; ++j) mbar_wait(full(j % S), (j / S) & 1, p.status);
+}
+
+template <typename T, int D_>
+__device__ void tma_consumer(const AttnParams& p, unsigned char* base, int box_bytes) {
+  constexpr int KS = D_ / 16;
+  constexpr int NDH = D_ / 64;
+  constexpr int HB = D_ * 2;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t hdr = smem_u32(base);
+  const StepRec* recs = reinterpret_cast<const StepRec*>(base + 128);
+  const uint32_t stage0 = hdr + kTmaHeader;
+  const int S = p.stages;
+  const int n0 = 2 * (lane & 3), tq = lane >> 2;
+  const bool has = tq < p.G;
+  const int kr = (lane & 7) + ((lane >> 3) & 1) * 8, kc = lane >> 4;
+  const int vr = (lane & 7) + ((lane >> 4) & 1) * 8, vc = (lane >> 3) & 1;
+  const int head_region = warp * NDH * 2048;
+  uint32_t qf[KS][2];
+  float m0 = kNegInf, m1 = kNegInf, l0 = 0.f, l1 = 0.f;
+  float o[KS][4];
+  for (int k = 0;; ++k) {
+    const int s = k % S, round = k / S;
+    if (!mbar_wait(hdr + 8 * s, round & 1, p.status)) return;
+    const StepRec r = recs[s];
+    if (r.u < 0) return;
+    const uint32_t sb = stage0 + s * p.stage_bytes;
+    const uint32_t kb = sb + head_region, vb = sb + box_bytes + head_region;
+    if (r.first) {
+      const uint32_t qs = sb + 2 * box_bytes + (warp * p.G + tq) * HB + n0 * 2;
+#pragma unroll
+      for (int ks = 0; ks < KS; ++ks) {
+        qf[ks][0] = has ? lds32(qs + ks * 32) : 0u;
+        qf[ks][1] = has ? lds32(qs + ks * 32 + 16) : 0u;
+      }
+      m0 = m1 = kNegInf;
+      l0 = l1 = 0.f;
+#pragma unroll
+      for (int i = 0; i < KS; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+    }
+    const int nv = min(16, r.t1 - r.t);
+    if (nv < 16) {
+      // rows past the unit's end hold whatever the block holds: zero them in V
+      // (their scores are masked, but 0 * NaN would still poison the sum)
+      for (int idx = lane; idx < (16 - nv) * NDH * 8; idx += 32) {
+        const int row = nv + idx / (NDH * 8), rest = idx % (NDH * 8);
+        const uint32_t a = vb + (rest >> 3) * 2048 + row * 128 + (rest & 7) * 16;
+        asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(a), "r"(0) : "memory");
+      }
+      __syncwarp();
+    }
+    float sc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int ks = 0; ks < KS; ++ks) {
+      uint32_t a0, a1, a2, a3;
+      ldsm_x4(kb + tma_off(kr, 2 * ks + kc), a0, a1, a2, a3);
+      mma16816<T>(sc, a0, a1, a2, a3, qf[ks][0], qf[ks][1]);
+    }
+    const bool v0 = tq < nv, v1 = tq + 8 < nv;
+    const float x0 = v0 ? sc[0] * p.scale_log2 : kNegInf;
+    const float x1 = v0 ? sc[1] * p.scale_log2 : kNegInf;
+    const float x2 = v1 ? sc[2] * p.scale_log2 : kNegInf;
+    const float x3 = v1 ? sc[3] * p.scale_log2 : kNegInf;
+    float mx0 = fmaxf(x0, x2), mx1 = fmaxf(x1, x3);
+#pragma unroll
+    for (int o_ = 4; o_ < 32; o_ <<= 1) {
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o_));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o_));
+    }
+    const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+    const float b0 = mn0 == kNegInf ? 0.f : mn0, b1 = mn1 == kNegInf ? 0.f : mn1;
+    const float al0 = ex2(m0 - b0), al1 = ex2(m1 - b1);
+    const float p0 = ex2(x0 - b0), p1 = ex2(x1 - b1), p2 = ex2(x2 - b0), p3 = ex2(x3 - b1);
+    l0 = l0 * al0 + p0 + p2;
+    l1 = l1 * al1 + p1 + p3;
+    m0 = mn0;
+    m1 = mn1;
+    const uint32_t pb0 = movmatrix_t(pack2<T>(p0, p1));
+    const uint32_t pb1 = movmatrix_t(pack2<T>(p2, p3));
+#pragma unroll
+    for (int i = 0; i < KS; ++i) {
+      o[i][0] *= al0;
+      o[i][1] *= al1;
+      o[i][2] *= al0;
+      o[i][3] *= al1;
+      uint32_t a0, a1, a2, a3;
+      ldsm_x4_t(vb + tma_off(vr, 2 * i + vc), a0, a1, a2, a3);
+      mma16816<T>(o[i], a0, a1, a2, a3, pb0, pb1);
+    }
+    // release the slot (the tail zeroing wrote with the generic proxy: order it
+    // before the next tensor copy into this slot)
+    if (nv < 16) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    __syncwarp();
+    if (lane == 0) mbar_arrive(hdr + 64 + 8 * s);
+    if (r.last) {
+#pragma unroll
+      for (int o_ = 4; o_ < 32; o_ <<= 1) {
+        l0 += __shfl_xor_sync(0xffffffffu, l0, o_);
+        l1 += __shfl_xor_sync(0xffffffffu, l1, o_);
+      }
+      Work c;
+      c.w = 0;
+      c.u = r.u;
+      c.item = r.item;
+      c.slot = 0;
+      c.q_row = r.q_row;
+      c.t0 = r.t0;
+      c.t1 = r.t1;
+      c.unit_base = r.unit_base;
+      c.nparts = r.nsplits;
+      c.kvh = r.hg * p.HG + warp;
+      mma_epilogue<T, D_>(p, c, o, m0, m1, l0, l1);
+    }
+  }
+}
+
+template <typename T, int D_>
+__global__ void __launch_bounds__(288, 1) paged_attention_tma_kernel(const AttnParams p,
+                                                                  const __grid_constant__ CUtensorMap tk,
+                                                                  const __grid_constant__ CUtensorMap tv) {
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5;
+  const int box_bytes = p.HG * 16 * D_ * 2;
+  const int q_bytes = p.HG * p.G * D_ * 2;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < p.stages; ++s) {
+      mbar_init(smem_u32(base) + 8 * s, 1);
+      mbar_init(smem_u32(base) + 64 + 8 * s, p.HG);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+  const int n_units = min(__ldg(p.counts + 1), p.max_units);
+  const int total = n_units * p.n_hg;
+  if (warp == p.HG) {
+    if ((threadIdx.x & 31) == 0) tma_producer<T, D_>(p, &tk, &tv, base, total, box_bytes, q_bytes);
+  } else {
+    tma_consumer<T, D_>(p, base, box_bytes);
+  }
+}
+
+// ---------------------------------------------------------------- host side
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }
+  return fn;
+}
+
+// Tensor map over one pool (num_blocks, bs, Hkv, D).  permuted: dims
+// (d_lo, token, [d_hi,] head, block) with a box of 16 tokens x hg heads;
+// else increasing strides (d_lo, [d_hi,] head, token, block), box of one head.
+static bool encode_pool_map(CUtensorMap* map, const void* pool, int dtype, int D, int Hkv, int bs, int num_blocks,
+                            int hg, bool permuted) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  const CUtensorMapDataType dt = dtype == NF_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const cuuint64_t row = (cuuint64_t)Hkv * D * 2, head = (cuuint64_t)D * 2, blk = (cuuint64_t)bs * row;
+  cuuint64_t dims[5], strides[4];
+  cuuint32_t box[5], es[5] = {1, 1, 1, 1, 1};
+  cuuint32_t rank;
+  if (D == 64) {
+    rank = 4;
+    if (permuted) {
+      cuuint64_t d[4] = {64, (cuuint64_t)bs, (cuuint64_t)Hkv, (cuuint64_t)num_blocks};
+      cuuint64_t st[3] = {row, head, blk};
+      cuuint32_t b[4] = {64, 16, (cuuint32_t)hg, 1};
+      for (int i = 0; i < 4; ++i) { dims[i] = d[i]; box[i] = b[i]; }
+      for (int i = 0; i < 3; ++i) strides[i] = st[i];
+    } else {
+      cuuint64_t d[4] = {64, (cuuint64_t)Hkv, (cuuint64_t)bs, (cuuint64_t)num_blocks};
+      cuuint64_t st[3] = {head, row, blk};
+      cuuint32_t b[4] = {64, 1, 16, 1};
+      for (int i = 0; i < 4; ++i) { dims[i] = d[i]; box[i] = b[i]; }
+      for (int i = 0; i < 3; ++i) strides[i] = st[i];
+    }
+  } else {
+    rank = 5;
+    if (permuted) {
+      cuuint64_t d[5] = {64, (cuuint64_t)bs, 2, (cuuint64_t)Hkv, (cuuint64_t)num_blocks};
+      cuuint64_t st[4] = {row, 128, head, blk};
+      cuuint32_t b[5] = {64, 16, 2, (cuuint32_t)hg, 1};
+      for (int i = 0; i < 5; ++i) { dims[i] = d[i]; box[i] = b[i]; }
+      for (int i = 0; i < 4; ++i) strides[i] = st[i];
+    } else {
+      cuuint64_t d[5] = {64, 2, (cuuint64_t)Hkv, (cuuint64_t)bs, (cuuint64_t)num_blocks};
+      cuuint64_t st[4] = {128, head, row, blk};
+      cuuint32_t b[5] = {64, 1, 1, 16, 1};
+      for (int i = 0; i < 5; ++i) { dims[i] = d[i]; box[i] = b[i]; }
+      for (int i = 0; i < 4; ++i) strides[i] = st[i];
+    }
+  }
+  const CUresult r = fn(map, dt, rank, const_cast<void*>(pool), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// Launches the tensor-map kernel.  Returns NF_EUNSUPPORTED (nothing launched)
+// when the shape or the driver rules it out; the caller then uses the
+// per-warp cp.async kernel.
+int launch_attention_tma(AttnParams p, int dtype, long long want, cudaStream_t st, int* path) {
+  if (dtype != NF_BF16 && dtype != NF_F16) return NF_EUNSUPPORTED;
+  if ((p.D != 64 && p.D != 128) || p.bs % 16 != 0 || !p.q_smem || p.G > 8) return NF_EUNSUPPORTED;
+  if ((reinterpret_cast<uintptr_t>(p.kp) | reinterpret_cast<uintptr_t>(p.vp)) & 15) return NF_EUNSUPPORTED;
+  int hg = 0;
+  for (int h = p.Hkv < 8 ? p.Hkv : 8; h >= 1; --h)
+    if (p.Hkv % h == 0) {
+      hg = h;
+      break;
+    }
+  const int HB = p.D * 2;
+  const int box = hg * 16 * HB, qb = hg * p.G * HB;
+  const int stage = ((2 * box + qb + 1023) / 1024) * 1024;
+  int stages = (227 * 1024 - kTmaHeader - 1024) / stage;
+  if (stages > kTmaMaxStages) stages = kTmaMaxStages;
+  if (stages < 2) return NF_EUNSUPPORTED;
+  CUtensorMap tk, tv;
+  bool permuted = encode_pool_map(&tk, p.kp, dtype, p.D, p.Hkv, p.bs, p.num_blocks, hg, true) &&
+                  encode_pool_map(&tv, p.vp, dtype, p.D, p.Hkv, p.bs, p.num_blocks, hg, true);
+  if (!permuted && !(encode_pool_map(&tk, p.kp, dtype, p.D, p.Hkv, p.bs, p.num_blocks, hg, false) &&
+                     encode_pool_map(&tv, p.vp, dtype, p.D, p.Hkv, p.bs, p.num_blocks, hg, false)))
+    return NF_EUNSUPPORTED;
+  p.HG = hg;
+  p.n_hg = p.Hkv / hg;
+  p.stages = stages;
+  p.stage_bytes = stage;
+  p.swz = permuted ? 1 : 0;  // reused as "one box covers all heads of the group"
+  p.W = hg;
+  const int smem = kTmaHeader + stages * stage + 1024;  // + alignment slack
+  auto kern = (dtype == NF_BF16) ? (p.D == 64 ? paged_attention_tma_kernel<__nv_bfloat16, 64>
+                                              : paged_attention_tma_kernel<__nv_bfloat16, 128>)
+                                 : (p.D == 64 ? paged_attention_tma_kernel<__half, 64>
+                                              : paged_attention_tma_kernel<__half, 128>);
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return fail(NF_ECUDA, "nf_paged_attention: smem attribute: %s", cudaGetErrorString(e));
+  int per_sm = 1;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, (hg + 1) * 32, smem) != cudaSuccess || per_sm < 1)
+    per_sm = 1;
+  long long grid = (long long)sm_count() * per_sm;
+  const long long need = (want + p.Hkv - 1) / p.Hkv * p.n_hg;  // work items: units x head groups
+  if (need < grid) grid = need;
+  if (grid < 1) grid = 1;
+  kern<<<(int)grid, (hg + 1) * 32, smem, st>>>(p, tk, tv);
+  *path = permuted ? 1 : 2;
+  return check_launch("nf_paged_attention");
+}
+
+}  // namespace nf

@@ -13,4 +13,6 @@ int check_launch(const char* what);
 // Number of SMs of the current device (queried once per device).
 int sm_count();
 size_t dtype_size(int dtype);
+// Which attention kernel the calling thread launched last (see nf_last_attention_path).
+void set_attention_path(int path);
 }  // namespace nf
