@@ -495,7 +495,7 @@ __device__ void warp_simt(const AttnParams& p, uint32_t ring, unsigned char* rin
       }
     } else {
       const int DP = p.D + 4;
-      float* wb = p.ws + ((long long)c.u * p.Hq + c.kvh * p.G) * DP;
+      float* wb = p.ws + ((long long)part_index(p, c) * p.Hq + c.kvh * p.G) * DP;
 #pragma unroll
       for (int n = 0; n < 8; ++n) {
         if (n < p.G) {
@@ -510,7 +510,7 @@ __device__ void warp_simt(const AttnParams& p, uint32_t ring, unsigned char* rin
           }
         }
       }
-      finish_partial<T>(p, c);
+      finish_partial<T, 2>(p, c);
     }
   }
   cp_async_wait(0);

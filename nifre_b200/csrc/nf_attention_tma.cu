@@ -30,11 +30,21 @@
 
 namespace nf {
 
-constexpr int kTmaHeader = 1024;  // mbarriers (full[8] at 0, empty[8] at 64) + step records at 128
+// Shared-memory header: stage barriers (full[8] at 0, empty[8] at 64), step
+// records (8 x 64 B at 128), epilogue-ring barriers (full[3][2] at 640,
+// empty[3][2] at 704) and epilogue records (3 x 2 x 32 B at 768).
+constexpr int kTmaHeader = 1024;
 constexpr int kTmaMaxStages = 8;
+constexpr int kEpiWarps = 3, kEpiSlots = 2;
+constexpr int kEpiFull = 640, kEpiEmpty = 704, kEpiRec = 768;
+constexpr int kTmaMaxThreads = (8 + 1 + kEpiWarps) * 32;
 
 struct StepRec {  // one 16-key step as the producer describes it to the consumers
   int u, item, q_row, t0, t1, unit_base, nsplits, hg, t, first, last, pad[5];
+};
+
+struct EpiRec {  // one unit's split-K bookkeeping, handed to an epilogue warp
+  int item, q_row, unit_base, nparts, t0, hg, flag, pad;  // flag 0: no more units
 };
 
 __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2, int c3,
@@ -136,6 +146,22 @@ __device__ void tma_producer(const AttnParams& p, const CUtensorMap* tk, const C
   for (int j = max(0, k - S); j < k; ++j) mbar_wait(full(j % S), (j / S) & 1, p.status);
 }
 
+// Hands this warp's head of the j-th split unit of the CTA to epilogue warp
+// (warp % kEpiWarps), which serves consumer warps e, e + 3, ...: every
+// consumer warp calls it after storing its head's part, and the lowest warp
+// of the ring writes the record.  Returns false if a wait ran out.
+__device__ __forceinline__ bool epi_push(const AttnParams& p, unsigned char* base, int j, const EpiRec& x) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t hdr = smem_u32(base);
+  const int e = warp % kEpiWarps, round = j / kEpiSlots;
+  const int idx = e * kEpiSlots + j % kEpiSlots;
+  if (!mbar_wait(hdr + kEpiEmpty + 8 * idx, (round & 1) ^ 1, p.status)) return false;
+  if (warp == e && lane == 0) reinterpret_cast<EpiRec*>(base + kEpiRec)[idx] = x;
+  __syncwarp();  // orders the warp's part stores before lane 0's (release) arrive
+  if (lane == 0) mbar_arrive(hdr + kEpiFull + 8 * idx);
+  return true;
+}
+
 template <typename T, int D_>
 __device__ void tma_consumer(const AttnParams& p, unsigned char* base, int box_bytes) {
   constexpr int KS = D_ / 16;
@@ -154,11 +180,17 @@ __device__ void tma_consumer(const AttnParams& p, unsigned char* base, int box_b
   uint32_t qf[KS][2];
   float m0 = kNegInf, m1 = kNegInf, l0 = 0.f, l1 = 0.f;
   float o[KS][4];
+  int nj = 0;  // split units handed to the epilogue warps
   for (int k = 0;; ++k) {
     const int s = k % S, round = k / S;
     if (!mbar_wait(hdr + 8 * s, round & 1, p.status)) return;
     const StepRec r = recs[s];
-    if (r.u < 0) return;
+    if (r.u < 0) {
+      // no more work: an end record for this warp's epilogue warp
+      const EpiRec x = {};
+      epi_push(p, base, nj, x);
+      return;
+    }
     const uint32_t sb = stage0 + s * p.stage_bytes;
     const uint32_t kb = sb + head_region, vb = sb + box_bytes + head_region;
     if (r.first) {
@@ -244,13 +276,74 @@ __device__ void tma_consumer(const AttnParams& p, unsigned char* base, int box_b
       c.unit_base = r.unit_base;
       c.nparts = r.nsplits;
       c.kvh = r.hg * p.HG + warp;
-      mma_epilogue<T, D_>(p, c, o, m0, m1, l0, l1);
+      if (r.nsplits == 1) {
+        mma_store_output<T, D_>(p, c, o, l0, l1);
+      } else {
+        mma_store_part<T, D_>(p, c, o, m0, m1, l0, l1);
+        // Peek at the next step.  While more units follow, the fence, the
+        // part count and the merge run on an epilogue warp and this warp goes
+        // straight on; after the CTA's last unit nothing is left to overlap,
+        // so every consumer warp finishes its own head (the merges of the
+        // heads then run side by side).
+        const int s2 = (k + 1) % S;
+        if (!mbar_wait(hdr + 8 * s2, ((k + 1) / S) & 1, p.status)) return;
+        if (recs[s2].u < 0) {
+          finish_partial<T, D_ == 64 ? 8 : 4>(p, c);
+        } else {
+          const EpiRec x = {r.item, r.q_row, r.unit_base, r.nsplits, r.t0, r.hg, 1, 0};
+          if (!epi_push(p, base, nj++, x)) return;
+        }
+      }
+    }
+  }
+}
+
+// Epilogue warp e: for each split unit handed to it, makes the consumers'
+// part stores visible, counts the parts of heads e, e + 3, ... of the group
+// and merges the heads whose count completes.
+template <typename T>
+__device__ void tma_epilogue_warp(const AttnParams& p, unsigned char* base, int e) {
+  if (e >= p.HG) return;  // no consumer warp feeds this one
+  const int lane = threadIdx.x & 31;
+  const uint32_t hdr = smem_u32(base);
+  const EpiRec* recs = reinterpret_cast<const EpiRec*>(base + kEpiRec);
+  for (int j = 0;; ++j) {
+    const int round = j / kEpiSlots, idx = e * kEpiSlots + j % kEpiSlots;
+    if (!mbar_wait(hdr + kEpiFull + 8 * idx, round & 1, p.status)) return;
+    const EpiRec r = recs[idx];
+    __syncwarp();
+    if (lane == 0) mbar_arrive(hdr + kEpiEmpty + 8 * idx);  // record copied: the slot is free
+    if (!r.flag) return;
+    __threadfence();  // the parts, ordered before this by the ring barrier, become visible
+    int* ctr = p.cnt + (long long)r.item * p.Hkv + r.hg * p.HG;
+    const int h = e + kEpiWarps * lane;  // lane i counts head e + 3 i of the group
+    const bool last = h < p.HG && atomicAdd(ctr + h, 1) == r.nparts - 1;
+    unsigned mask = __ballot_sync(0xffffffffu, last);
+    if (mask) {
+      __threadfence();
+      Work c;
+      c.w = 0;
+      c.u = 0;
+      c.item = r.item;
+      c.slot = 0;
+      c.q_row = r.q_row;
+      c.t0 = r.t0;
+      c.t1 = 0;
+      c.unit_base = r.unit_base;
+      c.nparts = r.nparts;
+      while (mask) {
+        const int i = __ffs(mask) - 1;
+        mask &= mask - 1;
+        c.kvh = r.hg * p.HG + e + kEpiWarps * i;
+        merge_partials<T, 8>(p, c);
+        if (lane == 0) ctr[e + kEpiWarps * i] = 0;  // workspace left clean for the next launch
+      }
     }
   }
 }
 
 template <typename T, int D_>
-__global__ void __launch_bounds__(288, 1) paged_attention_tma_kernel(const AttnParams p,
+__global__ void __launch_bounds__(kTmaMaxThreads, 1) paged_attention_tma_kernel(const AttnParams p,
                                                                   const __grid_constant__ CUtensorMap tk,
                                                                   const __grid_constant__ CUtensorMap tv) {
   extern __shared__ unsigned char smem_raw[];
@@ -263,15 +356,24 @@ __global__ void __launch_bounds__(288, 1) paged_attention_tma_kernel(const AttnP
       mbar_init(smem_u32(base) + 8 * s, 1);
       mbar_init(smem_u32(base) + 64 + 8 * s, p.HG);
     }
+    for (int e = 0; e < kEpiWarps; ++e) {
+      const int feeders = e < p.HG ? (p.HG - 1 - e) / kEpiWarps + 1 : 1;  // consumer warps e, e + 3, ...
+      for (int sl = 0; sl < kEpiSlots; ++sl) {
+        mbar_init(smem_u32(base) + kEpiFull + 8 * (e * kEpiSlots + sl), feeders);
+        mbar_init(smem_u32(base) + kEpiEmpty + 8 * (e * kEpiSlots + sl), 1);
+      }
+    }
     fence_mbar_init();
   }
   __syncthreads();
   const int n_units = min(__ldg(p.counts + 1), p.max_units);
   const int total = n_units * p.n_hg;
-  if (warp == p.HG) {
+  if (warp < p.HG) {
+    tma_consumer<T, D_>(p, base, box_bytes);
+  } else if (warp == p.HG) {
     if ((threadIdx.x & 31) == 0) tma_producer<T, D_>(p, &tk, &tv, base, total, box_bytes, q_bytes);
   } else {
-    tma_consumer<T, D_>(p, base, box_bytes);
+    tma_epilogue_warp<T>(p, base, warp - p.HG - 1);
   }
 }
 
@@ -375,13 +477,14 @@ int launch_attention_tma(AttnParams p, int dtype, long long want, cudaStream_t s
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return fail(NF_ECUDA, "nf_paged_attention: smem attribute: %s", cudaGetErrorString(e));
   int per_sm = 1;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, (hg + 1) * 32, smem) != cudaSuccess || per_sm < 1)
+  const int threads = (hg + 1 + kEpiWarps) * 32;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, smem) != cudaSuccess || per_sm < 1)
     per_sm = 1;
   long long grid = (long long)sm_count() * per_sm;
   const long long need = (want + p.Hkv - 1) / p.Hkv * p.n_hg;  // work items: units x head groups
   if (need < grid) grid = need;
   if (grid < 1) grid = 1;
-  kern<<<(int)grid, (hg + 1) * 32, smem, st>>>(p, tk, tv);
+  kern<<<(int)grid, threads, smem, st>>>(p, tk, tv);
   *path = permuted ? 1 : 2;
   return check_launch("nf_paged_attention");
 }

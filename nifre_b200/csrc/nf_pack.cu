@@ -33,44 +33,50 @@ struct PackParams {
 
 constexpr int kPackThreads = 1024;
 
+// One round of a CTA-wide exclusive scan: returns carry + the sum of x over
+// the threads before this one, and advances every thread's carry by the
+// round's total.  Every thread of the CTA calls it.
+__device__ int cta_scan_round(int x, int& carry) {
+  __shared__ int warp_tot[32];
+  __shared__ int round_tot;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  int incl = x;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  if (lane == 31) warp_tot[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    const int w = warp_tot[lane];
+    int wi = w;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, wi, o);
+      if (lane >= o) wi += y;
+    }
+    warp_tot[lane] = wi - w;  // exclusive prefix of the warp totals
+    if (lane == 31) round_tot = wi;
+  }
+  __syncthreads();
+  const int excl = carry + warp_tot[warp] + incl - x;
+  carry += round_tot;
+  __syncthreads();  // warp_tot and round_tot are rewritten by the next round
+  return excl;
+}
+
 // Exclusive scan, in place, of a[i * stride] for i < n by one CTA.
 // Returns the total to every thread.
 __device__ int cta_exclusive_scan(int* a, int n, int stride) {
-  __shared__ int warp_tot[32];
-  __shared__ int carry_sh;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  if (tid == 0) carry_sh = 0;
-  __syncthreads();
+  int carry = 0;
   for (int base = 0; base < n; base += kPackThreads) {
-    const int i = base + tid;
+    const int i = base + threadIdx.x;
     const int x = (i < n) ? a[(long long)i * stride] : 0;
-    int incl = x;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      int y = __shfl_up_sync(0xffffffffu, incl, o);
-      if (lane >= o) incl += y;
-    }
-    if (lane == 31) warp_tot[warp] = incl;
-    __syncthreads();
-    if (warp == 0) {
-      int w = warp_tot[lane];
-      int wi = w;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        int y = __shfl_up_sync(0xffffffffu, wi, o);
-        if (lane >= o) wi += y;
-      }
-      warp_tot[lane] = wi - w;  // exclusive prefix of warp totals
-    }
-    __syncthreads();
-    const int carry = carry_sh;
-    const int excl = carry + warp_tot[warp] + incl - x;
-    if (i < n) a[(long long)i * stride] = excl;
-    __syncthreads();
-    if (tid == kPackThreads - 1) carry_sh = excl + x;
-    __syncthreads();
+    const int e = cta_scan_round(x, carry);
+    if (i < n) a[(long long)i * stride] = e;
   }
-  return carry_sh;
+  return carry;
 }
 
 __global__ void __launch_bounds__(kPackThreads) pack_kernel(const PackParams p) {
@@ -130,16 +136,60 @@ __global__ void __launch_bounds__(kPackThreads) pack_kernel(const PackParams p) 
   __syncthreads();
   // 4. unit base of each item: scan of the split counts.
   const int n_units = cta_exclusive_scan(p.items + 3, T, 4);
-  // 5. the unit list: one self-contained record per key range of an item.
+  // 5. the unit list, one self-contained record per key range of an item.
+  // Full-length units come first, then each item's shorter remainder unit,
+  // longest first (64 buckets of split/64 keys; any order inside a bucket):
+  // workers that take units in list order then end on the shortest ones,
+  // which evens out their finish times.  The record keeps the item's
+  // unit_base and the range's first key, so a unit's split-K part index is
+  // unit_base + key_begin / split wherever it sits in the list, and the
+  // results do not depend on the order.
+  constexpr int kBuckets = 64;
+  __shared__ int bucket_n[kBuckets], bucket_off[kBuckets];
+  __shared__ int n_rem_sh;
+  for (int b = tid; b < kBuckets; b += kPackThreads) bucket_n[b] = 0;
+  if (tid == 0) n_rem_sh = 0;
+  __syncthreads();
+  auto bucket_of = [&](int rem) { return (int)(((long long)(rem - 1) * kBuckets) / p.split); };
+  int my_rem = 0;
   for (int t = tid; t < T; t += kPackThreads) {
-    const int4 it = reinterpret_cast<const int4*>(p.items)[t];
-    const int n = (it.z + p.split - 1) / p.split;
-    for (int j = 0; j < n; ++j) {
-      const int u = it.w + j;
-      if (u < p.max_units) {
-        int4* rec = reinterpret_cast<int4*>(p.units) + 2 * u;
-        rec[0] = make_int4(t, it.x, it.y, it.z);
-        rec[1] = make_int4(j * p.split, min((j + 1) * p.split, it.z), it.w, n);
+    const int rem = p.items[4 * t + 2] % p.split;
+    if (rem) {
+      ++my_rem;
+      atomicAdd(&bucket_n[bucket_of(rem)], 1);
+    }
+  }
+  if (my_rem) atomicAdd(&n_rem_sh, my_rem);
+  __syncthreads();
+  const int n_full = n_units - n_rem_sh;
+  if (tid == 0) {
+    int acc = n_full;
+    for (int b = kBuckets - 1; b >= 0; --b) {
+      bucket_off[b] = acc;  // list position of the next remainder unit of bucket b
+      acc += bucket_n[b];
+    }
+  }
+  __syncthreads();
+  int rem_carry = 0;
+  for (int base = 0; base < T; base += kPackThreads) {
+    const int t = base + tid;
+    int4 it = make_int4(0, 0, 0, 0);
+    int rem = 0;
+    if (t < T) {
+      it = reinterpret_cast<const int4*>(p.items)[t];
+      rem = it.z % p.split;
+    }
+    const int r = cta_scan_round(rem != 0, rem_carry);  // remainder units of the items before t
+    if (t < T) {
+      const int nfull = it.z / p.split, n = nfull + (rem != 0);
+      const int f = it.w - r;  // full units of the items before t
+      for (int j = 0; j < n; ++j) {
+        const int u = j < nfull ? f + j : atomicAdd(&bucket_off[bucket_of(rem)], 1);
+        if (u < p.max_units) {
+          int4* rec = reinterpret_cast<int4*>(p.units) + 2 * u;
+          rec[0] = make_int4(t, it.x, it.y, it.z);
+          rec[1] = make_int4(j * p.split, min((j + 1) * p.split, it.z), it.w, n);
+        }
       }
     }
   }

@@ -143,6 +143,63 @@ def test_decode_vs_oracle(dtype, D, Hq, Hkv, split):
     cache.check_status()
 
 
+def test_pack_unit_list():
+    """Every key range of every item appears once; full units first, remainders longest first."""
+    import numpy as np
+    rng = np.random.default_rng(3)
+    ctx = rng.integers(1, 3000, size=64).tolist()
+    cache, _ = _random_cache(8, 2, 64, 16, ctx, torch.bfloat16, seed=3)
+    B, split = len(ctx), 128
+    plan = cache.plan(list(range(B)), [1] * B, list(range(B)), split=split)
+    kv = np.array(ctx) + 1
+    n_units = int(((kv + split - 1) // split).sum())
+    counts = plan.counts.cpu().numpy()
+    assert counts[0] == B and counts[1] == n_units
+    items = plan.items.cpu().numpy().reshape(-1, 4)[:B]
+    units = plan.units.cpu().numpy().reshape(-1, 8)[:n_units]
+    nsp = (kv + split - 1) // split
+    assert (items[:, 2] == kv).all()
+    assert (items[:, 3] == np.concatenate([[0], np.cumsum(nsp)[:-1]])).all()  # unit_base
+    seen = set()
+    for t, slot, q_row, kvl, k0, k1, ub, n in units.tolist():
+        assert (slot, q_row, kvl, ub, n) == (t, t, kv[t], items[t, 3], nsp[t])
+        assert k0 % split == 0 and k1 == min(k0 + split, kvl)
+        seen.add((t, k0 // split))
+    assert seen == {(t, j) for t in range(B) for j in range(nsp[t])}
+    lens = units[:, 5] - units[:, 4]
+    n_full = int((kv // split).sum())
+    assert (lens[:n_full] == split).all() and (lens[n_full:] < split).all()
+    assert (units[:n_full, 0] == np.repeat(np.arange(B), kv // split)).all()  # full units in item order
+    buckets = (lens[n_full:] - 1) * 64 // split
+    assert (np.diff(buckets) <= 0).all()
+    cache.check_status()
+
+
+@pytest.mark.parametrize("D,Hq,Hkv", [(64, 32, 8), (128, 32, 8)])
+def test_decode_many_seqs_vs_oracle(D, Hq, Hkv):
+    """A decode batch of 64 ragged contexts with a small split: many parts, merges and queue rounds."""
+    import numpy as np
+    dtype = torch.bfloat16
+    ctx = np.random.default_rng(D).integers(1, 2500, size=64).tolist()
+    cache, g = _random_cache(Hq, Hkv, D, 16, ctx, dtype, seed=11)
+    B = len(ctx)
+    q = torch.randn(B, Hq * D, generator=g).to(dtype).to(DEV)
+    kn = torch.randn(B, Hkv * D, generator=g).to(dtype).to(DEV)
+    vn = torch.randn(B, Hkv * D, generator=g).to(dtype).to(DEV)
+    plan = cache.plan(list(range(B)), [1] * B, list(range(B)), split=128)
+    cache.append_step(0, kn, vn, plan)
+    out = torch.zeros_like(q)
+    for _ in range(2):  # the second launch runs on the counters the first left behind
+        out.zero_()
+        cache.attention_step(0, q, plan, out)
+    kp, vp = cache.k[0].cpu(), cache.v[0].cpu()
+    for b in range(B):
+        ref = attend_paged_fp32(q[b].view(1, Hq, D).cpu(), kp, vp, cache.block_tables[b].physical_blocks(),
+                                ctx[b] + 1, Hq // Hkv)
+        torch.testing.assert_close(out[b].view(Hq, D).float().cpu(), ref[0], **_tol(dtype))
+    cache.check_status()
+
+
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
 def test_chunked_prefill_with_past_vs_oracle(dtype):
     """Prefill chunks continuing cached prefixes (mask key > past + i), mixed with decodes."""
