@@ -58,7 +58,7 @@ extern "C" {
 #define NF_SEQ_FIELDS 4   /* slot, q_start (row of the first new token), q_len, ctx_before */
 #define NF_PATCH_FIELDS 3 /* slot, logical block index, physical block id */
 #define NF_ITEM_FIELDS 4  /* slot, q_row, kv_len, unit_base */
-#define NF_UNIT_FIELDS 8  /* item, slot, q_row, kv_len, key_begin, key_end, unit_base, n_splits */
+#define NF_UNIT_FIELDS 8  /* item, slot, q_row, part, key_begin, key_end, unit_base, n_parts */
 
 /* Message of the last failed call on this thread ("" if none). */
 const char* nf_last_error(void);
@@ -89,15 +89,23 @@ int nf_last_attention_path(void);
  *   src_rows[t]        row of token t in the caller's q/k/v tensors,
  *   positions[t]       absolute position (int64, may be NULL),
  *   items[t][4]        attention work item of the query at token t,
- * and the split-K work list units[max_units][8] (16-byte aligned) of key
- * ranges [key_begin, key_end) of at most split_tokens keys, each record
- * self-contained so a kernel needs one read per unit;
+ * and the split-K work list units[max_units][8] (16-byte aligned): key
+ * ranges [key_begin, key_end) of an item, each record self-contained so a
+ * kernel needs one read per unit.  The queries of sequence s use units of
+ * seq_split[s] keys (device, n_seqs entries; NULL, or an entry that is not a
+ * positive multiple of 16, means split_tokens).  An item's n_parts units are
+ * its parts 0..n_parts-1 in key order, with split-K partial slots
+ * unit_base + part; the list holds the units of sequences at split_tokens
+ * first and those of sequences with a smaller unit size after them, each
+ * class in item order, so that a dynamic queue over the list ends on short
+ * units.  split_tokens must be a positive multiple of 16.
  * counts[0] = n_tokens, counts[1] = number of units.
  */
 int nf_pack_step(const int32_t* seqs, int32_t n_seqs,
                  const int32_t* patches, int32_t n_patches,
                  int32_t* block_tables, int32_t num_slots, int32_t max_blocks_per_seq,
                  int32_t block_size, int32_t num_blocks, int32_t split_tokens,
+                 const int32_t* seq_split,
                  int32_t* slot_mapping, int32_t* src_rows, int64_t* positions,
                  int32_t* items, int32_t* units, int32_t* counts,
                  int32_t n_tokens, int32_t max_units,
@@ -136,9 +144,12 @@ int nf_attention_workspace(int32_t max_units, int32_t max_items, int32_t num_q_h
  * [0, kv_len) of the item's sequence, for every work item produced by
  * nf_pack_step, with query head j reading KV head j / (num_q_heads/num_kv_heads).
  * q/out rows hold num_q_heads*head_dim elements of `dtype` (the pool dtype);
- * rows start every q_row_stride / out_row_stride elements.  Work is split
- * into units of split_tokens keys; partial results go to ws_partials and are
- * merged by the last unit of each item to finish (no extra launch).
+ * rows start every q_row_stride / out_row_stride elements.  Work is the
+ * unit list of nf_pack_step (split_tokens: the value given there, checked
+ * again here); partial results go to ws_partials and are merged at the end
+ * of the same launch, once every unit is done (the kernel is launched
+ * cooperatively: all its CTAs are resident at once).  items (16-byte
+ * aligned) locate each item's parts.
  */
 int nf_paged_attention(void* out, int64_t out_row_stride,
                        const void* q, int64_t q_row_stride,
@@ -165,7 +176,7 @@ int nf_paged_attention(void* out, int64_t out_row_stride,
  * (so make that first call before any stream capture), and every call clears
  * the buffer's counters with cudaMemsetAsync on `stream`.  A step whose
  * scratch (max_units * num_q_heads * (head_dim + 4) floats, rounded up to
- * 256 bytes, plus max_items * num_kv_heads + 2 ints) exceeds the buffer is
+ * 256 bytes, plus max_items * num_kv_heads + 4 ints) exceeds the buffer is
  * rejected with NF_EINVAL.  All calls share the one buffer: calls that
  * overlap on the GPU (other streams, other threads) race and give wrong
  * results.  Arguments and results are otherwise those of nf_paged_attention.

@@ -36,7 +36,7 @@ _SIGNATURES = {
     "nf_last_error": ([], ctypes.c_char_p),
     "nf_abi_version": ([], ctypes.c_int),
     "nf_last_attention_path": ([], ctypes.c_int),
-    "nf_pack_step": ([_P, _I32, _P, _I32, _P, _I32, _I32, _I32, _I32, _I32,
+    "nf_pack_step": ([_P, _I32, _P, _I32, _P, _I32, _I32, _I32, _I32, _I32, _P,
                       _P, _P, _P, _P, _P, _P, _I32, _I32, _P, _P], ctypes.c_int),
     "nf_kv_append": ([_P, _P, _I32, _I64, _P, _P, _I32, _I64, _I64, _P, _P, _I32,
                       _I32, _I32, _P, _I32, _P, _P, _P], ctypes.c_int),

@@ -116,7 +116,7 @@ def causal_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, head_dim
     status = torch.zeros(1, dtype=torch.int32, device=dev)
     stream = _lib.stream_handle(dev)
     lib = _lib.load()
-    _lib.check(lib.nf_pack_step(seqs_d.data_ptr(), B, None, 0, bt.data_ptr(), B, 1, T, B, split,
+    _lib.check(lib.nf_pack_step(seqs_d.data_ptr(), B, None, 0, bt.data_ptr(), B, 1, T, B, split, None,
                                 slot_mapping.data_ptr(), src_rows.data_ptr(), None, items.data_ptr(),
                                 units.data_ptr(), counts.data_ptr(), n_tok, max_units, status.data_ptr(),
                                 stream), "nf_pack_step")

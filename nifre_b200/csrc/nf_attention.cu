@@ -85,7 +85,7 @@ __device__ __forceinline__ void fifo_push(unsigned char* fifo, Loader& L) {
     int* e = reinterpret_cast<int*>(fifo) + (L.fifo_w % kFifo) * kFifoInts;
     const Work& c = L.c;
     e[0] = c.w; e[1] = c.u; e[2] = c.item; e[3] = c.slot; e[4] = c.q_row;
-    e[5] = c.t0; e[6] = c.t1; e[7] = c.unit_base; e[8] = c.nparts; e[9] = c.kvh;
+    e[5] = c.t0; e[6] = c.t1; e[7] = c.unit_base; e[8] = c.nparts; e[9] = c.kvh; e[10] = c.part;
   }
   ++L.fifo_w;
   __syncwarp();
@@ -107,6 +107,7 @@ __device__ __forceinline__ void loader_enter(const AttnParams& p, Loader& L, uns
   c.item = L.na.x;
   c.slot = L.na.y;
   c.q_row = L.na.z;
+  c.part = L.na.w;
   c.t0 = L.nb.x;
   c.t1 = L.nb.y;
   c.unit_base = L.nb.z;
@@ -159,7 +160,7 @@ __device__ __forceinline__ Work fifo_pop(const unsigned char* fifo, int& r) {
   ++r;
   Work c;
   c.w = e[0]; c.u = e[1]; c.item = e[2]; c.slot = e[3]; c.q_row = e[4];
-  c.t0 = e[5]; c.t1 = e[6]; c.unit_base = e[7]; c.nparts = e[8]; c.kvh = e[9];
+  c.t0 = e[5]; c.t1 = e[6]; c.unit_base = e[7]; c.nparts = e[8]; c.kvh = e[9]; c.part = e[10];
   return c;
 }
 
@@ -266,8 +267,9 @@ __device__ __forceinline__ void issue_tile_fast(const AttnParams& p, const Loade
 
 // ---------------------------------------------------------------- 16-bit pools: tensor-core tiles
 // D_: head dim (64 or 128).  MT: 16-key m-tiles per warp tile (TILE = 16*MT keys).
+// Both warp loops return the number of work items the warp finished.
 template <typename T, int D_, int MT>
-__device__ void warp_mma(const AttnParams& p, uint32_t ring, unsigned char* fifo, int total) {
+__device__ int warp_mma(const AttnParams& p, uint32_t ring, unsigned char* fifo, int total) {
   constexpr int KS = D_ / 16;  // k-steps of S^T and m-tiles of O^T
   constexpr int HB = D_ * 2;   // bytes of one head row
   constexpr int TILE = 16 * MT;
@@ -290,10 +292,11 @@ __device__ void warp_mma(const AttnParams& p, uint32_t ring, unsigned char* fifo
   // fragment addressing (rows this lane supplies to ldmatrix, before the swizzle)
   const int kr = (lane & 7) + ((lane >> 3) & 1) * 8, kc = lane >> 4;        // K: row, chunk parity
   const int vr = (lane & 7) + ((lane >> 4) & 1) * 8, vc = (lane >> 3) & 1;  // V: row, chunk parity
-  int k = 0, fr = 0;
+  int k = 0, fr = 0, done = 0;
   while (true) {
     const Work c = fifo_pop(fifo, fr);
     if (c.w < 0) break;
+    ++done;
     uint32_t qf[KS][2];
     if (!p.q_smem) {
       const T* qp = reinterpret_cast<const T*>(p.q) + (long long)c.q_row * p.q_stride +
@@ -403,15 +406,15 @@ __device__ void warp_mma(const AttnParams& p, uint32_t ring, unsigned char* fifo
     mma_epilogue<T, D_>(p, c, o, m0, m1, l0, l1);
   }
   cp_async_wait(0);
-  retire_worker(p, gridDim.x * p.W);
+  return done;
 }
 
 // ---------------------------------------------------------------- any dtype: CUDA-core path
 // Any head_dim <= 32*DPL, up to 8 query heads per KV head; lanes split the
 // head dimension.  Same pipeline and queue as the tensor-core path.
 template <typename T, int DPL>
-__device__ void warp_simt(const AttnParams& p, uint32_t ring, unsigned char* ring_ptr, unsigned char* fifo,
-                          int total) {
+__device__ int warp_simt(const AttnParams& p, uint32_t ring, unsigned char* ring_ptr, unsigned char* fifo,
+                         int total) {
   const int lane = threadIdx.x & 31;
   const int S = p.stages;
   const int HB = p.head_bytes;
@@ -424,10 +427,11 @@ __device__ void warp_simt(const AttnParams& p, uint32_t ring, unsigned char* rin
     }
     cp_async_commit();
   }
-  int k = 0, fr = 0;
+  int k = 0, fr = 0, done = 0;
   while (true) {
     const Work c = fifo_pop(fifo, fr);
     if (c.w < 0) break;
+    ++done;
     float qv[8][DPL], acc[8][DPL], m[8], l[8];
     const T* qp = reinterpret_cast<const T*>(p.q) + (long long)c.q_row * p.q_stride + (long long)(c.kvh * p.G) * p.D;
 #pragma unroll
@@ -510,25 +514,30 @@ __device__ void warp_simt(const AttnParams& p, uint32_t ring, unsigned char* rin
           }
         }
       }
-      finish_partial<T, 2>(p, c);
     }
   }
   cp_async_wait(0);
-  retire_worker(p, gridDim.x * p.W);
+  return done;
 }
 
 // ---------------------------------------------------------------- kernel
 template <typename T, int D_, int MT, bool MMA, int DPL>
 __global__ void __launch_bounds__(256) paged_attention_kernel(const AttnParams p) {
   extern __shared__ __align__(128) unsigned char smem[];
+  __shared__ int cta_done;
+  if (threadIdx.x == 0) cta_done = 0;
+  __syncthreads();
   const int warp = threadIdx.x >> 5;
   const int n_units = min(__ldg(p.counts + 1), p.max_units);
   const int total = n_units * p.Hkv;
   unsigned char* ring_ptr = smem + (size_t)warp * p.stages * p.stage_bytes;
   unsigned char* fifo = smem + (size_t)p.W * p.stages * p.stage_bytes + warp * kFifoBytes;
   const uint32_t ring = smem_u32(ring_ptr);
-  if constexpr (MMA) warp_mma<T, D_, MT>(p, ring, fifo, total);
-  else warp_simt<T, DPL>(p, ring, ring_ptr, fifo, total);
+  int done;
+  if constexpr (MMA) done = warp_mma<T, D_, MT>(p, ring, fifo, total);
+  else done = warp_simt<T, DPL>(p, ring, ring_ptr, fifo, total);
+  if ((threadIdx.x & 31) == 0 && done) atomicAdd(&cta_done, done);
+  finish_launch<T, 8>(p, &cta_done, total);
 }
 
 // ---------------------------------------------------------------- host plan
@@ -562,7 +571,9 @@ static int make_plan(int dtype, int Hq, int Hkv, int D, bool q_smem_ok, Plan& pl
   // Warps per CTA and ring depth: the most warps resident per SM with >= 3
   // slots per warp (each warp keeps two tiles in flight); ties go to fewer,
   // larger CTAs.  Two slots only as a last resort.
-  const int kSmemSM = 228 * 1024, kSmemCTA = 227 * 1024, kReserve = 1024;
+  // per CTA: 1 KB the system reserves and up to 256 B of the kernel's static
+  // shared memory (finish_launch) besides the dynamic buffer
+  const int kSmemSM = 228 * 1024, kSmemCTA = 227 * 1024 - 256, kReserve = 1024 + 256;
   int best = 0;
   pl.W = 0;
   for (int min_st = 3; min_st >= 2 && !pl.W; --min_st) {
@@ -596,7 +607,19 @@ static int launch_attn(const AttnParams& p, const Plan& pl, long long want, cuda
   const long long need = (want + pl.W - 1) / pl.W;  // no more warps than work items
   if (need < grid) grid = need;
   if (grid < 1) grid = 1;
-  kern<<<(int)grid, pl.W * 32, pl.smem, st>>>(p);
+  // cooperative: the end-of-launch merge waits for every CTA
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3(pl.W * 32);
+  cfg.dynamicSmemBytes = pl.smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, kern, p);
+  if (e != cudaSuccess) return fail(NF_ECUDA, "nf_paged_attention: launch: %s", cudaGetErrorString(e));
   return check_launch("nf_paged_attention");
 }
 
@@ -628,7 +651,7 @@ extern "C" int nf_attention_workspace(int32_t max_units, int32_t max_items, int3
   if (max_units <= 0 || max_items <= 0 || !partial_floats || !counter_ints)
     return fail(NF_EINVAL, "nf_attention_workspace: bad arguments");
   *partial_floats = (int64_t)max_units * num_q_heads * (head_dim + 4);
-  *counter_ints = (int64_t)max_items * num_kv_heads + 2;
+  *counter_ints = (int64_t)max_items * num_kv_heads + 4;
   return ok();
 }
 
@@ -640,26 +663,26 @@ extern "C" int nf_paged_attention(void* out, int64_t out_row_stride, const void*
                                   int32_t split_tokens, float scale, float* ws_partials, int64_t ws_partial_floats,
                                   int32_t* ws_counters, int64_t ws_counter_ints, int32_t* status, void* stream) {
   using namespace nf;
-  (void)items;  // unit records are self-contained; the argument stays for ABI stability
   const size_t es = dtype_size(dtype);
   auto al = [](const void* ptr, size_t a) { return (reinterpret_cast<uintptr_t>(ptr) % a) == 0; };
   const bool q_smem_ok = es && al(q, 16) && (q_row_stride * (int64_t)es) % 16 == 0;
   Plan pl;
   int rc = make_plan(dtype, num_q_heads, num_kv_heads, head_dim, q_smem_ok, pl);
   if (rc) return rc;
-  if (!out || !q || !k_pool || !v_pool || !block_tables || !units || !counts || !status)
+  if (!out || !q || !k_pool || !v_pool || !block_tables || !items || !units || !counts || !status)
     return fail(NF_EINVAL, "nf_paged_attention: null pointer argument");
   if (block_size <= 0 || num_blocks <= 0 || max_blocks_per_seq <= 0 || max_units <= 0 || max_items <= 0)
     return fail(NF_EINVAL, "nf_paged_attention: sizes must be positive");
   if (split_tokens <= 0 || split_tokens % 16 != 0)
     return fail(NF_EINVAL, "nf_paged_attention: split_tokens (%d) must be a positive multiple of 16", split_tokens);
   const int64_t need_p = (int64_t)max_units * num_q_heads * (head_dim + 4);
-  const int64_t need_c = (int64_t)max_items * num_kv_heads + 2;
+  const int64_t need_c = (int64_t)max_items * num_kv_heads + 4;
   if (!ws_partials || ws_partial_floats < need_p || !ws_counters || ws_counter_ints < need_c)
     return fail(NF_EINVAL, "nf_paged_attention: workspace too small (need %lld floats, %lld counters)",
                 (long long)need_p, (long long)need_c);
   if (!al(k_pool, 16) || !al(v_pool, 16)) return fail(NF_EINVAL, "nf_paged_attention: pools must be 16-byte aligned");
-  if (!al(units, 16)) return fail(NF_EINVAL, "nf_paged_attention: units must be 16-byte aligned");
+  if (!al(units, 16) || !al(items, 16))
+    return fail(NF_EINVAL, "nf_paged_attention: items and units must be 16-byte aligned");
   if (!al(ws_partials, 16)) return fail(NF_EINVAL, "nf_paged_attention: partials must be 16-byte aligned");
   if (pl.mma && (!al(q, 4) || (q_row_stride * (int64_t)es) % 4 != 0))
     return fail(NF_EINVAL, "nf_paged_attention: q rows must be 4-byte aligned");
@@ -686,6 +709,9 @@ extern "C" int nf_paged_attention(void* out, int64_t out_row_stride, const void*
   p.ws = ws_partials;
   p.cnt = ws_counters;
   p.queue = ws_counters + (int64_t)max_items * num_kv_heads;
+  p.items = items;
+  p.max_items = max_items;
+  p.merge = max_units > max_items;  // else every item has exactly one part
   p.status = status;
   p.W = pl.W;
   p.stages = pl.stages;
@@ -697,21 +723,22 @@ extern "C" int nf_paged_attention(void* out, int64_t out_row_stride, const void*
   p.q_smem = pl.q_smem;
   const long long want = (long long)max_units * num_kv_heads;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int arc = NF_EUNSUPPORTED;
   if (pl.mma) {
     int path = 0;
-    const int trc = launch_attention_tma(p, dtype, want, st, &path);
-    if (trc != NF_EUNSUPPORTED) {
-      set_attention_path(path);
-      return trc;
+    arc = launch_attention_tma(p, dtype, want, st, &path);
+    if (arc != NF_EUNSUPPORTED) set_attention_path(path);
+  }
+  if (arc == NF_EUNSUPPORTED) {
+    set_attention_path(0);
+    switch (dtype) {
+      case NF_F32: arc = dispatch_attn<float>(p, pl, want, st); break;
+      case NF_F16: arc = dispatch_attn<__half>(p, pl, want, st); break;
+      case NF_BF16: arc = dispatch_attn<__nv_bfloat16>(p, pl, want, st); break;
+      default: return fail(NF_EINVAL, "nf_paged_attention: bad dtype %d", dtype);
     }
   }
-  set_attention_path(0);
-  switch (dtype) {
-    case NF_F32: return dispatch_attn<float>(p, pl, want, st);
-    case NF_F16: return dispatch_attn<__half>(p, pl, want, st);
-    case NF_BF16: return dispatch_attn<__nv_bfloat16>(p, pl, want, st);
-  }
-  return fail(NF_EINVAL, "nf_paged_attention: bad dtype %d", dtype);
+  return arc;
 }
 
 // ---------------------------------------------------------------- allocation-free variant
@@ -738,7 +765,7 @@ extern "C" int nf_paged_attention_noalloc(void* out, int64_t out_row_stride, con
   if (max_units <= 0 || max_items <= 0 || num_q_heads <= 0 || num_kv_heads <= 0 || head_dim <= 0)
     return fail(NF_EINVAL, "nf_paged_attention_noalloc: sizes must be positive");
   const int64_t part_floats = (int64_t)max_units * num_q_heads * (head_dim + 4);
-  const int64_t cnt_ints = (int64_t)max_items * num_kv_heads + 2;
+  const int64_t cnt_ints = (int64_t)max_items * num_kv_heads + 4;
   const int64_t part_bytes = ((part_floats * 4 + 255) / 256) * 256;
   const int64_t need = part_bytes + cnt_ints * 4;
   if (need > (int64_t)NF_NOALLOC_SCRATCH_BYTES)

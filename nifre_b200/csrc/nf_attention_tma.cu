@@ -19,9 +19,12 @@
 // head (and per 64-element half of the head) gives the same layout.
 //
 // Consumer warp h computes KV head h of the group exactly as the per-warp
-// path does (mma.sync S^T = K Q^T, online softmax, O^T += V^T P^T, split-K
-// parts and merge).  Every wait is an mbarrier wait with a time limit: a wait
-// that runs out sets NF_STATUS_WAIT_TIMEOUT and the warp leaves its loop.
+// path does (mma.sync S^T = K Q^T, online softmax, O^T += V^T P^T), two
+// staged 16-key tiles per update.  A unit that is one split-K part of a
+// longer item ends with the part's (acc, m, l) store; once every unit of the
+// launch is done, all warps of the grid merge the parts (finish_launch).  Every wait is an mbarrier wait with a
+// time limit: a wait that runs out sets NF_STATUS_WAIT_TIMEOUT and the warp
+// leaves its loop.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -30,21 +33,14 @@
 
 namespace nf {
 
-// Shared-memory header: stage barriers (full[8] at 0, empty[8] at 64), step
-// records (8 x 64 B at 128), epilogue-ring barriers (full[3][2] at 640,
-// empty[3][2] at 704) and epilogue records (3 x 2 x 32 B at 768).
+// Shared-memory header: stage barriers (full[8] at 0, empty[8] at 64) and
+// step records (8 x 64 B at 128).
 constexpr int kTmaHeader = 1024;
 constexpr int kTmaMaxStages = 8;
-constexpr int kEpiWarps = 3, kEpiSlots = 2;
-constexpr int kEpiFull = 640, kEpiEmpty = 704, kEpiRec = 768;
-constexpr int kTmaMaxThreads = (8 + 1 + kEpiWarps) * 32;
+constexpr int kTmaMaxThreads = (8 + 1) * 32;
 
 struct StepRec {  // one 16-key step as the producer describes it to the consumers
-  int u, item, q_row, t0, t1, unit_base, nsplits, hg, t, first, last, pad[5];
-};
-
-struct EpiRec {  // one unit's split-K bookkeeping, handed to an epilogue warp
-  int item, q_row, unit_base, nparts, t0, hg, flag, pad;  // flag 0: no more units
+  int u, item, q_row, t0, t1, unit_base, nsplits, hg, t, first, last, part, pad[4];
 };
 
 __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2, int c3,
@@ -71,9 +67,10 @@ __device__ __forceinline__ int tma_off(int r, int c) {
   return (c >> 3) * 2048 + r * 128 + (((c & 7) ^ (r & 7)) << 4);
 }
 
+// Returns the number of work items this CTA took.
 template <typename T, int D_>
-__device__ void tma_producer(const AttnParams& p, const CUtensorMap* tk, const CUtensorMap* tv, unsigned char* base,
-                             int total, int box_bytes, int q_bytes) {
+__device__ int tma_producer(const AttnParams& p, const CUtensorMap* tk, const CUtensorMap* tv, unsigned char* base,
+                            int total, int box_bytes, int q_bytes) {
   constexpr int NDH = D_ / 64;  // 64-element halves of a head row
   const uint32_t hdr = smem_u32(base);
   auto full = [&](int s) { return hdr + 8 * s; };
@@ -81,25 +78,53 @@ __device__ void tma_producer(const AttnParams& p, const CUtensorMap* tk, const C
   StepRec* recs = reinterpret_cast<StepRec*>(base + 128);
   const uint32_t stage0 = hdr + kTmaHeader;
   const int S = p.stages;
-  int k = 0;
+  // The switch to the next unit needs three dependent round trips (ticket,
+  // unit record, first block-table entry) of 1-2 us each under full load,
+  // and this thread stalls on each result while no copy is issued.  So the
+  // next ticket is requested kAhead steps (about 6 us of streaming) before the
+  // current unit's last step, its record is loaded kGap steps later and its
+  // first block-table entry kGap steps after that, each once the previous
+  // result has had time to arrive.  Short units take the stalls.
+  constexpr int kAhead = 8, kGap = 2;
+  const int4* urec = reinterpret_cast<const int4*>(p.units);
+  int k = 0;           // steps issued
+  int s = 0;           // slot of step k (k mod S)
+  uint32_t pe = 1;     // parity that frees slot s for step k: ((k / S) & 1) ^ 1
   bool ok = true;
-  while (ok) {
-    const int w = atomicAdd(p.queue, 1);
-    if (w >= total) break;
+  int w = atomicAdd(p.queue, 1);
+  int4 ra = make_int4(0, 0, 0, 0), rb = ra;
+  if (w < total) {
+    ra = __ldg(urec + 2 * (w / p.n_hg));
+    rb = __ldg(urec + 2 * (w / p.n_hg) + 1);
+  }
+  int taken = 0;
+  while (w < total) {
+    ++taken;
     const int u = w / p.n_hg, hg = w - u * p.n_hg;
-    const int4 ra = __ldg(reinterpret_cast<const int4*>(p.units) + 2 * u);
-    const int4 rb = __ldg(reinterpret_cast<const int4*>(p.units) + 2 * u + 1);
     const int* btrow = p.bt + (long long)ra.y * p.max_blocks;
     const int h0 = hg * p.HG;
-    for (int t = rb.x; t < rb.y; t += 16, ++k) {
-      const int s = k % S, round = k / S;
-      if (!mbar_wait(empty(s), (round & 1) ^ 1, p.status)) {
+    const int nsteps = (rb.y - rb.x + 15) >> 4;
+    const int ask = nsteps - 1 - min(kAhead, nsteps - 1);  // step that requests the next ticket
+    int wn = total;
+    int4 na = make_int4(0, 0, 0, 0), nb = na;
+    for (int i = 0, t = rb.x; i < nsteps; ++i, t += 16, ++k) {
+      if (i == ask) {
+        wn = atomicAdd(p.queue, 1);
+      } else if (i == ask + kGap && wn < total) {
+        na = __ldg(urec + 2 * (wn / p.n_hg));
+        nb = __ldg(urec + 2 * (wn / p.n_hg) + 1);
+      } else if (i == ask + 2 * kGap && wn < total) {
+        const int lb = nb.x / p.bs;
+        if (lb < p.max_blocks)
+          asm volatile("prefetch.global.L1 [%0];" ::"l"(p.bt + (long long)na.y * p.max_blocks + lb));
+      }
+      if (!mbar_wait(empty(s), pe, p.status)) {
         ok = false;
         break;
       }
       StepRec& r = recs[s];
       r.u = u; r.item = ra.x; r.q_row = ra.z; r.t0 = rb.x; r.t1 = rb.y; r.unit_base = rb.z;
-      r.nsplits = rb.w; r.hg = hg; r.t = t; r.first = t == rb.x; r.last = t + 16 >= rb.y;
+      r.nsplits = rb.w; r.hg = hg; r.t = t; r.first = i == 0; r.last = i == nsteps - 1; r.part = ra.w;
       const int lb = t / p.bs, off = t - lb * p.bs;
       const int phys = checked_block(p, btrow, lb);
       const uint32_t sb = stage0 + s * p.stage_bytes;
@@ -130,36 +155,103 @@ __device__ void tma_producer(const AttnParams& p, const CUtensorMap* tk, const C
         const char* qrow = p.q + ((long long)ra.z * p.q_stride + (long long)h0 * p.G * p.D) * (long long)sizeof(T);
         bulk_g2s(sb + 2 * box_bytes, qrow, q_bytes, full(s));
       }
+      if (++s == S) {
+        s = 0;
+        pe ^= 1;
+      }
     }
+    if (!ok) break;
+    if (ask + kGap > nsteps - 1 && wn < total) {  // a short unit: the record was not loaded yet
+      na = __ldg(urec + 2 * (wn / p.n_hg));
+      nb = __ldg(urec + 2 * (wn / p.n_hg) + 1);
+    }
+    w = wn;
+    ra = na;
+    rb = nb;
   }
   if (ok) {
     // end of work: a record with u = -1, published by a plain arrive
-    const int s = k % S, round = k / S;
-    if (mbar_wait(empty(s), (round & 1) ^ 1, p.status)) {
+    if (mbar_wait(empty(s), pe, p.status)) {
       recs[s].u = -1;
       mbar_arrive(full(s));
-      retire_worker(p, gridDim.x);
-      return;
+      return taken;
     }
   }
   // a wait ran out: leave no copy in flight into this CTA's shared memory
   for (int j = max(0, k - S); j < k; ++j) mbar_wait(full(j % S), (j / S) & 1, p.status);
+  return taken;
 }
 
-// Hands this warp's head of the j-th split unit of the CTA to epilogue warp
-// (warp % kEpiWarps), which serves consumer warps e, e + 3, ...: every
-// consumer warp calls it after storing its head's part, and the lowest warp
-// of the ring writes the record.  Returns false if a wait ran out.
-__device__ __forceinline__ bool epi_push(const AttnParams& p, unsigned char* base, int j, const EpiRec& x) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint32_t hdr = smem_u32(base);
-  const int e = warp % kEpiWarps, round = j / kEpiSlots;
-  const int idx = e * kEpiSlots + j % kEpiSlots;
-  if (!mbar_wait(hdr + kEpiEmpty + 8 * idx, (round & 1) ^ 1, p.status)) return false;
-  if (warp == e && lane == 0) reinterpret_cast<EpiRec*>(base + kEpiRec)[idx] = x;
-  __syncwarp();  // orders the warp's part stores before lane 0's (release) arrive
-  if (lane == 0) mbar_arrive(hdr + kEpiFull + 8 * idx);
-  return true;
+// One consumer update over NT staged 16-key tiles of this warp's head (K
+// tiles at kb[j], V tiles at vb[j]; keys at or past nv are masked): S^T = K
+// Q^T per tile, one running-max update for all NT x 16 keys, O^T += V^T P^T.
+// Two tiles give two independent MMA chains and halve the per-key cost of
+// the max shuffles, the rescale of O and the barrier traffic.
+template <typename T, int D_, int NT>
+__device__ __forceinline__ void consume_tiles(const AttnParams& p, const uint32_t (&kb)[2], const uint32_t (&vb)[2],
+                                              int nv, const uint32_t (&qf)[D_ / 16][2], float (&o)[D_ / 16][4],
+                                              float& m0, float& m1, float& l0, float& l1) {
+  constexpr int KS = D_ / 16;
+  const int lane = threadIdx.x & 31;
+  const int tq = lane >> 2;
+  const int kr = (lane & 7) + ((lane >> 3) & 1) * 8, kc = lane >> 4;
+  const int vr = (lane & 7) + ((lane >> 4) & 1) * 8, vc = (lane >> 3) & 1;
+  float x[NT][4];
+#pragma unroll
+  for (int j = 0; j < NT; ++j) {
+    float sc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int ks = 0; ks < KS; ++ks) {
+      uint32_t a0, a1, a2, a3;
+      ldsm_x4(kb[j] + tma_off(kr, 2 * ks + kc), a0, a1, a2, a3);
+      mma16816<T>(sc, a0, a1, a2, a3, qf[ks][0], qf[ks][1]);
+    }
+    const bool v0 = 16 * j + tq < nv, v1 = 16 * j + tq + 8 < nv;
+    x[j][0] = v0 ? sc[0] * p.scale_log2 : kNegInf;
+    x[j][1] = v0 ? sc[1] * p.scale_log2 : kNegInf;
+    x[j][2] = v1 ? sc[2] * p.scale_log2 : kNegInf;
+    x[j][3] = v1 ? sc[3] * p.scale_log2 : kNegInf;
+  }
+  float mx0 = fmaxf(x[0][0], x[0][2]), mx1 = fmaxf(x[0][1], x[0][3]);
+#pragma unroll
+  for (int j = 1; j < NT; ++j) {
+    mx0 = fmaxf(mx0, fmaxf(x[j][0], x[j][2]));
+    mx1 = fmaxf(mx1, fmaxf(x[j][1], x[j][3]));
+  }
+#pragma unroll
+  for (int o_ = 4; o_ < 32; o_ <<= 1) {
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o_));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o_));
+  }
+  const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+  const float b0 = mn0 == kNegInf ? 0.f : mn0, b1 = mn1 == kNegInf ? 0.f : mn1;
+  const float al0 = ex2(m0 - b0), al1 = ex2(m1 - b1);
+  l0 *= al0;
+  l1 *= al1;
+  uint32_t pb[NT][2];
+#pragma unroll
+  for (int j = 0; j < NT; ++j) {
+    const float p0 = ex2(x[j][0] - b0), p1 = ex2(x[j][1] - b1), p2 = ex2(x[j][2] - b0), p3 = ex2(x[j][3] - b1);
+    l0 += p0 + p2;
+    l1 += p1 + p3;
+    pb[j][0] = movmatrix_t(pack2<T>(p0, p1));
+    pb[j][1] = movmatrix_t(pack2<T>(p2, p3));
+  }
+  m0 = mn0;
+  m1 = mn1;
+#pragma unroll
+  for (int i = 0; i < KS; ++i) {
+    o[i][0] *= al0;
+    o[i][1] *= al1;
+    o[i][2] *= al0;
+    o[i][3] *= al1;
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+      uint32_t a0, a1, a2, a3;
+      ldsm_x4_t(vb[j] + tma_off(vr, 2 * i + vc), a0, a1, a2, a3);
+      mma16816<T>(o[i], a0, a1, a2, a3, pb[j][0], pb[j][1]);
+    }
+  }
 }
 
 template <typename T, int D_>
@@ -174,27 +266,39 @@ __device__ void tma_consumer(const AttnParams& p, unsigned char* base, int box_b
   const int S = p.stages;
   const int n0 = 2 * (lane & 3), tq = lane >> 2;
   const bool has = tq < p.G;
-  const int kr = (lane & 7) + ((lane >> 3) & 1) * 8, kc = lane >> 4;
-  const int vr = (lane & 7) + ((lane >> 4) & 1) * 8, vc = (lane >> 3) & 1;
   const int head_region = warp * NDH * 2048;
   uint32_t qf[KS][2];
   float m0 = kNegInf, m1 = kNegInf, l0 = 0.f, l1 = 0.f;
   float o[KS][4];
-  int nj = 0;  // split units handed to the epilogue warps
-  for (int k = 0;; ++k) {
-    const int s = k % S, round = k / S;
-    if (!mbar_wait(hdr + 8 * s, round & 1, p.status)) return;
-    const StepRec r = recs[s];
-    if (r.u < 0) {
-      // no more work: an end record for this warp's epilogue warp
-      const EpiRec x = {};
-      epi_push(p, base, nj, x);
-      return;
+  int s = 0;        // slot of the next step
+  uint32_t ph = 0;  // parity of its full barrier
+  auto advance = [&]() {
+    if (++s == S) {
+      s = 0;
+      ph ^= 1;
     }
-    const uint32_t sb = stage0 + s * p.stage_bytes;
-    const uint32_t kb = sb + head_region, vb = sb + box_bytes + head_region;
+  };
+  for (;;) {
+    if (!mbar_wait(hdr + 8 * s, ph, p.status)) return;
+    const StepRec r = recs[s];
+    if (r.u < 0) return;  // no more work
+    // take the unit's next step too when it has one: 32 keys per update
+    const int s0 = s;
+    advance();
+    const bool pair = !r.last;
+    int s1 = s0;
+    bool last = true;
+    if (pair) {
+      if (!mbar_wait(hdr + 8 * s, ph, p.status)) return;
+      s1 = s;
+      last = recs[s1].last;
+      advance();
+    }
+    const uint32_t sb0 = stage0 + s0 * p.stage_bytes, sb1 = stage0 + s1 * p.stage_bytes;
+    const uint32_t kb[2] = {sb0 + head_region, sb1 + head_region};
+    const uint32_t vb[2] = {sb0 + box_bytes + head_region, sb1 + box_bytes + head_region};
     if (r.first) {
-      const uint32_t qs = sb + 2 * box_bytes + (warp * p.G + tq) * HB + n0 * 2;
+      const uint32_t qs = sb0 + 2 * box_bytes + (warp * p.G + tq) * HB + n0 * 2;
 #pragma unroll
       for (int ks = 0; ks < KS; ++ks) {
         qf[ks][0] = has ? lds32(qs + ks * 32) : 0u;
@@ -205,61 +309,32 @@ __device__ void tma_consumer(const AttnParams& p, unsigned char* base, int box_b
 #pragma unroll
       for (int i = 0; i < KS; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
     }
-    const int nv = min(16, r.t1 - r.t);
-    if (nv < 16) {
+    const int nv = min(pair ? 32 : 16, r.t1 - r.t);
+    const int nvl = nv - (pair ? 16 : 0);  // valid rows of the last tile
+    if (nvl < 16) {
       // rows past the unit's end hold whatever the block holds: zero them in V
       // (their scores are masked, but 0 * NaN would still poison the sum)
-      for (int idx = lane; idx < (16 - nv) * NDH * 8; idx += 32) {
-        const int row = nv + idx / (NDH * 8), rest = idx % (NDH * 8);
-        const uint32_t a = vb + (rest >> 3) * 2048 + row * 128 + (rest & 7) * 16;
+      const uint32_t vl = pair ? vb[1] : vb[0];
+      for (int idx = lane; idx < (16 - nvl) * NDH * 8; idx += 32) {
+        const int row = nvl + idx / (NDH * 8), rest = idx % (NDH * 8);
+        const uint32_t a = vl + (rest >> 3) * 2048 + row * 128 + (rest & 7) * 16;
         asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(a), "r"(0) : "memory");
       }
       __syncwarp();
     }
-    float sc[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-    for (int ks = 0; ks < KS; ++ks) {
-      uint32_t a0, a1, a2, a3;
-      ldsm_x4(kb + tma_off(kr, 2 * ks + kc), a0, a1, a2, a3);
-      mma16816<T>(sc, a0, a1, a2, a3, qf[ks][0], qf[ks][1]);
-    }
-    const bool v0 = tq < nv, v1 = tq + 8 < nv;
-    const float x0 = v0 ? sc[0] * p.scale_log2 : kNegInf;
-    const float x1 = v0 ? sc[1] * p.scale_log2 : kNegInf;
-    const float x2 = v1 ? sc[2] * p.scale_log2 : kNegInf;
-    const float x3 = v1 ? sc[3] * p.scale_log2 : kNegInf;
-    float mx0 = fmaxf(x0, x2), mx1 = fmaxf(x1, x3);
-#pragma unroll
-    for (int o_ = 4; o_ < 32; o_ <<= 1) {
-      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o_));
-      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o_));
-    }
-    const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
-    const float b0 = mn0 == kNegInf ? 0.f : mn0, b1 = mn1 == kNegInf ? 0.f : mn1;
-    const float al0 = ex2(m0 - b0), al1 = ex2(m1 - b1);
-    const float p0 = ex2(x0 - b0), p1 = ex2(x1 - b1), p2 = ex2(x2 - b0), p3 = ex2(x3 - b1);
-    l0 = l0 * al0 + p0 + p2;
-    l1 = l1 * al1 + p1 + p3;
-    m0 = mn0;
-    m1 = mn1;
-    const uint32_t pb0 = movmatrix_t(pack2<T>(p0, p1));
-    const uint32_t pb1 = movmatrix_t(pack2<T>(p2, p3));
-#pragma unroll
-    for (int i = 0; i < KS; ++i) {
-      o[i][0] *= al0;
-      o[i][1] *= al1;
-      o[i][2] *= al0;
-      o[i][3] *= al1;
-      uint32_t a0, a1, a2, a3;
-      ldsm_x4_t(vb + tma_off(vr, 2 * i + vc), a0, a1, a2, a3);
-      mma16816<T>(o[i], a0, a1, a2, a3, pb0, pb1);
-    }
-    // release the slot (the tail zeroing wrote with the generic proxy: order it
-    // before the next tensor copy into this slot)
-    if (nv < 16) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    if (pair)
+      consume_tiles<T, D_, 2>(p, kb, vb, nv, qf, o, m0, m1, l0, l1);
+    else
+      consume_tiles<T, D_, 1>(p, kb, vb, nv, qf, o, m0, m1, l0, l1);
+    // release the slots (the tail zeroing wrote with the generic proxy: order
+    // it before the next tensor copy into the slot)
+    if (nvl < 16) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     __syncwarp();
-    if (lane == 0) mbar_arrive(hdr + 64 + 8 * s);
-    if (r.last) {
+    if (lane == 0) {
+      mbar_arrive(hdr + 64 + 8 * s0);
+      if (pair) mbar_arrive(hdr + 64 + 8 * s1);
+    }
+    if (last) {
 #pragma unroll
       for (int o_ = 4; o_ < 32; o_ <<= 1) {
         l0 += __shfl_xor_sync(0xffffffffu, l0, o_);
@@ -276,68 +351,11 @@ __device__ void tma_consumer(const AttnParams& p, unsigned char* base, int box_b
       c.unit_base = r.unit_base;
       c.nparts = r.nsplits;
       c.kvh = r.hg * p.HG + warp;
-      if (r.nsplits == 1) {
+      c.part = r.part;
+      if (r.nsplits == 1)
         mma_store_output<T, D_>(p, c, o, l0, l1);
-      } else {
+      else
         mma_store_part<T, D_>(p, c, o, m0, m1, l0, l1);
-        // Peek at the next step.  While more units follow, the fence, the
-        // part count and the merge run on an epilogue warp and this warp goes
-        // straight on; after the CTA's last unit nothing is left to overlap,
-        // so every consumer warp finishes its own head (the merges of the
-        // heads then run side by side).
-        const int s2 = (k + 1) % S;
-        if (!mbar_wait(hdr + 8 * s2, ((k + 1) / S) & 1, p.status)) return;
-        if (recs[s2].u < 0) {
-          finish_partial<T, D_ == 64 ? 8 : 4>(p, c);
-        } else {
-          const EpiRec x = {r.item, r.q_row, r.unit_base, r.nsplits, r.t0, r.hg, 1, 0};
-          if (!epi_push(p, base, nj++, x)) return;
-        }
-      }
-    }
-  }
-}
-
-// Epilogue warp e: for each split unit handed to it, makes the consumers'
-// part stores visible, counts the parts of heads e, e + 3, ... of the group
-// and merges the heads whose count completes.
-template <typename T>
-__device__ void tma_epilogue_warp(const AttnParams& p, unsigned char* base, int e) {
-  if (e >= p.HG) return;  // no consumer warp feeds this one
-  const int lane = threadIdx.x & 31;
-  const uint32_t hdr = smem_u32(base);
-  const EpiRec* recs = reinterpret_cast<const EpiRec*>(base + kEpiRec);
-  for (int j = 0;; ++j) {
-    const int round = j / kEpiSlots, idx = e * kEpiSlots + j % kEpiSlots;
-    if (!mbar_wait(hdr + kEpiFull + 8 * idx, round & 1, p.status)) return;
-    const EpiRec r = recs[idx];
-    __syncwarp();
-    if (lane == 0) mbar_arrive(hdr + kEpiEmpty + 8 * idx);  // record copied: the slot is free
-    if (!r.flag) return;
-    __threadfence();  // the parts, ordered before this by the ring barrier, become visible
-    int* ctr = p.cnt + (long long)r.item * p.Hkv + r.hg * p.HG;
-    const int h = e + kEpiWarps * lane;  // lane i counts head e + 3 i of the group
-    const bool last = h < p.HG && atomicAdd(ctr + h, 1) == r.nparts - 1;
-    unsigned mask = __ballot_sync(0xffffffffu, last);
-    if (mask) {
-      __threadfence();
-      Work c;
-      c.w = 0;
-      c.u = 0;
-      c.item = r.item;
-      c.slot = 0;
-      c.q_row = r.q_row;
-      c.t0 = r.t0;
-      c.t1 = 0;
-      c.unit_base = r.unit_base;
-      c.nparts = r.nparts;
-      while (mask) {
-        const int i = __ffs(mask) - 1;
-        mask &= mask - 1;
-        c.kvh = r.hg * p.HG + e + kEpiWarps * i;
-        merge_partials<T, 8>(p, c);
-        if (lane == 0) ctr[e + kEpiWarps * i] = 0;  // workspace left clean for the next launch
-      }
     }
   }
 }
@@ -347,6 +365,7 @@ __global__ void __launch_bounds__(kTmaMaxThreads, 1) paged_attention_tma_kernel(
                                                                   const __grid_constant__ CUtensorMap tk,
                                                                   const __grid_constant__ CUtensorMap tv) {
   extern __shared__ unsigned char smem_raw[];
+  __shared__ int cta_done;
   unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5;
   const int box_bytes = p.HG * 16 * D_ * 2;
@@ -356,25 +375,18 @@ __global__ void __launch_bounds__(kTmaMaxThreads, 1) paged_attention_tma_kernel(
       mbar_init(smem_u32(base) + 8 * s, 1);
       mbar_init(smem_u32(base) + 64 + 8 * s, p.HG);
     }
-    for (int e = 0; e < kEpiWarps; ++e) {
-      const int feeders = e < p.HG ? (p.HG - 1 - e) / kEpiWarps + 1 : 1;  // consumer warps e, e + 3, ...
-      for (int sl = 0; sl < kEpiSlots; ++sl) {
-        mbar_init(smem_u32(base) + kEpiFull + 8 * (e * kEpiSlots + sl), feeders);
-        mbar_init(smem_u32(base) + kEpiEmpty + 8 * (e * kEpiSlots + sl), 1);
-      }
-    }
     fence_mbar_init();
+    cta_done = 0;
   }
   __syncthreads();
   const int n_units = min(__ldg(p.counts + 1), p.max_units);
   const int total = n_units * p.n_hg;
   if (warp < p.HG) {
     tma_consumer<T, D_>(p, base, box_bytes);
-  } else if (warp == p.HG) {
-    if ((threadIdx.x & 31) == 0) tma_producer<T, D_>(p, &tk, &tv, base, total, box_bytes, q_bytes);
-  } else {
-    tma_epilogue_warp<T>(p, base, warp - p.HG - 1);
+  } else if ((threadIdx.x & 31) == 0) {
+    cta_done = tma_producer<T, D_>(p, &tk, &tv, base, total, box_bytes, q_bytes);
   }
+  finish_launch<T, 8>(p, &cta_done, total);
 }
 
 // ---------------------------------------------------------------- host side
@@ -477,14 +489,26 @@ int launch_attention_tma(AttnParams p, int dtype, long long want, cudaStream_t s
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return fail(NF_ECUDA, "nf_paged_attention: smem attribute: %s", cudaGetErrorString(e));
   int per_sm = 1;
-  const int threads = (hg + 1 + kEpiWarps) * 32;
+  const int threads = (hg + 1) * 32;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, smem) != cudaSuccess || per_sm < 1)
     per_sm = 1;
   long long grid = (long long)sm_count() * per_sm;
   const long long need = (want + p.Hkv - 1) / p.Hkv * p.n_hg;  // work items: units x head groups
   if (need < grid) grid = need;
   if (grid < 1) grid = 1;
-  kern<<<(int)grid, threads, smem, st>>>(p, tk, tv);
+  // cooperative: the end-of-launch merge waits for every CTA
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3(threads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, kern, p, tk, tv);
+  if (e != cudaSuccess) return fail(NF_ECUDA, "nf_paged_attention: launch: %s", cudaGetErrorString(e));
   *path = permuted ? 1 : 2;
   return check_launch("nf_paged_attention");
 }

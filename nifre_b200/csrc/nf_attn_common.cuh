@@ -23,9 +23,12 @@ struct AttnParams {
   int max_units, split;
   float scale_log2;
   float* ws;    // partials [max_units][Hq][D + 4]: acc[D], m, l, pad
-  int* cnt;     // parts finished per (item, KV head)
-  int* queue;   // {next work item, warps finished}; zero between launches
+  int* cnt;     // reserved (per (item, KV head) counters of the workspace layout)
+  int* queue;   // {next work item, spare, work items finished, CTAs done}; zero between launches
   int* status;
+  const int* items;  // per query: slot, q_row, kv_len, unit_base
+  int max_items;
+  int merge;    // some item has more than one part
   // launch plan
   int W, stages, head_bytes, stage_bytes, swz, tile, bs16, q_smem;
   int HG, n_hg;  // tensor-map path: KV heads per CTA and head groups
@@ -43,6 +46,7 @@ __device__ __forceinline__ int tile_off(int r, int c, int head_bytes, int swz) {
 struct Work {
   int w;  // work item index; < 0 marks the end of this warp's work
   int u, item, slot, q_row, t0, t1, unit_base, nparts, kvh;
+  int part;  // index of this unit among its item's parts
 };
 
 __device__ __forceinline__ int checked_block(const AttnParams& p, const int* btrow, int lb) {
@@ -57,115 +61,124 @@ __device__ __forceinline__ int checked_block(const AttnParams& p, const int* btr
 // Split-K part slot of a unit in the workspace: the parts of one item are
 // contiguous from its unit_base, in key order, wherever the unit sits in the
 // unit list.
-__device__ __forceinline__ int part_index(const AttnParams& p, const Work& c) { return c.unit_base + c.t0 / p.split; }
+__device__ __forceinline__ int part_index(const AttnParams&, const Work& c) { return c.unit_base + c.part; }
 
 // ---------------------------------------------------------------- split-K merge
-// Merges the nparts (acc, m, l) records of one (item, KV head) into the
-// output: out = sum_j 2^(m_j - M) acc_j / sum_j 2^(m_j - M) l_j.  Lane e owns
-// float4 chunks e and e + 32 of the group's G x D outputs; one pass over the
-// parts with PB parts' loads in flight per lane and a running maximum (the
-// sums are rescaled when it grows), so the merge costs about nparts / PB
-// round trips to L2.
+// Merges float4 chunks c0 .. c0+31 (one per lane) of the G x D outputs of
+// one (item, KV head): out = sum_j 2^(m_j - M) acc_j / sum_j 2^(m_j - M) l_j,
+// one pass over the parts with PB parts' loads in flight and a running
+// maximum (the sums are rescaled when it grows).
 template <typename T, int PB>
-__device__ void merge_partials(const AttnParams& p, const Work& c) {
+__device__ void merge_chunk(const AttnParams& p, const Work& c, int c0) {
   const int lane = threadIdx.x & 31;
-  const int D = p.D, DP = D + 4, G = p.G;
-  const float* part0 = p.ws + ((long long)c.unit_base * p.Hq + (long long)c.kvh * G) * DP;
+  const int D = p.D, DP = D + 4, D4 = D >> 2, GD4 = p.G * D4;
+  const int e = min(c0 + lane, GD4 - 1), hn = e / D4, d = (e - hn * D4) * 4;
+  const float* pe = p.ws + ((long long)c.unit_base * p.Hq + (long long)c.kvh * p.G + hn) * DP;
   const long long ps = (long long)p.Hq * DP;  // between consecutive parts
-  T* o = reinterpret_cast<T*>(p.out) + (long long)c.q_row * p.out_stride + (long long)c.kvh * G * D;
-  const int D4 = D >> 2, GD4 = G * D4;
-  for (int e0 = 0; e0 < GD4; e0 += 64) {
-    const int ea = min(e0 + lane, GD4 - 1), eb = min(e0 + 32 + lane, GD4 - 1);
-    const int ha = ea / D4, hb = eb / D4;
-    const float* pa = part0 + ha * DP + (ea - ha * D4) * 4;
-    const float* pb = part0 + hb * DP + (eb - hb * D4) * 4;
-    const float* ma = part0 + ha * DP + D;
-    const float* mb = part0 + hb * DP + D;
-    float Ma = kNegInf, Mb = kNegInf, La = 0.f, Lb = 0.f;
-    float4 A = make_float4(0.f, 0.f, 0.f, 0.f), B = A;
-    for (int j = 0; j < c.nparts; j += PB) {
-      float4 xa[PB], xb[PB];
-      float2 la[PB], lb[PB];
+  float M = kNegInf, L = 0.f;
+  float4 A = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int j = 0; j < c.nparts; j += PB) {
+    float4 x[PB];
+    float2 ml[PB];
 #pragma unroll
-      for (int u = 0; u < PB; ++u) {
-        if (j + u < c.nparts) {
-          const long long off = (long long)(j + u) * ps;
-          la[u] = __ldcg(reinterpret_cast<const float2*>(ma + off));
-          lb[u] = __ldcg(reinterpret_cast<const float2*>(mb + off));
-          xa[u] = __ldcg(reinterpret_cast<const float4*>(pa + off));
-          xb[u] = __ldcg(reinterpret_cast<const float4*>(pb + off));
-        } else {
-          la[u] = lb[u] = make_float2(kNegInf, 0.f);
-          xa[u] = xb[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-        }
+    for (int u = 0; u < PB; ++u) {
+      if (j + u < c.nparts) {
+        const float* pj = pe + (j + u) * ps;
+        ml[u] = __ldcg(reinterpret_cast<const float2*>(pj + D));
+        x[u] = __ldcg(reinterpret_cast<const float4*>(pj + d));
+      } else {
+        ml[u] = make_float2(kNegInf, 0.f);
+        x[u] = make_float4(0.f, 0.f, 0.f, 0.f);
       }
-      float na = Ma, nb = Mb;
+    }
+    float nm = M;
 #pragma unroll
-      for (int u = 0; u < PB; ++u) {
-        na = fmaxf(na, la[u].x);
-        nb = fmaxf(nb, lb[u].x);
-      }
-      // parts with m = -inf saw no key; 2^(-inf) = 0 drops them
-      const float ba = na == kNegInf ? 0.f : na, bb = nb == kNegInf ? 0.f : nb;
-      const float sa = ex2(Ma - ba), sb = ex2(Mb - bb);
-      A.x *= sa; A.y *= sa; A.z *= sa; A.w *= sa; La *= sa;
-      B.x *= sb; B.y *= sb; B.z *= sb; B.w *= sb; Lb *= sb;
+    for (int u = 0; u < PB; ++u) nm = fmaxf(nm, ml[u].x);
+    const float b = nm == kNegInf ? 0.f : nm;  // parts with m = -inf saw no key: 2^(-inf) = 0
+    const float sc = ex2(M - b);
+    A.x *= sc; A.y *= sc; A.z *= sc; A.w *= sc; L *= sc;
 #pragma unroll
-      for (int u = 0; u < PB; ++u) {
-        const float wa = la[u].x == kNegInf ? 0.f : ex2(la[u].x - ba);
-        const float wb = lb[u].x == kNegInf ? 0.f : ex2(lb[u].x - bb);
-        A.x += xa[u].x * wa; A.y += xa[u].y * wa; A.z += xa[u].z * wa; A.w += xa[u].w * wa; La += la[u].y * wa;
-        B.x += xb[u].x * wb; B.y += xb[u].y * wb; B.z += xb[u].z * wb; B.w += xb[u].w * wb; Lb += lb[u].y * wb;
-      }
-      Ma = na;
-      Mb = nb;
+    for (int u = 0; u < PB; ++u) {
+      const float w = ml[u].x == kNegInf ? 0.f : ex2(ml[u].x - b);
+      A.x += x[u].x * w; A.y += x[u].y * w; A.z += x[u].z * w; A.w += x[u].w * w; L += ml[u].y * w;
     }
-    if (e0 + lane < GD4) {
-      const float inv = La > 0.f ? 1.f / La : 0.f;
-      T* od = o + ha * D + (ea - ha * D4) * 4;
-      od[0] = Elem<T>::from_f(A.x * inv);
-      od[1] = Elem<T>::from_f(A.y * inv);
-      od[2] = Elem<T>::from_f(A.z * inv);
-      od[3] = Elem<T>::from_f(A.w * inv);
-    }
-    if (e0 + 32 + lane < GD4) {
-      const float inv = Lb > 0.f ? 1.f / Lb : 0.f;
-      T* od = o + hb * D + (eb - hb * D4) * 4;
-      od[0] = Elem<T>::from_f(B.x * inv);
-      od[1] = Elem<T>::from_f(B.y * inv);
-      od[2] = Elem<T>::from_f(B.z * inv);
-      od[3] = Elem<T>::from_f(B.w * inv);
-    }
+    M = nm;
+  }
+  if (c0 + lane < GD4) {
+    const float inv = L > 0.f ? 1.f / L : 0.f;
+    T* od = reinterpret_cast<T*>(p.out) + (long long)c.q_row * p.out_stride + ((long long)c.kvh * p.G + hn) * D + d;
+    od[0] = Elem<T>::from_f(A.x * inv);
+    od[1] = Elem<T>::from_f(A.y * inv);
+    od[2] = Elem<T>::from_f(A.z * inv);
+    od[3] = Elem<T>::from_f(A.w * inv);
   }
 }
 
-// After this warp wrote its part: count it; the last part merges (PB: parts'
-// loads in flight per lane, see merge_partials).
+// End of a launch, called by every thread of every CTA once the CTA's work
+// items are done (my_done of them, summed over the CTA by the caller in
+// *cta_done).  Thread 0 adds them to the grid count and waits, with a time
+// limit, until all `total` work items have stored their outputs or parts;
+// then every warp of the grid takes a share of the split-K merges (one warp
+// per (item, KV head) with more than one part).  The last CTA out resets the
+// queue and the counts for the next launch.  The wait needs every CTA
+// resident at once: the kernels are launched cooperatively.
 template <typename T, int PB>
-__device__ void finish_partial(const AttnParams& p, const Work& c) {
-  __threadfence();
-  __syncwarp();
-  int last = 0;
-  int* ctr = p.cnt + (long long)c.item * p.Hkv + c.kvh;
-  if ((threadIdx.x & 31) == 0) last = (atomicAdd(ctr, 1) == c.nparts - 1);
-  last = __shfl_sync(0xffffffffu, last, 0);
-  if (last) {
+__device__ void finish_launch(const AttnParams& p, int* cta_done, int total) {
+  __shared__ int go;
+  __syncthreads();  // the CTA's output and part stores are issued
+  if (threadIdx.x == 0) {
     __threadfence();
-    merge_partials<T, PB>(p, c);
-    if ((threadIdx.x & 31) == 0) *ctr = 0;  // workspace left clean for the next launch
-  }
-}
-
-// The last of `participants` queue users (warps or CTAs) to run out of work
-// resets the queue for the next launch.
-__device__ __forceinline__ void retire_worker(const AttnParams& p, int participants) {
-  if ((threadIdx.x & 31) == 0) {
-    __threadfence();
-    if (atomicAdd(p.queue + 1, 1) == participants - 1) {
-      p.queue[0] = 0;
-      p.queue[1] = 0;
-      __threadfence();
+    atomicAdd(p.queue + 2, *cta_done);
+    int ok = 1;
+    const long long t0 = clock64();
+    while (*reinterpret_cast<volatile int*>(p.queue + 2) < total) {
+      if (clock64() - t0 > kWaitLimitCycles) {
+        atomicOr(p.status, NF_STATUS_WAIT_TIMEOUT);
+        ok = 0;
+        break;
+      }
+      __nanosleep(256);
     }
+    __threadfence();
+    go = ok;
+  }
+  __syncthreads();
+  if (go && p.merge) {
+    // tasks: (item, KV head, group of 32 output chunks), dealt round-robin
+    // over the CTAs so that every SM takes a share
+    const int n_items = min(__ldg(p.counts), p.max_items);
+    const int n_units = min(__ldg(p.counts + 1), p.max_units);
+    const int groups = (p.G * (p.D >> 2) + 31) >> 5;
+    const int tasks = n_items * p.Hkv * groups;
+    const int stride = gridDim.x * (blockDim.x >> 5);
+    for (int task = (threadIdx.x >> 5) * gridDim.x + blockIdx.x; task < tasks; task += stride) {
+      const int pair = task / groups, grp = task - pair * groups;
+      const int t = pair / p.Hkv;
+      const int4 it = __ldg(reinterpret_cast<const int4*>(p.items) + t);
+      const int next = t + 1 < n_items ? __ldg(p.items + 4 * (t + 1) + 3) : n_units;
+      const int nparts = next - it.w;
+      if (nparts <= 1 || it.w < 0 || next > p.max_units) continue;  // written directly, or a flagged overflow
+      Work c;
+      c.w = task;
+      c.u = 0;
+      c.item = t;
+      c.slot = it.x;
+      c.q_row = it.y;
+      c.t0 = c.t1 = 0;
+      c.unit_base = it.w;
+      c.nparts = nparts;
+      c.kvh = pair - t * p.Hkv;
+      c.part = 0;
+      merge_chunk<T, PB>(p, c, grp * 32);
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && atomicAdd(p.queue + 3, 1) == (int)gridDim.x - 1) {
+    p.queue[0] = 0;
+    p.queue[1] = 0;
+    p.queue[2] = 0;
+    p.queue[3] = 0;
+    __threadfence();
   }
 }
 
@@ -231,17 +244,15 @@ __device__ __forceinline__ void mma_store_part(const AttnParams& p, const Work& 
   }
 }
 
-// Output rows when the item has one part, else the part record and the
-// split-K bookkeeping (the last part merges).
+// Output rows when the item has one part, else the part record (merged at
+// the end of the launch, finish_launch).
 template <typename T, int D_>
 __device__ __forceinline__ void mma_epilogue(const AttnParams& p, const Work& c, float (&o)[D_ / 16][4], float m0,
                                              float m1, float l0, float l1) {
-  if (c.nparts == 1) {
+  if (c.nparts == 1)
     mma_store_output<T, D_>(p, c, o, l0, l1);
-  } else {
+  else
     mma_store_part<T, D_>(p, c, o, m0, m1, l0, l1);
-    finish_partial<T, 2>(p, c);
-  }
 }
 
 }  // namespace nf

@@ -21,6 +21,7 @@ struct PackParams {
   int n_patches;
   int* bt;
   int num_slots, max_blocks, bs, num_blocks, split;
+  const int* seq_split;  // per-sequence unit size (NULL: split for all)
   int* slot_mapping;
   int* src_rows;
   long long* positions;
@@ -79,6 +80,24 @@ __device__ int cta_exclusive_scan(int* a, int n, int stride) {
   return carry;
 }
 
+// Sequence of token t: the last s with cu[s] <= t (cu = query offsets).
+__device__ __forceinline__ int seq_of(const int* cu, int n_seqs, int t) {
+  int lo = 0, hi = n_seqs - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (cu[mid] <= t) lo = mid; else hi = mid - 1;
+  }
+  return lo;
+}
+
+// Unit size of sequence s: its seq_split entry when that is a positive
+// multiple of 16, else the step's split.
+__device__ __forceinline__ int unit_size(const PackParams& p, int s) {
+  if (!p.seq_split) return p.split;
+  const int v = p.seq_split[s];
+  return (v > 0 && (v & 15) == 0) ? v : p.split;
+}
+
 __global__ void __launch_bounds__(kPackThreads) pack_kernel(const PackParams p) {
   extern __shared__ int cu[];  // n_seqs + 1 query offsets
   const int tid = threadIdx.x;
@@ -103,12 +122,7 @@ __global__ void __launch_bounds__(kPackThreads) pack_kernel(const PackParams p) 
 
   // 3. per-token expansion: slot mapping, source row, position, work item.
   for (int t = tid; t < T; t += kPackThreads) {
-    int lo = 0, hi = p.n_seqs - 1;  // last s with cu[s] <= t
-    while (lo < hi) {
-      const int mid = (lo + hi + 1) >> 1;
-      if (cu[mid] <= t) lo = mid; else hi = mid - 1;
-    }
-    const int s = lo, i = t - cu[s];
+    const int s = seq_of(cu, p.n_seqs, t), i = t - cu[s];
     int slot = p.seqs[4 * s];
     const int q_start = p.seqs[4 * s + 1], ctx_before = p.seqs[4 * s + 3];
     if (slot < 0 || slot >= p.num_slots) {
@@ -130,65 +144,53 @@ __global__ void __launch_bounds__(kPackThreads) pack_kernel(const PackParams p) 
     it.x = slot;
     it.y = q_start + i;
     it.z = kv_len;
-    it.w = (kv_len + p.split - 1) / p.split;  // number of splits; scanned below
+    const int us = unit_size(p, s);
+    it.w = (kv_len + us - 1) / us;  // number of parts; scanned below
     reinterpret_cast<int4*>(p.items)[t] = it;
   }
   __syncthreads();
   // 4. unit base of each item: scan of the split counts.
   const int n_units = cta_exclusive_scan(p.items + 3, T, 4);
-  // 5. the unit list, one self-contained record per key range of an item.
-  // Full-length units come first, then each item's shorter remainder unit,
-  // longest first (64 buckets of split/64 keys; any order inside a bucket):
-  // workers that take units in list order then end on the shortest ones,
-  // which evens out their finish times.  The record keeps the item's
-  // unit_base and the range's first key, so a unit's split-K part index is
-  // unit_base + key_begin / split wherever it sits in the list, and the
-  // results do not depend on the order.
-  constexpr int kBuckets = 64;
-  __shared__ int bucket_n[kBuckets], bucket_off[kBuckets];
-  __shared__ int n_rem_sh;
-  for (int b = tid; b < kBuckets; b += kPackThreads) bucket_n[b] = 0;
-  if (tid == 0) n_rem_sh = 0;
+  // 5. the unit list, one self-contained record per key range of an item:
+  // (item, slot, q_row, part, key_begin, key_end, unit_base, n_parts).  The
+  // parts of an item are contiguous from its unit_base in key order (that is
+  // where the kernels put their split-K partials); the list itself holds the
+  // units of sequences with the step's split first and the units of
+  // sequences given a smaller unit size after them, each class in item
+  // order.  Workers that take units in list order so end on short units and
+  // finish close together, and the items of the first class complete, and
+  // merge, while the bulk of the keys still streams.
+  __shared__ int n_fine_sh;
+  if (tid == 0) n_fine_sh = 0;
   __syncthreads();
-  auto bucket_of = [&](int rem) { return (int)(((long long)(rem - 1) * kBuckets) / p.split); };
-  int my_rem = 0;
+  int my_fine = 0;
   for (int t = tid; t < T; t += kPackThreads) {
-    const int rem = p.items[4 * t + 2] % p.split;
-    if (rem) {
-      ++my_rem;
-      atomicAdd(&bucket_n[bucket_of(rem)], 1);
-    }
+    const int us = unit_size(p, seq_of(cu, p.n_seqs, t));
+    if (us < p.split) my_fine += (p.items[4 * t + 2] + us - 1) / us;
   }
-  if (my_rem) atomicAdd(&n_rem_sh, my_rem);
+  if (my_fine) atomicAdd(&n_fine_sh, my_fine);
   __syncthreads();
-  const int n_full = n_units - n_rem_sh;
-  if (tid == 0) {
-    int acc = n_full;
-    for (int b = kBuckets - 1; b >= 0; --b) {
-      bucket_off[b] = acc;  // list position of the next remainder unit of bucket b
-      acc += bucket_n[b];
-    }
-  }
-  __syncthreads();
-  int rem_carry = 0;
+  const int n_bulk = n_units - n_fine_sh;
+  int fine_carry = 0;
   for (int base = 0; base < T; base += kPackThreads) {
     const int t = base + tid;
     int4 it = make_int4(0, 0, 0, 0);
-    int rem = 0;
+    int us = p.split, n = 0;
     if (t < T) {
       it = reinterpret_cast<const int4*>(p.items)[t];
-      rem = it.z % p.split;
+      us = unit_size(p, seq_of(cu, p.n_seqs, t));
+      n = (it.z + us - 1) / us;
     }
-    const int r = cta_scan_round(rem != 0, rem_carry);  // remainder units of the items before t
+    const bool fine = us < p.split;
+    const int fb = cta_scan_round(fine ? n : 0, fine_carry);  // fine units of the items before t
     if (t < T) {
-      const int nfull = it.z / p.split, n = nfull + (rem != 0);
-      const int f = it.w - r;  // full units of the items before t
+      const int first = fine ? n_bulk + fb : it.w - fb;  // list position of the item's first unit
       for (int j = 0; j < n; ++j) {
-        const int u = j < nfull ? f + j : atomicAdd(&bucket_off[bucket_of(rem)], 1);
+        const int u = first + j;
         if (u < p.max_units) {
           int4* rec = reinterpret_cast<int4*>(p.units) + 2 * u;
-          rec[0] = make_int4(t, it.x, it.y, it.z);
-          rec[1] = make_int4(j * p.split, min((j + 1) * p.split, it.z), it.w, n);
+          rec[0] = make_int4(t, it.x, it.y, j);
+          rec[1] = make_int4(j * us, min((j + 1) * us, it.z), it.w, n);
         }
       }
     }
@@ -205,6 +207,7 @@ __global__ void __launch_bounds__(kPackThreads) pack_kernel(const PackParams p) 
 extern "C" int nf_pack_step(const int32_t* seqs, int32_t n_seqs, const int32_t* patches, int32_t n_patches,
                             int32_t* block_tables, int32_t num_slots, int32_t max_blocks_per_seq,
                             int32_t block_size, int32_t num_blocks, int32_t split_tokens,
+                            const int32_t* seq_split,
                             int32_t* slot_mapping, int32_t* src_rows, int64_t* positions, int32_t* items,
                             int32_t* units, int32_t* counts, int32_t n_tokens, int32_t max_units,
                             int32_t* status, void* stream) {
@@ -216,6 +219,8 @@ extern "C" int nf_pack_step(const int32_t* seqs, int32_t n_seqs, const int32_t* 
   if (block_size <= 0 || split_tokens <= 0 || num_slots <= 0 || max_blocks_per_seq <= 0 || num_blocks <= 0)
     return fail(NF_EINVAL, "nf_pack_step: sizes must be positive");
   if (max_units <= 0) return fail(NF_EINVAL, "nf_pack_step: max_units must be positive");
+  if (split_tokens % 16 != 0)
+    return fail(NF_EINVAL, "nf_pack_step: split_tokens (%d) must be a multiple of 16", split_tokens);
   if ((reinterpret_cast<uintptr_t>(items) & 15) != 0 || (reinterpret_cast<uintptr_t>(units) & 15) != 0)
     return fail(NF_EINVAL, "nf_pack_step: items and units must be 16-byte aligned");
   const size_t smem = sizeof(int) * (size_t)(n_seqs + 1);
@@ -232,6 +237,7 @@ extern "C" int nf_pack_step(const int32_t* seqs, int32_t n_seqs, const int32_t* 
   p.bs = block_size;
   p.num_blocks = num_blocks;
   p.split = split_tokens;
+  p.seq_split = seq_split;
   p.slot_mapping = slot_mapping;
   p.src_rows = src_rows;
   p.positions = reinterpret_cast<long long*>(positions);

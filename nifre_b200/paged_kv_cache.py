@@ -55,6 +55,29 @@ class _DeviceBuffer:
         return self.t
 
 
+def seq_unit_sizes(seq_keys: np.ndarray, split: int, sms: int, fine_div: int = 4) -> np.ndarray:
+    """Split-K unit size of each sequence of a step.
+
+    The bulk of the step uses ``split`` keys per unit.  The shortest
+    sequences that together hold at least one wave of units (``sms * split``
+    keys) use ``split / fine_div`` (a multiple of 16); nf_pack_step lists their
+    units after all others, so a dynamic queue ends on short units and the
+    workers finish close together, while being short keeps their split-K
+    merges cheap.  Steps with under two waves of keys use ``split``
+    throughout.
+    """
+    seq_keys = np.asarray(seq_keys, dtype=np.int64)
+    sizes = np.full(len(seq_keys), split, dtype=np.int32)
+    fine = max(16, (split // fine_div) // 16 * 16)
+    wave = sms * split
+    if fine >= split or int(seq_keys.sum()) < 2 * wave:
+        return sizes
+    order = np.argsort(seq_keys, kind="stable")  # shortest first
+    n_fine = int(np.searchsorted(np.cumsum(seq_keys[order]), wave)) + 1
+    sizes[order[:n_fine]] = fine
+    return sizes
+
+
 class StepPlan:
     """Device metadata of one forward pass over a ragged batch.
 
@@ -62,7 +85,7 @@ class StepPlan:
     last layer has appended.
     """
 
-    def __init__(self, slots, q_lens, q_starts, ctx_before, split, max_units):
+    def __init__(self, slots, q_lens, q_starts, ctx_before, split, max_units, seq_split=None):
         self.slots = slots
         self.q_lens = q_lens
         self.q_starts = q_starts
@@ -71,6 +94,7 @@ class StepPlan:
         self.n_tokens = int(q_lens.sum())
         self.rows_needed = int((q_starts + q_lens).max())
         self.split = split
+        self.seq_split = seq_split  # unit size of each sequence (numpy)
         self.max_units = max_units
         self.key = None
         self.closed = False
@@ -204,19 +228,27 @@ class PagedKVCache:
         self.pos[slot] = value
 
     # ------------------------------------------------------------------ step planning
+    @property
+    def sm_count(self) -> int:
+        if getattr(self, "_sm_count", None) is None:
+            self._sm_count = torch.cuda.get_device_properties(self.device).multi_processor_count
+        return self._sm_count
+
     def split_for(self, total_keys: int, units_per_sm: int = 4) -> int:
         """Keys per split-K unit: ~units_per_sm units per SM, a multiple of 128."""
-        sms = torch.cuda.get_device_properties(self.device).multi_processor_count
-        s = total_keys / max(1, units_per_sm * sms)
+        s = total_keys / max(1, units_per_sm * self.sm_count)
         return max(128, int(math.ceil(s / 128.0)) * 128)
 
-    def plan(self, slots, q_lens, q_starts, split: int | None = None) -> StepPlan:
+    def plan(self, slots, q_lens, q_starts, split: int | None = None, fine_tail: bool = True) -> StepPlan:
         """Allocate blocks for a step and pack its metadata on the GPU.
 
         ``slots[i]`` gets ``q_lens[i]`` new tokens whose rows in the caller's
         q/k/v tensors start at ``q_starts[i]``.  Allocation happens in list
         order, like the reference's row loop (paged_kv_cache.py:110-111).
         Raises before any launch on an over-long sequence or an exhausted pool.
+        ``split`` (a multiple of 16) overrides the unit size chosen for the
+        step; ``fine_tail`` gives the shortest sequences smaller units
+        (``seq_unit_sizes``).
         """
         slots = np.asarray(slots, dtype=np.int64)
         q_lens = np.asarray(q_lens, dtype=np.int64)
@@ -258,13 +290,20 @@ class PagedKVCache:
         kv = np.repeat(ctx + 1, q_lens) + (np.arange(T) - np.repeat(np.cumsum(q_lens) - q_lens, q_lens))
         if split is None:
             split = self.split_for(int(kv.sum()))
-        max_units = int(((kv + split - 1) // split).sum())
+        if split <= 0 or split % 16:
+            raise ValueError(f"split ({split}) must be a positive multiple of 16")
+        seq_keys = q_lens * (ctx + 1) + q_lens * (q_lens - 1) // 2
+        seq_split = (seq_unit_sizes(seq_keys, split, self.sm_count) if fine_tail
+                     else np.full(S, split, dtype=np.int32))
+        item_split = np.repeat(seq_split.astype(np.int64), q_lens)
+        max_units = int(((kv + item_split - 1) // item_split).sum())
 
-        host = np.empty(S * 4 + P * 3, dtype=np.int32)
+        host = np.empty(S * 5 + P * 3, dtype=np.int32)
         host[: S * 4] = np.stack([slots, q_starts, q_lens, ctx], axis=1).reshape(-1)
         if P:
-            host[S * 4:] = np.asarray(patches, dtype=np.int32).reshape(-1)
-        off_slot = _align4(S * 4 + P * 3)
+            host[S * 4: S * 4 + P * 3] = np.asarray(patches, dtype=np.int32).reshape(-1)
+        host[S * 4 + P * 3:] = seq_split
+        off_slot = _align4(S * 5 + P * 3)
         off_src = off_slot + T
         off_items = _align4(off_src + T)
         off_units = off_items + 4 * T
@@ -273,7 +312,7 @@ class PagedKVCache:
         meta[: host.size].copy_(torch.from_numpy(host).pin_memory(), non_blocking=True)
         pos_dev = self._pos_buf.get(T)
 
-        plan = StepPlan(slots, q_lens, q_starts, ctx, split, max_units)
+        plan = StepPlan(slots, q_lens, q_starts, ctx, split, max_units, seq_split)
         plan.seqs = meta[: S * 4]
         plan.slot_mapping = meta[off_slot: off_slot + T]
         plan.src_rows = meta[off_src: off_src + T]
@@ -285,7 +324,8 @@ class PagedKVCache:
         _lib.check(lib.nf_pack_step(
             meta.data_ptr(), S, meta.data_ptr() + 4 * S * 4 if P else None, P,
             self.bt_dev.data_ptr(), self.batch_size, self.max_blocks_per_seq, self.block_size,
-            self.num_blocks, split, plan.slot_mapping.data_ptr(), plan.src_rows.data_ptr(),
+            self.num_blocks, split, meta.data_ptr() + 4 * (S * 4 + P * 3),
+            plan.slot_mapping.data_ptr(), plan.src_rows.data_ptr(),
             plan.positions.data_ptr(), plan.items.data_ptr(), plan.units.data_ptr(), plan.counts.data_ptr(),
             T, max_units, self.status.data_ptr(), _lib.stream_handle(self.device)), "nf_pack_step")
         self._plan = plan

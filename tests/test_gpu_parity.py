@@ -144,7 +144,8 @@ def test_decode_vs_oracle(dtype, D, Hq, Hkv, split):
 
 
 def test_pack_unit_list():
-    """Every key range of every item appears once; full units first, remainders longest first."""
+    """Every key range of every item appears once with its part index; the units of
+    sequences at the step's split come first, then the short-unit tail, each in item order."""
     import numpy as np
     rng = np.random.default_rng(3)
     ctx = rng.integers(1, 3000, size=64).tolist()
@@ -152,26 +153,27 @@ def test_pack_unit_list():
     B, split = len(ctx), 128
     plan = cache.plan(list(range(B)), [1] * B, list(range(B)), split=split)
     kv = np.array(ctx) + 1
-    n_units = int(((kv + split - 1) // split).sum())
+    us = plan.seq_split.astype(np.int64)
+    assert (us < split).any() and (us == split).any()
+    nsp = (kv + us - 1) // us
+    n_units = int(nsp.sum())
     counts = plan.counts.cpu().numpy()
-    assert counts[0] == B and counts[1] == n_units
+    assert counts[0] == B and counts[1] == n_units == plan.max_units
     items = plan.items.cpu().numpy().reshape(-1, 4)[:B]
     units = plan.units.cpu().numpy().reshape(-1, 8)[:n_units]
-    nsp = (kv + split - 1) // split
     assert (items[:, 2] == kv).all()
     assert (items[:, 3] == np.concatenate([[0], np.cumsum(nsp)[:-1]])).all()  # unit_base
     seen = set()
-    for t, slot, q_row, kvl, k0, k1, ub, n in units.tolist():
-        assert (slot, q_row, kvl, ub, n) == (t, t, kv[t], items[t, 3], nsp[t])
-        assert k0 % split == 0 and k1 == min(k0 + split, kvl)
-        seen.add((t, k0 // split))
+    for t, slot, q_row, part, k0, k1, ub, n in units.tolist():
+        assert (slot, q_row, ub, n) == (t, t, items[t, 3], nsp[t])
+        assert k0 == part * us[t] and k1 == min(k0 + us[t], kv[t])
+        seen.add((t, part))
     assert seen == {(t, j) for t in range(B) for j in range(nsp[t])}
-    lens = units[:, 5] - units[:, 4]
-    n_full = int((kv // split).sum())
-    assert (lens[:n_full] == split).all() and (lens[n_full:] < split).all()
-    assert (units[:n_full, 0] == np.repeat(np.arange(B), kv // split)).all()  # full units in item order
-    buckets = (lens[n_full:] - 1) * 64 // split
-    assert (np.diff(buckets) <= 0).all()
+    fine = us[units[:, 0]] < split
+    n_bulk = int(nsp[us == split].sum())
+    assert not fine[:n_bulk].any() and fine[n_bulk:].all()
+    key = units[:, 0].astype(np.int64) * 100000 + units[:, 3]  # (item, part)
+    assert (np.diff(key[:n_bulk]) > 0).all() and (np.diff(key[n_bulk:]) > 0).all()
     cache.check_status()
 
 

@@ -199,7 +199,7 @@ def test_library_exports_every_declared_symbol():
     for s in syms:
         assert hasattr(lib, s), s
     assert set(_lib.EXPORTS) <= set(syms)
-    assert _lib.load().nf_abi_version() == 3
+    assert _lib.load().nf_abi_version() == 4
 
 
 def test_workspace_sizing_and_argument_errors():
@@ -207,9 +207,9 @@ def test_workspace_sizing_and_argument_errors():
     from nifre_b200 import _lib
     import torch
     pf, ci = _lib.workspace_sizes(100, 64, 32, 8, 64, torch.bfloat16)
-    assert pf == 100 * 32 * 68 and ci == 64 * 8 + 2  # (acc, m, l, pad) per part; counters + work queue
+    assert pf == 100 * 32 * 68 and ci == 64 * 8 + 4  # (acc, m, l, pad) per part; counters + work queue
     pf, ci = _lib.workspace_sizes(10, 4, 8, 1, 128, torch.bfloat16)
-    assert pf == 10 * 8 * 132 and ci == 4 + 2
+    assert pf == 10 * 8 * 132 and ci == 4 + 4
     with pytest.raises(_lib.NifreError, match="multiple of num_kv_heads"):
         _lib.workspace_sizes(1, 1, 6, 4, 64, torch.bfloat16)
     with pytest.raises(_lib.NifreError, match="more than 8"):
@@ -217,3 +217,22 @@ def test_workspace_sizing_and_argument_errors():
     lib = _lib.load()
     rc = lib.nf_kv_append(None, None, 0, 0, None, None, 0, 0, 0, None, None, 0, 1, 1, None, 0, None, None, None)
     assert rc == 1 and b"n_tokens" in lib.nf_last_error()
+
+
+def test_seq_unit_sizes_policy():
+    """The shortest sequences holding one wave of keys get quarter-size units; small steps none."""
+    import numpy as np
+    from nifre_b200.paged_kv_cache import seq_unit_sizes
+    rng = np.random.default_rng(0)
+    keys = rng.integers(500, 4000, size=64)
+    split, sms = 256, 148
+    small = seq_unit_sizes(keys[:4], split, sms)
+    assert (small == split).all()
+    sizes = seq_unit_sizes(keys, split, sms)
+    fine = sizes < split
+    assert set(sizes.tolist()) == {split, split // 4}
+    wave = sms * split
+    assert keys[fine].sum() >= wave
+    assert keys[fine].max() <= keys[~fine].min()  # the shortest ones
+    assert keys[fine].sum() - keys[fine].max() < wave  # and no more than needed
+    assert (seq_unit_sizes(keys, 32, sms) >= 16).all()
