@@ -43,21 +43,29 @@ struct StepRec {  // one 16-key step as the producer describes it to the consume
   int u, item, q_row, t0, t1, unit_base, nsplits, hg, t, first, last, part, pad[4];
 };
 
+// Keys and values are read once per launch: their lines go first when L2
+// needs room, so the split-K parts and the queries stay cached.
+__device__ __forceinline__ uint64_t l2_evict_first() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+
 __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2, int c3,
-                                            uint32_t bar) {
+                                            uint32_t bar, uint64_t pol) {
   asm volatile(
-      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], "
-      "[%6];" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar)
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, {%2, "
+      "%3, %4, %5}], [%6], %7;" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar), "l"(pol)
       : "memory");
 }
 
 __device__ __forceinline__ void tma_load_5d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2, int c3,
-                                            int c4, uint32_t bar) {
+                                            int c4, uint32_t bar, uint64_t pol) {
   asm volatile(
-      "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5, "
-      "%6}], [%7];" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4), "r"(bar)
+      "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, {%2, "
+      "%3, %4, %5, %6}], [%7], %8;" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4), "r"(bar), "l"(pol)
       : "memory");
 }
 
@@ -86,6 +94,7 @@ __device__ int tma_producer(const AttnParams& p, const CUtensorMap* tk, const CU
   // first block-table entry kGap steps after that, each once the previous
   // result has had time to arrive.  Short units take the stalls.
   constexpr int kAhead = 8, kGap = 2;
+  const uint64_t pol = l2_evict_first();
   const int4* urec = reinterpret_cast<const int4*>(p.units);
   int k = 0;           // steps issued
   int s = 0;           // slot of step k (k mod S)
@@ -131,11 +140,11 @@ __device__ int tma_producer(const AttnParams& p, const CUtensorMap* tk, const CU
       mbar_arrive_expect_tx(full(s), 2 * box_bytes + (r.first ? q_bytes : 0));
       if (p.swz) {  // permuted-stride map: one box = 16 tokens x HG heads
         if constexpr (D_ == 64) {
-          tma_load_4d(sb, tk, 0, off, h0, phys, full(s));
-          tma_load_4d(sb + box_bytes, tv, 0, off, h0, phys, full(s));
+          tma_load_4d(sb, tk, 0, off, h0, phys, full(s), pol);
+          tma_load_4d(sb + box_bytes, tv, 0, off, h0, phys, full(s), pol);
         } else {
-          tma_load_5d(sb, tk, 0, off, 0, h0, phys, full(s));
-          tma_load_5d(sb + box_bytes, tv, 0, off, 0, h0, phys, full(s));
+          tma_load_5d(sb, tk, 0, off, 0, h0, phys, full(s), pol);
+          tma_load_5d(sb + box_bytes, tv, 0, off, 0, h0, phys, full(s), pol);
         }
       } else {  // increasing-stride map: one box per head (and per half of a 128-wide head)
         for (int h = 0; h < p.HG; ++h)
@@ -143,11 +152,11 @@ __device__ int tma_producer(const AttnParams& p, const CUtensorMap* tk, const CU
           for (int dh = 0; dh < NDH; ++dh) {
             const uint32_t d = sb + (h * NDH + dh) * 2048;
             if constexpr (D_ == 64) {
-              tma_load_4d(d, tk, 0, h0 + h, off, phys, full(s));
-              tma_load_4d(d + box_bytes, tv, 0, h0 + h, off, phys, full(s));
+              tma_load_4d(d, tk, 0, h0 + h, off, phys, full(s), pol);
+              tma_load_4d(d + box_bytes, tv, 0, h0 + h, off, phys, full(s), pol);
             } else {
-              tma_load_5d(d, tk, 0, dh, h0 + h, off, phys, full(s));
-              tma_load_5d(d + box_bytes, tv, 0, dh, h0 + h, off, phys, full(s));
+              tma_load_5d(d, tk, 0, dh, h0 + h, off, phys, full(s), pol);
+              tma_load_5d(d + box_bytes, tv, 0, dh, h0 + h, off, phys, full(s), pol);
             }
           }
       }
