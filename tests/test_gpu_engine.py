@@ -1,0 +1,52 @@
+"""The engine on a B200 against the reference Engine's recorded outputs.
+
+Config 1 of the benchmark: the reference GptModel (seed 0, fp32) behind
+Engine(max_concurrent_requests=8, prefill_chunk_size=128,
+max_tokens_per_step=2048), 8 prompts of U[32, 256] ids, 64 greedy tokens each;
+plus a 2-layer model with 2 slots and chunk 4 (slot reuse, prefix reloads).
+Pass: identical greedy tokens, the same number of engine steps and the same
+pool size as the reference run on the CPU (tests/golden/engine_golden.pt).
+The smallest top-1/top-2 logit gap of the reference run is recorded with the
+fixture (1.5e-4 for config 1); float32 GEMMs (no TF32) keep the GPU logits
+within about 1e-5 of it.
+"""
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("name", ["tiny", "gpt124m_cfg1"])
+def test_engine_greedy_tokens_match_reference(golden_engine, name):
+    from nifre_b200 import Engine, GptInferenceModel, GptModel
+    case = golden_engine[name]
+    torch.backends.cuda.matmul.allow_tf32 = False
+    torch.manual_seed(case["seed"])
+    model = GptModel(case["cfg"]).eval().to("cuda")
+    eng = Engine(GptInferenceModel(model), max_concurrent_requests=case["slots"], device="cuda",
+                 prefill_chunk_size=case["chunk"], max_tokens_per_step=2048)
+    new_tokens = len(case["tokens"][0])
+    ids = [eng.add_request(p, new_tokens) for p in case["prompts"]]
+    steps = 0
+    while eng.step():
+        steps += 1
+    done = eng.get_completed()
+    assert [done[i].output_token_ids for i in ids] == case["tokens"]
+    assert steps == case["steps"]
+    assert eng.cache.num_blocks == case["num_blocks"]
+    eng.cache.check_status()
+
+
+def test_engine_generate_and_stream_agree():
+    """generate() and generate_stream() give the same tokens for the same prompt."""
+    from nifre_b200 import Engine, GptInferenceModel, GptModel
+    cfg = dict(vocab_size=257, context_length=128, emb_dim=64, num_heads=4, num_layers=2, drop_rate=0.0,
+               qkv_bias=True)
+    torch.manual_seed(1)
+    model = GptModel(cfg).eval().to("cuda")
+    eng = Engine(GptInferenceModel(model), max_concurrent_requests=2, device="cuda", prefill_chunk_size=8)
+    prompt = list(range(3, 40))
+    a = eng.generate(prompt, 6).output_token_ids
+    b = list(eng.generate_stream(prompt, 6))
+    assert a == b and len(a) == 6
