@@ -39,27 +39,50 @@ import torch  # noqa: E402
 
 # DRAM bytes (read + write) of one nf_paged_attention launch over algorithmic
 # bytes, from an ncu capture (dram__bytes_read.sum + dram__bytes_write.sum) of
-# the 1-layer case of this workload: 317.28 MB for 307.57 MB of keys, values,
-# queries, outputs and block-table entries.  Traffic scales with the keys read.
+# the 1-layer case of the 1B workload: 317.28 MB for 307.57 MB of keys,
+# values, queries, outputs and block-table entries.  Traffic scales with the
+# keys read.
 ATTN_TRAFFIC_RATIO = 1.0316
 
-CFG = dict(name="llama3.2-1b-decode", layers=16, hq=32, hkv=8, d=64, bs=16, seqs=64, ctx_lo=512, ctx_hi=4096,
-           dtype="bf16", seed=0)
-METRIC = "paged-attn decode tok/s (1B shape, 16 layers)"
+# resident: layers held in HBM and run per step (a full 8B step's KV, ~618 GB,
+# exceeds one GPU); tok/s counts every step as `layers` layers at the measured
+# per-layer time.  scaling: weak = batch grows with N (64*N sequences), strong
+# = the same 256 sequences with the KV heads sharded over N GPUs.
+WORKLOADS = {
+    "llama3.2-1b-decode": dict(layers=16, resident=16, hq=32, hkv=8, d=64, bs=16, seqs=64, ctx_lo=512,
+                               ctx_hi=4096, seed=0, scaling="weak", steps=300, cpu_sample=8,
+                               metric="paged-attn decode tok/s (1B shape, 16 layers)",
+                               traffic_ratio=ATTN_TRAFFIC_RATIO,
+                               traffic_source="ncu capture of the 1-layer case, scaled by keys read"),
+    "llama3-8b-long": dict(layers=32, resident=4, hq=32, hkv=8, d=128, bs=16, seqs=256, ctx_lo=4096,
+                           ctx_hi=32768, seed=0, scaling="strong", steps=20, cpu_sample=2,
+                           metric="paged-attn decode tok/s (8B shape, 32 layers, 4 resident, per-layer timed)"),
+}
+CFG = dict(name="llama3.2-1b-decode", **WORKLOADS["llama3.2-1b-decode"])
+METRIC = CFG["metric"]
 
 
 def _args():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=300)
+    ap.add_argument("--steps", type=int, default=None)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--e2e-steps", type=int, default=50)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--layers", type=int, default=None, help="fewer layers (profiling a small case)")
+    ap.add_argument("--layers", type=int, default=None, help="fewer resident layers (profiling a small case)")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="llama3.2-1b-decode")
     a = ap.parse_args()
-    if a.layers:
-        CFG["layers"] = a.layers
+    global METRIC
+    CFG.clear()
+    CFG.update(name=a.workload, **WORKLOADS[a.workload])
+    METRIC = CFG["metric"]
+    if a.steps is None:
+        a.steps = CFG["steps"]
+    if a.layers:  # profiling a small case: fewer resident layers (and, for the 1B shape, a shallower model)
+        CFG["resident"] = a.layers
+        if a.workload == "llama3.2-1b-decode":
+            CFG["layers"] = a.layers
     return a
 
 
@@ -138,11 +161,12 @@ class CpuOracleDecode:
     every call sees the same contexts.
     """
 
-    def __init__(self, n_sample: int = 8, threads: int | None = None):
+    def __init__(self, n_sample: int | None = None, threads: int | None = None):
         from oracle.paged import OracleStore
 
         if threads:
             torch.set_num_threads(threads)
+        n_sample = n_sample or CFG["cpu_sample"]
         self.n = n_sample
         self.ctx = _ctx_lens(CFG["seqs"], CFG["seed"])[:n_sample]
         H, D, bs = CFG["hkv"], CFG["d"], CFG["bs"]
@@ -204,28 +228,40 @@ def run_ours(args):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     if CFG["hkv"] % world:
         raise SystemExit(f"--gpus {world} must divide {CFG['hkv']} KV heads")
-    L, D, bs = CFG["layers"], CFG["d"], CFG["bs"]
+    L, L_model, D, bs = CFG["resident"], CFG["layers"], CFG["d"], CFG["bs"]
     hkv, hq = CFG["hkv"] // world, CFG["hq"] // world
-    B = CFG["seqs"] * world
+    B = CFG["seqs"] * world if CFG["scaling"] == "weak" else CFG["seqs"]
     ctx = _ctx_lens(B, CFG["seed"])
     steps_total = args.warmup + args.steps + args.e2e_steps + 2
     max_seq = CFG["ctx_hi"] + steps_total + 16
     dt = torch.bfloat16
-    cache = PagedKVCache(L, max_seq, hkv, D, device=dev, dtype=dt, block_size=bs, enable_prefix_cache=False)
+    # the pool holds the contexts plus the steps' tokens (sum of ceil(ctx/bs) blocks), shuffled below
+    n_blocks = sum((c + steps_total + 16 + bs - 1) // bs for c in ctx)
+    cache = PagedKVCache(L, max_seq, hkv, D, device=dev, dtype=dt, block_size=bs, enable_prefix_cache=False,
+                         num_blocks=n_blocks)
     cache.init_batch(B)
     g = torch.Generator().manual_seed(CFG["seed"])
     cache.block_allocator.set_free_order(torch.randperm(cache.num_blocks, generator=g).tolist())
-    # fill the contexts (N(0,1) keys and values) through the append path, layer by layer
-    T0 = sum(ctx)
-    plan = cache.plan(list(range(B)), ctx, np.cumsum([0] + ctx[:-1]).tolist())
+    # fill the contexts (N(0,1) keys and values) through the append path, layer
+    # by layer, in groups of sequences of at most ~1M tokens
     gd = torch.Generator(device=dev).manual_seed(CFG["seed"] + rank)
-    kfill = torch.empty(T0, hkv * D, device=dev, dtype=dt)
-    vfill = torch.empty_like(kfill)
-    for layer in range(L):
-        kfill.normal_(generator=gd)
-        vfill.normal_(generator=gd)
-        cache.append_step(layer, kfill, vfill, plan)
-    del kfill, vfill
+    groups, cur = [], []
+    for s_ in range(B):
+        if cur and sum(ctx[i] for i in cur) + ctx[s_] > (1 << 20):
+            groups.append(cur)
+            cur = []
+        cur.append(s_)
+    groups.append(cur)
+    for grp in groups:
+        lens = [ctx[i] for i in grp]
+        plan = cache.plan(grp, lens, np.cumsum([0] + lens[:-1]).tolist())
+        kfill = torch.empty(sum(lens), hkv * D, device=dev, dtype=dt)
+        vfill = torch.empty_like(kfill)
+        for layer in range(L):
+            kfill.normal_(generator=gd)
+            vfill.normal_(generator=gd)
+            cache.append_step(layer, kfill, vfill, plan)
+        del kfill, vfill, plan
     q_all = torch.randn(L, B, hq * D, device=dev, dtype=dt, generator=gd)
     k_all = torch.randn(L, B, hkv * D, device=dev, dtype=dt, generator=gd)
     v_all = torch.randn(L, B, hkv * D, device=dev, dtype=dt, generator=gd)
@@ -332,7 +368,7 @@ def run_ours(args):
             ems = float(t.item())
         cache.check_status()
         n_e2e = args.e2e_steps - 1
-        e2e = {"value": B * n_e2e / (ems * 1e-3), "unit": "tok/s",
+        e2e = {"value": B * n_e2e / (ems * 1e-3) * L / L_model, "unit": "tok/s",
                "h2d_bytes_per_step": L * B * (hq + 2 * hkv) * D * 2,
                "d2h_bytes_per_step": L * B * hq * D * 2,
                "ms_per_step": ems / n_e2e, "path": "nifre_b200.Attention.forward per layer, pinned host q/k/v"}
@@ -343,19 +379,25 @@ def run_ours(args):
             cpu = cpu_decode_rate(12.0)
             cpu["kind"] = "port"
         line = {
-            "metric": METRIC, "value": B * args.steps / (ms * 1e-3), "unit": "tok/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "metric": METRIC, "value": B * args.steps / (ms * 1e-3) * L / L_model, "unit": "tok/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms / args.steps * L_model / L,
+            "higher_is_better": True, "scaling": CFG["scaling"], "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded N(0,1) Q/K/V, random block permutation)",
-            "config": {"workload": CFG["name"], "layers": L, "q_heads": CFG["hq"], "kv_heads": CFG["hkv"],
-                       "head_dim": D, "block_size": bs, "seqs_per_gpu_x_heads": f"{B} seqs x {hkv} kv heads",
+            "config": {"workload": CFG["name"], "layers": L_model, "layers_timed": L, "q_heads": CFG["hq"],
+                       "kv_heads": CFG["hkv"], "head_dim": D, "block_size": bs,
+                       "seqs_per_gpu_x_heads": f"{B} seqs x {hkv} kv heads",
                        "global_batch": B, "ctx": f"U[{CFG['ctx_lo']},{CFG['ctx_hi']}] + step",
                        "parallelism": f"kv-head shard x{world}" if world > 1 else "single GPU",
-                       "l2": "inputs larger than L2 (each layer reads a distinct ~300 MB pool)"},
+                       "method": ("all layers run every step" if L == L_model else
+                                  f"{L} resident layers run per step; tok/s and ms_per_step scaled to "
+                                  f"{L_model} layers at the measured per-layer time"),
+                       "l2": "inputs larger than L2 (each layer reads a distinct pool of >=300 MB)"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak,
-                         "traffic": ATTN_TRAFFIC_RATIO * sum(att_bytes) / len(att_bytes),
-                         "traffic_source": "ncu capture of the 1-layer case, scaled by keys read",
+                         "traffic": (CFG["traffic_ratio"] * sum(att_bytes) / len(att_bytes)
+                                     if CFG.get("traffic_ratio") else None),
+                         "traffic_source": CFG.get("traffic_source"),
                          "kernel": "nf_paged_attention",
                          "kernel_path": {0: "per-warp cp.async", 1: "tensor map, one copy per block",
                                          2: "tensor map, one copy per head"}.get(att_path, str(att_path)),

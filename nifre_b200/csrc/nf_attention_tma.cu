@@ -291,12 +291,14 @@ __device__ void tma_consumer(const AttnParams& p, unsigned char* base, int box_b
     if (!mbar_wait(hdr + 8 * s, ph, p.status)) return;
     const StepRec r = recs[s];
     if (r.u < 0) return;  // no more work
-    // take the unit's next step too when it has one: 32 keys per update
+    // head_dim 64: take the unit's next step too when it has one (32 keys
+    // per update); head_dim 128 has the instruction-level parallelism of
+    // 8 k-steps per tile and too few stages per CTA to hold two
     const int s0 = s;
     advance();
-    const bool pair = !r.last;
+    const bool pair = D_ == 64 && !r.last;
     int s1 = s0;
-    bool last = true;
+    bool last = r.last;
     if (pair) {
       if (!mbar_wait(hdr + 8 * s, ph, p.status)) return;
       s1 = s;
@@ -466,8 +468,14 @@ int launch_attention_tma(AttnParams p, int dtype, long long want, cudaStream_t s
   if (dtype != NF_BF16 && dtype != NF_F16) return NF_EUNSUPPORTED;
   if ((p.D != 64 && p.D != 128) || p.bs % 16 != 0 || !p.q_smem || p.G > 8) return NF_EUNSUPPORTED;
   if ((reinterpret_cast<uintptr_t>(p.kp) | reinterpret_cast<uintptr_t>(p.vp)) & 15) return NF_EUNSUPPORTED;
+  // head_dim 64: one CTA per SM with up to 8 KV heads and 6 stages of 36 KB;
+  // head_dim 128: two CTAs per SM with up to 4 KV heads and 3 stages of 36 KB
+  // each.  Either way about four stages (128 KB) per SM are in flight while
+  // the consumers hold the ones they compute on, and 8 consumer warps share
+  // the SM.
+  const int max_hg = p.D == 64 ? 8 : 4, ctas = p.D == 64 ? 1 : 2;
   int hg = 0;
-  for (int h = p.Hkv < 8 ? p.Hkv : 8; h >= 1; --h)
+  for (int h = p.Hkv < max_hg ? p.Hkv : max_hg; h >= 1; --h)
     if (p.Hkv % h == 0) {
       hg = h;
       break;
@@ -475,7 +483,10 @@ int launch_attention_tma(AttnParams p, int dtype, long long want, cudaStream_t s
   const int HB = p.D * 2;
   const int box = hg * 16 * HB, qb = hg * p.G * HB;
   const int stage = ((2 * box + qb + 1023) / 1024) * 1024;
-  int stages = (227 * 1024 - kTmaHeader - 1024) / stage;
+  // per CTA: 1 KB reserved by the system, the header, 1 KB of alignment slack
+  // and the static shared memory of finish_launch
+  const int budget = 228 * 1024 / ctas - 1024 - kTmaHeader - 1024 - 256;
+  int stages = budget / stage;
   if (stages > kTmaMaxStages) stages = kTmaMaxStages;
   if (stages < 2) return NF_EUNSUPPORTED;
   CUtensorMap tk, tv;
