@@ -229,7 +229,9 @@ def run_ours(args):
     if CFG["hkv"] % world:
         raise SystemExit(f"--gpus {world} must divide {CFG['hkv']} KV heads")
     L, L_model, D, bs = CFG["resident"], CFG["layers"], CFG["d"], CFG["bs"]
-    hkv, hq = CFG["hkv"] // world, CFG["hq"] // world
+    from nifre_b200.sharding import HeadShard
+    shard = HeadShard(world, rank, CFG["hq"], CFG["hkv"], CFG["d"])
+    hkv, hq = shard.kv_heads, shard.q_heads
     B = CFG["seqs"] * world if CFG["scaling"] == "weak" else CFG["seqs"]
     ctx = _ctx_lens(B, CFG["seed"])
     steps_total = args.warmup + args.steps + args.e2e_steps + 2
@@ -266,7 +268,7 @@ def run_ours(args):
     k_all = torch.randn(L, B, hkv * D, device=dev, dtype=dt, generator=gd)
     v_all = torch.randn(L, B, hkv * D, device=dev, dtype=dt, generator=gd)
     out_loc = torch.empty(L, B, hq * D, device=dev, dtype=dt)
-    gathered = torch.empty(world, B, hq * D, device=dev, dtype=dt) if world > 1 else None
+    gathered = torch.empty(world * B, hq * D, device=dev, dtype=dt) if world > 1 else None
     slots, ones, rows = list(range(B)), [1] * B, list(range(B))
     stream = torch.cuda.current_stream(dev)
     att_events = []
@@ -284,9 +286,8 @@ def run_ours(args):
                 e1.record(stream)
                 att_events.append((e0, e1, p))
             if world > 1:
-                dist.all_gather_into_tensor(gathered, out_loc[layer])
-                # heads of rank r are query heads [r*hq, (r+1)*hq): (N, B, hq*D) -> (B, N*hq*D)
-                gathered.permute(1, 0, 2).reshape(B, world * hq * D)
+                # heads of rank r are query heads [r*hq, (r+1)*hq): (N*B, hq*D) -> (B, N*hq*D)
+                shard.gather(out_loc[layer], buffer=gathered)
 
     for _ in range(args.warmup):
         step()
@@ -344,8 +345,7 @@ def run_ours(args):
                 vd = hv_host[layer].to(dev, non_blocking=True)
                 o = attn(qd, kd, vd, kv_cache=cache, layer_id=layer, cache_batch_indices=slots)
                 if world > 1:
-                    dist.all_gather_into_tensor(gathered, o.view(B, -1))
-                    o = gathered.permute(1, 0, 2).reshape(B, 1, world * hq * D)
+                    o = shard.gather(o.view(B, -1), buffer=gathered).view(B, 1, world * hq * D)
                     ho_host[layer].copy_(o[:, :, : hq * D], non_blocking=True)
                 else:
                     ho_host[layer].copy_(o, non_blocking=True)
