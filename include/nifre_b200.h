@@ -76,6 +76,16 @@ int nf_abi_version(void);
 int nf_last_attention_path(void);
 
 /*
+ * Diagnostic, no counterpart in the reference: one 128 x N x K bfloat16
+ * tensor-core (tcgen05) product from 128-byte-swizzled shared memory into
+ * tensor memory, the building block of the prefill kernel.  A: 128 x K,
+ * B: N x K (mode 0, C = A B^T) or K x N (mode 1, C = A B), row-major device
+ * arrays; C: 128 x N float32.  N, K in {64, 128}.
+ */
+int nf_selftest_umma(const void* A, const void* B, float* C, int32_t N, int32_t K, int32_t mode,
+                     int32_t* status, void* stream);
+
+/*
  * nf_pack_step: expand one step's ragged batch on the device.
  *
  * seqs[n_seqs][4]      (device) slot, q_start, q_len, ctx_before of each
