@@ -102,14 +102,16 @@ int nf_selftest_umma(const void* A, const void* B, float* C, int32_t N, int32_t 
  * and the split-K work list units[max_units][8] (16-byte aligned): key
  * ranges [key_begin, key_end) of an item, each record self-contained so a
  * kernel needs one read per unit.  The queries of sequence s use units of
- * seq_split[s] keys (device, n_seqs entries; NULL, or an entry that is not a
- * positive multiple of 16, means split_tokens).  An item's n_parts units are
+ * seq_split[s] keys (device, n_seqs entries; NULL, or an entry that is
+ * negative or not a multiple of 16, means split_tokens; 0 means no units:
+ * the sequence's queries are left to nf_prefill_attention).  An item's n_parts units are
  * its parts 0..n_parts-1 in key order, with split-K partial slots
  * unit_base + part; the list holds the units of sequences at split_tokens
  * first and those of sequences with a smaller unit size after them, each
  * class in item order, so that a dynamic queue over the list ends on short
  * units.  split_tokens must be a positive multiple of 16.
- * counts[0] = n_tokens, counts[1] = number of units.
+ * counts[3]: counts[0] = n_tokens, counts[1] = number of units, counts[2] = 1
+ * if some item has more than one part (the attention launch then merges).
  */
 int nf_pack_step(const int32_t* seqs, int32_t n_seqs,
                  const int32_t* patches, int32_t n_patches,
@@ -172,6 +174,24 @@ int nf_paged_attention(void* out, int64_t out_row_stride,
                        float* ws_partials, int64_t ws_partial_floats,
                        int32_t* ws_counters, int64_t ws_counter_ints,
                        int32_t* status, void* stream);
+
+/*
+ * nf_prefill_attention: causal attention of prefill chunks on the tensor
+ * cores (tcgen05, tensor memory), for 16-bit pools with head_dim 64 or 128,
+ * 1, 2, 4 or 8 query heads per KV head and block_size a multiple of 16.
+ * tiles[n_tiles][4] (device, 16-byte aligned): slot, q_row0, ntok, pos0 -- the
+ * ntok (<= 128 / group size) consecutive query tokens of one sequence whose
+ * rows in q/out start at q_row0 and whose absolute positions start at pos0;
+ * query pos0 + i attends over keys [0, pos0 + i] of the slot's block table
+ * (attention.py:144-152), all already appended.  Writes those rows of out.
+ */
+int nf_prefill_attention(void* out, int64_t out_row_stride, const void* q, int64_t q_row_stride,
+                         const void* k_pool, const void* v_pool, int32_t dtype,
+                         int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                         int32_t block_size, int32_t num_blocks,
+                         const int32_t* block_tables, int32_t max_blocks_per_seq,
+                         const int32_t* tiles, int32_t n_tiles, float scale,
+                         int32_t* status, void* stream);
 
 /*
  * nf_paged_attention_noalloc: nf_paged_attention without a caller workspace.

@@ -65,7 +65,7 @@ class Attention(nn.Module):
         plan = cache._plan
         if plan is None or plan.key != key or plan.closed:
             starts = [i * T + (T - n) for i, n in enumerate(lens)]
-            plan = cache.plan(slots, lens, starts)
+            plan = cache.plan(slots, lens, starts, q_heads=self.num_heads)
             plan.key = key
         q2 = q.reshape(B * T, q.shape[-1])
         k2 = k.reshape(B * T, k.shape[-1])
@@ -112,7 +112,7 @@ def causal_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, head_dim
     src_rows = torch.empty_like(slot_mapping)
     items = torch.empty(4 * n_tok, dtype=torch.int32, device=dev)
     units = torch.empty(_lib.UNIT_FIELDS * max_units, dtype=torch.int32, device=dev)
-    counts = torch.empty(2, dtype=torch.int32, device=dev)
+    counts = torch.empty(3, dtype=torch.int32, device=dev)
     status = torch.zeros(1, dtype=torch.int32, device=dev)
     stream = _lib.stream_handle(dev)
     lib = _lib.load()

@@ -711,7 +711,6 @@ extern "C" int nf_paged_attention(void* out, int64_t out_row_stride, const void*
   p.queue = ws_counters + (int64_t)max_items * num_kv_heads;
   p.items = items;
   p.max_items = max_items;
-  p.merge = max_units > max_items;  // else every item has exactly one part
   p.status = status;
   p.W = pl.W;
   p.stages = pl.stages;

@@ -30,6 +30,7 @@
 
 #include "nf_attn_common.cuh"
 #include "nf_internal.h"
+#include "nf_tma.cuh"
 
 namespace nf {
 
@@ -42,32 +43,6 @@ constexpr int kTmaMaxThreads = (8 + 1) * 32;
 struct StepRec {  // one 16-key step as the producer describes it to the consumers
   int u, item, q_row, t0, t1, unit_base, nsplits, hg, t, first, last, part, pad[4];
 };
-
-// Keys and values are read once per launch: their lines go first when L2
-// needs room, so the split-K parts and the queries stay cached.
-__device__ __forceinline__ uint64_t l2_evict_first() {
-  uint64_t pol;
-  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
-  return pol;
-}
-
-__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2, int c3,
-                                            uint32_t bar, uint64_t pol) {
-  asm volatile(
-      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, {%2, "
-      "%3, %4, %5}], [%6], %7;" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar), "l"(pol)
-      : "memory");
-}
-
-__device__ __forceinline__ void tma_load_5d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2, int c3,
-                                            int c4, uint32_t bar, uint64_t pol) {
-  asm volatile(
-      "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, {%2, "
-      "%3, %4, %5, %6}], [%7], %8;" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4), "r"(bar), "l"(pol)
-      : "memory");
-}
 
 // Byte offset of key row r, 16-byte chunk c, in one head's staged tile:
 // [d_hi][16 rows][128 B], chunks XOR-swizzled by the row (the TMA 128B mode).
@@ -413,10 +388,7 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// Tensor map over one pool (num_blocks, bs, Hkv, D).  permuted: dims
-// (d_lo, token, [d_hi,] head, block) with a box of 16 tokens x hg heads;
-// else increasing strides (d_lo, [d_hi,] head, token, block), box of one head.
-static bool encode_pool_map(CUtensorMap* map, const void* pool, int dtype, int D, int Hkv, int bs, int num_blocks,
+bool encode_pool_map(CUtensorMap* map, const void* pool, int dtype, int D, int Hkv, int bs, int num_blocks,
                             int hg, bool permuted) {
   auto fn = encode_fn();
   if (!fn) return false;

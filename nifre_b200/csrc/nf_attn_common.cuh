@@ -28,7 +28,6 @@ struct AttnParams {
   int* status;
   const int* items;  // per query: slot, q_row, kv_len, unit_base
   int max_items;
-  int merge;    // some item has more than one part
   // launch plan
   int W, stages, head_bytes, stage_bytes, swz, tile, bs16, q_smem;
   int HG, n_hg;  // tensor-map path: KV heads per CTA and head groups
@@ -126,12 +125,13 @@ template <typename T, int PB>
 __device__ void finish_launch(const AttnParams& p, int* cta_done, int total) {
   __shared__ int go;
   __syncthreads();  // the CTA's output and part stores are issued
+  const bool merge = __ldg(p.counts + 2) != 0;  // set by the pack when an item has several parts
   if (threadIdx.x == 0) {
     __threadfence();
     atomicAdd(p.queue + 2, *cta_done);
     int ok = 1;
     const long long t0 = clock64();
-    while (*reinterpret_cast<volatile int*>(p.queue + 2) < total) {
+    while (merge && *reinterpret_cast<volatile int*>(p.queue + 2) < total) {
       if (clock64() - t0 > kWaitLimitCycles) {
         atomicOr(p.status, NF_STATUS_WAIT_TIMEOUT);
         ok = 0;
@@ -143,7 +143,7 @@ __device__ void finish_launch(const AttnParams& p, int* cta_done, int total) {
     go = ok;
   }
   __syncthreads();
-  if (go && p.merge) {
+  if (go && merge) {
     // tasks: (item, KV head, group of 32 output chunks), dealt round-robin
     // over the CTAs so that every SM takes a share
     const int n_items = min(__ldg(p.counts), p.max_items);

@@ -91,12 +91,16 @@ __device__ __forceinline__ int seq_of(const int* cu, int n_seqs, int t) {
 }
 
 // Unit size of sequence s: its seq_split entry when that is a positive
-// multiple of 16, else the step's split.
+// multiple of 16, 0 when the entry is 0 (the sequence's queries are left to
+// another kernel: no units), else the step's split.
 __device__ __forceinline__ int unit_size(const PackParams& p, int s) {
   if (!p.seq_split) return p.split;
   const int v = p.seq_split[s];
+  if (v == 0) return 0;
   return (v > 0 && (v & 15) == 0) ? v : p.split;
 }
+
+__device__ __forceinline__ int parts_of(int kv_len, int us) { return us > 0 ? (kv_len + us - 1) / us : 0; }
 
 __global__ void __launch_bounds__(kPackThreads) pack_kernel(const PackParams p) {
   extern __shared__ int cu[];  // n_seqs + 1 query offsets
@@ -111,6 +115,8 @@ __global__ void __launch_bounds__(kPackThreads) pack_kernel(const PackParams p) 
     }
     p.bt[(long long)slot * p.max_blocks + lb] = phys;
   }
+  __shared__ int multi_sh;
+  if (tid == 0) multi_sh = 0;
   // 2. query offsets: scan of q_len.
   for (int s = tid; s < p.n_seqs; s += kPackThreads) cu[s] = p.seqs[4 * s + 2];
   __syncthreads();
@@ -145,7 +151,8 @@ __global__ void __launch_bounds__(kPackThreads) pack_kernel(const PackParams p) 
     it.y = q_start + i;
     it.z = kv_len;
     const int us = unit_size(p, s);
-    it.w = (kv_len + us - 1) / us;  // number of parts; scanned below
+    it.w = parts_of(kv_len, us);  // number of parts; scanned below
+    if (it.w > 1) multi_sh = 1;
     reinterpret_cast<int4*>(p.items)[t] = it;
   }
   __syncthreads();
@@ -166,7 +173,7 @@ __global__ void __launch_bounds__(kPackThreads) pack_kernel(const PackParams p) 
   int my_fine = 0;
   for (int t = tid; t < T; t += kPackThreads) {
     const int us = unit_size(p, seq_of(cu, p.n_seqs, t));
-    if (us < p.split) my_fine += (p.items[4 * t + 2] + us - 1) / us;
+    if (us < p.split) my_fine += parts_of(p.items[4 * t + 2], us);
   }
   if (my_fine) atomicAdd(&n_fine_sh, my_fine);
   __syncthreads();
@@ -179,7 +186,7 @@ __global__ void __launch_bounds__(kPackThreads) pack_kernel(const PackParams p) 
     if (t < T) {
       it = reinterpret_cast<const int4*>(p.items)[t];
       us = unit_size(p, seq_of(cu, p.n_seqs, t));
-      n = (it.z + us - 1) / us;
+      n = parts_of(it.z, us);
     }
     const bool fine = us < p.split;
     const int fb = cta_scan_round(fine ? n : 0, fine_carry);  // fine units of the items before t
@@ -199,6 +206,7 @@ __global__ void __launch_bounds__(kPackThreads) pack_kernel(const PackParams p) 
     if (n_units > p.max_units) atomicOr(p.status, NF_STATUS_UNIT_OVERFLOW);
     p.counts[0] = T;
     p.counts[1] = min(n_units, p.max_units);
+    p.counts[2] = multi_sh;  // some item has more than one part: the attention launch merges
   }
 }
 

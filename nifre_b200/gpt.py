@@ -176,7 +176,7 @@ class GptModel(nn.Module):
         pos0 = kv_cache.pos_host[slots]
         positions = torch.from_numpy(np.concatenate([np.arange(p, p + n) for p, n in zip(pos0, lens)]))
         rows = torch.arange(sum(lens), device=in_idx.device)
-        plan = kv_cache.plan(slots, lens, starts)
+        plan = kv_cache.plan(slots, lens, starts, q_heads=self.cfg["num_heads"])
         logits = self.forward_step(ids, positions.to(in_idx.device), kv_cache, plan, rows)
         out = torch.zeros(B, T, logits.shape[-1], device=logits.device, dtype=logits.dtype)
         for i, (s, n) in enumerate(zip(starts, lens)):

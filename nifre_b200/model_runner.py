@@ -80,7 +80,7 @@ class ModelRunner:
         starts = np.concatenate([[0], np.cumsum(lens)[:-1]]).astype(np.int64)
         pos0 = cache.pos_host[slots]
         positions = np.repeat(pos0 - starts, lens) + np.arange(len(ids))
-        plan = cache.plan(slots, lens, starts.tolist())
+        plan = cache.plan(slots, lens, starts.tolist(), q_heads=getattr(self.model.config, "n_heads", None))
         dev = self.device
         host = torch.from_numpy(np.concatenate([np.asarray(ids, np.int64), positions.astype(np.int64),
                                                 np.asarray(sample, np.int64)])).pin_memory()

@@ -101,6 +101,11 @@ class StepPlan:
         # device views, filled by PagedKVCache.plan
         self.seqs = self.slot_mapping = self.src_rows = self.items = self.units = self.counts = None
         self.positions = None
+        # split-K units of the step, and the tensor-core prefill tiles (tiles, n_tiles, q_heads)
+        self.decode_units = max_units
+        self.tiles = None
+        self.n_tiles = 0
+        self.q_heads = None
 
     @property
     def kv_lens(self) -> np.ndarray:
@@ -239,7 +244,18 @@ class PagedKVCache:
         s = total_keys / max(1, units_per_sm * self.sm_count)
         return max(128, int(math.ceil(s / 128.0)) * 128)
 
-    def plan(self, slots, q_lens, q_starts, split: int | None = None, fine_tail: bool = True) -> StepPlan:
+    # sequences with at least this many new tokens go to the tensor-core prefill kernel
+    PREFILL_MIN_TOKENS = 16
+
+    def prefill_supported(self, q_heads: int | None) -> bool:
+        """True when nf_prefill_attention serves this cache with q_heads query heads."""
+        if q_heads is None or q_heads % self.n_heads:
+            return False
+        return (self.dtype in (torch.bfloat16, torch.float16) and self.head_dim in (64, 128)
+                and q_heads // self.n_heads in (1, 2, 4, 8) and self.block_size % 16 == 0)
+
+    def plan(self, slots, q_lens, q_starts, split: int | None = None, fine_tail: bool = True,
+             q_heads: int | None = None) -> StepPlan:
         """Allocate blocks for a step and pack its metadata on the GPU.
 
         ``slots[i]`` gets ``q_lens[i]`` new tokens whose rows in the caller's
@@ -248,7 +264,11 @@ class PagedKVCache:
         Raises before any launch on an over-long sequence or an exhausted pool.
         ``split`` (a multiple of 16) overrides the unit size chosen for the
         step; ``fine_tail`` gives the shortest sequences smaller units
-        (``seq_unit_sizes``).
+        (``seq_unit_sizes``).  With ``q_heads`` (the query head count of the
+        attention calls) and a supported shape, sequences with at least
+        ``PREFILL_MIN_TOKENS`` new tokens are attended by the tensor-core
+        prefill kernel, in tiles of 128 query rows; the rest by the split-K
+        kernel.
         """
         slots = np.asarray(slots, dtype=np.int64)
         q_lens = np.asarray(q_lens, dtype=np.int64)
@@ -288,22 +308,38 @@ class PagedKVCache:
         T = int(q_lens.sum())
         # every query token is one work item attending over keys [0, ctx + i]
         kv = np.repeat(ctx + 1, q_lens) + (np.arange(T) - np.repeat(np.cumsum(q_lens) - q_lens, q_lens))
+        routed = (q_lens >= self.PREFILL_MIN_TOKENS) if self.prefill_supported(q_heads) else np.zeros(S, bool)
+        dec = ~routed
+        kv_dec = kv[np.repeat(dec, q_lens)]
         if split is None:
-            split = self.split_for(int(kv.sum()))
+            split = self.split_for(max(1, int(kv_dec.sum())))
         if split <= 0 or split % 16:
             raise ValueError(f"split ({split}) must be a positive multiple of 16")
         seq_keys = q_lens * (ctx + 1) + q_lens * (q_lens - 1) // 2
-        seq_split = (seq_unit_sizes(seq_keys, split, self.sm_count) if fine_tail
-                     else np.full(S, split, dtype=np.int32))
+        seq_split = np.zeros(S, dtype=np.int32)  # 0: the prefill kernel serves the sequence
+        if dec.any():
+            seq_split[dec] = (seq_unit_sizes(seq_keys[dec], split, self.sm_count) if fine_tail else split)
         item_split = np.repeat(seq_split.astype(np.int64), q_lens)
-        max_units = int(((kv + item_split - 1) // item_split).sum())
+        n_units = int(((kv_dec + item_split[item_split > 0] - 1) // item_split[item_split > 0]).sum())
+        max_units = max(1, n_units)
+        tiles = []
+        if routed.any():
+            tt = 128 // (q_heads // self.n_heads)  # query tokens per 128-row tile
+            for i in np.flatnonzero(routed).tolist():
+                n, c, r0 = int(q_lens[i]), int(ctx[i]), int(q_starts[i])
+                for t0 in reversed(range(0, n, tt)):  # most keys first
+                    tiles.append((int(slots[i]), r0 + t0, min(tt, n - t0), c + t0))
 
-        host = np.empty(S * 5 + P * 3, dtype=np.int32)
+        n_tiles = len(tiles)
+        off_tiles = _align4(S * 5 + P * 3)
+        host = np.zeros(off_tiles + 4 * n_tiles, dtype=np.int32)
         host[: S * 4] = np.stack([slots, q_starts, q_lens, ctx], axis=1).reshape(-1)
         if P:
             host[S * 4: S * 4 + P * 3] = np.asarray(patches, dtype=np.int32).reshape(-1)
-        host[S * 4 + P * 3:] = seq_split
-        off_slot = _align4(S * 5 + P * 3)
+        host[S * 4 + P * 3: S * 5 + P * 3] = seq_split
+        if n_tiles:
+            host[off_tiles:] = np.asarray(tiles, dtype=np.int32).reshape(-1)
+        off_slot = off_tiles + 4 * n_tiles
         off_src = off_slot + T
         off_items = _align4(off_src + T)
         off_units = off_items + 4 * T
@@ -313,12 +349,16 @@ class PagedKVCache:
         pos_dev = self._pos_buf.get(T)
 
         plan = StepPlan(slots, q_lens, q_starts, ctx, split, max_units, seq_split)
+        plan.decode_units = n_units
+        plan.q_heads = q_heads
+        plan.n_tiles = n_tiles
+        plan.tiles = meta[off_tiles: off_tiles + 4 * n_tiles]
         plan.seqs = meta[: S * 4]
         plan.slot_mapping = meta[off_slot: off_slot + T]
         plan.src_rows = meta[off_src: off_src + T]
         plan.items = meta[off_items: off_items + 4 * T]
         plan.units = meta[off_units: off_units + _lib.UNIT_FIELDS * max_units]
-        plan.counts = meta[off_counts: off_counts + 2]
+        plan.counts = meta[off_counts: off_counts + 3]
         plan.positions = pos_dev[:T]
         lib = _lib.load()
         _lib.check(lib.nf_pack_step(
@@ -382,21 +422,31 @@ class PagedKVCache:
         if not 0 <= layer_id < self.num_layers:
             raise IndexError(f"layer_id {layer_id} out of range [0, {self.num_layers})")
         hq = q.shape[1] // D
-        max_items = plan.n_tokens
-        pf, ci = _lib.workspace_sizes(plan.max_units, max_items, hq, self.n_heads, D, self.dtype)
-        ws = self._ws_partials.get(pf)
-        cnt = self._ws_counters.get(ci)
+        if plan.n_tiles and hq != plan.q_heads:
+            raise ValueError(f"the plan's prefill tiles are for {plan.q_heads} query heads, q has {hq}")
         if scale is None:
             scale = 1.0 / math.sqrt(D)
         lib = _lib.load()
-        _lib.check(lib.nf_paged_attention(
-            out.data_ptr(), out.stride(0), q.data_ptr(), q.stride(0),
-            self.k[layer_id].data_ptr(), self.v[layer_id].data_ptr(), _lib.dtype_code(self.dtype),
-            hq, self.n_heads, D, self.block_size, self.num_blocks, self.bt_dev.data_ptr(),
-            self.max_blocks_per_seq, plan.items.data_ptr(), plan.units.data_ptr(), plan.counts.data_ptr(),
-            max_items, plan.max_units, plan.split, float(scale), ws.data_ptr(), ws.numel(),
-            cnt.data_ptr(), cnt.numel(), self.status.data_ptr(), _lib.stream_handle(self.device)),
-            "nf_paged_attention")
+        stream = _lib.stream_handle(self.device)
+        if plan.n_tiles:
+            _lib.check(lib.nf_prefill_attention(
+                out.data_ptr(), out.stride(0), q.data_ptr(), q.stride(0),
+                self.k[layer_id].data_ptr(), self.v[layer_id].data_ptr(), _lib.dtype_code(self.dtype),
+                hq, self.n_heads, D, self.block_size, self.num_blocks, self.bt_dev.data_ptr(),
+                self.max_blocks_per_seq, plan.tiles.data_ptr(), plan.n_tiles, float(scale),
+                self.status.data_ptr(), stream), "nf_prefill_attention")
+        if plan.decode_units:
+            max_items = plan.n_tokens
+            pf, ci = _lib.workspace_sizes(plan.max_units, max_items, hq, self.n_heads, D, self.dtype)
+            ws = self._ws_partials.get(pf)
+            cnt = self._ws_counters.get(ci)
+            _lib.check(lib.nf_paged_attention(
+                out.data_ptr(), out.stride(0), q.data_ptr(), q.stride(0),
+                self.k[layer_id].data_ptr(), self.v[layer_id].data_ptr(), _lib.dtype_code(self.dtype),
+                hq, self.n_heads, D, self.block_size, self.num_blocks, self.bt_dev.data_ptr(),
+                self.max_blocks_per_seq, plan.items.data_ptr(), plan.units.data_ptr(), plan.counts.data_ptr(),
+                max_items, plan.max_units, plan.split, float(scale), ws.data_ptr(), ws.numel(),
+                cnt.data_ptr(), cnt.numel(), self.status.data_ptr(), stream), "nf_paged_attention")
         return out
 
     # ------------------------------------------------------------------ diagnostics

@@ -100,12 +100,13 @@ def test_golden_smoke_sequence(golden_paged):
     cache.check_status()
 
 
-def _random_cache(Hq, Hkv, D, bs, ctx_lens, dtype, seed, L=1, shuffle=True):
-    """Fill a cache with N(0,1) keys for the given contexts through the prefill path."""
+def _random_cache(Hq, Hkv, D, bs, ctx_lens, dtype, seed, L=1, shuffle=True, room=8):
+    """Fill a cache with N(0,1) keys for the given contexts through the prefill path
+    (``room`` more tokens fit after the longest context)."""
     from nifre_b200 import PagedKVCache
     g = torch.Generator().manual_seed(seed)
     B = len(ctx_lens)
-    max_len = max(ctx_lens) + 8
+    max_len = max(ctx_lens) + room
     cache = PagedKVCache(L, max_len, Hkv, D, device=DEV, dtype=dtype, block_size=bs, enable_prefix_cache=False)
     cache.init_batch(B)
     if shuffle:
@@ -273,3 +274,32 @@ def test_errors_before_launch():
     with pytest.raises(ValueError, match="layer_id is required"):
         Attention(2, 64)(torch.zeros(1, 1, 128, device=DEV), torch.zeros(1, 1, 128, device=DEV),
                          torch.zeros(1, 1, 128, device=DEV), kv_cache=cache)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("D,Hq,Hkv", [(64, 32, 8), (128, 32, 8), (64, 8, 8), (64, 16, 2), (128, 16, 16)])
+def test_prefill_kernel_vs_oracle(dtype, D, Hq, Hkv):
+    """Tensor-core prefill tiles (q_len >= 16) mixed with decodes and short chunks in one step."""
+    past = [0, 5, 16, 300, 1000, 2048, 40, 7, 600]
+    qlens = [16, 37, 64, 130, 512, 100, 1, 8, 1]
+    if dtype == torch.float16 and D == 128:
+        past, qlens = past[:5], qlens[:5]
+    cache, g = _random_cache(Hq, Hkv, D, 16, [max(p, 1) for p in past], dtype, seed=D + Hq + Hkv, room=600)
+    cache.reset_slot(0)
+    T = sum(qlens)
+    q = torch.randn(T, Hq * D, generator=g).to(dtype).to(DEV)
+    k = torch.randn(T, Hkv * D, generator=g).to(dtype).to(DEV)
+    v = torch.randn(T, Hkv * D, generator=g).to(dtype).to(DEV)
+    starts = [sum(qlens[:i]) for i in range(len(qlens))]
+    before = [cache.length(s) for s in range(len(qlens))]
+    plan = cache.plan(list(range(len(qlens))), qlens, starts, q_heads=Hq)
+    assert plan.n_tiles > 0
+    cache.append_step(0, k, v, plan)
+    out = torch.full_like(q, float("nan"))
+    cache.attention_step(0, q, plan, out)
+    kp, vp = cache.k[0].cpu(), cache.v[0].cpu()
+    for s, (st, n) in enumerate(zip(starts, qlens)):
+        ref = attend_paged_fp32(q[st:st + n].view(n, Hq, D).cpu(), kp, vp, cache.block_tables[s].physical_blocks(),
+                                before[s] + n, Hq // Hkv, causal_base=before[s])
+        torch.testing.assert_close(out[st:st + n].view(n, Hq, D).float().cpu(), ref, **_tol(dtype))
+    cache.check_status()
