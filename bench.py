@@ -57,6 +57,13 @@ WORKLOADS = {
     "llama3-8b-long": dict(layers=32, resident=4, hq=32, hkv=8, d=128, bs=16, seqs=256, ctx_lo=4096,
                            ctx_hi=32768, seed=0, scaling="strong", steps=20, cpu_sample=2,
                            metric="paged-attn decode tok/s (8B shape, 32 layers, 4 resident, per-layer timed)"),
+    # one continuous-batching step of the 1B shape: 4 prefill chunks of 512 tokens continuing cached
+    # prefixes U[0, 2048] (rewound every step, so every timed step is this one) + 96 decodes U[256, 2048]
+    "llama3.2-1b-mixed": dict(kind="mixed", layers=16, resident=16, hq=32, hkv=8, d=64, bs=16, seed=0,
+                              scaling="strong", steps=30, chunks=4, chunk=512, prefix_hi=2048, decodes=96,
+                              dctx_lo=256, dctx_hi=2048, seqs=100, ctx_lo=256, ctx_hi=2048, cpu_sample=8,
+                              metric="mixed prefill+decode step tok/s (1B shape, 16 layers, 4x512 chunks + 96 "
+                                     "decodes)"),
 }
 CFG = dict(name="llama3.2-1b-decode", **WORKLOADS["llama3.2-1b-decode"])
 METRIC = CFG["metric"]
@@ -149,6 +156,17 @@ def _peaks():
         d = json.loads(p.read_text())
         return float(d["hbm_gbs"]), "measured"
     return 6650.0, "fallback"
+
+
+def _tensor_peak():
+    """Dense bf16 peak for a kernel timed inside a long step: the sustained figure."""
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        if "bf16_tflops_sustained" in d:
+            return float(d["bf16_tflops_sustained"]), "measured (sustained)"
+        return float(d["bf16_tflops"]), "measured (burst)"
+    return 1400.0, "fallback (sustained)"
 
 
 # ---------------------------------------------------------------------------- CPU baseline (oracle)
@@ -419,13 +437,21 @@ def run_reference(args):
     if rank != 0:
         return
     threads = os.cpu_count() or 1
-    cpu = CpuOracleDecode(threads=threads)
-    for _ in range(args.warmup):
-        cpu.layer()
-    times = [cpu.layer() for _ in range(args.steps)]
-    v = cpu.rate(sum(times) / len(times))
+    if CFG.get("kind") == "mixed":
+        cpu = CpuOracleMixed(threads=threads)
+        for _ in range(args.warmup):
+            cpu.layer()
+        pairs = [cpu.layer() for _ in range(args.steps)]
+        v = cpu.rate(sum(a for a, _ in pairs) / len(pairs), sum(b for _, b in pairs) / len(pairs))
+        times = [a + b for a, b in pairs]
+    else:
+        cpu = CpuOracleDecode(threads=threads)
+        for _ in range(args.warmup):
+            cpu.layer()
+        times = [cpu.layer() for _ in range(args.steps)]
+        v = cpu.rate(sum(times) / len(times))
     line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": CFG["scaling"],
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": CFG["name"], "layers": CFG["layers"], "q_heads": CFG["hq"],
                        "kv_heads": CFG["hkv"], "head_dim": CFG["d"], "block_size": CFG["bs"]},
@@ -435,10 +461,270 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+# ---------------------------------------------------------------------------- mixed step (prefill + decode)
+def _mixed_shape():
+    rng = np.random.default_rng(CFG["seed"])
+    prefix = rng.integers(0, CFG["prefix_hi"] + 1, size=CFG["chunks"]).tolist()
+    dctx = rng.integers(CFG["dctx_lo"], CFG["dctx_hi"] + 1, size=CFG["decodes"]).tolist()
+    return prefix, dctx
+
+
+def _mixed_flops(prefix, hq, d, chunk):
+    """Algorithmic prefill FLOPs of one layer: unmasked causal pairs only, 4*Hq*D per pair."""
+    return 4.0 * hq * d * sum(chunk * p + chunk * (chunk + 1) / 2 for p in prefix)
+
+
+class CpuOracleMixed:
+    """The reference algorithm on the host for the mixed step: one 512-token chunk and 8 decodes per call."""
+
+    def __init__(self, threads: int | None = None):
+        from oracle.paged import OracleStore
+
+        if threads:
+            torch.set_num_threads(threads)
+        prefix, dctx = _mixed_shape()
+        self.prefix, self.dctx = prefix, dctx
+        H, D, bs, C = CFG["hkv"], CFG["d"], CFG["bs"], CFG["chunk"]
+        self.nd = min(CFG["cpu_sample"], len(dctx))
+        ctx = [prefix[0]] + dctx[: self.nd]
+        st = OracleStore(2, max(ctx) + C + 64, H, D, batch_size=len(ctx), dtype=torch.bfloat16, block_size=bs,
+                         prefix=False)
+        g = torch.Generator().manual_seed(1)
+        for sl, c in enumerate(ctx):
+            if c == 0:
+                continue
+            st.tables[sl].ensure(c)
+            kk = torch.randn(c, H, D, generator=g).to(torch.bfloat16)
+            vv = torch.randn(c, H, D, generator=g).to(torch.bfloat16)
+            for i, b in enumerate(st.tables[sl].blocks):
+                n = min(bs, c - i * bs)
+                st.k[0][b, :n] = kk[i * bs: i * bs + n]
+                st.v[0][b, :n] = vv[i * bs: i * bs + n]
+            st.pos[sl] = c
+        self.store = st
+        hq = CFG["hq"]
+        self.qc = torch.randn(1, C, hq * D, generator=g).to(torch.bfloat16)
+        self.kc = torch.randn(1, C, H * D, generator=g).to(torch.bfloat16)
+        self.qd = torch.randn(self.nd, 1, hq * D, generator=g).to(torch.bfloat16)
+        self.kd = torch.randn(self.nd, 1, H * D, generator=g).to(torch.bfloat16)
+
+    def layer(self) -> tuple[float, float]:
+        from oracle.attention import forward_with_cache
+
+        t0 = time.perf_counter()
+        forward_with_cache(self.store, 0, self.qc, self.kc, self.kc, CFG["hq"], slots=[0])
+        t1 = time.perf_counter()
+        forward_with_cache(self.store, 0, self.qd, self.kd, self.kd, CFG["hq"], slots=list(range(1, self.nd + 1)))
+        return t1 - t0, time.perf_counter() - t1
+
+    def rate(self, t_chunk: float, t_dec: float) -> float:
+        t_layer = len(self.prefix) * t_chunk + len(self.dctx) / self.nd * t_dec
+        tokens = len(self.prefix) * CFG["chunk"] + len(self.dctx)
+        return tokens / (CFG["layers"] * t_layer)
+
+    def describe(self, calls: int, seconds: float) -> str:
+        return (f"one 512-token chunk (prefix {self.prefix[0]}) and {self.nd} of {len(self.dctx)} decodes, one "
+                f"layer x {calls} calls in {seconds:.1f} s, scaled to 4 chunks + 96 decodes x {CFG['layers']} layers")
+
+
+def cpu_mixed_rate(seconds: float, threads: int | None = None):
+    cpu = CpuOracleMixed(threads=threads)
+    tc, td = [], []
+    while sum(tc) + sum(td) < seconds:
+        a, b = cpu.layer()
+        tc.append(a)
+        td.append(b)
+    return {"value": cpu.rate(sum(tc) / len(tc), sum(td) / len(td)), "unit": "tok/s",
+            "cores": torch.get_num_threads(), "sample": cpu.describe(len(tc), sum(tc) + sum(td))}
+
+
+def run_mixed(args):
+    from nifre_b200 import PagedKVCache
+    from nifre_b200.sharding import HeadShard
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    shard = HeadShard(world, rank, CFG["hq"], CFG["hkv"], CFG["d"])
+    hkv, hq = shard.kv_heads, shard.q_heads
+    L, D, bs, C = CFG["layers"], CFG["d"], CFG["bs"], CFG["chunk"]
+    prefix, dctx = _mixed_shape()
+    P, ND = len(prefix), len(dctx)
+    B = P + ND
+    steps_total = args.warmup + args.steps + args.e2e_steps + 2
+    max_seq = max(max(prefix) + C, max(dctx) + steps_total) + 16
+    n_blocks = sum((p + C + bs - 1) // bs for p in prefix) + sum((c + steps_total + 16 + bs - 1) // bs for c in dctx)
+    dt = torch.bfloat16
+    cache = PagedKVCache(L, max_seq, hkv, D, device=dev, dtype=dt, block_size=bs, enable_prefix_cache=False,
+                         num_blocks=n_blocks)
+    cache.init_batch(B)
+    g = torch.Generator().manual_seed(CFG["seed"])
+    cache.block_allocator.set_free_order(torch.randperm(cache.num_blocks, generator=g).tolist())
+    gd = torch.Generator(device=dev).manual_seed(CFG["seed"] + rank)
+    ctx = prefix + dctx
+    fill = [i for i in range(B) if ctx[i] > 0]
+    lens = [ctx[i] for i in fill]
+    plan = cache.plan(fill, lens, np.cumsum([0] + lens[:-1]).tolist())
+    kfill = torch.empty(sum(lens), hkv * D, device=dev, dtype=dt)
+    vfill = torch.empty_like(kfill)
+    for layer in range(L):
+        kfill.normal_(generator=gd)
+        vfill.normal_(generator=gd)
+        cache.append_step(layer, kfill, vfill, plan)
+    del kfill, vfill, plan
+    q_lens = [C] * P + [1] * ND
+    starts = np.cumsum([0] + q_lens[:-1]).tolist()
+    T = sum(q_lens)
+    q_all = torch.randn(L, T, hq * D, device=dev, dtype=dt, generator=gd)
+    k_all = torch.randn(L, T, hkv * D, device=dev, dtype=dt, generator=gd)
+    v_all = torch.randn(L, T, hkv * D, device=dev, dtype=dt, generator=gd)
+    out_loc = torch.empty(L, T, hq * D, device=dev, dtype=dt)
+    gathered = torch.empty(world * T, hq * D, device=dev, dtype=dt) if world > 1 else None
+    slots = list(range(B))
+    stream = torch.cuda.current_stream(dev)
+    kev = []
+
+    def rewind():  # every step continues the same prefixes (the decodes keep growing)
+        for i in range(P):
+            cache._set_pos(i, prefix[i])
+
+    def step(record=False, host=None):
+        rewind()
+        p = cache.plan(slots, q_lens, starts, q_heads=hq)
+        for layer in range(L):
+            if host is not None:
+                qd = host[0][layer].to(dev, non_blocking=True)
+                kd = host[1][layer].to(dev, non_blocking=True)
+                vd = host[2][layer].to(dev, non_blocking=True)
+            else:
+                qd, kd, vd = q_all[layer], k_all[layer], v_all[layer]
+            cache.append_step(layer, kd, vd, p)
+            ev = None
+            if record:
+                ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+                kev.append((ev, p))
+            cache.attention_step(layer, qd, p, out_loc[layer], events=ev)
+            o = out_loc[layer]
+            if world > 1:
+                o = shard.gather(o, buffer=gathered)
+            if host is not None:
+                host[3][layer].copy_(o[:, : hq * D] if world > 1 else o, non_blocking=True)
+        return p
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    cache.check_status()
+    if world > 1:
+        dist.barrier()
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.25)
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        p_last = step(record=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    cache.check_status()
+    pre_ms = [a[0].elapsed_time(a[1]) for a, _ in kev]
+    dec_ms = [a[1].elapsed_time(a[2]) for a, _ in kev]
+    pre_avg, dec_avg = sum(pre_ms) / len(pre_ms), sum(dec_ms) / len(dec_ms)
+    flops = _mixed_flops(prefix, hq, D, C)  # this rank's heads
+    dec_bytes = []
+    for _, p in kev:
+        kv = p.kv_lens[P:]
+        dec_bytes.append(int(kv.sum()) * hkv * D * 4 + 2 * ND * hq * D * 2 + 4 * int(((kv + bs - 1) // bs).sum()))
+    hbm_peak, hbm_kind = _peaks()
+    tf_peak, tf_kind = _tensor_peak()
+    # e2e: the same steps through the cache API with q/k/v copied from pinned host memory and the
+    # attention output copied back every layer
+    e2e = None
+    if args.e2e_steps > 1:
+        host = (q_all.cpu().pin_memory(), k_all.cpu().pin_memory(), v_all.cpu().pin_memory(),
+                torch.empty(L, T, hq * D * world, dtype=dt).pin_memory())
+        step(host=host)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(args.e2e_steps - 1):
+            step(host=host)
+        b.record(stream)
+        torch.cuda.synchronize()
+        ems = a.elapsed_time(b)
+        if world > 1:
+            t = torch.tensor([ems], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ems = float(t.item())
+        n = args.e2e_steps - 1
+        e2e = {"value": T * n / (ems * 1e-3), "unit": "tok/s",
+               "h2d_bytes_per_step": L * T * (hq + 2 * hkv) * D * 2, "d2h_bytes_per_step": L * T * hq * world * D * 2,
+               "ms_per_step": ems / n, "path": "PagedKVCache.plan/append_step/attention_step, pinned host q/k/v"}
+        cache.check_status()
+    if rank == 0:
+        cpu = None
+        if not args.no_cpu_baseline:
+            cpu = cpu_mixed_rate(12.0)
+            cpu["kind"] = "port"
+        pre_tf = flops * world / (pre_avg * 1e-3) / 1e12
+        dec_gbs = (sum(dec_bytes) / len(dec_bytes)) / (dec_avg * 1e-3) / 1e9
+        line = {
+            "metric": METRIC, "value": T * args.steps / (ms * 1e-3), "unit": "tok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+            "higher_is_better": True, "scaling": CFG["scaling"], "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1) Q/K/V, random block permutation)",
+            "config": {"workload": CFG["name"], "layers": L, "q_heads": CFG["hq"], "kv_heads": CFG["hkv"],
+                       "head_dim": D, "block_size": bs, "prefill_chunks": P, "chunk_tokens": C,
+                       "prefixes": prefix, "decodes": ND, "decode_ctx": f"U[{CFG['dctx_lo']},{CFG['dctx_hi']}]",
+                       "tokens_per_step": T, "global_batch": B,
+                       "parallelism": f"kv-head shard x{world}" if world > 1 else "single GPU",
+                       "method": "prefill slots rewound to their prefixes every step; decodes grow by one",
+                       "l2": "inputs larger than L2 (each layer reads a distinct pool of ~250 MB)"},
+            "roofline": {"bound": "tensor", "achieved": pre_tf, "peak": tf_peak, "unit": "TFLOP/s",
+                         "frac": pre_tf / tf_peak, "traffic": None, "kernel": "nf_prefill_attention",
+                         "peak_source": tf_kind, "avg_launch_us": pre_avg * 1e3,
+                         "flops_per_launch": flops * world,
+                         "flops_counted": "4*Hq*D per unmasked (query, key) pair"},
+            "roofline_decode": {"bound": "hbm", "achieved": dec_gbs, "peak": hbm_peak, "unit": "GB/s",
+                                "frac": dec_gbs / hbm_peak, "kernel": "nf_paged_attention",
+                                "peak_source": hbm_kind, "avg_launch_us": dec_avg * 1e3},
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "gpu_launches": args.steps * (1 + 3 * L),
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     args = _args()
+    mixed = CFG.get("kind") == "mixed"
     if args.impl == "reference":
         run_reference(args)
+    elif mixed:
+        run_mixed(args)
     else:
         run_ours(args)
 

@@ -403,11 +403,13 @@ class PagedKVCache:
             self._close(plan)
 
     def attention_step(self, layer_id: int, q: torch.Tensor, plan: StepPlan, out: torch.Tensor,
-                       scale: float | None = None) -> torch.Tensor:
+                       scale: float | None = None, events=None) -> torch.Tensor:
         """out[row] = attention of q[row] over the cached keys of its sequence, for the step's rows.
 
         ``q``/``out``: (rows, Hq*D) in the pool dtype with unit column stride.
-        Rows not in the step are left untouched.
+        Rows not in the step are left untouched.  ``events``: optional three
+        CUDA events recorded before the prefill launch, between the prefill and
+        the split-K launches, and after them (kernel timing).
         """
         _lib.require_cuda(q, "q")
         D = self.head_dim
@@ -428,6 +430,8 @@ class PagedKVCache:
             scale = 1.0 / math.sqrt(D)
         lib = _lib.load()
         stream = _lib.stream_handle(self.device)
+        if events is not None:
+            events[0].record()
         if plan.n_tiles:
             _lib.check(lib.nf_prefill_attention(
                 out.data_ptr(), out.stride(0), q.data_ptr(), q.stride(0),
@@ -435,6 +439,8 @@ class PagedKVCache:
                 hq, self.n_heads, D, self.block_size, self.num_blocks, self.bt_dev.data_ptr(),
                 self.max_blocks_per_seq, plan.tiles.data_ptr(), plan.n_tiles, float(scale),
                 self.status.data_ptr(), stream), "nf_prefill_attention")
+        if events is not None:
+            events[1].record()
         if plan.decode_units:
             max_items = plan.n_tokens
             pf, ci = _lib.workspace_sizes(plan.max_units, max_items, hq, self.n_heads, D, self.dtype)
@@ -447,6 +453,8 @@ class PagedKVCache:
                 self.max_blocks_per_seq, plan.items.data_ptr(), plan.units.data_ptr(), plan.counts.data_ptr(),
                 max_items, plan.max_units, plan.split, float(scale), ws.data_ptr(), ws.numel(),
                 cnt.data_ptr(), cnt.numel(), self.status.data_ptr(), stream), "nf_paged_attention")
+        if events is not None:
+            events[2].record()
         return out
 
     # ------------------------------------------------------------------ diagnostics
