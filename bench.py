@@ -88,7 +88,7 @@ def _args():
         a.steps = CFG["steps"]
     if a.layers:  # profiling a small case: fewer resident layers (and, for the 1B shape, a shallower model)
         CFG["resident"] = a.layers
-        if a.workload == "llama3.2-1b-decode":
+        if a.workload != "llama3-8b-long":
             CFG["layers"] = a.layers
     return a
 

@@ -45,6 +45,8 @@ struct PrefillParams {
   int max_blocks;
   const int* tiles;  // [n_tiles] x {slot, q_row0, ntok, pos0}
   int n_tiles;
+  const int* sched;  // optional: [n_ctas + 1] offsets, then the items (tile * Hkv + kv head) of each CTA
+  int n_ctas;
   float scale_log2;
   int* status;
   int stages;
@@ -64,6 +66,31 @@ __device__ __forceinline__ uint32_t pf_off_sfull(int b) { return 64 + 8 * b; }
 __device__ __forceinline__ uint32_t pf_off_sempty(int b) { return 80 + 8 * b; }
 constexpr uint32_t kPfPfull = 96, kPfOdone = 104, kPfQfull = 112, kPfTmem = 128;
 
+// The work items of this CTA: its list in the schedule, or every gridDim.x-th item.
+struct PfItems {
+  int i, end, step;
+  const int* list;
+  __device__ PfItems(const PrefillParams& p) {
+    if (p.sched) {
+      i = __ldg(p.sched + blockIdx.x);
+      end = __ldg(p.sched + blockIdx.x + 1);
+      step = 1;
+      list = p.sched + p.n_ctas + 1;
+    } else {
+      i = blockIdx.x;
+      end = p.n_tiles * p.Hkv;
+      step = gridDim.x;
+      list = nullptr;
+    }
+  }
+  __device__ bool next(int& item) {
+    if (i >= end) return false;
+    item = list ? __ldg(list + i) : i;
+    i += step;
+    return true;
+  }
+};
+
 __device__ __forceinline__ int pf_block(const PrefillParams& p, const int* btrow, int lb) {
   int phys = lb < p.max_blocks ? __ldg(btrow + lb) : -1;
   if (phys < 0 || phys >= p.num_blocks) {
@@ -80,10 +107,10 @@ __device__ void pf_producer(const PrefillParams& p, const CUtensorMap* tk, const
   constexpr uint32_t TILE = 128 * D_ * 2;  // bytes of a 128-key K or V tile
   const int S = p.stages;
   const uint64_t pol = l2_evict_last();  // every query tile of a chunk reads the same keys
-  const int n_items = p.n_tiles * p.Hkv;
   int st = 0;
   uint32_t pe = 1;
-  for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
+  PfItems items(p);
+  for (int item; items.next(item);) {
     const int t = item / p.Hkv, kvh = item - t * p.Hkv;
     const int4 tl = __ldg(reinterpret_cast<const int4*>(p.tiles) + t);
     const int nkeys = tl.w + tl.z, nkt = (nkeys + 127) >> 7;
@@ -125,7 +152,6 @@ __device__ void pf_mma(const PrefillParams& p, uint32_t hdr, uint32_t tmem, uint
   const uint32_t idesc_s = umma_idesc_f16(bf, 128, 128, false, false);
   const uint32_t idesc_o = umma_idesc_f16(bf, 128, D_, false, true);
   const int S = p.stages;
-  const int n_items = p.n_tiles * p.Hkv;
   int st = 0, tc = 0, npv = 0, nq = 0;
   uint32_t pf = 0;
   auto issue_pv = [&](int stage, bool first) -> bool {
@@ -143,7 +169,8 @@ __device__ void pf_mma(const PrefillParams& p, uint32_t hdr, uint32_t tmem, uint
     umma_commit(hdr + pf_off_kvempty(stage));
     return true;
   };
-  for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
+  PfItems items(p);
+  for (int item; items.next(item);) {
     const int t = item / p.Hkv;
     const int4 tl = __ldg(reinterpret_cast<const int4*>(p.tiles) + t);
     const int nkt = (tl.w + tl.z + 127) >> 7;
@@ -187,9 +214,9 @@ __device__ void pf_softmax(const PrefillParams& p, uint32_t hdr, uint32_t tmem, 
   const uint32_t lane_addr = (uint32_t)(quad * 32) << 16;
   const int S = p.stages;
   const int G = p.G;
-  const int n_items = p.n_tiles * p.Hkv;
   int tc = 0, nod = 0, st = 0, nq = 0;
-  for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
+  PfItems items(p);
+  for (int item; items.next(item);) {
     const int t = item / p.Hkv, kvh = item - t * p.Hkv;
     const int4 tl = __ldg(reinterpret_cast<const int4*>(p.tiles) + t);
     const int nkeys = tl.w + tl.z, nkt = (nkeys + 127) >> 7;
@@ -225,32 +252,48 @@ __device__ void pf_softmax(const PrefillParams& p, uint32_t hdr, uint32_t tmem, 
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(hdr + pf_off_sempty(b));
-      // causal mask (key k visible to the query at qpos iff k <= qpos), scale, tile max
+      // causal mask (key k visible to the query at qpos iff k <= qpos), only
+      // on tiles that cross some row's diagonal; tile max of the raw scores
+      // over 8 independent chains
       const int k0 = j * 128;
       const int lim = valid ? qpos - k0 : -1;  // columns <= lim are visible
-      float mt = kPfNegInf;
+      if (!__all_sync(0xffffffffu, lim >= 127)) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (c * 32 + i > lim) x[c][i] = __float_as_uint(kPfNegInf);
+      }
+      float acc[8];
+#pragma unroll
+      for (int a = 0; a < 8; ++a) acc[a] = kPfNegInf;
 #pragma unroll
       for (int c = 0; c < 4; ++c)
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const float v = (c * 32 + i <= lim) ? __uint_as_float(x[c][i]) * p.scale_log2 : kPfNegInf;
-          x[c][i] = __float_as_uint(v);
-          mt = fmaxf(mt, v);
-        }
-      const float mn = fmaxf(m, mt);
-      const float base = mn == kPfNegInf ? 0.f : mn;
-      const float alpha = ex2(m - base);
-      float sum = 0.f;
+        for (int i = 0; i < 32; ++i) acc[i & 7] = fmaxf(acc[i & 7], __uint_as_float(x[c][i]));
+      const float mt = fmaxf(fmaxf(fmaxf(acc[0], acc[1]), fmaxf(acc[2], acc[3])),
+                             fmaxf(fmaxf(acc[4], acc[5]), fmaxf(acc[6], acc[7]))) * p.scale_log2;
+      // lazy rescaling: the reference max moves (and O and l are rescaled)
+      // only when the tile's max exceeds it by more than 8, so exponents stay
+      // <= 2^8 and most tiles need no O round trip through registers
+      const bool grow = mt > m + 8.f;
+      const float mn = grow ? mt : m;
+      const float alpha = grow ? ex2(m - mn) : 1.f;  // 0 on the first visible tile
+      const float nbase = mn == kPfNegInf ? 0.f : -mn;
+      float sa[8];
+#pragma unroll
+      for (int a = 0; a < 8; ++a) sa[a] = 0.f;
       uint32_t pk[64];
 #pragma unroll
       for (int c = 0; c < 4; ++c)
 #pragma unroll
         for (int i = 0; i < 32; i += 2) {
-          const float p0 = ex2(__uint_as_float(x[c][i]) - base), p1 = ex2(__uint_as_float(x[c][i + 1]) - base);
-          sum += p0 + p1;
+          const float p0 = ex2(fmaf(__uint_as_float(x[c][i]), p.scale_log2, nbase));
+          const float p1 = ex2(fmaf(__uint_as_float(x[c][i + 1]), p.scale_log2, nbase));
+          sa[(i >> 1) & 7] += p0 + p1;
           pk[c * 16 + i / 2] = pack2<T>(p0, p1);
         }
-      l = l * alpha + sum;
+      l = l * alpha + (((sa[0] + sa[1]) + (sa[2] + sa[3])) + ((sa[4] + sa[5]) + (sa[6] + sa[7])));
       m = mn;
       if (j > 0) {
         // O += P V of the previous tile must be done: rescale O, then P is free
@@ -368,7 +411,8 @@ extern "C" int nf_prefill_attention(void* out, int64_t out_row_stride, const voi
                                     const void* k_pool, const void* v_pool, int32_t dtype, int32_t num_q_heads,
                                     int32_t num_kv_heads, int32_t head_dim, int32_t block_size, int32_t num_blocks,
                                     const int32_t* block_tables, int32_t max_blocks_per_seq, const int32_t* tiles,
-                                    int32_t n_tiles, float scale, int32_t* status, void* stream) {
+                                    int32_t n_tiles, const int32_t* schedule, int32_t n_ctas, float scale,
+                                    int32_t* status, void* stream) {
   using namespace nf;
   if (dtype != NF_BF16 && dtype != NF_F16)
     return fail(NF_EUNSUPPORTED, "nf_prefill_attention: 16-bit pools only (dtype %d)", dtype);
@@ -408,6 +452,10 @@ extern "C" int nf_prefill_attention(void* out, int64_t out_row_stride, const voi
   p.max_blocks = max_blocks_per_seq;
   p.tiles = tiles;
   p.n_tiles = n_tiles;
+  p.sched = schedule;
+  p.n_ctas = n_ctas;
+  if (schedule && (n_ctas <= 0 || n_ctas > sm_count()))
+    return fail(NF_EINVAL, "nf_prefill_attention: a schedule needs 1..%d CTAs (got %d)", sm_count(), n_ctas);
   p.scale_log2 = scale * 1.4426950408889634f;
   p.status = status;
   p.stages = head_dim == 64 ? 4 : 2;
@@ -421,6 +469,7 @@ extern "C" int nf_prefill_attention(void* out, int64_t out_row_stride, const voi
   if (e != cudaSuccess) return fail(NF_ECUDA, "nf_prefill_attention: smem attribute: %s", cudaGetErrorString(e));
   long long grid = (long long)n_tiles * num_kv_heads;
   if (grid > sm_count()) grid = sm_count();
+  if (schedule) grid = n_ctas;
   kern<<<(int)grid, kPfThreads, smem, static_cast<cudaStream_t>(stream)>>>(p, tk, tv);
   return check_launch("nf_prefill_attention");
 }

@@ -29,6 +29,7 @@ advances only when the last layer of a step has appended
 
 from __future__ import annotations
 
+import heapq
 import math
 
 import numpy as np
@@ -78,6 +79,28 @@ def seq_unit_sizes(seq_keys: np.ndarray, split: int, sms: int, fine_div: int = 4
     return sizes
 
 
+def _prefill_schedule(tiles, kv_heads: int, sms: int) -> np.ndarray:
+    """Per-CTA lists of the prefill kernel's (tile, KV head) items, longest first.
+
+    An item costs its 128-key tiles plus one (query load and epilogue); items
+    go in decreasing cost to the least-loaded CTA (longest processing time
+    first), which keeps CTAs within about one item of each other.  Returns the
+    int32 array [n_ctas + 1 offsets, items] that nf_prefill_attention reads.
+    """
+    costs = [(pos0 + ntok + 127) // 128 + 1 for (_, _, ntok, pos0) in tiles]
+    n_items = len(tiles) * kv_heads
+    n_ctas = min(sms, n_items)
+    order = sorted(range(n_items), key=lambda it: -costs[it // kv_heads])
+    heap = [(0, b) for b in range(n_ctas)]
+    lists = [[] for _ in range(n_ctas)]
+    for it in order:
+        load, b = heapq.heappop(heap)
+        lists[b].append(it)
+        heapq.heappush(heap, (load + costs[it // kv_heads], b))
+    offs = np.cumsum([0] + [len(x) for x in lists])
+    return np.concatenate([offs, np.concatenate([np.asarray(x, np.int64) for x in lists])]).astype(np.int32)
+
+
 class StepPlan:
     """Device metadata of one forward pass over a ragged batch.
 
@@ -106,6 +129,8 @@ class StepPlan:
         self.tiles = None
         self.n_tiles = 0
         self.q_heads = None
+        self.sched = None
+        self.n_ctas = 0
 
     @property
     def kv_lens(self) -> np.ndarray:
@@ -331,15 +356,19 @@ class PagedKVCache:
                     tiles.append((int(slots[i]), r0 + t0, min(tt, n - t0), c + t0))
 
         n_tiles = len(tiles)
+        sched = _prefill_schedule(tiles, self.n_heads, self.sm_count) if n_tiles else np.zeros(0, np.int32)
+        n_ctas = int(min(self.sm_count, n_tiles * self.n_heads)) if n_tiles else 0
         off_tiles = _align4(S * 5 + P * 3)
-        host = np.zeros(off_tiles + 4 * n_tiles, dtype=np.int32)
+        off_sched = off_tiles + 4 * n_tiles
+        host = np.zeros(off_sched + sched.size, dtype=np.int32)
         host[: S * 4] = np.stack([slots, q_starts, q_lens, ctx], axis=1).reshape(-1)
         if P:
             host[S * 4: S * 4 + P * 3] = np.asarray(patches, dtype=np.int32).reshape(-1)
         host[S * 4 + P * 3: S * 5 + P * 3] = seq_split
         if n_tiles:
-            host[off_tiles:] = np.asarray(tiles, dtype=np.int32).reshape(-1)
-        off_slot = off_tiles + 4 * n_tiles
+            host[off_tiles:off_sched] = np.asarray(tiles, dtype=np.int32).reshape(-1)
+            host[off_sched:] = sched
+        off_slot = _align4(off_sched + sched.size)
         off_src = off_slot + T
         off_items = _align4(off_src + T)
         off_units = off_items + 4 * T
@@ -353,6 +382,8 @@ class PagedKVCache:
         plan.q_heads = q_heads
         plan.n_tiles = n_tiles
         plan.tiles = meta[off_tiles: off_tiles + 4 * n_tiles]
+        plan.sched = meta[off_sched: off_sched + sched.size]
+        plan.n_ctas = n_ctas
         plan.seqs = meta[: S * 4]
         plan.slot_mapping = meta[off_slot: off_slot + T]
         plan.src_rows = meta[off_src: off_src + T]
@@ -437,8 +468,8 @@ class PagedKVCache:
                 out.data_ptr(), out.stride(0), q.data_ptr(), q.stride(0),
                 self.k[layer_id].data_ptr(), self.v[layer_id].data_ptr(), _lib.dtype_code(self.dtype),
                 hq, self.n_heads, D, self.block_size, self.num_blocks, self.bt_dev.data_ptr(),
-                self.max_blocks_per_seq, plan.tiles.data_ptr(), plan.n_tiles, float(scale),
-                self.status.data_ptr(), stream), "nf_prefill_attention")
+                self.max_blocks_per_seq, plan.tiles.data_ptr(), plan.n_tiles, plan.sched.data_ptr(),
+                plan.n_ctas, float(scale), self.status.data_ptr(), stream), "nf_prefill_attention")
         if events is not None:
             events[1].record()
         if plan.decode_units:
