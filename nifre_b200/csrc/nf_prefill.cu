@@ -54,7 +54,6 @@ struct PrefillParams {
 
 constexpr int kPfThreads = 192;  // warp 0 producer, warp 1 MMA, warps 2-5 softmax
 constexpr float kPfNegInf = -INFINITY;
-constexpr int kPfMaxStages = 4;
 constexpr int kPfHdr = 1024;     // mbarriers and the tensor-memory base
 constexpr uint32_t kTmemCols = 512;
 
@@ -91,13 +90,15 @@ struct PfItems {
   }
 };
 
-__device__ __forceinline__ int pf_block(const PrefillParams& p, const int* btrow, int lb) {
-  int phys = lb < p.max_blocks ? __ldg(btrow + lb) : -1;
-  if (phys < 0 || phys >= p.num_blocks) {
-    atomicOr(p.status, NF_STATUS_BAD_BLOCK);
-    phys = 0;
+// Block ids of the eight 16-key blocks of key tile j (keys >= nkeys: 0, not
+// loaded).  The eight loads are independent, so they cost one round trip.
+__device__ __forceinline__ void pf_tile_blocks(const PrefillParams& p, const int* btrow, int j, int nkeys,
+                                               int (&ph)[8]) {
+#pragma unroll
+  for (int b = 0; b < 8; ++b) {
+    const int key = (j * 8 + b) * 16, lb = key / p.bs;
+    ph[b] = (key < nkeys && lb < p.max_blocks) ? __ldg(btrow + lb) : (key < nkeys ? -1 : 0);
   }
-  return phys;
 }
 
 template <int D_>
@@ -115,15 +116,26 @@ __device__ void pf_producer(const PrefillParams& p, const CUtensorMap* tk, const
     const int4 tl = __ldg(reinterpret_cast<const int4*>(p.tiles) + t);
     const int nkeys = tl.w + tl.z, nkt = (nkeys + 127) >> 7;
     const int* btrow = p.bt + (long long)tl.x * p.max_blocks;
+    // the next tile's block ids are loaded while this tile's copies are in
+    // flight and the next stage is awaited: a tile's copies never wait on
+    // the block table
+    int cur[8], nxt[8];
+    pf_tile_blocks(p, btrow, 0, nkeys, cur);
     for (int j = 0; j < nkt; ++j) {
       if (!mbar_wait(hdr + pf_off_kvempty(st), pe, p.status)) return;
       const int nb = min(8, (nkeys - j * 128 + 15) >> 4);
       const uint32_t full = hdr + pf_off_kvfull(st);
       mbar_arrive_expect_tx(full, nb * NDH * 2 * 2048);
       const uint32_t ks = kv_s + st * 2 * TILE, vs = ks + TILE;
-      for (int b = 0; b < nb; ++b) {
-        const int key = (j * 8 + b) * 16, lb = key / p.bs, off = key - lb * p.bs;
-        const int phys = pf_block(p, btrow, lb);
+#pragma unroll
+      for (int b = 0; b < 8; ++b) {
+        if (b >= nb) break;
+        const int key = (j * 8 + b) * 16, off = key % p.bs;
+        int phys = cur[b];
+        if (phys < 0 || phys >= p.num_blocks) {
+          atomicOr(p.status, NF_STATUS_BAD_BLOCK);
+          phys = 0;
+        }
 #pragma unroll
         for (int dh = 0; dh < NDH; ++dh) {
           const uint32_t dst = dh * 128 * 128 + b * 2048;
@@ -135,6 +147,11 @@ __device__ void pf_producer(const PrefillParams& p, const CUtensorMap* tk, const
             tma_load_5d(vs + dst, tv, 0, dh, kvh, off, phys, full, pol);
           }
         }
+      }
+      if (j + 1 < nkt) {
+        pf_tile_blocks(p, btrow, j + 1, nkeys, nxt);
+#pragma unroll
+        for (int b = 0; b < 8; ++b) cur[b] = nxt[b];
       }
       if (++st == S) {
         st = 0;
