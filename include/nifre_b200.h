@@ -184,10 +184,12 @@ int nf_paged_attention(void* out, int64_t out_row_stride,
  * rows in q/out start at q_row0 and whose absolute positions start at pos0;
  * query pos0 + i attends over keys [0, pos0 + i] of the slot's block table
  * (attention.py:144-152), all already appended.  Writes those rows of out.
- * Work items are (tile, KV head), numbered tile * num_kv_heads + head.
- * schedule (device, may be NULL): n_ctas + 1 offsets followed by the items,
- * CTA b running items [offsets[b], offsets[b+1]) in that order (n_ctas <= the
- * SM count; the caller balances the lists); NULL deals items round-robin.
+ * Work items are (tile, KV head), numbered tile * num_kv_heads + head.  The
+ * kernel runs nf_prefill_pipelines(head_dim) independent pipelines per SM.
+ * schedule (device, may be NULL): n_lists + 1 offsets followed by the items,
+ * pipeline w running items [offsets[w], offsets[w+1]) in that order (n_lists
+ * <= SMs x pipelines; the caller balances the lists); NULL deals items
+ * round-robin.
  */
 int nf_prefill_attention(void* out, int64_t out_row_stride, const void* q, int64_t q_row_stride,
                          const void* k_pool, const void* v_pool, int32_t dtype,
@@ -195,8 +197,11 @@ int nf_prefill_attention(void* out, int64_t out_row_stride, const void* q, int64
                          int32_t block_size, int32_t num_blocks,
                          const int32_t* block_tables, int32_t max_blocks_per_seq,
                          const int32_t* tiles, int32_t n_tiles,
-                         const int32_t* schedule, int32_t n_ctas, float scale,
+                         const int32_t* schedule, int32_t n_lists, float scale,
                          int32_t* status, void* stream);
+
+/* Independent pipelines per SM of nf_prefill_attention for this head_dim. */
+int nf_prefill_pipelines(int32_t head_dim);
 
 /*
  * nf_paged_attention_noalloc: nf_paged_attention without a caller workspace.

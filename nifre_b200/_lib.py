@@ -26,7 +26,7 @@ _DTYPE_CODE = {torch.float32: NF_F32, torch.float16: NF_F16, torch.bfloat16: NF_
 
 EXPORTS = ("nf_last_error", "nf_abi_version", "nf_pack_step", "nf_kv_append",
            "nf_attention_workspace", "nf_paged_attention", "nf_paged_attention_noalloc",
-           "nf_last_attention_path", "nf_selftest_umma", "nf_prefill_attention")
+           "nf_last_attention_path", "nf_selftest_umma", "nf_prefill_attention", "nf_prefill_pipelines")
 
 _P = ctypes.c_void_p
 _I32 = ctypes.c_int32
@@ -37,6 +37,7 @@ _SIGNATURES = {
     "nf_abi_version": ([], ctypes.c_int),
     "nf_last_attention_path": ([], ctypes.c_int),
     "nf_selftest_umma": ([_P, _P, _P, _I32, _I32, _I32, _P, _P], ctypes.c_int),
+    "nf_prefill_pipelines": ([_I32], ctypes.c_int),
     "nf_prefill_attention": ([_P, _I64, _P, _I64, _P, _P, _I32, _I32, _I32, _I32, _I32, _I32,
                               _P, _I32, _P, _I32, _P, _I32, ctypes.c_float, _P, _P], ctypes.c_int),
     "nf_pack_step": ([_P, _I32, _P, _I32, _P, _I32, _I32, _I32, _I32, _I32, _P,

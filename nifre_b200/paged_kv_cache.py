@@ -80,7 +80,8 @@ def seq_unit_sizes(seq_keys: np.ndarray, split: int, sms: int, fine_div: int = 4
 
 
 def _prefill_schedule(tiles, kv_heads: int, sms: int) -> np.ndarray:
-    """Per-CTA lists of the prefill kernel's (tile, KV head) items, longest first.
+    """Per-worker lists of the prefill kernel's (tile, KV head) items, longest first
+    (``sms``: the number of workers, the kernel's pipelines on all SMs).
 
     An item costs its 128-key tiles plus one (query load and epilogue); items
     go in decreasing cost to the least-loaded CTA (longest processing time
@@ -356,8 +357,9 @@ class PagedKVCache:
                     tiles.append((int(slots[i]), r0 + t0, min(tt, n - t0), c + t0))
 
         n_tiles = len(tiles)
-        sched = _prefill_schedule(tiles, self.n_heads, self.sm_count) if n_tiles else np.zeros(0, np.int32)
-        n_ctas = int(min(self.sm_count, n_tiles * self.n_heads)) if n_tiles else 0
+        workers = self.sm_count * _lib.load().nf_prefill_pipelines(self.head_dim)  # independent pipelines
+        sched = _prefill_schedule(tiles, self.n_heads, workers) if n_tiles else np.zeros(0, np.int32)
+        n_ctas = int(min(workers, n_tiles * self.n_heads)) if n_tiles else 0  # number of lists
         off_tiles = _align4(S * 5 + P * 3)
         off_sched = off_tiles + 4 * n_tiles
         host = np.zeros(off_sched + sched.size, dtype=np.int32)

@@ -244,7 +244,7 @@ def test_prefill_schedule_covers_items_and_balances():
     from nifre_b200.paged_kv_cache import _prefill_schedule
     rng = np.random.default_rng(0)
     tiles = [(0, 32 * t, 32, int(p) + 32 * t) for t, p in enumerate(rng.integers(0, 2048, size=60))]
-    H, sms = 8, 148
+    H, sms = 8, 296
     arr = _prefill_schedule(tiles, H, sms)
     n_ctas = min(sms, len(tiles) * H)
     offs, items = arr[: n_ctas + 1], arr[n_ctas + 1:]
