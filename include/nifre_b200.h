@@ -53,6 +53,7 @@ extern "C" {
 #define NF_STATUS_UNIT_OVERFLOW 2 /* more work units than the caller's workspace holds */
 #define NF_STATUS_WAIT_TIMEOUT 4  /* a pipeline wait gave up after its time limit */
 #define NF_STATUS_BAD_SLOT 8    /* cache slot out of range: entry skipped */
+#define NF_STATUS_BAD_TILE 16   /* prefill tile longer than nf_prefill_tile_rows() rows: rest skipped */
 
 /* Record layouts (int32) of the step descriptor the host uploads. */
 #define NF_SEQ_FIELDS 4   /* slot, q_start (row of the first new token), q_len, ctx_before */
@@ -79,8 +80,9 @@ int nf_last_attention_path(void);
  * Diagnostic, no counterpart in the reference: one 128 x N x K bfloat16
  * tensor-core (tcgen05) product from 128-byte-swizzled shared memory into
  * tensor memory, the building block of the prefill kernel.  A: 128 x K,
- * B: N x K (mode 0, C = A B^T) or K x N (mode 1, C = A B), row-major device
- * arrays; C: 128 x N float32.  N, K in {64, 128}.
+ * B: N x K (mode 0, C = A B^T) or K x N (mode 1 and 2, C = A B), row-major
+ * device arrays; mode 2 stages A in tensor memory (the P V operand form of
+ * the prefill kernel).  C: 128 x N float32.  N, K in {64, 128}.
  */
 int nf_selftest_umma(const void* A, const void* B, float* C, int32_t N, int32_t K, int32_t mode,
                      int32_t* status, void* stream);
@@ -180,16 +182,15 @@ int nf_paged_attention(void* out, int64_t out_row_stride,
  * cores (tcgen05, tensor memory), for 16-bit pools with head_dim 64 or 128,
  * 1, 2, 4 or 8 query heads per KV head and block_size a multiple of 16.
  * tiles[n_tiles][4] (device, 16-byte aligned): slot, q_row0, ntok, pos0 -- the
- * ntok (<= 128 / group size) consecutive query tokens of one sequence whose
- * rows in q/out start at q_row0 and whose absolute positions start at pos0;
- * query pos0 + i attends over keys [0, pos0 + i] of the slot's block table
- * (attention.py:144-152), all already appended.  Writes those rows of out.
- * Work items are (tile, KV head), numbered tile * num_kv_heads + head.  The
- * kernel runs nf_prefill_pipelines(head_dim) independent pipelines per SM.
+ * ntok (<= nf_prefill_tile_rows() / group size) consecutive query tokens of
+ * one sequence whose rows in q/out start at q_row0 and whose absolute
+ * positions start at pos0; query pos0 + i attends over keys [0, pos0 + i] of
+ * the slot's block table (attention.py:144-152), all already appended.
+ * Writes those rows of out.  Work items are (tile, KV head), numbered
+ * tile * num_kv_heads + head; one CTA per SM runs a list of them.
  * schedule (device, may be NULL): n_lists + 1 offsets followed by the items,
- * pipeline w running items [offsets[w], offsets[w+1]) in that order (n_lists
- * <= SMs x pipelines; the caller balances the lists); NULL deals items
- * round-robin.
+ * CTA w running items [offsets[w], offsets[w+1]) in that order (n_lists <=
+ * SMs; the caller balances the lists); NULL deals items round-robin.
  */
 int nf_prefill_attention(void* out, int64_t out_row_stride, const void* q, int64_t q_row_stride,
                          const void* k_pool, const void* v_pool, int32_t dtype,
@@ -200,8 +201,8 @@ int nf_prefill_attention(void* out, int64_t out_row_stride, const void* q, int64
                          const int32_t* schedule, int32_t n_lists, float scale,
                          int32_t* status, void* stream);
 
-/* Independent pipelines per SM of nf_prefill_attention for this head_dim. */
-int nf_prefill_pipelines(int32_t head_dim);
+/* Query rows (tokens x query heads per KV head) of one nf_prefill_attention work item: 256. */
+int nf_prefill_tile_rows(void);
 
 /*
  * nf_paged_attention_noalloc: nf_paged_attention without a caller workspace.

@@ -19,6 +19,7 @@ NF_STATUS_BAD_BLOCK = 1
 NF_STATUS_UNIT_OVERFLOW = 2
 NF_STATUS_WAIT_TIMEOUT = 4
 NF_STATUS_BAD_SLOT = 8
+NF_STATUS_BAD_TILE = 16
 
 SEQ_FIELDS, PATCH_FIELDS, ITEM_FIELDS, UNIT_FIELDS = 4, 3, 4, 8
 
@@ -26,7 +27,7 @@ _DTYPE_CODE = {torch.float32: NF_F32, torch.float16: NF_F16, torch.bfloat16: NF_
 
 EXPORTS = ("nf_last_error", "nf_abi_version", "nf_pack_step", "nf_kv_append",
            "nf_attention_workspace", "nf_paged_attention", "nf_paged_attention_noalloc",
-           "nf_last_attention_path", "nf_selftest_umma", "nf_prefill_attention", "nf_prefill_pipelines")
+           "nf_last_attention_path", "nf_selftest_umma", "nf_prefill_attention", "nf_prefill_tile_rows")
 
 _P = ctypes.c_void_p
 _I32 = ctypes.c_int32
@@ -37,7 +38,7 @@ _SIGNATURES = {
     "nf_abi_version": ([], ctypes.c_int),
     "nf_last_attention_path": ([], ctypes.c_int),
     "nf_selftest_umma": ([_P, _P, _P, _I32, _I32, _I32, _P, _P], ctypes.c_int),
-    "nf_prefill_pipelines": ([_I32], ctypes.c_int),
+    "nf_prefill_tile_rows": ([], ctypes.c_int),
     "nf_prefill_attention": ([_P, _I64, _P, _I64, _P, _P, _I32, _I32, _I32, _I32, _I32, _I32,
                               _P, _I32, _P, _I32, _P, _I32, ctypes.c_float, _P, _P], ctypes.c_int),
     "nf_pack_step": ([_P, _I32, _P, _I32, _P, _I32, _I32, _I32, _I32, _I32, _P,

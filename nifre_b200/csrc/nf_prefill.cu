@@ -3,30 +3,37 @@
 // The reference computes a prefill chunk per row as get -> cat -> q @ k^T ->
 // causal mask (query i at position past + i sees keys <= past + i) ->
 // softmax(scores / sqrt(D)) -> @ v (src/inference/attention.py:106-152).
-// Here a work item is a tile of 128 query rows -- 128/G tokens of one
+// Here a work item is 256 query rows -- 256/G consecutive tokens of one
 // sequence times the G query heads that share a KV head -- against all keys
-// up to its last token, for one KV head.  A CTA runs NP independent
-// pipelines (two for head_dim 64, one for 128), each with its own work list,
-// shared-memory region and tensor-memory columns:
+// up to its last token, for one KV head.  The rows form two 128-row halves
+// that share one stream of K and V tiles; each CTA is persistent over its
+// list of items:
 //
-//   producer lane: TMA copies of 128-key K and V tiles from the paged pools
-//     (one 16-token box per block and 64-element half of a head, landing as
-//     128-byte-swizzled rows), a ring of stages; the next tile's block ids
-//     are loaded while the current tile's copies are in flight;
-//   MMA lane: S = Q K^T (M=128, N=128, K=D) into tensor memory, then
-//     O += P V (N=D, K=128) into O in tensor memory, each completion
-//     committed to an mbarrier;
-//   softmax warpgroup (thread = row): reads S from tensor memory twice, 64
-//     columns at a time (the tile max, then the exponents), causal mask only
-//     on tiles that cross the diagonal, exp2 with the scale folded into one
-//     FMA, a reference max that moves only when a row's max grows by more
-//     than 2^8 (O and the row sum rescaled then), P written as bfloat16/half
-//     into the swizzled shared-memory A operand of P V; at the end it divides
-//     by the row sum and stores the row.
+//   producer warp: TMA copies of 128-key K and V tiles from the paged pools
+//     (one 16-token box per block and 64-element part of a head, landing as
+//     128-byte-swizzled rows) into separate K and V rings, so that a K stage
+//     is refilled as soon as both halves' S = Q K^T have read it; the next
+//     tile's block ids are loaded while the current tile's copies fly;
+//   MMA warp (one lane issues): per key tile, S_h = Q_h K^T (M=128, N=128, K=D) into tensor
+//     memory for each half h, then O_h += P_h V (N=D, K=128) with P_h read
+//     from tensor memory (the TS form: A in tensor memory, V in shared);
+//   two softmax warpgroups, one per half (thread = row, 216 registers), which alternate on
+//     the tensor core: each reads its S_h tile from tensor memory once into
+//     registers (for head_dim 64 the S buffer is released right away, so the
+//     next S_h overlaps the exponentials), applies the causal mask only on
+//     tiles that cross the diagonal, keeps a reference max that moves only
+//     when a row's max grows by more than 2^8 (O_h and the row sum rescaled
+//     then), computes exp2 with the scale folded into one packed FMA -- a
+//     quarter of them as a polynomial on the FMA pipe, the rest on the
+//     special-function unit, which alone would bound head_dim 64 -- and stores P_h
+//     as bfloat16/half pairs into tensor memory; at the end it divides by the
+//     row sum and stores the row.
 //
-// With two pipelines the SM holds two softmax warps per scheduler, so one
-// pipeline's exponentials and waits overlap the other's.  Every wait is an
-// mbarrier wait with a time limit (NF_STATUS_WAIT_TIMEOUT).
+// Tensor memory (512 columns): S_0, S_1 at 0 and 128, O_0, O_1 from 256; P_h
+// has its own 64 columns from 384 for head_dim 64 and overwrites the first
+// half of S_h for head_dim 128 (no room left), where the MMA warp then issues
+// P_h V before the next S_h.  Every wait is an mbarrier wait with a time
+// limit (NF_STATUS_WAIT_TIMEOUT).
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -46,7 +53,7 @@ struct PrefillParams {
   long long out_stride;
   const char* q;
   long long q_stride;
-  int Hq, Hkv, G, bs, num_blocks;
+  int Hq, Hkv, G, TT, bs, num_blocks;  // TT: tokens per 128-row half
   const int* bt;
   int max_blocks;
   const int* tiles;  // [n_tiles] x {slot, q_row0, ntok, pos0}
@@ -58,39 +65,126 @@ struct PrefillParams {
 };
 
 constexpr float kPfNegInf = -INFINITY;
+constexpr int kPfRows = 256;  // query rows of a work item
 
-// Resources of one pipeline, per head_dim and pipelines per CTA.
-template <int D_, int NP>
+template <int D_>
 struct PfCfg {
-  static constexpr uint32_t TILE = 128 * D_ * 2;         // a 128-row Q tile, or a 128-key K or V tile
-  static constexpr uint32_t PB = 128 * 128 * 2;          // P: 128 rows x 128 keys
-  static constexpr int NSB = NP == 1 ? 2 : 1;            // S buffers in tensor memory
-  static constexpr int STAGES = NP == 1 ? (D_ == 64 ? 4 : 2) : 2;
-  static constexpr uint32_t PIPE = TILE + PB + STAGES * 2 * TILE;  // Q, P, K/V stages
-  static constexpr uint32_t SMEM = 1024 + 1024 + NP * PIPE;        // alignment slack, barriers, pipelines
-  static constexpr uint32_t TM_PIPE = 256;               // tensor-memory columns per pipeline
-  static constexpr uint32_t O_COL = NSB * 128;           // O after the S buffers
-  static constexpr int THREADS = (4 + 4 * NP) * 32;      // warps 0..NP-1 producers, 2..2+NP-1 MMA, softmax from 4
+  static constexpr uint32_t TILE = 128 * D_ * 2;  // a 128-row Q half, or a 128-key K or V tile
+  static constexpr int KST = D_ == 64 ? 5 : 2;    // K ring
+  static constexpr int VST = D_ == 64 ? 6 : 3;    // V ring (held one tile longer than K)
+  static constexpr bool P_ALIAS = D_ == 128;      // P_h over the first 64 columns of S_h
+  static constexpr uint32_t Q_OFF = 1024;         // after the barrier header
+  static constexpr uint32_t K_OFF = Q_OFF + 2 * TILE;
+  static constexpr uint32_t V_OFF = K_OFF + KST * TILE;
+  static constexpr uint32_t SMEM = 1024 + V_OFF + VST * TILE;  // + alignment slack
+  static constexpr int THREADS = 384;             // warp 0 producer, 1 MMA, 4-7 half 0, 8-11 half 1
+  // registers per thread: 168 at launch (384 x 168 <= 64K); the first
+  // warpgroup gives back to 72 and the softmax warpgroups take 216, which
+  // adds up to the launch total: 72 x 128 + 216 x 256 = 384 x 168
+  static constexpr int REGS_CTRL = 72, REGS_SOFTMAX = 216;
+  static __device__ __forceinline__ uint32_t s_col(int h) { return h * 128; }
+  static __device__ __forceinline__ uint32_t o_col(int h) { return 256 + h * D_; }
+  static __device__ __forceinline__ uint32_t p_col(int h) { return P_ALIAS ? h * 128 : 384 + h * 64; }
 };
 constexpr uint32_t kTmemCols = 512;
 
-// Barriers of pipeline pi, 128 bytes each at the start of the header:
-// kv_full[4] 0, kv_empty[4] 32, s_full[2] 64, s_empty[2] 80, p_full 96,
-// o_done 104, q_full 112; tensor-memory base at header + 512.
+// Barriers at the start of the header: k_full[8] 0, k_empty[8] 64,
+// v_full[8] 128, v_empty[8] 192, then per half s_full 256, s_free 272,
+// p_full 288, o_done 304, q_full 320; tensor-memory base at 512.
 struct PfBars {
-  uint32_t base;
-  __device__ PfBars(uint32_t hdr, int pi) : base(hdr + 128 * pi) {}
-  __device__ uint32_t kv_full(int s) const { return base + 8 * s; }
-  __device__ uint32_t kv_empty(int s) const { return base + 32 + 8 * s; }
-  __device__ uint32_t s_full(int b) const { return base + 64 + 8 * b; }
-  __device__ uint32_t s_empty(int b) const { return base + 80 + 8 * b; }
-  __device__ uint32_t p_full() const { return base + 96; }
-  __device__ uint32_t o_done() const { return base + 104; }
-  __device__ uint32_t q_full() const { return base + 112; }
+  uint32_t hdr;
+  __device__ explicit PfBars(uint32_t h) : hdr(h) {}
+  __device__ uint32_t k_full(int s) const { return hdr + 8 * s; }
+  __device__ uint32_t k_empty(int s) const { return hdr + 64 + 8 * s; }
+  __device__ uint32_t v_full(int s) const { return hdr + 128 + 8 * s; }
+  __device__ uint32_t v_empty(int s) const { return hdr + 192 + 8 * s; }
+  __device__ uint32_t s_full(int h) const { return hdr + 256 + 8 * h; }
+  __device__ uint32_t s_free(int h) const { return hdr + 272 + 8 * h; }
+  __device__ uint32_t p_full(int h) const { return hdr + 288 + 8 * h; }
+  __device__ uint32_t o_done(int h) const { return hdr + 304 + 8 * h; }
+  __device__ uint32_t q_full(int h) const { return hdr + 320 + 8 * h; }
 };
 constexpr uint32_t kPfTmemPtr = 512;
 
-// The work items of pipeline `worker`: its list in the schedule, or every
+// ---------------------------------------------------------------- softmax arithmetic
+// Pairs of fp32 values in one 64-bit register, for the packed fp32x2
+// instructions of sm_100 (two FMAs or adds per issue).
+__device__ __forceinline__ uint64_t f2_pack(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// 2^y for a pair y <= 8 on the FMA pipe instead of the special-function
+// unit: y = j + f with j = round(y) (adding and subtracting 1.5 * 2^23), 2^f
+// on [-1/2, 1/2] by 1 + c1 f + c2 f^2 + c3 f^3 fitted for minimum relative
+// error (Lawson-weighted least squares; error 1.0e-4, far below the 2^-8 step
+// of a 16-bit P), and j added to the exponent field.  y is clamped at -127;
+// with the constant term exactly 1 the result there is exactly +0 and never
+// negative or NaN above it.
+__device__ __forceinline__ void exp2_poly2(uint64_t y2, float& r0, float& r1) {
+  float y0, y1;
+  f2_unpack(y2, y0, y1);
+  const uint64_t y = f2_pack(fmaxf(y0, -127.f), fmaxf(y1, -127.f));
+  const uint64_t t = f2_add(y, f2_pack(12582912.f, 12582912.f));
+  const uint64_t j = f2_add(t, f2_pack(-12582912.f, -12582912.f));
+  const uint64_t fr = f2_fma(j, f2_pack(-1.f, -1.f), y);  // y - j, exact
+  uint64_t q = f2_fma(f2_pack(0.0550089292f, 0.0550089292f), fr, f2_pack(0.242210954f, 0.242210954f));
+  q = f2_fma(q, fr, f2_pack(0.693282902f, 0.693282902f));
+  q = f2_fma(q, fr, f2_pack(1.f, 1.f));
+  float q0, q1, t0, t1;
+  f2_unpack(q, q0, q1);
+  f2_unpack(t, t0, t1);
+  // t's low mantissa bits hold j (two's complement): shifted, they add j to the exponent
+  r0 = __uint_as_float(__float_as_uint(q0) + (__float_as_uint(t0) << 23));
+  r1 = __uint_as_float(__float_as_uint(q1) + (__float_as_uint(t1) << 23));
+}
+
+#ifndef NF_PF_POLY
+#define NF_PF_POLY 0
+#endif
+// Of every 8 pairs of exponentials, this many go to the polynomial (FMA
+// pipe) and the rest to ex2 (special-function unit, 16 per clock per SM).
+constexpr int kPfPolyPairs = NF_PF_POLY;
+
+// A ring position: stage index and the parity of its current fill.
+struct Ring {
+  int st = 0;
+  uint32_t ph = 0;
+  __device__ void next(int n) {
+    if (++st == n) {
+      st = 0;
+      ph ^= 1;
+    }
+  }
+  __device__ Ring ahead(int k, int n) const {  // the position k fills later
+    Ring r;
+    const int t = st + k;
+    r.st = t % n;
+    r.ph = ph ^ ((uint32_t)(t / n) & 1u);
+    return r;
+  }
+};
+
+// The work items of CTA `worker`: its list in the schedule, or every
 // n_workers-th item.
 struct PfItems {
   int i, end, step;
@@ -120,196 +214,251 @@ struct PfItems {
   }
 };
 
-// Block ids of the eight 16-key blocks of key tile j (keys >= nkeys: 0, not
-// loaded).  The eight loads are independent, so they cost one round trip.
-__device__ __forceinline__ void pf_tile_blocks(const PrefillParams& p, const int* btrow, int j, int nkeys,
-                                               int (&ph)[8]) {
-#pragma unroll
-  for (int b = 0; b < 8; ++b) {
-    const int key = (j * 8 + b) * 16, lb = key / p.bs;
-    ph[b] = (key < nkeys && lb < p.max_blocks) ? __ldg(btrow + lb) : (key < nkeys ? -1 : 0);
+// Shape of one work item: its key tiles, the halves that hold tokens and
+// each half's key tiles (half 0 ends up to 128/G tokens earlier).
+struct PfItem {
+  int4 tl;  // slot, q_row0, ntok, pos0
+  int kvh, nkeys, nkt, n_half, nkt_h[2];
+  __device__ PfItem(const PrefillParams& p, int item) {
+    const int t = item / p.Hkv;
+    kvh = item - t * p.Hkv;
+    tl = __ldg(reinterpret_cast<const int4*>(p.tiles) + t);
+    const int ntok = min(tl.z, 2 * p.TT);
+    nkeys = tl.w + ntok;
+    nkt = (nkeys + 127) >> 7;
+    n_half = ntok > p.TT ? 2 : 1;
+    nkt_h[0] = (tl.w + min(ntok, p.TT) + 127) >> 7;
+    nkt_h[1] = nkt;
   }
+  __device__ bool active(int h, int j) const { return h < n_half && j >= 0 && j < nkt_h[h]; }
+};
+
+// Block id of 16-key block `lane` (< 8) of key tile j (keys >= nkeys: 0,
+// not loaded); lanes 0..7 load theirs together, one round trip per tile.
+__device__ __forceinline__ int pf_block_id(const PrefillParams& p, const int* btrow, int j, int nkeys, int lane) {
+  const int key = (j * 8 + lane) * 16, lb = key / p.bs;
+  if (lane >= 8 || key >= nkeys) return 0;
+  return lb < p.max_blocks ? __ldg(btrow + lb) : -1;
 }
 
-template <int D_, int NP>
-__device__ void pf_producer(const PrefillParams& p, const CUtensorMap* tk, const CUtensorMap* tv, const PfBars& bar,
-                            uint32_t kv_s, int worker, int n_workers) {
-  using C = PfCfg<D_, NP>;
+// Copies of one 128-key K or V tile: lane b < nb copies 16-key block b
+// (both 64-element parts of a head for head_dim 128) after lane 0 has
+// armed the stage's barrier with the tile's bytes.
+template <int D_>
+__device__ __forceinline__ void pf_load_tile(const PrefillParams& p, const CUtensorMap* tm, uint32_t dst0,
+                                             uint32_t full, int blk, int j, int nb, int kvh, uint64_t pol, int lane) {
   constexpr int NDH = D_ / 64;
-  const uint64_t pol = l2_evict_last();  // every query tile of a chunk reads the same keys
-  int st = 0;
-  uint32_t pe = 1;
-  PfItems items(p, worker, n_workers);
-  for (int item; items.next(item);) {
-    const int t = item / p.Hkv, kvh = item - t * p.Hkv;
-    const int4 tl = __ldg(reinterpret_cast<const int4*>(p.tiles) + t);
-    const int nkeys = tl.w + tl.z, nkt = (nkeys + 127) >> 7;
-    const int* btrow = p.bt + (long long)tl.x * p.max_blocks;
-    int cur[8], nxt[8];
-    pf_tile_blocks(p, btrow, 0, nkeys, cur);
-    for (int j = 0; j < nkt; ++j) {
-      if (!mbar_wait(bar.kv_empty(st), pe, p.status)) return;
-      const int nb = min(8, (nkeys - j * 128 + 15) >> 4);
-      const uint32_t full = bar.kv_full(st);
-      mbar_arrive_expect_tx(full, nb * NDH * 2 * 2048);
-      const uint32_t ks = kv_s + st * 2 * C::TILE, vs = ks + C::TILE;
+  if (lane == 0) mbar_arrive_expect_tx(full, nb * NDH * 2048);
+  __syncwarp();
+  if (lane < nb) {
+    const int off = ((j * 8 + lane) * 16) % p.bs;
+    int phys = blk;
+    if (phys < 0 || phys >= p.num_blocks) {
+      atomicOr(p.status, NF_STATUS_BAD_BLOCK);
+      phys = 0;
+    }
 #pragma unroll
-      for (int b = 0; b < 8; ++b) {
-        if (b >= nb) break;
-        const int off = ((j * 8 + b) * 16) % p.bs;
-        int phys = cur[b];
-        if (phys < 0 || phys >= p.num_blocks) {
-          atomicOr(p.status, NF_STATUS_BAD_BLOCK);
-          phys = 0;
-        }
-#pragma unroll
-        for (int dh = 0; dh < NDH; ++dh) {
-          const uint32_t dst = dh * 128 * 128 + b * 2048;
-          if constexpr (D_ == 64) {
-            tma_load_4d(ks + dst, tk, 0, kvh, off, phys, full, pol);
-            tma_load_4d(vs + dst, tv, 0, kvh, off, phys, full, pol);
-          } else {
-            tma_load_5d(ks + dst, tk, 0, dh, kvh, off, phys, full, pol);
-            tma_load_5d(vs + dst, tv, 0, dh, kvh, off, phys, full, pol);
-          }
-        }
-      }
-      if (j + 1 < nkt) {
-        pf_tile_blocks(p, btrow, j + 1, nkeys, nxt);
-#pragma unroll
-        for (int b = 0; b < 8; ++b) cur[b] = nxt[b];
-      }
-      if (++st == C::STAGES) {
-        st = 0;
-        pe ^= 1;
-      }
+    for (int dh = 0; dh < NDH; ++dh) {
+      const uint32_t dst = dst0 + dh * 128 * 128 + lane * 2048;
+      if constexpr (D_ == 64)
+        tma_load_4d(dst, tm, 0, kvh, off, phys, full, pol);
+      else
+        tma_load_5d(dst, tm, 0, dh, kvh, off, phys, full, pol);
     }
   }
 }
 
-template <int D_, int NP>
-__device__ void pf_mma(const PrefillParams& p, const PfBars& bar, uint32_t tmem, uint32_t q_s, uint32_t p_s,
-                       uint32_t kv_s, bool bf, int worker, int n_workers) {
-  using C = PfCfg<D_, NP>;
+// The producer warp: every lane runs the loop (waits included), lanes 0..7
+// load block ids and issue the tensor copies.
+template <int D_>
+__device__ void pf_producer(const PrefillParams& p, const CUtensorMap* tk, const CUtensorMap* tv, const PfBars& bar,
+                            uint32_t k_s, uint32_t v_s, int worker, int n_workers) {
+  using C = PfCfg<D_>;
+  const int lane = threadIdx.x & 31;
+  const uint64_t pol = l2_evict_last();  // every query tile of a chunk reads the same keys
+  Ring kr, vr;
+  PfItems items(p, worker, n_workers);
+  for (int it; items.next(it);) {
+    const PfItem w(p, it);
+    const int* btrow = p.bt + (long long)w.tl.x * p.max_blocks;
+    int cur = pf_block_id(p, btrow, 0, w.nkeys, lane);
+    for (int j = 0; j < w.nkt; ++j) {
+      const int nb = min(8, (w.nkeys - j * 128 + 15) >> 4);
+      if (!mbar_wait(bar.k_empty(kr.st), kr.ph ^ 1, p.status)) return;
+      pf_load_tile<D_>(p, tk, k_s + kr.st * C::TILE, bar.k_full(kr.st), cur, j, nb, w.kvh, pol, lane);
+      kr.next(C::KST);
+      if (!mbar_wait(bar.v_empty(vr.st), vr.ph ^ 1, p.status)) return;
+      pf_load_tile<D_>(p, tv, v_s + vr.st * C::TILE, bar.v_full(vr.st), cur, j, nb, w.kvh, pol, lane);
+      vr.next(C::VST);
+      if (j + 1 < w.nkt) cur = pf_block_id(p, btrow, j + 1, w.nkeys, lane);
+    }
+  }
+}
+
+// The MMA warp: every lane runs the loop and its waits; lane 0 issues the
+// MMAs and the commits that track them.
+template <int D_>
+__device__ void pf_mma(const PrefillParams& p, const PfBars& bar, uint32_t tmem, uint32_t q_s, uint32_t k_s,
+                       uint32_t v_s, bool bf, int worker, int n_workers) {
+  using C = PfCfg<D_>;
+  const bool leader = (threadIdx.x & 31) == 0;
   constexpr uint32_t REG = 128 * 128;  // one 64-element region of a 128-row operand
   const uint32_t idesc_s = umma_idesc_f16(bf, 128, 128, false, false);
   const uint32_t idesc_o = umma_idesc_f16(bf, 128, D_, false, true);
-  int st = 0, tc = 0, npv = 0, nq = 0;
-  uint32_t pf = 0;
-  auto issue_pv = [&](int stage, bool first) -> bool {
-    if (!mbar_wait(bar.p_full(), npv & 1, p.status)) return false;
-    ++npv;
-    tc_fence_after();
-    const uint32_t vs = kv_s + stage * 2 * C::TILE + C::TILE;
-#pragma unroll
-    for (int kk = 0; kk < 8; ++kk) {
-      const uint64_t a = umma_sdesc_sw128(p_s + (kk >> 2) * REG + (kk & 3) * 32, 16, 1024);
-      const uint64_t b = umma_sdesc_sw128(vs + kk * 16 * 128, REG, 1024);
-      umma_f16_ss(tmem + C::O_COL, a, b, idesc_o, (first && kk == 0) ? 0u : 1u);
-    }
-    umma_commit(bar.o_done());
-    umma_commit(bar.kv_empty(stage));
+  Ring kr, vr;
+  int n_s[2] = {0, 0}, n_p[2] = {0, 0}, n_q[2] = {0, 0};
+  auto wait_p = [&](int h) -> bool {
+    if (!mbar_wait(bar.p_full(h), n_p[h] & 1, p.status)) return false;
+    ++n_p[h];
     return true;
   };
-  PfItems items(p, worker, n_workers);
-  for (int item; items.next(item);) {
-    const int t = item / p.Hkv;
-    const int4 tl = __ldg(reinterpret_cast<const int4*>(p.tiles) + t);
-    const int nkt = (tl.w + tl.z + 127) >> 7;
-    if (!mbar_wait(bar.q_full(), nq & 1, p.status)) return;
-    ++nq;
+  // O_h += P_h V of the tile in V stage vst (first: overwrite O_h)
+  auto issue_pv = [&](int h, int vst, bool first) {
     tc_fence_after();
-    int prev = -1;
-    for (int j = 0; j < nkt; ++j) {
-      if (!mbar_wait(bar.kv_full(st), pf, p.status)) return;
-      const int b = C::NSB == 2 ? (tc & 1) : 0;
-      const int use = C::NSB == 2 ? (tc >> 1) : tc;  // uses of this S buffer so far
-      if (!mbar_wait(bar.s_empty(b), (use & 1) ^ 1, p.status)) return;
-      ++tc;
-      tc_fence_after();
-      const uint32_t ks = kv_s + st * 2 * C::TILE;
+    if (!leader) return;
+    const uint32_t vs = v_s + vst * C::TILE;
 #pragma unroll
-      for (int k = 0; k < D_ / 16; ++k) {
-        const uint64_t a = umma_sdesc_sw128(q_s + (k >> 2) * REG + (k & 3) * 32, 16, 1024);
-        const uint64_t bd = umma_sdesc_sw128(ks + (k >> 2) * REG + (k & 3) * 32, 16, 1024);
-        umma_f16_ss(tmem + b * 128, a, bd, idesc_s, k > 0 ? 1u : 0u);
-      }
-      umma_commit(bar.s_full(b));
-      if (prev >= 0 && !issue_pv(prev, j == 1)) return;
-      prev = st;
-      if (++st == C::STAGES) {
-        st = 0;
-        pf ^= 1;
-      }
+    for (int kk = 0; kk < 8; ++kk) {
+      const uint64_t b = umma_sdesc_sw128(vs + kk * 16 * 128, REG, 1024);
+      umma_f16_ts(tmem + C::o_col(h), tmem + C::p_col(h) + kk * 8, b, idesc_o, (first && kk == 0) ? 0u : 1u);
     }
-    if (!issue_pv(prev, nkt == 1)) return;
+    umma_commit(bar.o_done(h));
+  };
+  auto issue_s = [&](int h, int kst) {
+    if (!leader) return;
+    const uint32_t ks = k_s + kst * C::TILE, qs = q_s + h * C::TILE;
+#pragma unroll
+    for (int k = 0; k < D_ / 16; ++k) {
+      const uint64_t a = umma_sdesc_sw128(qs + (k >> 2) * REG + (k & 3) * 32, 16, 1024);
+      const uint64_t b = umma_sdesc_sw128(ks + (k >> 2) * REG + (k & 3) * 32, 16, 1024);
+      umma_f16_ss(tmem + C::s_col(h), a, b, idesc_s, k > 0 ? 1u : 0u);
+    }
+    umma_commit(bar.s_full(h));
+  };
+  PfItems items(p, worker, n_workers);
+  for (int it; items.next(it);) {
+    const PfItem w(p, it);
+    int vprev = -1;  // V stage of tile j-1
+    for (int j = 0; j < w.nkt; ++j) {
+      if (!mbar_wait(bar.k_full(kr.st), kr.ph, p.status)) return;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        if (C::P_ALIAS && w.active(h, j - 1)) {
+          // P_h of tile j-1 sits in S_h: consume it before S_h is rewritten
+          if (!wait_p(h)) return;
+          issue_pv(h, vprev, j == 1);
+        }
+        if (!w.active(h, j)) continue;
+        if (j == 0) {
+          if (!mbar_wait(bar.q_full(h), n_q[h] & 1, p.status)) return;
+          ++n_q[h];
+        }
+        if (!C::P_ALIAS) {
+          if (!mbar_wait(bar.s_free(h), (n_s[h] & 1) ^ 1, p.status)) return;
+        }
+        ++n_s[h];
+        tc_fence_after();
+        issue_s(h, kr.st);
+      }
+      if (leader) umma_commit(bar.k_empty(kr.st));
+      kr.next(C::KST);
+      if (j > 0) {
+        if (!C::P_ALIAS) {
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            if (!w.active(h, j - 1)) continue;
+            if (!wait_p(h)) return;
+            issue_pv(h, vprev, j == 1);
+          }
+        }
+        if (leader) umma_commit(bar.v_empty(vprev));
+      }
+      if (!mbar_wait(bar.v_full(vr.st), vr.ph, p.status)) return;
+      vprev = vr.st;
+      vr.next(C::VST);
+    }
+    // the last tile: rows of V past the last key are zeroed by the last
+    // half's warpgroup, so both halves' P must be in before either P V
+    const int jl = w.nkt - 1;
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+      if (w.active(h, jl) && !wait_p(h)) return;
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+      if (w.active(h, jl)) issue_pv(h, vprev, jl == 0);
+    if (leader) umma_commit(bar.v_empty(vprev));
   }
 }
 
-template <typename T, int D_, int NP>
-__device__ void pf_softmax(const PrefillParams& p, const PfBars& bar, uint32_t tmem, uint32_t q_s, uint32_t p_s,
-                           uint32_t kv_s, int worker, int n_workers) {
-  using C = PfCfg<D_, NP>;
+template <typename T, int D_>
+__device__ void pf_softmax(const PrefillParams& p, const PfBars& bar, uint32_t tmem, uint32_t q_s, uint32_t v_s,
+                           int h, int worker, int n_workers) {
+  using C = PfCfg<D_>;
   constexpr int NDH = D_ / 64;
   constexpr uint32_t REG = 128 * 128;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int quad = warp & 3, row = quad * 32 + lane;
+  const int quad = warp & 3, row = quad * 32 + lane;  // tensor-memory lanes of this warp: quad*32..
   const uint32_t lane_addr = (uint32_t)(quad * 32) << 16;
+  const uint32_t s_addr = tmem + lane_addr + C::s_col(h), o_addr = tmem + lane_addr + C::o_col(h);
+  const uint32_t p_addr = tmem + lane_addr + C::p_col(h);
+  const uint32_t qh_s = q_s + h * C::TILE;
   const int G = p.G;
-  int tc = 0, nod = 0, st = 0;
+  int n_s = 0, n_o = 0;
+  Ring vr;  // V ring position of this CTA's current tile (every item advances it)
   PfItems items(p, worker, n_workers);
-  for (int item; items.next(item);) {
-    const int t = item / p.Hkv, kvh = item - t * p.Hkv;
-    const int4 tl = __ldg(reinterpret_cast<const int4*>(p.tiles) + t);
-    const int nkeys = tl.w + tl.z, nkt = (nkeys + 127) >> 7;
-    const int tok = row / G, h = row - tok * G;
-    const bool valid = tok < tl.z;
-    const int qpos = tl.w + tok;
+  for (int it; items.next(it);) {
+    const PfItem w(p, it);
+    if (h == 0 && w.tl.z > 2 * p.TT && threadIdx.x == 128) atomicOr(p.status, NF_STATUS_BAD_TILE);
+    const Ring vlast = vr.ahead(w.nkt - 1, C::VST);  // V stage of the item's last tile
+    vr = vr.ahead(w.nkt, C::VST);
+    if (h >= w.n_half) continue;
+    const int nkt = w.nkt_h[h];
+    const int tok = h * p.TT + row / G, hd = row % G;
+    const bool valid = tok < min(w.tl.z, 2 * p.TT);
+    const int qpos = w.tl.w + tok;
     // this row of Q into the swizzled A operand
     {
-      const char* src = p.q + ((long long)(tl.y + tok) * p.q_stride + (long long)(kvh * G + h) * D_) * 2;
+      const char* src = p.q + ((long long)(w.tl.y + tok) * p.q_stride + (long long)(w.kvh * G + hd) * D_) * 2;
 #pragma unroll
       for (int c = 0; c < NDH * 8; ++c) {
         uint4 v = make_uint4(0u, 0u, 0u, 0u);
         if (valid) v = __ldg(reinterpret_cast<const uint4*>(src) + c);
-        const uint32_t a = q_s + (c >> 3) * REG + row * 128 + (((c & 7) ^ (row & 7)) << 4);
+        const uint32_t a = qh_s + (c >> 3) * REG + row * 128 + (((c & 7) ^ (row & 7)) << 4);
         asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
                      : "memory");
       }
     }
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     __syncwarp();
-    if (lane == 0) mbar_arrive(bar.q_full());
+    if (lane == 0) mbar_arrive(bar.q_full(h));
     float m = kPfNegInf, l = 0.f;
     for (int j = 0; j < nkt; ++j) {
-      const int b = C::NSB == 2 ? (tc & 1) : 0;
-      const int use = C::NSB == 2 ? (tc >> 1) : tc;
-      if (!mbar_wait(bar.s_full(b), use & 1, p.status)) return;
-      ++tc;
+      if (!mbar_wait(bar.s_full(h), n_s & 1, p.status)) return;
+      ++n_s;
       tc_fence_after();
-      const uint32_t s_addr = tmem + lane_addr + b * 128;
+      uint32_t x[128];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld32(s_addr + c * 32, *reinterpret_cast<uint32_t(*)[32]>(x + 32 * c));
+      tmem_wait_ld();
+      if (!C::P_ALIAS) {  // S_h is in registers: the next S_h may be computed
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar.s_free(h));
+      }
       const int k0 = j * 128;
       const int lim = valid ? qpos - k0 : -1;  // columns <= lim are visible (key k <= qpos)
-      const bool full = __all_sync(0xffffffffu, lim >= 127);  // no row of the warp crosses the diagonal
-      // pass 1: tile max of the raw scores, 64 columns at a time, 8 chains;
-      // the causal mask only where some row of the warp crosses the diagonal
+      if (!__all_sync(0xffffffffu, lim >= 127)) {  // some row of the warp crosses the diagonal
+#pragma unroll
+        for (int i = 0; i < 128; ++i)
+          if (i > lim) x[i] = __float_as_uint(kPfNegInf);
+      }
       float acc[8];
 #pragma unroll
-      for (int a = 0; a < 8; ++a) acc[a] = kPfNegInf;
+      for (int a = 0; a < 8; ++a) acc[a] = fmaxf(__uint_as_float(x[a]), __uint_as_float(x[a + 8]));
 #pragma unroll
-      for (int h2 = 0; h2 < 2; ++h2) {
-        uint32_t x[64];
-        tmem_ld32(s_addr + h2 * 64, *reinterpret_cast<uint32_t(*)[32]>(x));
-        tmem_ld32(s_addr + h2 * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(x + 32));
-        tmem_wait_ld();
-        if (!full) {
+      for (int i = 16; i < 128; i += 16)
 #pragma unroll
-          for (int i = 0; i < 64; ++i)
-            if (h2 * 64 + i > lim) x[i] = __float_as_uint(kPfNegInf);
-        }
-#pragma unroll
-        for (int i = 0; i < 64; ++i) acc[i & 7] = fmaxf(acc[i & 7], __uint_as_float(x[i]));
-      }
+        for (int a = 0; a < 8; ++a) acc[a] = fmax3(acc[a], __uint_as_float(x[i + a]), __uint_as_float(x[i + 8 + a]));
       const float mt = fmaxf(fmaxf(fmaxf(acc[0], acc[1]), fmaxf(acc[2], acc[3])),
                              fmaxf(fmaxf(acc[4], acc[5]), fmaxf(acc[6], acc[7]))) * p.scale_log2;
       // lazy rescaling: the reference max moves (O and l rescaled) only when
@@ -318,177 +467,155 @@ __device__ void pf_softmax(const PrefillParams& p, const PfBars& bar, uint32_t t
       const float mn = grow ? mt : m;
       const float alpha = grow ? ex2(m - mn) : 1.f;  // 0 on the first visible tile
       const float nbase = mn == kPfNegInf ? 0.f : -mn;
-      // P and V of the previous tile must be consumed before P is rewritten:
-      // wait for O += P V of tile j-1 (and rescale O if a row's max moved)
+      // exponents (packed pairs: scale and offset in one fp32x2 FMA), row
+      // sum, P packed in pairs into the low half of x
+      const uint64_t sc2 = f2_pack(p.scale_log2, p.scale_log2), nb2 = f2_pack(nbase, nbase);
+      uint64_t sum2[4];
+#pragma unroll
+      for (int a = 0; a < 4; ++a) sum2[a] = 0ull;
+#pragma unroll
+      for (int i = 0; i < 128; i += 2) {
+        const uint64_t y2 = f2_fma(f2_pack(__uint_as_float(x[i]), __uint_as_float(x[i + 1])), sc2, nb2);
+        float p0, p1;
+        if (((i >> 1) & 7) < kPfPolyPairs) {
+          exp2_poly2(y2, p0, p1);
+        } else {
+          float y0, y1;
+          f2_unpack(y2, y0, y1);
+          p0 = ex2(y0);
+          p1 = ex2(y1);
+        }
+        sum2[(i >> 1) & 3] = f2_add(sum2[(i >> 1) & 3], f2_pack(p0, p1));
+        x[i >> 1] = pack2<T>(p0, p1);
+      }
+      // O_h += P_h V of tile j-1 must be done before P_h is rewritten and
+      // before O_h is rescaled (when a row's max moved)
       if (j > 0) {
-        if (!mbar_wait(bar.o_done(), nod & 1, p.status)) return;
-        ++nod;
+        if (!mbar_wait(bar.o_done(h), n_o & 1, p.status)) return;
+        ++n_o;
         tc_fence_after();
-        if (__any_sync(0xffffffffu, alpha != 1.f)) {
+      }
+      tmem_st32(p_addr, *reinterpret_cast<uint32_t(*)[32]>(x));
+      tmem_st32(p_addr + 32, *reinterpret_cast<uint32_t(*)[32]>(x + 32));
+      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll
-          for (int c = 0; c < D_ / 32; ++c) {
-            uint32_t o[32];
-            tmem_ld32(tmem + lane_addr + C::O_COL + c * 32, o);
-            tmem_wait_ld();
+        for (int c = 0; c < D_ / 32; ++c) {
+          uint32_t o[32];
+          tmem_ld32(o_addr + c * 32, o);
+          tmem_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-            tmem_st32(tmem + lane_addr + C::O_COL + c * 32, o);
-          }
-          tmem_wait_st();
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          tmem_st32(o_addr + c * 32, o);
         }
       }
-      // pass 2: exponents, row sum, P (16 chunks of 8 keys; keys 64r.. in region r)
       float sa[8];
 #pragma unroll
-      for (int a = 0; a < 8; ++a) sa[a] = 0.f;
-#pragma unroll
-      for (int h2 = 0; h2 < 2; ++h2) {
-        uint32_t x[64];
-        tmem_ld32(s_addr + h2 * 64, *reinterpret_cast<uint32_t(*)[32]>(x));
-        tmem_ld32(s_addr + h2 * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(x + 32));
-        tmem_wait_ld();
-        if (h2 == 1) {  // S fully read: the MMA may overwrite this buffer
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(bar.s_empty(b));
-        }
-        if (!full) {
-#pragma unroll
-          for (int i = 0; i < 64; ++i)
-            if (h2 * 64 + i > lim) x[i] = __float_as_uint(kPfNegInf);
-        }
-#pragma unroll
-        for (int i = 0; i < 64; i += 2) {
-          const float p0 = ex2(fmaf(__uint_as_float(x[i]), p.scale_log2, nbase));
-          const float p1 = ex2(fmaf(__uint_as_float(x[i + 1]), p.scale_log2, nbase));
-          sa[(i >> 1) & 7] += p0 + p1;
-          x[i >> 1] = pack2<T>(p0, p1);  // packed P reuses the low half of x
-        }
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          const uint32_t a = p_s + h2 * REG + row * 128 + ((c ^ (row & 7)) << 4);
-          asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(x[4 * c]), "r"(x[4 * c + 1]),
-                       "r"(x[4 * c + 2]), "r"(x[4 * c + 3])
-                       : "memory");
-        }
-      }
+      for (int a = 0; a < 4; ++a) f2_unpack(sum2[a], sa[2 * a], sa[2 * a + 1]);
       l = l * alpha + (((sa[0] + sa[1]) + (sa[2] + sa[3])) + ((sa[4] + sa[5]) + (sa[6] + sa[7])));
       m = mn;
-      if (j == nkt - 1 && k0 + row >= nkeys) {
-        // V rows past the tile's last visible key (their P is 0) may hold
-        // anything: zero them so that 0 * NaN cannot reach O
-        const uint32_t vs = kv_s + st * 2 * C::TILE + C::TILE;
+      if (h == w.n_half - 1 && j == nkt - 1 && k0 + row >= w.nkeys) {
+        // V rows past the item's last key (their P is 0) may hold anything:
+        // zero them so that 0 * NaN cannot reach O
+        if (!mbar_wait(bar.v_full(vlast.st), vlast.ph, p.status)) return;
+        const uint32_t vs = v_s + vlast.st * C::TILE;
 #pragma unroll
         for (int dh = 0; dh < NDH; ++dh)
 #pragma unroll
           for (int c = 0; c < 8; ++c)
             asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(vs + dh * REG + row * 128 + c * 16), "r"(0)
                          : "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       }
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar.p_full());
-      if (++st == C::STAGES) st = 0;
+      if (lane == 0) mbar_arrive(bar.p_full(h));
     }
-    // epilogue: O / l for the valid rows
-    if (!mbar_wait(bar.o_done(), nod & 1, p.status)) return;
-    ++nod;
+    // epilogue: O_h / l for the valid rows
+    if (!mbar_wait(bar.o_done(h), n_o & 1, p.status)) return;
+    ++n_o;
     tc_fence_after();
     const float inv = l > 0.f ? 1.f / l : 0.f;
-    T* dst = reinterpret_cast<T*>(p.out) + (long long)(tl.y + tok) * p.out_stride + (long long)(kvh * G + h) * D_;
+    T* dst = reinterpret_cast<T*>(p.out) + (long long)(w.tl.y + tok) * p.out_stride + (long long)(w.kvh * G + hd) * D_;
 #pragma unroll
     for (int c = 0; c < D_ / 32; ++c) {
       uint32_t o[32];
-      tmem_ld32(tmem + lane_addr + C::O_COL + c * 32, o);
+      tmem_ld32(o_addr + c * 32, o);
       tmem_wait_ld();
       if (valid) {
-        uint32_t w[16];
+        uint32_t wv[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i)
-          w[i] = pack2<T>(__uint_as_float(o[2 * i]) * inv, __uint_as_float(o[2 * i + 1]) * inv);
+          wv[i] = pack2<T>(__uint_as_float(o[2 * i]) * inv, __uint_as_float(o[2 * i + 1]) * inv);
         uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) d4[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+        for (int i = 0; i < 4; ++i) d4[i] = make_uint4(wv[4 * i], wv[4 * i + 1], wv[4 * i + 2], wv[4 * i + 3]);
       }
     }
     tc_fence_before();
   }
 }
 
-template <typename T, int D_, int NP>
-__global__ void __launch_bounds__(PfCfg<D_, NP>::THREADS, 1)
+template <typename T, int D_>
+__global__ void __launch_bounds__(PfCfg<D_>::THREADS, 1)
     prefill_attention_kernel(const PrefillParams p, const __grid_constant__ CUtensorMap tk,
                              const __grid_constant__ CUtensorMap tv) {
-  using C = PfCfg<D_, NP>;
+  using C = PfCfg<D_>;
   extern __shared__ unsigned char smem_raw[];
   unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t hdr = smem_u32(base);
+  const PfBars bar(hdr);
   const int warp = threadIdx.x >> 5;
   if (threadIdx.x == 0) {
-    for (int pi = 0; pi < NP; ++pi) {
-      const PfBars bar(hdr, pi);
-      for (int s = 0; s < C::STAGES; ++s) {
-        mbar_init(bar.kv_full(s), 1);
-        mbar_init(bar.kv_empty(s), 1);
-      }
-      for (int b = 0; b < C::NSB; ++b) {
-        mbar_init(bar.s_full(b), 1);
-        mbar_init(bar.s_empty(b), 4);
-      }
-      mbar_init(bar.p_full(), 4);
-      mbar_init(bar.o_done(), 1);
-      mbar_init(bar.q_full(), 4);
+    for (int s = 0; s < C::KST; ++s) {
+      mbar_init(bar.k_full(s), 1);
+      mbar_init(bar.k_empty(s), 1);
+    }
+    for (int s = 0; s < C::VST; ++s) {
+      mbar_init(bar.v_full(s), 1);
+      mbar_init(bar.v_empty(s), 1);
+    }
+    for (int h = 0; h < 2; ++h) {
+      mbar_init(bar.s_full(h), 1);
+      mbar_init(bar.s_free(h), 4);
+      mbar_init(bar.p_full(h), 4);
+      mbar_init(bar.o_done(h), 1);
+      mbar_init(bar.q_full(h), 4);
     }
     fence_mbar_init();
   }
-  if (warp == 2) tmem_alloc(hdr + kPfTmemPtr, kTmemCols);
+  if (warp == 1) tmem_alloc(hdr + kPfTmemPtr, kTmemCols);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem0 = *reinterpret_cast<volatile uint32_t*>(base + kPfTmemPtr);
-  const int n_workers = gridDim.x * NP;
-  // role and pipeline of this warp: producers 0..NP-1, MMA 2..2+NP-1, softmax warpgroups from warp 4
-  int pi = -1, role = -1;
-  if (warp < NP) {
-    pi = warp;
-    role = 0;
-  } else if (warp >= 2 && warp < 2 + NP) {
-    pi = warp - 2;
-    role = 1;
-  } else if (warp >= 4) {
-    pi = (warp - 4) >> 2;
-    role = 2;
-  }
-  if (role >= 0) {
-    const PfBars bar(hdr, pi);
-    const uint32_t q_s = hdr + 1024 + pi * C::PIPE, p_s = q_s + C::TILE, kv_s = p_s + C::PB;
-    const uint32_t tmem = tmem0 + pi * C::TM_PIPE;
-    const int worker = blockIdx.x * NP + pi;
-    if (role == 0) {
-      if ((threadIdx.x & 31) == 0) pf_producer<D_, NP>(p, &tk, &tv, bar, kv_s, worker, n_workers);
-    } else if (role == 1) {
-      if ((threadIdx.x & 31) == 0)
-        pf_mma<D_, NP>(p, bar, tmem, q_s, p_s, kv_s, std::is_same<T, __nv_bfloat16>::value, worker, n_workers);
-    } else {
-      pf_softmax<T, D_, NP>(p, bar, tmem, q_s, p_s, kv_s, worker, n_workers);
-    }
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(base + kPfTmemPtr);
+  const uint32_t q_s = hdr + C::Q_OFF, k_s = hdr + C::K_OFF, v_s = hdr + C::V_OFF;
+  const int worker = blockIdx.x, n_workers = gridDim.x;
+  static_assert(C::REGS_CTRL * 128 + C::REGS_SOFTMAX * 256 <= 168 * C::THREADS, "register split exceeds the launch");
+  if (warp < 4) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(C::REGS_CTRL));
+    if (warp == 0)
+      pf_producer<D_>(p, &tk, &tv, bar, k_s, v_s, worker, n_workers);
+    else if (warp == 1)
+      pf_mma<D_>(p, bar, tmem, q_s, k_s, v_s, std::is_same<T, __nv_bfloat16>::value, worker, n_workers);
+  } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(C::REGS_SOFTMAX));
+    pf_softmax<T, D_>(p, bar, tmem, q_s, v_s, (warp - 4) >> 2, worker, n_workers);
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 2) tmem_dealloc(tmem0, kTmemCols);
+  if (warp == 1) tmem_dealloc(tmem, kTmemCols);
 }
 
 template <typename T, int D_>
 static int launch_prefill(const PrefillParams& p, const CUtensorMap& tk, const CUtensorMap& tv, int n_items,
                           cudaStream_t st) {
-  constexpr int NP = D_ == 64 ? 2 : 1;
-  using C = PfCfg<D_, NP>;
-  auto kern = prefill_attention_kernel<T, D_, NP>;
+  using C = PfCfg<D_>;
+  auto kern = prefill_attention_kernel<T, D_>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
   if (e != cudaSuccess) return fail(NF_ECUDA, "nf_prefill_attention: smem attribute: %s", cudaGetErrorString(e));
-  long long grid = p.sched ? (p.n_lists + NP - 1) / NP : ((long long)n_items + NP - 1) / NP;
+  long long grid = p.sched ? p.n_lists : n_items;
   if (grid > sm_count()) grid = sm_count();
   kern<<<(int)grid, C::THREADS, C::SMEM, st>>>(p, tk, tv);
   return check_launch("nf_prefill_attention");
@@ -496,7 +623,7 @@ static int launch_prefill(const PrefillParams& p, const CUtensorMap& tk, const C
 
 }  // namespace nf
 
-extern "C" int nf_prefill_pipelines(int32_t head_dim) { return head_dim == 64 ? 2 : 1; }
+extern "C" int nf_prefill_tile_rows(void) { return nf::kPfRows; }
 
 extern "C" int nf_prefill_attention(void* out, int64_t out_row_stride, const void* q, int64_t q_row_stride,
                                     const void* k_pool, const void* v_pool, int32_t dtype, int32_t num_q_heads,
@@ -521,9 +648,8 @@ extern "C" int nf_prefill_attention(void* out, int64_t out_row_stride, const voi
   if (n_tiles == 0) return ok();
   if (!out || !q || !k_pool || !v_pool || !block_tables || !tiles || !status)
     return fail(NF_EINVAL, "nf_prefill_attention: null pointer argument");
-  const int np = nf_prefill_pipelines(head_dim);
-  if (schedule && (n_lists <= 0 || n_lists > sm_count() * np))
-    return fail(NF_EINVAL, "nf_prefill_attention: a schedule needs 1..%d lists (got %d)", sm_count() * np, n_lists);
+  if (schedule && (n_lists <= 0 || n_lists > sm_count()))
+    return fail(NF_EINVAL, "nf_prefill_attention: a schedule needs 1..%d lists (got %d)", sm_count(), n_lists);
   auto al = [](const void* ptr, size_t a) { return (reinterpret_cast<uintptr_t>(ptr) % a) == 0; };
   if (!al(q, 16) || !al(out, 16) || (q_row_stride * 2) % 16 || (out_row_stride * 2) % 16 || !al(tiles, 16) ||
       !al(k_pool, 16) || !al(v_pool, 16))
@@ -540,6 +666,7 @@ extern "C" int nf_prefill_attention(void* out, int64_t out_row_stride, const voi
   p.Hq = num_q_heads;
   p.Hkv = num_kv_heads;
   p.G = G;
+  p.TT = 128 / G;
   p.bs = block_size;
   p.num_blocks = num_blocks;
   p.bt = block_tables;

@@ -18,6 +18,8 @@ __device__ __forceinline__ uint32_t sw128_off(int row, int col, int rows) {
 
 // mode 0: C[m][n] = sum_k A[m][k] B[n][k]  (B K-major, as K in S = Q K^T)
 // mode 1: C[m][n] = sum_k A[m][k] B[k][n]  (B MN-major, as V in O = P V)
+// mode 2: as mode 1 with A in tensor memory (row m in lane m, columns 128..),
+//         written there by tcgen05.st (P in O = P V)
 __global__ void __launch_bounds__(128) umma_selftest_kernel(const __nv_bfloat16* A, const __nv_bfloat16* B,
                                                              float* C, int N, int K, int mode, int* status) {
   extern __shared__ unsigned char smem_raw[];
@@ -52,9 +54,31 @@ __global__ void __launch_bounds__(128) umma_selftest_kernel(const __nv_bfloat16*
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = tmem_base;
+  if (mode == 2) {
+    // row `tid` of A, packed in pairs, into columns 128 .. 128 + K/2 of lane `tid`
+    const uint32_t lane_addr = (uint32_t)(warp * 32) << 16;
+    for (int c0 = 0; c0 < K / 2; c0 += 32) {
+      uint32_t r[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const __nv_bfloat162 v = __halves2bfloat162(A[tid * K + 2 * (c0 + j)], A[tid * K + 2 * (c0 + j) + 1]);
+        r[j] = *reinterpret_cast<const uint32_t*>(&v);
+      }
+      tmem_st32(tbase + lane_addr + 128 + c0, r);
+    }
+    tmem_wait_st();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+  }
   if (tid == 0) {
-    const uint32_t idesc = umma_idesc_f16(true, 128, N, false, mode == 1);
+    const uint32_t idesc = umma_idesc_f16(true, 128, N, false, mode != 0);
     for (int ks = 0; ks < K / 16; ++ks) {
+      if (mode == 2) {
+        umma_f16_ts(tbase, tbase + 128 + ks * 8, umma_sdesc_sw128(smem_u32(Bs) + ks * 16 * 128, K * 128, 1024),
+                    idesc, ks > 0);
+        continue;
+      }
       const uint32_t a = smem_u32(As) + (ks >> 2) * 128 * 128 + (ks & 3) * 32;
       uint64_t bd;
       if (mode == 0) {
@@ -92,8 +116,8 @@ extern "C" int nf_selftest_umma(const void* A, const void* B, float* C, int32_t 
                                 int32_t* status, void* stream) {
   using namespace nf;
   if (!A || !B || !C || !status) return fail(NF_EINVAL, "nf_selftest_umma: null pointer");
-  if ((N != 64 && N != 128) || (K != 64 && K != 128) || (mode != 0 && mode != 1))
-    return fail(NF_EINVAL, "nf_selftest_umma: N, K in {64, 128}, mode 0 or 1");
+  if ((N != 64 && N != 128) || (K != 64 && K != 128) || mode < 0 || mode > 2)
+    return fail(NF_EINVAL, "nf_selftest_umma: N, K in {64, 128}, mode 0, 1 or 2");
   const int smem = 1024 + 128 * K * 2 + N * K * 2;
   cudaError_t e = cudaFuncSetAttribute(umma_selftest_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return fail(NF_ECUDA, "nf_selftest_umma: %s", cudaGetErrorString(e));

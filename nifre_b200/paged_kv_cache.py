@@ -81,7 +81,7 @@ def seq_unit_sizes(seq_keys: np.ndarray, split: int, sms: int, fine_div: int = 4
 
 def _prefill_schedule(tiles, kv_heads: int, sms: int) -> np.ndarray:
     """Per-worker lists of the prefill kernel's (tile, KV head) items, longest first
-    (``sms``: the number of workers, the kernel's pipelines on all SMs).
+    (``sms``: the number of workers, one CTA per SM).
 
     An item costs its 128-key tiles plus one (query load and epilogue); items
     go in decreasing cost to the least-loaded CTA (longest processing time
@@ -350,14 +350,14 @@ class PagedKVCache:
         max_units = max(1, n_units)
         tiles = []
         if routed.any():
-            tt = 128 // (q_heads // self.n_heads)  # query tokens per 128-row tile
+            tt = _lib.load().nf_prefill_tile_rows() // (q_heads // self.n_heads)  # query tokens per work item
             for i in np.flatnonzero(routed).tolist():
                 n, c, r0 = int(q_lens[i]), int(ctx[i]), int(q_starts[i])
                 for t0 in reversed(range(0, n, tt)):  # most keys first
                     tiles.append((int(slots[i]), r0 + t0, min(tt, n - t0), c + t0))
 
         n_tiles = len(tiles)
-        workers = self.sm_count * _lib.load().nf_prefill_pipelines(self.head_dim)  # independent pipelines
+        workers = self.sm_count  # one persistent CTA per SM
         sched = _prefill_schedule(tiles, self.n_heads, workers) if n_tiles else np.zeros(0, np.int32)
         n_ctas = int(min(workers, n_tiles * self.n_heads)) if n_tiles else 0  # number of lists
         off_tiles = _align4(S * 5 + P * 3)
@@ -497,7 +497,7 @@ class PagedKVCache:
         if st:
             self.status.zero_()
             raise _lib.NifreError(f"device status {st:#x} (bad block={st & 1}, unit overflow={st >> 1 & 1}, "
-                                  f"wait timeout={st >> 2 & 1}, bad slot={st >> 3 & 1})")
+                                  f"wait timeout={st >> 2 & 1}, bad slot={st >> 3 & 1}, bad tile={st >> 4 & 1})")
 
     def device_block_table(self, slot: int, n: int | None = None) -> list[int]:
         row = self.bt_dev[slot].tolist()

@@ -6,7 +6,7 @@ import torch
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("mode", [0, 1])
+@pytest.mark.parametrize("mode", [0, 1, 2])
 @pytest.mark.parametrize("N,K", [(64, 64), (128, 64), (64, 128), (128, 128)])
 def test_umma_selftest(mode, N, K):
     from nifre_b200 import _lib

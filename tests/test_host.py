@@ -199,7 +199,7 @@ def test_library_exports_every_declared_symbol():
     for s in syms:
         assert hasattr(lib, s), s
     assert set(_lib.EXPORTS) <= set(syms)
-    assert _lib.load().nf_abi_version() == 6
+    assert _lib.load().nf_abi_version() == 7
 
 
 def test_workspace_sizing_and_argument_errors():
@@ -243,8 +243,8 @@ def test_prefill_schedule_covers_items_and_balances():
     import numpy as np
     from nifre_b200.paged_kv_cache import _prefill_schedule
     rng = np.random.default_rng(0)
-    tiles = [(0, 32 * t, 32, int(p) + 32 * t) for t, p in enumerate(rng.integers(0, 2048, size=60))]
-    H, sms = 8, 296
+    tiles = [(0, 64 * t, 64, int(p) + 64 * t) for t, p in enumerate(rng.integers(0, 2048, size=60))]
+    H, sms = 8, 148
     arr = _prefill_schedule(tiles, H, sms)
     n_ctas = min(sms, len(tiles) * H)
     offs, items = arr[: n_ctas + 1], arr[n_ctas + 1:]
