@@ -186,14 +186,15 @@ int nf_paged_attention(void* out, int64_t out_row_stride,
  * one sequence whose rows in q/out start at q_row0 and whose absolute
  * positions start at pos0; query pos0 + i attends over keys [0, pos0 + i] of
  * the slot's block table (attention.py:144-152), all already appended.
- * Writes those rows of out.  Work items are (tile, KV head), numbered
+ * Writes those rows of out (rows >= num_rows, the rows of q and out, are
+ * neither read nor written).  Work items are (tile, KV head), numbered
  * tile * num_kv_heads + head; one CTA per SM runs a list of them.
  * schedule (device, may be NULL): n_lists + 1 offsets followed by the items,
  * CTA w running items [offsets[w], offsets[w+1]) in that order (n_lists <=
  * SMs; the caller balances the lists); NULL deals items round-robin.
  */
 int nf_prefill_attention(void* out, int64_t out_row_stride, const void* q, int64_t q_row_stride,
-                         const void* k_pool, const void* v_pool, int32_t dtype,
+                         int32_t num_rows, const void* k_pool, const void* v_pool, int32_t dtype,
                          int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
                          int32_t block_size, int32_t num_blocks,
                          const int32_t* block_tables, int32_t max_blocks_per_seq,

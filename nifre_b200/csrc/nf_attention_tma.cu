@@ -433,6 +433,34 @@ bool encode_pool_map(CUtensorMap* map, const void* pool, int dtype, int D, int H
   return r == CUDA_SUCCESS;
 }
 
+bool encode_rows_map(CUtensorMap* map, const void* base, int dtype, int D, int H, long long rows, long long row_stride,
+                     int g, int tt) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  const CUtensorMapDataType dt = dtype == NF_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  cuuint64_t dims[4], strides[3];
+  cuuint32_t box[4], es[4] = {1, 1, 1, 1};
+  cuuint32_t rank;
+  if (D == 64) {
+    rank = 3;
+    cuuint64_t d[3] = {64, (cuuint64_t)H, (cuuint64_t)rows};
+    cuuint64_t st[2] = {(cuuint64_t)D * 2, (cuuint64_t)row_stride * 2};
+    cuuint32_t b[3] = {64, (cuuint32_t)g, (cuuint32_t)tt};
+    for (int i = 0; i < 3; ++i) { dims[i] = d[i]; box[i] = b[i]; }
+    for (int i = 0; i < 2; ++i) strides[i] = st[i];
+  } else {
+    rank = 4;
+    cuuint64_t d[4] = {64, 2, (cuuint64_t)H, (cuuint64_t)rows};
+    cuuint64_t st[3] = {128, (cuuint64_t)D * 2, (cuuint64_t)row_stride * 2};
+    cuuint32_t b[4] = {64, 1, (cuuint32_t)g, (cuuint32_t)tt};
+    for (int i = 0; i < 4; ++i) { dims[i] = d[i]; box[i] = b[i]; }
+    for (int i = 0; i < 3; ++i) strides[i] = st[i];
+  }
+  const CUresult r = fn(map, dt, rank, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 // Launches the tensor-map kernel.  Returns NF_EUNSUPPORTED (nothing launched)
 // when the shape or the driver rules it out; the caller then uses the
 // per-warp cp.async kernel.

@@ -53,6 +53,7 @@ struct PrefillParams {
   long long out_stride;
   const char* q;
   long long q_stride;
+  int rows;                             // rows of q and out
   int Hq, Hkv, G, TT, bs, num_blocks;  // TT: tokens per 128-row half
   const int* bt;
   int max_blocks;
@@ -70,11 +71,12 @@ constexpr int kPfRows = 256;  // query rows of a work item
 template <int D_>
 struct PfCfg {
   static constexpr uint32_t TILE = 128 * D_ * 2;  // a 128-row Q half, or a 128-key K or V tile
-  static constexpr int KST = D_ == 64 ? 5 : 2;    // K ring
-  static constexpr int VST = D_ == 64 ? 6 : 3;    // V ring (held one tile longer than K)
+  static constexpr int QST = D_ == 64 ? 2 : 1;    // Q ring (both halves of an item per stage)
+  static constexpr int KST = D_ == 64 ? 4 : 2;    // K ring
+  static constexpr int VST = D_ == 64 ? 5 : 3;    // V ring (held one tile longer than K)
   static constexpr bool P_ALIAS = D_ == 128;      // P_h over the first 64 columns of S_h
   static constexpr uint32_t Q_OFF = 1024;         // after the barrier header
-  static constexpr uint32_t K_OFF = Q_OFF + 2 * TILE;
+  static constexpr uint32_t K_OFF = Q_OFF + QST * 2 * TILE;
   static constexpr uint32_t V_OFF = K_OFF + KST * TILE;
   static constexpr uint32_t SMEM = 1024 + V_OFF + VST * TILE;  // + alignment slack
   static constexpr int THREADS = 384;             // warp 0 producer, 1 MMA, 4-7 half 0, 8-11 half 1
@@ -90,7 +92,8 @@ constexpr uint32_t kTmemCols = 512;
 
 // Barriers at the start of the header: k_full[8] 0, k_empty[8] 64,
 // v_full[8] 128, v_empty[8] 192, then per half s_full 256, s_free 272,
-// p_full 288, o_done 304, q_full 320; tensor-memory base at 512.
+// p_full 288, o_done 304, and per Q stage q_full 320, q_empty 336;
+// tensor-memory base at 512.
 struct PfBars {
   uint32_t hdr;
   __device__ explicit PfBars(uint32_t h) : hdr(h) {}
@@ -102,7 +105,8 @@ struct PfBars {
   __device__ uint32_t s_free(int h) const { return hdr + 272 + 8 * h; }
   __device__ uint32_t p_full(int h) const { return hdr + 288 + 8 * h; }
   __device__ uint32_t o_done(int h) const { return hdr + 304 + 8 * h; }
-  __device__ uint32_t q_full(int h) const { return hdr + 320 + 8 * h; }
+  __device__ uint32_t q_full(int s) const { return hdr + 320 + 8 * s; }
+  __device__ uint32_t q_empty(int s) const { return hdr + 336 + 8 * s; }
 };
 constexpr uint32_t kPfTmemPtr = 512;
 
@@ -271,15 +275,33 @@ __device__ __forceinline__ void pf_load_tile(const PrefillParams& p, const CUten
 // The producer warp: every lane runs the loop (waits included), lanes 0..7
 // load block ids and issue the tensor copies.
 template <int D_>
-__device__ void pf_producer(const PrefillParams& p, const CUtensorMap* tk, const CUtensorMap* tv, const PfBars& bar,
-                            uint32_t k_s, uint32_t v_s, int worker, int n_workers) {
+__device__ void pf_producer(const PrefillParams& p, const CUtensorMap* tq, const CUtensorMap* tk,
+                            const CUtensorMap* tv, const PfBars& bar, uint32_t q_s, uint32_t k_s, uint32_t v_s,
+                            int worker, int n_workers) {
   using C = PfCfg<D_>;
+  constexpr int NDH = D_ / 64;
   const int lane = threadIdx.x & 31;
   const uint64_t pol = l2_evict_last();  // every query tile of a chunk reads the same keys
-  Ring kr, vr;
+  const uint64_t pol_q = l2_evict_first();  // queries are read once
+  Ring qr, kr, vr;
   PfItems items(p, worker, n_workers);
   for (int it; items.next(it);) {
     const PfItem w(p, it);
+    // the item's query rows, both halves (one copy per half and 64-element part)
+    if (!mbar_wait(bar.q_empty(qr.st), qr.ph ^ 1, p.status)) return;
+    const int nq = w.n_half * NDH;
+    if (lane == 0) mbar_arrive_expect_tx(bar.q_full(qr.st), nq * 128 * 128);
+    __syncwarp();
+    if (lane < nq) {
+      const int h = lane / NDH, dh = lane - h * NDH;
+      const uint32_t dst = q_s + (qr.st * 2 + h) * C::TILE + dh * 128 * 128;
+      const int row0 = w.tl.y + h * p.TT;
+      if constexpr (D_ == 64)
+        tma_load_3d(dst, tq, 0, w.kvh * p.G, row0, bar.q_full(qr.st), pol_q);
+      else
+        tma_load_4d(dst, tq, 0, dh, w.kvh * p.G, row0, bar.q_full(qr.st), pol_q);
+    }
+    qr.next(C::QST);
     const int* btrow = p.bt + (long long)w.tl.x * p.max_blocks;
     int cur = pf_block_id(p, btrow, 0, w.nkeys, lane);
     for (int j = 0; j < w.nkt; ++j) {
@@ -301,44 +323,58 @@ template <int D_>
 __device__ void pf_mma(const PrefillParams& p, const PfBars& bar, uint32_t tmem, uint32_t q_s, uint32_t k_s,
                        uint32_t v_s, bool bf, int worker, int n_workers) {
   using C = PfCfg<D_>;
-  const bool leader = (threadIdx.x & 31) == 0;
+  const bool leader = elect_one();
   constexpr uint32_t REG = 128 * 128;  // one 64-element region of a 128-row operand
   const uint32_t idesc_s = umma_idesc_f16(bf, 128, 128, false, false);
   const uint32_t idesc_o = umma_idesc_f16(bf, 128, D_, false, true);
-  Ring kr, vr;
-  int n_s[2] = {0, 0}, n_p[2] = {0, 0}, n_q[2] = {0, 0};
+  Ring qr, kr, vr;
+  int n_s[2] = {0, 0}, n_p[2] = {0, 0};
   auto wait_p = [&](int h) -> bool {
     if (!mbar_wait(bar.p_full(h), n_p[h] & 1, p.status)) return false;
     ++n_p[h];
     return true;
   };
+  // Operands of tcgen05.mma live in warp-uniform registers: the tensor-memory
+  // and shared-memory bases are broadcast from lane 0 so that the compiler
+  // knows them uniform, and the descriptors of Q half 0, K stage 0 and V
+  // stage 0 are built once; other stages, halves and k-steps are constant
+  // offsets in the 16-byte address field (all below 2^18 bytes, so no carry
+  // leaves it).  Lane 0 issues.
+  tmem = __shfl_sync(0xffffffffu, tmem, 0);
+  const uint64_t dq = umma_sdesc_sw128(__shfl_sync(0xffffffffu, q_s, 0), 16, 1024);
+  const uint64_t dk = umma_sdesc_sw128(__shfl_sync(0xffffffffu, k_s, 0), 16, 1024);
+  const uint64_t dv = umma_sdesc_sw128(__shfl_sync(0xffffffffu, v_s, 0), REG, 1024);
   // O_h += P_h V of the tile in V stage vst (first: overwrite O_h)
   auto issue_pv = [&](int h, int vst, bool first) {
     tc_fence_after();
-    if (!leader) return;
-    const uint32_t vs = v_s + vst * C::TILE;
+    const uint64_t b0 = dv + (uint64_t)(vst * (C::TILE >> 4));
+    const uint32_t d = tmem + C::o_col(h), a0 = tmem + C::p_col(h);
+    if (leader) {
+      umma_f16_ts(d, a0, b0, idesc_o, first ? 0u : 1u);
 #pragma unroll
-    for (int kk = 0; kk < 8; ++kk) {
-      const uint64_t b = umma_sdesc_sw128(vs + kk * 16 * 128, REG, 1024);
-      umma_f16_ts(tmem + C::o_col(h), tmem + C::p_col(h) + kk * 8, b, idesc_o, (first && kk == 0) ? 0u : 1u);
+      for (int kk = 1; kk < 8; ++kk) umma_f16_ts(d, a0 + kk * 8, b0 + (uint64_t)(kk * 16 * 128 >> 4), idesc_o, 1u);
+      umma_commit(bar.o_done(h));
     }
-    umma_commit(bar.o_done(h));
+    __syncwarp();
   };
   auto issue_s = [&](int h, int kst) {
-    if (!leader) return;
-    const uint32_t ks = k_s + kst * C::TILE, qs = q_s + h * C::TILE;
+    const uint64_t a0 = dq + (uint64_t)((qr.st * 2 + h) * (C::TILE >> 4)), b0 = dk + (uint64_t)(kst * (C::TILE >> 4));
+    const uint32_t d = tmem + C::s_col(h);
+    if (leader) {
 #pragma unroll
-    for (int k = 0; k < D_ / 16; ++k) {
-      const uint64_t a = umma_sdesc_sw128(qs + (k >> 2) * REG + (k & 3) * 32, 16, 1024);
-      const uint64_t b = umma_sdesc_sw128(ks + (k >> 2) * REG + (k & 3) * 32, 16, 1024);
-      umma_f16_ss(tmem + C::s_col(h), a, b, idesc_s, k > 0 ? 1u : 0u);
+      for (int k = 0; k < D_ / 16; ++k) {
+        const uint64_t off = (uint64_t)(((k >> 2) * REG + (k & 3) * 32) >> 4);
+        umma_f16_ss(d, a0 + off, b0 + off, idesc_s, k > 0 ? 1u : 0u);
+      }
+      umma_commit(bar.s_full(h));
     }
-    umma_commit(bar.s_full(h));
+    __syncwarp();
   };
   PfItems items(p, worker, n_workers);
   for (int it; items.next(it);) {
     const PfItem w(p, it);
     int vprev = -1;  // V stage of tile j-1
+    if (!mbar_wait(bar.q_full(qr.st), qr.ph, p.status)) return;
     for (int j = 0; j < w.nkt; ++j) {
       if (!mbar_wait(bar.k_full(kr.st), kr.ph, p.status)) return;
 #pragma unroll
@@ -349,10 +385,6 @@ __device__ void pf_mma(const PrefillParams& p, const PfBars& bar, uint32_t tmem,
           issue_pv(h, vprev, j == 1);
         }
         if (!w.active(h, j)) continue;
-        if (j == 0) {
-          if (!mbar_wait(bar.q_full(h), n_q[h] & 1, p.status)) return;
-          ++n_q[h];
-        }
         if (!C::P_ALIAS) {
           if (!mbar_wait(bar.s_free(h), (n_s[h] & 1) ^ 1, p.status)) return;
         }
@@ -377,6 +409,9 @@ __device__ void pf_mma(const PrefillParams& p, const PfBars& bar, uint32_t tmem,
       vprev = vr.st;
       vr.next(C::VST);
     }
+    // every S of the item is issued: the Q stage is free once they complete
+    if (leader) umma_commit(bar.q_empty(qr.st));
+    qr.next(C::QST);
     // the last tile: rows of V past the last key are zeroed by the last
     // half's warpgroup, so both halves' P must be in before either P V
     const int jl = w.nkt - 1;
@@ -391,8 +426,8 @@ __device__ void pf_mma(const PrefillParams& p, const PfBars& bar, uint32_t tmem,
 }
 
 template <typename T, int D_>
-__device__ void pf_softmax(const PrefillParams& p, const PfBars& bar, uint32_t tmem, uint32_t q_s, uint32_t v_s,
-                           int h, int worker, int n_workers) {
+__device__ void pf_softmax(const PrefillParams& p, const PfBars& bar, uint32_t tmem, uint32_t v_s, int h, int worker,
+                           int n_workers) {
   using C = PfCfg<D_>;
   constexpr int NDH = D_ / 64;
   constexpr uint32_t REG = 128 * 128;
@@ -401,7 +436,6 @@ __device__ void pf_softmax(const PrefillParams& p, const PfBars& bar, uint32_t t
   const uint32_t lane_addr = (uint32_t)(quad * 32) << 16;
   const uint32_t s_addr = tmem + lane_addr + C::s_col(h), o_addr = tmem + lane_addr + C::o_col(h);
   const uint32_t p_addr = tmem + lane_addr + C::p_col(h);
-  const uint32_t qh_s = q_s + h * C::TILE;
   const int G = p.G;
   int n_s = 0, n_o = 0;
   Ring vr;  // V ring position of this CTA's current tile (every item advances it)
@@ -414,23 +448,8 @@ __device__ void pf_softmax(const PrefillParams& p, const PfBars& bar, uint32_t t
     if (h >= w.n_half) continue;
     const int nkt = w.nkt_h[h];
     const int tok = h * p.TT + row / G, hd = row % G;
-    const bool valid = tok < min(w.tl.z, 2 * p.TT);
+    const bool valid = tok < min(w.tl.z, 2 * p.TT) && w.tl.y + tok < p.rows;
     const int qpos = w.tl.w + tok;
-    // this row of Q into the swizzled A operand
-    {
-      const char* src = p.q + ((long long)(w.tl.y + tok) * p.q_stride + (long long)(w.kvh * G + hd) * D_) * 2;
-#pragma unroll
-      for (int c = 0; c < NDH * 8; ++c) {
-        uint4 v = make_uint4(0u, 0u, 0u, 0u);
-        if (valid) v = __ldg(reinterpret_cast<const uint4*>(src) + c);
-        const uint32_t a = qh_s + (c >> 3) * REG + row * 128 + (((c & 7) ^ (row & 7)) << 4);
-        asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
-                     : "memory");
-      }
-    }
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    __syncwarp();
-    if (lane == 0) mbar_arrive(bar.q_full(h));
     float m = kPfNegInf, l = 0.f;
     for (int j = 0; j < nkt; ++j) {
       if (!mbar_wait(bar.s_full(h), n_s & 1, p.status)) return;
@@ -558,8 +577,8 @@ __device__ void pf_softmax(const PrefillParams& p, const PfBars& bar, uint32_t t
 
 template <typename T, int D_>
 __global__ void __launch_bounds__(PfCfg<D_>::THREADS, 1)
-    prefill_attention_kernel(const PrefillParams p, const __grid_constant__ CUtensorMap tk,
-                             const __grid_constant__ CUtensorMap tv) {
+    prefill_attention_kernel(const PrefillParams p, const __grid_constant__ CUtensorMap tq,
+                             const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv) {
   using C = PfCfg<D_>;
   extern __shared__ unsigned char smem_raw[];
   unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -580,7 +599,10 @@ __global__ void __launch_bounds__(PfCfg<D_>::THREADS, 1)
       mbar_init(bar.s_free(h), 4);
       mbar_init(bar.p_full(h), 4);
       mbar_init(bar.o_done(h), 1);
-      mbar_init(bar.q_full(h), 4);
+    }
+    for (int s = 0; s < C::QST; ++s) {
+      mbar_init(bar.q_full(s), 1);
+      mbar_init(bar.q_empty(s), 1);
     }
     fence_mbar_init();
   }
@@ -595,12 +617,12 @@ __global__ void __launch_bounds__(PfCfg<D_>::THREADS, 1)
   if (warp < 4) {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(C::REGS_CTRL));
     if (warp == 0)
-      pf_producer<D_>(p, &tk, &tv, bar, k_s, v_s, worker, n_workers);
+      pf_producer<D_>(p, &tq, &tk, &tv, bar, q_s, k_s, v_s, worker, n_workers);
     else if (warp == 1)
       pf_mma<D_>(p, bar, tmem, q_s, k_s, v_s, std::is_same<T, __nv_bfloat16>::value, worker, n_workers);
   } else {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(C::REGS_SOFTMAX));
-    pf_softmax<T, D_>(p, bar, tmem, q_s, v_s, (warp - 4) >> 2, worker, n_workers);
+    pf_softmax<T, D_>(p, bar, tmem, v_s, (warp - 4) >> 2, worker, n_workers);
   }
   tc_fence_before();
   __syncthreads();
@@ -609,15 +631,15 @@ __global__ void __launch_bounds__(PfCfg<D_>::THREADS, 1)
 }
 
 template <typename T, int D_>
-static int launch_prefill(const PrefillParams& p, const CUtensorMap& tk, const CUtensorMap& tv, int n_items,
-                          cudaStream_t st) {
+static int launch_prefill(const PrefillParams& p, const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+                          int n_items, cudaStream_t st) {
   using C = PfCfg<D_>;
   auto kern = prefill_attention_kernel<T, D_>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
   if (e != cudaSuccess) return fail(NF_ECUDA, "nf_prefill_attention: smem attribute: %s", cudaGetErrorString(e));
   long long grid = p.sched ? p.n_lists : n_items;
   if (grid > sm_count()) grid = sm_count();
-  kern<<<(int)grid, C::THREADS, C::SMEM, st>>>(p, tk, tv);
+  kern<<<(int)grid, C::THREADS, C::SMEM, st>>>(p, tq, tk, tv);
   return check_launch("nf_prefill_attention");
 }
 
@@ -626,7 +648,7 @@ static int launch_prefill(const PrefillParams& p, const CUtensorMap& tk, const C
 extern "C" int nf_prefill_tile_rows(void) { return nf::kPfRows; }
 
 extern "C" int nf_prefill_attention(void* out, int64_t out_row_stride, const void* q, int64_t q_row_stride,
-                                    const void* k_pool, const void* v_pool, int32_t dtype, int32_t num_q_heads,
+                                    int32_t num_rows, const void* k_pool, const void* v_pool, int32_t dtype, int32_t num_q_heads,
                                     int32_t num_kv_heads, int32_t head_dim, int32_t block_size, int32_t num_blocks,
                                     const int32_t* block_tables, int32_t max_blocks_per_seq, const int32_t* tiles,
                                     int32_t n_tiles, const int32_t* schedule, int32_t n_lists, float scale,
@@ -643,7 +665,7 @@ extern "C" int nf_prefill_attention(void* out, int64_t out_row_stride, const voi
     return fail(NF_EUNSUPPORTED, "nf_prefill_attention: %d query heads per KV head (1, 2, 4 or 8)", G);
   if (block_size <= 0 || block_size % 16)
     return fail(NF_EUNSUPPORTED, "nf_prefill_attention: block_size %d is not a multiple of 16", block_size);
-  if (n_tiles < 0 || num_blocks <= 0 || max_blocks_per_seq <= 0)
+  if (n_tiles < 0 || num_blocks <= 0 || max_blocks_per_seq <= 0 || num_rows <= 0)
     return fail(NF_EINVAL, "nf_prefill_attention: sizes must be positive");
   if (n_tiles == 0) return ok();
   if (!out || !q || !k_pool || !v_pool || !block_tables || !tiles || !status)
@@ -654,8 +676,9 @@ extern "C" int nf_prefill_attention(void* out, int64_t out_row_stride, const voi
   if (!al(q, 16) || !al(out, 16) || (q_row_stride * 2) % 16 || (out_row_stride * 2) % 16 || !al(tiles, 16) ||
       !al(k_pool, 16) || !al(v_pool, 16))
     return fail(NF_EINVAL, "nf_prefill_attention: q/out rows, pools and tiles must be 16-byte aligned");
-  CUtensorMap tk, tv;
-  if (!encode_pool_map(&tk, k_pool, dtype, head_dim, num_kv_heads, block_size, num_blocks, 1, false) ||
+  CUtensorMap tq, tk, tv;
+  if (!encode_rows_map(&tq, q, dtype, head_dim, num_q_heads, num_rows, q_row_stride, G, 128 / G) ||
+      !encode_pool_map(&tk, k_pool, dtype, head_dim, num_kv_heads, block_size, num_blocks, 1, false) ||
       !encode_pool_map(&tv, v_pool, dtype, head_dim, num_kv_heads, block_size, num_blocks, 1, false))
     return fail(NF_ECUDA, "nf_prefill_attention: tensor map encoding failed");
   PrefillParams p;
@@ -663,6 +686,7 @@ extern "C" int nf_prefill_attention(void* out, int64_t out_row_stride, const voi
   p.out_stride = out_row_stride;
   p.q = static_cast<const char*>(q);
   p.q_stride = q_row_stride;
+  p.rows = num_rows;
   p.Hq = num_q_heads;
   p.Hkv = num_kv_heads;
   p.G = G;
@@ -680,8 +704,8 @@ extern "C" int nf_prefill_attention(void* out, int64_t out_row_stride, const voi
   const int n_items = n_tiles * num_kv_heads;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (dtype == NF_BF16)
-    return head_dim == 64 ? launch_prefill<__nv_bfloat16, 64>(p, tk, tv, n_items, st)
-                          : launch_prefill<__nv_bfloat16, 128>(p, tk, tv, n_items, st);
-  return head_dim == 64 ? launch_prefill<__half, 64>(p, tk, tv, n_items, st)
-                        : launch_prefill<__half, 128>(p, tk, tv, n_items, st);
+    return head_dim == 64 ? launch_prefill<__nv_bfloat16, 64>(p, tq, tk, tv, n_items, st)
+                          : launch_prefill<__nv_bfloat16, 128>(p, tq, tk, tv, n_items, st);
+  return head_dim == 64 ? launch_prefill<__half, 64>(p, tq, tk, tv, n_items, st)
+                        : launch_prefill<__half, 128>(p, tq, tk, tv, n_items, st);
 }

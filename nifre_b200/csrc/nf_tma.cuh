@@ -23,6 +23,15 @@ __device__ __forceinline__ uint64_t l2_evict_last() {
   return pol;
 }
 
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2, uint32_t bar,
+                                            uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, {%2, "
+      "%3, %4}], [%5], %6;" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(bar), "l"(pol)
+      : "memory");
+}
+
 __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2, int c3,
                                             uint32_t bar, uint64_t pol) {
   asm volatile(
@@ -47,5 +56,12 @@ __device__ __forceinline__ void tma_load_5d(uint32_t dst, const CUtensorMap* map
 // box of one head (and one 64-element half of a 128-wide head) x 16 tokens.
 bool encode_pool_map(CUtensorMap* map, const void* pool, int dtype, int D, int Hkv, int bs, int num_blocks, int hg,
                      bool permuted);
+
+// Tensor map over query rows (rows, H, D) with row stride `row_stride`
+// elements, 16-bit, 128-byte swizzle: dims (d_lo, [d_hi,] head, row), box of
+// 64 elements x g heads x tt rows, landing as tt*g rows of 128 bytes (row
+// major in (row, head)).
+bool encode_rows_map(CUtensorMap* map, const void* base, int dtype, int D, int H, long long rows, long long row_stride,
+                     int g, int tt);
 
 }  // namespace nf

@@ -467,7 +467,7 @@ class PagedKVCache:
             events[0].record()
         if plan.n_tiles:
             _lib.check(lib.nf_prefill_attention(
-                out.data_ptr(), out.stride(0), q.data_ptr(), q.stride(0),
+                out.data_ptr(), out.stride(0), q.data_ptr(), q.stride(0), min(q.shape[0], out.shape[0]),
                 self.k[layer_id].data_ptr(), self.v[layer_id].data_ptr(), _lib.dtype_code(self.dtype),
                 hq, self.n_heads, D, self.block_size, self.num_blocks, self.bt_dev.data_ptr(),
                 self.max_blocks_per_seq, plan.tiles.data_ptr(), plan.n_tiles, plan.sched.data_ptr(),
