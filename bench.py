@@ -78,6 +78,7 @@ def _args():
     ap.add_argument("--e2e-steps", type=int, default=50)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=None, help="fewer resident layers (profiling a small case)")
+    ap.add_argument("--seqs", type=int, default=None, help="fewer decode sequences (profiling a small case)")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="llama3.2-1b-decode")
     a = ap.parse_args()
     global METRIC
@@ -90,6 +91,8 @@ def _args():
         CFG["resident"] = a.layers
         if a.workload != "llama3-8b-long":
             CFG["layers"] = a.layers
+    if a.seqs:
+        CFG["seqs"] = a.seqs
     return a
 
 
