@@ -64,6 +64,13 @@ WORKLOADS = {
                               dctx_lo=256, dctx_hi=2048, seqs=100, ctx_lo=256, ctx_hi=2048, cpu_sample=8,
                               metric="mixed prefill+decode step tok/s (1B shape, 16 layers, 4x512 chunks + 96 "
                                      "decodes)"),
+    # decode over shared prefixes on the 1B shape: 128 requests, each one of 4 common 1024-token
+    # prefixes (64 shared blocks, imported through the prefix cache) + a unique U[64, 256] suffix
+    "llama3.2-1b-prefix": dict(kind="prefix", layers=16, resident=16, hq=32, hkv=8, d=64, bs=16, seed=1,
+                               scaling="strong", steps=40, seqs=128, prefixes=4, prefix_len=1024, suffix_lo=64,
+                               suffix_hi=256, vocab=50257, cpu_sample=8,
+                               metric="paged-attn decode tok/s over shared prefixes (1B shape, 16 layers, 128 seqs "
+                                      "on 4 shared 1024-token prefixes)"),
 }
 CFG = dict(name="llama3.2-1b-decode", **WORKLOADS["llama3.2-1b-decode"])
 METRIC = CFG["metric"]
@@ -97,8 +104,21 @@ def _args():
 
 
 def _ctx_lens(n, seed):
+    if CFG.get("kind") == "prefix":
+        _, group, suffix = _prefix_shape(n)
+        return [CFG["prefix_len"] + len(suffix[r]) for r in range(n)]
     rng = np.random.default_rng(seed)
     return rng.integers(CFG["ctx_lo"], CFG["ctx_hi"] + 1, size=n).tolist()
+
+
+def _prefix_shape(n):
+    """Token ids of the shared prefixes, each request's prefix and its unique suffix (seeded)."""
+    rng = np.random.default_rng(CFG["seed"])
+    prefixes = [rng.integers(0, CFG["vocab"], size=CFG["prefix_len"]).tolist() for _ in range(CFG["prefixes"])]
+    group = rng.integers(0, CFG["prefixes"], size=n).tolist()
+    suffix = [rng.integers(0, CFG["vocab"], size=int(rng.integers(CFG["suffix_lo"], CFG["suffix_hi"] + 1))).tolist()
+              for _ in range(n)]
+    return prefixes, group, suffix
 
 
 # ---------------------------------------------------------------------------- clocks
@@ -234,8 +254,6 @@ def cpu_decode_rate(seconds: float, threads: int | None = None):
 
 # ---------------------------------------------------------------------------- our arm
 def run_ours(args):
-    from nifre_b200 import Attention, PagedKVCache
-
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -249,15 +267,26 @@ def run_ours(args):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     if CFG["hkv"] % world:
         raise SystemExit(f"--gpus {world} must divide {CFG['hkv']} KV heads")
-    L, L_model, D, bs = CFG["resident"], CFG["layers"], CFG["d"], CFG["bs"]
     from nifre_b200.sharding import HeadShard
     shard = HeadShard(world, rank, CFG["hq"], CFG["hkv"], CFG["d"])
     hkv, hq = shard.kv_heads, shard.q_heads
     B = CFG["seqs"] * world if CFG["scaling"] == "weak" else CFG["seqs"]
     ctx = _ctx_lens(B, CFG["seed"])
     steps_total = args.warmup + args.steps + args.e2e_steps + 2
-    max_seq = CFG["ctx_hi"] + steps_total + 16
     dt = torch.bfloat16
+    if CFG.get("kind") == "prefix":
+        return _run_decode_timed(args, _build_prefix_cache(B, ctx, steps_total, hkv, dev, dt), B, ctx, world, rank,
+                                 local, dev, dist, shard, hkv, hq)
+    return _run_decode_timed(args, _build_decode_cache(B, ctx, steps_total, hkv, dev, dt, rank), B, ctx, world, rank,
+                             local, dev, dist, shard, hkv, hq)
+
+
+def _build_decode_cache(B, ctx, steps_total, hkv, dev, dt, rank):
+    """Pool of the decode workloads: contexts filled with N(0,1) K/V over a randomly permuted free list."""
+    from nifre_b200 import PagedKVCache
+
+    L, D, bs = CFG["resident"], CFG["d"], CFG["bs"]
+    max_seq = max(ctx) + steps_total + 16
     # the pool holds the contexts plus the steps' tokens (sum of ceil(ctx/bs) blocks), shuffled below
     n_blocks = sum((c + steps_total + 16 + bs - 1) // bs for c in ctx)
     cache = PagedKVCache(L, max_seq, hkv, D, device=dev, dtype=dt, block_size=bs, enable_prefix_cache=False,
@@ -285,6 +314,46 @@ def run_ours(args):
             vfill.normal_(generator=gd)
             cache.append_step(layer, kfill, vfill, plan)
         del kfill, vfill, plan
+    return cache
+
+
+def _build_prefix_cache(B, ctx, steps_total, hkv, dev, dt):
+    """Pool of the shared-prefix workload, built the way the engine builds it: each request imports
+    the longest cached prefix (``try_load_prefix``), prefills the rest, and registers its prompt
+    once complete (``register_prefix``), so later requests share the first request's prefix blocks."""
+    from nifre_b200 import PagedKVCache
+
+    L, D, bs = CFG["resident"], CFG["d"], CFG["bs"]
+    prefixes, group, suffix = _prefix_shape(B)
+    max_seq = max(ctx) + steps_total + 16
+    n_blocks = CFG["prefixes"] * (CFG["prefix_len"] // bs) + sum(
+        (len(sfx) + steps_total + 16 + bs - 1) // bs + 1 for sfx in suffix)
+    cache = PagedKVCache(L, max_seq, hkv, D, device=dev, dtype=dt, block_size=bs, enable_prefix_cache=True,
+                         num_blocks=n_blocks)
+    cache.init_batch(B)
+    gd = torch.Generator(device=dev).manual_seed(CFG["seed"])
+    for r in range(B):
+        tokens = prefixes[group[r]] + suffix[r]
+        matched = cache.try_load_prefix(r, tokens)
+        n_new = len(tokens) - matched
+        plan = cache.plan([r], [n_new], [0])
+        kf = torch.empty(n_new, hkv * D, device=dev, dtype=dt)
+        vf = torch.empty_like(kf)
+        for layer in range(L):
+            kf.normal_(generator=gd)
+            vf.normal_(generator=gd)
+            cache.append_step(layer, kf, vf, plan)
+        cache.register_prefix(r, tokens)
+    cache.shared_prefix_keys = (B - len(set(group))) * CFG["prefix_len"]  # keys a cascade would not re-read
+    return cache
+
+
+def _run_decode_timed(args, cache, B, ctx, world, rank, local, dev, dist, shard, hkv, hq):
+    from nifre_b200 import Attention
+
+    L, L_model, D, bs = CFG["resident"], CFG["layers"], CFG["d"], CFG["bs"]
+    dt = torch.bfloat16
+    gd = torch.Generator(device=dev).manual_seed(CFG["seed"] + 1000 + rank)
     q_all = torch.randn(L, B, hq * D, device=dev, dtype=dt, generator=gd)
     k_all = torch.randn(L, B, hkv * D, device=dev, dtype=dt, generator=gd)
     v_all = torch.randn(L, B, hkv * D, device=dev, dtype=dt, generator=gd)
@@ -336,11 +405,13 @@ def run_ours(args):
     cache.check_status()
     # attention kernel: algorithmic bytes per launch / event duration
     att_ms = [a.elapsed_time(b) for a, b, _ in att_events]
-    att_bytes = []
+    att_bytes, logical_bytes = [], []
+    shared = getattr(cache, "shared_prefix_keys", 0)  # prefix keys of other sequences: read once (unique bytes)
     for _, _, p in att_events:
         kv = int(p.kv_lens.sum())
         nblk = int(((p.kv_lens + bs - 1) // bs).sum())
-        att_bytes.append(kv * hkv * D * 2 * 2 + 2 * B * hq * D * 2 + 4 * nblk + 16 * B)
+        att_bytes.append((kv - shared) * hkv * D * 2 * 2 + 2 * B * hq * D * 2 + 4 * nblk + 16 * B)
+        logical_bytes.append(kv * hkv * D * 2 * 2 + 2 * B * hq * D * 2 + 4 * nblk + 16 * B)
     from nifre_b200 import _lib
     att_path = _lib.load().nf_last_attention_path()
     att_avg_ms = sum(att_ms) / len(att_ms)
@@ -408,12 +479,18 @@ def run_ours(args):
             "config": {"workload": CFG["name"], "layers": L_model, "layers_timed": L, "q_heads": CFG["hq"],
                        "kv_heads": CFG["hkv"], "head_dim": D, "block_size": bs,
                        "seqs_per_gpu_x_heads": f"{B} seqs x {hkv} kv heads",
-                       "global_batch": B, "ctx": f"U[{CFG['ctx_lo']},{CFG['ctx_hi']}] + step",
+                       "global_batch": B,
+                       "ctx": (f"U[{CFG['ctx_lo']},{CFG['ctx_hi']}] + step" if "ctx_lo" in CFG else
+                               f"{CFG['prefix_len']}-token prefix (one of {CFG['prefixes']}, shared blocks) + "
+                               f"U[{CFG['suffix_lo']},{CFG['suffix_hi']}] suffix + step"),
                        "parallelism": f"kv-head shard x{world}" if world > 1 else "single GPU",
                        "method": ("all layers run every step" if L == L_model else
                                   f"{L} resident layers run per step; tok/s and ms_per_step scaled to "
                                   f"{L_model} layers at the measured per-layer time"),
-                       "l2": "inputs larger than L2 (each layer reads a distinct pool of >=300 MB)"},
+                       "l2": ("inputs larger than L2 (each layer reads a distinct pool of >=300 MB)"
+                              if not shared else
+                              "each layer reads a distinct pool; shared prefix blocks (16 MB per layer) are read by "
+                              "every sequence that imported them: the roofline counts them once (unique bytes)")},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak,
                          "traffic": (CFG["traffic_ratio"] * sum(att_bytes) / len(att_bytes)
@@ -422,7 +499,10 @@ def run_ours(args):
                          "kernel": "nf_paged_attention",
                          "kernel_path": {0: "per-warp cp.async", 1: "tensor map, one copy per block",
                                          2: "tensor map, one copy per head"}.get(att_path, str(att_path)),
-                         "peak_source": peak_kind, "avg_launch_us": att_avg_ms * 1e3},
+                         "peak_source": peak_kind, "avg_launch_us": att_avg_ms * 1e3,
+                         **({"bytes": "unique (shared prefix blocks once)",
+                             "achieved_logical": (sum(logical_bytes) / len(logical_bytes)) / (att_avg_ms * 1e-3) / 1e9}
+                            if shared else {})},
             "cpu_baseline": cpu,
             "e2e": e2e,
             "gpu_launches": args.steps * (1 + 2 * L),
