@@ -188,10 +188,12 @@ int nf_paged_attention(void* out, int64_t out_row_stride,
  * the slot's block table (attention.py:144-152), all already appended.
  * Writes those rows of out (rows >= num_rows, the rows of q and out, are
  * neither read nor written).  Work items are (tile, KV head), numbered
- * tile * num_kv_heads + head; one CTA per SM runs a list of them.
- * schedule (device, may be NULL): n_lists + 1 offsets followed by the items,
- * CTA w running items [offsets[w], offsets[w+1]) in that order (n_lists <=
- * SMs; the caller balances the lists); NULL deals items round-robin.
+ * tile * num_kv_heads + head.  One persistent CTA per SM takes items from a
+ * queue shared by all CTAs, in the order given by `order` (device, n_tiles *
+ * num_kv_heads item numbers, longest first for balance; NULL: item number
+ * order).  queue (device, int32[2]) must be zero on entry; the kernel leaves
+ * it zero, so one buffer serves every launch on a stream (launches that share
+ * it must not overlap).
  */
 int nf_prefill_attention(void* out, int64_t out_row_stride, const void* q, int64_t q_row_stride,
                          int32_t num_rows, const void* k_pool, const void* v_pool, int32_t dtype,
@@ -199,7 +201,7 @@ int nf_prefill_attention(void* out, int64_t out_row_stride, const void* q, int64
                          int32_t block_size, int32_t num_blocks,
                          const int32_t* block_tables, int32_t max_blocks_per_seq,
                          const int32_t* tiles, int32_t n_tiles,
-                         const int32_t* schedule, int32_t n_lists, float scale,
+                         const int32_t* order, int32_t* queue, float scale,
                          int32_t* status, void* stream);
 
 /* Query rows (tokens x query heads per KV head) of one nf_prefill_attention work item: 256. */

@@ -59,8 +59,8 @@ struct PrefillParams {
   int max_blocks;
   const int* tiles;  // [n_tiles] x {slot, q_row0, ntok, pos0}
   int n_tiles;
-  const int* sched;  // optional: [n_lists + 1] offsets, then the items (tile * Hkv + kv head) of each list
-  int n_lists;
+  const int* order;  // optional: the items (tile * Hkv + kv head) in the order CTAs take them
+  int* queue;        // [2]: next position in the order, CTAs finished (zero on entry and on exit)
   float scale_log2;
   int* status;
 };
@@ -92,8 +92,9 @@ constexpr uint32_t kTmemCols = 512;
 
 // Barriers at the start of the header: k_full[8] 0, k_empty[8] 64,
 // v_full[8] 128, v_empty[8] 192, then per half s_full 256, s_free 272,
-// p_full 288, o_done 304, and per Q stage q_full 320, q_empty 336;
-// tensor-memory base at 512.
+// p_full 288, o_done 304, per Q stage q_full 320, q_empty 336, and per item
+// slot item_full 384, item_empty 416; tensor-memory base at 512, item slots
+// (8 ints each) from 640.
 struct PfBars {
   uint32_t hdr;
   __device__ explicit PfBars(uint32_t h) : hdr(h) {}
@@ -107,8 +108,13 @@ struct PfBars {
   __device__ uint32_t o_done(int h) const { return hdr + 304 + 8 * h; }
   __device__ uint32_t q_full(int s) const { return hdr + 320 + 8 * s; }
   __device__ uint32_t q_empty(int s) const { return hdr + 336 + 8 * s; }
+  __device__ uint32_t item_full(int s) const { return hdr + 384 + 8 * s; }
+  __device__ uint32_t item_empty(int s) const { return hdr + 416 + 8 * s; }
 };
 constexpr uint32_t kPfTmemPtr = 512;
+constexpr uint32_t kPfItemSlots = 640;
+constexpr int kPfItemRing = 4;
+constexpr int kPfItemReaders = 9;  // the MMA warp and the eight softmax warps
 
 // ---------------------------------------------------------------- softmax arithmetic
 // Pairs of fp32 values in one 64-bit register, for the packed fp32x2
@@ -188,45 +194,61 @@ struct Ring {
   }
 };
 
-// The work items of CTA `worker`: its list in the schedule, or every
-// n_workers-th item.
-struct PfItems {
-  int i, end, step;
-  const int* list;
-  __device__ PfItems(const PrefillParams& p, int worker, int n_workers) {
-    if (p.sched) {
-      if (worker < p.n_lists) {
-        i = __ldg(p.sched + worker);
-        end = __ldg(p.sched + worker + 1);
-      } else {
-        i = end = 0;
-      }
-      step = 1;
-      list = p.sched + p.n_lists + 1;
-    } else {
-      i = worker;
-      end = p.n_tiles * p.Hkv;
-      step = n_workers;
-      list = nullptr;
-    }
-  }
-  __device__ bool next(int& item) {
-    if (i >= end) return false;
-    item = list ? __ldg(list + i) : i;
-    i += step;
-    return true;
+// Work items come from one queue shared by all CTAs: the producer warp of
+// a CTA claims the next position in the order (longest items first) when it
+// starts loading an item, so CTAs that finish early take more, and passes
+// the item with its tile descriptor to the CTA's other warps through a ring
+// of shared-memory slots.  A slot holding -1 ends the CTA's work.
+struct PfItemRing {
+  const PfBars& bar;
+  unsigned char* slots;
+  Ring r;
+  __device__ PfItemRing(const PfBars& b, unsigned char* base) : bar(b), slots(base + kPfItemSlots) {}
+  __device__ int* slot(int st) const { return reinterpret_cast<int*>(slots + 32 * st); }
+  // a reader warp: the next item (false at the end)
+  __device__ bool next(int& item, int4& tl, int* status) {
+    if (!mbar_wait(bar.item_full(r.st), r.ph, status)) return false;
+    const volatile int* sl = slot(r.st);
+    item = sl[0];
+    tl = make_int4(sl[1], sl[2], sl[3], sl[4]);
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0) mbar_arrive(bar.item_empty(r.st));
+    r.next(kPfItemRing);
+    return item >= 0;
   }
 };
+
+// The producer warp's side of the queue: claim the next item, publish it.
+__device__ __forceinline__ bool pf_claim_item(const PrefillParams& p, PfItemRing& ring, int& item, int4& tl) {
+  const int lane = threadIdx.x & 31;
+  int pos = 0;
+  if (lane == 0) pos = atomicAdd(p.queue, 1);
+  pos = __shfl_sync(0xffffffffu, pos, 0);
+  const int n_items = p.n_tiles * p.Hkv;
+  item = pos < n_items ? (p.order ? __ldg(p.order + pos) : pos) : -1;
+  tl = item >= 0 ? __ldg(reinterpret_cast<const int4*>(p.tiles) + item / p.Hkv) : make_int4(0, 0, 0, 0);
+  if (!mbar_wait(ring.bar.item_empty(ring.r.st), ring.r.ph ^ 1, p.status)) return false;
+  if (lane == 0) {
+    volatile int* sl = ring.slot(ring.r.st);
+    sl[0] = item;
+    sl[1] = tl.x;
+    sl[2] = tl.y;
+    sl[3] = tl.z;
+    sl[4] = tl.w;
+    mbar_arrive(ring.bar.item_full(ring.r.st));
+  }
+  __syncwarp();
+  ring.r.next(kPfItemRing);
+  return item >= 0;
+}
 
 // Shape of one work item: its key tiles, the halves that hold tokens and
 // each half's key tiles (half 0 ends up to 128/G tokens earlier).
 struct PfItem {
   int4 tl;  // slot, q_row0, ntok, pos0
   int kvh, nkeys, nkt, n_half, nkt_h[2];
-  __device__ PfItem(const PrefillParams& p, int item) {
-    const int t = item / p.Hkv;
-    kvh = item - t * p.Hkv;
-    tl = __ldg(reinterpret_cast<const int4*>(p.tiles) + t);
+  __device__ PfItem(const PrefillParams& p, int item, int4 t) : tl(t) {
+    kvh = item % p.Hkv;
     const int ntok = min(tl.z, 2 * p.TT);
     nkeys = tl.w + ntok;
     nkt = (nkeys + 127) >> 7;
@@ -277,16 +299,17 @@ __device__ __forceinline__ void pf_load_tile(const PrefillParams& p, const CUten
 template <int D_>
 __device__ void pf_producer(const PrefillParams& p, const CUtensorMap* tq, const CUtensorMap* tk,
                             const CUtensorMap* tv, const PfBars& bar, uint32_t q_s, uint32_t k_s, uint32_t v_s,
-                            int worker, int n_workers) {
+                            PfItemRing& ring) {
   using C = PfCfg<D_>;
   constexpr int NDH = D_ / 64;
   const int lane = threadIdx.x & 31;
   const uint64_t pol = l2_evict_last();  // every query tile of a chunk reads the same keys
   const uint64_t pol_q = l2_evict_first();  // queries are read once
   Ring qr, kr, vr;
-  PfItems items(p, worker, n_workers);
-  for (int it; items.next(it);) {
-    const PfItem w(p, it);
+  int it;
+  int4 itl;
+  while (pf_claim_item(p, ring, it, itl)) {
+    const PfItem w(p, it, itl);
     // the item's query rows, both halves (one copy per half and 64-element part)
     if (!mbar_wait(bar.q_empty(qr.st), qr.ph ^ 1, p.status)) return;
     const int nq = w.n_half * NDH;
@@ -321,7 +344,7 @@ __device__ void pf_producer(const PrefillParams& p, const CUtensorMap* tq, const
 // MMAs and the commits that track them.
 template <int D_>
 __device__ void pf_mma(const PrefillParams& p, const PfBars& bar, uint32_t tmem, uint32_t q_s, uint32_t k_s,
-                       uint32_t v_s, bool bf, int worker, int n_workers) {
+                       uint32_t v_s, bool bf, PfItemRing& ring) {
   using C = PfCfg<D_>;
   const bool leader = elect_one();
   constexpr uint32_t REG = 128 * 128;  // one 64-element region of a 128-row operand
@@ -370,9 +393,10 @@ __device__ void pf_mma(const PrefillParams& p, const PfBars& bar, uint32_t tmem,
     }
     __syncwarp();
   };
-  PfItems items(p, worker, n_workers);
-  for (int it; items.next(it);) {
-    const PfItem w(p, it);
+  int it;
+  int4 itl;
+  while (ring.next(it, itl, p.status)) {
+    const PfItem w(p, it, itl);
     int vprev = -1;  // V stage of tile j-1
     if (!mbar_wait(bar.q_full(qr.st), qr.ph, p.status)) return;
     for (int j = 0; j < w.nkt; ++j) {
@@ -426,8 +450,8 @@ __device__ void pf_mma(const PrefillParams& p, const PfBars& bar, uint32_t tmem,
 }
 
 template <typename T, int D_>
-__device__ void pf_softmax(const PrefillParams& p, const PfBars& bar, uint32_t tmem, uint32_t v_s, int h, int worker,
-                           int n_workers) {
+__device__ void pf_softmax(const PrefillParams& p, const PfBars& bar, uint32_t tmem, uint32_t v_s, int h,
+                           PfItemRing& ring) {
   using C = PfCfg<D_>;
   constexpr int NDH = D_ / 64;
   constexpr uint32_t REG = 128 * 128;
@@ -439,9 +463,10 @@ __device__ void pf_softmax(const PrefillParams& p, const PfBars& bar, uint32_t t
   const int G = p.G;
   int n_s = 0, n_o = 0;
   Ring vr;  // V ring position of this CTA's current tile (every item advances it)
-  PfItems items(p, worker, n_workers);
-  for (int it; items.next(it);) {
-    const PfItem w(p, it);
+  int it;
+  int4 itl;
+  while (ring.next(it, itl, p.status)) {
+    const PfItem w(p, it, itl);
     if (h == 0 && w.tl.z > 2 * p.TT && threadIdx.x == 128) atomicOr(p.status, NF_STATUS_BAD_TILE);
     const Ring vlast = vr.ahead(w.nkt - 1, C::VST);  // V stage of the item's last tile
     vr = vr.ahead(w.nkt, C::VST);
@@ -604,6 +629,10 @@ __global__ void __launch_bounds__(PfCfg<D_>::THREADS, 1)
       mbar_init(bar.q_full(s), 1);
       mbar_init(bar.q_empty(s), 1);
     }
+    for (int s = 0; s < kPfItemRing; ++s) {
+      mbar_init(bar.item_full(s), 1);
+      mbar_init(bar.item_empty(s), kPfItemReaders);
+    }
     fence_mbar_init();
   }
   if (warp == 1) tmem_alloc(hdr + kPfTmemPtr, kTmemCols);
@@ -612,22 +641,27 @@ __global__ void __launch_bounds__(PfCfg<D_>::THREADS, 1)
   tc_fence_after();
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(base + kPfTmemPtr);
   const uint32_t q_s = hdr + C::Q_OFF, k_s = hdr + C::K_OFF, v_s = hdr + C::V_OFF;
-  const int worker = blockIdx.x, n_workers = gridDim.x;
+  PfItemRing ring(bar, base);
   static_assert(C::REGS_CTRL * 128 + C::REGS_SOFTMAX * 256 <= 168 * C::THREADS, "register split exceeds the launch");
   if (warp < 4) {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(C::REGS_CTRL));
     if (warp == 0)
-      pf_producer<D_>(p, &tq, &tk, &tv, bar, q_s, k_s, v_s, worker, n_workers);
+      pf_producer<D_>(p, &tq, &tk, &tv, bar, q_s, k_s, v_s, ring);
     else if (warp == 1)
-      pf_mma<D_>(p, bar, tmem, q_s, k_s, v_s, std::is_same<T, __nv_bfloat16>::value, worker, n_workers);
+      pf_mma<D_>(p, bar, tmem, q_s, k_s, v_s, std::is_same<T, __nv_bfloat16>::value, ring);
   } else {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(C::REGS_SOFTMAX));
-    pf_softmax<T, D_>(p, bar, tmem, v_s, (warp - 4) >> 2, worker, n_workers);
+    pf_softmax<T, D_>(p, bar, tmem, v_s, (warp - 4) >> 2, ring);
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   if (warp == 1) tmem_dealloc(tmem, kTmemCols);
+  // every claim of this CTA is made; the last CTA out rewinds the queue for the next launch
+  if (threadIdx.x == 0 && atomicAdd(p.queue + 1, 1) == (int)gridDim.x - 1) {
+    atomicExch(p.queue, 0);
+    atomicExch(p.queue + 1, 0);
+  }
 }
 
 template <typename T, int D_>
@@ -637,7 +671,7 @@ static int launch_prefill(const PrefillParams& p, const CUtensorMap& tq, const C
   auto kern = prefill_attention_kernel<T, D_>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
   if (e != cudaSuccess) return fail(NF_ECUDA, "nf_prefill_attention: smem attribute: %s", cudaGetErrorString(e));
-  long long grid = p.sched ? p.n_lists : n_items;
+  long long grid = n_items;
   if (grid > sm_count()) grid = sm_count();
   kern<<<(int)grid, C::THREADS, C::SMEM, st>>>(p, tq, tk, tv);
   return check_launch("nf_prefill_attention");
@@ -651,7 +685,7 @@ extern "C" int nf_prefill_attention(void* out, int64_t out_row_stride, const voi
                                     int32_t num_rows, const void* k_pool, const void* v_pool, int32_t dtype, int32_t num_q_heads,
                                     int32_t num_kv_heads, int32_t head_dim, int32_t block_size, int32_t num_blocks,
                                     const int32_t* block_tables, int32_t max_blocks_per_seq, const int32_t* tiles,
-                                    int32_t n_tiles, const int32_t* schedule, int32_t n_lists, float scale,
+                                    int32_t n_tiles, const int32_t* order, int32_t* queue, float scale,
                                     int32_t* status, void* stream) {
   using namespace nf;
   if (dtype != NF_BF16 && dtype != NF_F16)
@@ -670,8 +704,7 @@ extern "C" int nf_prefill_attention(void* out, int64_t out_row_stride, const voi
   if (n_tiles == 0) return ok();
   if (!out || !q || !k_pool || !v_pool || !block_tables || !tiles || !status)
     return fail(NF_EINVAL, "nf_prefill_attention: null pointer argument");
-  if (schedule && (n_lists <= 0 || n_lists > sm_count()))
-    return fail(NF_EINVAL, "nf_prefill_attention: a schedule needs 1..%d lists (got %d)", sm_count(), n_lists);
+  if (!queue) return fail(NF_EINVAL, "nf_prefill_attention: null work queue");
   auto al = [](const void* ptr, size_t a) { return (reinterpret_cast<uintptr_t>(ptr) % a) == 0; };
   if (!al(q, 16) || !al(out, 16) || (q_row_stride * 2) % 16 || (out_row_stride * 2) % 16 || !al(tiles, 16) ||
       !al(k_pool, 16) || !al(v_pool, 16))
@@ -697,8 +730,8 @@ extern "C" int nf_prefill_attention(void* out, int64_t out_row_stride, const voi
   p.max_blocks = max_blocks_per_seq;
   p.tiles = tiles;
   p.n_tiles = n_tiles;
-  p.sched = schedule;
-  p.n_lists = n_lists;
+  p.order = order;
+  p.queue = queue;
   p.scale_log2 = scale * 1.4426950408889634f;
   p.status = status;
   const int n_items = n_tiles * num_kv_heads;

@@ -29,7 +29,6 @@ advances only when the last layer of a step has appended
 
 from __future__ import annotations
 
-import heapq
 import math
 
 import numpy as np
@@ -79,27 +78,18 @@ def seq_unit_sizes(seq_keys: np.ndarray, split: int, sms: int, fine_div: int = 4
     return sizes
 
 
-def _prefill_schedule(tiles, kv_heads: int, sms: int) -> np.ndarray:
-    """Per-worker lists of the prefill kernel's (tile, KV head) items, longest first
-    (``sms``: the number of workers, one CTA per SM).
+def _prefill_order(tiles, kv_heads: int) -> np.ndarray:
+    """The order in which the prefill kernel's CTAs take its (tile, KV head) items.
 
-    An item costs its 128-key tiles plus one (query load and epilogue); items
-    go in decreasing cost to the least-loaded CTA (longest processing time
-    first), which keeps CTAs within about one item of each other.  Returns the
-    int32 array [n_ctas + 1 offsets, items] that nf_prefill_attention reads.
+    An item costs its 128-key tiles plus one (query load and epilogue).  CTAs
+    take items from one shared queue as they free up, so listing the items by
+    decreasing cost gives the longest-processing-time-first schedule, adapted
+    at run time to the real per-item times.  Returns int32 item numbers
+    (tile * kv_heads + head).
     """
-    costs = [(pos0 + ntok + 127) // 128 + 1 for (_, _, ntok, pos0) in tiles]
-    n_items = len(tiles) * kv_heads
-    n_ctas = min(sms, n_items)
-    order = sorted(range(n_items), key=lambda it: -costs[it // kv_heads])
-    heap = [(0, b) for b in range(n_ctas)]
-    lists = [[] for _ in range(n_ctas)]
-    for it in order:
-        load, b = heapq.heappop(heap)
-        lists[b].append(it)
-        heapq.heappush(heap, (load + costs[it // kv_heads], b))
-    offs = np.cumsum([0] + [len(x) for x in lists])
-    return np.concatenate([offs, np.concatenate([np.asarray(x, np.int64) for x in lists])]).astype(np.int32)
+    costs = np.asarray([(pos0 + ntok + 127) // 128 + 1 for (_, _, ntok, pos0) in tiles], dtype=np.int64)
+    items = np.arange(len(tiles) * kv_heads, dtype=np.int64)
+    return items[np.argsort(-costs[items // kv_heads], kind="stable")].astype(np.int32)
 
 
 class StepPlan:
@@ -131,7 +121,6 @@ class StepPlan:
         self.n_tiles = 0
         self.q_heads = None
         self.sched = None
-        self.n_ctas = 0
 
     @property
     def kv_lens(self) -> np.ndarray:
@@ -189,6 +178,7 @@ class PagedKVCache:
         self.bt_dev = torch.zeros((batch_size, self.max_blocks_per_seq), dtype=torch.int32, device=self.device)
         self._synced = [(-1, 0)] * batch_size  # (table epoch, entries mirrored on the device)
         self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self._pf_queue = torch.zeros(2, dtype=torch.int32, device=self.device)  # prefill work queue (kernel-reset)
         self._meta = _DeviceBuffer(torch.int32, self.device)
         self._pos_buf = _DeviceBuffer(torch.int64, self.device)
         self._ws_partials = _DeviceBuffer(torch.float32, self.device)
@@ -357,9 +347,7 @@ class PagedKVCache:
                     tiles.append((int(slots[i]), r0 + t0, min(tt, n - t0), c + t0))
 
         n_tiles = len(tiles)
-        workers = self.sm_count  # one persistent CTA per SM
-        sched = _prefill_schedule(tiles, self.n_heads, workers) if n_tiles else np.zeros(0, np.int32)
-        n_ctas = int(min(workers, n_tiles * self.n_heads)) if n_tiles else 0  # number of lists
+        sched = _prefill_order(tiles, self.n_heads) if n_tiles else np.zeros(0, np.int32)
         off_tiles = _align4(S * 5 + P * 3)
         off_sched = off_tiles + 4 * n_tiles
         host = np.zeros(off_sched + sched.size, dtype=np.int32)
@@ -385,7 +373,6 @@ class PagedKVCache:
         plan.n_tiles = n_tiles
         plan.tiles = meta[off_tiles: off_tiles + 4 * n_tiles]
         plan.sched = meta[off_sched: off_sched + sched.size]
-        plan.n_ctas = n_ctas
         plan.seqs = meta[: S * 4]
         plan.slot_mapping = meta[off_slot: off_slot + T]
         plan.src_rows = meta[off_src: off_src + T]
@@ -471,7 +458,7 @@ class PagedKVCache:
                 self.k[layer_id].data_ptr(), self.v[layer_id].data_ptr(), _lib.dtype_code(self.dtype),
                 hq, self.n_heads, D, self.block_size, self.num_blocks, self.bt_dev.data_ptr(),
                 self.max_blocks_per_seq, plan.tiles.data_ptr(), plan.n_tiles, plan.sched.data_ptr(),
-                plan.n_ctas, float(scale), self.status.data_ptr(), stream), "nf_prefill_attention")
+                self._pf_queue.data_ptr(), float(scale), self.status.data_ptr(), stream), "nf_prefill_attention")
         if events is not None:
             events[1].record()
         if plan.decode_units:

@@ -199,7 +199,7 @@ def test_library_exports_every_declared_symbol():
     for s in syms:
         assert hasattr(lib, s), s
     assert set(_lib.EXPORTS) <= set(syms)
-    assert _lib.load().nf_abi_version() == 8
+    assert _lib.load().nf_abi_version() == 9
 
 
 def test_workspace_sizing_and_argument_errors():
@@ -238,18 +238,16 @@ def test_seq_unit_sizes_policy():
     assert (seq_unit_sizes(keys, 32, sms) >= 16).all()
 
 
-def test_prefill_schedule_covers_items_and_balances():
-    """Longest-first lists: every (tile, KV head) item once; CTA loads within one item of each other."""
+def test_prefill_order_covers_items_longest_first():
+    """The prefill queue order: every (tile, KV head) item once, by decreasing key tiles."""
     import numpy as np
-    from nifre_b200.paged_kv_cache import _prefill_schedule
+    from nifre_b200.paged_kv_cache import _prefill_order
     rng = np.random.default_rng(0)
     tiles = [(0, 64 * t, 64, int(p) + 64 * t) for t, p in enumerate(rng.integers(0, 2048, size=60))]
-    H, sms = 8, 148
-    arr = _prefill_schedule(tiles, H, sms)
-    n_ctas = min(sms, len(tiles) * H)
-    offs, items = arr[: n_ctas + 1], arr[n_ctas + 1:]
-    assert offs[0] == 0 and offs[-1] == len(items) == len(tiles) * H
-    assert sorted(items.tolist()) == list(range(len(tiles) * H))
+    H = 8
+    order = _prefill_order(tiles, H)
+    assert order.dtype == np.int32
+    assert sorted(order.tolist()) == list(range(len(tiles) * H))
     cost = [(p + n + 127) // 128 + 1 for (_, _, n, p) in tiles]
-    loads = [sum(cost[i // H] for i in items[offs[b]:offs[b + 1]]) for b in range(n_ctas)]
-    assert max(loads) - min(loads) <= max(cost)
+    c = [cost[i // H] for i in order.tolist()]
+    assert all(a >= b for a, b in zip(c, c[1:]))
