@@ -204,8 +204,9 @@ int nf_prefill_attention(void* out, int64_t out_row_stride, const void* q, int64
                          const int32_t* order, int32_t* queue, float scale,
                          int32_t* status, void* stream);
 
-/* Query rows (tokens x query heads per KV head) of one nf_prefill_attention work item: 256. */
-int nf_prefill_tile_rows(void);
+/* Query rows (tokens x query heads per KV head) of one nf_prefill_attention work item for this
+ * head_dim: 128 for 64 (one half per CTA, two CTAs per SM), 256 for 128 (two halves sharing K/V). */
+int nf_prefill_tile_rows(int32_t head_dim);
 
 /*
  * nf_paged_attention_noalloc: nf_paged_attention without a caller workspace.

@@ -38,7 +38,7 @@ _SIGNATURES = {
     "nf_abi_version": ([], ctypes.c_int),
     "nf_last_attention_path": ([], ctypes.c_int),
     "nf_selftest_umma": ([_P, _P, _P, _I32, _I32, _I32, _P, _P], ctypes.c_int),
-    "nf_prefill_tile_rows": ([], ctypes.c_int),
+    "nf_prefill_tile_rows": ([_I32], ctypes.c_int),
     "nf_prefill_attention": ([_P, _I64, _P, _I64, _I32, _P, _P, _I32, _I32, _I32, _I32, _I32, _I32,
                               _P, _I32, _P, _I32, _P, _P, ctypes.c_float, _P, _P], ctypes.c_int),
     "nf_pack_step": ([_P, _I32, _P, _I32, _P, _I32, _I32, _I32, _I32, _I32, _P,

@@ -54,7 +54,7 @@ struct PrefillParams {
   const char* q;
   long long q_stride;
   int rows;                             // rows of q and out
-  int Hq, Hkv, G, TT, bs, num_blocks;  // TT: tokens per 128-row half
+  int Hq, Hkv, G, TT, NH, bs, num_blocks;  // TT: tokens per 128-row half; NH: halves per item
   const int* bt;
   int max_blocks;
   const int* tiles;  // [n_tiles] x {slot, q_row0, ntok, pos0}
@@ -66,29 +66,42 @@ struct PrefillParams {
 };
 
 constexpr float kPfNegInf = -INFINITY;
-constexpr int kPfRows = 256;  // query rows of a work item
+#ifndef NF_PF_HALVES_64
+#define NF_PF_HALVES_64 2
+#endif
+// 128-row query halves per work item (and CTA): head_dim 64 runs one half per
+// CTA and two CTAs per SM, whose softmax warps then drift out of step and
+// overlap one another's exponentials with their loads and stores; head_dim
+// 128 (tensor work per tile doubled, tensor memory full) runs two halves that
+// share one K/V stream.
+__host__ __device__ constexpr int pf_halves(int d) { return d == 64 ? NF_PF_HALVES_64 : 2; }
 
-template <int D_>
+template <int D_, int NH = pf_halves(D_)>
 struct PfCfg {
   static constexpr uint32_t TILE = 128 * D_ * 2;  // a 128-row Q half, or a 128-key K or V tile
-  static constexpr int QST = D_ == 64 ? 2 : 1;    // Q ring (both halves of an item per stage)
-  static constexpr int KST = D_ == 64 ? 4 : 2;    // K ring
-  static constexpr int VST = D_ == 64 ? 5 : 3;    // V ring (held one tile longer than K)
+  static constexpr int NH_ = NH;
+  static constexpr int MINB = NH == 1 ? 2 : 1;    // CTAs per SM
+  static constexpr int QST = (D_ == 64 || NH == 1) ? 2 : 1;           // Q ring (an item's halves per stage)
+  static constexpr int KST = NH == 1 ? 2 : (D_ == 64 ? 4 : 2);        // K ring
+  static constexpr int VST = NH == 1 ? 2 : (D_ == 64 ? 5 : 3);        // V ring (held one tile longer than K)
   static constexpr bool P_ALIAS = D_ == 128;      // P_h over the first 64 columns of S_h
   static constexpr uint32_t Q_OFF = 1024;         // after the barrier header
-  static constexpr uint32_t K_OFF = Q_OFF + QST * 2 * TILE;
+  static constexpr uint32_t K_OFF = Q_OFF + QST * NH * TILE;
   static constexpr uint32_t V_OFF = K_OFF + KST * TILE;
   static constexpr uint32_t SMEM = 1024 + V_OFF + VST * TILE;  // + alignment slack
-  static constexpr int THREADS = 384;             // warp 0 producer, 1 MMA, 4-7 half 0, 8-11 half 1
-  // registers per thread: 168 at launch (384 x 168 <= 64K); the first
-  // warpgroup gives back to 72 and the softmax warpgroups take 216, which
-  // adds up to the launch total: 72 x 128 + 216 x 256 = 384 x 168
-  static constexpr int REGS_CTRL = 72, REGS_SOFTMAX = 216;
+  static constexpr int THREADS = 128 * (1 + NH);  // warp 0 producer, 1 MMA, 4-7 half 0, 8-11 half 1
+  // registers per thread at launch: 64K / (threads x CTAs per SM), rounded
+  // to 8 (168 for two halves, 128 for one); the first warpgroup gives back
+  // to REGS_CTRL and the softmax warpgroups take REGS_SOFTMAX, adding up to
+  // the launch total (checked against the compiled count before a launch)
+  static constexpr int LAUNCH_REGS = (65536 / (THREADS * MINB)) / 8 * 8;
+  static constexpr int REGS_CTRL = NH == 1 ? 64 : 72, REGS_SOFTMAX = NH == 1 ? 192 : 216;
+  static_assert(REGS_CTRL * 128 + REGS_SOFTMAX * 128 * NH <= LAUNCH_REGS * THREADS, "register split exceeds the launch");
+  static constexpr uint32_t TMEM_COLS = NH == 1 ? 256 : 512;
   static __device__ __forceinline__ uint32_t s_col(int h) { return h * 128; }
-  static __device__ __forceinline__ uint32_t o_col(int h) { return 256 + h * D_; }
-  static __device__ __forceinline__ uint32_t p_col(int h) { return P_ALIAS ? h * 128 : 384 + h * 64; }
+  static __device__ __forceinline__ uint32_t o_col(int h) { return NH * 128 + h * D_; }
+  static __device__ __forceinline__ uint32_t p_col(int h) { return P_ALIAS ? h * 128 : NH * (128 + D_) + h * 64; }
 };
-constexpr uint32_t kTmemCols = 512;
 
 // Barriers at the start of the header: k_full[8] 0, k_empty[8] 64,
 // v_full[8] 128, v_empty[8] 192, then per half s_full 256, s_free 272,
@@ -114,7 +127,7 @@ struct PfBars {
 constexpr uint32_t kPfTmemPtr = 512;
 constexpr uint32_t kPfItemSlots = 640;
 constexpr int kPfItemRing = 4;
-constexpr int kPfItemReaders = 9;  // the MMA warp and the eight softmax warps
+
 
 // ---------------------------------------------------------------- softmax arithmetic
 // Pairs of fp32 values in one 64-bit register, for the packed fp32x2
@@ -249,7 +262,7 @@ struct PfItem {
   int kvh, nkeys, nkt, n_half, nkt_h[2];
   __device__ PfItem(const PrefillParams& p, int item, int4 t) : tl(t) {
     kvh = item % p.Hkv;
-    const int ntok = min(tl.z, 2 * p.TT);
+    const int ntok = min(tl.z, p.NH * p.TT);
     nkeys = tl.w + ntok;
     nkt = (nkeys + 127) >> 7;
     n_half = ntok > p.TT ? 2 : 1;
@@ -317,7 +330,7 @@ __device__ void pf_producer(const PrefillParams& p, const CUtensorMap* tq, const
     __syncwarp();
     if (lane < nq) {
       const int h = lane / NDH, dh = lane - h * NDH;
-      const uint32_t dst = q_s + (qr.st * 2 + h) * C::TILE + dh * 128 * 128;
+      const uint32_t dst = q_s + (qr.st * C::NH_ + h) * C::TILE + dh * 128 * 128;
       const int row0 = w.tl.y + h * p.TT;
       if constexpr (D_ == 64)
         tma_load_3d(dst, tq, 0, w.kvh * p.G, row0, bar.q_full(qr.st), pol_q);
@@ -381,7 +394,7 @@ __device__ void pf_mma(const PrefillParams& p, const PfBars& bar, uint32_t tmem,
     __syncwarp();
   };
   auto issue_s = [&](int h, int kst) {
-    const uint64_t a0 = dq + (uint64_t)((qr.st * 2 + h) * (C::TILE >> 4)), b0 = dk + (uint64_t)(kst * (C::TILE >> 4));
+    const uint64_t a0 = dq + (uint64_t)((qr.st * C::NH_ + h) * (C::TILE >> 4)), b0 = dk + (uint64_t)(kst * (C::TILE >> 4));
     const uint32_t d = tmem + C::s_col(h);
     if (leader) {
 #pragma unroll
@@ -402,7 +415,7 @@ __device__ void pf_mma(const PrefillParams& p, const PfBars& bar, uint32_t tmem,
     for (int j = 0; j < w.nkt; ++j) {
       if (!mbar_wait(bar.k_full(kr.st), kr.ph, p.status)) return;
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
+      for (int h = 0; h < C::NH_; ++h) {
         if (C::P_ALIAS && w.active(h, j - 1)) {
           // P_h of tile j-1 sits in S_h: consume it before S_h is rewritten
           if (!wait_p(h)) return;
@@ -421,7 +434,7 @@ __device__ void pf_mma(const PrefillParams& p, const PfBars& bar, uint32_t tmem,
       if (j > 0) {
         if (!C::P_ALIAS) {
 #pragma unroll
-          for (int h = 0; h < 2; ++h) {
+          for (int h = 0; h < C::NH_; ++h) {
             if (!w.active(h, j - 1)) continue;
             if (!wait_p(h)) return;
             issue_pv(h, vprev, j == 1);
@@ -440,10 +453,10 @@ __device__ void pf_mma(const PrefillParams& p, const PfBars& bar, uint32_t tmem,
     // half's warpgroup, so both halves' P must be in before either P V
     const int jl = w.nkt - 1;
 #pragma unroll
-    for (int h = 0; h < 2; ++h)
+    for (int h = 0; h < C::NH_; ++h)
       if (w.active(h, jl) && !wait_p(h)) return;
 #pragma unroll
-    for (int h = 0; h < 2; ++h)
+    for (int h = 0; h < C::NH_; ++h)
       if (w.active(h, jl)) issue_pv(h, vprev, jl == 0);
     if (leader) umma_commit(bar.v_empty(vprev));
   }
@@ -467,13 +480,13 @@ __device__ void pf_softmax(const PrefillParams& p, const PfBars& bar, uint32_t t
   int4 itl;
   while (ring.next(it, itl, p.status)) {
     const PfItem w(p, it, itl);
-    if (h == 0 && w.tl.z > 2 * p.TT && threadIdx.x == 128) atomicOr(p.status, NF_STATUS_BAD_TILE);
+    if (h == 0 && w.tl.z > p.NH * p.TT && threadIdx.x == 128) atomicOr(p.status, NF_STATUS_BAD_TILE);
     const Ring vlast = vr.ahead(w.nkt - 1, C::VST);  // V stage of the item's last tile
     vr = vr.ahead(w.nkt, C::VST);
     if (h >= w.n_half) continue;
     const int nkt = w.nkt_h[h];
     const int tok = h * p.TT + row / G, hd = row % G;
-    const bool valid = tok < min(w.tl.z, 2 * p.TT) && w.tl.y + tok < p.rows;
+    const bool valid = tok < min(w.tl.z, p.NH * p.TT) && w.tl.y + tok < p.rows;
     const int qpos = w.tl.w + tok;
     float m = kPfNegInf, l = 0.f;
     for (int j = 0; j < nkt; ++j) {
@@ -601,7 +614,7 @@ __device__ void pf_softmax(const PrefillParams& p, const PfBars& bar, uint32_t t
 }
 
 template <typename T, int D_>
-__global__ void __launch_bounds__(PfCfg<D_>::THREADS, 1)
+__global__ void __launch_bounds__(PfCfg<D_>::THREADS, PfCfg<D_>::MINB)
     prefill_attention_kernel(const PrefillParams p, const __grid_constant__ CUtensorMap tq,
                              const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv) {
   using C = PfCfg<D_>;
@@ -631,18 +644,17 @@ __global__ void __launch_bounds__(PfCfg<D_>::THREADS, 1)
     }
     for (int s = 0; s < kPfItemRing; ++s) {
       mbar_init(bar.item_full(s), 1);
-      mbar_init(bar.item_empty(s), kPfItemReaders);
+      mbar_init(bar.item_empty(s), 1 + 4 * C::NH_);  // the MMA warp and the softmax warps
     }
     fence_mbar_init();
   }
-  if (warp == 1) tmem_alloc(hdr + kPfTmemPtr, kTmemCols);
+  if (warp == 1) tmem_alloc(hdr + kPfTmemPtr, C::TMEM_COLS);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(base + kPfTmemPtr);
   const uint32_t q_s = hdr + C::Q_OFF, k_s = hdr + C::K_OFF, v_s = hdr + C::V_OFF;
   PfItemRing ring(bar, base);
-  static_assert(C::REGS_CTRL * 128 + C::REGS_SOFTMAX * 256 <= 168 * C::THREADS, "register split exceeds the launch");
   if (warp < 4) {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(C::REGS_CTRL));
     if (warp == 0)
@@ -656,7 +668,7 @@ __global__ void __launch_bounds__(PfCfg<D_>::THREADS, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 1) tmem_dealloc(tmem, kTmemCols);
+  if (warp == 1) tmem_dealloc(tmem, C::TMEM_COLS);
   // every claim of this CTA is made; the last CTA out rewinds the queue for the next launch
   if (threadIdx.x == 0 && atomicAdd(p.queue + 1, 1) == (int)gridDim.x - 1) {
     atomicExch(p.queue, 0);
@@ -671,15 +683,22 @@ static int launch_prefill(const PrefillParams& p, const CUtensorMap& tq, const C
   auto kern = prefill_attention_kernel<T, D_>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
   if (e != cudaSuccess) return fail(NF_ECUDA, "nf_prefill_attention: smem attribute: %s", cudaGetErrorString(e));
+  // setmaxnreg moves registers between warpgroups within the launch total:
+  // refuse a build whose register count would not cover the split
+  cudaFuncAttributes fa;
+  if (cudaFuncGetAttributes(&fa, kern) != cudaSuccess ||
+      C::REGS_CTRL * 128 + C::REGS_SOFTMAX * 128 * C::NH_ > fa.numRegs * C::THREADS)
+    return fail(NF_EUNSUPPORTED, "nf_prefill_attention: kernel built with %d registers per thread, the warpgroup "
+                "split needs %d", fa.numRegs, C::LAUNCH_REGS);
   long long grid = n_items;
-  if (grid > sm_count()) grid = sm_count();
+  if (grid > (long long)sm_count() * C::MINB) grid = (long long)sm_count() * C::MINB;
   kern<<<(int)grid, C::THREADS, C::SMEM, st>>>(p, tq, tk, tv);
   return check_launch("nf_prefill_attention");
 }
 
 }  // namespace nf
 
-extern "C" int nf_prefill_tile_rows(void) { return nf::kPfRows; }
+extern "C" int nf_prefill_tile_rows(int32_t head_dim) { return 128 * nf::pf_halves(head_dim); }
 
 extern "C" int nf_prefill_attention(void* out, int64_t out_row_stride, const void* q, int64_t q_row_stride,
                                     int32_t num_rows, const void* k_pool, const void* v_pool, int32_t dtype, int32_t num_q_heads,
@@ -724,6 +743,7 @@ extern "C" int nf_prefill_attention(void* out, int64_t out_row_stride, const voi
   p.Hkv = num_kv_heads;
   p.G = G;
   p.TT = 128 / G;
+  p.NH = pf_halves(head_dim);
   p.bs = block_size;
   p.num_blocks = num_blocks;
   p.bt = block_tables;

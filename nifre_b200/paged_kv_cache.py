@@ -340,7 +340,7 @@ class PagedKVCache:
         max_units = max(1, n_units)
         tiles = []
         if routed.any():
-            tt = _lib.load().nf_prefill_tile_rows() // (q_heads // self.n_heads)  # query tokens per work item
+            tt = _lib.load().nf_prefill_tile_rows(self.head_dim) // (q_heads // self.n_heads)  # tokens per item
             for i in np.flatnonzero(routed).tolist():
                 n, c, r0 = int(q_lens[i]), int(ctx[i]), int(q_starts[i])
                 for t0 in reversed(range(0, n, tt)):  # most keys first
