@@ -1,5 +1,6 @@
 // Tensor-map (TMA) copies of key/value blocks from the paged pools into
-// shared memory, shared by the decode and prefill kernels.  No multicast.
+// shared memory, shared by the decode and prefill kernels.  Every copy lands in
+// the issuing CTA only.
 #pragma once
 
 #include <cuda.h>
