@@ -430,44 +430,17 @@ def _run_decode_timed(args, cache, B, ctx, world, rank, local, dev, dist, shard,
         hk_host.copy_(k_all.view(L, B, 1, -1).cpu())
         hv_host.copy_(v_all.view(L, B, 1, -1).cpu())
 
-        # inputs go up on a copy stream one layer ahead (two device buffers),
-        # outputs come down on another, so the transfers overlap the kernels
-        h2d, d2h = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
-        dq = [torch.empty(B, 1, hq * D, device=dev, dtype=dt) for _ in range(2)]
-        dk = [torch.empty(B, 1, hkv * D, device=dev, dtype=dt) for _ in range(2)]
-        dv = [torch.empty(B, 1, hkv * D, device=dev, dtype=dt) for _ in range(2)]
-        freed = [torch.cuda.Event(), torch.cuda.Event()]
-        for e in freed:
-            e.record(stream)
-
-        def upload(layer, buf):
-            with torch.cuda.stream(h2d):
-                h2d.wait_event(freed[buf])  # the attention that read this buffer two layers ago is done
-                dq[buf].copy_(hq_host[layer], non_blocking=True)
-                dk[buf].copy_(hk_host[layer], non_blocking=True)
-                dv[buf].copy_(hv_host[layer], non_blocking=True)
-                ev = torch.cuda.Event()
-                ev.record(h2d)
-            return ev
-
         def e2e_step():
-            ready = upload(0, 0)
             for layer in range(L):
-                buf = layer & 1
-                nxt = upload(layer + 1, buf ^ 1) if layer + 1 < L else None
-                stream.wait_event(ready)
-                o = attn(dq[buf], dk[buf], dv[buf], kv_cache=cache, layer_id=layer, cache_batch_indices=slots)
-                freed[buf].record(stream)
+                qd = hq_host[layer].to(dev, non_blocking=True)
+                kd = hk_host[layer].to(dev, non_blocking=True)
+                vd = hv_host[layer].to(dev, non_blocking=True)
+                o = attn(qd, kd, vd, kv_cache=cache, layer_id=layer, cache_batch_indices=slots)
                 if world > 1:
-                    o = shard.gather(o.view(B, -1), buffer=gathered).view(B, 1, world * hq * D)[:, :, : hq * D]
-                done = torch.cuda.Event()
-                done.record(stream)
-                with torch.cuda.stream(d2h):
-                    d2h.wait_event(done)
+                    o = shard.gather(o.view(B, -1), buffer=gathered).view(B, 1, world * hq * D)
+                    ho_host[layer].copy_(o[:, :, : hq * D], non_blocking=True)
+                else:
                     ho_host[layer].copy_(o, non_blocking=True)
-                    o.record_stream(d2h)
-                ready = nxt
-            stream.wait_stream(d2h)  # the step ends when its last output is on the host
 
         e2e_step()
         torch.cuda.synchronize()
@@ -490,9 +463,7 @@ def _run_decode_timed(args, cache, B, ctx, world, rank, local, dev, dist, shard,
         e2e = {"value": B * n_e2e / (ems * 1e-3) * L / L_model, "unit": "tok/s",
                "h2d_bytes_per_step": L * B * (hq + 2 * hkv) * D * 2,
                "d2h_bytes_per_step": L * B * hq * D * 2,
-               "ms_per_step": ems / n_e2e,
-               "path": "nifre_b200.Attention.forward per layer, pinned host q/k/v copied up one layer ahead "
-                       "and outputs copied down on side streams"}
+               "ms_per_step": ems / n_e2e, "path": "nifre_b200.Attention.forward per layer, pinned host q/k/v"}
 
     if rank == 0:
         cpu = None
