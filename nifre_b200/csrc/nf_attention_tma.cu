@@ -472,14 +472,17 @@ int launch_attention_tma(AttnParams p, int dtype, long long want, cudaStream_t s
   // head_dim 128: two CTAs per SM with up to 4 KV heads and 3 stages of 36 KB
   // each.  Either way about four stages (128 KB) per SM are in flight while
   // the consumers hold the ones they compute on, and 8 consumer warps share
-  // the SM.
-  const int max_hg = p.D == 64 ? 8 : 4, ctas = p.D == 64 ? 1 : 2;
+  // the SM.  With fewer KV heads (a shard of the heads on each of several
+  // GPUs) the CTAs get smaller and more of them share an SM, so that 8
+  // consumer warps still stream per SM.
+  const int max_hg = p.D == 64 ? 8 : 4;
   int hg = 0;
   for (int h = p.Hkv < max_hg ? p.Hkv : max_hg; h >= 1; --h)
     if (p.Hkv % h == 0) {
       hg = h;
       break;
     }
+  const int ctas = (p.D == 64 ? 1 : 2) * (max_hg / hg);
   const int HB = p.D * 2;
   const int box = hg * 16 * HB, qb = hg * p.G * HB;
   const int stage = ((2 * box + qb + 1023) / 1024) * 1024;
