@@ -123,7 +123,7 @@ def _random_cache(Hq, Hkv, D, bs, ctx_lens, dtype, seed, L=1, shuffle=True, room
 
 @pytest.mark.parametrize("split", [None, 128])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
-@pytest.mark.parametrize("D,Hq,Hkv", [(64, 32, 8), (128, 32, 8), (64, 12, 12), (128, 8, 1), (128, 16, 2)])
+@pytest.mark.parametrize("D,Hq,Hkv", [(64, 32, 8), (128, 32, 8), (64, 12, 12), (128, 8, 1), (128, 16, 2), (64, 4, 1), (64, 8, 2)])
 def test_decode_vs_oracle(dtype, D, Hq, Hkv, split):
     ctx = [1, 15, 16, 17, 100, 513, 1000, 2049]
     cache, g = _random_cache(Hq, Hkv, D, 16, ctx, dtype, seed=D + Hq)
