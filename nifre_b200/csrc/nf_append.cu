@@ -61,6 +61,7 @@ template <> struct Vec8<__nv_bfloat16> : Vec8Half<__nv_bfloat16> {};
 // Same-type rows: raw 16-byte copies (bit exact by construction).
 template <typename T>
 __global__ void append_copy_kernel(const AppendParams p) {
+  pdl_launch_dependents();
   constexpr int V = 16 / sizeof(T);
   const int chunks = p.row_elems / V;
   const long long total = (long long)p.n_tokens * 2 * chunks;
@@ -89,6 +90,7 @@ __global__ void append_copy_kernel(const AppendParams p) {
 // round-to-nearest-even per element like torch's copy_.
 template <typename Ts, typename Td>
 __global__ void append_convert_kernel(const AppendParams p) {
+  pdl_launch_dependents();
   const int chunks = p.row_elems / 8;
   const long long total = (long long)p.n_tokens * 2 * chunks;
   for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < total;
@@ -117,6 +119,7 @@ __global__ void append_convert_kernel(const AppendParams p) {
 // Rows whose length or alignment does not allow vectors: one element per thread.
 template <typename Ts, typename Td>
 __global__ void append_scalar_kernel(const AppendParams p) {
+  pdl_launch_dependents();
   const long long total = (long long)p.n_tokens * 2 * p.row_elems;
   for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < total;
        idx += (long long)gridDim.x * blockDim.x) {

@@ -365,6 +365,9 @@ __global__ void __launch_bounds__(kTmaMaxThreads, 1) paged_attention_tma_kernel(
     cta_done = 0;
   }
   __syncthreads();
+  // the KV append (or pack) before this launch may still run: everything
+  // above touches only this CTA's shared memory
+  pdl_wait();
   const int n_units = min(__ldg(p.counts + 1), p.max_units);
   const int total = n_units * p.n_hg;
   if (warp < p.HG) {
@@ -525,12 +528,21 @@ int launch_attention_tma(AttnParams p, int dtype, long long want, cudaStream_t s
   cfg.blockDim = dim3(threads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  // programmatic stream serialization: the launch overlaps the kernel before
+  // it (the KV append), whose writes the kernel waits for in pdl_wait()
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeCooperative;
   attr[0].val.cooperative = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   e = cudaLaunchKernelEx(&cfg, kern, p, tk, tv);
+  if (e != cudaSuccess) {  // not available with this launch: plain stream order
+    (void)cudaGetLastError();
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, kern, p, tk, tv);
+  }
   if (e != cudaSuccess) return fail(NF_ECUDA, "nf_paged_attention: launch: %s", cudaGetErrorString(e));
   *path = permuted ? 1 : 2;
   return check_launch("nf_paged_attention");

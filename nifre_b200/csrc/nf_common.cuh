@@ -78,6 +78,15 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Programmatic dependent launch.  A kernel launched with programmatic stream
+// serialization may start while the kernel before it on the stream runs; it
+// calls pdl_wait() before its first read of anything that kernel writes,
+// which returns once that kernel has completed and its writes are visible
+// (immediately when there is no such launch).  pdl_launch_dependents() lets
+// the next such kernel start launching now.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }
+
 // Time limit of every pipeline wait: about two seconds at the B200's top SM
 // clock.  A wait that runs out flags NF_STATUS_WAIT_TIMEOUT and returns false;
 // the caller then leaves its loops, so no kernel can spin forever.
