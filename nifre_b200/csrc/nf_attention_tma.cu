@@ -81,6 +81,16 @@ __device__ int tma_producer(const AttnParams& p, const CUtensorMap* tk, const CU
     ra = __ldg(urec + 2 * (w / p.n_hg));
     rb = __ldg(urec + 2 * (w / p.n_hg) + 1);
   }
+  // This launch may overlap the kernel before it on the stream (the KV
+  // append of this layer, with programmatic stream serialization).  The
+  // ticket, unit records and block tables come from the step's pack, which
+  // completed before that kernel began; only the pools, where the append
+  // writes the new keys and values, must wait for it.
+  if (w < total) {
+    const int lb = rb.x / p.bs;
+    if (lb < p.max_blocks) asm volatile("prefetch.global.L1 [%0];" ::"l"(p.bt + (long long)ra.y * p.max_blocks + lb));
+  }
+  pdl_wait();
   int taken = 0;
   while (w < total) {
     ++taken;
@@ -365,9 +375,6 @@ __global__ void __launch_bounds__(kTmaMaxThreads, 1) paged_attention_tma_kernel(
     cta_done = 0;
   }
   __syncthreads();
-  // the KV append (or pack) before this launch may still run: everything
-  // above touches only this CTA's shared memory
-  pdl_wait();
   const int n_units = min(__ldg(p.counts + 1), p.max_units);
   const int total = n_units * p.n_hg;
   if (warp < p.HG) {
