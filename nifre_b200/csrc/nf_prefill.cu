@@ -497,6 +497,8 @@ __device__ void pf_softmax(const PrefillParams& p, const PfBars& bar, uint32_t t
 #pragma unroll
       for (int c = 0; c < 4; ++c) tmem_ld32(s_addr + c * 32, *reinterpret_cast<uint32_t(*)[32]>(x + 32 * c));
       tmem_wait_ld();
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_reg_fence(*reinterpret_cast<uint32_t(*)[32]>(x + 32 * c));
       if (!C::P_ALIAS) {  // S_h is in registers: the next S_h may be computed
         tc_fence_before();
         __syncwarp();
@@ -560,6 +562,7 @@ __device__ void pf_softmax(const PrefillParams& p, const PfBars& bar, uint32_t t
           uint32_t o[32];
           tmem_ld32(o_addr + c * 32, o);
           tmem_wait_ld();
+          tmem_reg_fence(o);
 #pragma unroll
           for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
           tmem_st32(o_addr + c * 32, o);
@@ -599,6 +602,7 @@ __device__ void pf_softmax(const PrefillParams& p, const PfBars& bar, uint32_t t
       uint32_t o[32];
       tmem_ld32(o_addr + c * 32, o);
       tmem_wait_ld();
+      tmem_reg_fence(o);
       if (valid) {
         uint32_t wv[16];
 #pragma unroll

@@ -101,6 +101,7 @@ __global__ void __launch_bounds__(128) umma_selftest_kernel(const __nv_bfloat16*
       uint32_t r[32];
       tmem_ld32(tbase + ((uint32_t)(warp * 32) << 16) + c0, r);
       tmem_wait_ld();
+      tmem_reg_fence(r);
 #pragma unroll
       for (int j = 0; j < 32; ++j) C[row * N + c0 + j] = __uint_as_float(r[j]);
     }
