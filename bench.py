@@ -687,11 +687,11 @@ def run_mixed(args):
     def step(record=False, host=None):
         rewind()
         p = cache.plan(slots, q_lens, starts, q_heads=hq)
+        if host is not None:  # the step's inputs up in one copy per tensor
+            qa, ka, va = (host[i].to(dev, non_blocking=True) for i in range(3))
         for layer in range(L):
             if host is not None:
-                qd = host[0][layer].to(dev, non_blocking=True)
-                kd = host[1][layer].to(dev, non_blocking=True)
-                vd = host[2][layer].to(dev, non_blocking=True)
+                qd, kd, vd = qa[layer], ka[layer], va[layer]
             else:
                 qd, kd, vd = q_all[layer], k_all[layer], v_all[layer]
             cache.append_step(layer, kd, vd, p)
@@ -703,8 +703,10 @@ def run_mixed(args):
             o = out_loc[layer]
             if world > 1:
                 o = shard.gather(o, buffer=gathered)
-            if host is not None:
-                host[3][layer].copy_(o[:, : hq * D] if world > 1 else o, non_blocking=True)
+                if host is not None:
+                    host[3][layer].copy_(o[:, : hq * D], non_blocking=True)
+        if host is not None and world == 1:  # the step's outputs down in one copy
+            host[3].copy_(out_loc, non_blocking=True)
         return p
 
     for _ in range(args.warmup):
@@ -766,7 +768,9 @@ def run_mixed(args):
         n = args.e2e_steps - 1
         e2e = {"value": T * n / (ems * 1e-3), "unit": "tok/s",
                "h2d_bytes_per_step": L * T * (hq + 2 * hkv) * D * 2, "d2h_bytes_per_step": L * T * hq * world * D * 2,
-               "ms_per_step": ems / n, "path": "PagedKVCache.plan/append_step/attention_step, pinned host q/k/v"}
+               "ms_per_step": ems / n,
+               "path": "PagedKVCache.plan/append_step/attention_step; the step's q/k/v up from pinned host memory in "
+                       "one copy per tensor, outputs down in one"}
         cache.check_status()
     if rank == 0:
         cpu = None
