@@ -255,9 +255,22 @@ class PagedKVCache:
             self._sm_count = torch.cuda.get_device_properties(self.device).multi_processor_count
         return self._sm_count
 
+    @property
+    def decode_workers(self) -> int:
+        """Decode CTAs the attention kernel keeps resident: one group of KV heads each.
+
+        A CTA covers up to 8 KV heads (4 for head_dim 128); with fewer heads in
+        the pool (one GPU's shard of the heads) the kernel runs proportionally
+        more, smaller CTAs per SM, and the split-K units are sized for them.
+        """
+        max_hg = 8 if self.head_dim == 64 else 4
+        hg = max(h for h in range(1, min(self.n_heads, max_hg) + 1) if self.n_heads % h == 0)
+        return self.sm_count * (max_hg // hg)
+
     def split_for(self, total_keys: int, units_per_sm: int = 4) -> int:
-        """Keys per split-K unit: ~units_per_sm units per SM, a multiple of 128."""
-        s = total_keys / max(1, units_per_sm * self.sm_count)
+        """Keys per split-K unit: ~units_per_sm units per SM (per decode CTA when the
+        pool holds few KV heads), a multiple of 128."""
+        s = total_keys / max(1, units_per_sm * self.decode_workers)
         return max(128, int(math.ceil(s / 128.0)) * 128)
 
     # sequences with at least this many new tokens go to the tensor-core prefill kernel
@@ -334,7 +347,7 @@ class PagedKVCache:
         seq_keys = q_lens * (ctx + 1) + q_lens * (q_lens - 1) // 2
         seq_split = np.zeros(S, dtype=np.int32)  # 0: the prefill kernel serves the sequence
         if dec.any():
-            seq_split[dec] = (seq_unit_sizes(seq_keys[dec], split, self.sm_count) if fine_tail else split)
+            seq_split[dec] = (seq_unit_sizes(seq_keys[dec], split, self.decode_workers) if fine_tail else split)
         item_split = np.repeat(seq_split.astype(np.int64), q_lens)
         n_units = int(((kv_dec + item_split[item_split > 0] - 1) // item_split[item_split > 0]).sum())
         max_units = max(1, n_units)

@@ -150,7 +150,7 @@ def test_pack_unit_list():
     import numpy as np
     rng = np.random.default_rng(3)
     ctx = rng.integers(1, 3000, size=64).tolist()
-    cache, _ = _random_cache(8, 2, 64, 16, ctx, torch.bfloat16, seed=3)
+    cache, _ = _random_cache(32, 8, 64, 16, ctx, torch.bfloat16, seed=3)  # a full KV-head group per CTA
     B, split = len(ctx), 128
     plan = cache.plan(list(range(B)), [1] * B, list(range(B)), split=split)
     kv = np.array(ctx) + 1
