@@ -363,10 +363,11 @@ def _run_decode_timed(args, cache, B, ctx, world, rank, local, dev, dist, shard,
     stream = torch.cuda.current_stream(dev)
     att_events = []
 
-    def step(record=False):
+    def step(rec_layer=-1):
         p = cache.plan(slots, ones, rows)
         for layer in range(L):
             cache.append_step(layer, k_all[layer], v_all[layer], p)
+            record = layer == rec_layer
             if record:
                 e0 = torch.cuda.Event(enable_timing=True)
                 e1 = torch.cuda.Event(enable_timing=True)
@@ -392,8 +393,11 @@ def _run_decode_timed(args, cache, B, ctx, world, rank, local, dev, dist, shard,
     e_start = torch.cuda.Event(enable_timing=True)
     e_end = torch.cuda.Event(enable_timing=True)
     e_start.record(stream)
-    for _ in range(args.steps):
-        step(record=True)
+    # the attention kernel is timed by events around one layer per step, a
+    # different layer each step: events between every pair of kernels would
+    # add a drain per event to the step
+    for s in range(args.steps):
+        step(rec_layer=s % L)
     e_end.record(stream)
     torch.cuda.synchronize()
     clk = clocks.stop()
@@ -684,7 +688,7 @@ def run_mixed(args):
         for i in range(P):
             cache._set_pos(i, prefix[i])
 
-    def step(record=False, host=None):
+    def step(rec_layer=-1, host=None):
         rewind()
         p = cache.plan(slots, q_lens, starts, q_heads=hq)
         if host is not None:  # the step's inputs up in one copy per tensor
@@ -696,7 +700,7 @@ def run_mixed(args):
                 qd, kd, vd = q_all[layer], k_all[layer], v_all[layer]
             cache.append_step(layer, kd, vd, p)
             ev = None
-            if record:
+            if layer == rec_layer:
                 ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
                 kev.append((ev, p))
             cache.attention_step(layer, qd, p, out_loc[layer], events=ev)
@@ -722,8 +726,12 @@ def run_mixed(args):
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    for _ in range(args.steps):
-        p_last = step(record=True)
+    # the kernels are timed by events around one layer per step, a different
+    # layer each step (events between every pair of kernels would add a
+    # drain per event to the step, and keep the decode from starting beside
+    # the KV append)
+    for s in range(args.steps):
+        step(rec_layer=s % L)
     e1.record(stream)
     torch.cuda.synchronize()
     clk = clocks.stop()
