@@ -50,7 +50,7 @@ class Attention(nn.Module):
         if lid is None:
             raise ValueError("layer_id is required when kv_cache is set")
         if not isinstance(kv_cache, PagedKVCache):
-            raise TypeError("nifre_b200.Attention runs on nifre_b200.PagedKVCache (or KVCache)")
+            raise TypeError("nifre_b200.Attention runs on nifre_b200.PagedKVCache or nifre_b200.KVCache")
         return self._forward_with_cache(q, k, v, kv_cache, lid, input_lens, cache_batch_indices)
 
     # ------------------------------------------------------------------ cached path

@@ -4,6 +4,7 @@ from __future__ import annotations
 
 import torch
 
+from .kv_cache import KVCache
 from .paged_kv_cache import PagedKVCache
 
 
@@ -14,6 +15,13 @@ def batch_token_ids(token_lists, device, pad_id):
     token_ids = torch.tensor(rows, device=device, dtype=torch.long)
     input_lens = torch.tensor([len(t) for t in token_lists], device=device, dtype=torch.long)
     return token_ids, input_lens
+
+
+def make_kv_cache(model_config, device, dtype=None) -> KVCache:
+    """Dense per-row KVCache for a ModelConfig (batching.py:22-32); KV heads are the config's ``kv_heads``."""
+    kv_heads = getattr(model_config, "kv_heads", model_config.n_heads)
+    return KVCache(num_layers=model_config.num_layers, max_seq_len=model_config.max_seq_len, n_heads=kv_heads,
+                   head_dim=model_config.head_dim, device=device, dtype=torch.float16 if dtype is None else dtype)
 
 
 def make_paged_kv_cache(model_config, device, dtype=None, block_size: int | None = None,

@@ -25,7 +25,7 @@ from typing import Callable, Iterator, List, Optional
 
 import torch
 
-from .batching import make_paged_kv_cache
+from .batching import make_kv_cache, make_paged_kv_cache
 from .data_model import EngineConfig, InferenceRequest, RequestState, validate_engine_config
 from .model_runner import ModelRunner
 from .scheduler import Scheduler
@@ -50,7 +50,6 @@ class Engine:
         self.max_tokens_per_step = max_tokens_per_step
         if getattr(model, "supports_prefix_cache", True) is False:
             use_prefix_cache = False
-        # the dense (non-paged) cache is served by the paged one: same API and results
         self.use_paged_kv_cache = use_paged_kv_cache
         self.use_prefix_cache = use_prefix_cache
         self._token_callbacks: dict[str, TokenCallback] = {}
@@ -86,12 +85,14 @@ class Engine:
         if self.cache is not None:
             return
         make = getattr(self.model, "make_kv_cache", None)
+        dtype = getattr(self.model, "dtype", torch.float16)
         if make is not None:
             self.cache = make(self.device, enable_prefix_cache=self.use_prefix_cache)
-        else:
-            self.cache = make_paged_kv_cache(self.model.config, self.device,
-                                             dtype=getattr(self.model, "dtype", torch.float16),
+        elif self.use_paged_kv_cache:
+            self.cache = make_paged_kv_cache(self.model.config, self.device, dtype=dtype,
                                              enable_prefix_cache=self.use_prefix_cache)
+        else:  # engine.py:226-227: the dense per-row cache
+            self.cache = make_kv_cache(self.model.config, self.device, dtype=dtype)
         self.cache.init_batch(self.max_concurrent_requests)
 
     def _fusable(self, prefills: List[InferenceRequest]) -> bool:
