@@ -364,7 +364,7 @@ def _run_decode_timed(args, cache, B, ctx, world, rank, local, dev, dist, shard,
     att_events = []
 
     def step(rec_layer=-1):
-        p = cache.plan(slots, ones, rows)
+        p = cache.plan(slots, ones, rows, q_heads=hq)
         for layer in range(L):
             cache.append_step(layer, k_all[layer], v_all[layer], p)
             record = layer == rec_layer

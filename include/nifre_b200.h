@@ -54,6 +54,7 @@ extern "C" {
 #define NF_STATUS_WAIT_TIMEOUT 4  /* a pipeline wait gave up after its time limit */
 #define NF_STATUS_BAD_SLOT 8    /* cache slot out of range: entry skipped */
 #define NF_STATUS_BAD_TILE 16   /* prefill tile longer than nf_prefill_tile_rows() rows: rest skipped */
+#define NF_STATUS_BAD_SHARED 32 /* shared-key record that leaves a query no key of its own: its keys skipped */
 
 /* Record layouts (int32) of the step descriptor the host uploads. */
 #define NF_SEQ_FIELDS 4   /* slot, q_start (row of the first new token), q_len, ctx_before */
@@ -112,14 +113,21 @@ int nf_selftest_umma(const void* A, const void* B, float* C, int32_t N, int32_t 
  * first and those of sequences with a smaller unit size after them, each
  * class in item order, so that a dynamic queue over the list ends on short
  * units.  split_tokens must be a positive multiple of 16.
- * counts[3]: counts[0] = n_tokens, counts[1] = number of units, counts[2] = 1
- * if some item has more than one part (the attention launch then merges).
+ * seq_shared[n_seqs][2] (device, may be NULL): per sequence the number of
+ * leading keys it shares with other sequences of the step and the number nc
+ * of cascade parts that nf_cascade_attention computes over them ({0, 0}:
+ * none).  Such an item's parts 0..nc-1 are those cascade parts (partial
+ * slots, no unit records); its units cover keys [shared, kv_len) as parts
+ * nc, nc+1, ...
+ * counts[4]: counts[0] = n_tokens, counts[1] = number of units in the list,
+ * counts[2] = 1 if some item has more than one part (the attention launch
+ * then merges), counts[3] = number of partial slots (units + cascade parts).
  */
 int nf_pack_step(const int32_t* seqs, int32_t n_seqs,
                  const int32_t* patches, int32_t n_patches,
                  int32_t* block_tables, int32_t num_slots, int32_t max_blocks_per_seq,
                  int32_t block_size, int32_t num_blocks, int32_t split_tokens,
-                 const int32_t* seq_split,
+                 const int32_t* seq_split, const int32_t* seq_shared,
                  int32_t* slot_mapping, int32_t* src_rows, int64_t* positions,
                  int32_t* items, int32_t* units, int32_t* counts,
                  int32_t n_tokens, int32_t max_units,
@@ -176,6 +184,36 @@ int nf_paged_attention(void* out, int64_t out_row_stride,
                        float* ws_partials, int64_t ws_partial_floats,
                        int32_t* ws_counters, int64_t ws_counter_ints,
                        int32_t* status, void* stream);
+
+/*
+ * nf_cascade_attention: partial attention of decode queries over keys that
+ * several sequences share (leading blocks imported from the prefix index,
+ * prefix_cache.py:33-81, paged_kv_cache.py:87-105), each shared block read
+ * once per group of sequences and KV head instead of once per sequence.
+ * groups[n_groups][4] (device, 16-byte aligned): representative slot (whose
+ * block table holds the shared blocks), first, count -- the group's query
+ * tokens are toks[first .. first+count) (item numbers of nf_pack_step, count
+ * * (num_q_heads / num_kv_heads) <= 128) -- and 0.  tasks[n_tasks][4]
+ * (device): group, key_begin, key_end (multiples of 16) and part: writes
+ * the partial softmax state of every query of the group over keys
+ * [key_begin, key_end) into partial slot items[t].unit_base + part of
+ * ws_partials (the layout of nf_attention_workspace).  The same step's
+ * nf_pack_step must have been given, through seq_shared, the shared key
+ * count and cascade part count of each such sequence; the following
+ * nf_paged_attention on the same stream and workspace then merges these
+ * parts with the queries' own keys.  16-bit pools, head_dim 64 or 128,
+ * block_size a multiple of 16.
+ */
+int nf_cascade_attention(float* ws_partials, int64_t ws_partial_floats,
+                         const void* q, int64_t q_row_stride,
+                         const void* k_pool, const void* v_pool, int32_t dtype,
+                         int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                         int32_t block_size, int32_t num_blocks,
+                         const int32_t* block_tables, int32_t max_blocks_per_seq,
+                         const int32_t* items, const int32_t* counts, int32_t max_items, int32_t max_units,
+                         const int32_t* groups, int32_t n_groups, const int32_t* tasks, int32_t n_tasks,
+                         const int32_t* toks, int32_t n_toks, float scale,
+                         int32_t* status, void* stream);
 
 /*
  * nf_prefill_attention: causal attention of prefill chunks on the tensor

@@ -20,6 +20,7 @@ NF_STATUS_UNIT_OVERFLOW = 2
 NF_STATUS_WAIT_TIMEOUT = 4
 NF_STATUS_BAD_SLOT = 8
 NF_STATUS_BAD_TILE = 16
+NF_STATUS_BAD_SHARED = 32
 
 SEQ_FIELDS, PATCH_FIELDS, ITEM_FIELDS, UNIT_FIELDS = 4, 3, 4, 8
 
@@ -27,7 +28,8 @@ _DTYPE_CODE = {torch.float32: NF_F32, torch.float16: NF_F16, torch.bfloat16: NF_
 
 EXPORTS = ("nf_last_error", "nf_abi_version", "nf_pack_step", "nf_kv_append",
            "nf_attention_workspace", "nf_paged_attention", "nf_paged_attention_noalloc",
-           "nf_last_attention_path", "nf_selftest_umma", "nf_prefill_attention", "nf_prefill_tile_rows")
+           "nf_last_attention_path", "nf_selftest_umma", "nf_prefill_attention", "nf_prefill_tile_rows",
+           "nf_cascade_attention")
 
 _P = ctypes.c_void_p
 _I32 = ctypes.c_int32
@@ -41,8 +43,11 @@ _SIGNATURES = {
     "nf_prefill_tile_rows": ([_I32], ctypes.c_int),
     "nf_prefill_attention": ([_P, _I64, _P, _I64, _I32, _P, _P, _I32, _I32, _I32, _I32, _I32, _I32,
                               _P, _I32, _P, _I32, _P, _P, ctypes.c_float, _P, _P], ctypes.c_int),
-    "nf_pack_step": ([_P, _I32, _P, _I32, _P, _I32, _I32, _I32, _I32, _I32, _P,
+    "nf_pack_step": ([_P, _I32, _P, _I32, _P, _I32, _I32, _I32, _I32, _I32, _P, _P,
                       _P, _P, _P, _P, _P, _P, _I32, _I32, _P, _P], ctypes.c_int),
+    "nf_cascade_attention": ([_P, _I64, _P, _I64, _P, _P, _I32, _I32, _I32, _I32, _I32, _I32, _P, _I32,
+                              _P, _P, _I32, _I32, _P, _I32, _P, _I32, _P, _I32, ctypes.c_float, _P, _P],
+                             ctypes.c_int),
     "nf_kv_append": ([_P, _P, _I32, _I64, _P, _P, _I32, _I64, _I64, _P, _P, _I32,
                       _I32, _I32, _P, _I32, _P, _P, _P], ctypes.c_int),
     "nf_attention_workspace": ([_I32, _I32, _I32, _I32, _I32, _I32,

@@ -112,11 +112,11 @@ def causal_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, head_dim
     src_rows = torch.empty_like(slot_mapping)
     items = torch.empty(4 * n_tok, dtype=torch.int32, device=dev)
     units = torch.empty(_lib.UNIT_FIELDS * max_units, dtype=torch.int32, device=dev)
-    counts = torch.empty(3, dtype=torch.int32, device=dev)
+    counts = torch.empty(4, dtype=torch.int32, device=dev)
     status = torch.zeros(1, dtype=torch.int32, device=dev)
     stream = _lib.stream_handle(dev)
     lib = _lib.load()
-    _lib.check(lib.nf_pack_step(seqs_d.data_ptr(), B, None, 0, bt.data_ptr(), B, 1, T, B, split, None,
+    _lib.check(lib.nf_pack_step(seqs_d.data_ptr(), B, None, 0, bt.data_ptr(), B, 1, T, B, split, None, None,
                                 slot_mapping.data_ptr(), src_rows.data_ptr(), None, items.data_ptr(),
                                 units.data_ptr(), counts.data_ptr(), n_tok, max_units, status.data_ptr(),
                                 stream), "nf_pack_step")

@@ -147,7 +147,7 @@ __device__ void finish_launch(const AttnParams& p, int* cta_done, int total) {
     // tasks: (item, KV head, group of 32 output chunks), dealt round-robin
     // over the CTAs so that every SM takes a share
     const int n_items = min(__ldg(p.counts), p.max_items);
-    const int n_units = min(__ldg(p.counts + 1), p.max_units);
+    const int n_units = min(__ldg(p.counts + 3), p.max_units);  // partial slots, cascade parts included
     const int groups = (p.G * (p.D >> 2) + 31) >> 5;
     const int tasks = n_items * p.Hkv * groups;
     const int stride = gridDim.x * (blockDim.x >> 5);

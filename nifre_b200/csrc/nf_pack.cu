@@ -22,6 +22,7 @@ struct PackParams {
   int* bt;
   int num_slots, max_blocks, bs, num_blocks, split;
   const int* seq_split;  // per-sequence unit size (NULL: split for all)
+  const int* seq_shared; // per sequence: keys [0, shared) served by cascade parts, their count (NULL: none)
   int* slot_mapping;
   int* src_rows;
   long long* positions;
@@ -102,6 +103,26 @@ __device__ __forceinline__ int unit_size(const PackParams& p, int s) {
 
 __device__ __forceinline__ int parts_of(int kv_len, int us) { return us > 0 ? (kv_len + us - 1) / us : 0; }
 
+// Keys [0, shared) of sequence s and the number nc of cascade parts that
+// hold their partial results (both 0 without a record).  A record must leave
+// the query at least one key of its own (0 < shared < kv_len) and belong to
+// a sequence with units; otherwise the sequence is flagged, its cascade
+// slots are kept (nf_cascade_attention may write them) and its own keys
+// are skipped.
+__device__ __forceinline__ void shared_of(const PackParams& p, int s, int kv_len, int& shared, int& nc) {
+  shared = nc = 0;
+  if (!p.seq_shared) return;
+  const int sh = p.seq_shared[2 * s], n = p.seq_shared[2 * s + 1];
+  if (sh == 0 && n == 0) return;
+  nc = min(max(n, 0), 1 << 16);
+  if (sh > 0 && sh < kv_len && n > 0 && unit_size(p, s) > 0) {
+    shared = sh;
+  } else {
+    shared = kv_len;
+    atomicOr(p.status, NF_STATUS_BAD_SHARED);
+  }
+}
+
 __global__ void __launch_bounds__(kPackThreads) pack_kernel(const PackParams p) {
   extern __shared__ int cu[];  // n_seqs + 1 query offsets
   const int tid = threadIdx.x;
@@ -151,13 +172,19 @@ __global__ void __launch_bounds__(kPackThreads) pack_kernel(const PackParams p) 
     it.y = q_start + i;
     it.z = kv_len;
     const int us = unit_size(p, s);
-    it.w = parts_of(kv_len, us);  // number of parts; scanned below
+    int shared = 0, nc = 0;
+    shared_of(p, s, kv_len, shared, nc);
+    it.w = nc + parts_of(kv_len - shared, us);  // number of parts; scanned below
     if (it.w > 1) multi_sh = 1;
     reinterpret_cast<int4*>(p.items)[t] = it;
   }
   __syncthreads();
   // 4. unit base of each item: scan of the split counts.
   const int n_units = cta_exclusive_scan(p.items + 3, T, 4);
+  // The first nc parts of an item whose sequence shares its first keys with
+  // others (cascade parts, written by nf_cascade_attention) have partial
+  // slots but no record in the list; its own keys follow them as parts
+  // nc, nc+1, ...
   // 5. the unit list, one self-contained record per key range of an item:
   // (item, slot, q_row, part, key_begin, key_end, unit_base, n_parts).  The
   // parts of an item are contiguous from its unit_base in key order (that is
@@ -167,37 +194,46 @@ __global__ void __launch_bounds__(kPackThreads) pack_kernel(const PackParams p) 
   // order.  Workers that take units in list order so end on short units and
   // finish close together, and the items of the first class complete, and
   // merge, while the bulk of the keys still streams.
-  __shared__ int n_fine_sh;
-  if (tid == 0) n_fine_sh = 0;
+  __shared__ int n_fine_sh, n_casc_sh;
+  if (tid == 0) n_fine_sh = n_casc_sh = 0;
   __syncthreads();
-  int my_fine = 0;
+  int my_fine = 0, my_casc = 0;
   for (int t = tid; t < T; t += kPackThreads) {
-    const int us = unit_size(p, seq_of(cu, p.n_seqs, t));
-    if (us < p.split) my_fine += parts_of(p.items[4 * t + 2], us);
+    const int s = seq_of(cu, p.n_seqs, t), kv_len = p.items[4 * t + 2];
+    const int us = unit_size(p, s);
+    int shared = 0, nc = 0;
+    shared_of(p, s, kv_len, shared, nc);
+    if (us < p.split) my_fine += parts_of(kv_len - shared, us);
+    my_casc += nc;
   }
   if (my_fine) atomicAdd(&n_fine_sh, my_fine);
+  if (my_casc) atomicAdd(&n_casc_sh, my_casc);
   __syncthreads();
-  const int n_bulk = n_units - n_fine_sh;
-  int fine_carry = 0;
+  const int n_list = n_units - n_casc_sh;  // units in the list: every part but the cascade ones
+  const int n_bulk = n_list - n_fine_sh;
+  int fine_carry = 0, casc_carry = 0;
   for (int base = 0; base < T; base += kPackThreads) {
     const int t = base + tid;
     int4 it = make_int4(0, 0, 0, 0);
-    int us = p.split, n = 0;
+    int us = p.split, n = 0, shared = 0, nc = 0;
     if (t < T) {
+      const int s = seq_of(cu, p.n_seqs, t);
       it = reinterpret_cast<const int4*>(p.items)[t];
-      us = unit_size(p, seq_of(cu, p.n_seqs, t));
-      n = parts_of(it.z, us);
+      us = unit_size(p, s);
+      shared_of(p, s, it.z, shared, nc);
+      n = parts_of(it.z - shared, us);
     }
     const bool fine = us < p.split;
     const int fb = cta_scan_round(fine ? n : 0, fine_carry);  // fine units of the items before t
+    const int cb = cta_scan_round(nc, casc_carry);           // cascade parts of the items before t
     if (t < T) {
-      const int first = fine ? n_bulk + fb : it.w - fb;  // list position of the item's first unit
+      const int first = fine ? n_bulk + fb : it.w - fb - cb;  // list position of the item's first unit
       for (int j = 0; j < n; ++j) {
         const int u = first + j;
         if (u < p.max_units) {
           int4* rec = reinterpret_cast<int4*>(p.units) + 2 * u;
-          rec[0] = make_int4(t, it.x, it.y, j);
-          rec[1] = make_int4(j * us, min((j + 1) * us, it.z), it.w, n);
+          rec[0] = make_int4(t, it.x, it.y, nc + j);
+          rec[1] = make_int4(shared + j * us, min(shared + (j + 1) * us, it.z), it.w, nc + n);
         }
       }
     }
@@ -205,8 +241,9 @@ __global__ void __launch_bounds__(kPackThreads) pack_kernel(const PackParams p) 
   if (tid == 0) {
     if (n_units > p.max_units) atomicOr(p.status, NF_STATUS_UNIT_OVERFLOW);
     p.counts[0] = T;
-    p.counts[1] = min(n_units, p.max_units);
+    p.counts[1] = min(n_list, p.max_units);
     p.counts[2] = multi_sh;  // some item has more than one part: the attention launch merges
+    p.counts[3] = min(n_units, p.max_units);  // partial slots of all items, cascade parts included
   }
 }
 
@@ -215,7 +252,7 @@ __global__ void __launch_bounds__(kPackThreads) pack_kernel(const PackParams p) 
 extern "C" int nf_pack_step(const int32_t* seqs, int32_t n_seqs, const int32_t* patches, int32_t n_patches,
                             int32_t* block_tables, int32_t num_slots, int32_t max_blocks_per_seq,
                             int32_t block_size, int32_t num_blocks, int32_t split_tokens,
-                            const int32_t* seq_split,
+                            const int32_t* seq_split, const int32_t* seq_shared,
                             int32_t* slot_mapping, int32_t* src_rows, int64_t* positions, int32_t* items,
                             int32_t* units, int32_t* counts, int32_t n_tokens, int32_t max_units,
                             int32_t* status, void* stream) {
@@ -246,6 +283,7 @@ extern "C" int nf_pack_step(const int32_t* seqs, int32_t n_seqs, const int32_t* 
   p.num_blocks = num_blocks;
   p.split = split_tokens;
   p.seq_split = seq_split;
+  p.seq_shared = seq_shared;
   p.slot_mapping = slot_mapping;
   p.src_rows = src_rows;
   p.positions = reinterpret_cast<long long*>(positions);

@@ -117,6 +117,9 @@ class StepPlan:
         self.positions = None
         # split-K units of the step, and the tensor-core prefill tiles (tiles, n_tiles, q_heads)
         self.decode_units = max_units
+        self.shared_keys = None  # per sequence: leading keys served by the cascade kernel (numpy)
+        self.n_casc_groups = self.n_casc_tasks = self.n_casc_toks = 0
+        self.casc_groups = self.casc_tasks = self.casc_toks = None
         self.tiles = None
         self.n_tiles = 0
         self.q_heads = None
@@ -142,6 +145,9 @@ class PagedKVCache:
         self.dtype = dtype
         self.block_size = block_size
         self.enable_prefix_cache = enable_prefix_cache
+        # decode sequences that share leading blocks get those keys attended once per group (cascade)
+        self.enable_cascade = True
+        self._cascade_memo = None  # (batch key, grouping) of the last step planned
         self.prefix_cache_max_entries = prefix_cache_max_entries
         self._num_blocks_override = num_blocks
         self.batch_size = 0
@@ -283,6 +289,83 @@ class PagedKVCache:
         return (self.dtype in (torch.bfloat16, torch.float16) and self.head_dim in (64, 128)
                 and q_heads // self.n_heads in (1, 2, 4, 8) and self.block_size % 16 == 0)
 
+    # cascade over shared keys: at least this many shared keys and two sequences
+    CASCADE_MIN_KEYS = 64
+    CASCADE_ROWS = 128  # query rows per nf_cascade_attention CTA
+    CASCADE_MAX_KEYS = 256  # keys per nf_cascade_attention task
+
+    def cascade_supported(self, q_heads: int | None) -> bool:
+        """True when nf_cascade_attention serves this cache with q_heads query heads."""
+        if not self.enable_cascade or q_heads is None or q_heads % self.n_heads:
+            return False
+        return (self.dtype in (torch.bfloat16, torch.float16) and self.head_dim in (64, 128)
+                and q_heads // self.n_heads <= self.CASCADE_ROWS and self.block_size % 16 == 0)
+
+    def _cascade_groups(self, slots, q_lens, ctx, dec, group: int):
+        """Decode sequences that start with the same physical blocks, and the cascade work over those keys.
+
+        Sequences with one new token whose tables begin with the same block
+        are grouped; a group's shared keys are the blocks all its members
+        hold at the same positions (imported prefix blocks: full, written
+        before the step).  Members are cut into CTA groups of at most
+        ``CASCADE_ROWS / group`` sequences (at least two each) and the shared
+        keys into ranges of a common size (64 to ``CASCADE_MAX_KEYS`` keys)
+        chosen so that the tasks fill about one wave of SMs.  Returns per-sequence shared keys and cascade part
+        counts, and the (slot, first, count, 0) groups, (group, key_begin,
+        key_end, part) tasks and query tokens for ``nf_cascade_attention``.
+        """
+        S, bs = len(slots), self.block_size
+        # Decode steps repeat the same batch: while its sequences, their new
+        # token counts and their tables' epochs (which change only when
+        # leading entries are replaced) are those of the previous step, the
+        # shared runs are unchanged and the previous grouping stands.
+        key = (slots.tobytes(), q_lens.tobytes(), dec.tobytes(), group,
+               tuple(self.block_tables[s].epoch for s in slots.tolist()))
+        if (self._cascade_memo is not None and self._cascade_memo[0] == key
+                and (self._cascade_memo[1][0] <= ctx).all()):  # no position moved back under a shared run
+            return self._cascade_memo[1]
+        shared = np.zeros(S, dtype=np.int32)
+        nparts = np.zeros(S, dtype=np.int32)
+        buckets: dict[int, list[int]] = {}
+        for i in np.flatnonzero(dec & (q_lens == 1)).tolist():
+            if int(ctx[i]) // bs * bs < self.CASCADE_MIN_KEYS:
+                continue
+            blocks = self.block_tables[int(slots[i])]._physical_blocks
+            buckets.setdefault(blocks[0], []).append(i)
+        per_cta = self.CASCADE_ROWS // group
+        cuts = []  # (members, shared keys)
+        for members in buckets.values():
+            if len(members) < 2:
+                continue
+            n = min(int(ctx[i]) // bs for i in members)
+            ref = self.block_tables[int(slots[members[0]])]._physical_blocks
+            for i in members[1:]:
+                other = self.block_tables[int(slots[i])]._physical_blocks
+                if other[:n] != ref[:n]:
+                    n = int(np.argmin(np.asarray(ref[:n]) == np.asarray(other[:n])))
+            if n * bs < self.CASCADE_MIN_KEYS:
+                continue
+            for c0 in range(0, len(members), per_cta):
+                part = members[c0: c0 + per_cta]
+                if len(part) >= 2:
+                    cuts.append((part, n * bs))
+        groups, tasks, toks = [], [], []
+        if not cuts:
+            self._cascade_memo = (key, (shared, nparts, groups, tasks, toks))
+            return shared, nparts, groups, tasks, toks
+        want = sum(p for _, p in cuts) * self.n_heads / max(1, self.sm_count)
+        ck = int(min(self.CASCADE_MAX_KEYS, max(64, math.ceil(want / 64.0) * 64)))
+        tok_off = np.cumsum(q_lens) - q_lens
+        for g, (members, p) in enumerate(cuts):
+            nc = (p + ck - 1) // ck
+            groups.append((int(slots[members[0]]), len(toks), len(members), 0))
+            tasks.extend((g, c * ck, min((c + 1) * ck, p), c) for c in range(nc))
+            toks.extend(int(tok_off[i]) for i in members)
+            shared[members] = p
+            nparts[members] = nc
+        self._cascade_memo = (key, (shared, nparts, groups, tasks, toks))
+        return shared, nparts, groups, tasks, toks
+
     def plan(self, slots, q_lens, q_starts, split: int | None = None, fine_tail: bool = True,
              q_heads: int | None = None) -> StepPlan:
         """Allocate blocks for a step and pack its metadata on the GPU.
@@ -297,7 +380,9 @@ class PagedKVCache:
         attention calls) and a supported shape, sequences with at least
         ``PREFILL_MIN_TOKENS`` new tokens are attended by the tensor-core
         prefill kernel, in tiles of 128 query rows; the rest by the split-K
-        kernel.
+        kernel, and decode sequences that share leading blocks (imported
+        prefixes) have those keys attended once per group of sequences by
+        the cascade kernel (``_cascade_groups``).
         """
         slots = np.asarray(slots, dtype=np.int64)
         q_lens = np.asarray(q_lens, dtype=np.int64)
@@ -339,18 +424,25 @@ class PagedKVCache:
         kv = np.repeat(ctx + 1, q_lens) + (np.arange(T) - np.repeat(np.cumsum(q_lens) - q_lens, q_lens))
         routed = (q_lens >= self.PREFILL_MIN_TOKENS) if self.prefill_supported(q_heads) else np.zeros(S, bool)
         dec = ~routed
-        kv_dec = kv[np.repeat(dec, q_lens)]
+        if self.cascade_supported(q_heads) and dec.any():
+            shared, nparts, cgroups, ctasks, ctoks = self._cascade_groups(slots, q_lens, ctx, dec,
+                                                                          q_heads // self.n_heads)
+        else:
+            shared, nparts, cgroups, ctasks, ctoks = (np.zeros(S, np.int32), np.zeros(S, np.int32), [], [], [])
+        tok_dec = np.repeat(dec, q_lens)
+        kv_dec = kv[tok_dec] - np.repeat(shared.astype(np.int64), q_lens)[tok_dec]  # each query's own keys
         if split is None:
             split = self.split_for(max(1, int(kv_dec.sum())))
         if split <= 0 or split % 16:
             raise ValueError(f"split ({split}) must be a positive multiple of 16")
-        seq_keys = q_lens * (ctx + 1) + q_lens * (q_lens - 1) // 2
+        seq_keys = q_lens * (ctx + 1) + q_lens * (q_lens - 1) // 2 - q_lens * shared
         seq_split = np.zeros(S, dtype=np.int32)  # 0: the prefill kernel serves the sequence
         if dec.any():
             seq_split[dec] = (seq_unit_sizes(seq_keys[dec], split, self.decode_workers) if fine_tail else split)
         item_split = np.repeat(seq_split.astype(np.int64), q_lens)
         n_units = int(((kv_dec + item_split[item_split > 0] - 1) // item_split[item_split > 0]).sum())
-        max_units = max(1, n_units)
+        n_casc = int(nparts.sum())  # partial slots of the cascade parts (q_len 1: one item per sequence)
+        max_units = max(1, n_units + n_casc)
         tiles = []
         if routed.any():
             tt = _lib.load().nf_prefill_tile_rows(self.head_dim) // (q_heads // self.n_heads)  # tokens per item
@@ -363,15 +455,25 @@ class PagedKVCache:
         sched = _prefill_order(tiles, self.n_heads) if n_tiles else np.zeros(0, np.int32)
         off_tiles = _align4(S * 5 + P * 3)
         off_sched = off_tiles + 4 * n_tiles
-        host = np.zeros(off_sched + sched.size, dtype=np.int32)
+        n_cg, n_ct, n_tok = len(cgroups), len(ctasks), len(ctoks)
+        off_shared = _align4(off_sched + sched.size)
+        off_cg = _align4(off_shared + 2 * S)
+        off_ct = off_cg + 4 * n_cg
+        off_tok = off_ct + 4 * n_ct
+        host = np.zeros(off_tok + n_tok, dtype=np.int32)
         host[: S * 4] = np.stack([slots, q_starts, q_lens, ctx], axis=1).reshape(-1)
         if P:
             host[S * 4: S * 4 + P * 3] = np.asarray(patches, dtype=np.int32).reshape(-1)
         host[S * 4 + P * 3: S * 5 + P * 3] = seq_split
         if n_tiles:
             host[off_tiles:off_sched] = np.asarray(tiles, dtype=np.int32).reshape(-1)
-            host[off_sched:] = sched
-        off_slot = _align4(off_sched + sched.size)
+            host[off_sched:off_sched + sched.size] = sched
+        if n_ct:
+            host[off_shared:off_shared + 2 * S] = np.stack([shared, nparts], axis=1).reshape(-1)
+            host[off_cg:off_ct] = np.asarray(cgroups, dtype=np.int32).reshape(-1)
+            host[off_ct:off_tok] = np.asarray(ctasks, dtype=np.int32).reshape(-1)
+            host[off_tok:] = np.asarray(ctoks, dtype=np.int32)
+        off_slot = _align4(host.size)
         off_src = off_slot + T
         off_items = _align4(off_src + T)
         off_units = off_items + 4 * T
@@ -383,6 +485,11 @@ class PagedKVCache:
         plan = StepPlan(slots, q_lens, q_starts, ctx, split, max_units, seq_split)
         plan.decode_units = n_units
         plan.q_heads = q_heads
+        plan.shared_keys = shared
+        plan.n_casc_groups, plan.n_casc_tasks, plan.n_casc_toks = n_cg, n_ct, n_tok
+        plan.casc_groups = meta[off_cg: off_ct]
+        plan.casc_tasks = meta[off_ct: off_tok]
+        plan.casc_toks = meta[off_tok: off_tok + n_tok]
         plan.n_tiles = n_tiles
         plan.tiles = meta[off_tiles: off_tiles + 4 * n_tiles]
         plan.sched = meta[off_sched: off_sched + sched.size]
@@ -391,14 +498,14 @@ class PagedKVCache:
         plan.src_rows = meta[off_src: off_src + T]
         plan.items = meta[off_items: off_items + 4 * T]
         plan.units = meta[off_units: off_units + _lib.UNIT_FIELDS * max_units]
-        plan.counts = meta[off_counts: off_counts + 3]
+        plan.counts = meta[off_counts: off_counts + 4]
         plan.positions = pos_dev[:T]
         lib = _lib.load()
         _lib.check(lib.nf_pack_step(
             meta.data_ptr(), S, meta.data_ptr() + 4 * S * 4 if P else None, P,
             self.bt_dev.data_ptr(), self.batch_size, self.max_blocks_per_seq, self.block_size,
             self.num_blocks, split, meta.data_ptr() + 4 * (S * 4 + P * 3),
-            plan.slot_mapping.data_ptr(), plan.src_rows.data_ptr(),
+            meta.data_ptr() + 4 * off_shared if n_ct else None, plan.slot_mapping.data_ptr(), plan.src_rows.data_ptr(),
             plan.positions.data_ptr(), plan.items.data_ptr(), plan.units.data_ptr(), plan.counts.data_ptr(),
             T, max_units, self.status.data_ptr(), _lib.stream_handle(self.device)), "nf_pack_step")
         self._plan = plan
@@ -479,6 +586,18 @@ class PagedKVCache:
             pf, ci = _lib.workspace_sizes(plan.max_units, max_items, hq, self.n_heads, D, self.dtype)
             ws = self._ws_partials.get(pf)
             cnt = self._ws_counters.get(ci)
+            if plan.n_casc_tasks:
+                if hq != plan.q_heads:
+                    raise ValueError(f"the plan's cascade groups are for {plan.q_heads} query heads, q has {hq}")
+                # partials over the shared keys, merged by the decode launch with each query's own keys
+                _lib.check(lib.nf_cascade_attention(
+                    ws.data_ptr(), ws.numel(), q.data_ptr(), q.stride(0),
+                    self.k[layer_id].data_ptr(), self.v[layer_id].data_ptr(), _lib.dtype_code(self.dtype),
+                    hq, self.n_heads, D, self.block_size, self.num_blocks, self.bt_dev.data_ptr(),
+                    self.max_blocks_per_seq, plan.items.data_ptr(), plan.counts.data_ptr(), max_items,
+                    plan.max_units, plan.casc_groups.data_ptr(), plan.n_casc_groups, plan.casc_tasks.data_ptr(),
+                    plan.n_casc_tasks, plan.casc_toks.data_ptr(), plan.n_casc_toks, float(scale),
+                    self.status.data_ptr(), stream), "nf_cascade_attention")
             _lib.check(lib.nf_paged_attention(
                 out.data_ptr(), out.stride(0), q.data_ptr(), q.stride(0),
                 self.k[layer_id].data_ptr(), self.v[layer_id].data_ptr(), _lib.dtype_code(self.dtype),
@@ -497,7 +616,8 @@ class PagedKVCache:
         if st:
             self.status.zero_()
             raise _lib.NifreError(f"device status {st:#x} (bad block={st & 1}, unit overflow={st >> 1 & 1}, "
-                                  f"wait timeout={st >> 2 & 1}, bad slot={st >> 3 & 1}, bad tile={st >> 4 & 1})")
+                                  f"wait timeout={st >> 2 & 1}, bad slot={st >> 3 & 1}, bad tile={st >> 4 & 1}, "
+                                  f"bad shared keys={st >> 5 & 1})")
 
     def device_block_table(self, slot: int, n: int | None = None) -> list[int]:
         row = self.bt_dev[slot].tolist()

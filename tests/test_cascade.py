@@ -1,0 +1,190 @@
+"""Cascade attention over shared prefix blocks: grouping on the host (CPU) and parity (B200).
+
+Decode sequences that imported the same prefix blocks (``try_load_prefix``,
+nifre ``src/inference/paged_kv_cache.py:87-105``) have those keys attended
+once per group by ``nf_cascade_attention``; the decode launch covers the
+rest and merges.  The result must be the same attention as without the
+cascade: bfloat16 within rtol/atol 2e-2 of the float32 oracle over each
+sequence's own block table.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle.attention import attend_paged_fp32
+
+DEV = "cuda"
+TOL = dict(rtol=2e-2, atol=2e-2)
+
+
+def _host_cache(tables, ctx, bs=16, hkv=8):
+    """A PagedKVCache with host state only (block tables and positions), for the planning logic."""
+    from nifre_b200 import BlockAllocator, BlockTable, PagedKVCache
+    c = PagedKVCache(1, 4096, hkv, 64, device="cpu", dtype=torch.bfloat16, block_size=bs)
+    n = 1 + max(max(t) for t in tables)
+    c.block_allocator = BlockAllocator(n)
+    c.block_tables = []
+    for t in tables:
+        bt = BlockTable(c.block_allocator, bs)
+        bt._physical_blocks = list(t)
+        c.block_tables.append(bt)
+    c.pos_host = np.asarray(ctx, dtype=np.int64)
+    c._sm_count = 148
+    return c
+
+
+def test_cascade_groups_host():
+    """Groups = decode sequences sharing leading blocks, cut to <= 128 / G sequences; shared keys = common blocks."""
+    bs = 16
+    pre_a = list(range(0, 64))          # 1024-key prefix
+    pre_b = list(range(100, 104))       # 64 keys: the minimum
+    tables, ctx = [], []
+    for i in range(40):                 # 40 sequences on prefix A (32 + 8 with G = 4)
+        tables.append(pre_a + [1000 + 2 * i, 1001 + 2 * i])
+        ctx.append(len(pre_a) * bs + 20)
+    tables.append(pre_a[:10] + [2000, 2001])  # diverges after 10 blocks: shortens A's common run
+    ctx.append(10 * bs + 5)
+    for i in range(2):
+        tables.append(pre_b + [3000 + i])
+        ctx.append(len(pre_b) * bs + 3)
+    tables.append([4000, 4001])         # alone: no cascade
+    ctx.append(20)
+    c = _host_cache(tables, ctx, bs)
+    S = len(tables)
+    slots = np.arange(S)
+    q_lens = np.ones(S, dtype=np.int64)
+    dec = np.ones(S, dtype=bool)
+    shared, nparts, groups, tasks, toks = c._cascade_groups(slots, q_lens, np.asarray(ctx), dec, 4)
+    # prefix A: 41 members whose common run is 10 blocks -> groups of 32 and 9
+    assert shared[:41].tolist() == [160] * 41
+    assert shared[41:43].tolist() == [64, 64] and shared[43] == 0
+    assert [g[2] for g in groups] == [32, 9, 2]
+    assert sorted(toks) == list(range(43))
+    for g, (slot, first, count, _) in enumerate(groups):
+        members = toks[first:first + count]
+        assert slot == members[0]
+        mine = [t for t in tasks if t[0] == g]
+        assert [t[3] for t in mine] == list(range(len(mine)))
+        assert mine[0][1] == 0 and mine[-1][2] == shared[members[0]]
+        assert all(a[2] == b[1] for a, b in zip(mine, mine[1:]))  # contiguous key ranges
+        assert all(t[1] % 16 == 0 and t[2] % 16 == 0 for t in mine)
+        assert all(nparts[m] == len(mine) for m in members)
+    # sequences with more than one new token are never grouped
+    q2 = q_lens.copy()
+    q2[:] = 2
+    assert c._cascade_groups(slots, q2, np.asarray(ctx), dec, 4)[2] == []
+    # with G = 8, at most 16 sequences per group
+    groups8 = c._cascade_groups(slots, q_lens, np.asarray(ctx), dec, 8)[2]
+    assert max(g[2] for g in groups8) == 16
+    # the next decode step of the same batch reuses the grouping; a replaced table or a position moved
+    # back under a shared run recomputes it
+    again = c._cascade_groups(slots, q_lens, np.asarray(ctx) + 1, dec, 8)
+    assert again is c._cascade_groups(slots, q_lens, np.asarray(ctx) + 2, dec, 8)
+    assert c._cascade_groups(slots, q_lens, np.asarray(ctx) - 1000, dec, 8) is not again
+    c.block_tables[3].epoch += 1
+    assert c._cascade_groups(slots, q_lens, np.asarray(ctx), dec, 8) is not again
+
+
+def _shared_prefix_cache(hq, hkv, D, prefixes, n_per, suffix, dtype, seed, tail_div=None):
+    """Requests importing shared prompt prefixes the way the engine does (try_load_prefix, prefill the rest,
+    register_prefix), each with its own random suffix; ``tail_div`` requests diverge inside the prefix."""
+    from nifre_b200 import PagedKVCache
+    rng = np.random.default_rng(seed)
+    g = torch.Generator().manual_seed(seed)
+    prompts = []
+    for p in prefixes:
+        base = rng.integers(0, 50000, size=p).tolist()
+        for j in range(n_per):
+            prompts.append(base + rng.integers(0, 50000, size=int(rng.integers(*suffix))).tolist())
+    if tail_div:
+        for r in range(0, len(prompts), tail_div):
+            cut = len(prompts[r]) // 3
+            prompts[r] = prompts[r][:cut] + rng.integers(0, 50000, size=len(prompts[r]) - cut).tolist()
+    B = len(prompts)
+    cache = PagedKVCache(1, max(len(p) for p in prompts) + 8, hkv, D, device=DEV, dtype=dtype, block_size=16)
+    cache.init_batch(B)
+    for r, toks in enumerate(prompts):
+        m = cache.try_load_prefix(r, toks)
+        n = len(toks) - m
+        plan = cache.plan([r], [n], [0])
+        k = torch.randn(n, hkv * D, generator=g).to(dtype).to(DEV)
+        v = torch.randn(n, hkv * D, generator=g).to(dtype).to(DEV)
+        cache.append_step(0, k, v, plan)
+        cache.register_prefix(r, toks)
+    return cache, g
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("D,hq,hkv", [(64, 32, 8), (128, 32, 8), (64, 8, 8), (64, 16, 2)])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_cascade_decode_vs_oracle(D, hq, hkv, dtype):
+    """A decode step over shared prefixes: cascade + decode merge equals the oracle per sequence."""
+    cache, g = _shared_prefix_cache(hq, hkv, D, [256, 512, 48], 12, (1, 90), dtype, seed=D + hq,
+                                    tail_div=7)
+    B = cache.batch_size
+    before = [cache.length(s) for s in range(B)]
+    plan = cache.plan(list(range(B)), [1] * B, list(range(B)), q_heads=hq)
+    assert plan.n_casc_tasks > 0 and (plan.shared_keys > 0).sum() >= 2 * 2
+    q = torch.randn(B, hq * D, generator=g).to(dtype).to(DEV)
+    k = torch.randn(B, hkv * D, generator=g).to(dtype).to(DEV)
+    v = torch.randn(B, hkv * D, generator=g).to(dtype).to(DEV)
+    cache.append_step(0, k, v, plan)
+    out = torch.zeros_like(q)
+    cache.attention_step(0, q, plan, out)
+    cache.check_status()
+    kp, vp = cache.k[0].cpu(), cache.v[0].cpu()
+    for b in range(B):
+        ref = attend_paged_fp32(q[b].view(1, hq, D).cpu(), kp, vp, cache.block_tables[b].physical_blocks(),
+                                before[b] + 1, hq // hkv)
+        torch.testing.assert_close(out[b].view(hq, D).float().cpu(), ref[0], **TOL)
+
+
+@pytest.mark.gpu
+def test_cascade_matches_plain_decode_and_many_groups():
+    """Same step with and without the cascade (two caches built alike): outputs agree; 40 sequences on one
+    prefix with G = 4 make a group of 32 and one of 8; a long prefix gives several key ranges per group."""
+    outs = []
+    for casc in (True, False):
+        cache, g = _shared_prefix_cache(32, 8, 64, [2048], 40, (1, 40), torch.bfloat16, seed=5)
+        cache.enable_cascade = casc
+        B = cache.batch_size
+        plan = cache.plan(list(range(B)), [1] * B, list(range(B)), q_heads=32)
+        assert (plan.n_casc_tasks > 0) == casc
+        if casc:
+            groups = plan.casc_groups.view(-1, 4).cpu().numpy()
+            assert sorted(groups[:, 2].tolist()) == [8, 32]
+            assert plan.n_casc_tasks > 2 * 8 // 8
+        q = torch.randn(B, 32 * 64, generator=g).to(torch.bfloat16).to(DEV)
+        k = torch.randn(B, 8 * 64, generator=g).to(torch.bfloat16).to(DEV)
+        v = torch.randn(B, 8 * 64, generator=g).to(torch.bfloat16).to(DEV)
+        cache.append_step(0, k, v, plan)
+        out = torch.zeros_like(q)
+        cache.attention_step(0, q, plan, out)
+        cache.check_status()
+        outs.append(out.float().cpu())
+    torch.testing.assert_close(outs[0], outs[1], **TOL)
+
+
+@pytest.mark.gpu
+def test_cascade_bad_task_flagged():
+    """A task naming a group that does not exist is flagged on the status word and writes nothing."""
+    from nifre_b200 import _lib
+    cache, g = _shared_prefix_cache(32, 8, 64, [256], 4, (1, 20), torch.bfloat16, seed=9)
+    B = cache.batch_size
+    plan = cache.plan(list(range(B)), [1] * B, list(range(B)), q_heads=32)
+    assert plan.n_casc_tasks > 0
+    lib = _lib.load()
+    ws = torch.zeros(plan.max_units * 32 * 68, dtype=torch.float32, device=DEV)
+    bad = torch.tensor([7, 0, 64, 0], dtype=torch.int32, device=DEV)
+    q = torch.zeros(B, 32 * 64, dtype=torch.bfloat16, device=DEV)
+    _lib.check(lib.nf_cascade_attention(
+        ws.data_ptr(), ws.numel(), q.data_ptr(), q.stride(0), cache.k[0].data_ptr(), cache.v[0].data_ptr(),
+        _lib.NF_BF16, 32, 8, 64, 16, cache.num_blocks, cache.bt_dev.data_ptr(), cache.max_blocks_per_seq,
+        plan.items.data_ptr(), plan.counts.data_ptr(), B, plan.max_units, plan.casc_groups.data_ptr(),
+        plan.n_casc_groups, bad.data_ptr(), 1, plan.casc_toks.data_ptr(), plan.n_casc_toks, 0.125,
+        cache.status.data_ptr(), _lib.stream_handle(cache.device)), "nf_cascade_attention")
+    torch.cuda.synchronize()
+    assert int(cache.status.item()) == _lib.NF_STATUS_BAD_SHARED
+    assert int(torch.count_nonzero(ws)) == 0
+    cache.status.zero_()

@@ -195,11 +195,11 @@ def test_library_exports_every_declared_symbol():
     lib = ctypes.CDLL(str(_lib.LIB_PATH))
     syms = _declared_symbols()
     assert set(syms) >= {"nf_pack_step", "nf_kv_append", "nf_paged_attention", "nf_attention_workspace",
-                         "nf_last_error", "nf_abi_version"}
+                         "nf_last_error", "nf_abi_version", "nf_cascade_attention"}
     for s in syms:
         assert hasattr(lib, s), s
     assert set(_lib.EXPORTS) <= set(syms)
-    assert _lib.load().nf_abi_version() == 10
+    assert _lib.load().nf_abi_version() == 11
 
 
 def test_workspace_sizing_and_argument_errors():
