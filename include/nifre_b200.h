@@ -190,14 +190,15 @@ int nf_paged_attention(void* out, int64_t out_row_stride,
  * several sequences share (leading blocks imported from the prefix index,
  * prefix_cache.py:33-81, paged_kv_cache.py:87-105), each shared block read
  * once per group of sequences and KV head instead of once per sequence.
- * groups[n_groups][4] (device, 16-byte aligned): representative slot (whose
- * block table holds the shared blocks), first, count -- the group's query
- * tokens are toks[first .. first+count) (item numbers of nf_pack_step, count
- * * (num_q_heads / num_kv_heads) <= 128) -- and 0.  tasks[n_tasks][4]
- * (device): group, key_begin, key_end (multiples of 16) and part: writes
- * the partial softmax state of every query of the group over keys
- * [key_begin, key_end) into partial slot items[t].unit_base + part of
- * ws_partials (the layout of nf_attention_workspace).  The same step's
+ * tasks[n_tasks][8] (device, 16-byte aligned): slot (whose block table
+ * holds the shared blocks), first, count, part, key_begin, key_end (multiples
+ * of 16, at most 256 keys apart), 0, 0 -- the task's queries are
+ * toks[first .. first+count), count * (num_q_heads / num_kv_heads) <= 128,
+ * where toks[n_toks][2] (device, 8-byte aligned) holds (item number of
+ * nf_pack_step, row of the query in q).  Each task writes the partial
+ * softmax state of its queries over keys [key_begin, key_end) into partial
+ * slot items[item].unit_base + part of ws_partials (the layout of
+ * nf_attention_workspace), for every KV head (one CTA per task and head).  The same step's
  * nf_pack_step must have been given, through seq_shared, the shared key
  * count and cascade part count of each such sequence; the following
  * nf_paged_attention on the same stream and workspace then merges these
@@ -211,8 +212,8 @@ int nf_cascade_attention(float* ws_partials, int64_t ws_partial_floats,
                          int32_t block_size, int32_t num_blocks,
                          const int32_t* block_tables, int32_t max_blocks_per_seq,
                          const int32_t* items, const int32_t* counts, int32_t max_items, int32_t max_units,
-                         const int32_t* groups, int32_t n_groups, const int32_t* tasks, int32_t n_tasks,
-                         const int32_t* toks, int32_t n_toks, float scale,
+                         const int32_t* tasks, int32_t n_tasks, const int32_t* toks, int32_t n_toks,
+                         float scale,
                          int32_t* status, void* stream);
 
 /*

@@ -46,8 +46,7 @@ _SIGNATURES = {
     "nf_pack_step": ([_P, _I32, _P, _I32, _P, _I32, _I32, _I32, _I32, _I32, _P, _P,
                       _P, _P, _P, _P, _P, _P, _I32, _I32, _P, _P], ctypes.c_int),
     "nf_cascade_attention": ([_P, _I64, _P, _I64, _P, _P, _I32, _I32, _I32, _I32, _I32, _I32, _P, _I32,
-                              _P, _P, _I32, _I32, _P, _I32, _P, _I32, _P, _I32, ctypes.c_float, _P, _P],
-                             ctypes.c_int),
+                              _P, _P, _I32, _I32, _P, _I32, _P, _I32, ctypes.c_float, _P, _P], ctypes.c_int),
     "nf_kv_append": ([_P, _P, _I32, _I64, _P, _P, _I32, _I64, _I64, _P, _P, _I32,
                       _I32, _I32, _P, _I32, _P, _P, _P], ctypes.c_int),
     "nf_attention_workspace": ([_I32, _I32, _I32, _I32, _I32, _I32,

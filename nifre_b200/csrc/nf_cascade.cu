@@ -40,11 +40,9 @@ struct CascadeParams {
   const int* items;   // per query token: slot, q_row, kv_len, unit_base
   const int* counts;  // of nf_pack_step: [0] tokens, [3] partial slots
   int max_items, max_units;
-  const int* groups;  // [n_groups][4]: representative slot, first, count, 0
-  int n_groups;
-  const int* tasks;   // [n_tasks][4]: group, key_begin, key_end, part
+  const int* tasks;   // [n_tasks][8]: slot, first, count, part, key_begin, key_end, 0, 0
   int n_tasks;
-  const int* toks;    // query tokens of the groups
+  const int* toks;    // [n_toks][2]: item (query token), q row
   int n_toks;
   float scale_log2;
   int* status;
@@ -67,29 +65,34 @@ __global__ void __launch_bounds__(kCascThreads, D_ == 64 ? 2 : 1) cascade_kernel
   constexpr int CHUNKS = D_ / 8;            // 16-byte chunks per key row
   const int task = blockIdx.x, kvh = blockIdx.y;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int4 tk = __ldg(reinterpret_cast<const int4*>(p.tasks) + task);
-  if (tk.x < 0 || tk.x >= p.n_groups) {
+  // the task: ta = (slot whose table holds the shared blocks, first query, queries, part), tb.x/y = keys
+  const int4 ta = __ldg(reinterpret_cast<const int4*>(p.tasks) + 2 * task);
+  const int4 tb = __ldg(reinterpret_cast<const int4*>(p.tasks) + 2 * task + 1);
+  const int k0 = tb.x, k1 = tb.y;
+  if (ta.x < 0 || ta.y < 0 || ta.z <= 0 || ta.y + ta.z > p.n_toks || ta.z > kCascRows / p.G || ta.w < 0 ||
+      k0 < 0 || k1 <= k0 || (k0 & 15) || (k1 & 15) || k1 > p.max_blocks * p.bs ||
+      k1 - k0 > kCascStages * kCascKeys) {
     if (tid == 0) atomicOr(p.status, NF_STATUS_BAD_SHARED);
     return;
   }
-  const int4 gr = __ldg(reinterpret_cast<const int4*>(p.groups) + tk.x);
-  const int per_cta = kCascRows / p.G;  // sequences a CTA holds
-  if (gr.x < 0 || gr.y < 0 || gr.z <= 0 || gr.y + gr.z > p.n_toks || gr.z > per_cta || tk.y < 0 ||
-      tk.z <= tk.y || (tk.y & 15) || (tk.z & 15) || tk.z > p.max_blocks * p.bs || tk.w < 0 ||
-      tk.z - tk.y > kCascStages * kCascKeys) {
-    if (tid == 0) atomicOr(p.status, NF_STATUS_BAD_SHARED);
-    return;
-  }
+  // this thread's rows: r0 = 16 warp + lane / 4 and r0 + 8 (row = query * G + head); their
+  // records are requested now, beside the block ids
+  const int r0 = warp * 16 + (lane >> 2), r1 = r0 + 8;
+  const int rows = ta.z * p.G;
+  const bool live = warp * 16 < rows;  // warps past the last row only stage
+  int2 tq0 = make_int2(-1, 0), tq1 = make_int2(-1, 0);
+  if (r0 < rows) tq0 = __ldg(reinterpret_cast<const int2*>(p.toks) + ta.y + r0 / p.G);
+  if (r1 < rows) tq1 = __ldg(reinterpret_cast<const int2*>(p.toks) + ta.y + r1 / p.G);
   const int n_items = min(__ldg(p.counts), p.max_items);
   const int n_slots = min(__ldg(p.counts + 3), p.max_units);
-  const int* btrow = p.bt + (long long)gr.x * p.max_blocks;
+  const int* btrow = p.bt + (long long)ta.x * p.max_blocks;
   const uint32_t sK = smem_u32(casc_smem), sV = sK + kCascStages * SLICE;
 
   // pool row of the first key of each 16-key group of the range (-1: a bad block id)
   __shared__ long long grp_row[kCascStages * kCascKeys / 16];
-  const int n_grp = (tk.z - tk.y) >> 4;
+  const int n_grp = (k1 - k0) >> 4;
   if (tid < n_grp) {
-    const int key = tk.y + 16 * tid;
+    const int key = k0 + 16 * tid;
     const int blk = __ldg(btrow + key / p.bs);
     if (blk < 0 || blk >= p.num_blocks) {
       atomicOr(p.status, NF_STATUS_BAD_BLOCK);
@@ -101,7 +104,7 @@ __global__ void __launch_bounds__(kCascThreads, D_ == 64 ? 2 : 1) cascade_kernel
   __syncthreads();
   // every slice of the range in flight at once, one copy group per slice;
   // rows past the range are zeros (their scores are masked; 0 * P stays 0)
-  const int n_slices = (tk.z - tk.y + kCascKeys - 1) / kCascKeys;
+  const int n_slices = (k1 - k0 + kCascKeys - 1) / kCascKeys;
   for (int i = 0; i < n_slices; ++i) {
     for (int c = tid; c < kCascKeys * CHUNKS; c += kCascThreads) {
       const int r = c / CHUNKS, ch = c - r * CHUNKS;
@@ -120,26 +123,28 @@ __global__ void __launch_bounds__(kCascThreads, D_ == 64 ? 2 : 1) cascade_kernel
     cp_async_commit();
   }
 
-  // this thread's rows: r0 = 16 warp + lane / 4 and r0 + 8 (row = sequence * G + head)
-  const int r0 = warp * 16 + (lane >> 2), r1 = r0 + 8;
-  const int rows = gr.z * p.G;
-  const bool live = warp * 16 < rows;  // warps past the last row only stage
-  int tok0 = -1, tok1 = -1;
-  if (r0 < rows) tok0 = __ldg(p.toks + gr.y + r0 / p.G);
-  if (r1 < rows) tok1 = __ldg(p.toks + gr.y + r1 / p.G);
-  if (tok0 >= n_items) tok0 = -1;
-  if (tok1 >= n_items) tok1 = -1;
-  // Q fragments (A operand, rows r0/r1, columns 16 ks + 2 (lane % 4) (+1, +8, +9))
+  const int tok0 = tq0.x >= 0 && tq0.x < n_items ? tq0.x : -1;
+  const int tok1 = tq1.x >= 0 && tq1.x < n_items ? tq1.x : -1;
+  // partial slots of the rows' items (checked at the store), requested beside the query rows
+  int base0 = -1, next0 = 0, base1 = -1, next1 = 0;
+  if (tok0 >= 0) {
+    base0 = __ldg(p.items + 4 * tok0 + 3);
+    next0 = tok0 + 1 < n_items ? __ldg(p.items + 4 * (tok0 + 1) + 3) : n_slots;
+  }
+  if (tok1 >= 0) {
+    base1 = __ldg(p.items + 4 * tok1 + 3);
+    next1 = tok1 + 1 < n_items ? __ldg(p.items + 4 * (tok1 + 1) + 3) : n_slots;
+  }
+  // Q fragments (A operand, rows r0/r1, columns 16 ks + 2 (lane % 4) (+1, +8, +9)); the q rows
+  // come with the query records (the rows nf_pack_step gives these items)
   uint32_t qa[KS][4];
   {
     const T* q0 = nullptr;
     const T* q1 = nullptr;
     if (tok0 >= 0)
-      q0 = reinterpret_cast<const T*>(p.q) + (long long)__ldg(p.items + 4 * tok0 + 1) * p.q_stride +
-           (long long)(kvh * p.G + r0 % p.G) * D_;
+      q0 = reinterpret_cast<const T*>(p.q) + (long long)tq0.y * p.q_stride + (long long)(kvh * p.G + r0 % p.G) * D_;
     if (tok1 >= 0)
-      q1 = reinterpret_cast<const T*>(p.q) + (long long)__ldg(p.items + 4 * tok1 + 1) * p.q_stride +
-           (long long)(kvh * p.G + r1 % p.G) * D_;
+      q1 = reinterpret_cast<const T*>(p.q) + (long long)tq1.y * p.q_stride + (long long)(kvh * p.G + r1 % p.G) * D_;
     const int c = 2 * (lane & 3);
 #pragma unroll
     for (int ks = 0; ks < KS; ++ks) {
@@ -176,11 +181,11 @@ __global__ void __launch_bounds__(kCascThreads, D_ == 64 ? 2 : 1) cascade_kernel
         }
       }
       // scale, mask keys past the range, running maximum per row
-      const int kbase = tk.y + i * kCascKeys + 2 * (lane & 3);
+      const int kbase = k0 + i * kCascKeys + 2 * (lane & 3);
       float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        const bool v0 = kbase + 8 * j < tk.z, v1 = kbase + 8 * j + 1 < tk.z;
+        const bool v0 = kbase + 8 * j < k1, v1 = kbase + 8 * j + 1 < k1;
         s[j][0] = v0 ? s[j][0] * p.scale_log2 : -INFINITY;
         s[j][1] = v1 ? s[j][1] * p.scale_log2 : -INFINITY;
         s[j][2] = v0 ? s[j][2] * p.scale_log2 : -INFINITY;
@@ -234,11 +239,9 @@ __global__ void __launch_bounds__(kCascThreads, D_ == 64 ? 2 : 1) cascade_kernel
   l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
   l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
   // partial records: slot unit_base + part of each row's item, inside that item's slots
-  auto store = [&](int tok, int r, float (&acc)[NO][4], int h, float m, float l) {
+  auto store = [&](int tok, int base, int next, int r, float (&acc)[NO][4], int h, float m, float l) {
     if (tok < 0) return;
-    const int base = __ldg(p.items + 4 * tok + 3);
-    const int next = tok + 1 < n_items ? __ldg(p.items + 4 * (tok + 1) + 3) : n_slots;
-    const int slot = base + tk.w;
+    const int slot = base + ta.w;
     if (base < 0 || slot >= next || slot >= p.max_units) {
       if ((lane & 3) == 0) atomicOr(p.status, NF_STATUS_UNIT_OVERFLOW);
       return;
@@ -250,8 +253,8 @@ __global__ void __launch_bounds__(kCascThreads, D_ == 64 ? 2 : 1) cascade_kernel
       __stcg(reinterpret_cast<float2*>(w + 8 * n + c), make_float2(acc[n][h], acc[n][h + 1]));
     if ((lane & 3) == 0) __stcg(reinterpret_cast<float2*>(w + D_), make_float2(m, l));
   };
-  store(tok0, r0, o, 0, m0, l0);
-  store(tok1, r1, o, 2, m1, l1);
+  store(tok0, base0, next0, r0, o, 0, m0, l0);
+  store(tok1, base1, next1, r1, o, 2, m1, l1);
 }
 
 }  // namespace nf
@@ -261,9 +264,8 @@ extern "C" int nf_cascade_attention(float* ws_partials, int64_t ws_partial_float
                                     int32_t num_kv_heads, int32_t head_dim, int32_t block_size, int32_t num_blocks,
                                     const int32_t* block_tables, int32_t max_blocks_per_seq, const int32_t* items,
                                     const int32_t* counts, int32_t max_items, int32_t max_units,
-                                    const int32_t* groups, int32_t n_groups, const int32_t* tasks, int32_t n_tasks,
-                                    const int32_t* toks, int32_t n_toks, float scale, int32_t* status,
-                                    void* stream) {
+                                    const int32_t* tasks, int32_t n_tasks, const int32_t* toks, int32_t n_toks,
+                                    float scale, int32_t* status, void* stream) {
   using namespace nf;
   if (n_tasks == 0) return ok();
   if (dtype != NF_BF16 && dtype != NF_F16)
@@ -276,19 +278,17 @@ extern "C" int nf_cascade_attention(float* ws_partials, int64_t ws_partial_float
   if (G > kCascRows) return fail(NF_EUNSUPPORTED, "nf_cascade_attention: %d query heads per KV head", G);
   if (block_size <= 0 || block_size % 16)
     return fail(NF_EUNSUPPORTED, "nf_cascade_attention: block_size %d is not a multiple of 16", block_size);
-  if (!ws_partials || !q || !k_pool || !v_pool || !block_tables || !items || !counts || !groups || !tasks || !toks ||
-      !status)
+  if (!ws_partials || !q || !k_pool || !v_pool || !block_tables || !items || !counts || !tasks || !toks || !status)
     return fail(NF_EINVAL, "nf_cascade_attention: null pointer argument");
-  if (n_tasks < 0 || n_groups <= 0 || n_toks <= 0 || num_blocks <= 0 || max_blocks_per_seq <= 0 || max_items <= 0 ||
-      max_units <= 0)
+  if (n_tasks < 0 || n_toks <= 0 || num_blocks <= 0 || max_blocks_per_seq <= 0 || max_items <= 0 || max_units <= 0)
     return fail(NF_EINVAL, "nf_cascade_attention: sizes must be positive");
   if ((int64_t)max_units * num_q_heads * (head_dim + 4) > ws_partial_floats)
     return fail(NF_EINVAL, "nf_cascade_attention: workspace holds fewer than max_units partial slots");
   auto al = [](const void* ptr, size_t a) { return (reinterpret_cast<uintptr_t>(ptr) % a) == 0; };
   if (!al(k_pool, 16) || !al(v_pool, 16) || !al(q, 4) || (q_row_stride * 2) % 4 != 0)
     return fail(NF_EINVAL, "nf_cascade_attention: pools must be 16-byte and q rows 4-byte aligned");
-  if (!al(ws_partials, 8) || !al(items, 16) || !al(groups, 16) || !al(tasks, 16))
-    return fail(NF_EINVAL, "nf_cascade_attention: items, groups and tasks must be 16-byte aligned");
+  if (!al(ws_partials, 8) || !al(items, 16) || !al(tasks, 16) || !al(toks, 8))
+    return fail(NF_EINVAL, "nf_cascade_attention: items and tasks must be 16-byte, toks 8-byte aligned");
   if (n_tasks > 65535 * 1024) return fail(NF_EINVAL, "nf_cascade_attention: too many tasks (%d)", n_tasks);
   CascadeParams p;
   p.ws = ws_partials;
@@ -308,8 +308,6 @@ extern "C" int nf_cascade_attention(float* ws_partials, int64_t ws_partial_float
   p.counts = counts;
   p.max_items = max_items;
   p.max_units = max_units;
-  p.groups = groups;
-  p.n_groups = n_groups;
   p.tasks = tasks;
   p.n_tasks = n_tasks;
   p.toks = toks;

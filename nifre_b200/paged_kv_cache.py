@@ -118,8 +118,9 @@ class StepPlan:
         # split-K units of the step, and the tensor-core prefill tiles (tiles, n_tiles, q_heads)
         self.decode_units = max_units
         self.shared_keys = None  # per sequence: leading keys served by the cascade kernel (numpy)
-        self.n_casc_groups = self.n_casc_tasks = self.n_casc_toks = 0
-        self.casc_groups = self.casc_tasks = self.casc_toks = None
+        self.ws_sizes = None  # (query heads, partial floats, counter ints) of the split-K workspace
+        self.n_casc_tasks = self.n_casc_toks = 0
+        self.casc_tasks = self.casc_toks = None  # device: (slot, first, count, part, k0, k1, 0, 0), (item, q row)
         self.tiles = None
         self.n_tiles = 0
         self.q_heads = None
@@ -293,6 +294,7 @@ class PagedKVCache:
     CASCADE_MIN_KEYS = 64
     CASCADE_ROWS = 128  # query rows per nf_cascade_attention CTA
     CASCADE_MAX_KEYS = 256  # keys per nf_cascade_attention task
+    CASCADE_WAVES = 2  # cascade CTAs per SM aimed for (two are resident at once)
 
     def cascade_supported(self, q_heads: int | None) -> bool:
         """True when nf_cascade_attention serves this cache with q_heads query heads."""
@@ -301,25 +303,28 @@ class PagedKVCache:
         return (self.dtype in (torch.bfloat16, torch.float16) and self.head_dim in (64, 128)
                 and q_heads // self.n_heads <= self.CASCADE_ROWS and self.block_size % 16 == 0)
 
-    def _cascade_groups(self, slots, q_lens, ctx, dec, group: int):
+    def _cascade_groups(self, slots, q_lens, q_starts, ctx, dec, group: int):
         """Decode sequences that start with the same physical blocks, and the cascade work over those keys.
 
         Sequences with one new token whose tables begin with the same block
         are grouped; a group's shared keys are the blocks all its members
         hold at the same positions (imported prefix blocks: full, written
         before the step).  Members are cut into CTA groups of at most
-        ``CASCADE_ROWS / group`` sequences (at least two each) and the shared
-        keys into ranges of a common size (64 to ``CASCADE_MAX_KEYS`` keys)
-        chosen so that the tasks fill about one wave of SMs.  Returns per-sequence shared keys and cascade part
-        counts, and the (slot, first, count, 0) groups, (group, key_begin,
-        key_end, part) tasks and query tokens for ``nf_cascade_attention``.
+        ``CASCADE_ROWS / group`` sequences (at least two each) and each
+        group's shared keys into near-equal ranges of whole 16-key tiles, at
+        most ``CASCADE_MAX_KEYS`` keys, with ranges handed out in proportion
+        to the groups' shared keys so that (range, KV head) CTAs number about
+        ``CASCADE_WAVES`` per SM.  Returns per-sequence shared keys and
+        cascade part counts, the (slot, first, count, part, key_begin,
+        key_end, 0, 0) tasks and the (item, q row) query records for
+        ``nf_cascade_attention``.
         """
         S, bs = len(slots), self.block_size
         # Decode steps repeat the same batch: while its sequences, their new
         # token counts and their tables' epochs (which change only when
         # leading entries are replaced) are those of the previous step, the
         # shared runs are unchanged and the previous grouping stands.
-        key = (slots.tobytes(), q_lens.tobytes(), dec.tobytes(), group,
+        key = (slots.tobytes(), q_lens.tobytes(), q_starts.tobytes(), dec.tobytes(), group,
                tuple(self.block_tables[s].epoch for s in slots.tolist()))
         if (self._cascade_memo is not None and self._cascade_memo[0] == key
                 and (self._cascade_memo[1][0] <= ctx).all()):  # no position moved back under a shared run
@@ -349,22 +354,24 @@ class PagedKVCache:
                 part = members[c0: c0 + per_cta]
                 if len(part) >= 2:
                     cuts.append((part, n * bs))
-        groups, tasks, toks = [], [], []
-        if not cuts:
-            self._cascade_memo = (key, (shared, nparts, groups, tasks, toks))
-            return shared, nparts, groups, tasks, toks
-        want = sum(p for _, p in cuts) * self.n_heads / max(1, self.sm_count)
-        ck = int(min(self.CASCADE_MAX_KEYS, max(64, math.ceil(want / 64.0) * 64)))
-        tok_off = np.cumsum(q_lens) - q_lens
-        for g, (members, p) in enumerate(cuts):
-            nc = (p + ck - 1) // ck
-            groups.append((int(slots[members[0]]), len(toks), len(members), 0))
-            tasks.extend((g, c * ck, min((c + 1) * ck, p), c) for c in range(nc))
-            toks.extend(int(tok_off[i]) for i in members)
-            shared[members] = p
-            nparts[members] = nc
-        self._cascade_memo = (key, (shared, nparts, groups, tasks, toks))
-        return shared, nparts, groups, tasks, toks
+        tasks, toks = [], []
+        if cuts:
+            total = sum(p for _, p in cuts)
+            want = max(len(cuts), round(self.CASCADE_WAVES * self.sm_count / self.n_heads))
+            tok_off = np.cumsum(q_lens) - q_lens
+            for members, p in cuts:
+                tiles = p // 16
+                nc = max(1, round(want * p / total), -(-p // self.CASCADE_MAX_KEYS))
+                nc = min(nc, tiles)
+                edges = [16 * (tiles * c // nc) for c in range(nc + 1)]
+                first = len(toks)
+                toks.extend((int(tok_off[i]), int(q_starts[i])) for i in members)
+                tasks.extend((int(slots[members[0]]), first, len(members), c, edges[c], edges[c + 1], 0, 0)
+                             for c in range(nc))
+                shared[members] = p
+                nparts[members] = nc
+        self._cascade_memo = (key, (shared, nparts, tasks, toks))
+        return shared, nparts, tasks, toks
 
     def plan(self, slots, q_lens, q_starts, split: int | None = None, fine_tail: bool = True,
              q_heads: int | None = None) -> StepPlan:
@@ -425,10 +432,10 @@ class PagedKVCache:
         routed = (q_lens >= self.PREFILL_MIN_TOKENS) if self.prefill_supported(q_heads) else np.zeros(S, bool)
         dec = ~routed
         if self.cascade_supported(q_heads) and dec.any():
-            shared, nparts, cgroups, ctasks, ctoks = self._cascade_groups(slots, q_lens, ctx, dec,
-                                                                          q_heads // self.n_heads)
+            shared, nparts, ctasks, ctoks = self._cascade_groups(slots, q_lens, q_starts, ctx, dec,
+                                                                 q_heads // self.n_heads)
         else:
-            shared, nparts, cgroups, ctasks, ctoks = (np.zeros(S, np.int32), np.zeros(S, np.int32), [], [], [])
+            shared, nparts, ctasks, ctoks = np.zeros(S, np.int32), np.zeros(S, np.int32), [], []
         tok_dec = np.repeat(dec, q_lens)
         kv_dec = kv[tok_dec] - np.repeat(shared.astype(np.int64), q_lens)[tok_dec]  # each query's own keys
         if split is None:
@@ -455,12 +462,11 @@ class PagedKVCache:
         sched = _prefill_order(tiles, self.n_heads) if n_tiles else np.zeros(0, np.int32)
         off_tiles = _align4(S * 5 + P * 3)
         off_sched = off_tiles + 4 * n_tiles
-        n_cg, n_ct, n_tok = len(cgroups), len(ctasks), len(ctoks)
+        n_ct, n_tok = len(ctasks), len(ctoks)
         off_shared = _align4(off_sched + sched.size)
-        off_cg = _align4(off_shared + 2 * S)
-        off_ct = off_cg + 4 * n_cg
-        off_tok = off_ct + 4 * n_ct
-        host = np.zeros(off_tok + n_tok, dtype=np.int32)
+        off_ct = _align4(off_shared + 2 * S)
+        off_tok = off_ct + 8 * n_ct
+        host = np.zeros(off_tok + 2 * n_tok, dtype=np.int32)
         host[: S * 4] = np.stack([slots, q_starts, q_lens, ctx], axis=1).reshape(-1)
         if P:
             host[S * 4: S * 4 + P * 3] = np.asarray(patches, dtype=np.int32).reshape(-1)
@@ -470,9 +476,8 @@ class PagedKVCache:
             host[off_sched:off_sched + sched.size] = sched
         if n_ct:
             host[off_shared:off_shared + 2 * S] = np.stack([shared, nparts], axis=1).reshape(-1)
-            host[off_cg:off_ct] = np.asarray(cgroups, dtype=np.int32).reshape(-1)
             host[off_ct:off_tok] = np.asarray(ctasks, dtype=np.int32).reshape(-1)
-            host[off_tok:] = np.asarray(ctoks, dtype=np.int32)
+            host[off_tok:] = np.asarray(ctoks, dtype=np.int32).reshape(-1)
         off_slot = _align4(host.size)
         off_src = off_slot + T
         off_items = _align4(off_src + T)
@@ -486,10 +491,9 @@ class PagedKVCache:
         plan.decode_units = n_units
         plan.q_heads = q_heads
         plan.shared_keys = shared
-        plan.n_casc_groups, plan.n_casc_tasks, plan.n_casc_toks = n_cg, n_ct, n_tok
-        plan.casc_groups = meta[off_cg: off_ct]
+        plan.n_casc_tasks, plan.n_casc_toks = n_ct, n_tok
         plan.casc_tasks = meta[off_ct: off_tok]
-        plan.casc_toks = meta[off_tok: off_tok + n_tok]
+        plan.casc_toks = meta[off_tok: off_tok + 2 * n_tok]
         plan.n_tiles = n_tiles
         plan.tiles = meta[off_tiles: off_tiles + 4 * n_tiles]
         plan.sched = meta[off_sched: off_sched + sched.size]
@@ -583,7 +587,10 @@ class PagedKVCache:
             events[1].record()
         if plan.decode_units:
             max_items = plan.n_tokens
-            pf, ci = _lib.workspace_sizes(plan.max_units, max_items, hq, self.n_heads, D, self.dtype)
+            if plan.ws_sizes is None or plan.ws_sizes[0] != hq:  # the same for every layer of the step
+                plan.ws_sizes = (hq, *_lib.workspace_sizes(plan.max_units, max_items, hq, self.n_heads, D,
+                                                           self.dtype))
+            _, pf, ci = plan.ws_sizes
             ws = self._ws_partials.get(pf)
             cnt = self._ws_counters.get(ci)
             if plan.n_casc_tasks:
@@ -595,7 +602,7 @@ class PagedKVCache:
                     self.k[layer_id].data_ptr(), self.v[layer_id].data_ptr(), _lib.dtype_code(self.dtype),
                     hq, self.n_heads, D, self.block_size, self.num_blocks, self.bt_dev.data_ptr(),
                     self.max_blocks_per_seq, plan.items.data_ptr(), plan.counts.data_ptr(), max_items,
-                    plan.max_units, plan.casc_groups.data_ptr(), plan.n_casc_groups, plan.casc_tasks.data_ptr(),
+                    plan.max_units, plan.casc_tasks.data_ptr(),
                     plan.n_casc_tasks, plan.casc_toks.data_ptr(), plan.n_casc_toks, float(scale),
                     self.status.data_ptr(), stream), "nf_cascade_attention")
             _lib.check(lib.nf_paged_attention(

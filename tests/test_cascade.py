@@ -54,36 +54,48 @@ def test_cascade_groups_host():
     S = len(tables)
     slots = np.arange(S)
     q_lens = np.ones(S, dtype=np.int64)
+    q_starts = np.arange(S, dtype=np.int64) * 3 + 5  # rows of the queries in q
     dec = np.ones(S, dtype=bool)
-    shared, nparts, groups, tasks, toks = c._cascade_groups(slots, q_lens, np.asarray(ctx), dec, 4)
+    shared, nparts, tasks, toks = c._cascade_groups(slots, q_lens, q_starts, np.asarray(ctx), dec, 4)
     # prefix A: 41 members whose common run is 10 blocks -> groups of 32 and 9
     assert shared[:41].tolist() == [160] * 41
     assert shared[41:43].tolist() == [64, 64] and shared[43] == 0
+    groups = sorted({(t[0], t[1], t[2]) for t in tasks}, key=lambda g: g[1])
     assert [g[2] for g in groups] == [32, 9, 2]
-    assert sorted(toks) == list(range(43))
-    for g, (slot, first, count, _) in enumerate(groups):
-        members = toks[first:first + count]
+    assert sorted(t for t, _ in toks) == list(range(43))
+    assert all(row == q_starts[t] for t, row in toks)
+    # CASCADE_WAVES x 148 SMs / 8 KV heads = 37 ranges wanted, in proportion to the shared keys; runs this
+    # short give one 16-key tile per range (10 + 10 + 4)
+    assert len(tasks) == 24
+    for slot, first, count in groups:
+        members = [t for t, _ in toks[first:first + count]]
         assert slot == members[0]
-        mine = [t for t in tasks if t[0] == g]
+        mine = [t for t in tasks if t[1] == first]
         assert [t[3] for t in mine] == list(range(len(mine)))
-        assert mine[0][1] == 0 and mine[-1][2] == shared[members[0]]
-        assert all(a[2] == b[1] for a, b in zip(mine, mine[1:]))  # contiguous key ranges
-        assert all(t[1] % 16 == 0 and t[2] % 16 == 0 for t in mine)
+        assert mine[0][4] == 0 and mine[-1][5] == shared[members[0]]
+        assert all(a[5] == b[4] for a, b in zip(mine, mine[1:]))  # contiguous key ranges
+        assert all(t[4] % 16 == 0 and t[5] % 16 == 0 and 16 <= t[5] - t[4] <= c.CASCADE_MAX_KEYS for t in mine)
+        assert max(t[5] - t[4] for t in mine) - min(t[5] - t[4] for t in mine) <= 16  # near-equal ranges
         assert all(nparts[m] == len(mine) for m in members)
     # sequences with more than one new token are never grouped
     q2 = q_lens.copy()
     q2[:] = 2
-    assert c._cascade_groups(slots, q2, np.asarray(ctx), dec, 4)[2] == []
+    assert c._cascade_groups(slots, q2, q_starts, np.asarray(ctx), dec, 4)[2] == []
     # with G = 8, at most 16 sequences per group
-    groups8 = c._cascade_groups(slots, q_lens, np.asarray(ctx), dec, 8)[2]
-    assert max(g[2] for g in groups8) == 16
+    tasks8 = c._cascade_groups(slots, q_lens, q_starts, np.asarray(ctx), dec, 8)[2]
+    assert max(t[2] for t in tasks8) == 16
+    # a long shared run is cut into ranges of at most CASCADE_MAX_KEYS keys
+    long_c = _host_cache([list(range(200)) + [900 + i] for i in range(4)], [200 * bs + 7] * 4, bs)
+    lt = long_c._cascade_groups(np.arange(4), np.ones(4, np.int64), np.arange(4), np.full(4, 200 * bs + 7),
+                                np.ones(4, bool), 4)[2]
+    assert len(lt) == 37 and max(t[5] - t[4] for t in lt) <= 256  # 37 ranges of 5-6 tiles
     # the next decode step of the same batch reuses the grouping; a replaced table or a position moved
     # back under a shared run recomputes it
-    again = c._cascade_groups(slots, q_lens, np.asarray(ctx) + 1, dec, 8)
-    assert again is c._cascade_groups(slots, q_lens, np.asarray(ctx) + 2, dec, 8)
-    assert c._cascade_groups(slots, q_lens, np.asarray(ctx) - 1000, dec, 8) is not again
+    again = c._cascade_groups(slots, q_lens, q_starts, np.asarray(ctx) + 1, dec, 8)
+    assert again is c._cascade_groups(slots, q_lens, q_starts, np.asarray(ctx) + 2, dec, 8)
+    assert c._cascade_groups(slots, q_lens, q_starts, np.asarray(ctx) - 1000, dec, 8) is not again
     c.block_tables[3].epoch += 1
-    assert c._cascade_groups(slots, q_lens, np.asarray(ctx), dec, 8) is not again
+    assert c._cascade_groups(slots, q_lens, q_starts, np.asarray(ctx), dec, 8) is not again
 
 
 def _shared_prefix_cache(hq, hkv, D, prefixes, n_per, suffix, dtype, seed, tail_div=None):
@@ -152,9 +164,9 @@ def test_cascade_matches_plain_decode_and_many_groups():
         plan = cache.plan(list(range(B)), [1] * B, list(range(B)), q_heads=32)
         assert (plan.n_casc_tasks > 0) == casc
         if casc:
-            groups = plan.casc_groups.view(-1, 4).cpu().numpy()
-            assert sorted(groups[:, 2].tolist()) == [8, 32]
-            assert plan.n_casc_tasks > 2 * 8 // 8
+            tasks = plan.casc_tasks.view(-1, 8).cpu().numpy()
+            assert sorted({(int(t[1]), int(t[2])) for t in tasks}) == [(0, 32), (32, 8)]
+            assert plan.n_casc_tasks > 2
         q = torch.randn(B, 32 * 64, generator=g).to(torch.bfloat16).to(DEV)
         k = torch.randn(B, 8 * 64, generator=g).to(torch.bfloat16).to(DEV)
         v = torch.randn(B, 8 * 64, generator=g).to(torch.bfloat16).to(DEV)
@@ -168,7 +180,7 @@ def test_cascade_matches_plain_decode_and_many_groups():
 
 @pytest.mark.gpu
 def test_cascade_bad_task_flagged():
-    """A task naming a group that does not exist is flagged on the status word and writes nothing."""
+    """A task naming more queries than there are records is flagged on the status word and writes nothing."""
     from nifre_b200 import _lib
     cache, g = _shared_prefix_cache(32, 8, 64, [256], 4, (1, 20), torch.bfloat16, seed=9)
     B = cache.batch_size
@@ -176,13 +188,13 @@ def test_cascade_bad_task_flagged():
     assert plan.n_casc_tasks > 0
     lib = _lib.load()
     ws = torch.zeros(plan.max_units * 32 * 68, dtype=torch.float32, device=DEV)
-    bad = torch.tensor([7, 0, 64, 0], dtype=torch.int32, device=DEV)
+    bad = torch.tensor([0, 0, 1000, 0, 0, 64, 0, 0], dtype=torch.int32, device=DEV)  # more queries than records
     q = torch.zeros(B, 32 * 64, dtype=torch.bfloat16, device=DEV)
     _lib.check(lib.nf_cascade_attention(
         ws.data_ptr(), ws.numel(), q.data_ptr(), q.stride(0), cache.k[0].data_ptr(), cache.v[0].data_ptr(),
         _lib.NF_BF16, 32, 8, 64, 16, cache.num_blocks, cache.bt_dev.data_ptr(), cache.max_blocks_per_seq,
-        plan.items.data_ptr(), plan.counts.data_ptr(), B, plan.max_units, plan.casc_groups.data_ptr(),
-        plan.n_casc_groups, bad.data_ptr(), 1, plan.casc_toks.data_ptr(), plan.n_casc_toks, 0.125,
+        plan.items.data_ptr(), plan.counts.data_ptr(), B, plan.max_units, bad.data_ptr(), 1,
+        plan.casc_toks.data_ptr(), plan.n_casc_toks, 0.125,
         cache.status.data_ptr(), _lib.stream_handle(cache.device)), "nf_cascade_attention")
     torch.cuda.synchronize()
     assert int(cache.status.item()) == _lib.NF_STATUS_BAD_SHARED
