@@ -71,6 +71,12 @@ WORKLOADS = {
                                suffix_hi=256, vocab=50257, cpu_sample=8,
                                metric="paged-attn decode tok/s over shared prefixes (1B shape, 16 layers, 128 seqs "
                                       "on 4 shared 1024-token prefixes)"),
+    # the end-to-end configuration: the GPT-124M engine (fp32, context 2048, seed 0) generating 64 greedy
+    # tokens for 8 requests whose prompts are U[32, 256] random ids, through Engine.add_request / step
+    "gpt124m-engine": dict(kind="engine", layers=12, resident=12, hq=12, hkv=12, d=64, bs=16, seed=0,
+                           scaling="weak", steps=130, requests=8, prompt_lo=32, prompt_hi=256, new_tokens=64,
+                           seqs=8, ctx_lo=32, ctx_hi=320, cpu_sample=1,
+                           metric="engine greedy generation tok/s (GPT-124M fp32, 8 requests x 64 new tokens)"),
 }
 CFG = dict(name="llama3.2-1b-decode", **WORKLOADS["llama3.2-1b-decode"])
 METRIC = CFG["metric"]
@@ -529,6 +535,16 @@ def run_reference(args):
     if rank != 0:
         return
     threads = os.cpu_count() or 1
+    if CFG.get("kind") == "engine":
+        cpu = cpu_engine_rate(max(5.0, 1.0 * args.steps / 10), threads=threads)
+        line = {"impl": "reference", "metric": METRIC, "value": cpu["value"], "unit": "tok/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": CFG["scaling"],
+                "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
+                "config": {"workload": CFG["name"], "model": "GPT-124M (12 layers, 12 heads, d 64, context 2048)"},
+                "cpu_baseline": dict(cpu, kind="port"),
+                "e2e": {"value": cpu["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
     if CFG.get("kind") == "mixed":
         cpu = CpuOracleMixed(threads=threads)
         for _ in range(args.warmup):
@@ -818,6 +834,192 @@ def run_mixed(args):
         dist.destroy_process_group()
 
 
+# ---------------------------------------------------------------------------- end-to-end engine (GPT-124M)
+def _engine_prompts(seed):
+    """The workload's prompts: Python's random seeded with ``seed`` (seed 0 is the end-to-end configuration)."""
+    import random
+    rnd = random.Random(seed)
+    out = []
+    for _ in range(CFG["requests"]):
+        n = rnd.randint(CFG["prompt_lo"], CFG["prompt_hi"])
+        out.append([rnd.randrange(50257) for _ in range(n)])
+    return out
+
+
+def _engine_model(dev):
+    from nifre_b200.gpt import GPT_CONFIG_124M, GptModel
+    cfg = dict(GPT_CONFIG_124M, context_length=2048)
+    torch.manual_seed(CFG["seed"])
+    return GptModel(cfg).eval().to(dev)
+
+
+def cpu_engine_rate(seconds: float, threads: int | None = None):
+    """The reference's greedy generation on the host cores (oracle/engine.py port, one request at a time as the
+    reference's rows are): decode tok/s over the first prompts of the workload, stopped after ``seconds``."""
+    from oracle.engine import greedy_generate
+    if threads:
+        torch.set_num_threads(threads)
+    model = _engine_model("cpu")
+    toks, spent, n_req = 0, 0.0, 0
+    for prompt in _engine_prompts(CFG["seed"]):
+        _, t, n = greedy_generate(model, prompt, CFG["new_tokens"])
+        toks += n
+        spent += t
+        n_req += 1
+        if spent >= seconds:
+            break
+    return {"value": toks / spent, "unit": "tok/s", "cores": torch.get_num_threads(),
+            "sample": f"{n_req} of {CFG['requests']} requests, {toks} decode steps of one request each "
+                      f"({spent:.1f} s), prefill excluded"}
+
+
+def run_engine(args):
+    """Greedy generation through the engine: every timed step is one Engine.step() (host scheduling, one
+    upload of the step's ids/positions, the flat forward, one download of the sampled tokens); N GPUs run N
+    independent replicas."""
+    from nifre_b200 import Engine, GptInferenceModel
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    torch.backends.cuda.matmul.allow_tf32 = False  # fp32 GEMMs, as the parity test runs them
+    eng = Engine(GptInferenceModel(_engine_model(dev)), max_concurrent_requests=CFG["requests"], device=dev,
+                 prefill_chunk_size=128, max_tokens_per_step=2048)
+    stream = torch.cuda.current_stream(dev)
+    stats = {"steps": 0, "tokens": 0, "h2d": 0, "d2h": 0, "launches": 0, "rec": [], "record": False}
+
+    def generation(seed):
+        ids = [eng.add_request(p, CFG["new_tokens"]) for p in _engine_prompts(seed)]
+        while eng.step():
+            stats["steps"] += 1
+        done = eng.get_completed()
+        stats["tokens"] += sum(len(done[i].output_token_ids) for i in ids)
+
+    generation(1000 + rank)  # warm-up generation: builds the cache, the workspaces and cuBLAS handles
+    for w in range(args.warmup - 1):
+        generation(2000 + w)
+    cache = eng.cache
+    plan_fn, append_fn, attn_fn = cache.plan, cache.append_step, cache.attention_step
+    run_fn = eng.model_runner.run_step
+    last = {}
+
+    def plan_w(*a, **k):
+        p = plan_fn(*a, **k)
+        last["plan"] = p
+        stats["h2d"] += p.upload_bytes + 16 * p.n_tokens  # step metadata, token ids and positions (int64)
+        stats["launches"] += 1
+        return p
+
+    def append_w(layer, *a, **k):
+        stats["launches"] += 1
+        return append_fn(layer, *a, **k)
+
+    def attn_w(layer, q, p, out, *a, **k):
+        stats["launches"] += (p.n_tiles > 0) + (p.n_casc_tasks > 0) + (p.decode_units > 0)
+        if stats["record"] and layer == stats["steps"] % cache.num_layers and p.n_tiles == 0 \
+                and (p.q_lens == 1).all():
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+            stats["rec"].append((ev, p))
+            return attn_fn(layer, q, p, out, *a, events=ev, **k)
+        return attn_fn(layer, q, p, out, *a, **k)
+
+    def run_w(*a, **k):
+        replays = eng.model_runner.graph_replays
+        pre, dec = run_fn(*a, **k)
+        if eng.model_runner.graph_replays != replays:  # a replayed step: its layers' kernels ran from the graph
+            p = last["plan"]
+            stats["launches"] += cache.num_layers * (1 + (p.n_casc_tasks > 0) + (p.decode_units > 0))
+        n = sum(t is not None for t in pre) + len(dec)
+        stats["h2d"] += 8 * n  # sampled rows
+        stats["d2h"] += 8 * n  # sampled tokens
+        return pre, dec
+
+    cache.plan, cache.append_step, cache.attention_step, eng.model_runner.run_step = plan_w, append_w, attn_w, run_w
+    for k in ("steps", "tokens", "h2d", "d2h", "launches"):
+        stats[k] = 0
+    if world > 1:
+        dist.barrier()
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.25)
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    gen = 0
+    while stats["steps"] < args.steps:
+        generation(gen)  # seed 0 first: the end-to-end configuration's prompts
+        gen += 1
+    e1.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = e0.elapsed_time(e1)
+    tokens, steps, launches, h2d, d2h = (stats[k] for k in ("tokens", "steps", "launches", "h2d", "d2h"))
+    replays = eng.model_runner.graph_replays
+    # the attention kernel's duration: events around one layer per decode step of an untimed generation
+    # run eagerly (graph replays run the same kernels but cannot be split by events)
+    eng.model_runner.use_cuda_graphs, stats["record"] = False, True
+    generation(3000 + rank)
+    torch.cuda.synchronize()
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        n = torch.tensor([tokens], device=dev, dtype=torch.float64)
+        dist.all_reduce(n)
+        tokens = int(n.item())
+    cache.check_status()
+    att_ms = [a[1].elapsed_time(a[2]) for a, _ in stats["rec"]]
+    att_bytes = [int(p.kv_lens.sum()) * CFG["hkv"] * CFG["d"] * 4 * 2 + 2 * p.n_tokens * CFG["hq"] * CFG["d"] * 4
+                 for _, p in stats["rec"]]
+    hbm_peak, hbm_kind = _peaks()
+    if rank == 0:
+        cpu = None
+        if not args.no_cpu_baseline:
+            cpu = cpu_engine_rate(12.0)
+            cpu["kind"] = "port"
+        att_avg = sum(att_ms) / max(1, len(att_ms))
+        gbs = (sum(att_bytes) / max(1, len(att_bytes))) / (att_avg * 1e-3) / 1e9 if att_ms else None
+        value = tokens / (ms * 1e-3)
+        line = {
+            "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": steps,
+            "warmup": args.warmup, "ms_per_step": ms / steps, "higher_is_better": True, "scaling": CFG["scaling"],
+            "vs_baseline": None, "dtype": "fp32", "data": "synthetic (random-init GPT-124M, seed 0; prompts of "
+                                                           "U[32, 256] random ids, seeded)",
+            "config": {"workload": CFG["name"], "model": "GPT-124M (12 layers, 12 heads, d 64, context 2048)",
+                       "global_batch": CFG["requests"] * world, "new_tokens": CFG["new_tokens"],
+                       "engine": "Engine(max_concurrent_requests=8, prefill_chunk_size=128, "
+                                 "max_tokens_per_step=2048)", "generations": gen,
+                       "decode_steps_replayed_from_cuda_graph": replays,
+                       "parallelism": f"{world} independent replicas" if world > 1 else "single GPU",
+                       "l2": "not flushed: the per-step working set (weights 0.5 GB) exceeds L2"},
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm_peak, "unit": "GB/s",
+                         "frac": gbs / hbm_peak if gbs else None, "traffic": None, "kernel": "nf_paged_attention",
+                         "peak_source": hbm_kind, "avg_launch_us": att_avg * 1e3,
+                         "note": "decode steps of 8 rows: a few MB per launch, latency-bound; the step is "
+                                 "dominated by the fp32 projections (cuBLAS); timed in an untimed eager "
+                                 "generation after the timed region"},
+            "cpu_baseline": cpu,
+            "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": h2d / steps,
+                    "d2h_bytes_per_step": d2h / steps,
+                    "path": "Engine.add_request/step/get_completed: prompts and tokens on the host; every step "
+                            "uploads its metadata, ids, positions and sampled rows and downloads the sampled "
+                            "tokens (value is this end-to-end rate)"},
+            "gpu_launches": launches, "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     args = _args()
     mixed = CFG.get("kind") == "mixed"
@@ -825,6 +1027,8 @@ def main():
         run_reference(args)
     elif mixed:
         run_mixed(args)
+    elif CFG.get("kind") == "engine":
+        run_engine(args)
     else:
         run_ours(args)
 

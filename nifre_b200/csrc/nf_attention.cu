@@ -456,30 +456,61 @@ __device__ int warp_simt(const AttnParams& p, uint32_t ring, unsigned char* ring
       const unsigned char* kb = ring_ptr + (k % S) * p.stage_bytes;
       const unsigned char* vb = kb + p.tile * HB;
       const int nv = min(p.tile, c.t1 - tb);
-      for (int j = 0; j < nv; ++j) {
-        float kk[DPL], vv[DPL];
+      // KB keys per softmax update: their dot products reduce across the warp side by side, so the
+      // shuffle latency is paid once per KB keys instead of once per key (fewer for wide heads, whose
+      // registers hold more of each row)
+      constexpr int KB = DPL <= 2 ? 4 : (DPL <= 4 ? 2 : 1);
+      for (int j0 = 0; j0 < nv; j0 += KB) {
+        float kk[KB][DPL], vv[KB][DPL];
 #pragma unroll
-        for (int i = 0; i < DPL; ++i) {
-          const int d = lane + 32 * i;
-          const int byte = d * (int)sizeof(T);
-          const int off = tile_off(j, byte >> 4, HB, p.swz) + (byte & 15);
-          kk[i] = d < p.D ? Elem<T>::to_f(*reinterpret_cast<const T*>(kb + off)) : 0.f;
-          vv[i] = d < p.D ? Elem<T>::to_f(*reinterpret_cast<const T*>(vb + off)) : 0.f;
+        for (int u = 0; u < KB; ++u) {
+          const bool live = j0 + u < nv;  // rows past the unit hold whatever the block holds: not read
+#pragma unroll
+          for (int i = 0; i < DPL; ++i) {
+            const int d = lane + 32 * i;
+            const int byte = d * (int)sizeof(T);
+            const int off = tile_off(j0 + u, byte >> 4, HB, p.swz) + (byte & 15);
+            kk[u][i] = live && d < p.D ? Elem<T>::to_f(*reinterpret_cast<const T*>(kb + off)) : 0.f;
+            vv[u][i] = live && d < p.D ? Elem<T>::to_f(*reinterpret_cast<const T*>(vb + off)) : 0.f;
+          }
         }
 #pragma unroll
         for (int n = 0; n < 8; ++n) {
           if (n < p.G) {
-            float sdot = 0.f;
+            float s[KB];
 #pragma unroll
-            for (int i = 0; i < DPL; ++i) sdot = fmaf(qv[n][i], kk[i], sdot);
+            for (int u = 0; u < KB; ++u) {
+              s[u] = 0.f;
 #pragma unroll
-            for (int o_ = 16; o_ > 0; o_ >>= 1) sdot += __shfl_xor_sync(0xffffffffu, sdot, o_);
-            const float mn = fmaxf(m[n], sdot);
-            const float al = ex2(m[n] - mn), pj = ex2(sdot - mn);
-            l[n] = l[n] * al + pj;
+              for (int i = 0; i < DPL; ++i) s[u] = fmaf(qv[n][i], kk[u][i], s[u]);
+            }
+#pragma unroll
+            for (int o_ = 16; o_ > 0; o_ >>= 1) {
+#pragma unroll
+              for (int u = 0; u < KB; ++u) s[u] += __shfl_xor_sync(0xffffffffu, s[u], o_);
+            }
+            float mn = m[n];
+#pragma unroll
+            for (int u = 0; u < KB; ++u) {
+              if (j0 + u >= nv) s[u] = kNegInf;
+              mn = fmaxf(mn, s[u]);  // finite: the first key of the group is live
+            }
+            const float al = ex2(m[n] - mn);
+            float pu[KB], ps = 0.f;
+#pragma unroll
+            for (int u = 0; u < KB; ++u) {
+              pu[u] = ex2(s[u] - mn);
+              ps += pu[u];
+            }
+            l[n] = l[n] * al + ps;
             m[n] = mn;
 #pragma unroll
-            for (int i = 0; i < DPL; ++i) acc[n][i] = fmaf(pj, vv[i], acc[n][i] * al);
+            for (int i = 0; i < DPL; ++i) {
+              float a = acc[n][i] * al;
+#pragma unroll
+              for (int u = 0; u < KB; ++u) a = fmaf(pu[u], vv[u][i], a);
+              acc[n][i] = a;
+            }
           }
         }
       }

@@ -36,14 +36,14 @@ TokenCallback = Callable[[int], None]
 class Engine:
     def __init__(self, model, max_concurrent_requests: int, device, metrics_collector=None,
                  prefill_chunk_size: int = 128, max_tokens_per_step: int = 2048, use_paged_kv_cache: bool = True,
-                 use_prefix_cache: bool = True):
+                 use_prefix_cache: bool = True, use_cuda_graphs: bool = True):
         self.model = model
         self.device = torch.device(device)
         if self.device.type != "cuda":
             raise ValueError("nifre_b200.Engine runs on a CUDA device")
         self.max_concurrent_requests = max_concurrent_requests
         self.scheduler = Scheduler(max_concurrent_requests, max_tokens_per_step)
-        self.model_runner = ModelRunner(model, self.device)
+        self.model_runner = ModelRunner(model, self.device, use_cuda_graphs=use_cuda_graphs)
         self.cache = None
         self.metrics = metrics_collector
         self.prefill_chunk_size = prefill_chunk_size

@@ -119,6 +119,7 @@ class StepPlan:
         self.decode_units = max_units
         self.shared_keys = None  # per sequence: leading keys served by the cascade kernel (numpy)
         self.ws_sizes = None  # (query heads, partial floats, counter ints) of the split-K workspace
+        self.upload_bytes = 0  # bytes of the step's host-to-device metadata copy
         self.n_casc_tasks = self.n_casc_toks = 0
         self.casc_tasks = self.casc_toks = None  # device: (slot, first, count, part, k0, k1, 0, 0), (item, q row)
         self.tiles = None
@@ -275,10 +276,21 @@ class PagedKVCache:
         return self.sm_count * (max_hg // hg)
 
     def split_for(self, total_keys: int, units_per_sm: int = 4) -> int:
-        """Keys per split-K unit: ~units_per_sm units per SM (per decode CTA when the
-        pool holds few KV heads), a multiple of 128."""
-        s = total_keys / max(1, units_per_sm * self.decode_workers)
-        return max(128, int(math.ceil(s / 128.0)) * 128)
+        """Keys per split-K unit.
+
+        Tensor-map kernel (16-bit pools, head_dim 64/128, blocks of a multiple
+        of 16): ~units_per_sm units per SM (per decode CTA when the pool holds
+        few KV heads), a multiple of 128.  Per-warp kernel (float32 and other
+        shapes), where one warp takes one (unit, KV head) and walks its keys
+        serially: about two such items per resident warp (64 per SM), a
+        multiple of 32, so that small batches spread over the GPU.
+        """
+        if self.dtype in (torch.bfloat16, torch.float16) and self.head_dim in (64, 128) \
+                and self.block_size % 16 == 0:
+            s = total_keys / max(1, units_per_sm * self.decode_workers)
+            return max(128, int(math.ceil(s / 128.0)) * 128)
+        s = total_keys * self.n_heads / max(1, 64 * self.sm_count)
+        return max(32, int(math.ceil(s / 32.0)) * 32)
 
     # sequences with at least this many new tokens go to the tensor-core prefill kernel
     PREFILL_MIN_TOKENS = 16
@@ -374,7 +386,7 @@ class PagedKVCache:
         return shared, nparts, tasks, toks
 
     def plan(self, slots, q_lens, q_starts, split: int | None = None, fine_tail: bool = True,
-             q_heads: int | None = None) -> StepPlan:
+             q_heads: int | None = None, fixed_layout: bool = False) -> StepPlan:
         """Allocate blocks for a step and pack its metadata on the GPU.
 
         ``slots[i]`` gets ``q_lens[i]`` new tokens whose rows in the caller's
@@ -389,7 +401,12 @@ class PagedKVCache:
         prefill kernel, in tiles of 128 query rows; the rest by the split-K
         kernel, and decode sequences that share leading blocks (imported
         prefixes) have those keys attended once per group of sequences by
-        the cascade kernel (``_cascade_groups``).
+        the cascade kernel (``_cascade_groups``).  ``fixed_layout`` keeps the
+        device addresses and launch sizes the per-layer kernels see the same
+        from one decode step of a batch to the next (room for one block-table
+        patch per sequence, the unit capacity rounded up to 64), so that a
+        captured CUDA graph of the layers stays valid: ``plan.layout_key``
+        changes whenever they do not.
         """
         slots = np.asarray(slots, dtype=np.int64)
         q_lens = np.asarray(q_lens, dtype=np.int64)
@@ -450,6 +467,8 @@ class PagedKVCache:
         n_units = int(((kv_dec + item_split[item_split > 0] - 1) // item_split[item_split > 0]).sum())
         n_casc = int(nparts.sum())  # partial slots of the cascade parts (q_len 1: one item per sequence)
         max_units = max(1, n_units + n_casc)
+        if fixed_layout:
+            max_units = (max_units + 63) // 64 * 64
         tiles = []
         if routed.any():
             tt = _lib.load().nf_prefill_tile_rows(self.head_dim) // (q_heads // self.n_heads)  # tokens per item
@@ -460,7 +479,10 @@ class PagedKVCache:
 
         n_tiles = len(tiles)
         sched = _prefill_order(tiles, self.n_heads) if n_tiles else np.zeros(0, np.int32)
-        off_tiles = _align4(S * 5 + P * 3)
+        # seqs, per-sequence unit sizes, block-table patches (room for one per sequence with fixed_layout),
+        # prefill tiles and order, shared keys, cascade tasks and query records; the device outputs follow
+        p_room = max(P, S) if fixed_layout else P
+        off_tiles = _align4(S * 5 + p_room * 3)
         off_sched = off_tiles + 4 * n_tiles
         n_ct, n_tok = len(ctasks), len(ctoks)
         off_shared = _align4(off_sched + sched.size)
@@ -468,9 +490,9 @@ class PagedKVCache:
         off_tok = off_ct + 8 * n_ct
         host = np.zeros(off_tok + 2 * n_tok, dtype=np.int32)
         host[: S * 4] = np.stack([slots, q_starts, q_lens, ctx], axis=1).reshape(-1)
+        host[S * 4: S * 5] = seq_split
         if P:
-            host[S * 4: S * 4 + P * 3] = np.asarray(patches, dtype=np.int32).reshape(-1)
-        host[S * 4 + P * 3: S * 5 + P * 3] = seq_split
+            host[S * 5: S * 5 + P * 3] = np.asarray(patches, dtype=np.int32).reshape(-1)
         if n_tiles:
             host[off_tiles:off_sched] = np.asarray(tiles, dtype=np.int32).reshape(-1)
             host[off_sched:off_sched + sched.size] = sched
@@ -488,6 +510,10 @@ class PagedKVCache:
         pos_dev = self._pos_buf.get(T)
 
         plan = StepPlan(slots, q_lens, q_starts, ctx, split, max_units, seq_split)
+        plan.upload_bytes = host.nbytes
+        # what a captured graph of the per-layer kernels depends on besides the cache's own buffers
+        plan.layout_key = (meta.data_ptr(), off_ct, off_tok, off_slot, off_units, off_counts, max_units, S, T,
+                           n_ct, n_tok, n_tiles, q_heads)
         plan.decode_units = n_units
         plan.q_heads = q_heads
         plan.shared_keys = shared
@@ -506,9 +532,9 @@ class PagedKVCache:
         plan.positions = pos_dev[:T]
         lib = _lib.load()
         _lib.check(lib.nf_pack_step(
-            meta.data_ptr(), S, meta.data_ptr() + 4 * S * 4 if P else None, P,
+            meta.data_ptr(), S, meta.data_ptr() + 4 * S * 5 if P else None, P,
             self.bt_dev.data_ptr(), self.batch_size, self.max_blocks_per_seq, self.block_size,
-            self.num_blocks, split, meta.data_ptr() + 4 * (S * 4 + P * 3),
+            self.num_blocks, split, meta.data_ptr() + 4 * S * 4,
             meta.data_ptr() + 4 * off_shared if n_ct else None, plan.slot_mapping.data_ptr(), plan.src_rows.data_ptr(),
             plan.positions.data_ptr(), plan.items.data_ptr(), plan.units.data_ptr(), plan.counts.data_ptr(),
             T, max_units, self.status.data_ptr(), _lib.stream_handle(self.device)), "nf_pack_step")

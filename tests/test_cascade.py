@@ -200,3 +200,68 @@ def test_cascade_bad_task_flagged():
     assert int(cache.status.item()) == _lib.NF_STATUS_BAD_SHARED
     assert int(torch.count_nonzero(ws)) == 0
     cache.status.zero_()
+
+
+@pytest.mark.gpu
+def test_cascade_across_steps_and_mixed_step():
+    """Several decode steps in a row (the grouping memoised, contexts crossing block boundaries, two layers),
+    then one step mixing prefill chunks with the cascaded decodes; every output checked against the oracle."""
+    from nifre_b200 import PagedKVCache
+    hq, hkv, D, L = 32, 8, 64, 2
+    rng = np.random.default_rng(21)
+    g = torch.Generator().manual_seed(21)
+    base = rng.integers(0, 50000, size=300).tolist()
+    prompts = [base + rng.integers(0, 50000, size=int(rng.integers(1, 30))).tolist() for _ in range(10)]
+    extra = [rng.integers(0, 50000, size=int(n)).tolist() for n in (200, 40)]  # later prefills
+    B = len(prompts) + len(extra)
+    cache = PagedKVCache(L, 700, hkv, D, device=DEV, dtype=torch.bfloat16, block_size=16)
+    cache.init_batch(B)
+    for r, toks in enumerate(prompts):
+        m = cache.try_load_prefix(r, toks)
+        n = len(toks) - m
+        plan = cache.plan([r], [n], [0])
+        for layer in range(L):
+            cache.append_step(layer, torch.randn(n, hkv * D, generator=g).to(torch.bfloat16).to(DEV),
+                              torch.randn(n, hkv * D, generator=g).to(torch.bfloat16).to(DEV), plan)
+        cache.register_prefix(r, toks)
+
+    def check(slots, q_lens, q, out, before, layer):
+        kp, vp = cache.k[layer].cpu(), cache.v[layer].cpu()
+        row = 0
+        for s, n in zip(slots, q_lens):
+            ref = attend_paged_fp32(q[row:row + n].view(n, hq, D).cpu(), kp, vp, cache.block_tables[s].physical_blocks(),
+                                    before[s] + n, hq // hkv, causal_base=before[s])
+            torch.testing.assert_close(out[row:row + n].view(n, hq, D).float().cpu(), ref, **TOL)
+            row += n
+
+    dec = list(range(len(prompts)))
+    for step in range(20):  # 20 steps: every sequence crosses at least one block boundary
+        before = {s: cache.length(s) for s in dec}
+        plan = cache.plan(dec, [1] * len(dec), dec, q_heads=hq)
+        assert plan.n_casc_tasks > 0
+        for layer in range(L):
+            q = torch.randn(len(dec), hq * D, generator=g).to(torch.bfloat16).to(DEV)
+            k = torch.randn(len(dec), hkv * D, generator=g).to(torch.bfloat16).to(DEV)
+            v = torch.randn(len(dec), hkv * D, generator=g).to(torch.bfloat16).to(DEV)
+            cache.append_step(layer, k, v, plan)
+            out = torch.zeros_like(q)
+            cache.attention_step(layer, q, plan, out)
+            if step % 6 == 0 or step == 19:
+                check(dec, [1] * len(dec), q, out, before, layer)
+    # mixed: two prefill chunks (new slots) first, then the decodes, in one plan
+    slots = [len(prompts), len(prompts) + 1] + dec
+    q_lens = [len(extra[0]), len(extra[1])] + [1] * len(dec)
+    starts = np.concatenate([[0], np.cumsum(q_lens)[:-1]]).tolist()
+    before = {s: cache.length(s) for s in slots}
+    plan = cache.plan(slots, q_lens, starts, q_heads=hq)
+    assert plan.n_tiles > 0 and plan.n_casc_tasks > 0
+    T = sum(q_lens)
+    for layer in range(L):
+        q = torch.randn(T, hq * D, generator=g).to(torch.bfloat16).to(DEV)
+        k = torch.randn(T, hkv * D, generator=g).to(torch.bfloat16).to(DEV)
+        v = torch.randn(T, hkv * D, generator=g).to(torch.bfloat16).to(DEV)
+        cache.append_step(layer, k, v, plan)
+        out = torch.zeros_like(q)
+        cache.attention_step(layer, q, plan, out)
+        check(slots, q_lens, q, out, before, layer)
+    cache.check_status()

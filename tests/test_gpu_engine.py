@@ -17,15 +17,17 @@ import torch
 pytestmark = pytest.mark.gpu
 
 
+@pytest.mark.parametrize("graphs", [True, False])
 @pytest.mark.parametrize("name", ["tiny", "gpt124m_cfg1"])
-def test_engine_greedy_tokens_match_reference(golden_engine, name):
+def test_engine_greedy_tokens_match_reference(golden_engine, name, graphs):
+    """With CUDA-graph replay of the decode steps (the default) and without it."""
     from nifre_b200 import Engine, GptInferenceModel, GptModel
     case = golden_engine[name]
     torch.backends.cuda.matmul.allow_tf32 = False
     torch.manual_seed(case["seed"])
     model = GptModel(case["cfg"]).eval().to("cuda")
     eng = Engine(GptInferenceModel(model), max_concurrent_requests=case["slots"], device="cuda",
-                 prefill_chunk_size=case["chunk"], max_tokens_per_step=2048)
+                 prefill_chunk_size=case["chunk"], max_tokens_per_step=2048, use_cuda_graphs=graphs)
     new_tokens = len(case["tokens"][0])
     ids = [eng.add_request(p, new_tokens) for p in case["prompts"]]
     steps = 0
@@ -36,6 +38,10 @@ def test_engine_greedy_tokens_match_reference(golden_engine, name):
     assert steps == case["steps"]
     assert eng.cache.num_blocks == case["num_blocks"]
     eng.cache.check_status()
+    if graphs and name == "gpt124m_cfg1":  # 63 decode-only steps of one batch: most replayed from the graph
+        assert eng.model_runner.use_cuda_graphs and eng.model_runner.graph_replays >= 40
+    if not graphs:
+        assert eng.model_runner.graph_replays == 0
 
 
 def test_engine_generate_and_stream_agree():

@@ -1,9 +1,11 @@
 """Pin the CPU oracle to outputs of the reference implementation (CPU only).
 
 The fixtures were produced by tests/golden/make_golden.py, which runs the
-reference's own Attention / PagedKVCache / BlockAllocator / PrefixCache.
+reference's own Attention / PagedKVCache / BlockAllocator / PrefixCache,
+and the greedy tokens of the reference Engine (engine_golden.pt).
 """
 
+import pytest
 import torch
 
 from oracle.attention import attend_paged_fp32, forward_with_cache, full_causal
@@ -158,3 +160,16 @@ def test_full_causal_matches_row_loop():
     store = OracleStore(1, 16, 2, 4, batch_size=2, block_size=4)
     ref = forward_with_cache(store, 0, q, k, v, 2)
     torch.testing.assert_close(out, ref, rtol=1e-6, atol=1e-6)
+
+
+@pytest.mark.parametrize("name,n_prompts", [("tiny", 3), ("gpt124m_cfg1", 1)])
+def test_oracle_engine_port_greedy_tokens(golden_engine, name, n_prompts):
+    """The CPU port of greedy generation (oracle/engine.py) gives the reference Engine's recorded tokens."""
+    from nifre_b200.gpt import GptModel
+    from oracle.engine import greedy_generate
+    case = golden_engine[name]
+    torch.manual_seed(case["seed"])
+    model = GptModel(case["cfg"]).eval()
+    for prompt, want in list(zip(case["prompts"], case["tokens"]))[:n_prompts]:
+        got, _, _ = greedy_generate(model, prompt, len(want))
+        assert got == want
