@@ -56,8 +56,7 @@ constexpr int kCascStages = 4;     // slices per CTA: key ranges of at most 256 
 __host__ __device__ constexpr int casc_pitch(int D) { return D * 2 + 16; }  // padded row: conflict-free ldmatrix
 
 template <typename T, int D_>
-__global__ void __launch_bounds__(kCascThreads, D_ == 64 ? 2 : 1) cascade_kernel(const CascadeParams p) {
-  extern __shared__ __align__(128) unsigned char casc_smem[];
+__device__ __forceinline__ void cascade_body(const CascadeParams& p, unsigned char* casc_smem) {
   constexpr int PITCH = casc_pitch(D_);
   constexpr int SLICE = kCascKeys * PITCH;  // bytes of one slice of K (or V)
   constexpr int KS = D_ / 16;               // k-steps of Q K^T
@@ -257,6 +256,21 @@ __global__ void __launch_bounds__(kCascThreads, D_ == 64 ? 2 : 1) cascade_kernel
   store(tok1, base1, next1, r1, o, 2, m1, l1);
 }
 
+// Launched with programmatic stream serialization behind the step's KV
+// append (or prefill), whose writes it does not read: the shared blocks are
+// full and the append fills only each sequence's own last block.  So the
+// launch starts while that kernel runs, lets the decode launch that follows
+// start as its CTAs free SMs (the decode waits for this grid before reading
+// the pools), and ends only after the kernel before it has ended, so that
+// whatever waits for this grid also sees that kernel's writes.
+template <typename T, int D_>
+__global__ void __launch_bounds__(kCascThreads, D_ == 64 ? 2 : 1) cascade_kernel(const CascadeParams p) {
+  extern __shared__ __align__(128) unsigned char casc_smem[];
+  pdl_launch_dependents();
+  cascade_body<T, D_>(p, casc_smem);
+  if (threadIdx.x == 0) pdl_wait();
+}
+
 }  // namespace nf
 
 extern "C" int nf_cascade_attention(float* ws_partials, int64_t ws_partial_floats, const void* q, int64_t q_row_stride,
@@ -318,10 +332,28 @@ extern "C" int nf_cascade_attention(float* ws_partials, int64_t ws_partial_float
   const dim3 grid((unsigned)n_tasks, (unsigned)num_kv_heads);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   cudaError_t e = cudaSuccess;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kCascThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  // programmatic serialization where the launch accepts it, else plain stream order
 #define NF_CASC_LAUNCH(T, D)                                                                               \
   do {                                                                                                     \
     e = cudaFuncSetAttribute(cascade_kernel<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);     \
-    if (e == cudaSuccess) cascade_kernel<T, D><<<grid, kCascThreads, smem, st>>>(p);                       \
+    if (e == cudaSuccess) {                                                                                \
+      e = cudaLaunchKernelEx(&cfg, cascade_kernel<T, D>, p);                                               \
+      if (e != cudaSuccess) {                                                                              \
+        (void)cudaGetLastError();                                                                          \
+        cfg.numAttrs = 0;                                                                                  \
+        e = cudaLaunchKernelEx(&cfg, cascade_kernel<T, D>, p);                                             \
+      }                                                                                                    \
+    }                                                                                                      \
   } while (0)
   if (dtype == NF_BF16) {
     if (head_dim == 64) NF_CASC_LAUNCH(__nv_bfloat16, 64); else NF_CASC_LAUNCH(__nv_bfloat16, 128);
