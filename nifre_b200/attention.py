@@ -56,12 +56,17 @@ class Attention(nn.Module):
     # ------------------------------------------------------------------ cached path
     def _forward_with_cache(self, q, k, v, cache: PagedKVCache, layer_id, input_lens, cache_batch_indices):
         B, T, _ = q.shape
-        slots = list(range(B)) if cache_batch_indices is None else [int(s) for s in cache_batch_indices]
+        if cache_batch_indices is None:
+            slots = tuple(range(B))
+        elif isinstance(cache_batch_indices, (list, tuple)) and all(type(s) is int for s in cache_batch_indices):
+            slots = tuple(cache_batch_indices)
+        else:
+            slots = tuple(int(s) for s in cache_batch_indices)
         if input_lens is not None and T > 1:
             lens = input_lens.tolist() if torch.is_tensor(input_lens) else [int(x) for x in input_lens]
         else:
             lens = [T] * B
-        key = (tuple(slots), tuple(lens), T)
+        key = (slots, tuple(lens), T)
         plan = cache._plan
         if plan is None or plan.key != key or plan.closed:
             starts = [i * T + (T - n) for i, n in enumerate(lens)]
@@ -75,7 +80,9 @@ class Attention(nn.Module):
         if v2.stride(1) != 1:
             v2 = v2.contiguous()
         qk = q2 if q2.dtype == cache.dtype and q2.stride(1) == 1 else q2.to(cache.dtype).contiguous()
-        out = torch.zeros((B * T, q.shape[-1]), dtype=cache.dtype, device=q.device)
+        # padding rows of a left-padded prefill stay zero (attention.py:79); without padding every row is written
+        padded = T > 1 and any(n != T for n in lens)
+        out = (torch.zeros if padded else torch.empty)((B * T, q.shape[-1]), dtype=cache.dtype, device=q.device)
         cache.append_step(layer_id, k2, v2, plan)
         cache.attention_step(layer_id, qk, plan, out, scale=1.0 / math.sqrt(self.head_dim))
         return out.view(B, T, -1).to(q.dtype)
