@@ -101,7 +101,15 @@ def ptr(t: torch.Tensor | None) -> int | None:
     return None if t is None else t.data_ptr()
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def stream_handle(device: torch.device) -> int:
+    """torch's current CUDA stream on ``device`` (raw handle), read without building a Stream object."""
+    if _raw_stream is not None:
+        idx = device.index if isinstance(device, torch.device) and device.index is not None else \
+            torch.cuda.current_device()
+        return _raw_stream(idx)
     return torch.cuda.current_stream(device).cuda_stream
 
 

@@ -58,10 +58,10 @@ class Attention(nn.Module):
         B, T, _ = q.shape
         if cache_batch_indices is None:
             slots = tuple(range(B))
-        elif isinstance(cache_batch_indices, (list, tuple)) and all(type(s) is int for s in cache_batch_indices):
-            slots = tuple(cache_batch_indices)
+        elif torch.is_tensor(cache_batch_indices):
+            slots = tuple(cache_batch_indices.tolist())
         else:
-            slots = tuple(int(s) for s in cache_batch_indices)
+            slots = tuple(cache_batch_indices)  # compared as given; made ints below when a plan is built
         if input_lens is not None and T > 1:
             lens = input_lens.tolist() if torch.is_tensor(input_lens) else [int(x) for x in input_lens]
         else:
@@ -69,6 +69,7 @@ class Attention(nn.Module):
         key = (slots, tuple(lens), T)
         plan = cache._plan
         if plan is None or plan.key != key or plan.closed:
+            slots = [int(s) for s in slots]
             starts = [i * T + (T - n) for i, n in enumerate(lens)]
             plan = cache.plan(slots, lens, starts, q_heads=self.num_heads)
             plan.key = key
