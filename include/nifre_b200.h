@@ -202,8 +202,12 @@ int nf_paged_attention(void* out, int64_t out_row_stride,
  * nf_pack_step must have been given, through seq_shared, the shared key
  * count and cascade part count of each such sequence; the following
  * nf_paged_attention on the same stream and workspace then merges these
- * parts with the queries' own keys.  16-bit pools, head_dim 64 or 128,
- * block_size a multiple of 16.
+ * parts with the queries' own keys (nf_paged_attention_noalloc cannot: its
+ * workspace is its own, so plans with cascade parts go to nf_paged_attention).
+ * 16-bit pools, head_dim 64 or 128, block_size a multiple of 16.  Launched
+ * with programmatic stream serialization: the launch before it on the stream
+ * must not write the shared blocks, q, items or counts (the step's KV append
+ * writes none of them); the launch ends after that one.
  */
 int nf_cascade_attention(float* ws_partials, int64_t ws_partial_floats,
                          const void* q, int64_t q_row_stride,
