@@ -412,6 +412,80 @@ __device__ int warp_mma(const AttnParams& p, uint32_t ring, unsigned char* fifo,
 // ---------------------------------------------------------------- any dtype: CUDA-core path
 // Any head_dim <= 32*DPL, up to 8 query heads per KV head; lanes split the
 // head dimension.  Same pipeline and queue as the tensor-core path.
+// One staged 16-key tile of the CUDA-core path for heads of up to 64
+// dimensions (lane l holds dimensions l and l + 32).  Each lane's partial
+// dot products for the 16 keys are summed over the warp by a reduce-scatter
+// (one butterfly stage over the lane halves, then four halving stages), so
+// that lane l ends with the full score of key l % 16 after 31 shuffles for
+// the whole tile; the softmax statistics reduce over 16 lanes once per tile
+// and the probabilities are broadcast back for O += P V.
+template <typename T, int DPL>
+__device__ __forceinline__ void simt_tile16(const AttnParams& p, const unsigned char* kb, const unsigned char* vb,
+                                            int nv, const float (&qv)[8][DPL], float (&acc)[8][DPL], float (&m)[8],
+                                            float (&l)[8]) {
+  constexpr int TK = 16;
+  const int lane = threadIdx.x & 31;
+  const int HB = p.head_bytes;
+  float kk[TK][DPL], vv[TK][DPL];
+#pragma unroll
+  for (int j = 0; j < TK; ++j) {
+    const bool live = j < nv;  // rows past the unit hold whatever the block holds: not read
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) {
+      const int d = lane + 32 * i;
+      const int byte = d * (int)sizeof(T);
+      const int off = tile_off(j, byte >> 4, HB, p.swz) + (byte & 15);
+      kk[j][i] = live && d < p.D ? Elem<T>::to_f(*reinterpret_cast<const T*>(kb + off)) : 0.f;
+      vv[j][i] = live && d < p.D ? Elem<T>::to_f(*reinterpret_cast<const T*>(vb + off)) : 0.f;
+    }
+  }
+  const int key = lane & (TK - 1);
+#pragma unroll
+  for (int n = 0; n < 8; ++n) {
+    if (n < p.G) {
+      float s[TK];
+#pragma unroll
+      for (int j = 0; j < TK; ++j) {
+        s[j] = 0.f;
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) s[j] = fmaf(qv[n][i], kk[j][i], s[j]);
+      }
+#pragma unroll
+      for (int j = 0; j < TK; ++j) s[j] += __shfl_xor_sync(0xffffffffu, s[j], 16);
+#pragma unroll
+      for (int o = TK / 2; o >= 1; o >>= 1) {
+        const bool up = lane & o;
+#pragma unroll
+        for (int j = 0; j < o; ++j) {
+          const float send = up ? s[j] : s[j + o];
+          const float keep = up ? s[j + o] : s[j];
+          s[j] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+        }
+      }
+      const float sc = key < nv ? s[0] : kNegInf;  // the score of key `key` (scale folded into q)
+      float mx = sc;
+#pragma unroll
+      for (int o = TK / 2; o >= 1; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      const float mn = fmaxf(m[n], mx);  // finite: key 0 of the tile is live
+      const float al = ex2(m[n] - mn);
+      const float pk = ex2(sc - mn);
+      float ps = pk;
+#pragma unroll
+      for (int o = TK / 2; o >= 1; o >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
+      l[n] = l[n] * al + ps;
+      m[n] = mn;
+#pragma unroll
+      for (int i = 0; i < DPL; ++i) acc[n][i] *= al;
+#pragma unroll
+      for (int j = 0; j < TK; ++j) {
+        const float pj = __shfl_sync(0xffffffffu, pk, j);
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) acc[n][i] = fmaf(pj, vv[j][i], acc[n][i]);
+      }
+    }
+  }
+}
+
 template <typename T, int DPL>
 __device__ int warp_simt(const AttnParams& p, uint32_t ring, unsigned char* ring_ptr, unsigned char* fifo,
                          int total) {
@@ -456,6 +530,12 @@ __device__ int warp_simt(const AttnParams& p, uint32_t ring, unsigned char* ring
       const unsigned char* kb = ring_ptr + (k % S) * p.stage_bytes;
       const unsigned char* vb = kb + p.tile * HB;
       const int nv = min(p.tile, c.t1 - tb);
+      if constexpr (DPL <= 2) {
+        if (p.tile == 16) {  // the tile of this kernel (make_plan)
+          simt_tile16<T, DPL>(p, kb, vb, nv, qv, acc, m, l);
+          continue;
+        }
+      }
       // KB keys per softmax update: their dot products reduce across the warp side by side, so the
       // shuffle latency is paid once per KB keys instead of once per key (fewer for wide heads, whose
       // registers hold more of each row)
