@@ -251,3 +251,24 @@ def test_prefill_order_covers_items_longest_first():
     cost = [(p + n + 127) // 128 + 1 for (_, _, n, p) in tiles]
     c = [cost[i // H] for i in order.tolist()]
     assert all(a >= b for a, b in zip(c, c[1:]))
+
+
+def test_split_for_policy():
+    """Unit sizes: multiples of 128 sized per resident decode CTA for the tensor-map kernel; multiples of 32
+    sized per resident warp for the per-warp kernel (float32 pools), so small batches spread over the GPU."""
+    import torch
+
+    from nifre_b200 import PagedKVCache
+    bf = PagedKVCache(1, 4096, 8, 64, device="cpu", dtype=torch.bfloat16, block_size=16)
+    bf._sm_count = 148
+    assert bf.decode_workers == 148  # one CTA per SM covers the 8 KV heads
+    assert bf.split_for(64 * 2000) == 256 and bf.split_for(100) == 128
+    assert all(bf.split_for(n) % 128 == 0 for n in (1, 10_000, 1_000_000, 10_000_000))
+    shard = PagedKVCache(1, 4096, 1, 64, device="cpu", dtype=torch.bfloat16, block_size=16)
+    shard._sm_count = 148
+    assert shard.decode_workers == 148 * 8  # one KV head per CTA: eight smaller CTAs per SM
+    f32 = PagedKVCache(1, 4096, 12, 64, device="cpu", dtype=torch.float32, block_size=16)
+    f32._sm_count = 148
+    assert f32.split_for(8 * 300) == 32  # 8 sequences x 12 heads: 32-key units
+    big = f32.split_for(64 * 4000)
+    assert big % 32 == 0 and big > 32
