@@ -1,26 +1,37 @@
 #!/usr/bin/env python
-"""Benchmark of the ragged paged-attention decode path on B200.
+"""Benchmark of the ragged paged-attention path on B200.
 
-Workload (default): Llama-3.2-1B-shaped paged decode, bfloat16 -- 16 layers,
-32 query heads, 8 KV heads, head_dim 64, block size 16, 64 sequences with
-context lengths uniform in [512, 4096] (seed 0), Q/K/V ~ N(0, 1), block ids a
-seeded random permutation of the pool.  One step = one decode token for every
-sequence: pack the step on the GPU, then per layer append the new K/V and run
-paged attention.  Contexts grow by one token per step.  Every layer reads a
-different ~300 MB pool, larger than the 126 MB L2, so no flush is needed.
+Headline workload (default): Llama-3.2-1B-shaped paged decode, bfloat16 -- 16
+layers, 32 query heads, 8 KV heads, head_dim 64, block size 16, 64 sequences
+with context lengths uniform in [512, 4096] (seed 0), Q/K/V ~ N(0, 1), block
+ids a seeded random permutation of the pool.  One step = one decode token for
+every sequence: pack the step on the GPU, then per layer append the new K/V
+and run paged attention.  Contexts grow by one token per step.  Every layer
+reads a different ~300 MB pool, larger than the 126 MB L2, so no flush is
+needed.
+
+The same JSON line carries two sub-results measured in the same run, each
+with its own kernel roofline: the Llama-3-8B-shaped long-context decode (256
+sequences, contexts U[4096, 32768], head_dim 128; HBM roofline of the decode
+kernel) and the mixed continuous-batching step (4 prefill chunks of 512
+tokens over cached prefixes plus 96 decodes; tensor roofline of the prefill
+kernel, HBM roofline of the decode kernel).
 
 With --gpus N (torchrun, one process per GPU) each rank holds 8/N KV heads
-(and the matching 32/N query heads) of a batch of 64*N sequences -- fixed
-work per GPU -- and the attention outputs are all-gathered over NCCL after
-every layer.
+(and the matching 32/N query heads); the 1B decode keeps the work per GPU
+fixed (64*N sequences), the 8B decode and the mixed step shard one batch, and
+the attention outputs are all-gathered over NCCL after every layer.
 
-Prints one JSON line (rank 0).  --impl reference times the CPU oracle (the
-reference's per-row algorithm restated) on the host cores instead.
+Prints one JSON line (rank 0).  --impl reference times the reference's own
+CPU attention path (installed unmodified in baseline/_ref, grouped-query heads
+stored expanded to the query head count) on the host cores instead, or the
+CPU port of it when that install is absent.
 """
 
 from __future__ import annotations
 
 import argparse
+import contextlib
 import json
 import math
 import os
@@ -47,7 +58,7 @@ ATTN_TRAFFIC_RATIO = 1.0316
 # resident: layers held in HBM and run per step (a full 8B step's KV, ~618 GB,
 # exceeds one GPU); tok/s counts every step as `layers` layers at the measured
 # per-layer time.  scaling: weak = batch grows with N (64*N sequences), strong
-# = the same 256 sequences with the KV heads sharded over N GPUs.
+# = the same batch with the KV heads sharded over N GPUs.
 WORKLOADS = {
     "llama3.2-1b-decode": dict(layers=16, resident=16, hq=32, hkv=8, d=64, bs=16, seqs=64, ctx_lo=512,
                                ctx_hi=4096, seed=0, scaling="weak", steps=300, cpu_sample=8,
@@ -81,6 +92,9 @@ WORKLOADS = {
 CFG = dict(name="llama3.2-1b-decode", **WORKLOADS["llama3.2-1b-decode"])
 METRIC = CFG["metric"]
 
+# sub-results of the default run: (workload, resident layers, timed steps)
+SUB_RESULTS = (("llama3-8b-long", 1, 12), ("llama3.2-1b-mixed", 16, 16))
+
 
 def _args():
     ap = argparse.ArgumentParser()
@@ -90,14 +104,12 @@ def _args():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--e2e-steps", type=int, default=50)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-sub", action="store_true", help="skip the 8B-decode and mixed-step sub-results")
     ap.add_argument("--layers", type=int, default=None, help="fewer resident layers (profiling a small case)")
     ap.add_argument("--seqs", type=int, default=None, help="fewer decode sequences (profiling a small case)")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="llama3.2-1b-decode")
     a = ap.parse_args()
-    global METRIC
-    CFG.clear()
-    CFG.update(name=a.workload, **WORKLOADS[a.workload])
-    METRIC = CFG["metric"]
+    _use_workload(a.workload)
     if a.steps is None:
         a.steps = CFG["steps"]
     if a.layers:  # profiling a small case: fewer resident layers (and, for the 1B shape, a shallower model)
@@ -107,6 +119,28 @@ def _args():
     if a.seqs:
         CFG["seqs"] = a.seqs
     return a
+
+
+def _use_workload(name: str, **over) -> None:
+    global METRIC
+    CFG.clear()
+    CFG.update(name=name, **WORKLOADS[name])
+    CFG.update(over)
+    METRIC = CFG["metric"]
+
+
+@contextlib.contextmanager
+def _workload(name: str, **over):
+    """Switch the workload for a sub-result; the headline's is restored after."""
+    saved = dict(CFG)
+    _use_workload(name, **over)
+    try:
+        yield
+    finally:
+        global METRIC
+        CFG.clear()
+        CFG.update(saved)
+        METRIC = CFG["metric"]
 
 
 def _ctx_lens(n, seed):
@@ -125,6 +159,27 @@ def _prefix_shape(n):
     suffix = [rng.integers(0, CFG["vocab"], size=int(rng.integers(CFG["suffix_lo"], CFG["suffix_hi"] + 1))).tolist()
               for _ in range(n)]
     return prefixes, group, suffix
+
+
+def _mixed_shape():
+    rng = np.random.default_rng(CFG["seed"])
+    prefix = rng.integers(0, CFG["prefix_hi"] + 1, size=CFG["chunks"]).tolist()
+    dctx = rng.integers(CFG["dctx_lo"], CFG["dctx_hi"] + 1, size=CFG["decodes"]).tolist()
+    return prefix, dctx
+
+
+def _mixed_flops(prefix, hq, d, chunk):
+    """Algorithmic prefill FLOPs of one layer: unmasked causal pairs only, 4*Hq*D per pair."""
+    return 4.0 * hq * d * sum(chunk * p + chunk * (chunk + 1) / 2 for p in prefix)
+
+
+def _stratified(values, n):
+    """Indices of n of the values at evenly spaced quantiles, so that the sample's mean matches the population's."""
+    values = np.asarray(values)
+    n = min(n, len(values))
+    order = np.argsort(values, kind="stable")
+    at = ((np.arange(n) + 0.5) * len(values) / n).astype(np.int64)
+    return sorted(order[at].tolist())
 
 
 # ---------------------------------------------------------------------------- clocks
@@ -187,51 +242,96 @@ def _peaks():
     return 6650.0, "fallback"
 
 
-def _tensor_peak():
-    """Dense bf16 peak for a kernel timed inside a long step: the sustained figure."""
+def _tensor_peaks():
+    """Dense bf16 peaks: (burst, sustained, source).  The burst figure is the one for a kernel timed
+    alone or inside a short timed region (milliseconds); the sustained one holds under the power cap in
+    regions of seconds."""
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
         d = json.loads(p.read_text())
-        if "bf16_tflops_sustained" in d:
-            return float(d["bf16_tflops_sustained"]), "measured (sustained)"
-        return float(d["bf16_tflops"]), "measured (burst)"
-    return 1400.0, "fallback (sustained)"
+        burst = float(d["bf16_tflops"])
+        return burst, float(d.get("bf16_tflops_sustained", burst)), "measured"
+    return 1590.0, 1400.0, "fallback"
 
 
-# ---------------------------------------------------------------------------- CPU baseline (oracle)
-class CpuOracleDecode:
-    """The reference algorithm on the host: per-row get -> append -> cat -> matmul -> softmax -> matmul.
+# ---------------------------------------------------------------------------- CPU baselines
+# Two CPU forms of the path, timed on the host cores of the GPU box in the same run:
+#  * "reference": the reference's own Attention._forward_with_cache over its own PagedKVCache
+#    (src/inference/attention.py:77-152, paged_kv_cache.py:107-142), installed unmodified into
+#    baseline/_ref by baseline/install_ref.sh.  The reference has one head count for queries and keys,
+#    so the grouped-query shapes run with the KV heads stored repeated to the query head count
+#    ("MHA-expanded"): the same outputs, 4x the KV bytes of the 8-KV-head model.
+#  * "port": the oracle's restatement of that algorithm (oracle/attention.py, oracle/paged.py), which
+#    keeps the 8 KV heads and expands them only for the matmuls.
+# Each times one layer of a bounded sample of the workload's sequences, chosen at evenly spaced
+# quantiles of the context lengths so that the sample's mean context matches the batch's.
 
-    One call of ``layer()`` is one layer of decode for the first ``n_sample``
-    sequences of the workload (grouped-query heads restated by repeating the
-    KV heads, as the reference has a single head count).  ``pos`` is held so
-    every call sees the same contexts.
+def _reference_modules():
+    """(Attention, PagedKVCache) of the reference installed in baseline/_ref, or None."""
+    ref = ROOT / "baseline" / "_ref"
+    if not (ref / "inference" / "attention.py").exists():
+        return None
+    if str(ref) not in sys.path:
+        sys.path.insert(0, str(ref))
+    try:
+        from inference.attention import Attention
+        from inference.paged_kv_cache import PagedKVCache
+    except Exception:  # noqa: BLE001 -- an unusable install is reported as absent
+        return None
+    return Attention, PagedKVCache
+
+
+class _CpuDecodeBase:
+    """A bounded sample of the decode workload's sequences on the host: subclasses fill the store."""
+
+    kind = ""
+
+    def __init__(self, n_sample: int | None = None, threads: int | None = None):
+        if threads:
+            torch.set_num_threads(threads)
+        n_sample = n_sample or CFG["cpu_sample"]
+        population = _ctx_lens(CFG["seqs"], CFG["seed"])
+        self.pop_mean = float(np.mean(population))
+        self.ctx = [population[i] for i in _stratified(population, n_sample)]
+        self.n = len(self.ctx)
+        self.g = torch.Generator().manual_seed(1)
+
+    def describe(self, calls: int, seconds: float) -> str:
+        return (f"{self.n} of {CFG['seqs']} sequences at evenly spaced context quantiles (mean ctx "
+                f"{sum(self.ctx) / self.n:.0f}, batch mean {self.pop_mean:.0f}), one layer x {calls} calls in "
+                f"{seconds:.1f} s, scaled to {CFG['layers']} layers")
+
+    def rate(self, t_layer: float) -> float:
+        return self.n / (CFG["layers"] * t_layer)
+
+
+class CpuOracleDecode(_CpuDecodeBase):
+    """The oracle port: per-row get -> append -> cat -> matmul -> softmax -> matmul, KV heads kept at Hkv.
+
+    ``pos`` is held (layer 0 of a 2-layer store), so every call sees the same contexts.
     """
+
+    kind = "port"
 
     def __init__(self, n_sample: int | None = None, threads: int | None = None):
         from oracle.paged import OracleStore
 
-        if threads:
-            torch.set_num_threads(threads)
-        n_sample = n_sample or CFG["cpu_sample"]
-        self.n = n_sample
-        self.ctx = _ctx_lens(CFG["seqs"], CFG["seed"])[:n_sample]
+        super().__init__(n_sample, threads)
         H, D, bs = CFG["hkv"], CFG["d"], CFG["bs"]
-        st = OracleStore(2, max(self.ctx) + 64, H, D, batch_size=n_sample, dtype=torch.bfloat16,
-                         block_size=bs, prefix=False)
-        g = torch.Generator().manual_seed(1)
+        st = OracleStore(2, max(self.ctx) + 64, H, D, batch_size=self.n, dtype=torch.bfloat16, block_size=bs,
+                         prefix=False)
         for s, c in enumerate(self.ctx):  # fill contexts block-wise (not timed)
             st.tables[s].ensure(c)
-            kk = torch.randn(c, H, D, generator=g).to(torch.bfloat16)
-            vv = torch.randn(c, H, D, generator=g).to(torch.bfloat16)
+            kk = torch.randn(c, H, D, generator=self.g).to(torch.bfloat16)
+            vv = torch.randn(c, H, D, generator=self.g).to(torch.bfloat16)
             for i, b in enumerate(st.tables[s].blocks):
                 n = min(bs, c - i * bs)
                 st.k[0][b, :n] = kk[i * bs: i * bs + n]
                 st.v[0][b, :n] = vv[i * bs: i * bs + n]
             st.pos[s] = c
         self.store = st
-        self.q = torch.randn(n_sample, 1, CFG["hq"] * D, generator=g).to(torch.bfloat16)
-        self.k = torch.randn(n_sample, 1, H * D, generator=g).to(torch.bfloat16)
+        self.q = torch.randn(self.n, 1, CFG["hq"] * D, generator=self.g).to(torch.bfloat16)
+        self.k = torch.randn(self.n, 1, H * D, generator=self.g).to(torch.bfloat16)
 
     def layer(self) -> float:
         from oracle.attention import forward_with_cache
@@ -240,26 +340,209 @@ class CpuOracleDecode:
         forward_with_cache(self.store, 0, self.q, self.k, self.k, CFG["hq"])  # layer 0 of 2: pos held
         return time.perf_counter() - t0
 
-    def describe(self, calls: int, seconds: float) -> str:
-        return (f"{self.n} of {CFG['seqs']} sequences (mean ctx {sum(self.ctx) / self.n:.0f}), one layer x "
-                f"{calls} calls in {seconds:.1f} s, scaled to {CFG['layers']} layers")
 
-    def rate(self, t_layer: float) -> float:
-        return self.n / (CFG["layers"] * t_layer)
+class CpuReferenceDecode(_CpuDecodeBase):
+    """The reference's own code: ``Attention(Hq, D)`` with its ``PagedKVCache`` (KV heads stored repeated).
+
+    The cache has two layers and the timed calls use layer 0, so ``pos`` is held
+    (the reference advances it on the last layer only) and every call sees the
+    same contexts.  Runs under ``torch.no_grad`` as the reference engine does.
+    """
+
+    kind = "reference"
+
+    def __init__(self, n_sample: int | None = None, threads: int | None = None):
+        super().__init__(n_sample, threads)
+        mods = _reference_modules()
+        if mods is None:
+            raise RuntimeError("the reference is not installed in baseline/_ref")
+        Attention, RefCache = mods
+        Hq, Hkv, D, bs = CFG["hq"], CFG["hkv"], CFG["d"], CFG["bs"]
+        G = Hq // Hkv
+        cache = RefCache(2, max(self.ctx) + 64, Hq, D, device="cpu", dtype=torch.bfloat16, block_size=bs,
+                         enable_prefix_cache=False)
+        cache.init_batch(self.n)
+        with torch.no_grad():
+            for s, c in enumerate(self.ctx):  # through the reference's own append, both layers (not timed)
+                kk = torch.randn(c, Hkv, D, generator=self.g).to(torch.bfloat16).repeat_interleave(G, dim=1)
+                vv = torch.randn(c, Hkv, D, generator=self.g).to(torch.bfloat16).repeat_interleave(G, dim=1)
+                cache.append(s, 0, kk, vv)
+                cache.append(s, 1, kk, vv)
+        self.cache = cache
+        self.attn = Attention(Hq, D)
+        self.q = torch.randn(self.n, 1, Hq * D, generator=self.g).to(torch.bfloat16)
+        self.k = (torch.randn(self.n, 1, Hkv, D, generator=self.g).to(torch.bfloat16)
+                  .repeat_interleave(G, dim=2).reshape(self.n, 1, Hq * D))
+
+    def layer(self) -> float:
+        with torch.no_grad():
+            t0 = time.perf_counter()
+            self.attn(self.q, self.k, self.k, kv_cache=self.cache, layer_id=0)
+            return time.perf_counter() - t0
 
 
-def cpu_decode_rate(seconds: float, threads: int | None = None):
-    cpu = CpuOracleDecode(threads=threads)
+def _time_cpu(make, seconds: float, warmup: int = 1):
+    cpu = make()
+    for _ in range(warmup):
+        cpu.layer()
     times = []
-    while sum(times) < seconds:
+    while sum(times) < seconds or len(times) < 2:
         times.append(cpu.layer())
     t = sum(times) / len(times)
-    return {"value": cpu.rate(t), "unit": "tok/s", "cores": torch.get_num_threads(),
-            "sample": cpu.describe(len(times), sum(times))}
+    return {"value": cpu.rate(t), "unit": "tok/s", "cores": torch.get_num_threads(), "host_cpus": os.cpu_count(),
+            "kind": cpu.kind, "sample": cpu.describe(len(times), sum(times))}
 
 
-# ---------------------------------------------------------------------------- our arm
-def run_ours(args):
+def cpu_baseline(seconds: float, port_cls, ref_cls, threads: int | None = None):
+    """The CPU baseline of a workload: the reference's own code when installed (its value is the line's),
+    the oracle port beside it."""
+    threads = threads or os.cpu_count() or 1
+    port = _time_cpu(lambda: port_cls(threads=threads), seconds)
+    ref = None
+    if ref_cls is not None and _reference_modules() is not None:
+        ref = _time_cpu(lambda: ref_cls(threads=threads), seconds)
+        ref["layout"] = f"MHA-expanded: KV heads stored repeated to {CFG['hq']} (the reference has one head count)"
+    if ref is None:
+        return dict(port, note="reference code not installed in baseline/_ref: the port is the baseline")
+    return dict(ref, port=port)
+
+
+# mixed step on the CPU: one prefill chunk and a sample of the decodes per call, all four chunks in turn
+class _CpuMixedBase:
+    kind = ""
+
+    def __init__(self, threads: int | None = None):
+        if threads:
+            torch.set_num_threads(threads)
+        prefix, dctx = _mixed_shape()
+        self.prefix, self.dctx = prefix, dctx
+        self.nd = min(CFG["cpu_sample"], len(dctx))
+        self.dsel = _stratified(dctx, self.nd)
+        self.ctx = prefix + [dctx[i] for i in self.dsel]  # slots 0..3 chunks, then the sampled decodes
+        self.g = torch.Generator().manual_seed(1)
+        self.calls = 0
+
+    def rate(self, t_chunk: float, t_dec: float) -> float:
+        t_layer = len(self.prefix) * t_chunk + len(self.dctx) / self.nd * t_dec
+        tokens = len(self.prefix) * CFG["chunk"] + len(self.dctx)
+        return tokens / (CFG["layers"] * t_layer)
+
+    def describe(self, calls: int, seconds: float) -> str:
+        return (f"each call one 512-token chunk (the 4 chunks, prefixes {self.prefix}, in turn) and {self.nd} of "
+                f"{len(self.dctx)} decodes at evenly spaced context quantiles, one layer x {calls} calls in "
+                f"{seconds:.1f} s, scaled to 4 chunks + {len(self.dctx)} decodes x {CFG['layers']} layers")
+
+
+class CpuOracleMixed(_CpuMixedBase):
+    kind = "port"
+
+    def __init__(self, threads: int | None = None):
+        from oracle.paged import OracleStore
+
+        super().__init__(threads)
+        H, D, bs, C = CFG["hkv"], CFG["d"], CFG["bs"], CFG["chunk"]
+        st = OracleStore(2, max(self.ctx) + C + 64, H, D, batch_size=len(self.ctx), dtype=torch.bfloat16,
+                         block_size=bs, prefix=False)
+        for sl, c in enumerate(self.ctx):
+            if c == 0:
+                continue
+            st.tables[sl].ensure(c)
+            kk = torch.randn(c, H, D, generator=self.g).to(torch.bfloat16)
+            vv = torch.randn(c, H, D, generator=self.g).to(torch.bfloat16)
+            for i, b in enumerate(st.tables[sl].blocks):
+                n = min(bs, c - i * bs)
+                st.k[0][b, :n] = kk[i * bs: i * bs + n]
+                st.v[0][b, :n] = vv[i * bs: i * bs + n]
+            st.pos[sl] = c
+        self.store = st
+        hq = CFG["hq"]
+        self.qc = torch.randn(1, C, hq * D, generator=self.g).to(torch.bfloat16)
+        self.kc = torch.randn(1, C, H * D, generator=self.g).to(torch.bfloat16)
+        self.qd = torch.randn(self.nd, 1, hq * D, generator=self.g).to(torch.bfloat16)
+        self.kd = torch.randn(self.nd, 1, H * D, generator=self.g).to(torch.bfloat16)
+
+    def layer(self) -> tuple[float, float]:
+        from oracle.attention import forward_with_cache
+
+        c = self.calls % len(self.prefix)
+        self.calls += 1
+        P = len(self.prefix)
+        t0 = time.perf_counter()  # layer 0 of 2: pos held, every call continues the same prefix
+        forward_with_cache(self.store, 0, self.qc, self.kc, self.kc, CFG["hq"], slots=[c])
+        t1 = time.perf_counter()
+        forward_with_cache(self.store, 0, self.qd, self.kd, self.kd, CFG["hq"], slots=list(range(P, P + self.nd)))
+        return t1 - t0, time.perf_counter() - t1
+
+
+class CpuReferenceMixed(_CpuMixedBase):
+    kind = "reference"
+
+    def __init__(self, threads: int | None = None):
+        super().__init__(threads)
+        mods = _reference_modules()
+        if mods is None:
+            raise RuntimeError("the reference is not installed in baseline/_ref")
+        Attention, RefCache = mods
+        Hq, Hkv, D, bs, C = CFG["hq"], CFG["hkv"], CFG["d"], CFG["bs"], CFG["chunk"]
+        G = Hq // Hkv
+        cache = RefCache(2, max(self.ctx) + C + 64, Hq, D, device="cpu", dtype=torch.bfloat16, block_size=bs,
+                         enable_prefix_cache=False)
+        cache.init_batch(len(self.ctx))
+
+        def rnd(n):
+            return torch.randn(n, Hkv, D, generator=self.g).to(torch.bfloat16).repeat_interleave(G, dim=1)
+
+        with torch.no_grad():
+            for s, c in enumerate(self.ctx):
+                if c:
+                    kk, vv = rnd(c), rnd(c)
+                    cache.append(s, 0, kk, vv)
+                    cache.append(s, 1, kk, vv)
+        self.cache = cache
+        self.attn = Attention(Hq, D)
+        self.qc = torch.randn(1, C, Hq * D, generator=self.g).to(torch.bfloat16)
+        self.kc = rnd(C).reshape(1, C, Hq * D)
+        self.qd = torch.randn(self.nd, 1, Hq * D, generator=self.g).to(torch.bfloat16)
+        self.kd = rnd(self.nd).reshape(self.nd, 1, Hq * D)
+
+    def layer(self) -> tuple[float, float]:
+        c = self.calls % len(self.prefix)
+        self.calls += 1
+        P = len(self.prefix)
+        with torch.no_grad():  # layer 0 of 2: pos held, every call continues the same prefix
+            t0 = time.perf_counter()
+            self.attn(self.qc, self.kc, self.kc, kv_cache=self.cache, layer_id=0, cache_batch_indices=[c])
+            t1 = time.perf_counter()
+            self.attn(self.qd, self.kd, self.kd, kv_cache=self.cache, layer_id=0,
+                      cache_batch_indices=list(range(P, P + self.nd)))
+            return t1 - t0, time.perf_counter() - t1
+
+
+def _time_cpu_mixed(make, seconds: float):
+    cpu = make()
+    cpu.layer()
+    tc, td = [], []
+    while sum(tc) + sum(td) < seconds or len(tc) < len(cpu.prefix):
+        a, b = cpu.layer()
+        tc.append(a)
+        td.append(b)
+    return {"value": cpu.rate(sum(tc) / len(tc), sum(td) / len(td)), "unit": "tok/s",
+            "cores": torch.get_num_threads(), "host_cpus": os.cpu_count(), "kind": cpu.kind,
+            "sample": cpu.describe(len(tc), sum(tc) + sum(td))}
+
+
+def cpu_mixed_baseline(seconds: float, threads: int | None = None):
+    threads = threads or os.cpu_count() or 1
+    port = _time_cpu_mixed(lambda: CpuOracleMixed(threads=threads), seconds)
+    if _reference_modules() is None:
+        return dict(port, note="reference code not installed in baseline/_ref: the port is the baseline")
+    ref = _time_cpu_mixed(lambda: CpuReferenceMixed(threads=threads), seconds)
+    ref["layout"] = f"MHA-expanded: KV heads stored repeated to {CFG['hq']} (the reference has one head count)"
+    return dict(ref, port=port)
+
+
+# ---------------------------------------------------------------------------- GPU helpers
+def _dist_setup():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -271,22 +554,41 @@ def run_ours(args):
 
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
-    if CFG["hkv"] % world:
-        raise SystemExit(f"--gpus {world} must divide {CFG['hkv']} KV heads")
-    from nifre_b200.sharding import HeadShard
-    shard = HeadShard(world, rank, CFG["hq"], CFG["hkv"], CFG["d"])
-    hkv, hq = shard.kv_heads, shard.q_heads
-    B = CFG["seqs"] * world if CFG["scaling"] == "weak" else CFG["seqs"]
-    ctx = _ctx_lens(B, CFG["seed"])
-    steps_total = args.warmup + args.steps + args.e2e_steps + 2
-    dt = torch.bfloat16
-    if CFG.get("kind") == "prefix":
-        return _run_decode_timed(args, _build_prefix_cache(B, ctx, steps_total, hkv, dev, dt), B, ctx, world, rank,
-                                 local, dev, dist, shard, hkv, hq)
-    return _run_decode_timed(args, _build_decode_cache(B, ctx, steps_total, hkv, dev, dt, rank), B, ctx, world, rank,
-                             local, dev, dist, shard, hkv, hq)
+    return world, rank, local, dev, dist
 
 
+def _max_over_ranks(x: float, dev, dist) -> float:
+    if dist is None:
+        return x
+    t = torch.tensor([x], device=dev, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _check_rows(cache, layer, q, out, checks, group):
+    """In-run parity: float32 attention of a few of the step's queries, computed with torch on the GPU
+    from the pool (the reference math: softmax(q k^T / sqrt(D)) v over keys [0, pos]), against the
+    kernel's output rows.  ``checks``: (slot, q_row, kv_len).  Returns the worst |error| and whether every
+    row is within the bf16 tolerance (rtol = atol = 2e-2)."""
+    D, bs = cache.head_dim, cache.block_size
+    worst, ok = 0.0, True
+    for slot, row, kv_len in checks:
+        nb = (kv_len + bs - 1) // bs
+        idx = torch.tensor(cache.block_tables[slot].physical_blocks()[:nb], device=q.device)
+        K = cache.k[layer].index_select(0, idx).reshape(nb * bs, -1, D)[:kv_len].float()
+        V = cache.v[layer].index_select(0, idx).reshape(nb * bs, -1, D)[:kv_len].float()
+        K = K.repeat_interleave(group, dim=1).transpose(0, 1)
+        V = V.repeat_interleave(group, dim=1).transpose(0, 1)
+        qs = q[row].view(-1, 1, D).float()
+        ref = (torch.softmax((qs @ K.transpose(1, 2)) / math.sqrt(D), dim=-1) @ V).reshape(-1)
+        got = out[row].float()
+        err = (got - ref).abs()
+        worst = max(worst, float(err.max()))
+        ok = ok and bool((err <= 2e-2 + 2e-2 * ref.abs()).all())
+    return worst, ok
+
+
+# ---------------------------------------------------------------------------- decode workloads
 def _build_decode_cache(B, ctx, steps_total, hkv, dev, dt, rank):
     """Pool of the decode workloads: contexts filled with N(0,1) K/V over a randomly permuted free list."""
     from nifre_b200 import PagedKVCache
@@ -354,7 +656,33 @@ def _build_prefix_cache(B, ctx, steps_total, hkv, dev, dt):
     return cache
 
 
-def _run_decode_timed(args, cache, B, ctx, world, rank, local, dev, dist, shard, hkv, hq):
+def measure_decode(steps, warmup, e2e_steps, world, rank, local, dev, dist):
+    """One decode workload (CFG): timed steps, the attention kernel's roofline, the end-to-end rate and an
+    in-run parity check.  Returns the JSON line's fields (the same on every rank; rank 0 prints)."""
+    from nifre_b200.sharding import HeadShard
+
+    if CFG["hkv"] % world:
+        raise SystemExit(f"--gpus {world} must divide {CFG['hkv']} KV heads")
+    shard = HeadShard(world, rank, CFG["hq"], CFG["hkv"], CFG["d"])
+    hkv, hq = shard.kv_heads, shard.q_heads
+    B = CFG["seqs"] * world if CFG["scaling"] == "weak" else CFG["seqs"]
+    ctx = _ctx_lens(B, CFG["seed"])
+    steps_total = warmup + steps + e2e_steps + 3
+    dt = torch.bfloat16
+    if CFG.get("kind") == "prefix":
+        cache = _build_prefix_cache(B, ctx, steps_total, hkv, dev, dt)
+    else:
+        cache = _build_decode_cache(B, ctx, steps_total, hkv, dev, dt, rank)
+    try:
+        return _run_decode_timed(steps, warmup, e2e_steps, cache, B, ctx, world, rank, local, dev, dist, shard,
+                                 hkv, hq)
+    finally:
+        del cache
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+
+
+def _run_decode_timed(steps, warmup, e2e_steps, cache, B, ctx, world, rank, local, dev, dist, shard, hkv, hq):
     from nifre_b200 import Attention
 
     L, L_model, D, bs = CFG["resident"], CFG["layers"], CFG["d"], CFG["bs"]
@@ -385,8 +713,9 @@ def _run_decode_timed(args, cache, B, ctx, world, rank, local, dev, dist, shard,
             if world > 1:
                 # heads of rank r are query heads [r*hq, (r+1)*hq): (N*B, hq*D) -> (B, N*hq*D)
                 shard.gather(out_loc[layer], buffer=gathered)
+        return p
 
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         step()
     torch.cuda.synchronize()
     cache.check_status()
@@ -402,16 +731,12 @@ def _run_decode_timed(args, cache, B, ctx, world, rank, local, dev, dist, shard,
     # the attention kernel is timed by events around one layer per step, a
     # different layer each step: events between every pair of kernels would
     # add a drain per event to the step
-    for s in range(args.steps):
+    for s in range(steps):
         step(rec_layer=s % L)
     e_end.record(stream)
     torch.cuda.synchronize()
     clk = clocks.stop()
-    ms = e_start.elapsed_time(e_end)
-    if world > 1:
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+    ms = _max_over_ranks(e_start.elapsed_time(e_end), dev, dist)
     cache.check_status()
     # attention kernel: algorithmic bytes per launch / event duration
     att_ms = [a.elapsed_time(b) for a, b, _ in att_events]
@@ -424,13 +749,23 @@ def _run_decode_timed(args, cache, B, ctx, world, rank, local, dev, dist, shard,
         logical_bytes.append(kv * hkv * D * 2 * 2 + 2 * B * hq * D * 2 + 4 * nblk + 16 * B)
     from nifre_b200 import _lib
     att_path = _lib.load().nf_last_attention_path()
-    att_avg_ms = sum(att_ms) / len(att_ms)
+    att_avg_ms = _max_over_ranks(sum(att_ms) / len(att_ms), dev, dist)
     achieved = (sum(att_bytes) / len(att_bytes)) / (att_avg_ms * 1e-3) / 1e9
     peak, peak_kind = _peaks()
 
+    # in-run parity: one more step, then a few of its queries against float32 attention over the pool
+    p = step()
+    torch.cuda.synchronize()
+    lay = L - 1
+    pick = _stratified(p.kv_lens, 6)
+    worst, ok = _check_rows(cache, lay, q_all[lay], out_loc[lay],
+                            [(i, i, int(p.kv_lens[i])) for i in pick], hq // hkv)
+    worst = _max_over_ranks(worst, dev, dist)
+    ok = _max_over_ranks(0.0 if ok else 1.0, dev, dist) == 0.0
+
     # e2e through the public drop-in API with host buffers
     e2e = None
-    if args.e2e_steps > 0:
+    if e2e_steps > 1:
         attn = Attention(hq, D)
         hq_host = torch.empty(L, B, 1, hq * D, dtype=dt).pin_memory()
         hk_host = torch.empty(L, B, 1, hkv * D, dtype=dt).pin_memory()
@@ -462,212 +797,78 @@ def _run_decode_timed(args, cache, B, ctx, world, rank, local, dev, dist, shard,
         a = torch.cuda.Event(enable_timing=True)
         b = torch.cuda.Event(enable_timing=True)
         a.record(stream)
-        for _ in range(args.e2e_steps - 1):
+        for _ in range(e2e_steps - 1):
             e2e_step()
         b.record(stream)
         torch.cuda.synchronize()
-        ems = a.elapsed_time(b)
-        if world > 1:
-            t = torch.tensor([ems], device=dev)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            ems = float(t.item())
+        ems = _max_over_ranks(a.elapsed_time(b), dev, dist)
         cache.check_status()
-        n_e2e = args.e2e_steps - 1
+        n_e2e = e2e_steps - 1
         e2e = {"value": B * n_e2e / (ems * 1e-3) * L / L_model, "unit": "tok/s",
                "h2d_bytes_per_step": L * B * (hq + 2 * hkv) * D * 2,
                "d2h_bytes_per_step": L * B * hq * D * 2,
-               "ms_per_step": ems / n_e2e,
+               "ms_per_step": ems / n_e2e * L_model / L,
                "path": "nifre_b200.Attention.forward per layer; the step's q/k/v copied up from pinned host memory "
                        "in one copy per tensor, its outputs copied down in one"}
 
-    if rank == 0:
-        cpu = None
-        if not args.no_cpu_baseline:
-            cpu = cpu_decode_rate(12.0)
-            cpu["kind"] = "port"
-        line = {
-            "metric": METRIC, "value": B * args.steps / (ms * 1e-3) * L / L_model, "unit": "tok/s",
-            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": ms / args.steps * L_model / L,
-            "higher_is_better": True, "scaling": CFG["scaling"], "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic (seeded N(0,1) Q/K/V, random block permutation)",
-            "config": {"workload": CFG["name"], "layers": L_model, "layers_timed": L, "q_heads": CFG["hq"],
-                       "kv_heads": CFG["hkv"], "head_dim": D, "block_size": bs,
-                       "seqs_per_gpu_x_heads": f"{B} seqs x {hkv} kv heads",
-                       "global_batch": B,
-                       "ctx": (f"U[{CFG['ctx_lo']},{CFG['ctx_hi']}] + step" if "ctx_lo" in CFG else
-                               f"{CFG['prefix_len']}-token prefix (one of {CFG['prefixes']}, shared blocks) + "
-                               f"U[{CFG['suffix_lo']},{CFG['suffix_hi']}] suffix + step"),
-                       "parallelism": f"kv-head shard x{world}" if world > 1 else "single GPU",
-                       "method": ("all layers run every step" if L == L_model else
-                                  f"{L} resident layers run per step; tok/s and ms_per_step scaled to "
-                                  f"{L_model} layers at the measured per-layer time"),
-                       "l2": ("inputs larger than L2 (each layer reads a distinct pool of >=300 MB)"
-                              if not shared else
-                              "each layer reads a distinct pool; shared prefix blocks (16 MB per layer) are read by "
-                              "every sequence that imported them: the roofline counts them once (unique bytes)")},
-            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak,
-                         "traffic": (CFG["traffic_ratio"] * sum(att_bytes) / len(att_bytes)
-                                     if CFG.get("traffic_ratio") else None),
-                         "traffic_source": CFG.get("traffic_source"),
-                         "kernel": "nf_paged_attention",
-                         "kernel_path": {0: "per-warp cp.async", 1: "tensor map, one copy per block",
-                                         2: "tensor map, one copy per head"}.get(att_path, str(att_path)),
-                         "peak_source": peak_kind, "avg_launch_us": att_avg_ms * 1e3,
-                         **({"bytes": "unique (shared prefix blocks once)",
-                             "achieved_logical": (sum(logical_bytes) / len(logical_bytes)) / (att_avg_ms * 1e-3) / 1e9}
-                            if shared else {})},
-            "cpu_baseline": cpu,
-            "e2e": e2e,
-            "gpu_launches": args.steps * (1 + 2 * L),
-            "clocks": clk,
-        }
-        print(json.dumps(line), flush=True)
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
-
-
-def run_reference(args):
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    if rank != 0:
-        return
-    threads = os.cpu_count() or 1
-    if CFG.get("kind") == "engine":
-        cpu = cpu_engine_rate(max(5.0, 1.0 * args.steps / 10), threads=threads)
-        line = {"impl": "reference", "metric": METRIC, "value": cpu["value"], "unit": "tok/s", "n_gpus": world,
-                "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": CFG["scaling"],
-                "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
-                "config": {"workload": CFG["name"], "model": "GPT-124M (12 layers, 12 heads, d 64, context 2048)"},
-                "cpu_baseline": dict(cpu, kind="port"),
-                "e2e": {"value": cpu["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-        print(json.dumps(line), flush=True)
-        return
-    if CFG.get("kind") == "mixed":
-        cpu = CpuOracleMixed(threads=threads)
-        for _ in range(args.warmup):
-            cpu.layer()
-        pairs = [cpu.layer() for _ in range(args.steps)]
-        v = cpu.rate(sum(a for a, _ in pairs) / len(pairs), sum(b for _, b in pairs) / len(pairs))
-        times = [a + b for a, b in pairs]
-    else:
-        cpu = CpuOracleDecode(threads=threads)
-        for _ in range(args.warmup):
-            cpu.layer()
-        times = [cpu.layer() for _ in range(args.steps)]
-        v = cpu.rate(sum(times) / len(times))
-    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": CFG["scaling"],
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": CFG["name"], "layers": CFG["layers"], "q_heads": CFG["hq"],
-                       "kv_heads": CFG["hkv"], "head_dim": CFG["d"], "block_size": CFG["bs"]},
-            "cpu_baseline": {"value": v, "unit": "tok/s", "cores": torch.get_num_threads(), "kind": "port",
-                             "sample": cpu.describe(len(times), sum(times)) + "; each step = one such call"},
-            "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-    print(json.dumps(line), flush=True)
+    return {
+        "metric": CFG["metric"], "value": B * steps / (ms * 1e-3) * L / L_model, "unit": "tok/s",
+        "n_gpus": world, "steps": steps, "warmup": warmup,
+        "ms_per_step": ms / steps * L_model / L,
+        "higher_is_better": True, "scaling": CFG["scaling"], "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) Q/K/V, random block permutation)",
+        "config": {"workload": CFG["name"], "layers": L_model, "layers_timed": L, "q_heads": CFG["hq"],
+                   "kv_heads": CFG["hkv"], "head_dim": D, "block_size": bs,
+                   "seqs_per_gpu_x_heads": f"{B} seqs x {hkv} kv heads",
+                   "global_batch": B,
+                   "ctx": (f"U[{CFG['ctx_lo']},{CFG['ctx_hi']}] + step" if "ctx_lo" in CFG else
+                           f"{CFG['prefix_len']}-token prefix (one of {CFG['prefixes']}, shared blocks) + "
+                           f"U[{CFG['suffix_lo']},{CFG['suffix_hi']}] suffix + step"),
+                   "parallelism": f"kv-head shard x{world}" if world > 1 else "single GPU",
+                   "method": ("all layers run every step" if L == L_model else
+                              f"{L} resident layer(s) run per step; tok/s and ms_per_step scaled to "
+                              f"{L_model} layers at the measured per-layer time"),
+                   "l2": ("inputs larger than L2 (each layer reads a distinct pool of >=300 MB)"
+                          if not shared else
+                          "each layer reads a distinct pool; shared prefix blocks (16 MB per layer) are read by "
+                          "every sequence that imported them: the roofline counts them once (unique bytes)")},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak,
+                     "traffic": (CFG["traffic_ratio"] * sum(att_bytes) / len(att_bytes)
+                                 if CFG.get("traffic_ratio") else None),
+                     "traffic_source": CFG.get("traffic_source"),
+                     "kernel": "nf_paged_attention",
+                     "kernel_path": {0: "per-warp cp.async", 1: "tensor map, one copy per block",
+                                     2: "tensor map, one copy per head"}.get(att_path, str(att_path)),
+                     "peak_source": peak_kind, "avg_launch_us": att_avg_ms * 1e3,
+                     "bytes_per_launch": sum(att_bytes) / len(att_bytes),
+                     **({"bytes": "unique (shared prefix blocks once)",
+                         "achieved_logical": (sum(logical_bytes) / len(logical_bytes)) / (att_avg_ms * 1e-3) / 1e9}
+                        if shared else {})},
+        "parity": {"rows_checked": len(pick) * world, "max_abs_err": worst, "within_tol": ok,
+                   "against": "float32 torch attention over the pool, last layer of one extra step",
+                   "tol": "rtol 2e-2, atol 2e-2"},
+        "e2e": e2e,
+        "gpu_launches": steps * (1 + 2 * L),
+        "clocks": clk,
+    }
 
 
 # ---------------------------------------------------------------------------- mixed step (prefill + decode)
-def _mixed_shape():
-    rng = np.random.default_rng(CFG["seed"])
-    prefix = rng.integers(0, CFG["prefix_hi"] + 1, size=CFG["chunks"]).tolist()
-    dctx = rng.integers(CFG["dctx_lo"], CFG["dctx_hi"] + 1, size=CFG["decodes"]).tolist()
-    return prefix, dctx
-
-
-def _mixed_flops(prefix, hq, d, chunk):
-    """Algorithmic prefill FLOPs of one layer: unmasked causal pairs only, 4*Hq*D per pair."""
-    return 4.0 * hq * d * sum(chunk * p + chunk * (chunk + 1) / 2 for p in prefix)
-
-
-class CpuOracleMixed:
-    """The reference algorithm on the host for the mixed step: one 512-token chunk and 8 decodes per call."""
-
-    def __init__(self, threads: int | None = None):
-        from oracle.paged import OracleStore
-
-        if threads:
-            torch.set_num_threads(threads)
-        prefix, dctx = _mixed_shape()
-        self.prefix, self.dctx = prefix, dctx
-        H, D, bs, C = CFG["hkv"], CFG["d"], CFG["bs"], CFG["chunk"]
-        self.nd = min(CFG["cpu_sample"], len(dctx))
-        ctx = [prefix[0]] + dctx[: self.nd]
-        st = OracleStore(2, max(ctx) + C + 64, H, D, batch_size=len(ctx), dtype=torch.bfloat16, block_size=bs,
-                         prefix=False)
-        g = torch.Generator().manual_seed(1)
-        for sl, c in enumerate(ctx):
-            if c == 0:
-                continue
-            st.tables[sl].ensure(c)
-            kk = torch.randn(c, H, D, generator=g).to(torch.bfloat16)
-            vv = torch.randn(c, H, D, generator=g).to(torch.bfloat16)
-            for i, b in enumerate(st.tables[sl].blocks):
-                n = min(bs, c - i * bs)
-                st.k[0][b, :n] = kk[i * bs: i * bs + n]
-                st.v[0][b, :n] = vv[i * bs: i * bs + n]
-            st.pos[sl] = c
-        self.store = st
-        hq = CFG["hq"]
-        self.qc = torch.randn(1, C, hq * D, generator=g).to(torch.bfloat16)
-        self.kc = torch.randn(1, C, H * D, generator=g).to(torch.bfloat16)
-        self.qd = torch.randn(self.nd, 1, hq * D, generator=g).to(torch.bfloat16)
-        self.kd = torch.randn(self.nd, 1, H * D, generator=g).to(torch.bfloat16)
-
-    def layer(self) -> tuple[float, float]:
-        from oracle.attention import forward_with_cache
-
-        t0 = time.perf_counter()
-        forward_with_cache(self.store, 0, self.qc, self.kc, self.kc, CFG["hq"], slots=[0])
-        t1 = time.perf_counter()
-        forward_with_cache(self.store, 0, self.qd, self.kd, self.kd, CFG["hq"], slots=list(range(1, self.nd + 1)))
-        return t1 - t0, time.perf_counter() - t1
-
-    def rate(self, t_chunk: float, t_dec: float) -> float:
-        t_layer = len(self.prefix) * t_chunk + len(self.dctx) / self.nd * t_dec
-        tokens = len(self.prefix) * CFG["chunk"] + len(self.dctx)
-        return tokens / (CFG["layers"] * t_layer)
-
-    def describe(self, calls: int, seconds: float) -> str:
-        return (f"one 512-token chunk (prefix {self.prefix[0]}) and {self.nd} of {len(self.dctx)} decodes, one "
-                f"layer x {calls} calls in {seconds:.1f} s, scaled to 4 chunks + 96 decodes x {CFG['layers']} layers")
-
-
-def cpu_mixed_rate(seconds: float, threads: int | None = None):
-    cpu = CpuOracleMixed(threads=threads)
-    tc, td = [], []
-    while sum(tc) + sum(td) < seconds:
-        a, b = cpu.layer()
-        tc.append(a)
-        td.append(b)
-    return {"value": cpu.rate(sum(tc) / len(tc), sum(td) / len(td)), "unit": "tok/s",
-            "cores": torch.get_num_threads(), "sample": cpu.describe(len(tc), sum(tc) + sum(td))}
-
-
-def run_mixed(args):
+def measure_mixed(steps, warmup, e2e_steps, world, rank, local, dev, dist):
+    """The mixed step (CFG): per layer the KV append, the tensor-core prefill of the 4 chunks and the split-K
+    decode, on one plan.  Returns the JSON line's fields."""
     from nifre_b200 import PagedKVCache
     from nifre_b200.sharding import HeadShard
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    dev = torch.device("cuda", local)
-    torch.cuda.set_device(dev)
-    dist = None
-    if world > 1:
-        import datetime
-
-        import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     shard = HeadShard(world, rank, CFG["hq"], CFG["hkv"], CFG["d"])
     hkv, hq = shard.kv_heads, shard.q_heads
-    L, D, bs, C = CFG["layers"], CFG["d"], CFG["bs"], CFG["chunk"]
+    L, D, bs, C = CFG["resident"], CFG["d"], CFG["bs"], CFG["chunk"]
+    L_model = CFG["layers"]
     prefix, dctx = _mixed_shape()
     P, ND = len(prefix), len(dctx)
     B = P + ND
-    steps_total = args.warmup + args.steps + args.e2e_steps + 2
+    steps_total = warmup + steps + e2e_steps + 3
     max_seq = max(max(prefix) + C, max(dctx) + steps_total) + 16
     n_blocks = sum((p + C + bs - 1) // bs for p in prefix) + sum((c + steps_total + 16 + bs - 1) // bs for c in dctx)
     dt = torch.bfloat16
@@ -729,7 +930,7 @@ def run_mixed(args):
             host[3].copy_(out_loc, non_blocking=True)
         return p
 
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         step()
     torch.cuda.synchronize()
     cache.check_status()
@@ -746,31 +947,37 @@ def run_mixed(args):
     # layer each step (events between every pair of kernels would add a
     # drain per event to the step, and keep the decode from starting beside
     # the KV append)
-    for s in range(args.steps):
+    for s in range(steps):
         step(rec_layer=s % L)
     e1.record(stream)
     torch.cuda.synchronize()
     clk = clocks.stop()
-    ms = e0.elapsed_time(e1)
-    if world > 1:
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+    ms = _max_over_ranks(e0.elapsed_time(e1), dev, dist)
     cache.check_status()
-    pre_ms = [a[0].elapsed_time(a[1]) for a, _ in kev]
-    dec_ms = [a[1].elapsed_time(a[2]) for a, _ in kev]
-    pre_avg, dec_avg = sum(pre_ms) / len(pre_ms), sum(dec_ms) / len(dec_ms)
+    pre_avg = _max_over_ranks(sum(a[0].elapsed_time(a[1]) for a, _ in kev) / len(kev), dev, dist)
+    dec_avg = _max_over_ranks(sum(a[1].elapsed_time(a[2]) for a, _ in kev) / len(kev), dev, dist)
     flops = _mixed_flops(prefix, hq, D, C)  # this rank's heads
     dec_bytes = []
     for _, p in kev:
         kv = p.kv_lens[P:]
         dec_bytes.append(int(kv.sum()) * hkv * D * 4 + 2 * ND * hq * D * 2 + 4 * int(((kv + bs - 1) // bs).sum()))
     hbm_peak, hbm_kind = _peaks()
-    tf_peak, tf_kind = _tensor_peak()
+    tf_burst, tf_sust, tf_kind = _tensor_peaks()
+
+    # in-run parity: one more step; the last 4 queries of every chunk and 8 decodes against float32 attention
+    p = step()
+    torch.cuda.synchronize()
+    lay = L - 1
+    checks = [(i, starts[i] + t, prefix[i] + t + 1) for i in range(P) for t in (C - 4, C - 3, C - 2, C - 1)]
+    checks += [(P + i, starts[P + i], int(p.kv_lens[P + i])) for i in _stratified(dctx, 8)]
+    worst, ok = _check_rows(cache, lay, q_all[lay], out_loc[lay], checks, hq // hkv)
+    worst = _max_over_ranks(worst, dev, dist)
+    ok = _max_over_ranks(0.0 if ok else 1.0, dev, dist) == 0.0
+
     # e2e: the same steps through the cache API with q/k/v copied from pinned host memory and the
-    # attention output copied back every layer
+    # attention output copied back
     e2e = None
-    if args.e2e_steps > 1:
+    if e2e_steps > 1:
         host = (q_all.cpu().pin_memory(), k_all.cpu().pin_memory(), v_all.cpu().pin_memory(),
                 torch.empty(L, T, hq * D * world, dtype=dt).pin_memory())
         step(host=host)
@@ -780,58 +987,138 @@ def run_mixed(args):
         a = torch.cuda.Event(enable_timing=True)
         b = torch.cuda.Event(enable_timing=True)
         a.record(stream)
-        for _ in range(args.e2e_steps - 1):
+        for _ in range(e2e_steps - 1):
             step(host=host)
         b.record(stream)
         torch.cuda.synchronize()
-        ems = a.elapsed_time(b)
-        if world > 1:
-            t = torch.tensor([ems], device=dev)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            ems = float(t.item())
-        n = args.e2e_steps - 1
-        e2e = {"value": T * n / (ems * 1e-3), "unit": "tok/s",
+        ems = _max_over_ranks(a.elapsed_time(b), dev, dist)
+        n = e2e_steps - 1
+        e2e = {"value": T * n / (ems * 1e-3) * L / L_model, "unit": "tok/s",
                "h2d_bytes_per_step": L * T * (hq + 2 * hkv) * D * 2, "d2h_bytes_per_step": L * T * hq * world * D * 2,
-               "ms_per_step": ems / n,
+               "ms_per_step": ems / n * L_model / L,
                "path": "PagedKVCache.plan/append_step/attention_step; the step's q/k/v up from pinned host memory in "
                        "one copy per tensor, outputs down in one"}
         cache.check_status()
+    del cache
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    pre_tf = flops * world / (pre_avg * 1e-3) / 1e12
+    dec_gbs = (sum(dec_bytes) / len(dec_bytes)) / (dec_avg * 1e-3) / 1e9
+    return {
+        "metric": CFG["metric"], "value": T * steps / (ms * 1e-3) * L / L_model, "unit": "tok/s", "n_gpus": world,
+        "steps": steps, "warmup": warmup, "ms_per_step": ms / steps * L_model / L,
+        "higher_is_better": True, "scaling": CFG["scaling"], "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) Q/K/V, random block permutation)",
+        "config": {"workload": CFG["name"], "layers": L_model, "layers_timed": L, "q_heads": CFG["hq"],
+                   "kv_heads": CFG["hkv"], "head_dim": D, "block_size": bs, "prefill_chunks": P, "chunk_tokens": C,
+                   "prefixes": prefix, "decodes": ND, "decode_ctx": f"U[{CFG['dctx_lo']},{CFG['dctx_hi']}]",
+                   "tokens_per_step": T, "global_batch": B,
+                   "parallelism": f"kv-head shard x{world}" if world > 1 else "single GPU",
+                   "method": "prefill slots rewound to their prefixes every step; decodes grow by one",
+                   "l2": "inputs larger than L2 (each layer reads a distinct pool of ~250 MB)"},
+        "roofline": {"bound": "tensor", "achieved": pre_tf, "peak": tf_burst, "unit": "TFLOP/s",
+                     "frac": pre_tf / tf_burst, "frac_of_sustained": pre_tf / tf_sust, "traffic": None,
+                     "kernel": "nf_prefill_attention",
+                     "peak_source": f"{tf_kind} burst (the timed region lasts milliseconds, not seconds)",
+                     "avg_launch_us": pre_avg * 1e3, "flops_per_launch": flops * world,
+                     "flops_counted": "4*Hq*D per unmasked (query, key) pair"},
+        "roofline_decode": {"bound": "hbm", "achieved": dec_gbs, "peak": hbm_peak, "unit": "GB/s",
+                            "frac": dec_gbs / hbm_peak, "kernel": "nf_paged_attention",
+                            "peak_source": hbm_kind, "avg_launch_us": dec_avg * 1e3},
+        "parity": {"rows_checked": len(checks) * world, "max_abs_err": worst, "within_tol": ok,
+                   "against": "float32 torch attention over the pool, last layer of one extra step",
+                   "tol": "rtol 2e-2, atol 2e-2"},
+        "e2e": e2e,
+        "gpu_launches": steps * (1 + 3 * L),
+        "clocks": clk,
+    }
+
+
+# ---------------------------------------------------------------------------- arms
+def _sub_result(line: dict) -> dict:
+    keep = ("metric", "value", "unit", "ms_per_step", "steps", "warmup", "config", "roofline", "roofline_decode",
+            "parity", "cpu_baseline", "clocks")
+    return {k: line[k] for k in keep if k in line}
+
+
+def run_ours(args):
+    world, rank, local, dev, dist = _dist_setup()
+    kind = CFG.get("kind")
+    if kind == "mixed":
+        line = measure_mixed(args.steps, args.warmup, args.e2e_steps, world, rank, local, dev, dist)
+        if rank == 0 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_mixed_baseline(12.0)
+    else:
+        line = measure_decode(args.steps, args.warmup, args.e2e_steps, world, rank, local, dev, dist)
+        if rank == 0 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(12.0, CpuOracleDecode,
+                                                CpuReferenceDecode if kind != "prefix" else None)
+    if CFG["name"] == "llama3.2-1b-decode" and not args.no_sub and not args.layers and not args.seqs:
+        subs = {}
+        for name, resident, steps in SUB_RESULTS:
+            with _workload(name, resident=resident):
+                if CFG.get("kind") == "mixed":
+                    sub = measure_mixed(steps, 3, 0, world, rank, local, dev, dist)
+                    if rank == 0 and not args.no_cpu_baseline:
+                        sub["cpu_baseline"] = cpu_mixed_baseline(8.0)
+                else:
+                    sub = measure_decode(steps, 3, 0, world, rank, local, dev, dist)
+                    if rank == 0 and not args.no_cpu_baseline:
+                        sub["cpu_baseline"] = cpu_baseline(8.0, CpuOracleDecode, CpuReferenceDecode)
+                subs[name] = _sub_result(sub)
+                line["gpu_launches"] += sub["gpu_launches"]
+        line["sub_results"] = subs
     if rank == 0:
-        cpu = None
-        if not args.no_cpu_baseline:
-            cpu = cpu_mixed_rate(12.0)
-            cpu["kind"] = "port"
-        pre_tf = flops * world / (pre_avg * 1e-3) / 1e12
-        dec_gbs = (sum(dec_bytes) / len(dec_bytes)) / (dec_avg * 1e-3) / 1e9
-        line = {
-            "metric": METRIC, "value": T * args.steps / (ms * 1e-3), "unit": "tok/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
-            "higher_is_better": True, "scaling": CFG["scaling"], "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic (seeded N(0,1) Q/K/V, random block permutation)",
-            "config": {"workload": CFG["name"], "layers": L, "q_heads": CFG["hq"], "kv_heads": CFG["hkv"],
-                       "head_dim": D, "block_size": bs, "prefill_chunks": P, "chunk_tokens": C,
-                       "prefixes": prefix, "decodes": ND, "decode_ctx": f"U[{CFG['dctx_lo']},{CFG['dctx_hi']}]",
-                       "tokens_per_step": T, "global_batch": B,
-                       "parallelism": f"kv-head shard x{world}" if world > 1 else "single GPU",
-                       "method": "prefill slots rewound to their prefixes every step; decodes grow by one",
-                       "l2": "inputs larger than L2 (each layer reads a distinct pool of ~250 MB)"},
-            "roofline": {"bound": "tensor", "achieved": pre_tf, "peak": tf_peak, "unit": "TFLOP/s",
-                         "frac": pre_tf / tf_peak, "traffic": None, "kernel": "nf_prefill_attention",
-                         "peak_source": tf_kind, "avg_launch_us": pre_avg * 1e3,
-                         "flops_per_launch": flops * world,
-                         "flops_counted": "4*Hq*D per unmasked (query, key) pair"},
-            "roofline_decode": {"bound": "hbm", "achieved": dec_gbs, "peak": hbm_peak, "unit": "GB/s",
-                                "frac": dec_gbs / hbm_peak, "kernel": "nf_paged_attention",
-                                "peak_source": hbm_kind, "avg_launch_us": dec_avg * 1e3},
-            "cpu_baseline": cpu,
-            "e2e": e2e,
-            "gpu_launches": args.steps * (1 + 3 * L),
-            "clocks": clk,
-        }
         print(json.dumps(line), flush=True)
-    if world > 1:
+    if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def run_reference(args):
+    """The reference's CPU path on the host cores (rank 0 alone; other ranks exit without work)."""
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    if CFG.get("kind") == "engine":
+        cpu = cpu_engine_rate(max(5.0, 1.0 * args.steps / 10), threads=threads)
+        line = {"impl": "reference", "metric": METRIC, "value": cpu["value"], "unit": "tok/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": CFG["scaling"],
+                "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
+                "config": {"workload": CFG["name"], "model": "GPT-124M (12 layers, 12 heads, d 64, context 2048)"},
+                "cpu_baseline": dict(cpu, kind="port"),
+                "e2e": {"value": cpu["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
+    use_ref = _reference_modules() is not None and CFG.get("kind") != "prefix"
+    if CFG.get("kind") == "mixed":
+        cpu = (CpuReferenceMixed if use_ref else CpuOracleMixed)(threads=threads)
+        for _ in range(args.warmup):
+            cpu.layer()
+        pairs = [cpu.layer() for _ in range(args.steps)]
+        v = cpu.rate(sum(a for a, _ in pairs) / len(pairs), sum(b for _, b in pairs) / len(pairs))
+        times = [a + b for a, b in pairs]
+    else:
+        cpu = (CpuReferenceDecode if use_ref else CpuOracleDecode)(threads=threads)
+        for _ in range(args.warmup):
+            cpu.layer()
+        times = [cpu.layer() for _ in range(args.steps)]
+        v = cpu.rate(sum(times) / len(times))
+    base = {"value": v, "unit": "tok/s", "cores": torch.get_num_threads(), "host_cpus": os.cpu_count(),
+            "kind": cpu.kind, "sample": cpu.describe(len(times), sum(times)) + "; each step = one such call"}
+    if use_ref:
+        base["layout"] = f"MHA-expanded: KV heads stored repeated to {CFG['hq']} (the reference has one head count)"
+        base["code"] = "reference src/inference/attention.py + paged_kv_cache.py, installed unmodified in baseline/_ref"
+    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": CFG["scaling"],
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": CFG["name"], "layers": CFG["layers"], "q_heads": CFG["hq"],
+                       "kv_heads": CFG["hkv"], "head_dim": CFG["d"], "block_size": CFG["bs"]},
+            "cpu_baseline": base,
+            "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
 
 
 # ---------------------------------------------------------------------------- end-to-end engine (GPT-124M)
@@ -1022,11 +1309,8 @@ def run_engine(args):
 
 def main():
     args = _args()
-    mixed = CFG.get("kind") == "mixed"
     if args.impl == "reference":
         run_reference(args)
-    elif mixed:
-        run_mixed(args)
     elif CFG.get("kind") == "engine":
         run_engine(args)
     else:

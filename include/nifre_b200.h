@@ -55,6 +55,7 @@ extern "C" {
 #define NF_STATUS_BAD_SLOT 8    /* cache slot out of range: entry skipped */
 #define NF_STATUS_BAD_TILE 16   /* prefill tile longer than nf_prefill_tile_rows() rows: rest skipped */
 #define NF_STATUS_BAD_SHARED 32 /* shared-key record that leaves a query no key of its own: its keys skipped */
+#define NF_STATUS_FOREIGN_PARTS 64 /* plan with cascade parts given to nf_paged_attention_noalloc: nothing computed */
 
 /* Record layouts (int32) of the step descriptor the host uploads. */
 #define NF_SEQ_FIELDS 4   /* slot, q_start (row of the first new token), q_len, ctx_before */
@@ -76,6 +77,20 @@ int nf_abi_version(void);
  * A diagnostic with no counterpart in the reference.
  */
 int nf_last_attention_path(void);
+
+/*
+ * Diagnostic, no counterpart in the reference: runs one of the bounded waits
+ * that every kernel of this library uses on a wait that nothing satisfies,
+ * with a limit of limit_cycles SM clock cycles (0 < limit <= the kernels' own
+ * limit of about two seconds).  kind 0: an mbarrier wait (the pipeline
+ * waits); kind 1: a wait until the device counter *counter reaches target
+ * (the split-K kernels' end-of-launch wait).  The kernel must end, set
+ * NF_STATUS_WAIT_TIMEOUT in *status and write 0 to *result (1 if the wait
+ * was satisfied: kind 1 with *counter >= target).  Used by the tests of the
+ * failure detection; nothing faults or hangs.
+ */
+int nf_selftest_wait(int32_t kind, int64_t limit_cycles, const int32_t* counter, int32_t target,
+                     int32_t* status, int32_t* result, void* stream);
 
 /*
  * Diagnostic, no counterpart in the reference: one 128 x N x K bfloat16
@@ -248,7 +263,7 @@ int nf_prefill_attention(void* out, int64_t out_row_stride, const void* q, int64
                          int32_t* status, void* stream);
 
 /* Query rows (tokens x query heads per KV head) of one nf_prefill_attention work item for this
- * head_dim: 128 for 64 (one half per CTA, two CTAs per SM), 256 for 128 (two halves sharing K/V). */
+ * head_dim: 256 (two 128-row halves sharing one stream of K/V tiles) for head_dim 64 and 128. */
 int nf_prefill_tile_rows(int32_t head_dim);
 
 /*
@@ -260,14 +275,19 @@ int nf_prefill_tile_rows(int32_t head_dim);
  * ws_partials / ws_counters.  The split-K scratch is instead a buffer of
  * NF_NOALLOC_SCRATCH_BYTES compiled into this library (every GPU that loads
  * the library holds it until the process exits).  The call allocates
- * nothing: the first call on a device looks up that buffer's device address
- * (so make that first call before any stream capture), and every call clears
- * the buffer's counters with cudaMemsetAsync on `stream`.  A step whose
- * scratch (max_units * num_q_heads * (head_dim + 4) floats, rounded up to
- * 256 bytes, plus max_items * num_kv_heads + 4 ints) exceeds the buffer is
- * rejected with NF_EINVAL.  All calls share the one buffer: calls that
- * overlap on the GPU (other streams, other threads) race and give wrong
- * results.  Arguments and results are otherwise those of nf_paged_attention.
+ * nothing: the first call in a CUDA context looks up that buffer's device
+ * address in that context (so make that first call before any stream
+ * capture), and every call clears the buffer's counters with cudaMemsetAsync
+ * on `stream`, after every argument check has passed (a refused call queues
+ * nothing).  A step whose scratch (max_units * num_q_heads * (head_dim + 4)
+ * floats, rounded up to 256 bytes, plus max_items * num_kv_heads + 4 ints)
+ * exceeds the buffer is rejected with NF_EINVAL.  All calls share the one
+ * buffer: calls that overlap on the GPU (other streams, other threads) race
+ * and give wrong results.  The buffer holds only this call's split-K parts,
+ * so a plan with cascade parts (nf_pack_step given seq_shared; they belong to
+ * nf_cascade_attention's workspace) is not computed: the kernel sets
+ * NF_STATUS_FOREIGN_PARTS and leaves out untouched.  Arguments and results
+ * are otherwise those of nf_paged_attention.
  */
 #define NF_NOALLOC_SCRATCH_BYTES (16u << 20)
 
@@ -280,6 +300,14 @@ int nf_paged_attention_noalloc(void* out, int64_t out_row_stride,
                                const int32_t* items, const int32_t* units, const int32_t* counts,
                                int32_t max_items, int32_t max_units, int32_t split_tokens, float scale,
                                int32_t* status, void* stream);
+
+/*
+ * Test hook of nf_paged_attention_noalloc, no counterpart in the reference:
+ * fills its built-in scratch buffer (in the current CUDA context) with the
+ * byte `byte` on `stream`, so that a test can show that every call of
+ * nf_paged_attention_noalloc clears what must start at zero itself.
+ */
+int nf_noalloc_scratch_fill(int32_t byte, void* stream);
 
 #ifdef __cplusplus
 }

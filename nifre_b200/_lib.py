@@ -21,6 +21,7 @@ NF_STATUS_WAIT_TIMEOUT = 4
 NF_STATUS_BAD_SLOT = 8
 NF_STATUS_BAD_TILE = 16
 NF_STATUS_BAD_SHARED = 32
+NF_STATUS_FOREIGN_PARTS = 64
 
 SEQ_FIELDS, PATCH_FIELDS, ITEM_FIELDS, UNIT_FIELDS = 4, 3, 4, 8
 
@@ -29,7 +30,7 @@ _DTYPE_CODE = {torch.float32: NF_F32, torch.float16: NF_F16, torch.bfloat16: NF_
 EXPORTS = ("nf_last_error", "nf_abi_version", "nf_pack_step", "nf_kv_append",
            "nf_attention_workspace", "nf_paged_attention", "nf_paged_attention_noalloc",
            "nf_last_attention_path", "nf_selftest_umma", "nf_prefill_attention", "nf_prefill_tile_rows",
-           "nf_cascade_attention")
+           "nf_cascade_attention", "nf_selftest_wait", "nf_noalloc_scratch_fill")
 
 _P = ctypes.c_void_p
 _I32 = ctypes.c_int32
@@ -40,6 +41,8 @@ _SIGNATURES = {
     "nf_abi_version": ([], ctypes.c_int),
     "nf_last_attention_path": ([], ctypes.c_int),
     "nf_selftest_umma": ([_P, _P, _P, _I32, _I32, _I32, _P, _P], ctypes.c_int),
+    "nf_selftest_wait": ([_I32, _I64, _P, _I32, _P, _P, _P], ctypes.c_int),
+    "nf_noalloc_scratch_fill": ([_I32, _P], ctypes.c_int),
     "nf_prefill_tile_rows": ([_I32], ctypes.c_int),
     "nf_prefill_attention": ([_P, _I64, _P, _I64, _I32, _P, _P, _I32, _I32, _I32, _I32, _I32, _I32,
                               _P, _I32, _P, _I32, _P, _P, ctypes.c_float, _P, _P], ctypes.c_int),

@@ -55,6 +55,14 @@ class Attention(nn.Module):
 
     # ------------------------------------------------------------------ cached path
     def _forward_with_cache(self, q, k, v, cache: PagedKVCache, layer_id, input_lens, cache_batch_indices):
+        # The reference attends in q's dtype with the step's new K/V at projection precision and the cached
+        # ones cast to q's dtype (attention.py:121-133); torch's matmul there needs q, k and v of one dtype.
+        # This path attends in the cache dtype, which is the same computation exactly when q/k/v share the
+        # cache's dtype (as every reference caller has it: engine.py:218-227 passes the model dtype); other
+        # combinations are refused before any launch rather than computed differently.
+        if not (q.dtype == k.dtype == v.dtype == cache.dtype):
+            raise ValueError(f"q/k/v dtypes ({q.dtype}, {k.dtype}, {v.dtype}) must equal the cache dtype "
+                             f"{cache.dtype}: create the cache with the model's dtype")
         B, T, _ = q.shape
         if cache_batch_indices is None:
             slots = tuple(range(B))
@@ -80,13 +88,13 @@ class Attention(nn.Module):
             k2 = k2.contiguous()
         if v2.stride(1) != 1:
             v2 = v2.contiguous()
-        qk = q2 if q2.dtype == cache.dtype and q2.stride(1) == 1 else q2.to(cache.dtype).contiguous()
+        qk = q2 if q2.stride(1) == 1 else q2.contiguous()
         # padding rows of a left-padded prefill stay zero (attention.py:79); without padding every row is written
         padded = T > 1 and any(n != T for n in lens)
         out = (torch.zeros if padded else torch.empty)((B * T, q.shape[-1]), dtype=cache.dtype, device=q.device)
         cache.append_step(layer_id, k2, v2, plan)
         cache.attention_step(layer_id, qk, plan, out, scale=1.0 / math.sqrt(self.head_dim))
-        return out.view(B, T, -1).to(q.dtype)
+        return out.view(B, T, -1)
 
     # ------------------------------------------------------------------ no-cache path
     def _forward_full_causal(self, q, k, v):

@@ -40,7 +40,11 @@
 // Split-K merge.  A unit whose item has more than one part writes (acc, m, l)
 // to the caller's workspace; the last warp to finish an (item, KV head) --
 // counted with one atomic -- merges all parts and writes the output.
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <math.h>
+
+#include <mutex>
 
 #include "nf_attn_common.cuh"
 #include "nf_internal.h"
@@ -639,7 +643,7 @@ __global__ void __launch_bounds__(256) paged_attention_kernel(const AttnParams p
   if (threadIdx.x == 0) cta_done = 0;
   __syncthreads();
   const int warp = threadIdx.x >> 5;
-  const int n_units = min(__ldg(p.counts + 1), p.max_units);
+  const int n_units = launch_units(p);
   const int total = n_units * p.Hkv;
   unsigned char* ring_ptr = smem + (size_t)warp * p.stages * p.stage_bytes;
   unsigned char* fifo = smem + (size_t)p.W * p.stages * p.stage_bytes + warp * kFifoBytes;
@@ -654,6 +658,9 @@ __global__ void __launch_bounds__(256) paged_attention_kernel(const AttnParams p
 // ---------------------------------------------------------------- host plan
 // Tensor-map staging (nf_attention_tma.cu); NF_EUNSUPPORTED means "use this file's kernel".
 int launch_attention_tma(AttnParams p, int dtype, long long want, cudaStream_t st, int* path);
+
+// Largest head count the entry points accept (keeps every size product in int64).
+constexpr int kMaxHeads = 1 << 16;
 
 struct Plan {
   int W, stages, head_bytes, stage_bytes, smem, swz, tile;
@@ -766,18 +773,23 @@ extern "C" int nf_attention_workspace(int32_t max_units, int32_t max_items, int3
   return ok();
 }
 
-extern "C" int nf_paged_attention(void* out, int64_t out_row_stride, const void* q, int64_t q_row_stride,
-                                  const void* k_pool, const void* v_pool, int32_t dtype, int32_t num_q_heads,
-                                  int32_t num_kv_heads, int32_t head_dim, int32_t block_size, int32_t num_blocks,
-                                  const int32_t* block_tables, int32_t max_blocks_per_seq, const int32_t* items,
-                                  const int32_t* units, const int32_t* counts, int32_t max_items, int32_t max_units,
-                                  int32_t split_tokens, float scale, float* ws_partials, int64_t ws_partial_floats,
-                                  int32_t* ws_counters, int64_t ws_counter_ints, int32_t* status, void* stream) {
-  using namespace nf;
+namespace nf {
+
+// Checks the arguments of nf_paged_attention and fills the launch parameters;
+// nothing is launched or queued.  The split-K workspace is checked against
+// the step's sizes here, so a caller that supplies its own scratch
+// (nf_paged_attention_noalloc) learns of every refusal before it queues work.
+static int prepare_attention(void* out, int64_t out_row_stride, const void* q, int64_t q_row_stride,
+                             const void* k_pool, const void* v_pool, int32_t dtype, int32_t num_q_heads,
+                             int32_t num_kv_heads, int32_t head_dim, int32_t block_size, int32_t num_blocks,
+                             const int32_t* block_tables, int32_t max_blocks_per_seq, const int32_t* items,
+                             const int32_t* units, const int32_t* counts, int32_t max_items, int32_t max_units,
+                             int32_t split_tokens, float scale, float* ws_partials, int64_t ws_partial_floats,
+                             int32_t* ws_counters, int64_t ws_counter_ints, int32_t* status, AttnParams& p,
+                             Plan& pl) {
   const size_t es = dtype_size(dtype);
   auto al = [](const void* ptr, size_t a) { return (reinterpret_cast<uintptr_t>(ptr) % a) == 0; };
   const bool q_smem_ok = es && al(q, 16) && (q_row_stride * (int64_t)es) % 16 == 0;
-  Plan pl;
   int rc = make_plan(dtype, num_q_heads, num_kv_heads, head_dim, q_smem_ok, pl);
   if (rc) return rc;
   if (!out || !q || !k_pool || !v_pool || !block_tables || !items || !units || !counts || !status)
@@ -786,6 +798,9 @@ extern "C" int nf_paged_attention(void* out, int64_t out_row_stride, const void*
     return fail(NF_EINVAL, "nf_paged_attention: sizes must be positive");
   if (split_tokens <= 0 || split_tokens % 16 != 0)
     return fail(NF_EINVAL, "nf_paged_attention: split_tokens (%d) must be a positive multiple of 16", split_tokens);
+  if (num_q_heads > kMaxHeads)
+    return fail(NF_EUNSUPPORTED, "nf_paged_attention: %d query heads (at most %d)", num_q_heads, kMaxHeads);
+  // every factor is bounded (units and items < 2^31, heads <= 2^16, head_dim <= 256): no product overflows
   const int64_t need_p = (int64_t)max_units * num_q_heads * (head_dim + 4);
   const int64_t need_c = (int64_t)max_items * num_kv_heads + 4;
   if (!ws_partials || ws_partial_floats < need_p || !ws_counters || ws_counter_ints < need_c)
@@ -797,7 +812,7 @@ extern "C" int nf_paged_attention(void* out, int64_t out_row_stride, const void*
   if (!al(ws_partials, 16)) return fail(NF_EINVAL, "nf_paged_attention: partials must be 16-byte aligned");
   if (pl.mma && (!al(q, 4) || (q_row_stride * (int64_t)es) % 4 != 0))
     return fail(NF_EINVAL, "nf_paged_attention: q rows must be 4-byte aligned");
-  AttnParams p;
+  p = AttnParams{};
   p.out = static_cast<char*>(out);
   p.out_stride = out_row_stride;
   p.q = static_cast<const char*>(q);
@@ -831,8 +846,13 @@ extern "C" int nf_paged_attention(void* out, int64_t out_row_stride, const void*
   p.tile = pl.tile;
   p.bs16 = block_size % 16 == 0;
   p.q_smem = pl.q_smem;
-  const long long want = (long long)max_units * num_kv_heads;
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  p.pdl = 1;
+  p.own_parts_only = 0;
+  return ok();
+}
+
+static int launch_prepared(const AttnParams& p, const Plan& pl, int dtype, cudaStream_t st) {
+  const long long want = (long long)p.max_units * p.Hkv;
   int arc = NF_EUNSUPPORTED;
   if (pl.mma) {
     int path = 0;
@@ -851,6 +871,26 @@ extern "C" int nf_paged_attention(void* out, int64_t out_row_stride, const void*
   return arc;
 }
 
+}  // namespace nf
+
+extern "C" int nf_paged_attention(void* out, int64_t out_row_stride, const void* q, int64_t q_row_stride,
+                                  const void* k_pool, const void* v_pool, int32_t dtype, int32_t num_q_heads,
+                                  int32_t num_kv_heads, int32_t head_dim, int32_t block_size, int32_t num_blocks,
+                                  const int32_t* block_tables, int32_t max_blocks_per_seq, const int32_t* items,
+                                  const int32_t* units, const int32_t* counts, int32_t max_items, int32_t max_units,
+                                  int32_t split_tokens, float scale, float* ws_partials, int64_t ws_partial_floats,
+                                  int32_t* ws_counters, int64_t ws_counter_ints, int32_t* status, void* stream) {
+  using namespace nf;
+  AttnParams p;
+  Plan pl;
+  const int rc = prepare_attention(out, out_row_stride, q, q_row_stride, k_pool, v_pool, dtype, num_q_heads,
+                                   num_kv_heads, head_dim, block_size, num_blocks, block_tables, max_blocks_per_seq,
+                                   items, units, counts, max_items, max_units, split_tokens, scale, ws_partials,
+                                   ws_partial_floats, ws_counters, ws_counter_ints, status, p, pl);
+  if (rc) return rc;
+  return launch_prepared(p, pl, dtype, static_cast<cudaStream_t>(stream));
+}
+
 // ---------------------------------------------------------------- allocation-free variant
 // Scratch for nf_paged_attention_noalloc: split-K partials followed by the
 // part counters and the work queue.  It lives in this library's image, so
@@ -858,10 +898,55 @@ extern "C" int nf_paged_attention(void* out, int64_t out_row_stride, const void*
 static __device__ __align__(256) unsigned char g_noalloc_scratch[NF_NOALLOC_SCRATCH_BYTES];
 
 namespace nf {
-// Device address of g_noalloc_scratch per device, looked up on the first call
-// made with that device current (host code cannot use the symbol itself: on
-// the host it names a stand-in, not device memory).
-static void* g_noalloc_ptr[64] = {nullptr};
+// Device address of g_noalloc_scratch in each CUDA context, looked up on the
+// first call made with that context current (host code cannot use the symbol
+// itself: on the host it names a stand-in, not device memory).  Keyed by the
+// context rather than the device, so a caller that runs in a context of its
+// own (not the device's primary context), or one created after a device
+// reset, gets the address of its own module's copy.
+struct ScratchAddr {
+  CUcontext ctx;
+  void* ptr;
+};
+static ScratchAddr g_noalloc_addr[64];
+static int g_noalloc_n = 0;
+static std::mutex g_noalloc_mu;
+
+static PFN_cuCtxGetCurrent_v4000 ctx_get_fn() {
+  static PFN_cuCtxGetCurrent_v4000 fn = nullptr;
+  if (!fn) {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &f, 4000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(f);
+  }
+  return fn;
+}
+
+// The scratch address in the current context (set up on first use).
+static int noalloc_scratch(unsigned char** out) {
+  // make sure a context is current (the runtime creates the primary one on first use)
+  cudaError_t e = cudaFree(nullptr);
+  if (e != cudaSuccess) return fail(NF_ECUDA, "nf_paged_attention_noalloc: no CUDA context: %s", cudaGetErrorString(e));
+  auto get_ctx = ctx_get_fn();
+  CUcontext ctx = nullptr;
+  if (!get_ctx || get_ctx(&ctx) != CUDA_SUCCESS || !ctx)
+    return fail(NF_ECUDA, "nf_paged_attention_noalloc: cannot identify the current CUDA context");
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  for (int i = 0; i < g_noalloc_n; ++i)
+    if (g_noalloc_addr[i].ctx == ctx) {
+      *out = static_cast<unsigned char*>(g_noalloc_addr[i].ptr);
+      return ok();
+    }
+  void* ptr = nullptr;
+  e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+  if (e != cudaSuccess || !ptr)
+    return fail(NF_ECUDA, "nf_paged_attention_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+  if (g_noalloc_n < 64) g_noalloc_addr[g_noalloc_n++] = ScratchAddr{ctx, ptr};
+  *out = static_cast<unsigned char*>(ptr);
+  return ok();
+}
 }  // namespace nf
 
 extern "C" int nf_paged_attention_noalloc(void* out, int64_t out_row_stride, const void* q, int64_t q_row_stride,
@@ -874,35 +959,48 @@ extern "C" int nf_paged_attention_noalloc(void* out, int64_t out_row_stride, con
   using namespace nf;
   if (max_units <= 0 || max_items <= 0 || num_q_heads <= 0 || num_kv_heads <= 0 || head_dim <= 0)
     return fail(NF_EINVAL, "nf_paged_attention_noalloc: sizes must be positive");
+  if (num_q_heads > kMaxHeads || num_kv_heads > num_q_heads || head_dim > 256)
+    return fail(NF_EINVAL, "nf_paged_attention_noalloc: head counts or head_dim out of range");
+  // each factor is bounded above, so no product overflows; each part is checked against the buffer on its own
+  const int64_t cap = (int64_t)NF_NOALLOC_SCRATCH_BYTES;
   const int64_t part_floats = (int64_t)max_units * num_q_heads * (head_dim + 4);
   const int64_t cnt_ints = (int64_t)max_items * num_kv_heads + 4;
   const int64_t part_bytes = ((part_floats * 4 + 255) / 256) * 256;
-  const int64_t need = part_bytes + cnt_ints * 4;
-  if (need > (int64_t)NF_NOALLOC_SCRATCH_BYTES)
+  if (part_bytes > cap || cnt_ints * 4 > cap || part_bytes + cnt_ints * 4 > cap)
     return fail(NF_EINVAL,
                 "nf_paged_attention_noalloc: this step needs %lld bytes of scratch, the built-in buffer holds %lld "
                 "(use nf_paged_attention with a caller-owned workspace, or a larger split_tokens)",
-                (long long)need, (long long)NF_NOALLOC_SCRATCH_BYTES);
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return fail(NF_ECUDA, "nf_paged_attention_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
-  if (dev < 0 || dev >= 64) return fail(NF_EUNSUPPORTED, "nf_paged_attention_noalloc: device index %d", dev);
-  if (!g_noalloc_ptr[dev]) {
-    void* ptr = nullptr;
-    e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
-    if (e != cudaSuccess || !ptr)
-      return fail(NF_ECUDA, "nf_paged_attention_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
-    g_noalloc_ptr[dev] = ptr;
-  }
-  unsigned char* base = static_cast<unsigned char*>(g_noalloc_ptr[dev]);
+                (long long)(part_bytes + cnt_ints * 4), (long long)cap);
+  unsigned char* base = nullptr;
+  int rc = noalloc_scratch(&base);
+  if (rc) return rc;
   float* partials = reinterpret_cast<float*>(base);
   int32_t* counters = reinterpret_cast<int32_t*>(base + part_bytes);
+  AttnParams p;
+  Plan pl;
+  rc = prepare_attention(out, out_row_stride, q, q_row_stride, k_pool, v_pool, dtype, num_q_heads, num_kv_heads,
+                         head_dim, block_size, num_blocks, block_tables, max_blocks_per_seq, items, units, counts,
+                         max_items, max_units, split_tokens, scale, partials, part_floats, counters, cnt_ints, status,
+                         p, pl);
+  if (rc) return rc;  // refused before anything is queued
+  // The buffer is shared by every call and keeps the last call's contents:
+  // the counters and the work queue must start at zero (the partials need no
+  // clearing).  The launch then goes in plain stream order behind the clear,
+  // and refuses plans with cascade parts, whose slots this buffer never holds.
+  p.pdl = 0;
+  p.own_parts_only = 1;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  // counters and the work queue must start at zero; the partials need no clearing
-  e = cudaMemsetAsync(counters, 0, cnt_ints * 4, st);
+  cudaError_t e = cudaMemsetAsync(counters, 0, cnt_ints * 4, st);
   if (e != cudaSuccess) return fail(NF_ECUDA, "nf_paged_attention_noalloc: clearing counters: %s", cudaGetErrorString(e));
-  return nf_paged_attention(out, out_row_stride, q, q_row_stride, k_pool, v_pool, dtype, num_q_heads, num_kv_heads,
-                            head_dim, block_size, num_blocks, block_tables, max_blocks_per_seq, items, units, counts,
-                            max_items, max_units, split_tokens, scale, partials, part_floats, counters, cnt_ints,
-                            status, stream);
+  return launch_prepared(p, pl, dtype, st);
+}
+
+extern "C" int nf_noalloc_scratch_fill(int32_t byte, void* stream) {
+  using namespace nf;
+  unsigned char* base = nullptr;
+  const int rc = noalloc_scratch(&base);
+  if (rc) return rc;
+  const cudaError_t e = cudaMemsetAsync(base, byte & 0xff, NF_NOALLOC_SCRATCH_BYTES, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return fail(NF_ECUDA, "nf_noalloc_scratch_fill: %s", cudaGetErrorString(e));
+  return ok();
 }

@@ -85,7 +85,10 @@ __device__ int tma_producer(const AttnParams& p, const CUtensorMap* tk, const CU
   // append of this layer, with programmatic stream serialization).  The
   // ticket, unit records and block tables come from the step's pack, which
   // completed before that kernel began; only the pools, where the append
-  // writes the new keys and values, must wait for it.
+  // writes the new keys and values, must wait for it.  A launch whose queue
+  // is cleared by the operation just before it (the allocation-free entry
+  // point's memset) goes without programmatic serialization (p.pdl = 0), so
+  // the first ticket is taken only after that clear.
   if (w < total) {
     const int lb = rb.x / p.bs;
     if (lb < p.max_blocks) asm volatile("prefetch.global.L1 [%0];" ::"l"(p.bt + (long long)ra.y * p.max_blocks + lb));
@@ -375,7 +378,7 @@ __global__ void __launch_bounds__(kTmaMaxThreads, 1) paged_attention_tma_kernel(
     cta_done = 0;
   }
   __syncthreads();
-  const int n_units = min(__ldg(p.counts + 1), p.max_units);
+  const int n_units = launch_units(p);
   const int total = n_units * p.n_hg;
   if (warp < p.HG) {
     tma_consumer<T, D_>(p, base, box_bytes);
@@ -543,7 +546,7 @@ int launch_attention_tma(AttnParams p, int dtype, long long want, cudaStream_t s
   attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 2;
+  cfg.numAttrs = p.pdl ? 2 : 1;
   e = cudaLaunchKernelEx(&cfg, kern, p, tk, tv);
   if (e != cudaSuccess) {  // not available with this launch: plain stream order
     (void)cudaGetLastError();

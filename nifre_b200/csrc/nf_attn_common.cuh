@@ -31,7 +31,27 @@ struct AttnParams {
   // launch plan
   int W, stages, head_bytes, stage_bytes, swz, tile, bs16, q_smem;
   int HG, n_hg;  // tensor-map path: KV heads per CTA and head groups
+  int pdl;             // 1: may be launched with programmatic stream serialization
+  int own_parts_only;  // 1: the workspace holds only this launch's parts (no cascade parts to merge)
 };
+
+// A launch whose workspace cannot hold partial slots written by another
+// kernel (own_parts_only) refuses a plan with cascade parts (partial slots
+// beyond its own units, counts[3] > counts[1]): it flags
+// NF_STATUS_FOREIGN_PARTS and does no work, instead of merging slots that
+// were never written.
+__device__ __forceinline__ bool parts_refused(const AttnParams& p) {
+  return p.own_parts_only && __ldg(p.counts + 3) > __ldg(p.counts + 1);
+}
+
+// Units of the launch (0 for a refused plan, which is flagged once).
+__device__ __forceinline__ int launch_units(const AttnParams& p) {
+  if (parts_refused(p)) {
+    if (blockIdx.x == 0 && threadIdx.x == 0) atomicOr(p.status, NF_STATUS_FOREIGN_PARTS);
+    return 0;
+  }
+  return min(__ldg(p.counts + 1), p.max_units);
+}
 
 constexpr float kNegInf = -INFINITY;
 
@@ -125,20 +145,12 @@ template <typename T, int PB>
 __device__ void finish_launch(const AttnParams& p, int* cta_done, int total) {
   __shared__ int go;
   __syncthreads();  // the CTA's output and part stores are issued
-  const bool merge = __ldg(p.counts + 2) != 0;  // set by the pack when an item has several parts
+  // set by the pack when an item has several parts
+  const bool merge = __ldg(p.counts + 2) != 0 && !parts_refused(p);
   if (threadIdx.x == 0) {
     __threadfence();
     atomicAdd(p.queue + 2, *cta_done);
-    int ok = 1;
-    const long long t0 = clock64();
-    while (merge && *reinterpret_cast<volatile int*>(p.queue + 2) < total) {
-      if (clock64() - t0 > kWaitLimitCycles) {
-        atomicOr(p.status, NF_STATUS_WAIT_TIMEOUT);
-        ok = 0;
-        break;
-      }
-      __nanosleep(256);
-    }
+    const bool ok = !merge || wait_count(p.queue + 2, total, p.status);
     __threadfence();
     go = ok;
   }

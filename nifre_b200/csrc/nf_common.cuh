@@ -92,16 +92,33 @@ __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepc
 // the caller then leaves its loops, so no kernel can spin forever.
 constexpr long long kWaitLimitCycles = 4000000000LL;
 
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* status) {
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* status,
+                                          long long limit = kWaitLimitCycles) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (clock64() - t0 > kWaitLimitCycles) {
+    if (clock64() - t0 > limit) {
       atomicOr(status, NF_STATUS_WAIT_TIMEOUT);
       return false;
     }
   }
+}
+
+// Waits, with the same kind of time limit, until the global counter reaches
+// `total` (the grid-wide wait of the attention kernels' end-of-launch merge).
+// Returns false, with NF_STATUS_WAIT_TIMEOUT set, when the limit runs out.
+__device__ __forceinline__ bool wait_count(const int* counter, int total, int* status,
+                                           long long limit = kWaitLimitCycles) {
+  const long long t0 = clock64();
+  while (*reinterpret_cast<const volatile int*>(counter) < total) {
+    if (clock64() - t0 > limit) {
+      atomicOr(status, NF_STATUS_WAIT_TIMEOUT);
+      return false;
+    }
+    __nanosleep(256);
+  }
+  return true;
 }
 
 // One-dimensional TMA bulk copy global -> shared, completing on an mbarrier.

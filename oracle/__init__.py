@@ -22,6 +22,7 @@ paged      -- block allocator, block table, prefix index, paged KV store
               ``prefix_cache.py``, ``paged_kv_cache.py``)
 attention  -- cached causal attention per row, with grouped-query heads
               expanded by ``repeat_interleave`` (reference ``attention.py``)
-workloads  -- seeded synthetic ragged batches with the shapes of the
-              benchmark configurations
+engine     -- greedy generation one request at a time (reference
+              ``engine.py``/``model_runner.py`` semantics), for the
+              end-to-end configuration's tokens and CPU baseline
 """

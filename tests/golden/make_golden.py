@@ -1,10 +1,10 @@
 """Generate the golden fixtures by running the reference implementation itself.
 
-Run from the repository root in a container where the reference checkout is
-mounted (it is read at ``/root/reference`` by default, override with
-``NIFRE_REF``):
+Run from the repository root where a checkout of the reference is available,
+giving its root directory (the one holding ``src/inference``) as the first
+argument or in ``NIFRE_REF``:
 
-    PYTHONDONTWRITEBYTECODE=1 python tests/golden/make_golden.py
+    PYTHONDONTWRITEBYTECODE=1 python tests/golden/make_golden.py <reference root>
 
 Every fixture records inputs and the outputs of the reference's own modules
 (``src/inference/attention.py``, ``paged_kv_cache.py``, ``block_allocator.py``,
@@ -27,7 +27,10 @@ from pathlib import Path
 
 import torch
 
-REF = Path(os.environ.get("NIFRE_REF", "/root/reference")) / "src"
+_root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("NIFRE_REF")
+if not _root:
+    raise SystemExit("usage: make_golden.py <reference root> (or set NIFRE_REF)")
+REF = Path(_root) / "src"
 sys.path.insert(0, str(REF))
 sys.dont_write_bytecode = True
 

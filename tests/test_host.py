@@ -199,7 +199,7 @@ def test_library_exports_every_declared_symbol():
     for s in syms:
         assert hasattr(lib, s), s
     assert set(_lib.EXPORTS) <= set(syms)
-    assert _lib.load().nf_abi_version() == 11
+    assert _lib.load().nf_abi_version() == 12
 
 
 def test_workspace_sizing_and_argument_errors():
@@ -272,3 +272,18 @@ def test_split_for_policy():
     assert f32.split_for(8 * 300) == 32  # 8 sequences x 12 heads: 32-key units
     big = f32.split_for(64 * 4000)
     assert big % 32 == 0 and big > 32
+
+
+def test_attention_refuses_dtypes_other_than_the_cache_dtype():
+    """The reference attends in q's dtype with new K/V at projection precision (attention.py:121-133); the
+    library attends in the cache dtype, so q/k/v of another dtype are refused on the host, before any launch."""
+    import torch
+    from nifre_b200 import Attention, PagedKVCache
+    cache = PagedKVCache(1, 64, 2, 64, device="cpu", dtype=torch.float16)
+    attn = Attention(4, 64)
+    q = torch.zeros(1, 1, 256)
+    kv = torch.zeros(1, 1, 128)
+    with pytest.raises(ValueError, match="must equal the cache dtype"):
+        attn(q, kv, kv, kv_cache=cache, layer_id=0)
+    with pytest.raises(ValueError, match="must equal the cache dtype"):
+        attn(q.half(), kv, kv.half(), kv_cache=cache, layer_id=0)
