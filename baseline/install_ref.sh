@@ -9,7 +9,8 @@ set -euo pipefail
 REF=${1:-/root/reference}
 HERE=$(cd "$(dirname "$0")" && pwd)
 TMP=$(mktemp -d /tmp/nifre_ref.XXXXXX)
-cp -r "$REF/src" "$TMP/src"
+mkdir -p "$TMP/src"
+cp -r "$REF/src/inference" "$REF/src/sampler.py" "$TMP/src/"
 cat > "$TMP/pyproject.toml" <<'TOML'
 [build-system]
 requires = ["setuptools"]
@@ -21,9 +22,10 @@ version = "0.0.0"
 
 [tool.setuptools.packages.find]
 where = ["src"]
+include = ["inference*"]
 
 [tool.setuptools]
-py-modules = []
+py-modules = ["sampler"]
 TOML
 python -m pip install --no-index --no-build-isolation --no-deps --find-links /opt/wheelhouse \
     --target "$HERE/_ref" --upgrade "$TMP"

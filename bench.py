@@ -67,7 +67,7 @@ WORKLOADS = {
                                traffic_source="ncu capture of the 1-layer case, scaled by keys read"),
     "llama3-8b-long": dict(layers=32, resident=4, hq=32, hkv=8, d=128, bs=16, seqs=256, ctx_lo=4096,
                            ctx_hi=32768, seed=0, scaling="strong", steps=20, cpu_sample=2,
-                           metric="paged-attn decode tok/s (8B shape, 32 layers, 4 resident, per-layer timed)"),
+                           metric="paged-attn decode tok/s (8B shape, 32 layers, per-layer timed)"),
     # one continuous-batching step of the 1B shape: 4 prefill chunks of 512 tokens continuing cached
     # prefixes U[0, 2048] (rewound every step, so every timed step is this one) + 96 decodes U[256, 2048]
     "llama3.2-1b-mixed": dict(kind="mixed", layers=16, resident=16, hq=32, hkv=8, d=64, bs=16, seed=0,
@@ -93,7 +93,8 @@ CFG = dict(name="llama3.2-1b-decode", **WORKLOADS["llama3.2-1b-decode"])
 METRIC = CFG["metric"]
 
 # sub-results of the default run: (workload, resident layers, timed steps)
-SUB_RESULTS = (("llama3-8b-long", 1, 12), ("llama3.2-1b-mixed", 16, 16))
+SUB_RESULTS = (("llama3-8b-long", 1, 12), ("llama3.2-1b-mixed", 16, 16), ("llama3.2-1b-prefix", 16, 20),
+               ("gpt124m-engine", 12, 130))
 
 
 def _args():
@@ -379,6 +380,50 @@ class CpuReferenceDecode(_CpuDecodeBase):
             t0 = time.perf_counter()
             self.attn(self.q, self.k, self.k, kv_cache=self.cache, layer_id=0)
             return time.perf_counter() - t0
+
+
+class CpuReferencePrefix(CpuReferenceDecode):
+    """The shared-prefix workload on the reference's own code: its PagedKVCache with its prefix cache enabled,
+    built the way its engine builds it (try_load_prefix, append the rest, register_prefix; prefix_cache.py:33-81,
+    paged_kv_cache.py:87-105), so that sampled requests on the same prefix share its blocks; then decode layers
+    through its Attention as in the decode workload."""
+
+    def __init__(self, n_sample: int | None = None, threads: int | None = None):
+        _CpuDecodeBase.__init__(self, n_sample, threads)
+        mods = _reference_modules()
+        if mods is None:
+            raise RuntimeError("the reference is not installed in baseline/_ref")
+        Attention, RefCache = mods
+        Hq, Hkv, D, bs = CFG["hq"], CFG["hkv"], CFG["d"], CFG["bs"]
+        G = Hq // Hkv
+        prefixes, group, suffix = _prefix_shape(CFG["seqs"])
+        population = [CFG["prefix_len"] + len(x) for x in suffix]
+        pick = _stratified(population, self.n)
+        self.ctx = [population[i] for i in pick]
+        cache = RefCache(2, max(self.ctx) + 64, Hq, D, device="cpu", dtype=torch.bfloat16, block_size=bs,
+                         enable_prefix_cache=True)
+        cache.init_batch(self.n)
+        with torch.no_grad():
+            for s_, r in enumerate(pick):
+                tokens = prefixes[group[r]] + suffix[r]
+                matched = cache.try_load_prefix(s_, tokens)
+                n_new = len(tokens) - matched
+                kk = torch.randn(n_new, Hkv, D, generator=self.g).to(torch.bfloat16).repeat_interleave(G, dim=1)
+                vv = torch.randn(n_new, Hkv, D, generator=self.g).to(torch.bfloat16).repeat_interleave(G, dim=1)
+                cache.append(s_, 0, kk, vv)
+                cache.append(s_, 1, kk, vv)
+                cache.register_prefix(s_, tokens)
+        # block references beyond the distinct blocks held: the imported (shared) prefix blocks
+        self.shared_blocks = int(sum(len(t.physical_blocks()) for t in cache.block_tables) - cache.allocated_blocks)
+        self.cache = cache
+        self.attn = Attention(Hq, D)
+        self.q = torch.randn(self.n, 1, Hq * D, generator=self.g).to(torch.bfloat16)
+        self.k = (torch.randn(self.n, 1, Hkv, D, generator=self.g).to(torch.bfloat16)
+                  .repeat_interleave(G, dim=2).reshape(self.n, 1, Hq * D))
+
+    def describe(self, calls: int, seconds: float) -> str:
+        return super().describe(calls, seconds) + (f"; {self.shared_blocks} block references shared through the "
+                                                   "reference prefix cache")
 
 
 def _time_cpu(make, seconds: float, warmup: int = 1):
@@ -1036,15 +1081,17 @@ def measure_mixed(steps, warmup, e2e_steps, world, rank, local, dev, dist):
 
 # ---------------------------------------------------------------------------- arms
 def _sub_result(line: dict) -> dict:
-    keep = ("metric", "value", "unit", "ms_per_step", "steps", "warmup", "config", "roofline", "roofline_decode",
-            "parity", "cpu_baseline", "clocks")
+    keep = ("metric", "value", "unit", "ms_per_step", "steps", "warmup", "dtype", "config", "roofline",
+            "roofline_decode", "parity", "cpu_baseline", "e2e", "clocks")
     return {k: line[k] for k in keep if k in line}
 
 
 def run_ours(args):
     world, rank, local, dev, dist = _dist_setup()
     kind = CFG.get("kind")
-    if kind == "mixed":
+    if kind == "engine":
+        line = measure_engine(args, world, rank, local, dev, dist)
+    elif kind == "mixed":
         line = measure_mixed(args.steps, args.warmup, args.e2e_steps, world, rank, local, dev, dist)
         if rank == 0 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_mixed_baseline(12.0)
@@ -1052,19 +1099,25 @@ def run_ours(args):
         line = measure_decode(args.steps, args.warmup, args.e2e_steps, world, rank, local, dev, dist)
         if rank == 0 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(12.0, CpuOracleDecode,
-                                                CpuReferenceDecode if kind != "prefix" else None)
+                                                CpuReferencePrefix if kind == "prefix" else CpuReferenceDecode)
     if CFG["name"] == "llama3.2-1b-decode" and not args.no_sub and not args.layers and not args.seqs:
         subs = {}
         for name, resident, steps in SUB_RESULTS:
             with _workload(name, resident=resident):
-                if CFG.get("kind") == "mixed":
+                sub_kind = CFG.get("kind")
+                if sub_kind == "engine":
+                    sub = measure_engine(argparse.Namespace(steps=steps, warmup=2,
+                                                            no_cpu_baseline=args.no_cpu_baseline),
+                                         world, rank, local, dev, dist)
+                elif sub_kind == "mixed":
                     sub = measure_mixed(steps, 3, 0, world, rank, local, dev, dist)
                     if rank == 0 and not args.no_cpu_baseline:
                         sub["cpu_baseline"] = cpu_mixed_baseline(8.0)
                 else:
                     sub = measure_decode(steps, 3, 0, world, rank, local, dev, dist)
                     if rank == 0 and not args.no_cpu_baseline:
-                        sub["cpu_baseline"] = cpu_baseline(8.0, CpuOracleDecode, CpuReferenceDecode)
+                        sub["cpu_baseline"] = cpu_baseline(
+                            8.0, CpuOracleDecode, CpuReferencePrefix if sub_kind == "prefix" else CpuReferenceDecode)
                 subs[name] = _sub_result(sub)
                 line["gpu_launches"] += sub["gpu_launches"]
         line["sub_results"] = subs
@@ -1083,16 +1136,19 @@ def run_reference(args):
         return
     threads = os.cpu_count() or 1
     if CFG.get("kind") == "engine":
-        cpu = cpu_engine_rate(max(5.0, 1.0 * args.steps / 10), threads=threads)
+        seconds = max(5.0, 1.0 * args.steps / 10)
+        cpu = cpu_engine_reference_rate(seconds, threads=threads)
+        if cpu is None:
+            cpu = dict(cpu_engine_rate(seconds, threads=threads), kind="port", host_cpus=os.cpu_count())
         line = {"impl": "reference", "metric": METRIC, "value": cpu["value"], "unit": "tok/s", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": CFG["scaling"],
                 "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
                 "config": {"workload": CFG["name"], "model": "GPT-124M (12 layers, 12 heads, d 64, context 2048)"},
-                "cpu_baseline": dict(cpu, kind="port"),
+                "cpu_baseline": cpu,
                 "e2e": {"value": cpu["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
         print(json.dumps(line), flush=True)
         return
-    use_ref = _reference_modules() is not None and CFG.get("kind") != "prefix"
+    use_ref = _reference_modules() is not None
     if CFG.get("kind") == "mixed":
         cpu = (CpuReferenceMixed if use_ref else CpuOracleMixed)(threads=threads)
         for _ in range(args.warmup):
@@ -1101,7 +1157,8 @@ def run_reference(args):
         v = cpu.rate(sum(a for a, _ in pairs) / len(pairs), sum(b for _, b in pairs) / len(pairs))
         times = [a + b for a, b in pairs]
     else:
-        cpu = (CpuReferenceDecode if use_ref else CpuOracleDecode)(threads=threads)
+        ref_cls = CpuReferencePrefix if CFG.get("kind") == "prefix" else CpuReferenceDecode
+        cpu = (ref_cls if use_ref else CpuOracleDecode)(threads=threads)
         for _ in range(args.warmup):
             cpu.layer()
         times = [cpu.layer() for _ in range(args.steps)]
@@ -1160,22 +1217,58 @@ def cpu_engine_rate(seconds: float, threads: int | None = None):
                       f"({spent:.1f} s), prefill excluded"}
 
 
-def run_engine(args):
+def cpu_engine_reference_rate(seconds: float, threads: int | None = None):
+    """The reference's own Engine with its own GPT-124M (random init, seed 0, fp32, context 2048) on the host
+    cores, generating the workload's 8 requests through add_request/step (tokens counted by its token
+    callbacks): tok/s over whole generations, prefill included, as the GPU engine's value is; bounded at about
+    ``seconds`` of steps."""
+    if _reference_modules() is None:
+        return None
+    from inference.backends.gpt import GptInferenceModel as RefInferenceModel
+    from inference.engine import Engine as RefEngine
+    from inference.models.gpt import GPT_CONFIG_124M as REF_CFG
+    from inference.models.gpt import GptModel as RefGptModel
+    if threads:
+        torch.set_num_threads(threads)
+    torch.manual_seed(CFG["seed"])
+    model = RefGptModel(dict(REF_CFG, context_length=2048)).eval()
+    eng = RefEngine(RefInferenceModel(model), max_concurrent_requests=CFG["requests"], device=torch.device("cpu"),
+                    prefill_chunk_size=128, max_tokens_per_step=2048)
+    count = [0]
+
+    def on_token(_tok):
+        count[0] += 1
+
+    for prompt in _engine_prompts(CFG["seed"]):
+        eng.register_token_callback(eng.add_request(prompt, CFG["new_tokens"]), on_token)
+    steps, t0 = 0, time.perf_counter()
+    with torch.no_grad():
+        while eng.step():
+            steps += 1
+            if time.perf_counter() - t0 >= seconds:
+                break
+    spent = time.perf_counter() - t0
+    return {"value": count[0] / spent, "unit": "tok/s", "cores": torch.get_num_threads(),
+            "host_cpus": os.cpu_count(), "kind": "reference",
+            "sample": f"the workload's {CFG['requests']} requests through the reference Engine: {steps} steps, "
+                      f"{count[0]} tokens in {spent:.1f} s (prefill included)",
+            "code": "reference src/inference/engine.py + models/gpt.py, installed unmodified in baseline/_ref"}
+
+
+def cpu_engine_baseline(seconds: float, threads: int | None = None):
+    threads = threads or os.cpu_count() or 1
+    port = dict(cpu_engine_rate(seconds, threads=threads), kind="port", host_cpus=os.cpu_count())
+    ref = cpu_engine_reference_rate(seconds, threads=threads)
+    if ref is None:
+        return dict(port, note="reference code not installed in baseline/_ref: the port is the baseline")
+    return dict(ref, port=port)
+
+
+def measure_engine(args, world, rank, local, dev, dist):
     """Greedy generation through the engine: every timed step is one Engine.step() (host scheduling, one
     upload of the step's ids/positions, the flat forward, one download of the sampled tokens); N GPUs run N
-    independent replicas."""
+    independent replicas.  Returns the JSON line's fields (rank 0's)."""
     from nifre_b200 import Engine, GptInferenceModel
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    dev = torch.device("cuda", local)
-    torch.cuda.set_device(dev)
-    dist = None
-    if world > 1:
-        import datetime
-
-        import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     torch.backends.cuda.matmul.allow_tf32 = False  # fp32 GEMMs, as the parity test runs them
     eng = Engine(GptInferenceModel(_engine_model(dev)), max_concurrent_requests=CFG["requests"], device=dev,
                  prefill_chunk_size=128, max_tokens_per_step=2048)
@@ -1267,11 +1360,10 @@ def run_engine(args):
     att_bytes = [int(p.kv_lens.sum()) * CFG["hkv"] * CFG["d"] * 4 * 2 + 2 * p.n_tokens * CFG["hq"] * CFG["d"] * 4
                  for _, p in stats["rec"]]
     hbm_peak, hbm_kind = _peaks()
-    if rank == 0:
+    if True:
         cpu = None
-        if not args.no_cpu_baseline:
-            cpu = cpu_engine_rate(12.0)
-            cpu["kind"] = "port"
+        if rank == 0 and not args.no_cpu_baseline:
+            cpu = cpu_engine_baseline(12.0)
         att_avg = sum(att_ms) / max(1, len(att_ms))
         gbs = (sum(att_bytes) / max(1, len(att_bytes))) / (att_avg * 1e-3) / 1e9 if att_ms else None
         value = tokens / (ms * 1e-3)
@@ -1301,18 +1393,16 @@ def run_engine(args):
                             "tokens (value is this end-to-end rate)"},
             "gpu_launches": launches, "clocks": clk,
         }
-        print(json.dumps(line), flush=True)
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
+    del eng, cache
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    return line
 
 
 def main():
     args = _args()
     if args.impl == "reference":
         run_reference(args)
-    elif CFG.get("kind") == "engine":
-        run_engine(args)
     else:
         run_ours(args)
 
