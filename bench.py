@@ -20,7 +20,9 @@ kernel, HBM roofline of the decode kernel).
 With --gpus N (torchrun, one process per GPU) each rank holds 8/N KV heads
 (and the matching 32/N query heads); the 1B decode keeps the work per GPU
 fixed (64*N sequences), the 8B decode and the mixed step shard one batch, and
-the attention outputs are all-gathered over NCCL after every layer.
+every layer's attention kernels store their output rows into all ranks'
+gathered buffers over NVLink (peer stores through CUDA IPC mappings) and end
+once every rank's rows are in place: no collective library call per layer.
 
 Prints one JSON line (rank 0).  --impl reference times the reference's own
 CPU attention path (installed unmodified in baseline/_ref, grouped-query heads
@@ -722,6 +724,12 @@ def measure_decode(steps, warmup, e2e_steps, world, rank, local, dev, dist):
         return _run_decode_timed(steps, warmup, e2e_steps, cache, B, ctx, world, rank, local, dev, dist, shard,
                                  hkv, hq)
     finally:
+        if cache.exchange is not None:
+            torch.cuda.synchronize()
+            if dist is not None:
+                dist.barrier()
+            cache.exchange.close()
+            cache.exchange = None
         del cache
         torch.cuda.synchronize()
         torch.cuda.empty_cache()
@@ -737,27 +745,34 @@ def _run_decode_timed(steps, warmup, e2e_steps, cache, B, ctx, world, rank, loca
     k_all = torch.randn(L, B, hkv * D, device=dev, dtype=dt, generator=gd)
     v_all = torch.randn(L, B, hkv * D, device=dev, dtype=dt, generator=gd)
     out_loc = torch.empty(L, B, hq * D, device=dev, dtype=dt)
-    gathered = torch.empty(world * B, hq * D, device=dev, dtype=dt) if world > 1 else None
     slots, ones, rows = list(range(B)), [1] * B, list(range(B))
     stream = torch.cuda.current_stream(dev)
     att_events = []
+    # N > 1: the attention kernels store every output row into all ranks' gathered buffers (peer stores
+    # over NVLink) and end once all ranks' rows are in place -- the exchange is inside the timed launch
+    ex = None
+    if world > 1:
+        from nifre_b200.sharding import PeerExchange
+        ex = PeerExchange(shard, B, dt, dev, slots=2 * L)
+        cache.exchange = ex
+
+    def out_of(layer):
+        return ex.out(ex.slot_for(layer, cache.steps_closed, L), B) if ex is not None else out_loc[layer]
 
     def step(rec_layer=-1):
         p = cache.plan(slots, ones, rows, q_heads=hq)
         for layer in range(L):
+            o = out_of(layer)
             cache.append_step(layer, k_all[layer], v_all[layer], p)
             record = layer == rec_layer
             if record:
                 e0 = torch.cuda.Event(enable_timing=True)
                 e1 = torch.cuda.Event(enable_timing=True)
                 e0.record(stream)
-            cache.attention_step(layer, q_all[layer], p, out_loc[layer])
+            cache.attention_step(layer, q_all[layer], p, o, exchange=ex)
             if record:
                 e1.record(stream)
                 att_events.append((e0, e1, p))
-            if world > 1:
-                # heads of rank r are query heads [r*hq, (r+1)*hq): (N*B, hq*D) -> (B, N*hq*D)
-                shard.gather(out_loc[layer], buffer=gathered)
         return p
 
     for _ in range(warmup):
@@ -799,12 +814,12 @@ def _run_decode_timed(steps, warmup, e2e_steps, cache, B, ctx, world, rank, loca
     peak, peak_kind = _peaks()
 
     # in-run parity: one more step, then a few of its queries against float32 attention over the pool
+    lay = L - 1
+    o_last = out_of(lay)
     p = step()
     torch.cuda.synchronize()
-    lay = L - 1
     pick = _stratified(p.kv_lens, 6)
-    worst, ok = _check_rows(cache, lay, q_all[lay], out_loc[lay],
-                            [(i, i, int(p.kv_lens[i])) for i in pick], hq // hkv)
+    worst, ok = _check_rows(cache, lay, q_all[lay], o_last, [(i, i, int(p.kv_lens[i])) for i in pick], hq // hkv)
     worst = _max_over_ranks(worst, dev, dist)
     ok = _max_over_ranks(0.0 if ok else 1.0, dev, dist) == 0.0
 
@@ -815,7 +830,7 @@ def _run_decode_timed(steps, warmup, e2e_steps, cache, B, ctx, world, rank, loca
         hq_host = torch.empty(L, B, 1, hq * D, dtype=dt).pin_memory()
         hk_host = torch.empty(L, B, 1, hkv * D, dtype=dt).pin_memory()
         hv_host = torch.empty_like(hk_host).pin_memory()
-        ho_host = torch.empty(L, B, 1, hq * D, dtype=dt).pin_memory()
+        ho_host = torch.empty(L, B, 1, world * hq * D, dtype=dt).pin_memory()
         hq_host.copy_(q_all.view(L, B, 1, -1).cpu())
         hk_host.copy_(k_all.view(L, B, 1, -1).cpu())
         hv_host.copy_(v_all.view(L, B, 1, -1).cpu())
@@ -828,10 +843,9 @@ def _run_decode_timed(steps, warmup, e2e_steps, cache, B, ctx, world, rank, loca
             vd_all = hv_host.to(dev, non_blocking=True)
             outs = []
             for layer in range(L):
+                # with N > 1 the cache's exchange makes this the gathered output of every rank's heads
                 o = attn(qd_all[layer], kd_all[layer], vd_all[layer], kv_cache=cache, layer_id=layer,
                          cache_batch_indices=slots)
-                if world > 1:
-                    o = shard.gather(o.view(B, -1), buffer=gathered).view(B, 1, world * hq * D)[:, :, : hq * D]
                 outs.append(o)
             ho_host.copy_(torch.stack(outs), non_blocking=True)
 
@@ -851,7 +865,7 @@ def _run_decode_timed(steps, warmup, e2e_steps, cache, B, ctx, world, rank, loca
         n_e2e = e2e_steps - 1
         e2e = {"value": B * n_e2e / (ems * 1e-3) * L / L_model, "unit": "tok/s",
                "h2d_bytes_per_step": L * B * (hq + 2 * hkv) * D * 2,
-               "d2h_bytes_per_step": L * B * hq * D * 2,
+               "d2h_bytes_per_step": L * B * world * hq * D * 2,
                "ms_per_step": ems / n_e2e * L_model / L,
                "path": "nifre_b200.Attention.forward per layer; the step's q/k/v copied up from pinned host memory "
                        "in one copy per tensor, its outputs copied down in one"}
@@ -869,7 +883,8 @@ def _run_decode_timed(steps, warmup, e2e_steps, cache, B, ctx, world, rank, loca
                    "ctx": (f"U[{CFG['ctx_lo']},{CFG['ctx_hi']}] + step" if "ctx_lo" in CFG else
                            f"{CFG['prefix_len']}-token prefix (one of {CFG['prefixes']}, shared blocks) + "
                            f"U[{CFG['suffix_lo']},{CFG['suffix_hi']}] suffix + step"),
-                   "parallelism": f"kv-head shard x{world}" if world > 1 else "single GPU",
+                   "parallelism": (f"kv-head shard x{world}; outputs gathered by the attention kernels' peer "
+                                   "stores over NVLink (no collective library call)" if world > 1 else "single GPU"),
                    "method": ("all layers run every step" if L == L_model else
                               f"{L} resident layer(s) run per step; tok/s and ms_per_step scaled to "
                               f"{L_model} layers at the measured per-layer time"),
@@ -941,10 +956,17 @@ def measure_mixed(steps, warmup, e2e_steps, world, rank, local, dev, dist):
     k_all = torch.randn(L, T, hkv * D, device=dev, dtype=dt, generator=gd)
     v_all = torch.randn(L, T, hkv * D, device=dev, dtype=dt, generator=gd)
     out_loc = torch.empty(L, T, hq * D, device=dev, dtype=dt)
-    gathered = torch.empty(world * T, hq * D, device=dev, dtype=dt) if world > 1 else None
     slots = list(range(B))
     stream = torch.cuda.current_stream(dev)
     kev = []
+    ex = None
+    if world > 1:  # outputs gathered by the kernels' peer stores (see measure_decode)
+        from nifre_b200.sharding import PeerExchange
+        ex = PeerExchange(shard, T, dt, dev, slots=2 * L)
+        cache.exchange = ex
+
+    def out_of(layer):
+        return ex.out(ex.slot_for(layer, cache.steps_closed, L), T) if ex is not None else out_loc[layer]
 
     def rewind():  # every step continues the same prefixes (the decodes keep growing)
         for i in range(P):
@@ -960,17 +982,16 @@ def measure_mixed(steps, warmup, e2e_steps, world, rank, local, dev, dist):
                 qd, kd, vd = qa[layer], ka[layer], va[layer]
             else:
                 qd, kd, vd = q_all[layer], k_all[layer], v_all[layer]
+            o = out_of(layer)
             cache.append_step(layer, kd, vd, p)
             ev = None
             if layer == rec_layer:
                 ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
                 kev.append((ev, p))
-            cache.attention_step(layer, qd, p, out_loc[layer], events=ev)
-            o = out_loc[layer]
-            if world > 1:
-                o = shard.gather(o, buffer=gathered)
-                if host is not None:
-                    host[3][layer].copy_(o[:, : hq * D], non_blocking=True)
+            cache.attention_step(layer, qd, p, o, events=ev, exchange=ex)
+            if ex is not None and host is not None:  # o is this rank's columns of the gathered rows
+                host[3][layer].copy_(o.as_strided((T, ex.width), (ex.width, 1), o.storage_offset() - hq * D * rank),
+                                     non_blocking=True)
         if host is not None and world == 1:  # the step's outputs down in one copy
             host[3].copy_(out_loc, non_blocking=True)
         return p
@@ -1010,12 +1031,13 @@ def measure_mixed(steps, warmup, e2e_steps, world, rank, local, dev, dist):
     tf_burst, tf_sust, tf_kind = _tensor_peaks()
 
     # in-run parity: one more step; the last 4 queries of every chunk and 8 decodes against float32 attention
+    lay = L - 1
+    o_last = out_of(lay)
     p = step()
     torch.cuda.synchronize()
-    lay = L - 1
     checks = [(i, starts[i] + t, prefix[i] + t + 1) for i in range(P) for t in (C - 4, C - 3, C - 2, C - 1)]
     checks += [(P + i, starts[P + i], int(p.kv_lens[P + i])) for i in _stratified(dctx, 8)]
-    worst, ok = _check_rows(cache, lay, q_all[lay], out_loc[lay], checks, hq // hkv)
+    worst, ok = _check_rows(cache, lay, q_all[lay], o_last, checks, hq // hkv)
     worst = _max_over_ranks(worst, dev, dist)
     ok = _max_over_ranks(0.0 if ok else 1.0, dev, dist) == 0.0
 
@@ -1044,6 +1066,11 @@ def measure_mixed(steps, warmup, e2e_steps, world, rank, local, dev, dist):
                "path": "PagedKVCache.plan/append_step/attention_step; the step's q/k/v up from pinned host memory in "
                        "one copy per tensor, outputs down in one"}
         cache.check_status()
+    if ex is not None:
+        torch.cuda.synchronize()
+        dist.barrier()
+        ex.close()
+        cache.exchange = None
     del cache
     torch.cuda.synchronize()
     torch.cuda.empty_cache()
@@ -1058,7 +1085,8 @@ def measure_mixed(steps, warmup, e2e_steps, world, rank, local, dev, dist):
                    "kv_heads": CFG["hkv"], "head_dim": D, "block_size": bs, "prefill_chunks": P, "chunk_tokens": C,
                    "prefixes": prefix, "decodes": ND, "decode_ctx": f"U[{CFG['dctx_lo']},{CFG['dctx_hi']}]",
                    "tokens_per_step": T, "global_batch": B,
-                   "parallelism": f"kv-head shard x{world}" if world > 1 else "single GPU",
+                   "parallelism": (f"kv-head shard x{world}; outputs gathered by the attention kernels' peer "
+                                   "stores over NVLink" if world > 1 else "single GPU"),
                    "method": "prefill slots rewound to their prefixes every step; decodes grow by one",
                    "l2": "inputs larger than L2 (each layer reads a distinct pool of ~250 MB)"},
         "roofline": {"bound": "tensor", "achieved": pre_tf, "peak": tf_burst, "unit": "TFLOP/s",
@@ -1089,6 +1117,8 @@ def _sub_result(line: dict) -> dict:
 def run_ours(args):
     world, rank, local, dev, dist = _dist_setup()
     kind = CFG.get("kind")
+    # the CPU baselines run on rank 0 at N = 1 only (the other arm times the reference at every N)
+    args.no_cpu_baseline = args.no_cpu_baseline or world > 1
     if kind == "engine":
         line = measure_engine(args, world, rank, local, dev, dist)
     elif kind == "mixed":

@@ -63,6 +63,28 @@ extern "C" {
 #define NF_ITEM_FIELDS 4  /* slot, q_row, kv_len, unit_base */
 #define NF_UNIT_FIELDS 8  /* item, slot, q_row, part, key_begin, key_end, unit_base, n_parts */
 
+/*
+ * Gathered output over several GPUs of one node (one process per GPU, KV
+ * heads sharded over the ranks).  The attention output rows of this rank's
+ * query heads go to `out` (this GPU's gathered buffer, at this rank's column
+ * offset) and, through peer stores over NVLink, to the same place in every
+ * other rank's gathered buffer: peer_out[i] is that address in the buffer of
+ * the i-th other rank (rank order, this rank left out), as mapped into this
+ * process by nf_ipc_open.  flags[r] is rank r's flag array (int32[n_ranks],
+ * zero when allocated, mapped likewise; flags[rank] is this GPU's own).
+ * epoch numbers the exchanges: the same value on every rank for the same
+ * call, increasing from 1.  n_ranks == 1 means no exchange.
+ */
+#define NF_MAX_RANKS 8
+typedef struct NfGather {
+  int32_t n_ranks;
+  int32_t rank;
+  int32_t epoch;
+  int32_t pad;
+  void* peer_out[NF_MAX_RANKS - 1];
+  int32_t* flags[NF_MAX_RANKS];
+} NfGather;
+
 /* Message of the last failed call on this thread ("" if none). */
 const char* nf_last_error(void);
 
@@ -201,6 +223,50 @@ int nf_paged_attention(void* out, int64_t out_row_stride,
                        int32_t* status, void* stream);
 
 /*
+ * nf_paged_attention_gather: nf_paged_attention whose output is gathered
+ * over the ranks of `gather` (see NfGather) in the same launch, replacing
+ * attention + an all-gather collective: every output row is stored on this
+ * GPU and on each peer; once all of the launch's rows are stored, its last
+ * CTA sets this rank's entry of every rank's flag array to gather->epoch
+ * and waits (time-limited: NF_STATUS_WAIT_TIMEOUT) until every rank has
+ * done the same, so the launch ends with the whole gathered output in this
+ * GPU's buffer.  Outputs written earlier on the same stream by
+ * nf_prefill_attention_gather are covered by the same signal.  Every rank
+ * must make the matching call (same epoch); ranks run on different GPUs.
+ * The shard-parallel form of reference attention.py:77-104 (one process per
+ * GPU, KV heads split over the ranks); gather == NULL is nf_paged_attention.
+ */
+int nf_paged_attention_gather(void* out, int64_t out_row_stride,
+                              const void* q, int64_t q_row_stride,
+                              const void* k_pool, const void* v_pool, int32_t dtype,
+                              int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                              int32_t block_size, int32_t num_blocks,
+                              const int32_t* block_tables, int32_t max_blocks_per_seq,
+                              const int32_t* items, const int32_t* units, const int32_t* counts,
+                              int32_t max_items, int32_t max_units, int32_t split_tokens, float scale,
+                              float* ws_partials, int64_t ws_partial_floats,
+                              int32_t* ws_counters, int64_t ws_counter_ints,
+                              const NfGather* gather, int32_t* status, void* stream);
+
+/*
+ * nf_exchange_barrier: the signal-and-wait of a gathered output on its own
+ * (one thread): for a layer whose rows were all written by
+ * nf_prefill_attention_gather (no decode launch follows to signal).
+ */
+int nf_exchange_barrier(const NfGather* gather, int32_t* status, void* stream);
+
+/*
+ * CUDA IPC mapping of a device buffer into the other processes of the node
+ * (for NfGather).  nf_ipc_handle writes the 64-byte handle of the allocation
+ * holding `ptr` and the offset of `ptr` inside it; nf_ipc_open maps another
+ * process's handle and returns the address at `offset` in this process;
+ * nf_ipc_close unmaps it (pass the address and offset nf_ipc_open gave).
+ */
+int nf_ipc_handle(const void* ptr, void* handle64, int64_t* offset);
+int nf_ipc_open(const void* handle64, int64_t offset, void** ptr);
+int nf_ipc_close(void* ptr, int64_t offset);
+
+/*
  * nf_cascade_attention: partial attention of decode queries over keys that
  * several sequences share (leading blocks imported from the prefix index,
  * prefix_cache.py:33-81, paged_kv_cache.py:87-105), each shared block read
@@ -261,6 +327,22 @@ int nf_prefill_attention(void* out, int64_t out_row_stride, const void* q, int64
                          const int32_t* tiles, int32_t n_tiles,
                          const int32_t* order, int32_t* queue, float scale,
                          int32_t* status, void* stream);
+
+/*
+ * nf_prefill_attention_gather: nf_prefill_attention whose output rows are
+ * also stored into the other ranks' gathered buffers (gather->peer_out,
+ * 16-byte aligned; see NfGather).  It sets no flag: the layer's
+ * nf_paged_attention_gather (or nf_exchange_barrier) on the same stream
+ * signals the peers for all of the layer's rows.
+ */
+int nf_prefill_attention_gather(void* out, int64_t out_row_stride, const void* q, int64_t q_row_stride,
+                                int32_t num_rows, const void* k_pool, const void* v_pool, int32_t dtype,
+                                int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                                int32_t block_size, int32_t num_blocks,
+                                const int32_t* block_tables, int32_t max_blocks_per_seq,
+                                const int32_t* tiles, int32_t n_tiles,
+                                const int32_t* order, int32_t* queue, float scale,
+                                const NfGather* gather, int32_t* status, void* stream);
 
 /* Query rows (tokens x query heads per KV head) of one nf_prefill_attention work item for this
  * head_dim: 256 (two 128-row halves sharing one stream of K/V tiles) for head_dim 64 and 128. */

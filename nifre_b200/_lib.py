@@ -30,11 +30,24 @@ _DTYPE_CODE = {torch.float32: NF_F32, torch.float16: NF_F16, torch.bfloat16: NF_
 EXPORTS = ("nf_last_error", "nf_abi_version", "nf_pack_step", "nf_kv_append",
            "nf_attention_workspace", "nf_paged_attention", "nf_paged_attention_noalloc",
            "nf_last_attention_path", "nf_selftest_umma", "nf_prefill_attention", "nf_prefill_tile_rows",
-           "nf_cascade_attention", "nf_selftest_wait", "nf_noalloc_scratch_fill")
+           "nf_cascade_attention", "nf_selftest_wait", "nf_noalloc_scratch_fill", "nf_paged_attention_gather",
+           "nf_prefill_attention_gather", "nf_exchange_barrier", "nf_ipc_handle", "nf_ipc_open", "nf_ipc_close")
 
 _P = ctypes.c_void_p
 _I32 = ctypes.c_int32
 _I64 = ctypes.c_int64
+
+MAX_RANKS = 8
+
+
+class NfGather(ctypes.Structure):
+    """struct NfGather of include/nifre_b200.h: a gathered output over the ranks of one node."""
+    _fields_ = [("n_ranks", ctypes.c_int32), ("rank", ctypes.c_int32), ("epoch", ctypes.c_int32),
+                ("pad", ctypes.c_int32), ("peer_out", ctypes.c_void_p * (MAX_RANKS - 1)),
+                ("flags", ctypes.c_void_p * MAX_RANKS)]
+
+
+_G = ctypes.POINTER(NfGather)
 
 _SIGNATURES = {
     "nf_last_error": ([], ctypes.c_char_p),
@@ -57,6 +70,15 @@ _SIGNATURES = {
     "nf_paged_attention": ([_P, _I64, _P, _I64, _P, _P, _I32, _I32, _I32, _I32, _I32, _I32,
                             _P, _I32, _P, _P, _P, _I32, _I32, _I32, ctypes.c_float,
                             _P, _I64, _P, _I64, _P, _P], ctypes.c_int),
+    "nf_paged_attention_gather": ([_P, _I64, _P, _I64, _P, _P, _I32, _I32, _I32, _I32, _I32, _I32,
+                                   _P, _I32, _P, _P, _P, _I32, _I32, _I32, ctypes.c_float,
+                                   _P, _I64, _P, _I64, _G, _P, _P], ctypes.c_int),
+    "nf_prefill_attention_gather": ([_P, _I64, _P, _I64, _I32, _P, _P, _I32, _I32, _I32, _I32, _I32, _I32,
+                                     _P, _I32, _P, _I32, _P, _P, ctypes.c_float, _G, _P, _P], ctypes.c_int),
+    "nf_exchange_barrier": ([_G, _P, _P], ctypes.c_int),
+    "nf_ipc_handle": ([_P, _P, ctypes.POINTER(_I64)], ctypes.c_int),
+    "nf_ipc_open": ([_P, _I64, ctypes.POINTER(_P)], ctypes.c_int),
+    "nf_ipc_close": ([_P, _I64], ctypes.c_int),
     "nf_paged_attention_noalloc": ([_P, _I64, _P, _I64, _P, _P, _I32, _I32, _I32, _I32, _I32, _I32,
                                     _P, _I32, _P, _P, _P, _I32, _I32, _I32, ctypes.c_float,
                                     _P, _P], ctypes.c_int),

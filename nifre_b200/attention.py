@@ -91,6 +91,17 @@ class Attention(nn.Module):
         qk = q2 if q2.stride(1) == 1 else q2.contiguous()
         # padding rows of a left-padded prefill stay zero (attention.py:79); without padding every row is written
         padded = T > 1 and any(n != T for n in lens)
+        ex = getattr(cache, "exchange", None)
+        if ex is not None:
+            # KV heads sharded over the ranks of a PeerExchange: the kernels write this rank's heads into every
+            # rank's gathered buffer; the result is the gathered output of all heads
+            if padded:
+                raise ValueError("a sharded cache (exchange set) takes unpadded rows only")
+            slot = ex.slot_for(layer_id, cache.steps_closed, cache.num_layers)
+            cache.append_step(layer_id, k2, v2, plan)
+            cache.attention_step(layer_id, qk, plan, ex.out(slot, B * T), scale=1.0 / math.sqrt(self.head_dim),
+                                 exchange=ex)
+            return ex.gathered(slot, B * T).view(B, T, -1)
         out = (torch.zeros if padded else torch.empty)((B * T, q.shape[-1]), dtype=cache.dtype, device=q.device)
         cache.append_step(layer_id, k2, v2, plan)
         cache.attention_step(layer_id, qk, plan, out, scale=1.0 / math.sqrt(self.head_dim))

@@ -600,7 +600,7 @@ __device__ int warp_simt(const AttnParams& p, uint32_t ring, unsigned char* ring
       }
     }
     if (c.nparts == 1) {
-      T* ob = reinterpret_cast<T*>(p.out) + (long long)c.q_row * p.out_stride + (long long)(c.kvh * p.G) * p.D;
+      const long long ob = (long long)c.q_row * p.out_stride + (long long)(c.kvh * p.G) * p.D;
 #pragma unroll
       for (int n = 0; n < 8; ++n) {
         if (n < p.G) {
@@ -608,7 +608,7 @@ __device__ int warp_simt(const AttnParams& p, uint32_t ring, unsigned char* ring
 #pragma unroll
           for (int i = 0; i < DPL; ++i) {
             const int d = lane + 32 * i;
-            if (d < p.D) ob[n * p.D + d] = Elem<T>::from_f(acc[n][i] * inv);
+            if (d < p.D) store_out<T>(p, ob + n * p.D + d, Elem<T>::from_f(acc[n][i] * inv));
           }
         }
       }
@@ -848,6 +848,36 @@ static int prepare_attention(void* out, int64_t out_row_stride, const void* q, i
   p.q_smem = pl.q_smem;
   p.pdl = 1;
   p.own_parts_only = 0;
+  const size_t vb = es == 2 ? 8 : 16;  // bytes of four output elements
+  p.vec_out = al(out, vb) && (out_row_stride * (int64_t)es) % (int64_t)vb == 0 && head_dim % 4 == 0;
+  p.n_peers = 0;
+  p.n_ranks = 1;
+  p.rank = 0;
+  p.epoch = 0;
+  return ok();
+}
+
+// Fills the gathered-output fields of p from an NfGather (checked); nothing is launched.
+static int apply_gather(AttnParams& p, const NfGather* g, size_t es) {
+  if (!g) return ok();
+  if (g->n_ranks < 1 || g->n_ranks > kMaxRanks || g->rank < 0 || g->rank >= g->n_ranks)
+    return fail(NF_EINVAL, "gathered output: %d ranks (1..%d), rank %d", g->n_ranks, kMaxRanks, g->rank);
+  if (g->n_ranks == 1) return ok();
+  auto al = [](const void* ptr, size_t a) { return (reinterpret_cast<uintptr_t>(ptr) % a) == 0; };
+  const size_t vb = es == 2 ? 8 : 16;
+  for (int r = 0; r < g->n_ranks - 1; ++r) {
+    if (!g->peer_out[r]) return fail(NF_EINVAL, "gathered output: peer_out[%d] is null", r);
+    if (!al(g->peer_out[r], vb)) p.vec_out = 0;
+    p.peer_out[r] = static_cast<char*>(g->peer_out[r]);
+  }
+  for (int r = 0; r < g->n_ranks; ++r) {
+    if (!g->flags[r] || !al(g->flags[r], 4)) return fail(NF_EINVAL, "gathered output: flags[%d] is null or unaligned", r);
+    p.rank_flags[r] = g->flags[r];
+  }
+  p.n_peers = g->n_ranks - 1;
+  p.n_ranks = g->n_ranks;
+  p.rank = g->rank;
+  p.epoch = g->epoch;
   return ok();
 }
 
@@ -887,6 +917,28 @@ extern "C" int nf_paged_attention(void* out, int64_t out_row_stride, const void*
                                    num_kv_heads, head_dim, block_size, num_blocks, block_tables, max_blocks_per_seq,
                                    items, units, counts, max_items, max_units, split_tokens, scale, ws_partials,
                                    ws_partial_floats, ws_counters, ws_counter_ints, status, p, pl);
+  if (rc) return rc;
+  return launch_prepared(p, pl, dtype, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int nf_paged_attention_gather(void* out, int64_t out_row_stride, const void* q, int64_t q_row_stride,
+                                         const void* k_pool, const void* v_pool, int32_t dtype, int32_t num_q_heads,
+                                         int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
+                                         int32_t num_blocks, const int32_t* block_tables, int32_t max_blocks_per_seq,
+                                         const int32_t* items, const int32_t* units, const int32_t* counts,
+                                         int32_t max_items, int32_t max_units, int32_t split_tokens, float scale,
+                                         float* ws_partials, int64_t ws_partial_floats, int32_t* ws_counters,
+                                         int64_t ws_counter_ints, const NfGather* gather, int32_t* status,
+                                         void* stream) {
+  using namespace nf;
+  AttnParams p;
+  Plan pl;
+  int rc = prepare_attention(out, out_row_stride, q, q_row_stride, k_pool, v_pool, dtype, num_q_heads, num_kv_heads,
+                             head_dim, block_size, num_blocks, block_tables, max_blocks_per_seq, items, units, counts,
+                             max_items, max_units, split_tokens, scale, ws_partials, ws_partial_floats, ws_counters,
+                             ws_counter_ints, status, p, pl);
+  if (rc) return rc;
+  rc = apply_gather(p, gather, dtype_size(dtype));
   if (rc) return rc;
   return launch_prepared(p, pl, dtype, static_cast<cudaStream_t>(stream));
 }

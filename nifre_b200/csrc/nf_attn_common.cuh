@@ -31,9 +31,39 @@ struct AttnParams {
   // launch plan
   int W, stages, head_bytes, stage_bytes, swz, tile, bs16, q_smem;
   int HG, n_hg;  // tensor-map path: KV heads per CTA and head groups
+  int vec_out;         // 1: out rows and strides allow 8-byte (16-bit types) / 16-byte (float) stores
   int pdl;             // 1: may be launched with programmatic stream serialization
   int own_parts_only;  // 1: the workspace holds only this launch's parts (no cascade parts to merge)
+  // Gathered output over several GPUs: every output row is also stored at
+  // peer_out[r] (another rank's buffer, same row stride and column offset as
+  // out) for r < n_peers; when the launch is done its last CTA sets this
+  // rank's entry of every rank's flag array to epoch and waits until all
+  // ranks have set theirs (n_ranks > 1).
+  int n_peers, n_ranks, rank, epoch;
+  char* peer_out[kMaxRanks - 1];
+  int* rank_flags[kMaxRanks];
 };
+
+// Stores of output elements at offset `off` (elements from out) on this GPU
+// and on every peer of a gathered output.
+template <typename T>
+__device__ __forceinline__ void store_out(const AttnParams& p, long long off, T v) {
+  reinterpret_cast<T*>(p.out)[off] = v;
+  for (int r = 0; r < p.n_peers; ++r) reinterpret_cast<T*>(p.peer_out[r])[off] = v;
+}
+template <typename T>
+__device__ __forceinline__ void store_out4(const AttnParams& p, long long off, float a, float b, float c, float d) {
+  // four consecutive elements (off a multiple of 4): one 8- or 16-byte store per destination
+  if constexpr (sizeof(T) == 2) {
+    const uint2 v = make_uint2(pack2<T>(a, b), pack2<T>(c, d));
+    *reinterpret_cast<uint2*>(reinterpret_cast<T*>(p.out) + off) = v;
+    for (int r = 0; r < p.n_peers; ++r) *reinterpret_cast<uint2*>(reinterpret_cast<T*>(p.peer_out[r]) + off) = v;
+  } else {
+    const float4 v = make_float4(a, b, c, d);
+    *reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + off) = v;
+    for (int r = 0; r < p.n_peers; ++r) *reinterpret_cast<float4*>(reinterpret_cast<float*>(p.peer_out[r]) + off) = v;
+  }
+}
 
 // A launch whose workspace cannot hold partial slots written by another
 // kernel (own_parts_only) refuses a plan with cascade parts (partial slots
@@ -125,11 +155,15 @@ __device__ void merge_chunk(const AttnParams& p, const Work& c, int c0) {
   }
   if (c0 + lane < GD4) {
     const float inv = L > 0.f ? 1.f / L : 0.f;
-    T* od = reinterpret_cast<T*>(p.out) + (long long)c.q_row * p.out_stride + ((long long)c.kvh * p.G + hn) * D + d;
-    od[0] = Elem<T>::from_f(A.x * inv);
-    od[1] = Elem<T>::from_f(A.y * inv);
-    od[2] = Elem<T>::from_f(A.z * inv);
-    od[3] = Elem<T>::from_f(A.w * inv);
+    const long long off = (long long)c.q_row * p.out_stride + ((long long)c.kvh * p.G + hn) * D + d;
+    if (p.vec_out)
+      store_out4<T>(p, off, A.x * inv, A.y * inv, A.z * inv, A.w * inv);
+    else {
+      store_out<T>(p, off, Elem<T>::from_f(A.x * inv));
+      store_out<T>(p, off + 1, Elem<T>::from_f(A.y * inv));
+      store_out<T>(p, off + 2, Elem<T>::from_f(A.z * inv));
+      store_out<T>(p, off + 3, Elem<T>::from_f(A.w * inv));
+    }
   }
 }
 
@@ -184,6 +218,9 @@ __device__ void finish_launch(const AttnParams& p, int* cta_done, int total) {
       merge_chunk<T, PB>(p, c, grp * 32);
     }
   }
+  // a gathered output: every thread's stores, to this GPU and to its peers,
+  // are made visible system-wide before the CTA counts itself done
+  if (p.n_ranks > 1) __threadfence_system();
   __syncthreads();
   if (threadIdx.x == 0 && atomicAdd(p.queue + 3, 1) == (int)gridDim.x - 1) {
     p.queue[0] = 0;
@@ -191,6 +228,10 @@ __device__ void finish_launch(const AttnParams& p, int* cta_done, int total) {
     p.queue[2] = 0;
     p.queue[3] = 0;
     __threadfence();
+    // the last CTA out: this rank's rows are in every rank's buffer; signal
+    // the peers and wait for theirs, so that the launch ends with the whole
+    // gathered output in place on this GPU
+    if (p.n_ranks > 1) exchange_signal_wait(p.rank_flags, p.n_ranks, p.rank, p.epoch, p.status);
   }
 }
 
@@ -206,18 +247,18 @@ __device__ __forceinline__ void mma_store_output(const AttnParams& p, const Work
   const int lane = threadIdx.x & 31;
   const int n0 = 2 * (lane & 3), tq = lane >> 2;
   const bool h0 = n0 < p.G, h1 = n0 + 1 < p.G;
-  T* ob = reinterpret_cast<T*>(p.out) + (long long)c.q_row * p.out_stride + (long long)(c.kvh * p.G) * D_;
+  const long long ob = (long long)c.q_row * p.out_stride + (long long)(c.kvh * p.G) * D_;
   const float i0 = l0 > 0.f ? 1.f / l0 : 0.f, i1 = l1 > 0.f ? 1.f / l1 : 0.f;
 #pragma unroll
   for (int i = 0; i < KS; ++i) {
     const int d = 16 * i + tq;
     if (h0) {
-      ob[n0 * D_ + d] = Elem<T>::from_f(o[i][0] * i0);
-      ob[n0 * D_ + d + 8] = Elem<T>::from_f(o[i][2] * i0);
+      store_out<T>(p, ob + n0 * D_ + d, Elem<T>::from_f(o[i][0] * i0));
+      store_out<T>(p, ob + n0 * D_ + d + 8, Elem<T>::from_f(o[i][2] * i0));
     }
     if (h1) {
-      ob[(n0 + 1) * D_ + d] = Elem<T>::from_f(o[i][1] * i1);
-      ob[(n0 + 1) * D_ + d + 8] = Elem<T>::from_f(o[i][3] * i1);
+      store_out<T>(p, ob + (n0 + 1) * D_ + d, Elem<T>::from_f(o[i][1] * i1));
+      store_out<T>(p, ob + (n0 + 1) * D_ + d + 8, Elem<T>::from_f(o[i][3] * i1));
     }
   }
 }

@@ -121,6 +121,46 @@ __device__ __forceinline__ bool wait_count(const int* counter, int total, int* s
   return true;
 }
 
+// ---------------------------------------------------------------- cross-GPU exchange
+// Ranks of one exchange (one process per GPU) publish the completion of a
+// launch through flag arrays in each other's memory (CUDA IPC mappings over
+// NVLink): flags[r] of every rank's array holds the last call number (epoch)
+// that rank r finished.  Plain loads and stores over peer memory only.
+constexpr int kMaxRanks = 8;
+
+__device__ __forceinline__ void st_release_sys(int* addr, int v) {
+  asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
+}
+__device__ __forceinline__ int ld_acquire_sys(const int* addr) {
+  int v;
+  asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(addr) : "memory");
+  return v;
+}
+
+// One thread: makes this GPU's earlier writes (its own and, through the
+// barrier before the call, its CTA's) visible system-wide, sets
+// flags[rank] = epoch in every rank's array, then waits, with a time limit,
+// until every rank has set its entry of this rank's array to epoch or later
+// (epochs compared modulo 2^32).  Returns false (NF_STATUS_WAIT_TIMEOUT set)
+// if the limit runs out.
+__device__ __forceinline__ bool exchange_signal_wait(int* const* rank_flags, int n_ranks, int rank, int epoch,
+                                                     int* status, long long limit = kWaitLimitCycles) {
+  __threadfence_system();
+  for (int r = 0; r < n_ranks; ++r) st_release_sys(rank_flags[r] + rank, epoch);
+  const int* mine = rank_flags[rank];
+  const long long t0 = clock64();
+  for (int r = 0; r < n_ranks; ++r) {
+    while (ld_acquire_sys(mine + r) - epoch < 0) {
+      if (clock64() - t0 > limit) {
+        atomicOr(status, NF_STATUS_WAIT_TIMEOUT);
+        return false;
+      }
+      __nanosleep(32);
+    }
+  }
+  return true;
+}
+
 // One-dimensional TMA bulk copy global -> shared, completing on an mbarrier.
 // dst, src and bytes must be multiples of 16.
 __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {

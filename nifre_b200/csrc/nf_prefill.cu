@@ -23,9 +23,10 @@
 //     next S_h overlaps the exponentials), applies the causal mask only on
 //     tiles that cross the diagonal, keeps a reference max that moves only
 //     when a row's max grows by more than 2^8 (O_h and the row sum rescaled
-//     then), computes exp2 with the scale folded into one packed FMA -- a
-//     quarter of them as a polynomial on the FMA pipe, the rest on the
-//     special-function unit, which alone would bound head_dim 64 -- and stores P_h
+//     then), computes exp2 with the scale folded into one packed FMA on the
+//     special-function unit (a polynomial on the FMA pipe is a build option,
+//     NF_PF_POLY: with two warps per scheduler the FMA pipe saturates first,
+//     so it gains nothing at head_dim 64), and stores P_h
 //     as bfloat16/half pairs into tensor memory; at the end it divides by the
 //     row sum and stores the row.
 //
@@ -63,6 +64,9 @@ struct PrefillParams {
   int* queue;        // [2]: next position in the order, CTAs finished (zero on entry and on exit)
   float scale_log2;
   int* status;
+  // gathered output over several GPUs: rows also stored at peer_out[r] (same layout as out), r < n_peers
+  int n_peers;
+  char* peer_out[kMaxRanks - 1];
 };
 
 constexpr float kPfNegInf = -INFINITY;
@@ -105,9 +109,10 @@ struct PfCfg {
 
 // Barriers at the start of the header: k_full[8] 0, k_empty[8] 64,
 // v_full[8] 128, v_empty[8] 192, then per half s_full 256, s_free 272,
-// p_full 288, o_done 304, per Q stage q_full 320, q_empty 336, and per item
-// slot item_full 384, item_empty 416; tensor-memory base at 512, item slots
-// (8 ints each) from 640.
+// p_full 288, o_done 304, per Q stage q_full 320, q_empty 336, per item
+// slot item_full 384, item_empty 416, and per (half, quad) of softmax warps
+// the exponent-pass turn 448; tensor-memory base at 512, item slots (8 ints
+// each) from 640.
 struct PfBars {
   uint32_t hdr;
   __device__ explicit PfBars(uint32_t h) : hdr(h) {}
@@ -123,6 +128,7 @@ struct PfBars {
   __device__ uint32_t q_empty(int s) const { return hdr + 336 + 8 * s; }
   __device__ uint32_t item_full(int s) const { return hdr + 384 + 8 * s; }
   __device__ uint32_t item_empty(int s) const { return hdr + 416 + 8 * s; }
+  __device__ uint32_t turn(int h, int quad) const { return hdr + 448 + 8 * (h * 4 + quad); }
 };
 constexpr uint32_t kPfTmemPtr = 512;
 constexpr uint32_t kPfItemSlots = 640;
@@ -187,6 +193,16 @@ __device__ __forceinline__ void exp2_poly2(uint64_t y2, float& r0, float& r1) {
 // Of every 8 pairs of exponentials, this many go to the polynomial (FMA
 // pipe) and the rest to ex2 (special-function unit, 16 per clock per SM).
 constexpr int kPfPolyPairs = NF_PF_POLY;
+
+#ifndef NF_PF_TURNS
+#define NF_PF_TURNS 0
+#endif
+// 1: the two halves' softmax warps on one scheduler take turns on the
+// special-function unit (see pf_softmax).  Measured slower on B200 (59.4 vs
+// 55.3 us on the mixed-step layer): the mbarrier hand-off costs ~300 cycles
+// per turn and each warp's non-exponent work grows once the halves are out
+// of step, so by default the halves share the unit in step.
+constexpr bool kPfTurns = NF_PF_TURNS != 0;
 
 // A ring position: stage index and the parity of its current fill.
 struct Ring {
@@ -468,6 +484,7 @@ __device__ void pf_softmax(const PrefillParams& p, const PfBars& bar, uint32_t t
   using C = PfCfg<D_>;
   constexpr int NDH = D_ / 64;
   constexpr uint32_t REG = 128 * 128;
+  constexpr bool kTurns = C::NH_ == 2 && kPfTurns;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int quad = warp & 3, row = quad * 32 + lane;  // tensor-memory lanes of this warp: quad*32..
   const uint32_t lane_addr = (uint32_t)(quad * 32) << 16;
@@ -475,6 +492,13 @@ __device__ void pf_softmax(const PrefillParams& p, const PfBars& bar, uint32_t t
   const uint32_t p_addr = tmem + lane_addr + C::p_col(h);
   const int G = p.G;
   int n_s = 0, n_o = 0;
+  // Turns on the special-function unit: this warp and the other half's warp
+  // on the same scheduler (same quad) take their exponent passes in turn,
+  // half 0 first, so that one's loads, maxima and stores overlap the other's
+  // exponentials.  turns counts the passes taken since the CTA started; a
+  // pass waits on the other warp's previous one (mbarrier, time-limited).
+  int turns = 0;
+  const uint32_t my_turn = bar.turn(h, quad), other_turn = bar.turn(h ^ 1, quad);
   Ring vr;  // V ring position of this CTA's current tile (every item advances it)
   int it;
   int4 itl;
@@ -483,70 +507,87 @@ __device__ void pf_softmax(const PrefillParams& p, const PfBars& bar, uint32_t t
     if (h == 0 && w.tl.z > p.NH * p.TT && threadIdx.x == 128) atomicOr(p.status, NF_STATUS_BAD_TILE);
     const Ring vlast = vr.ahead(w.nkt - 1, C::VST);  // V stage of the item's last tile
     vr = vr.ahead(w.nkt, C::VST);
-    if (h >= w.n_half) continue;
-    const int nkt = w.nkt_h[h];
+    const bool active = h < w.n_half;
+    const int nkt = active ? w.nkt_h[h] : 0;
+    // both warps of a quad take one turn per key tile of the item's longer half
+    const int rounds = kTurns ? w.nkt_h[w.n_half - 1] : nkt;
     const int tok = h * p.TT + row / G, hd = row % G;
     const bool valid = tok < min(w.tl.z, p.NH * p.TT) && w.tl.y + tok < p.rows;
     const int qpos = w.tl.w + tok;
     float m = kPfNegInf, l = 0.f;
-    for (int j = 0; j < nkt; ++j) {
-      if (!mbar_wait(bar.s_full(h), n_s & 1, p.status)) return;
-      ++n_s;
-      tc_fence_after();
+    for (int j = 0; j < rounds; ++j) {
+      const bool has = j < nkt;
       uint32_t x[128];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld32(s_addr + c * 32, *reinterpret_cast<uint32_t(*)[32]>(x + 32 * c));
-      tmem_wait_ld();
-#pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_reg_fence(*reinterpret_cast<uint32_t(*)[32]>(x + 32 * c));
-      if (!C::P_ALIAS) {  // S_h is in registers: the next S_h may be computed
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(bar.s_free(h));
-      }
-      const int k0 = j * 128;
-      const int lim = valid ? qpos - k0 : -1;  // columns <= lim are visible (key k <= qpos)
-      if (!__all_sync(0xffffffffu, lim >= 127)) {  // some row of the warp crosses the diagonal
-#pragma unroll
-        for (int i = 0; i < 128; ++i)
-          if (i > lim) x[i] = __float_as_uint(kPfNegInf);
-      }
-      float acc[8];
-#pragma unroll
-      for (int a = 0; a < 8; ++a) acc[a] = fmaxf(__uint_as_float(x[a]), __uint_as_float(x[a + 8]));
-#pragma unroll
-      for (int i = 16; i < 128; i += 16)
-#pragma unroll
-        for (int a = 0; a < 8; ++a) acc[a] = fmax3(acc[a], __uint_as_float(x[i + a]), __uint_as_float(x[i + 8 + a]));
-      const float mt = fmaxf(fmaxf(fmaxf(acc[0], acc[1]), fmaxf(acc[2], acc[3])),
-                             fmaxf(fmaxf(acc[4], acc[5]), fmaxf(acc[6], acc[7]))) * p.scale_log2;
-      // lazy rescaling: the reference max moves (O and l rescaled) only when
-      // the tile's max exceeds it by more than 8, so exponents stay <= 2^8
-      const bool grow = mt > m + 8.f;
-      const float mn = grow ? mt : m;
-      const float alpha = grow ? ex2(m - mn) : 1.f;  // 0 on the first visible tile
-      const float nbase = mn == kPfNegInf ? 0.f : -mn;
-      // exponents (packed pairs: scale and offset in one fp32x2 FMA), row
-      // sum, P packed in pairs into the low half of x
-      const uint64_t sc2 = f2_pack(p.scale_log2, p.scale_log2), nb2 = f2_pack(nbase, nbase);
+      float mn = 0.f, alpha = 1.f, nbase = 0.f;
       uint64_t sum2[4];
+      if (has) {
+        if (!mbar_wait(bar.s_full(h), n_s & 1, p.status)) return;
+        ++n_s;
+        tc_fence_after();
 #pragma unroll
-      for (int a = 0; a < 4; ++a) sum2[a] = 0ull;
+        for (int c = 0; c < 4; ++c) tmem_ld32(s_addr + c * 32, *reinterpret_cast<uint32_t(*)[32]>(x + 32 * c));
+        tmem_wait_ld();
 #pragma unroll
-      for (int i = 0; i < 128; i += 2) {
-        const uint64_t y2 = f2_fma(f2_pack(__uint_as_float(x[i]), __uint_as_float(x[i + 1])), sc2, nb2);
-        float p0, p1;
-        if (((i >> 1) & 7) < kPfPolyPairs) {
-          exp2_poly2(y2, p0, p1);
-        } else {
-          float y0, y1;
-          f2_unpack(y2, y0, y1);
-          p0 = ex2(y0);
-          p1 = ex2(y1);
+        for (int c = 0; c < 4; ++c) tmem_reg_fence(*reinterpret_cast<uint32_t(*)[32]>(x + 32 * c));
+        if (!C::P_ALIAS) {  // S_h is in registers: the next S_h may be computed
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar.s_free(h));
         }
-        sum2[(i >> 1) & 3] = f2_add(sum2[(i >> 1) & 3], f2_pack(p0, p1));
-        x[i >> 1] = pack2<T>(p0, p1);
+        const int k0 = j * 128;
+        const int lim = valid ? qpos - k0 : -1;  // columns <= lim are visible (key k <= qpos)
+        if (!__all_sync(0xffffffffu, lim >= 127)) {  // some row of the warp crosses the diagonal
+#pragma unroll
+          for (int i = 0; i < 128; ++i)
+            if (i > lim) x[i] = __float_as_uint(kPfNegInf);
+        }
+        float acc[8];
+#pragma unroll
+        for (int a = 0; a < 8; ++a) acc[a] = fmaxf(__uint_as_float(x[a]), __uint_as_float(x[a + 8]));
+#pragma unroll
+        for (int i = 16; i < 128; i += 16)
+#pragma unroll
+          for (int a = 0; a < 8; ++a) acc[a] = fmax3(acc[a], __uint_as_float(x[i + a]), __uint_as_float(x[i + 8 + a]));
+        const float mt = fmaxf(fmaxf(fmaxf(acc[0], acc[1]), fmaxf(acc[2], acc[3])),
+                               fmaxf(fmaxf(acc[4], acc[5]), fmaxf(acc[6], acc[7]))) * p.scale_log2;
+        // lazy rescaling: the reference max moves (O and l rescaled) only when
+        // the tile's max exceeds it by more than 8, so exponents stay <= 2^8
+        const bool grow = mt > m + 8.f;
+        mn = grow ? mt : m;
+        alpha = grow ? ex2(m - mn) : 1.f;  // 0 on the first visible tile
+        nbase = mn == kPfNegInf ? 0.f : -mn;
       }
+      if (kTurns && (h == 1 || turns > 0)) {  // the other warp's previous exponent pass is done
+        if (!mbar_wait(other_turn, (uint32_t)((turns - (h == 0 ? 1 : 0)) & 1), p.status)) return;
+      }
+      if (has) {
+        // exponents (packed pairs: scale and offset in one fp32x2 FMA), row
+        // sum, P packed in pairs into the low half of x
+        const uint64_t sc2 = f2_pack(p.scale_log2, p.scale_log2), nb2 = f2_pack(nbase, nbase);
+#pragma unroll
+        for (int a = 0; a < 4; ++a) sum2[a] = 0ull;
+#pragma unroll
+        for (int i = 0; i < 128; i += 2) {
+          const uint64_t y2 = f2_fma(f2_pack(__uint_as_float(x[i]), __uint_as_float(x[i + 1])), sc2, nb2);
+          float p0, p1;
+          if (((i >> 1) & 7) < kPfPolyPairs) {
+            exp2_poly2(y2, p0, p1);
+          } else {
+            float y0, y1;
+            f2_unpack(y2, y0, y1);
+            p0 = ex2(y0);
+            p1 = ex2(y1);
+          }
+          sum2[(i >> 1) & 3] = f2_add(sum2[(i >> 1) & 3], f2_pack(p0, p1));
+          x[i >> 1] = pack2<T>(p0, p1);
+        }
+      }
+      if (kTurns) {  // this warp's exponent pass is done: the other warp's turn
+        __syncwarp();
+        if (lane == 0) mbar_arrive(my_turn);
+        ++turns;
+      }
+      if (!has) continue;
       // O_h += P_h V of tile j-1 must be done before P_h is rewritten and
       // before O_h is rescaled (when a row's max moved)
       if (j > 0) {
@@ -573,7 +614,7 @@ __device__ void pf_softmax(const PrefillParams& p, const PfBars& bar, uint32_t t
       for (int a = 0; a < 4; ++a) f2_unpack(sum2[a], sa[2 * a], sa[2 * a + 1]);
       l = l * alpha + (((sa[0] + sa[1]) + (sa[2] + sa[3])) + ((sa[4] + sa[5]) + (sa[6] + sa[7])));
       m = mn;
-      if (h == w.n_half - 1 && j == nkt - 1 && k0 + row >= w.nkeys) {
+      if (h == w.n_half - 1 && j == nkt - 1 && j * 128 + row >= w.nkeys) {
         // V rows past the item's last key (their P is 0) may hold anything:
         // zero them so that 0 * NaN cannot reach O
         if (!mbar_wait(bar.v_full(vlast.st), vlast.ph, p.status)) return;
@@ -591,6 +632,7 @@ __device__ void pf_softmax(const PrefillParams& p, const PfBars& bar, uint32_t t
       __syncwarp();
       if (lane == 0) mbar_arrive(bar.p_full(h));
     }
+    if (!active) continue;
     // epilogue: O_h / l for the valid rows
     if (!mbar_wait(bar.o_done(h), n_o & 1, p.status)) return;
     ++n_o;
@@ -611,10 +653,19 @@ __device__ void pf_softmax(const PrefillParams& p, const PfBars& bar, uint32_t t
         uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
 #pragma unroll
         for (int i = 0; i < 4; ++i) d4[i] = make_uint4(wv[4 * i], wv[4 * i + 1], wv[4 * i + 2], wv[4 * i + 3]);
+        const long long off = reinterpret_cast<char*>(dst + c * 32) - p.out;
+        for (int r = 0; r < p.n_peers; ++r) {
+          uint4* e4 = reinterpret_cast<uint4*>(p.peer_out[r] + off);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) e4[i] = make_uint4(wv[4 * i], wv[4 * i + 1], wv[4 * i + 2], wv[4 * i + 3]);
+        }
       }
     }
     tc_fence_before();
   }
+  // a gathered output: the rows stored to other GPUs are visible system-wide
+  // before this warp is done (the launch that signals the peers follows)
+  if (p.n_peers) __threadfence_system();
 }
 
 template <typename T, int D_>
@@ -646,6 +697,7 @@ __global__ void __launch_bounds__(PfCfg<D_>::THREADS, PfCfg<D_>::MINB)
       mbar_init(bar.q_full(s), 1);
       mbar_init(bar.q_empty(s), 1);
     }
+    for (int t = 0; t < 8; ++t) mbar_init(bar.turn(t >> 2, t & 3), 1);
     for (int s = 0; s < kPfItemRing; ++s) {
       mbar_init(bar.item_full(s), 1);
       mbar_init(bar.item_empty(s), 1 + 4 * C::NH_);  // the MMA warp and the softmax warps
@@ -704,13 +756,24 @@ static int launch_prefill(const PrefillParams& p, const CUtensorMap& tq, const C
 
 extern "C" int nf_prefill_tile_rows(int32_t head_dim) { return 128 * nf::pf_halves(head_dim); }
 
-extern "C" int nf_prefill_attention(void* out, int64_t out_row_stride, const void* q, int64_t q_row_stride,
-                                    int32_t num_rows, const void* k_pool, const void* v_pool, int32_t dtype, int32_t num_q_heads,
-                                    int32_t num_kv_heads, int32_t head_dim, int32_t block_size, int32_t num_blocks,
-                                    const int32_t* block_tables, int32_t max_blocks_per_seq, const int32_t* tiles,
-                                    int32_t n_tiles, const int32_t* order, int32_t* queue, float scale,
-                                    int32_t* status, void* stream) {
+extern "C" int nf_prefill_attention_gather(void* out, int64_t out_row_stride, const void* q, int64_t q_row_stride,
+                                           int32_t num_rows, const void* k_pool, const void* v_pool, int32_t dtype,
+                                           int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                                           int32_t block_size, int32_t num_blocks, const int32_t* block_tables,
+                                           int32_t max_blocks_per_seq, const int32_t* tiles, int32_t n_tiles,
+                                           const int32_t* order, int32_t* queue, float scale, const NfGather* gather,
+                                           int32_t* status, void* stream) {
   using namespace nf;
+  int n_peers = 0;
+  if (gather) {
+    if (gather->n_ranks < 1 || gather->n_ranks > kMaxRanks || gather->rank < 0 || gather->rank >= gather->n_ranks)
+      return fail(NF_EINVAL, "nf_prefill_attention: gathered output of %d ranks (1..%d), rank %d", gather->n_ranks,
+                  kMaxRanks, gather->rank);
+    n_peers = gather->n_ranks - 1;
+    for (int r = 0; r < n_peers; ++r)
+      if (!gather->peer_out[r] || (reinterpret_cast<uintptr_t>(gather->peer_out[r]) & 15))
+        return fail(NF_EINVAL, "nf_prefill_attention: peer_out[%d] is null or not 16-byte aligned", r);
+  }
   if (dtype != NF_BF16 && dtype != NF_F16)
     return fail(NF_EUNSUPPORTED, "nf_prefill_attention: 16-bit pools only (dtype %d)", dtype);
   if (head_dim != 64 && head_dim != 128)
@@ -758,6 +821,8 @@ extern "C" int nf_prefill_attention(void* out, int64_t out_row_stride, const voi
   p.queue = queue;
   p.scale_log2 = scale * 1.4426950408889634f;
   p.status = status;
+  p.n_peers = n_peers;
+  for (int r = 0; r < n_peers; ++r) p.peer_out[r] = static_cast<char*>(gather->peer_out[r]);
   const int n_items = n_tiles * num_kv_heads;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (dtype == NF_BF16)
@@ -765,4 +830,15 @@ extern "C" int nf_prefill_attention(void* out, int64_t out_row_stride, const voi
                           : launch_prefill<__nv_bfloat16, 128>(p, tq, tk, tv, n_items, st);
   return head_dim == 64 ? launch_prefill<__half, 64>(p, tq, tk, tv, n_items, st)
                         : launch_prefill<__half, 128>(p, tq, tk, tv, n_items, st);
+}
+
+extern "C" int nf_prefill_attention(void* out, int64_t out_row_stride, const void* q, int64_t q_row_stride,
+                                    int32_t num_rows, const void* k_pool, const void* v_pool, int32_t dtype,
+                                    int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
+                                    int32_t num_blocks, const int32_t* block_tables, int32_t max_blocks_per_seq,
+                                    const int32_t* tiles, int32_t n_tiles, const int32_t* order, int32_t* queue,
+                                    float scale, int32_t* status, void* stream) {
+  return nf_prefill_attention_gather(out, out_row_stride, q, q_row_stride, num_rows, k_pool, v_pool, dtype,
+                                     num_q_heads, num_kv_heads, head_dim, block_size, num_blocks, block_tables,
+                                     max_blocks_per_seq, tiles, n_tiles, order, queue, scale, nullptr, status, stream);
 }

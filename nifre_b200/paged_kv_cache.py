@@ -29,6 +29,7 @@ advances only when the last layer of a step has appended
 
 from __future__ import annotations
 
+import ctypes
 import math
 
 import numpy as np
@@ -161,6 +162,10 @@ class PagedKVCache:
         self.block_tables: list[BlockTable] = []
         self.prefix_cache: PrefixCache | None = None
         self._plan: StepPlan | None = None
+        self.steps_closed = 0  # forward passes whose last layer has appended
+        # KV heads sharded over several GPUs: a sharding.PeerExchange whose gathered buffers receive every
+        # rank's attention output (Attention.forward then returns the gathered rows); None on one GPU
+        self.exchange = None
 
     # ------------------------------------------------------------------ setup
     def init_batch(self, batch_size: int) -> None:
@@ -543,6 +548,7 @@ class PagedKVCache:
 
     def _close(self, plan: StepPlan) -> None:
         self.pos_host[plan.slots] = plan.ctx_before + plan.q_lens
+        self.steps_closed += 1
         plan.closed = True
         if self._plan is plan:
             self._plan = None
@@ -573,13 +579,16 @@ class PagedKVCache:
             self._close(plan)
 
     def attention_step(self, layer_id: int, q: torch.Tensor, plan: StepPlan, out: torch.Tensor,
-                       scale: float | None = None, events=None) -> torch.Tensor:
+                       scale: float | None = None, events=None, exchange=None) -> torch.Tensor:
         """out[row] = attention of q[row] over the cached keys of its sequence, for the step's rows.
 
         ``q``/``out``: (rows, Hq*D) in the pool dtype with unit column stride.
         Rows not in the step are left untouched.  ``events``: optional three
         CUDA events recorded before the prefill launch, between the prefill and
-        the split-K launches, and after them (kernel timing).
+        the split-K launches, and after them (kernel timing).  ``exchange``
+        (a ``sharding.PeerExchange``, with ``out`` one of its ``out`` views):
+        the kernels also store the rows into the other ranks' gathered
+        buffers and the launch ends once every rank's rows are in this one's.
         """
         _lib.require_cuda(q, "q")
         D = self.head_dim
@@ -600,15 +609,18 @@ class PagedKVCache:
             scale = 1.0 / math.sqrt(D)
         lib = _lib.load()
         stream = _lib.stream_handle(self.device)
+        gather = exchange.next(out) if exchange is not None else None
+        gref = ctypes.byref(gather) if gather is not None else None
         if events is not None:
             events[0].record()
         if plan.n_tiles:
-            _lib.check(lib.nf_prefill_attention(
+            _lib.check(lib.nf_prefill_attention_gather(
                 out.data_ptr(), out.stride(0), q.data_ptr(), q.stride(0), min(q.shape[0], out.shape[0]),
                 self.k[layer_id].data_ptr(), self.v[layer_id].data_ptr(), _lib.dtype_code(self.dtype),
                 hq, self.n_heads, D, self.block_size, self.num_blocks, self.bt_dev.data_ptr(),
                 self.max_blocks_per_seq, plan.tiles.data_ptr(), plan.n_tiles, plan.sched.data_ptr(),
-                self._pf_queue.data_ptr(), float(scale), self.status.data_ptr(), stream), "nf_prefill_attention")
+                self._pf_queue.data_ptr(), float(scale), gref, self.status.data_ptr(), stream),
+                "nf_prefill_attention")
         if events is not None:
             events[1].record()
         if plan.decode_units:
@@ -631,13 +643,15 @@ class PagedKVCache:
                     plan.max_units, plan.casc_tasks.data_ptr(),
                     plan.n_casc_tasks, plan.casc_toks.data_ptr(), plan.n_casc_toks, float(scale),
                     self.status.data_ptr(), stream), "nf_cascade_attention")
-            _lib.check(lib.nf_paged_attention(
+            _lib.check(lib.nf_paged_attention_gather(
                 out.data_ptr(), out.stride(0), q.data_ptr(), q.stride(0),
                 self.k[layer_id].data_ptr(), self.v[layer_id].data_ptr(), _lib.dtype_code(self.dtype),
                 hq, self.n_heads, D, self.block_size, self.num_blocks, self.bt_dev.data_ptr(),
                 self.max_blocks_per_seq, plan.items.data_ptr(), plan.units.data_ptr(), plan.counts.data_ptr(),
                 max_items, plan.max_units, plan.split, float(scale), ws.data_ptr(), ws.numel(),
-                cnt.data_ptr(), cnt.numel(), self.status.data_ptr(), stream), "nf_paged_attention")
+                cnt.data_ptr(), cnt.numel(), gref, self.status.data_ptr(), stream), "nf_paged_attention")
+        elif gather is not None:  # every row came from the prefill kernel: signal the peers on their own
+            _lib.check(lib.nf_exchange_barrier(gref, self.status.data_ptr(), stream), "nf_exchange_barrier")
         if events is not None:
             events[2].record()
         return out
