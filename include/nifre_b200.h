@@ -190,6 +190,28 @@ int nf_kv_append(void* k_pool, void* v_pool, int32_t pool_dtype, int64_t pool_ro
                  int32_t* status, void* stream);
 
 /*
+ * nf_qkv_append: the attention input projection fused with the KV append
+ * (replaces GptAttention.forward's three nn.Linear calls + the cache append,
+ * models/gpt.py:38-51 and paged_kv_cache.py:107-121).  For the `rows` rows
+ * of x (row r = token r of the step, whose pool row is slot_mapping[r]):
+ *   y = x W^T (+ bias), W = weight (n_q + 2 n_kv rows of k_dim elements, the
+ *   q, k and v projection weights stacked in nn.Linear layout),
+ *   q_out[r] = y[r, 0:n_q], k_pool[slot] = y[r, n_q:n_q+n_kv],
+ *   v_pool[slot] = y[r, n_q+n_kv:],
+ * on the tensor cores (tcgen05, fp32 accumulation, rounded once to the
+ * 16-bit dtype of x, weight, q_out and the pools).  n_q and n_kv multiples
+ * of 64, k_dim of 8; pools hold pool_rows rows of n_kv elements; slots
+ * outside them are skipped and flagged (NF_STATUS_BAD_SLOT).  If pos_out is
+ * not NULL, pos_out[slot] = ctx_before + q_len for each of the n_seqs step
+ * records of nf_pack_step (the last layer's append, paged_kv_cache.py:120-121).
+ */
+int nf_qkv_append(const void* x, int64_t x_row_stride, int32_t rows, const void* weight, const void* bias,
+                  int32_t k_dim, int32_t n_q, int32_t n_kv, void* q_out, int64_t q_out_row_stride,
+                  void* k_pool, void* v_pool, int64_t pool_rows, int32_t dtype,
+                  const int32_t* slot_mapping, const int32_t* seqs, int32_t n_seqs, int64_t* pos_out,
+                  int32_t* status, void* stream);
+
+/*
  * nf_attention_workspace: sizes of the caller-owned split-K workspace for
  * nf_paged_attention (float partials and int32 counters).  Counters must be
  * zeroed once when allocated; the kernel leaves them zero when it returns.

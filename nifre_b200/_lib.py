@@ -31,7 +31,7 @@ EXPORTS = ("nf_last_error", "nf_abi_version", "nf_pack_step", "nf_kv_append",
            "nf_attention_workspace", "nf_paged_attention", "nf_paged_attention_noalloc",
            "nf_last_attention_path", "nf_selftest_umma", "nf_prefill_attention", "nf_prefill_tile_rows",
            "nf_cascade_attention", "nf_selftest_wait", "nf_noalloc_scratch_fill", "nf_paged_attention_gather",
-           "nf_prefill_attention_gather", "nf_exchange_barrier", "nf_ipc_handle", "nf_ipc_open", "nf_ipc_close")
+           "nf_prefill_attention_gather", "nf_exchange_barrier", "nf_ipc_handle", "nf_ipc_open", "nf_ipc_close", "nf_qkv_append")
 
 _P = ctypes.c_void_p
 _I32 = ctypes.c_int32
@@ -76,6 +76,8 @@ _SIGNATURES = {
     "nf_prefill_attention_gather": ([_P, _I64, _P, _I64, _I32, _P, _P, _I32, _I32, _I32, _I32, _I32, _I32,
                                      _P, _I32, _P, _I32, _P, _P, ctypes.c_float, _G, _P, _P], ctypes.c_int),
     "nf_exchange_barrier": ([_G, _P, _P], ctypes.c_int),
+    "nf_qkv_append": ([_P, _I64, _I32, _P, _P, _I32, _I32, _I32, _P, _I64, _P, _P, _I64, _I32, _P, _P, _I32, _P,
+                       _P, _P], ctypes.c_int),
     "nf_ipc_handle": ([_P, _P, ctypes.POINTER(_I64)], ctypes.c_int),
     "nf_ipc_open": ([_P, _I64, ctypes.POINTER(_P)], ctypes.c_int),
     "nf_ipc_close": ([_P, _I64], ctypes.c_int),

@@ -117,8 +117,11 @@ def causal_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, head_dim
     """Causal attention over (B, T, H*D) tensors without a cache (attention.py:59-75).
 
     Row b of ``k``/``v`` is used in place as block b of a pool whose block
-    size is T, with the identity block table; every query i of row b is a
-    work item over keys [0, i].
+    size is T, with the identity block table.  16-bit tensors with head_dim
+    64 or 128 (and 1, 2, 4 or 8 query heads per KV head) go to the
+    tensor-core prefill kernel, every row one chunk at position 0; other
+    shapes to the split-K kernel, every query i of row b a work item over
+    keys [0, i].
     """
     _lib.require_cuda(q, "q")
     B, T, hqd = q.shape
@@ -128,6 +131,9 @@ def causal_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, head_dim
     q = q.contiguous()
     hkv = k.shape[-1] // head_dim
     hq = hqd // head_dim
+    if (dtype in (torch.bfloat16, torch.float16) and head_dim in (64, 128) and hkv > 0 and hq % hkv == 0
+            and hq // hkv in (1, 2, 4, 8)):
+        return _causal_tensor_core(q, k, v, head_dim, hq, hkv)
     dev = q.device
     n_tok = B * T
     split = 128 * max(1, math.ceil(T / 128))
@@ -156,4 +162,41 @@ def causal_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, head_dim
         hq, hkv, head_dim, T, B, bt.data_ptr(), 1, items.data_ptr(), units.data_ptr(), counts.data_ptr(),
         n_tok, max_units, split, 1.0 / math.sqrt(head_dim), ws.data_ptr(), ws.numel(), cnt.data_ptr(),
         cnt.numel(), status.data_ptr(), stream), "nf_paged_attention")
+    return out
+
+
+def _causal_tensor_core(q, k, v, head_dim, hq, hkv):
+    """The no-cache path on nf_prefill_attention: row b of k/v is block b of a pool whose block size is T
+    rounded up to 16 (zero-padded when T is not a multiple of 16; the padding keys lie past every query's
+    causal limit), and the row's queries are chunks at position 0."""
+    from nifre_b200.paged_kv_cache import _prefill_order
+
+    B, T, hqd = q.shape
+    dev = q.device
+    bs = (T + 15) // 16 * 16
+    if bs != T:
+        kp = torch.zeros(B, bs, hkv * head_dim, dtype=q.dtype, device=dev)
+        vp = torch.zeros_like(kp)
+        kp[:, :T] = k
+        vp[:, :T] = v
+    else:
+        kp, vp = k, v
+    lib = _lib.load()
+    tt = lib.nf_prefill_tile_rows(head_dim) // (hq // hkv)  # tokens per work item
+    t0 = np.arange(0, T, tt, dtype=np.int64)
+    b = np.repeat(np.arange(B, dtype=np.int64), len(t0))
+    t0 = np.tile(t0, B)
+    tiles = np.stack([b, b * T + t0, np.minimum(tt, T - t0), t0], axis=1)
+    order = _prefill_order([tuple(r) for r in tiles.tolist()], hkv)
+    meta = torch.from_numpy(np.concatenate([tiles.reshape(-1), order]).astype(np.int32)).to(dev)
+    bt = torch.arange(B, dtype=torch.int32, device=dev).view(B, 1)
+    queue = torch.zeros(2, dtype=torch.int32, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    out = torch.empty_like(q)
+    n_tiles = len(tiles)
+    _lib.check(lib.nf_prefill_attention(
+        out.data_ptr(), hqd, q.data_ptr(), hqd, B * T, kp.data_ptr(), vp.data_ptr(), _lib.dtype_code(q.dtype),
+        hq, hkv, head_dim, bs, B, bt.data_ptr(), 1, meta.data_ptr(), n_tiles, meta.data_ptr() + 16 * n_tiles,
+        queue.data_ptr(), 1.0 / math.sqrt(head_dim), status.data_ptr(), _lib.stream_handle(dev)),
+        "nf_prefill_attention")
     return out

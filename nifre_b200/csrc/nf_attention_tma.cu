@@ -446,6 +446,19 @@ bool encode_pool_map(CUtensorMap* map, const void* pool, int dtype, int D, int H
   return r == CUDA_SUCCESS;
 }
 
+bool encode_matrix_map(CUtensorMap* map, const void* base, int dtype, long long cols, long long rows,
+                       long long row_stride, int box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  const CUtensorMapDataType dt = dtype == NF_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)row_stride * 2};
+  cuuint32_t box[2] = {64, (cuuint32_t)box_rows}, es[2] = {1, 1};
+  const CUresult r = fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 bool encode_rows_map(CUtensorMap* map, const void* base, int dtype, int D, int H, long long rows, long long row_stride,
                      int g, int tt) {
   auto fn = encode_fn();

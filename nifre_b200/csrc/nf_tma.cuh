@@ -24,6 +24,15 @@ __device__ __forceinline__ uint64_t l2_evict_last() {
   return pol;
 }
 
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int c0, int c1, uint32_t bar,
+                                            uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, {%2, "
+      "%3}], [%4], %5;" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(bar), "l"(pol)
+      : "memory");
+}
+
 __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2, uint32_t bar,
                                             uint64_t pol) {
   asm volatile(
@@ -64,5 +73,11 @@ bool encode_pool_map(CUtensorMap* map, const void* pool, int dtype, int D, int H
 // major in (row, head)).
 bool encode_rows_map(CUtensorMap* map, const void* base, int dtype, int D, int H, long long rows, long long row_stride,
                      int g, int tt);
+
+// Tensor map over a row-major matrix of 16-bit elements (rows x cols, row
+// stride `row_stride` elements), 128-byte swizzle, box of 64 columns x
+// box_rows rows (one 128-byte row of the box per matrix row).
+bool encode_matrix_map(CUtensorMap* map, const void* base, int dtype, long long cols, long long rows,
+                       long long row_stride, int box_rows);
 
 }  // namespace nf

@@ -100,6 +100,9 @@ class GptAttention(nn.Module):
 
 
 class TransformerBlock(nn.Module):
+    # bf16/fp16 models project and append in one tensor-core kernel on the flat step path
+    fused_projection = True
+
     def __init__(self, cfg):
         super().__init__()
         self.att = GptAttention(cfg["emb_dim"], cfg["emb_dim"], cfg["num_heads"], dropout=cfg["drop_rate"],
@@ -118,10 +121,17 @@ class TransformerBlock(nn.Module):
         """One layer over a flat step of rows (T, E), inference only (no dropout); see GptModel.forward_step."""
         E = x.shape[1]
         w, b = self.att.qkv_params()
-        qkv = F.linear(self.norm1(x), w, b)
-        cache.append_step(layer_id, qkv[:, E:2 * E], qkv[:, 2 * E:], plan)
+        xn = self.norm1(x)
+        if self.fused_projection and cache.projection_fusable(xn, plan, E) and w.dtype == cache.dtype:
+            # 16-bit model: one tcgen05 kernel projects and scatters K/V into the pools (nf_qkv_append)
+            q = torch.empty(x.shape[0], E, device=x.device, dtype=x.dtype)
+            cache.project_append_step(layer_id, xn, w, b, plan, q)
+        else:
+            qkv = F.linear(xn, w, b)
+            cache.append_step(layer_id, qkv[:, E:2 * E], qkv[:, 2 * E:], plan)
+            q = qkv[:, :E]
         ctx = torch.empty(x.shape[0], E, device=x.device, dtype=x.dtype)
-        cache.attention_step(layer_id, qkv[:, :E], plan, ctx)
+        cache.attention_step(layer_id, q, plan, ctx)
         x = x + self.att.out_proj(ctx)
         return x + self.ff(self.norm2(x))
 

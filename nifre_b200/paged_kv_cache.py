@@ -578,6 +578,43 @@ class PagedKVCache:
         if last:
             self._close(plan)
 
+    def projection_fusable(self, x: torch.Tensor, plan: StepPlan, n_q: int) -> bool:
+        """True when ``project_append_step`` serves this step: 16-bit pools and x of the same dtype, the step's
+        rows laid out as its tokens in order (row t = token t), widths multiples of 64."""
+        return (self.dtype in (torch.bfloat16, torch.float16) and x.dtype == self.dtype and x.dim() == 2
+                and x.stride(1) == 1 and x.shape[0] == plan.n_tokens and plan.rows_needed == plan.n_tokens
+                and bool((plan.q_starts == np.cumsum(plan.q_lens) - plan.q_lens).all())
+                and n_q % 64 == 0 and (self.n_heads * self.head_dim) % 64 == 0 and x.shape[1] % 8 == 0)
+
+    def project_append_step(self, layer_id: int, x: torch.Tensor, weight: torch.Tensor, bias, plan: StepPlan,
+                            q_out: torch.Tensor) -> torch.Tensor:
+        """The input projection fused with the KV append for layer ``layer_id``: ``[q | k | v] = x weight^T
+        (+ bias)`` on the tensor cores, q into ``q_out`` (rows, n_q) and k/v straight into the pools
+        (``nf_qkv_append``).  ``weight``: (n_q + 2 Hkv*D, in_features), the q, k and v weights stacked.
+        Same plan bookkeeping as ``append_step`` (``pos`` advances after the last layer)."""
+        if plan.closed:
+            raise RuntimeError("step plan already closed")
+        if not 0 <= layer_id < self.num_layers:
+            raise IndexError(f"layer_id {layer_id} out of range [0, {self.num_layers})")
+        n_kv = self.n_heads * self.head_dim
+        n_q = q_out.shape[1]
+        if weight.shape != (n_q + 2 * n_kv, x.shape[1]) or not weight.is_contiguous() or weight.dtype != self.dtype:
+            raise ValueError(f"weight must be a contiguous ({n_q + 2 * n_kv}, {x.shape[1]}) {self.dtype} tensor")
+        if not self.projection_fusable(x, plan, n_q) or q_out.stride(1) != 1 or q_out.dtype != self.dtype:
+            raise ValueError("this step cannot use the fused projection (see projection_fusable)")
+        last = layer_id == self.num_layers - 1
+        lib = _lib.load()
+        _lib.check(lib.nf_qkv_append(
+            x.data_ptr(), x.stride(0), x.shape[0], weight.data_ptr(), bias.data_ptr() if bias is not None else None,
+            x.shape[1], n_q, n_kv, q_out.data_ptr(), q_out.stride(0), self.k[layer_id].data_ptr(),
+            self.v[layer_id].data_ptr(), self.num_blocks * self.block_size, _lib.dtype_code(self.dtype),
+            plan.slot_mapping.data_ptr(), plan.seqs.data_ptr(), plan.n_seqs,
+            self.pos.data_ptr() if last else None, self.status.data_ptr(), _lib.stream_handle(self.device)),
+            "nf_qkv_append")
+        if last:
+            self._close(plan)
+        return q_out
+
     def attention_step(self, layer_id: int, q: torch.Tensor, plan: StepPlan, out: torch.Tensor,
                        scale: float | None = None, events=None, exchange=None) -> torch.Tensor:
         """out[row] = attention of q[row] over the cached keys of its sequence, for the step's rows.

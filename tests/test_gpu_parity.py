@@ -261,6 +261,17 @@ def test_no_cache_causal_vs_oracle(dtype):
     torch.testing.assert_close(out.float().cpu(), ref, **_tol(dtype))
 
 
+@pytest.mark.parametrize("B,T,H,D", [(2, 300, 8, 64), (3, 64, 4, 128), (1, 1000, 2, 64), (2, 17, 16, 64)])
+def test_no_cache_causal_tensor_core_vs_oracle(B, T, H, D):
+    """The no-cache path on the tensor-core prefill kernel (T a multiple of 16 or padded to one)."""
+    from nifre_b200 import Attention
+    g = torch.Generator().manual_seed(B * T + D)
+    q, k, v = (torch.randn(B, T, H * D, generator=g).to(torch.bfloat16) for _ in range(3))
+    out = Attention(H, D)(q.to(DEV), k.to(DEV), v.to(DEV))
+    ref = full_causal(q.float(), k.float(), v.float(), H)
+    torch.testing.assert_close(out.float().cpu(), ref, rtol=2e-2, atol=2e-2)
+
+
 def test_errors_before_launch():
     from nifre_b200 import BlockPoolExhaustedError, PagedKVCache
     cache = PagedKVCache(1, 32, 2, 64, device=DEV, dtype=torch.bfloat16, block_size=16, num_blocks=2)
