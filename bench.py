@@ -77,6 +77,11 @@ WORKLOADS = {
                               dctx_lo=256, dctx_hi=2048, seqs=100, ctx_lo=256, ctx_hi=2048, cpu_sample=8,
                               metric="mixed prefill+decode step tok/s (1B shape, 16 layers, 4x512 chunks + 96 "
                                      "decodes)"),
+    # the 1B decode step's input projection fused with the KV append: 64 rows x d_model 2048 against the stacked
+    # q/k/v weights (3072 x 2048, bf16, a distinct weight per layer), k/v scattered into the paged pools
+    "llama3.2-1b-qkv": dict(kind="qkv", layers=16, resident=16, hq=32, hkv=8, d=64, bs=16, seqs=64, ctx_lo=512,
+                            ctx_hi=4096, seed=0, scaling="weak", steps=50, d_model=2048, cpu_sample=8,
+                            metric="fused qkv projection + kv append, rows/s (1B shape, 64 decode rows, 16 layers)"),
     # decode over shared prefixes on the 1B shape: 128 requests, each one of 4 common 1024-token
     # prefixes (64 shared blocks, imported through the prefix cache) + a unique U[64, 256] suffix
     "llama3.2-1b-prefix": dict(kind="prefix", layers=16, resident=16, hq=32, hkv=8, d=64, bs=16, seed=1,
@@ -96,7 +101,7 @@ METRIC = CFG["metric"]
 
 # sub-results of the default run: (workload, resident layers, timed steps)
 SUB_RESULTS = (("llama3-8b-long", 1, 12), ("llama3.2-1b-mixed", 16, 16), ("llama3.2-1b-prefix", 16, 20),
-               ("gpt124m-engine", 12, 130))
+               ("llama3.2-1b-qkv", 16, 30), ("gpt124m-engine", 12, 130))
 
 
 def _args():
@@ -1107,6 +1112,148 @@ def measure_mixed(steps, warmup, e2e_steps, world, rank, local, dev, dist):
     }
 
 
+# ---------------------------------------------------------------------------- fused projection + append
+def measure_qkv(steps, warmup, world, rank, local, dev, dist):
+    """The decode step's input projection fused with the KV append (nf_qkv_append), per layer, against the
+    same work as cuBLAS F.linear + nf_kv_append.  Each rank projects its shard's heads (q heads 32/N, KV heads
+    8/N) of the full d_model rows.  Returns the JSON line's fields."""
+    import torch.nn.functional as F
+
+    from nifre_b200 import PagedKVCache
+    from nifre_b200.sharding import HeadShard
+
+    shard = HeadShard(world, rank, CFG["hq"], CFG["hkv"], CFG["d"])
+    hkv, hq = shard.kv_heads, shard.q_heads
+    L, D, bs, E = CFG["resident"], CFG["d"], CFG["bs"], CFG["d_model"]
+    B = CFG["seqs"] * world if CFG["scaling"] == "weak" else CFG["seqs"]
+    ctx = _ctx_lens(B, CFG["seed"])
+    total = 2 * (warmup + steps) + 8
+    dt = torch.bfloat16
+    n_blocks = sum((c + total + bs - 1) // bs for c in ctx)
+    cache = PagedKVCache(L, max(ctx) + total + 16, hkv, D, device=dev, dtype=dt, block_size=bs,
+                         enable_prefix_cache=False, num_blocks=n_blocks)
+    cache.init_batch(B)
+    g = torch.Generator().manual_seed(CFG["seed"])
+    cache.block_allocator.set_free_order(torch.randperm(cache.num_blocks, generator=g).tolist())
+    for s_ in range(B):  # contexts allocated (their contents play no part here)
+        cache.block_tables[s_].ensure_capacity(ctx[s_])
+        cache._set_pos(s_, ctx[s_])
+    gd = torch.Generator(device=dev).manual_seed(CFG["seed"] + rank)
+    nq, nkv = hq * D, hkv * D
+    x = torch.randn(L, B, E, device=dev, dtype=dt, generator=gd)
+    w = torch.randn(L, nq + 2 * nkv, E, device=dev, dtype=dt, generator=gd) / math.sqrt(E)
+    q = torch.empty(L, B, nq, device=dev, dtype=dt)
+    slots, ones, rows = list(range(B)), [1] * B, list(range(B))
+    stream = torch.cuda.current_stream(dev)
+
+    def step(fused, rec=None):
+        p = cache.plan(slots, ones, rows)
+        for layer in range(L):
+            if rec is not None and layer == rec[0]:
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+            if fused:
+                cache.project_append_step(layer, x[layer], w[layer], None, p, q[layer])
+            else:
+                y = F.linear(x[layer], w[layer])
+                cache.append_step(layer, y[:, nq:nq + nkv], y[:, nq + nkv:], p)
+                q[layer].copy_(y[:, :nq])
+            if rec is not None and layer == rec[0]:
+                e1.record(stream)
+                rec[1].append((e0, e1))
+
+    # kernel time without the host: the 16 layers' launches captured in a CUDA graph (one plan's slots reused,
+    # pos untouched) and replayed back to back
+    from nifre_b200 import _lib
+    lib = _lib.load()
+    p0 = cache.plan(slots, ones, rows)
+
+    def layers_raw(fused):
+        for layer in range(L):
+            if fused:
+                _lib.check(lib.nf_qkv_append(
+                    x[layer].data_ptr(), E, B, w[layer].data_ptr(), None, E, nq, nkv, q[layer].data_ptr(), nq,
+                    cache.k[layer].data_ptr(), cache.v[layer].data_ptr(), cache.num_blocks * bs, _lib.NF_BF16,
+                    p0.slot_mapping.data_ptr(), None, 0, None, cache.status.data_ptr(), _lib.stream_handle(dev)),
+                    "nf_qkv_append")
+            else:
+                y = F.linear(x[layer], w[layer])
+                _lib.check(lib.nf_kv_append(
+                    cache.k[layer].data_ptr(), cache.v[layer].data_ptr(), _lib.NF_BF16, cache.num_blocks * bs,
+                    y[:, nq:].data_ptr(), y[:, nq + nkv:].data_ptr(), _lib.NF_BF16, y.stride(0), y.stride(0),
+                    p0.slot_mapping.data_ptr(), p0.src_rows.data_ptr(), B, hkv, D, p0.seqs.data_ptr(), B, None,
+                    cache.status.data_ptr(), _lib.stream_handle(dev)), "nf_kv_append")
+                q[layer].copy_(y[:, :nq])
+
+    kern_us = {}
+    for fused in (False, True):
+        layers_raw(fused)  # warm (cuBLAS handles, function attributes)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            layers_raw(fused)
+        for _ in range(3):
+            graph.replay()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(20):
+            graph.replay()
+        b.record(stream)
+        torch.cuda.synchronize()
+        kern_us[fused] = _max_over_ranks(a.elapsed_time(b), dev, dist) * 1e3 / (20 * L)
+        del graph
+    cache._close(p0)
+
+    res = {}
+    for fused in (False, True):
+        for _ in range(warmup):
+            step(fused)
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+        ev = []
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for s_ in range(steps):
+            step(fused, (s_ % L, ev))
+        b.record(stream)
+        torch.cuda.synchronize()
+        res[fused] = (_max_over_ranks(a.elapsed_time(b), dev, dist),
+                      _max_over_ranks(sum(x_.elapsed_time(y_) for x_, y_ in ev) / len(ev), dev, dist))
+    cache.check_status()
+    # parity of the fused output of the last step's last layer against float32
+    ref = x[L - 1].float() @ w[L - 1].float().T
+    err = float((q[L - 1].float() - ref[:, :nq]).abs().max())
+    ok = bool(torch.allclose(q[L - 1].float(), ref[:, :nq], rtol=1e-2, atol=1e-2))
+    ms_f, lay_f = res[True]
+    ms_u, lay_u = res[False]
+    bytes_layer = (nq + 2 * nkv) * E * 2 + B * E * 2 + B * (nq + 2 * nkv) * 2 + 8 * B
+    peak, peak_kind = _peaks()
+    del cache
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    return {
+        "metric": CFG["metric"], "value": B * steps / (ms_f * 1e-3), "unit": "rows/s", "n_gpus": world,
+        "steps": steps, "warmup": warmup, "ms_per_step": ms_f / steps, "higher_is_better": True,
+        "scaling": CFG["scaling"], "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1))",
+        "config": {"workload": CFG["name"], "layers": L, "rows": B, "d_model": E, "q_heads": CFG["hq"],
+                   "kv_heads": CFG["hkv"], "head_dim": D, "weight_shape": [nq + 2 * nkv, E],
+                   "l2": "a distinct 12.6 MB weight per layer (201 MB over 16 layers): larger than L2",
+                   "method": "value: steps through PagedKVCache.plan + project_append_step per layer (host "
+                             "included); roofline: kernel time from CUDA-graph replays of the 16 launches",
+                   "baseline_path": "torch F.linear (cuBLAS) + nf_kv_append + the q copy",
+                   "baseline_ms_per_step": ms_u / steps, "baseline_api_us_per_layer": lay_u * 1e3,
+                   "baseline_kernels_us_per_layer": kern_us[False], "fused_api_us_per_layer": lay_f * 1e3},
+        "roofline": {"bound": "hbm", "achieved": bytes_layer / (kern_us[True] * 1e-6) / 1e9, "peak": peak,
+                     "unit": "GB/s", "frac": bytes_layer / (kern_us[True] * 1e-6) / 1e9 / peak, "traffic": None,
+                     "kernel": "nf_qkv_append", "peak_source": peak_kind, "avg_launch_us": kern_us[True],
+                     "bytes_per_launch": bytes_layer, "bytes": "weights + x rows + q/k/v outputs + slots"},
+        "parity": {"max_abs_err": err, "within_tol": ok, "against": "float32 x W^T", "tol": "rtol 1e-2, atol 1e-2"},
+        "gpu_launches": steps * (1 + L),
+    }
+
+
 # ---------------------------------------------------------------------------- arms
 def _sub_result(line: dict) -> dict:
     keep = ("metric", "value", "unit", "ms_per_step", "steps", "warmup", "dtype", "config", "roofline",
@@ -1121,6 +1268,8 @@ def run_ours(args):
     args.no_cpu_baseline = args.no_cpu_baseline or world > 1
     if kind == "engine":
         line = measure_engine(args, world, rank, local, dev, dist)
+    elif kind == "qkv":
+        line = measure_qkv(args.steps, args.warmup, world, rank, local, dev, dist)
     elif kind == "mixed":
         line = measure_mixed(args.steps, args.warmup, args.e2e_steps, world, rank, local, dev, dist)
         if rank == 0 and not args.no_cpu_baseline:
@@ -1139,6 +1288,8 @@ def run_ours(args):
                     sub = measure_engine(argparse.Namespace(steps=steps, warmup=2,
                                                             no_cpu_baseline=args.no_cpu_baseline),
                                          world, rank, local, dev, dist)
+                elif sub_kind == "qkv":
+                    sub = measure_qkv(steps, 3, world, rank, local, dev, dist)
                 elif sub_kind == "mixed":
                     sub = measure_mixed(steps, 3, 0, world, rank, local, dev, dist)
                     if rank == 0 and not args.no_cpu_baseline:
@@ -1156,6 +1307,59 @@ def run_ours(args):
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def _reference_qkv(args, world, threads, use_ref):
+    """The projection + append on the host cores: the three nn.Linear projections of the reference's
+    GptAttention (models/gpt.py:38-51, torch's CPU GEMM) and its PagedKVCache.append of the new k/v rows
+    (paged_kv_cache.py:107-121, the reference's own code when installed), one layer per call."""
+    torch.set_num_threads(threads)
+    Hq, Hkv, D, E, B = CFG["hq"], CFG["hkv"], CFG["d"], CFG["d_model"], CFG["seqs"]
+    g = torch.Generator().manual_seed(1)
+    x = torch.randn(B, E, generator=g).to(torch.bfloat16)
+    wq = (torch.randn(Hq * D, E, generator=g) / math.sqrt(E)).to(torch.bfloat16)
+    wk = (torch.randn(Hkv * D, E, generator=g) / math.sqrt(E)).to(torch.bfloat16)
+    wv = (torch.randn(Hkv * D, E, generator=g) / math.sqrt(E)).to(torch.bfloat16)
+    ctx = _ctx_lens(B, CFG["seed"])
+    if use_ref:
+        _, RefCache = _reference_modules()
+        cache = RefCache(2, max(ctx) + args.steps + args.warmup + 8, Hkv, D, device="cpu", dtype=torch.bfloat16,
+                         block_size=CFG["bs"], enable_prefix_cache=False)
+        cache.init_batch(B)
+        for s_ in range(B):
+            cache.block_tables[s_].ensure_capacity(ctx[s_])
+            cache.pos[s_] = ctx[s_]
+        kind = "reference"
+    else:
+        from oracle.paged import OracleStore
+        cache = OracleStore(2, max(ctx) + args.steps + args.warmup + 8, Hkv, D, batch_size=B, dtype=torch.bfloat16,
+                            block_size=CFG["bs"], prefix=False)
+        for s_ in range(B):
+            cache.tables[s_].ensure(ctx[s_])
+            cache.pos[s_] = ctx[s_]
+        kind = "port"
+    F = torch.nn.functional
+
+    def layer():
+        t0 = time.perf_counter()
+        with torch.no_grad():
+            qq, kk, vv = F.linear(x, wq), F.linear(x, wk), F.linear(x, wv)
+            for s_ in range(B):  # layer 0 of 2: pos held
+                cache.append(s_, 0, kk[s_].view(1, Hkv, D), vv[s_].view(1, Hkv, D))
+        return time.perf_counter() - t0
+
+    for _ in range(args.warmup):
+        layer()
+    times = [layer() for _ in range(args.steps)]
+    v = B / (CFG["layers"] * sum(times) / len(times))  # rows of 16-layer steps per second
+    base = {"value": v, "unit": "rows/s", "cores": torch.get_num_threads(), "host_cpus": os.cpu_count(), "kind": kind,
+            "sample": f"the {B} rows of one layer x {len(times)} calls in {sum(times):.1f} s, scaled to "
+                      f"{CFG['layers']} layers; each step = one call"}
+    return {"impl": "reference", "metric": METRIC, "value": v, "unit": "rows/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "higher_is_better": True, "scaling": CFG["scaling"], "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic", "config": {"workload": CFG["name"], "d_model": E, "rows": B},
+            "cpu_baseline": base, "e2e": {"value": v, "unit": "rows/s", "h2d_bytes_per_step": 0,
+                                          "d2h_bytes_per_step": 0}}
 
 
 def run_reference(args):
@@ -1179,6 +1383,10 @@ def run_reference(args):
         print(json.dumps(line), flush=True)
         return
     use_ref = _reference_modules() is not None
+    if CFG.get("kind") == "qkv":
+        line = _reference_qkv(args, world, threads, use_ref)
+        print(json.dumps(line), flush=True)
+        return
     if CFG.get("kind") == "mixed":
         cpu = (CpuReferenceMixed if use_ref else CpuOracleMixed)(threads=threads)
         for _ in range(args.warmup):

@@ -9,13 +9,14 @@
 // pool rows through the step's slot mapping -- so new keys and values never
 // make a round trip through HBM between the projection and the append.
 //
-// One CTA per 128-row x 64-column output tile: a producer warp streams 64-wide
-// K slices of the x tile and the weight tile into a 6-stage ring by TMA
-// (128-byte swizzle), one elected lane of the MMA warp issues
-// tcgen05.mma kind::f16 (M = 128, N = 64, K = 16, fp32 accumulator in
+// One CTA per 128-row x BN-column output tile (BN = 64, or 32 for steps with
+// few rows so that more SMs stream the weights): a producer warp streams
+// 64-wide K slices of the x tile and the weight tile into a 6-stage ring by
+// TMA (128-byte swizzle), one elected lane of the MMA warp issues
+// tcgen05.mma kind::f16 (M = 128, N = BN, K = 16, fp32 accumulator in
 // tensor memory) and releases each stage with a commit, and four epilogue
 // warps (thread = row) read the accumulator, add the bias, round to the
-// output type and store 128 bytes per row.  Every wait is time-limited.
+// output type and store 2*BN bytes per row.  Every wait is time-limited.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -43,14 +44,23 @@ struct QkvParams {
   int* status;
 };
 
-constexpr int kQkvBM = 128, kQkvBN = 64, kQkvStages = 6;
-constexpr uint32_t kQkvA = kQkvBM * 128, kQkvB = kQkvBN * 128;  // bytes of one 64-wide K slice of each operand
-constexpr uint32_t kQkvStage = kQkvA + kQkvB;
-constexpr uint32_t kQkvSmem = 1024 + kQkvStages * kQkvStage + 1024;  // header + ring + alignment slack
+// Output tiles are 128 rows x BN columns (BN = 64, or 32 when 64-wide tiles
+// would leave SMs idle: a decode step has few rows, and the weights are the
+// bytes to stream).
+constexpr int kQkvBM = 128, kQkvStages = 6;
+constexpr uint32_t kQkvA = kQkvBM * 128;  // bytes of one 64-wide K slice of the x tile
+template <int BN>
+struct QkvCfg {
+  static constexpr uint32_t B = BN * 128;  // one 64-wide K slice of the weight tile
+  static constexpr uint32_t STAGE = kQkvA + B;
+  static constexpr uint32_t SMEM = 1024 + kQkvStages * STAGE + 1024;  // header + ring + alignment slack
+};
 
-template <typename T>
+template <typename T, int BN>
 __global__ void __launch_bounds__(192, 1)
     qkv_append_kernel(const QkvParams p, const __grid_constant__ CUtensorMap tx, const __grid_constant__ CUtensorMap tw) {
+  constexpr uint32_t kQkvStage = QkvCfg<BN>::STAGE;
+  constexpr int kQkvBN = BN;
   extern __shared__ unsigned char smem_raw[];
   unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t hdr = smem_u32(base);
@@ -69,7 +79,7 @@ __global__ void __launch_bounds__(192, 1)
     mbar_init(acc_done, 1);
     fence_mbar_init();
   }
-  if (warp == 1) tmem_alloc(tmem_slot, 64);
+  if (warp == 1) tmem_alloc(tmem_slot, 64);  // >= BN fp32 columns (allocations are powers of two >= 32)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -118,14 +128,15 @@ __global__ void __launch_bounds__(192, 1)
     const int r = m0 + quad * 32 + lane;
     const bool ok = mbar_wait(acc_done, 0, p.status);
     tc_fence_after();
-    uint32_t a[2][32];
+    constexpr int NC = BN / 32;  // 32-column tensor-memory loads
+    uint32_t a[NC][32];
     if (ok) {
       const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16);
-      tmem_ld32(taddr, a[0]);
-      tmem_ld32(taddr + 32, a[1]);
+#pragma unroll
+      for (int c = 0; c < NC; ++c) tmem_ld32(taddr + 32 * c, a[c]);
       tmem_wait_ld();
-      tmem_reg_fence(a[0]);
-      tmem_reg_fence(a[1]);
+#pragma unroll
+      for (int c = 0; c < NC; ++c) tmem_reg_fence(a[c]);
     }
     if (ok && r < p.rows) {
       T* dst = nullptr;
@@ -143,9 +154,9 @@ __global__ void __launch_bounds__(192, 1)
       }
       if (dst) {
         const T* b = reinterpret_cast<const T*>(p.bias);
-        uint32_t wv[32];
+        uint32_t wv[BN / 2];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
+        for (int i = 0; i < BN / 2; ++i) {
           const int c = 2 * i;
           float v0 = __uint_as_float(a[c >> 5][c & 31]), v1 = __uint_as_float(a[(c + 1) >> 5][(c + 1) & 31]);
           if (b) {
@@ -156,7 +167,7 @@ __global__ void __launch_bounds__(192, 1)
         }
         uint4* d4 = reinterpret_cast<uint4*>(dst);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) d4[i] = make_uint4(wv[4 * i], wv[4 * i + 1], wv[4 * i + 2], wv[4 * i + 3]);
+        for (int i = 0; i < BN / 8; ++i) d4[i] = make_uint4(wv[4 * i], wv[4 * i + 1], wv[4 * i + 2], wv[4 * i + 3]);
       }
     }
     // the reference advances pos when the last layer appends (paged_kv_cache.py:120-121)
@@ -184,8 +195,8 @@ extern "C" int nf_qkv_append(const void* x, int64_t x_row_stride, int32_t rows, 
     return fail(NF_EUNSUPPORTED, "nf_qkv_append: 16-bit operands only (dtype %d)", dtype);
   if (rows < 0 || k_dim <= 0 || n_q <= 0 || n_kv <= 0 || pool_rows <= 0 || n_seqs < 0)
     return fail(NF_EINVAL, "nf_qkv_append: sizes must be positive");
-  if (n_q % kQkvBN || n_kv % kQkvBN)
-    return fail(NF_EUNSUPPORTED, "nf_qkv_append: q and k/v widths (%d, %d) must be multiples of %d", n_q, n_kv, kQkvBN);
+  if (n_q % 64 || n_kv % 64)
+    return fail(NF_EUNSUPPORTED, "nf_qkv_append: q and k/v widths (%d, %d) must be multiples of 64", n_q, n_kv);
   if (k_dim % 8) return fail(NF_EUNSUPPORTED, "nf_qkv_append: in_features %d is not a multiple of 8", k_dim);
   if (!x || !weight || !q_out || !k_pool || !v_pool || !slot_mapping || !status || (pos_out && !seqs))
     return fail(NF_EINVAL, "nf_qkv_append: null pointer argument");
@@ -212,15 +223,19 @@ extern "C" int nf_qkv_append(const void* x, int64_t x_row_stride, int32_t rows, 
   p.pos_out = reinterpret_cast<long long*>(pos_out);
   p.status = status;
   if (rows == 0) return ok();
-  CUtensorMap tx, tw;
   const long long n_all = (long long)n_q + 2LL * n_kv;
+  const long long row_tiles = (rows + kQkvBM - 1) / kQkvBM;
+  const int bn = row_tiles * (n_all / 64) < sm_count() ? 32 : 64;
+  CUtensorMap tx, tw;
   if (!encode_matrix_map(&tx, x, dtype, k_dim, rows, x_row_stride, kQkvBM) ||
-      !encode_matrix_map(&tw, weight, dtype, k_dim, n_all, k_dim, kQkvBN))
+      !encode_matrix_map(&tw, weight, dtype, k_dim, n_all, k_dim, bn))
     return fail(NF_ECUDA, "nf_qkv_append: tensor map encoding failed");
-  auto kern = dtype == NF_BF16 ? qkv_append_kernel<__nv_bfloat16> : qkv_append_kernel<__half>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kQkvSmem);
+  auto kern = dtype == NF_BF16 ? (bn == 32 ? qkv_append_kernel<__nv_bfloat16, 32> : qkv_append_kernel<__nv_bfloat16, 64>)
+                               : (bn == 32 ? qkv_append_kernel<__half, 32> : qkv_append_kernel<__half, 64>);
+  const int smem = bn == 32 ? (int)QkvCfg<32>::SMEM : (int)QkvCfg<64>::SMEM;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return fail(NF_ECUDA, "nf_qkv_append: smem attribute: %s", cudaGetErrorString(e));
-  const dim3 grid((unsigned)((rows + kQkvBM - 1) / kQkvBM), (unsigned)(n_all / kQkvBN));
-  kern<<<grid, 192, kQkvSmem, st>>>(p, tx, tw);
+  const dim3 grid((unsigned)row_tiles, (unsigned)(n_all / bn));
+  kern<<<grid, 192, smem, st>>>(p, tx, tw);
   return check_launch("nf_qkv_append");
 }
