@@ -828,52 +828,92 @@ def _run_decode_timed(steps, warmup, e2e_steps, cache, B, ctx, world, rank, loca
     worst = _max_over_ranks(worst, dev, dist)
     ok = _max_over_ranks(0.0 if ok else 1.0, dev, dist) == 0.0
 
-    # e2e through the public drop-in API with host buffers
+    # e2e through the public drop-in API with host buffers: every step uploads its q/k/v from pinned host
+    # memory (one copy per tensor, all layers) and downloads its attention outputs (one copy); uploads and
+    # downloads run on their own copy streams into double-buffered device tensors, so a step's copies overlap
+    # the neighbouring steps' kernels, as a serving loop that prefetches its next batch does
     e2e = None
     if e2e_steps > 1:
         attn = Attention(hq, D)
+        W = world * hq * D
         hq_host = torch.empty(L, B, 1, hq * D, dtype=dt).pin_memory()
         hk_host = torch.empty(L, B, 1, hkv * D, dtype=dt).pin_memory()
         hv_host = torch.empty_like(hk_host).pin_memory()
-        ho_host = torch.empty(L, B, 1, world * hq * D, dtype=dt).pin_memory()
+        ho_host = torch.empty(L, B, 1, W, dtype=dt).pin_memory()
         hq_host.copy_(q_all.view(L, B, 1, -1).cpu())
         hk_host.copy_(k_all.view(L, B, 1, -1).cpu())
         hv_host.copy_(v_all.view(L, B, 1, -1).cpu())
+        dev_in = [(torch.empty(L, B, 1, hq * D, device=dev, dtype=dt), torch.empty(L, B, 1, hkv * D, device=dev,
+                   dtype=dt), torch.empty(L, B, 1, hkv * D, device=dev, dtype=dt)) for _ in range(2)]
+        dev_out = [torch.empty(L, B, 1, W, device=dev, dtype=dt) for _ in range(2)]
+        up, down = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+        ev = lambda: torch.cuda.Event()  # noqa: E731
+        consumed = [None, None]  # compute finished reading buffer i (its inputs may be overwritten)
+        produced = [None, None]  # compute finished writing buffer i's outputs
+        drained = [None, None]   # buffer i's outputs are on the host
+        uploaded = [None, None]
 
-        def e2e_step():
-            # the step's inputs go up in one copy per tensor, its outputs come
-            # down in one copy: each layer runs through Attention.forward
-            qd_all = hq_host.to(dev, non_blocking=True)
-            kd_all = hk_host.to(dev, non_blocking=True)
-            vd_all = hv_host.to(dev, non_blocking=True)
+        def upload(i):
+            with torch.cuda.stream(up):
+                if consumed[i] is not None:
+                    up.wait_event(consumed[i])
+                for d_, h_ in zip(dev_in[i], (hq_host, hk_host, hv_host)):
+                    d_.copy_(h_, non_blocking=True)
+                uploaded[i] = ev()
+                uploaded[i].record(up)
+
+        def compute(i):
+            stream.wait_event(uploaded[i])
+            if drained[i] is not None:
+                stream.wait_event(drained[i])
+            qd, kd, vd = dev_in[i]
             outs = []
             for layer in range(L):
                 # with N > 1 the cache's exchange makes this the gathered output of every rank's heads
-                o = attn(qd_all[layer], kd_all[layer], vd_all[layer], kv_cache=cache, layer_id=layer,
-                         cache_batch_indices=slots)
-                outs.append(o)
-            ho_host.copy_(torch.stack(outs), non_blocking=True)
+                outs.append(attn(qd[layer], kd[layer], vd[layer], kv_cache=cache, layer_id=layer,
+                                 cache_batch_indices=slots))
+            torch.stack(outs, out=dev_out[i])
+            consumed[i] = ev()
+            consumed[i].record(stream)
+            produced[i] = consumed[i]
 
-        e2e_step()
+        def download(i):
+            with torch.cuda.stream(down):
+                down.wait_event(produced[i])
+                ho_host.copy_(dev_out[i], non_blocking=True)
+                drained[i] = ev()
+                drained[i].record(down)
+
+        def run(n):
+            upload(0)
+            for j in range(n):
+                if j + 1 < n:
+                    upload((j + 1) % 2)
+                compute(j % 2)
+                download(j % 2)
+            stream.wait_event(drained[(n - 1) % 2])
+
+        run(2)
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
         a = torch.cuda.Event(enable_timing=True)
         b = torch.cuda.Event(enable_timing=True)
         a.record(stream)
-        for _ in range(e2e_steps - 1):
-            e2e_step()
+        up.wait_event(a)
+        n_e2e = e2e_steps - 1
+        run(n_e2e)
         b.record(stream)
         torch.cuda.synchronize()
         ems = _max_over_ranks(a.elapsed_time(b), dev, dist)
         cache.check_status()
-        n_e2e = e2e_steps - 1
         e2e = {"value": B * n_e2e / (ems * 1e-3) * L / L_model, "unit": "tok/s",
                "h2d_bytes_per_step": L * B * (hq + 2 * hkv) * D * 2,
-               "d2h_bytes_per_step": L * B * world * hq * D * 2,
+               "d2h_bytes_per_step": L * B * W * 2,
                "ms_per_step": ems / n_e2e * L_model / L,
-               "path": "nifre_b200.Attention.forward per layer; the step's q/k/v copied up from pinned host memory "
-                       "in one copy per tensor, its outputs copied down in one"}
+               "path": "nifre_b200.Attention.forward per layer; every step's q/k/v copied up from pinned host memory "
+                       "(one copy per tensor) and its outputs copied down (one copy) on copy streams, double-buffered "
+                       "so that copies overlap the neighbouring steps' kernels; all copies inside the timed region"}
 
     return {
         "metric": CFG["metric"], "value": B * steps / (ms * 1e-3) * L / L_model, "unit": "tok/s",

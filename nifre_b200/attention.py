@@ -72,12 +72,16 @@ class Attention(nn.Module):
             slots = tuple(cache_batch_indices)  # compared as given; made ints below when a plan is built
         if input_lens is not None and T > 1:
             lens = input_lens.tolist() if torch.is_tensor(input_lens) else [int(x) for x in input_lens]
-        else:
-            lens = [T] * B
-        key = (slots, tuple(lens), T)
+            lens_key = tuple(lens)
+            padded = any(n != T for n in lens)
+        else:  # every row has T new tokens
+            lens, lens_key, padded = None, None, False
+        key = (slots, lens_key, T, B)
         plan = cache._plan
         if plan is None or plan.key != key or plan.closed:
             slots = [int(s) for s in slots]
+            if lens is None:
+                lens = [T] * B
             starts = [i * T + (T - n) for i, n in enumerate(lens)]
             plan = cache.plan(slots, lens, starts, q_heads=self.num_heads)
             plan.key = key
@@ -90,8 +94,7 @@ class Attention(nn.Module):
             v2 = v2.contiguous()
         qk = q2 if q2.stride(1) == 1 else q2.contiguous()
         # padding rows of a left-padded prefill stay zero (attention.py:79); without padding every row is written
-        padded = T > 1 and any(n != T for n in lens)
-        ex = getattr(cache, "exchange", None)
+        ex = cache.exchange
         if ex is not None:
             # KV heads sharded over the ranks of a PeerExchange: the kernels write this rank's heads into every
             # rank's gathered buffer; the result is the gathered output of all heads

@@ -716,11 +716,9 @@ static int make_plan(int dtype, int Hq, int Hkv, int D, bool q_smem_ok, Plan& pl
 template <typename T, int D_, int MT, bool MMA, int DPL>
 static int launch_attn(const AttnParams& p, const Plan& pl, long long want, cudaStream_t st) {
   auto kern = paged_attention_kernel<T, D_, MT, MMA, DPL>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, pl.smem);
-  if (e != cudaSuccess) return fail(NF_ECUDA, "nf_paged_attention: smem attribute: %s", cudaGetErrorString(e));
   int per_sm = 1;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, pl.W * 32, pl.smem) != cudaSuccess || per_sm < 1)
-    per_sm = 1;
+  cudaError_t e = prepare_launch(reinterpret_cast<const void*>(kern), pl.smem, pl.W * 32, &per_sm);
+  if (e != cudaSuccess) return fail(NF_ECUDA, "nf_paged_attention: smem attribute: %s", cudaGetErrorString(e));
   long long grid = (long long)sm_count() * per_sm;
   const long long need = (want + pl.W - 1) / pl.W;  // no more warps than work items
   if (need < grid) grid = need;

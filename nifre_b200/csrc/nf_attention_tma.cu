@@ -28,6 +28,8 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <mutex>
+
 #include "nf_attn_common.cuh"
 #include "nf_internal.h"
 #include "nf_tma.cuh"
@@ -401,8 +403,45 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-bool encode_pool_map(CUtensorMap* map, const void* pool, int dtype, int D, int Hkv, int bs, int num_blocks,
-                            int hg, bool permuted) {
+static bool encode_pool_map_uncached(CUtensorMap* map, const void* pool, int dtype, int D, int Hkv, int bs,
+                                     int num_blocks, int hg, bool permuted);
+
+// Pool maps depend only on the pool's address and shape: the last ones
+// encoded are kept (a step reuses every layer's maps), so a launch encodes
+// none in the steady state.  Keyed by everything the map encodes.
+bool encode_pool_map(CUtensorMap* map, const void* pool, int dtype, int D, int Hkv, int bs, int num_blocks, int hg,
+                     bool permuted) {
+  struct Entry {
+    const void* pool;
+    int dtype, D, Hkv, bs, num_blocks, hg, permuted;
+    bool ok;
+    CUtensorMap map;
+  };
+  static Entry table[96];
+  static int n = 0, next = 0;
+  static std::mutex mu;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    for (int i = 0; i < n; ++i) {
+      const Entry& t = table[i];
+      if (t.pool == pool && t.dtype == dtype && t.D == D && t.Hkv == Hkv && t.bs == bs && t.num_blocks == num_blocks &&
+          t.hg == hg && t.permuted == (int)permuted) {
+        *map = t.map;
+        return t.ok;
+      }
+    }
+  }
+  const bool ok = encode_pool_map_uncached(map, pool, dtype, D, Hkv, bs, num_blocks, hg, permuted);
+  std::lock_guard<std::mutex> lock(mu);
+  Entry& t = table[next];
+  t = Entry{pool, dtype, D, Hkv, bs, num_blocks, hg, (int)permuted, ok, *map};
+  next = (next + 1) % 96;
+  if (n < 96) ++n;
+  return ok;
+}
+
+static bool encode_pool_map_uncached(CUtensorMap* map, const void* pool, int dtype, int D, int Hkv, int bs,
+                                     int num_blocks, int hg, bool permuted) {
   auto fn = encode_fn();
   if (!fn) return false;
   const CUtensorMapDataType dt = dtype == NF_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
@@ -535,12 +574,10 @@ int launch_attention_tma(AttnParams p, int dtype, long long want, cudaStream_t s
                                               : paged_attention_tma_kernel<__nv_bfloat16, 128>)
                                  : (p.D == 64 ? paged_attention_tma_kernel<__half, 64>
                                               : paged_attention_tma_kernel<__half, 128>);
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  if (e != cudaSuccess) return fail(NF_ECUDA, "nf_paged_attention: smem attribute: %s", cudaGetErrorString(e));
   int per_sm = 1;
   const int threads = (hg + 1) * 32;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, smem) != cudaSuccess || per_sm < 1)
-    per_sm = 1;
+  cudaError_t e = prepare_launch(reinterpret_cast<const void*>(kern), smem, threads, &per_sm);
+  if (e != cudaSuccess) return fail(NF_ECUDA, "nf_paged_attention: smem attribute: %s", cudaGetErrorString(e));
   long long grid = (long long)sm_count() * per_sm;
   const long long need = (want + p.Hkv - 1) / p.Hkv * p.n_hg;  // work items: units x head groups
   if (need < grid) grid = need;

@@ -15,4 +15,9 @@ int sm_count();
 size_t dtype_size(int dtype);
 // Which attention kernel the calling thread launched last (see nf_last_attention_path).
 void set_attention_path(int path);
+// Raises the dynamic shared memory limit of kernel `func` to `smem` bytes and
+// returns in *per_sm its resident blocks per SM for `threads` threads (NULL:
+// not needed), doing the CUDA calls once per (device, kernel, smem, threads):
+// a launch path then costs no attribute or occupancy query per call.
+cudaError_t prepare_launch(const void* func, int smem, int threads, int* per_sm);
 }  // namespace nf

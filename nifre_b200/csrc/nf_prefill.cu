@@ -737,15 +737,19 @@ static int launch_prefill(const PrefillParams& p, const CUtensorMap& tq, const C
                           int n_items, cudaStream_t st) {
   using C = PfCfg<D_>;
   auto kern = prefill_attention_kernel<T, D_>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
+  cudaError_t e = prepare_launch(reinterpret_cast<const void*>(kern), (int)C::SMEM, C::THREADS, nullptr);
   if (e != cudaSuccess) return fail(NF_ECUDA, "nf_prefill_attention: smem attribute: %s", cudaGetErrorString(e));
   // setmaxnreg moves registers between warpgroups within the launch total:
   // refuse a build whose register count would not cover the split
-  cudaFuncAttributes fa;
-  if (cudaFuncGetAttributes(&fa, kern) != cudaSuccess ||
-      C::REGS_CTRL * 128 + C::REGS_SOFTMAX * 128 * C::NH_ > fa.numRegs * C::THREADS)
+  // (the count is a property of the binary: queried once)
+  static int regs = -1;
+  if (regs < 0) {
+    cudaFuncAttributes fa;
+    regs = cudaFuncGetAttributes(&fa, kern) == cudaSuccess ? fa.numRegs : 0;
+  }
+  if (C::REGS_CTRL * 128 + C::REGS_SOFTMAX * 128 * C::NH_ > regs * C::THREADS)
     return fail(NF_EUNSUPPORTED, "nf_prefill_attention: kernel built with %d registers per thread, the warpgroup "
-                "split needs %d", fa.numRegs, C::LAUNCH_REGS);
+                "split needs %d", regs, C::LAUNCH_REGS);
   long long grid = n_items;
   if (grid > (long long)sm_count() * C::MINB) grid = (long long)sm_count() * C::MINB;
   kern<<<(int)grid, C::THREADS, C::SMEM, st>>>(p, tq, tk, tv);

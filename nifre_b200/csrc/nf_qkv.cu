@@ -233,7 +233,7 @@ extern "C" int nf_qkv_append(const void* x, int64_t x_row_stride, int32_t rows, 
   auto kern = dtype == NF_BF16 ? (bn == 32 ? qkv_append_kernel<__nv_bfloat16, 32> : qkv_append_kernel<__nv_bfloat16, 64>)
                                : (bn == 32 ? qkv_append_kernel<__half, 32> : qkv_append_kernel<__half, 64>);
   const int smem = bn == 32 ? (int)QkvCfg<32>::SMEM : (int)QkvCfg<64>::SMEM;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  cudaError_t e = prepare_launch(reinterpret_cast<const void*>(kern), smem, 192, nullptr);
   if (e != cudaSuccess) return fail(NF_ECUDA, "nf_qkv_append: smem attribute: %s", cudaGetErrorString(e));
   const dim3 grid((unsigned)row_tiles, (unsigned)(n_all / bn));
   kern<<<grid, 192, smem, st>>>(p, tx, tw);

@@ -127,6 +127,8 @@ class StepPlan:
         self.n_tiles = 0
         self.q_heads = None
         self.sched = None
+        # per-plan constant arguments of the layers' C ABI calls, built on first use
+        self.append_args = self.decode_args = None
 
     @property
     def kv_lens(self) -> np.ndarray:
@@ -188,9 +190,21 @@ class PagedKVCache:
         self._v_all = torch.empty(shape, device=self.device, dtype=self.dtype)
         self.k = list(self._k_all.unbind(0))
         self.v = list(self._v_all.unbind(0))
+        # per-call constants of the C ABI calls (pointers, codes), so that a layer's launches cost little host time
+        self._k_ptr = [t.data_ptr() for t in self.k]
+        self._v_ptr = [t.data_ptr() for t in self.v]
+        self._dt_code = _lib.dtype_code(self.dtype)
+        self._pool_rows = self.num_blocks * self.block_size
+        self._row_width = self.n_heads * self.head_dim
         self.bt_dev = torch.zeros((batch_size, self.max_blocks_per_seq), dtype=torch.int32, device=self.device)
-        self._synced = [(-1, 0)] * batch_size  # (table epoch, entries mirrored on the device)
+        # per slot: the table epoch and the number of entries mirrored on the device
+        self._sync_epoch = np.full(batch_size, -1, dtype=np.int64)
+        self._sync_len = np.zeros(batch_size, dtype=np.int64)
         self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self._status_ptr = self.status.data_ptr()
+        self._bt_ptr = self.bt_dev.data_ptr()
+        self._pos_ptr = self.pos.data_ptr()
+        self._dev_index = self.device.index if self.device.index is not None else torch.cuda.current_device()
         self._pf_queue = torch.zeros(2, dtype=torch.int32, device=self.device)  # prefill work queue (kernel-reset)
         self._meta = _DeviceBuffer(torch.int32, self.device)
         self._pos_buf = _DeviceBuffer(torch.int64, self.device)
@@ -257,6 +271,10 @@ class PagedKVCache:
     def allocated_blocks(self) -> int:
         return 0 if self.block_allocator is None else self.block_allocator.allocated_count
 
+    def _stream(self) -> int:
+        raw = _lib._raw_stream
+        return raw(self._dev_index) if raw is not None else _lib.stream_handle(self.device)
+
     def _set_pos(self, slot: int, value: int) -> None:
         self.pos_host[slot] = value
         self.pos[slot] = value
@@ -320,7 +338,7 @@ class PagedKVCache:
         return (self.dtype in (torch.bfloat16, torch.float16) and self.head_dim in (64, 128)
                 and q_heads // self.n_heads <= self.CASCADE_ROWS and self.block_size % 16 == 0)
 
-    def _cascade_groups(self, slots, q_lens, q_starts, ctx, dec, group: int):
+    def _cascade_groups(self, slots, q_lens, q_starts, ctx, dec, group: int, epochs=None):
         """Decode sequences that start with the same physical blocks, and the cascade work over those keys.
 
         Sequences with one new token whose tables begin with the same block
@@ -341,8 +359,9 @@ class PagedKVCache:
         # token counts and their tables' epochs (which change only when
         # leading entries are replaced) are those of the previous step, the
         # shared runs are unchanged and the previous grouping stands.
-        key = (slots.tobytes(), q_lens.tobytes(), q_starts.tobytes(), dec.tobytes(), group,
-               tuple(self.block_tables[s].epoch for s in slots.tolist()))
+        if epochs is None:
+            epochs = np.fromiter((self.block_tables[s].epoch for s in slots.tolist()), np.int64, len(slots))
+        key = (slots.tobytes(), q_lens.tobytes(), q_starts.tobytes(), dec.tobytes(), group, epochs.tobytes())
         if (self._cascade_memo is not None and self._cascade_memo[0] == key
                 and (self._cascade_memo[1][0] <= ctx).all()):  # no position moved back under a shared run
             return self._cascade_memo[1]
@@ -434,20 +453,25 @@ class PagedKVCache:
             i = int(np.argmax(over))
             raise AssertionError(
                 f"slot {int(slots[i])}: {int(ctx[i])} + {int(q_lens[i])} tokens exceed max_seq_len {self.max_seq_len}")
-        for s, c, n in zip(slots.tolist(), ctx.tolist(), q_lens.tolist()):
-            self.block_tables[s].ensure_capacity(c + n)
+        sl = slots.tolist()
+        tabs = self.block_tables
+        S = len(sl)
+        # allocation in list order, as the reference's row loop (only the tables that must grow allocate)
+        have = np.fromiter((len(tabs[s]._physical_blocks) for s in sl), np.int64, S)
+        need = (ctx + q_lens + self.block_size - 1) // self.block_size
+        for i in np.flatnonzero(need > have).tolist():
+            tabs[sl[i]].ensure_capacity(int(ctx[i] + q_lens[i]))
+            have[i] = len(tabs[sl[i]]._physical_blocks)
+        # block-table patches: entries the device mirror lacks (all of a table whose epoch changed)
+        epochs = np.fromiter((tabs[s].epoch for s in sl), np.int64, S)
+        done = np.where(epochs != self._sync_epoch[slots], 0, self._sync_len[slots])
         patches = []
-        for s in slots.tolist():
-            tab = self.block_tables[s]
-            epoch, done = self._synced[s]
-            if epoch != tab.epoch:
-                done = 0
-            blocks = tab._physical_blocks
-            if len(blocks) > done:
-                for lb in range(done, len(blocks)):
-                    patches.append((s, lb, blocks[lb]))
-            self._synced[s] = (tab.epoch, len(blocks))
-        S, P = len(slots), len(patches)
+        for i in np.flatnonzero(have > done).tolist():
+            s_, blocks = sl[i], tabs[sl[i]]._physical_blocks
+            patches.extend((s_, lb, blocks[lb]) for lb in range(int(done[i]), int(have[i])))
+        self._sync_epoch[slots] = epochs
+        self._sync_len[slots] = have
+        P = len(patches)
         T = int(q_lens.sum())
         # every query token is one work item attending over keys [0, ctx + i]
         kv = np.repeat(ctx + 1, q_lens) + (np.arange(T) - np.repeat(np.cumsum(q_lens) - q_lens, q_lens))
@@ -455,7 +479,7 @@ class PagedKVCache:
         dec = ~routed
         if self.cascade_supported(q_heads) and dec.any():
             shared, nparts, ctasks, ctoks = self._cascade_groups(slots, q_lens, q_starts, ctx, dec,
-                                                                 q_heads // self.n_heads)
+                                                                 q_heads // self.n_heads, epochs)
         else:
             shared, nparts, ctasks, ctoks = np.zeros(S, np.int32), np.zeros(S, np.int32), [], []
         tok_dec = np.repeat(dec, q_lens)
@@ -558,23 +582,26 @@ class PagedKVCache:
         """Scatter the step's new K/V rows (rows of ``key``/``value``: n_rows x H*D) into layer ``layer_id``."""
         if plan.closed:
             raise RuntimeError("step plan already closed")
-        _lib.require_cuda(key, "key")
+        if not key.is_cuda:
+            _lib.require_cuda(key, "key")
+        w = self._row_width
         for name, t in (("key", key), ("value", value)):
-            if t.dim() != 2 or t.shape[1] != self.n_heads * self.head_dim or t.stride(1) != 1:
-                raise ValueError(f"{name} must be (rows, {self.n_heads * self.head_dim}) with unit column stride")
+            if t.dim() != 2 or t.shape[1] != w or t.stride(1) != 1:
+                raise ValueError(f"{name} must be (rows, {w}) with unit column stride")
         if key.shape[0] < plan.rows_needed or value.shape[0] < plan.rows_needed:
             raise ValueError(f"key/value have {key.shape[0]} rows, the step uses rows up to {plan.rows_needed}")
         if not 0 <= layer_id < self.num_layers:
             raise IndexError(f"layer_id {layer_id} out of range [0, {self.num_layers})")
         last = layer_id == self.num_layers - 1
-        lib = _lib.load()
-        _lib.check(lib.nf_kv_append(
-            self.k[layer_id].data_ptr(), self.v[layer_id].data_ptr(), _lib.dtype_code(self.dtype),
-            self.num_blocks * self.block_size, key.data_ptr(), value.data_ptr(), _lib.dtype_code(key.dtype),
-            key.stride(0), value.stride(0), plan.slot_mapping.data_ptr(), plan.src_rows.data_ptr(),
-            plan.n_tokens, self.n_heads, self.head_dim, plan.seqs.data_ptr(), plan.n_seqs,
-            self.pos.data_ptr() if last else None, self.status.data_ptr(),
-            _lib.stream_handle(self.device)), "nf_kv_append")
+        if plan.append_args is None:  # the plan's part of the call, the same for every layer
+            plan.append_args = (plan.slot_mapping.data_ptr(), plan.src_rows.data_ptr(), plan.n_tokens, self.n_heads,
+                                self.head_dim, plan.seqs.data_ptr(), plan.n_seqs)
+        rc = _lib.load().nf_kv_append(
+            self._k_ptr[layer_id], self._v_ptr[layer_id], self._dt_code, self._pool_rows, key.data_ptr(),
+            value.data_ptr(), _lib.dtype_code(key.dtype), key.stride(0), value.stride(0), *plan.append_args,
+            self._pos_ptr if last else None, self._status_ptr, self._stream())
+        if rc:
+            _lib.check(rc, "nf_kv_append")
         if last:
             self._close(plan)
 
@@ -627,9 +654,10 @@ class PagedKVCache:
         the kernels also store the rows into the other ranks' gathered
         buffers and the launch ends once every rank's rows are in this one's.
         """
-        _lib.require_cuda(q, "q")
+        if not q.is_cuda:
+            _lib.require_cuda(q, "q")
         D = self.head_dim
-        if q.dim() != 2 or q.shape[1] % (self.n_heads * D) != 0 or q.stride(1) != 1:
+        if q.dim() != 2 or q.shape[1] % self._row_width != 0 or q.stride(1) != 1:
             raise ValueError(f"q must be (rows, Hq*{D}) with Hq a multiple of {self.n_heads}")
         if out.shape != q.shape or out.stride(1) != 1:
             raise ValueError("out must have q's shape")
@@ -640,55 +668,55 @@ class PagedKVCache:
         if not 0 <= layer_id < self.num_layers:
             raise IndexError(f"layer_id {layer_id} out of range [0, {self.num_layers})")
         hq = q.shape[1] // D
-        if plan.n_tiles and hq != plan.q_heads:
-            raise ValueError(f"the plan's prefill tiles are for {plan.q_heads} query heads, q has {hq}")
+        if (plan.n_tiles or plan.n_casc_tasks) and hq != plan.q_heads:
+            raise ValueError(f"the plan's prefill tiles / cascade groups are for {plan.q_heads} query heads, q has {hq}")
         if scale is None:
             scale = 1.0 / math.sqrt(D)
         lib = _lib.load()
-        stream = _lib.stream_handle(self.device)
+        stream = self._stream()
         gather = exchange.next(out) if exchange is not None else None
         gref = ctypes.byref(gather) if gather is not None else None
+        kp, vp = self._k_ptr[layer_id], self._v_ptr[layer_id]
+        qp, op, qs, os_ = q.data_ptr(), out.data_ptr(), q.stride(0), out.stride(0)
         if events is not None:
             events[0].record()
         if plan.n_tiles:
             _lib.check(lib.nf_prefill_attention_gather(
-                out.data_ptr(), out.stride(0), q.data_ptr(), q.stride(0), min(q.shape[0], out.shape[0]),
-                self.k[layer_id].data_ptr(), self.v[layer_id].data_ptr(), _lib.dtype_code(self.dtype),
-                hq, self.n_heads, D, self.block_size, self.num_blocks, self.bt_dev.data_ptr(),
-                self.max_blocks_per_seq, plan.tiles.data_ptr(), plan.n_tiles, plan.sched.data_ptr(),
-                self._pf_queue.data_ptr(), float(scale), gref, self.status.data_ptr(), stream),
-                "nf_prefill_attention")
+                op, os_, qp, qs, min(q.shape[0], out.shape[0]), kp, vp, self._dt_code, hq, self.n_heads, D,
+                self.block_size, self.num_blocks, self._bt_ptr, self.max_blocks_per_seq, plan.tiles.data_ptr(),
+                plan.n_tiles, plan.sched.data_ptr(), self._pf_queue.data_ptr(), float(scale), gref,
+                self._status_ptr, stream), "nf_prefill_attention")
         if events is not None:
             events[1].record()
         if plan.decode_units:
             max_items = plan.n_tokens
             if plan.ws_sizes is None or plan.ws_sizes[0] != hq:  # the same for every layer of the step
-                plan.ws_sizes = (hq, *_lib.workspace_sizes(plan.max_units, max_items, hq, self.n_heads, D,
-                                                           self.dtype))
+                pf, ci = _lib.workspace_sizes(plan.max_units, max_items, hq, self.n_heads, D, self.dtype)
+                plan.ws_sizes = (hq, pf, ci)
+                plan.decode_args = (hq, self.n_heads, D, self.block_size, self.num_blocks, self._bt_ptr,
+                                    self.max_blocks_per_seq, plan.items.data_ptr(), plan.units.data_ptr(),
+                                    plan.counts.data_ptr(), max_items, plan.max_units, plan.split)
             _, pf, ci = plan.ws_sizes
             ws = self._ws_partials.get(pf)
             cnt = self._ws_counters.get(ci)
             if plan.n_casc_tasks:
-                if hq != plan.q_heads:
-                    raise ValueError(f"the plan's cascade groups are for {plan.q_heads} query heads, q has {hq}")
                 # partials over the shared keys, merged by the decode launch with each query's own keys
                 _lib.check(lib.nf_cascade_attention(
-                    ws.data_ptr(), ws.numel(), q.data_ptr(), q.stride(0),
-                    self.k[layer_id].data_ptr(), self.v[layer_id].data_ptr(), _lib.dtype_code(self.dtype),
-                    hq, self.n_heads, D, self.block_size, self.num_blocks, self.bt_dev.data_ptr(),
+                    ws.data_ptr(), ws.numel(), qp, qs, kp, vp, self._dt_code,
+                    hq, self.n_heads, D, self.block_size, self.num_blocks, self._bt_ptr,
                     self.max_blocks_per_seq, plan.items.data_ptr(), plan.counts.data_ptr(), max_items,
                     plan.max_units, plan.casc_tasks.data_ptr(),
                     plan.n_casc_tasks, plan.casc_toks.data_ptr(), plan.n_casc_toks, float(scale),
-                    self.status.data_ptr(), stream), "nf_cascade_attention")
-            _lib.check(lib.nf_paged_attention_gather(
-                out.data_ptr(), out.stride(0), q.data_ptr(), q.stride(0),
-                self.k[layer_id].data_ptr(), self.v[layer_id].data_ptr(), _lib.dtype_code(self.dtype),
-                hq, self.n_heads, D, self.block_size, self.num_blocks, self.bt_dev.data_ptr(),
-                self.max_blocks_per_seq, plan.items.data_ptr(), plan.units.data_ptr(), plan.counts.data_ptr(),
-                max_items, plan.max_units, plan.split, float(scale), ws.data_ptr(), ws.numel(),
-                cnt.data_ptr(), cnt.numel(), gref, self.status.data_ptr(), stream), "nf_paged_attention")
+                    self._status_ptr, stream), "nf_cascade_attention")
+            a = plan.decode_args
+            rc = lib.nf_paged_attention_gather(
+                op, os_, qp, qs, kp, vp, self._dt_code, a[0], a[1], a[2], a[3], a[4], a[5], a[6], a[7], a[8], a[9],
+                a[10], a[11], a[12], float(scale), ws.data_ptr(), ws.numel(), cnt.data_ptr(), cnt.numel(), gref,
+                self._status_ptr, stream)
+            if rc:
+                _lib.check(rc, "nf_paged_attention")
         elif gather is not None:  # every row came from the prefill kernel: signal the peers on their own
-            _lib.check(lib.nf_exchange_barrier(gref, self.status.data_ptr(), stream), "nf_exchange_barrier")
+            _lib.check(lib.nf_exchange_barrier(gref, self._status_ptr, stream), "nf_exchange_barrier")
         if events is not None:
             events[2].record()
         return out
