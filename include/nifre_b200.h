@@ -271,6 +271,56 @@ int nf_paged_attention_gather(void* out, int64_t out_row_stride,
                               const NfGather* gather, int32_t* status, void* stream);
 
 /*
+ * The per-layer calls with their arguments in one struct: a host binding
+ * fills the step's constant fields once and changes only the per-layer
+ * pointers between calls, so that a call marshals one pointer instead of
+ * twenty to thirty arguments (the binding's per-call cost is then the
+ * launch itself).  Fields and meaning are those of nf_paged_attention_gather
+ * and nf_kv_append, in the same order.
+ */
+typedef struct NfAttentionArgs {
+  void* out;
+  int64_t out_row_stride;
+  const void* q;
+  int64_t q_row_stride;
+  const void* k_pool;
+  const void* v_pool;
+  int32_t dtype, num_q_heads, num_kv_heads, head_dim, block_size, num_blocks;
+  const int32_t* block_tables;
+  int32_t max_blocks_per_seq, max_items, max_units, split_tokens;
+  const int32_t* items;
+  const int32_t* units;
+  const int32_t* counts;
+  float scale;
+  int32_t pad;
+  float* ws_partials;
+  int64_t ws_partial_floats;
+  int32_t* ws_counters;
+  int64_t ws_counter_ints;
+  const NfGather* gather;
+  int32_t* status;
+} NfAttentionArgs;
+
+int nf_paged_attention_args(const NfAttentionArgs* args, void* stream);
+
+typedef struct NfAppendArgs {
+  void* k_pool;
+  void* v_pool;
+  int64_t pool_rows;
+  const void* k_new;
+  const void* v_new;
+  int64_t k_src_row_stride, v_src_row_stride;
+  int32_t pool_dtype, src_dtype, n_tokens, num_kv_heads, head_dim, n_seqs;
+  const int32_t* slot_mapping;
+  const int32_t* src_rows;
+  const int32_t* seqs;
+  int64_t* pos_out;
+  int32_t* status;
+} NfAppendArgs;
+
+int nf_kv_append_args(const NfAppendArgs* args, void* stream);
+
+/*
  * nf_exchange_barrier: the signal-and-wait of a gathered output on its own
  * (one thread): for a layer whose rows were all written by
  * nf_prefill_attention_gather (no decode launch follows to signal).

@@ -31,7 +31,8 @@ EXPORTS = ("nf_last_error", "nf_abi_version", "nf_pack_step", "nf_kv_append",
            "nf_attention_workspace", "nf_paged_attention", "nf_paged_attention_noalloc",
            "nf_last_attention_path", "nf_selftest_umma", "nf_prefill_attention", "nf_prefill_tile_rows",
            "nf_cascade_attention", "nf_selftest_wait", "nf_noalloc_scratch_fill", "nf_paged_attention_gather",
-           "nf_prefill_attention_gather", "nf_exchange_barrier", "nf_ipc_handle", "nf_ipc_open", "nf_ipc_close", "nf_qkv_append")
+           "nf_prefill_attention_gather", "nf_exchange_barrier", "nf_ipc_handle", "nf_ipc_open", "nf_ipc_close", "nf_qkv_append",
+           "nf_paged_attention_args", "nf_kv_append_args")
 
 _P = ctypes.c_void_p
 _I32 = ctypes.c_int32
@@ -48,6 +49,30 @@ class NfGather(ctypes.Structure):
 
 
 _G = ctypes.POINTER(NfGather)
+
+
+class NfAttentionArgs(ctypes.Structure):
+    """struct NfAttentionArgs of include/nifre_b200.h (the arguments of nf_paged_attention_gather)."""
+    _fields_ = [("out", ctypes.c_void_p), ("out_row_stride", ctypes.c_int64), ("q", ctypes.c_void_p),
+                ("q_row_stride", ctypes.c_int64), ("k_pool", ctypes.c_void_p), ("v_pool", ctypes.c_void_p),
+                ("dtype", ctypes.c_int32), ("num_q_heads", ctypes.c_int32), ("num_kv_heads", ctypes.c_int32),
+                ("head_dim", ctypes.c_int32), ("block_size", ctypes.c_int32), ("num_blocks", ctypes.c_int32),
+                ("block_tables", ctypes.c_void_p), ("max_blocks_per_seq", ctypes.c_int32),
+                ("max_items", ctypes.c_int32), ("max_units", ctypes.c_int32), ("split_tokens", ctypes.c_int32),
+                ("items", ctypes.c_void_p), ("units", ctypes.c_void_p), ("counts", ctypes.c_void_p),
+                ("scale", ctypes.c_float), ("pad", ctypes.c_int32), ("ws_partials", ctypes.c_void_p),
+                ("ws_partial_floats", ctypes.c_int64), ("ws_counters", ctypes.c_void_p),
+                ("ws_counter_ints", ctypes.c_int64), ("gather", ctypes.c_void_p), ("status", ctypes.c_void_p)]
+
+
+class NfAppendArgs(ctypes.Structure):
+    """struct NfAppendArgs of include/nifre_b200.h (the arguments of nf_kv_append)."""
+    _fields_ = [("k_pool", ctypes.c_void_p), ("v_pool", ctypes.c_void_p), ("pool_rows", ctypes.c_int64),
+                ("k_new", ctypes.c_void_p), ("v_new", ctypes.c_void_p), ("k_src_row_stride", ctypes.c_int64),
+                ("v_src_row_stride", ctypes.c_int64), ("pool_dtype", ctypes.c_int32), ("src_dtype", ctypes.c_int32),
+                ("n_tokens", ctypes.c_int32), ("num_kv_heads", ctypes.c_int32), ("head_dim", ctypes.c_int32),
+                ("n_seqs", ctypes.c_int32), ("slot_mapping", ctypes.c_void_p), ("src_rows", ctypes.c_void_p),
+                ("seqs", ctypes.c_void_p), ("pos_out", ctypes.c_void_p), ("status", ctypes.c_void_p)]
 
 _SIGNATURES = {
     "nf_last_error": ([], ctypes.c_char_p),
@@ -76,6 +101,8 @@ _SIGNATURES = {
     "nf_prefill_attention_gather": ([_P, _I64, _P, _I64, _I32, _P, _P, _I32, _I32, _I32, _I32, _I32, _I32,
                                      _P, _I32, _P, _I32, _P, _P, ctypes.c_float, _G, _P, _P], ctypes.c_int),
     "nf_exchange_barrier": ([_G, _P, _P], ctypes.c_int),
+    "nf_paged_attention_args": ([_P, _P], ctypes.c_int),
+    "nf_kv_append_args": ([_P, _P], ctypes.c_int),
     "nf_qkv_append": ([_P, _I64, _I32, _P, _P, _I32, _I32, _I32, _P, _I64, _P, _P, _I64, _I32, _P, _P, _I32, _P,
                        _P, _P], ctypes.c_int),
     "nf_ipc_handle": ([_P, _P, ctypes.POINTER(_I64)], ctypes.c_int),

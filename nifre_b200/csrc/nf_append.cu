@@ -218,3 +218,10 @@ extern "C" int nf_kv_append(void* k_pool, void* v_pool, int32_t pool_dtype, int6
   }
   return fail(NF_EINVAL, "nf_kv_append: bad src dtype %d", src_dtype);
 }
+
+extern "C" int nf_kv_append_args(const NfAppendArgs* a, void* stream) {
+  if (!a) return nf::fail(NF_EINVAL, "nf_kv_append_args: null argument struct");
+  return nf_kv_append(a->k_pool, a->v_pool, a->pool_dtype, a->pool_rows, a->k_new, a->v_new, a->src_dtype,
+                      a->k_src_row_stride, a->v_src_row_stride, a->slot_mapping, a->src_rows, a->n_tokens,
+                      a->num_kv_heads, a->head_dim, a->seqs, a->n_seqs, a->pos_out, a->status, stream);
+}

@@ -1054,3 +1054,13 @@ extern "C" int nf_noalloc_scratch_fill(int32_t byte, void* stream) {
   if (e != cudaSuccess) return fail(NF_ECUDA, "nf_noalloc_scratch_fill: %s", cudaGetErrorString(e));
   return ok();
 }
+
+extern "C" int nf_paged_attention_args(const NfAttentionArgs* a, void* stream) {
+  if (!a) return nf::fail(NF_EINVAL, "nf_paged_attention_args: null argument struct");
+  return nf_paged_attention_gather(a->out, a->out_row_stride, a->q, a->q_row_stride, a->k_pool, a->v_pool, a->dtype,
+                                   a->num_q_heads, a->num_kv_heads, a->head_dim, a->block_size, a->num_blocks,
+                                   a->block_tables, a->max_blocks_per_seq, a->items, a->units, a->counts,
+                                   a->max_items, a->max_units, a->split_tokens, a->scale, a->ws_partials,
+                                   a->ws_partial_floats, a->ws_counters, a->ws_counter_ints, a->gather, a->status,
+                                   stream);
+}

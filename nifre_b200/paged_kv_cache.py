@@ -593,13 +593,19 @@ class PagedKVCache:
         if not 0 <= layer_id < self.num_layers:
             raise IndexError(f"layer_id {layer_id} out of range [0, {self.num_layers})")
         last = layer_id == self.num_layers - 1
-        if plan.append_args is None:  # the plan's part of the call, the same for every layer
-            plan.append_args = (plan.slot_mapping.data_ptr(), plan.src_rows.data_ptr(), plan.n_tokens, self.n_heads,
-                                self.head_dim, plan.seqs.data_ptr(), plan.n_seqs)
-        rc = _lib.load().nf_kv_append(
-            self._k_ptr[layer_id], self._v_ptr[layer_id], self._dt_code, self._pool_rows, key.data_ptr(),
-            value.data_ptr(), _lib.dtype_code(key.dtype), key.stride(0), value.stride(0), *plan.append_args,
-            self._pos_ptr if last else None, self._status_ptr, self._stream())
+        a = plan.append_args
+        if a is None:  # the plan's part of the call, the same for every layer
+            a = plan.append_args = _lib.NfAppendArgs(
+                pool_rows=self._pool_rows, pool_dtype=self._dt_code, n_tokens=plan.n_tokens,
+                num_kv_heads=self.n_heads, head_dim=self.head_dim, n_seqs=plan.n_seqs,
+                slot_mapping=plan.slot_mapping.data_ptr(), src_rows=plan.src_rows.data_ptr(),
+                seqs=plan.seqs.data_ptr(), status=self._status_ptr)
+        a.k_pool, a.v_pool = self._k_ptr[layer_id], self._v_ptr[layer_id]
+        a.k_new, a.v_new = key.data_ptr(), value.data_ptr()
+        a.k_src_row_stride, a.v_src_row_stride = key.stride(0), value.stride(0)
+        a.src_dtype = _lib.dtype_code(key.dtype)
+        a.pos_out = self._pos_ptr if last else None
+        rc = _lib.load().nf_kv_append_args(ctypes.addressof(a), self._stream())
         if rc:
             _lib.check(rc, "nf_kv_append")
         if last:
@@ -693,9 +699,12 @@ class PagedKVCache:
             if plan.ws_sizes is None or plan.ws_sizes[0] != hq:  # the same for every layer of the step
                 pf, ci = _lib.workspace_sizes(plan.max_units, max_items, hq, self.n_heads, D, self.dtype)
                 plan.ws_sizes = (hq, pf, ci)
-                plan.decode_args = (hq, self.n_heads, D, self.block_size, self.num_blocks, self._bt_ptr,
-                                    self.max_blocks_per_seq, plan.items.data_ptr(), plan.units.data_ptr(),
-                                    plan.counts.data_ptr(), max_items, plan.max_units, plan.split)
+                plan.decode_args = _lib.NfAttentionArgs(
+                    dtype=self._dt_code, num_q_heads=hq, num_kv_heads=self.n_heads, head_dim=D,
+                    block_size=self.block_size, num_blocks=self.num_blocks, block_tables=self._bt_ptr,
+                    max_blocks_per_seq=self.max_blocks_per_seq, max_items=max_items, max_units=plan.max_units,
+                    split_tokens=plan.split, items=plan.items.data_ptr(), units=plan.units.data_ptr(),
+                    counts=plan.counts.data_ptr(), status=self._status_ptr)
             _, pf, ci = plan.ws_sizes
             ws = self._ws_partials.get(pf)
             cnt = self._ws_counters.get(ci)
@@ -709,10 +718,12 @@ class PagedKVCache:
                     plan.n_casc_tasks, plan.casc_toks.data_ptr(), plan.n_casc_toks, float(scale),
                     self._status_ptr, stream), "nf_cascade_attention")
             a = plan.decode_args
-            rc = lib.nf_paged_attention_gather(
-                op, os_, qp, qs, kp, vp, self._dt_code, a[0], a[1], a[2], a[3], a[4], a[5], a[6], a[7], a[8], a[9],
-                a[10], a[11], a[12], float(scale), ws.data_ptr(), ws.numel(), cnt.data_ptr(), cnt.numel(), gref,
-                self._status_ptr, stream)
+            a.out, a.out_row_stride, a.q, a.q_row_stride, a.k_pool, a.v_pool = op, os_, qp, qs, kp, vp
+            a.scale = scale
+            a.ws_partials, a.ws_partial_floats = ws.data_ptr(), ws.numel()
+            a.ws_counters, a.ws_counter_ints = cnt.data_ptr(), cnt.numel()
+            a.gather = ctypes.addressof(gather) if gather is not None else None
+            rc = lib.nf_paged_attention_args(ctypes.addressof(a), stream)
             if rc:
                 _lib.check(rc, "nf_paged_attention")
         elif gather is not None:  # every row came from the prefill kernel: signal the peers on their own

@@ -287,3 +287,34 @@ def test_attention_refuses_dtypes_other_than_the_cache_dtype():
         attn(q, kv, kv, kv_cache=cache, layer_id=0)
     with pytest.raises(ValueError, match="must equal the cache dtype"):
         attn(q.half(), kv, kv.half(), kv_cache=cache, layer_id=0)
+
+
+def test_argument_structs_match_the_header(tmp_path):
+    """The ctypes mirrors of NfGather / NfAttentionArgs / NfAppendArgs have the C layout (sizes and offsets)."""
+    import ctypes
+    import shutil
+    import subprocess
+
+    from nifre_b200 import _lib
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    structs = {"NfGather": _lib.NfGather, "NfAttentionArgs": _lib.NfAttentionArgs, "NfAppendArgs": _lib.NfAppendArgs}
+    lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "nifre_b200.h"', 'int main(void) {']
+    for name, cls in structs.items():
+        lines.append(f'  printf("{name} size %zu\\n", sizeof({name}));')
+        for field, _ in cls._fields_:
+            lines.append(f'  printf("{name} {field} %zu\\n", offsetof({name}, {field}));')
+    lines.append("  return 0;\n}")
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines))
+    exe = tmp_path / "layout"
+    subprocess.check_call([cc, "-I", str(ROOT / "include"), str(src), "-o", str(exe)])
+    got = {}
+    for line in subprocess.check_output([str(exe)], text=True).splitlines():
+        name, field, val = line.split()
+        got[(name, field)] = int(val)
+    for name, cls in structs.items():
+        assert got[(name, "size")] == ctypes.sizeof(cls), name
+        for field, _ in cls._fields_:
+            assert got[(name, field)] == getattr(cls, field).offset, (name, field)
