@@ -344,26 +344,32 @@ int nf_ipc_close(void* ptr, int64_t offset);
  * prefix_cache.py:33-81, paged_kv_cache.py:87-105), each shared block read
  * once per group of sequences and KV head instead of once per sequence.
  * tasks[n_tasks][8] (device, 16-byte aligned): slot (whose block table
- * holds the shared blocks), first, count, part, key_begin, key_end (multiples
- * of 16, at most 256 keys apart), 0, 0 -- the task's queries are
- * toks[first .. first+count), count * (num_q_heads / num_kv_heads) <= 128,
- * where toks[n_toks][2] (device, 8-byte aligned) holds (item number of
- * nf_pack_step, row of the query in q).  Each task writes the partial
- * softmax state of its queries over keys [key_begin, key_end) into partial
- * slot items[item].unit_base + part of ws_partials (the layout of
- * nf_attention_workspace), for every KV head (one CTA per task and head).  The same step's
- * nf_pack_step must have been given, through seq_shared, the shared key
- * count and cascade part count of each such sequence; the following
- * nf_paged_attention on the same stream and workspace then merges these
- * parts with the queries' own keys (nf_paged_attention_noalloc cannot: its
- * workspace is its own, so plans with cascade parts go to nf_paged_attention).
- * 16-bit pools, head_dim 64 or 128, block_size a multiple of 16.  Launched
- * with programmatic stream serialization: the launch before it on the stream
- * must not write the shared blocks, q, items or counts (the step's KV append
- * writes none of them); the launch ends after that one.
+ * holds the shared blocks), first, count, part, key_begin, key_end
+ * (multiples of 16), 0, 0 -- the task's queries are toks[first ..
+ * first+count), where toks[n_toks][2] (device, 8-byte aligned) holds (item
+ * number of nf_pack_step, row of the query in q, below num_q_rows).  Each
+ * task writes the partial softmax state of its queries over keys
+ * [key_begin, key_end) into partial slot items[item].unit_base + part of
+ * ws_partials (the layout of nf_attention_workspace), for every KV head.
+ * The same step's nf_pack_step must have been given, through seq_shared,
+ * the shared key count and cascade part count of each such sequence; the
+ * following nf_paged_attention on the same stream and workspace then merges
+ * these parts with the queries' own keys (nf_paged_attention_noalloc
+ * cannot: its workspace is its own, so plans with cascade parts go to
+ * nf_paged_attention).  16-bit pools, head_dim 64 or 128, block_size a
+ * multiple of 16.  nf_cascade_limits gives the largest task: with 1, 2, 4
+ * or 8 query heads per KV head (G) the tasks run on the tensor cores (the
+ * prefill kernel's tcgen05 pipeline, one (task, KV head) item at a time per
+ * CTA: up to 256 / G queries and any whole number of 16-key groups, q rows
+ * 16-byte aligned); other group sizes use an mma.sync kernel (one CTA per
+ * task and KV head: up to 128 / G queries and 256 keys) launched with
+ * programmatic stream serialization: the launch before it on the stream
+ * must not write the shared blocks, q, items or counts (the step's KV
+ * append writes none of them).  A malformed task, or a query row outside
+ * [0, num_q_rows), sets NF_STATUS_BAD_SHARED and is skipped.
  */
 int nf_cascade_attention(float* ws_partials, int64_t ws_partial_floats,
-                         const void* q, int64_t q_row_stride,
+                         const void* q, int64_t q_row_stride, int32_t num_q_rows,
                          const void* k_pool, const void* v_pool, int32_t dtype,
                          int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
                          int32_t block_size, int32_t num_blocks,
@@ -372,6 +378,13 @@ int nf_cascade_attention(float* ws_partials, int64_t ws_partial_floats,
                          const int32_t* tasks, int32_t n_tasks, const int32_t* toks, int32_t n_toks,
                          float scale,
                          int32_t* status, void* stream);
+
+/*
+ * nf_cascade_limits: the largest task nf_cascade_attention takes for this
+ * shape -- query rows (queries x query heads per KV head) and keys.
+ */
+int nf_cascade_limits(int32_t dtype, int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
+                      int32_t* max_rows, int32_t* max_keys);
 
 /*
  * nf_prefill_attention: causal attention of prefill chunks on the tensor

@@ -32,7 +32,7 @@ EXPORTS = ("nf_last_error", "nf_abi_version", "nf_pack_step", "nf_kv_append",
            "nf_last_attention_path", "nf_selftest_umma", "nf_prefill_attention", "nf_prefill_tile_rows",
            "nf_cascade_attention", "nf_selftest_wait", "nf_noalloc_scratch_fill", "nf_paged_attention_gather",
            "nf_prefill_attention_gather", "nf_exchange_barrier", "nf_ipc_handle", "nf_ipc_open", "nf_ipc_close", "nf_qkv_append",
-           "nf_paged_attention_args", "nf_kv_append_args")
+           "nf_paged_attention_args", "nf_kv_append_args", "nf_cascade_limits")
 
 _P = ctypes.c_void_p
 _I32 = ctypes.c_int32
@@ -86,7 +86,7 @@ _SIGNATURES = {
                               _P, _I32, _P, _I32, _P, _P, ctypes.c_float, _P, _P], ctypes.c_int),
     "nf_pack_step": ([_P, _I32, _P, _I32, _P, _I32, _I32, _I32, _I32, _I32, _P, _P,
                       _P, _P, _P, _P, _P, _P, _I32, _I32, _P, _P], ctypes.c_int),
-    "nf_cascade_attention": ([_P, _I64, _P, _I64, _P, _P, _I32, _I32, _I32, _I32, _I32, _I32, _P, _I32,
+    "nf_cascade_attention": ([_P, _I64, _P, _I64, _I32, _P, _P, _I32, _I32, _I32, _I32, _I32, _I32, _P, _I32,
                               _P, _P, _I32, _I32, _P, _I32, _P, _I32, ctypes.c_float, _P, _P], ctypes.c_int),
     "nf_kv_append": ([_P, _P, _I32, _I64, _P, _P, _I32, _I64, _I64, _P, _P, _I32,
                       _I32, _I32, _P, _I32, _P, _P, _P], ctypes.c_int),
@@ -101,6 +101,7 @@ _SIGNATURES = {
     "nf_prefill_attention_gather": ([_P, _I64, _P, _I64, _I32, _P, _P, _I32, _I32, _I32, _I32, _I32, _I32,
                                      _P, _I32, _P, _I32, _P, _P, ctypes.c_float, _G, _P, _P], ctypes.c_int),
     "nf_exchange_barrier": ([_G, _P, _P], ctypes.c_int),
+    "nf_cascade_limits": ([_I32, _I32, _I32, _I32, _I32, ctypes.POINTER(_I32), ctypes.POINTER(_I32)], ctypes.c_int),
     "nf_paged_attention_args": ([_P, _P], ctypes.c_int),
     "nf_kv_append_args": ([_P, _P], ctypes.c_int),
     "nf_qkv_append": ([_P, _I64, _I32, _P, _P, _I32, _I32, _I32, _P, _I64, _P, _P, _I64, _I32, _P, _P, _I32, _P,

@@ -77,20 +77,22 @@ __device__ int tma_producer(const AttnParams& p, const CUtensorMap* tk, const CU
   int s = 0;           // slot of step k (k mod S)
   uint32_t pe = 1;     // parity that frees slot s for step k: ((k / S) & 1) ^ 1
   bool ok = true;
-  int w = atomicAdd(p.queue, 1);
+  // the first work item is this CTA's own (no round trip to the queue); the
+  // queue hands out the rest, from gridDim.x on
+  int w = blockIdx.x;
   int4 ra = make_int4(0, 0, 0, 0), rb = ra;
   if (w < total) {
     ra = __ldg(urec + 2 * (w / p.n_hg));
     rb = __ldg(urec + 2 * (w / p.n_hg) + 1);
   }
   // This launch may overlap the kernel before it on the stream (the KV
-  // append of this layer, with programmatic stream serialization).  The
-  // ticket, unit records and block tables come from the step's pack, which
-  // completed before that kernel began; only the pools, where the append
-  // writes the new keys and values, must wait for it.  A launch whose queue
-  // is cleared by the operation just before it (the allocation-free entry
-  // point's memset) goes without programmatic serialization (p.pdl = 0), so
-  // the first ticket is taken only after that clear.
+  // append of this layer, or the cascade, with programmatic stream
+  // serialization).  The unit records and block tables come from the step's
+  // pack, which completed before that kernel began; the pools (where the
+  // append writes the new keys and values), the cascade's partial records
+  // and the queue are touched only after the wait.  A launch whose queue is
+  // cleared by the operation just before it (the allocation-free entry
+  // point's memset) goes without programmatic serialization (p.pdl = 0).
   if (w < total) {
     const int lb = rb.x / p.bs;
     if (lb < p.max_blocks) asm volatile("prefetch.global.L1 [%0];" ::"l"(p.bt + (long long)ra.y * p.max_blocks + lb));
@@ -108,7 +110,7 @@ __device__ int tma_producer(const AttnParams& p, const CUtensorMap* tk, const CU
     int4 na = make_int4(0, 0, 0, 0), nb = na;
     for (int i = 0, t = rb.x; i < nsteps; ++i, t += 16, ++k) {
       if (i == ask) {
-        wn = atomicAdd(p.queue, 1);
+        wn = (int)gridDim.x + atomicAdd(p.queue, 1);
       } else if (i == ask + kGap && wn < total) {
         na = __ldg(urec + 2 * (wn / p.n_hg));
         nb = __ldg(urec + 2 * (wn / p.n_hg) + 1);

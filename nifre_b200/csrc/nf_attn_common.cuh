@@ -172,46 +172,68 @@ __device__ void merge_chunk(const AttnParams& p, const Work& c, int c0) {
 // *cta_done).  Thread 0 adds them to the grid count and waits, with a time
 // limit, until all `total` work items have stored their outputs or parts;
 // then every warp of the grid takes a share of the split-K merges (one warp
-// per (item, KV head) with more than one part).  The last CTA out resets the
-// queue and the counts for the next launch.  The wait needs every CTA
+// per (item, KV head, group of 32 output chunks) with more than one part).
+// The counts and each warp's first merge task's item records (the step's
+// pack wrote them before the launch) are requested before the wait, and
+// each task's successor's records before the task's parts, so that a merge
+// costs about one round trip once the wait ends.  The last CTA out resets
+// the queue and the counts for the next launch.  The wait needs every CTA
 // resident at once: the kernels are launched cooperatively.
 template <typename T, int PB>
 __device__ void finish_launch(const AttnParams& p, int* cta_done, int total) {
   __shared__ int go;
+  const int c_items = __ldg(p.counts), c_multi = __ldg(p.counts + 2), c_units = __ldg(p.counts + 3);
+  const int groups = (p.G * (p.D >> 2) + 31) >> 5;
+  const int stride = gridDim.x * (blockDim.x >> 5);
+  const int task0 = (threadIdx.x >> 5) * gridDim.x + blockIdx.x;
+  const int4* items4 = reinterpret_cast<const int4*>(p.items);
+  // records of a task's item t and the unit base of item t + 1 (within the buffers; checked against the counts
+  // when used)
+  auto records = [&](int task, int4& it, int& nx) {
+    const int t = task / groups / p.Hkv;
+    it = make_int4(0, 0, 0, -1);
+    nx = 0;
+    if (t < p.max_items) {
+      it = __ldg(items4 + t);
+      if (t + 1 < p.max_items) nx = __ldg(p.items + 4 * (t + 1) + 3);
+    }
+  };
+  int4 it;
+  int nx;
+  records(task0, it, nx);
   __syncthreads();  // the CTA's output and part stores are issued
   // set by the pack when an item has several parts
-  const bool merge = __ldg(p.counts + 2) != 0 && !parts_refused(p);
+  const bool merge = c_multi != 0 && !parts_refused(p);
   if (threadIdx.x == 0) {
     __threadfence();
-    atomicAdd(p.queue + 2, *cta_done);
-    const bool ok = !merge || wait_count(p.queue + 2, total, p.status);
+    const int mine = *cta_done;
+    const int now = atomicAdd(p.queue + 2, mine) + mine;  // the last CTA in needs no further poll
+    const bool ok = !merge || now >= total || wait_count(p.queue + 2, total, p.status);
     __threadfence();
     go = ok;
   }
   __syncthreads();
   if (go && merge) {
-    // tasks: (item, KV head, group of 32 output chunks), dealt round-robin
-    // over the CTAs so that every SM takes a share
-    const int n_items = min(__ldg(p.counts), p.max_items);
-    const int n_units = min(__ldg(p.counts + 3), p.max_units);  // partial slots, cascade parts included
-    const int groups = (p.G * (p.D >> 2) + 31) >> 5;
+    const int n_items = min(c_items, p.max_items);
+    const int n_units = min(c_units, p.max_units);  // partial slots, cascade parts included
     const int tasks = n_items * p.Hkv * groups;
-    const int stride = gridDim.x * (blockDim.x >> 5);
-    for (int task = (threadIdx.x >> 5) * gridDim.x + blockIdx.x; task < tasks; task += stride) {
+    // tasks dealt round-robin over the CTAs so that every SM takes a share
+    for (int task = task0; task < tasks; task += stride) {
       const int pair = task / groups, grp = task - pair * groups;
       const int t = pair / p.Hkv;
-      const int4 it = __ldg(reinterpret_cast<const int4*>(p.items) + t);
-      const int next = t + 1 < n_items ? __ldg(p.items + 4 * (t + 1) + 3) : n_units;
-      const int nparts = next - it.w;
-      if (nparts <= 1 || it.w < 0 || next > p.max_units) continue;  // written directly, or a flagged overflow
+      const int next = t + 1 < n_items ? nx : n_units;
+      const int4 cur = it;
+      if (task + stride < tasks) records(task + stride, it, nx);
+      const int nparts = next - cur.w;
+      if (nparts <= 1 || cur.w < 0 || next > p.max_units) continue;  // written directly, or a flagged overflow
       Work c;
       c.w = task;
       c.u = 0;
       c.item = t;
-      c.slot = it.x;
-      c.q_row = it.y;
+      c.slot = cur.x;
+      c.q_row = cur.y;
       c.t0 = c.t1 = 0;
-      c.unit_base = it.w;
+      c.unit_base = cur.w;
       c.nparts = nparts;
       c.kvh = pair - t * p.Hkv;
       c.part = 0;

@@ -32,6 +32,7 @@ struct CascadeParams {
   float* ws;  // partials [slots][Hq][D + 4]: acc[D], m, l, pad
   const char* q;
   long long q_stride;  // elements between query rows
+  int q_rows;          // rows of q: a query row outside [0, q_rows) is flagged
   const char* kp;
   const char* vp;
   int Hq, Hkv, D, G, bs, num_blocks;
@@ -122,8 +123,10 @@ __device__ __forceinline__ void cascade_body(const CascadeParams& p, unsigned ch
     cp_async_commit();
   }
 
-  const int tok0 = tq0.x >= 0 && tq0.x < n_items ? tq0.x : -1;
-  const int tok1 = tq1.x >= 0 && tq1.x < n_items ? tq1.x : -1;
+  const bool row0_ok = tq0.y >= 0 && tq0.y < p.q_rows, row1_ok = tq1.y >= 0 && tq1.y < p.q_rows;
+  if ((tq0.x >= 0 && !row0_ok) || (tq1.x >= 0 && !row1_ok)) atomicOr(p.status, NF_STATUS_BAD_SHARED);
+  const int tok0 = tq0.x >= 0 && tq0.x < n_items && row0_ok ? tq0.x : -1;
+  const int tok1 = tq1.x >= 0 && tq1.x < n_items && row1_ok ? tq1.x : -1;
   // partial slots of the rows' items (checked at the store), requested beside the query rows
   int base0 = -1, next0 = 0, base1 = -1, next1 = 0;
   if (tok0 >= 0) {
@@ -273,7 +276,33 @@ __global__ void __launch_bounds__(kCascThreads, D_ == 64 ? 2 : 1) cascade_kernel
 
 }  // namespace nf
 
+namespace nf {
+// The tensor-core path (the prefill kernel's pipeline, nf_prefill.cu) serves
+// 16-bit pools with head_dim 64/128, 1, 2, 4 or 8 query heads per KV head and
+// block sizes that are multiples of 16; other shapes use this file's kernel.
+static bool cascade_on_tensor_cores(int dtype, int Hq, int Hkv, int D, int bs) {
+  if ((dtype != NF_BF16 && dtype != NF_F16) || (D != 64 && D != 128) || bs % 16 || Hkv <= 0 || Hq % Hkv) return false;
+  const int G = Hq / Hkv;
+  return G == 1 || G == 2 || G == 4 || G == 8;
+}
+}  // namespace nf
+
+extern "C" int nf_cascade_limits(int32_t dtype, int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                                 int32_t block_size, int32_t* max_rows, int32_t* max_keys) {
+  using namespace nf;
+  if (!max_rows || !max_keys) return fail(NF_EINVAL, "nf_cascade_limits: null pointer argument");
+  if (cascade_on_tensor_cores(dtype, num_q_heads, num_kv_heads, head_dim, block_size)) {
+    *max_rows = 256;       // two 128-row halves sharing the task's K/V stream
+    *max_keys = 1 << 30;   // any whole number of 16-key groups
+  } else {
+    *max_rows = kCascRows;
+    *max_keys = kCascStages * kCascKeys;
+  }
+  return ok();
+}
+
 extern "C" int nf_cascade_attention(float* ws_partials, int64_t ws_partial_floats, const void* q, int64_t q_row_stride,
+                                    int32_t num_q_rows,
                                     const void* k_pool, const void* v_pool, int32_t dtype, int32_t num_q_heads,
                                     int32_t num_kv_heads, int32_t head_dim, int32_t block_size, int32_t num_blocks,
                                     const int32_t* block_tables, int32_t max_blocks_per_seq, const int32_t* items,
@@ -294,7 +323,8 @@ extern "C" int nf_cascade_attention(float* ws_partials, int64_t ws_partial_float
     return fail(NF_EUNSUPPORTED, "nf_cascade_attention: block_size %d is not a multiple of 16", block_size);
   if (!ws_partials || !q || !k_pool || !v_pool || !block_tables || !items || !counts || !tasks || !toks || !status)
     return fail(NF_EINVAL, "nf_cascade_attention: null pointer argument");
-  if (n_tasks < 0 || n_toks <= 0 || num_blocks <= 0 || max_blocks_per_seq <= 0 || max_items <= 0 || max_units <= 0)
+  if (n_tasks < 0 || n_toks <= 0 || num_q_rows <= 0 || num_blocks <= 0 || max_blocks_per_seq <= 0 || max_items <= 0 ||
+      max_units <= 0)
     return fail(NF_EINVAL, "nf_cascade_attention: sizes must be positive");
   if ((int64_t)max_units * num_q_heads * (head_dim + 4) > ws_partial_floats)
     return fail(NF_EINVAL, "nf_cascade_attention: workspace holds fewer than max_units partial slots");
@@ -304,10 +334,42 @@ extern "C" int nf_cascade_attention(float* ws_partials, int64_t ws_partial_float
   if (!al(ws_partials, 8) || !al(items, 16) || !al(tasks, 16) || !al(toks, 8))
     return fail(NF_EINVAL, "nf_cascade_attention: items and tasks must be 16-byte, toks 8-byte aligned");
   if (n_tasks > 65535 * 1024) return fail(NF_EINVAL, "nf_cascade_attention: too many tasks (%d)", n_tasks);
+  if (cascade_on_tensor_cores(dtype, num_q_heads, num_kv_heads, head_dim, block_size)) {
+    if (!al(q, 16) || (q_row_stride * 2) % 16 != 0)
+      return fail(NF_EINVAL, "nf_cascade_attention: q rows must be 16-byte aligned");
+    CascTcArgs a;
+    a.ws = ws_partials;
+    a.q = q;
+    a.q_stride = q_row_stride;
+    a.q_rows = num_q_rows;
+    a.kp = k_pool;
+    a.vp = v_pool;
+    a.dtype = dtype;
+    a.Hq = num_q_heads;
+    a.Hkv = num_kv_heads;
+    a.D = head_dim;
+    a.bs = block_size;
+    a.num_blocks = num_blocks;
+    a.bt = block_tables;
+    a.max_blocks = max_blocks_per_seq;
+    a.items = items;
+    a.counts = counts;
+    a.max_items = max_items;
+    a.max_units = max_units;
+    a.tasks = tasks;
+    a.n_tasks = n_tasks;
+    a.toks = toks;
+    a.n_toks = n_toks;
+    a.scale_log2 = scale * 1.4426950408889634f;
+    a.status = status;
+    a.stream = stream;
+    return cascade_tensor_core(a);
+  }
   CascadeParams p;
   p.ws = ws_partials;
   p.q = static_cast<const char*>(q);
   p.q_stride = q_row_stride;
+  p.q_rows = num_q_rows;
   p.kp = static_cast<const char*>(k_pool);
   p.vp = static_cast<const char*>(v_pool);
   p.Hq = num_q_heads;

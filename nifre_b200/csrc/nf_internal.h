@@ -20,4 +20,30 @@ void set_attention_path(int path);
 // not needed), doing the CUDA calls once per (device, kernel, smem, threads):
 // a launch path then costs no attribute or occupancy query per call.
 cudaError_t prepare_launch(const void* func, int smem, int threads, int* per_sm);
+
+// The cascade on the tensor cores (the prefill kernel's pipeline in its
+// cascade mode, nf_prefill.cu); NF_EUNSUPPORTED when the shape needs the
+// mma.sync kernel of nf_cascade.cu.
+struct CascTcArgs {
+  float* ws;
+  const void* q;
+  long long q_stride;
+  int q_rows;
+  const void* kp;
+  const void* vp;
+  int dtype, Hq, Hkv, D, bs, num_blocks;
+  const int* bt;
+  int max_blocks;
+  const int* items;
+  const int* counts;
+  int max_items, max_units;
+  const int* tasks;
+  int n_tasks;
+  const int* toks;
+  int n_toks;
+  float scale_log2;
+  int* status;
+  void* stream;
+};
+int cascade_tensor_core(const CascTcArgs& a);
 }  // namespace nf

@@ -67,6 +67,16 @@ struct PrefillParams {
   // gathered output over several GPUs: rows also stored at peer_out[r] (same layout as out), r < n_peers
   int n_peers;
   char* peer_out[kMaxRanks - 1];
+  // cascade mode (nf_cascade_attention on the tensor cores): an item is (task, KV head); its rows are the
+  // decode queries of a group of sequences, its keys the range [key_begin, key_end) of their shared blocks,
+  // and it writes split-K partial records instead of output rows
+  const int* tasks;   // [n_tiles][8]: slot, first, count, part, key_begin, key_end, 0, 0
+  const int* toks;    // [n_toks][2]: item of nf_pack_step, q row
+  int n_toks;
+  const int* items;   // nf_pack_step's work items (unit_base at [3])
+  const int* counts;  // nf_pack_step's counts ([3]: partial slots)
+  float* ws;          // partials [slots][Hq][D + 4]: acc[D], m, l, pad
+  int max_items, max_units;
 };
 
 constexpr float kPfNegInf = -INFINITY;
@@ -235,11 +245,12 @@ struct PfItemRing {
   __device__ PfItemRing(const PfBars& b, unsigned char* base) : bar(b), slots(base + kPfItemSlots) {}
   __device__ int* slot(int st) const { return reinterpret_cast<int*>(slots + 32 * st); }
   // a reader warp: the next item (false at the end)
-  __device__ bool next(int& item, int4& tl, int* status) {
+  __device__ bool next(int& item, int4& tl, int2& kr, int* status) {
     if (!mbar_wait(bar.item_full(r.st), r.ph, status)) return false;
     const volatile int* sl = slot(r.st);
     item = sl[0];
     tl = make_int4(sl[1], sl[2], sl[3], sl[4]);
+    kr = make_int2(sl[5], sl[6]);
     __syncwarp();
     if ((threadIdx.x & 31) == 0) mbar_arrive(bar.item_empty(r.st));
     r.next(kPfItemRing);
@@ -248,14 +259,33 @@ struct PfItemRing {
 };
 
 // The producer warp's side of the queue: claim the next item, publish it.
-__device__ __forceinline__ bool pf_claim_item(const PrefillParams& p, PfItemRing& ring, int& item, int4& tl) {
+// Cascade items are dealt in a fixed round-robin (claim k of CTA b is item
+// b + k * gridDim.x): they are alike in size, and the cascade entry point
+// has no queue buffer.
+template <bool CASC>
+__device__ __forceinline__ bool pf_claim_item(const PrefillParams& p, PfItemRing& ring, int& item, int4& tl, int2& kr,
+                                              int& claims) {
   const int lane = threadIdx.x & 31;
   int pos = 0;
-  if (lane == 0) pos = atomicAdd(p.queue, 1);
-  pos = __shfl_sync(0xffffffffu, pos, 0);
+  if (CASC) {
+    pos = blockIdx.x + claims * gridDim.x;
+  } else {
+    if (lane == 0) pos = atomicAdd(p.queue, 1);
+    pos = __shfl_sync(0xffffffffu, pos, 0);
+  }
+  ++claims;
   const int n_items = p.n_tiles * p.Hkv;
   item = pos < n_items ? (p.order ? __ldg(p.order + pos) : pos) : -1;
-  tl = item >= 0 ? __ldg(reinterpret_cast<const int4*>(p.tiles) + item / p.Hkv) : make_int4(0, 0, 0, 0);
+  kr = make_int2(0, 0);
+  if (item < 0) {
+    tl = make_int4(0, 0, 0, 0);
+  } else if (CASC) {
+    tl = __ldg(reinterpret_cast<const int4*>(p.tasks) + 2 * (item / p.Hkv));
+    const int4 tb = __ldg(reinterpret_cast<const int4*>(p.tasks) + 2 * (item / p.Hkv) + 1);
+    kr = make_int2(tb.x, tb.y);
+  } else {
+    tl = __ldg(reinterpret_cast<const int4*>(p.tiles) + item / p.Hkv);
+  }
   if (!mbar_wait(ring.bar.item_empty(ring.r.st), ring.r.ph ^ 1, p.status)) return false;
   if (lane == 0) {
     volatile int* sl = ring.slot(ring.r.st);
@@ -264,6 +294,8 @@ __device__ __forceinline__ bool pf_claim_item(const PrefillParams& p, PfItemRing
     sl[2] = tl.y;
     sl[3] = tl.z;
     sl[4] = tl.w;
+    sl[5] = kr.x;
+    sl[6] = kr.y;
     mbar_arrive(ring.bar.item_full(ring.r.st));
   }
   __syncwarp();
@@ -271,27 +303,46 @@ __device__ __forceinline__ bool pf_claim_item(const PrefillParams& p, PfItemRing
   return item >= 0;
 }
 
-// Shape of one work item: its key tiles, the halves that hold tokens and
-// each half's key tiles (half 0 ends up to 128/G tokens earlier).
+// Shape of one work item: its key tiles, the halves that hold rows and
+// each half's key tiles.  Prefill: tl = (slot, q_row0, ntok, pos0), keys
+// [0, pos0 + ntok) with the causal limit (half 0 ends up to 128/G tokens
+// earlier).  Cascade: tl = (slot, first query record, count, part), keys
+// [k0, k1) all visible to every row; a malformed task is flagged and
+// skipped by every role alike (bad).
+template <bool CASC>
 struct PfItem {
-  int4 tl;  // slot, q_row0, ntok, pos0
-  int kvh, nkeys, nkt, n_half, nkt_h[2];
-  __device__ PfItem(const PrefillParams& p, int item, int4 t) : tl(t) {
+  int4 tl;
+  int kvh, k0, nkeys, nkt, n_half, nkt_h[2];
+  bool bad;
+  __device__ PfItem(const PrefillParams& p, int item, int4 t, int2 kr) : tl(t) {
     kvh = item % p.Hkv;
-    const int ntok = min(tl.z, p.NH * p.TT);
-    nkeys = tl.w + ntok;
-    nkt = (nkeys + 127) >> 7;
-    n_half = ntok > p.TT ? 2 : 1;
-    nkt_h[0] = (tl.w + min(ntok, p.TT) + 127) >> 7;
-    nkt_h[1] = nkt;
+    if (CASC) {
+      k0 = kr.x;
+      nkeys = kr.y - kr.x;
+      bad = tl.x < 0 || tl.y < 0 || tl.z <= 0 || tl.y + tl.z > p.n_toks || tl.z > p.NH * p.TT || tl.w < 0 || k0 < 0 ||
+            nkeys <= 0 || (k0 & 15) || (nkeys & 15) || kr.y > p.max_blocks * p.bs;
+      nkt = bad ? 0 : (nkeys + 127) >> 7;
+      n_half = tl.z > p.TT ? 2 : 1;
+      nkt_h[0] = nkt_h[1] = nkt;
+    } else {
+      k0 = 0;
+      bad = false;
+      const int ntok = min(tl.z, p.NH * p.TT);
+      nkeys = tl.w + ntok;
+      nkt = (nkeys + 127) >> 7;
+      n_half = ntok > p.TT ? 2 : 1;
+      nkt_h[0] = (tl.w + min(ntok, p.TT) + 127) >> 7;
+      nkt_h[1] = nkt;
+    }
   }
   __device__ bool active(int h, int j) const { return h < n_half && j >= 0 && j < nkt_h[h]; }
 };
 
 // Block id of 16-key block `lane` (< 8) of key tile j (keys >= nkeys: 0,
 // not loaded); lanes 0..7 load theirs together, one round trip per tile.
-__device__ __forceinline__ int pf_block_id(const PrefillParams& p, const int* btrow, int j, int nkeys, int lane) {
-  const int key = (j * 8 + lane) * 16, lb = key / p.bs;
+__device__ __forceinline__ int pf_block_id(const PrefillParams& p, const int* btrow, int j, int nkeys, int k0,
+                                           int lane) {
+  const int key = (j * 8 + lane) * 16, lb = (k0 + key) / p.bs;
   if (lane >= 8 || key >= nkeys) return 0;
   return lb < p.max_blocks ? __ldg(btrow + lb) : -1;
 }
@@ -301,12 +352,13 @@ __device__ __forceinline__ int pf_block_id(const PrefillParams& p, const int* bt
 // armed the stage's barrier with the tile's bytes.
 template <int D_>
 __device__ __forceinline__ void pf_load_tile(const PrefillParams& p, const CUtensorMap* tm, uint32_t dst0,
-                                             uint32_t full, int blk, int j, int nb, int kvh, uint64_t pol, int lane) {
+                                             uint32_t full, int blk, int j, int nb, int kvh, int k0, uint64_t pol,
+                                             int lane) {
   constexpr int NDH = D_ / 64;
   if (lane == 0) mbar_arrive_expect_tx(full, nb * NDH * 2048);
   __syncwarp();
   if (lane < nb) {
-    const int off = ((j * 8 + lane) * 16) % p.bs;
+    const int off = (k0 + (j * 8 + lane) * 16) % p.bs;
     int phys = blk;
     if (phys < 0 || phys >= p.num_blocks) {
       atomicOr(p.status, NF_STATUS_BAD_BLOCK);
@@ -323,9 +375,60 @@ __device__ __forceinline__ void pf_load_tile(const PrefillParams& p, const CUten
   }
 }
 
+// The cascade item's query rows, gathered by tensor copies: row i * G + g
+// of half h is query head kvh * G + g of the group's (h * TT + i)-th query
+// (toks[first + ...]).  One copy per query (and 64-element part of a head)
+// brings its G heads -- G consecutive 128-byte rows of the tile, swizzled
+// by their shared-memory address exactly as a whole-tile copy would be.
+// The query rows come first, 32 per register and all in one round trip;
+// rows of the active halves past the group's last query are zeroed.  A row
+// outside [0, rows) is flagged (the tensor copy would read zeros there).
+template <int D_>
+__device__ __forceinline__ void pf_gather_queries(const PrefillParams& p, const PfItem<true>& w, const CUtensorMap* tq,
+                                                  uint32_t dst0, uint32_t full, uint64_t pol, int lane) {
+  using C = PfCfg<D_>;
+  constexpr int NDH = D_ / 64;
+  const int G = p.G, lg = __ffs(G) - 1;  // G is a power of two
+  const int nq = w.n_half * p.TT;        // query slots of the active halves
+  const int n = min(w.tl.z, nq);
+  int rowv[C::NH_ * 4];
+#pragma unroll
+  for (int s = 0; s < C::NH_ * 4; ++s) {
+    const int i = s * 32 + lane;
+    rowv[s] = i < n ? __ldg(p.toks + 2 * (w.tl.y + i) + 1) : 0;
+  }
+  const int zrow0 = n << lg, zrows = (nq - n) << lg;  // tile rows R = i * G + g over the active halves
+  for (int c = lane; c < zrows * NDH * 8; c += 32) {
+    const int R = zrow0 + c / (NDH * 8), rest = c % (NDH * 8);
+    const uint32_t dst = dst0 + (R >> 7) * C::TILE + (rest >> 3) * 128 * 128 + (R & 127) * 128 + ((rest & 7) << 4);
+    asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(dst), "r"(0) : "memory");
+  }
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  __syncwarp();
+  if (lane == 0) mbar_arrive_expect_tx(full, n * G * 128 * NDH);
+  __syncwarp();
+#pragma unroll
+  for (int s = 0; s < C::NH_ * 4; ++s) {
+    const int i = s * 32 + lane;
+    if (i < n) {
+      const int row = rowv[s];
+      if (row < 0 || row >= p.rows) atomicOr(p.status, NF_STATUS_BAD_SHARED);
+      const int R = i << lg;
+      const uint32_t d = dst0 + (R >> 7) * C::TILE + (R & 127) * 128;
+#pragma unroll
+      for (int dh = 0; dh < NDH; ++dh) {
+        if constexpr (D_ == 64)
+          tma_load_3d(d, tq, 0, w.kvh * G, row, full, pol);
+        else
+          tma_load_4d(d + dh * 128 * 128, tq, 0, dh, w.kvh * G, row, full, pol);
+      }
+    }
+  }
+}
+
 // The producer warp: every lane runs the loop (waits included), lanes 0..7
 // load block ids and issue the tensor copies.
-template <int D_>
+template <int D_, bool CASC>
 __device__ void pf_producer(const PrefillParams& p, const CUtensorMap* tq, const CUtensorMap* tk,
                             const CUtensorMap* tv, const PfBars& bar, uint32_t q_s, uint32_t k_s, uint32_t v_s,
                             PfItemRing& ring) {
@@ -335,43 +438,58 @@ __device__ void pf_producer(const PrefillParams& p, const CUtensorMap* tq, const
   const uint64_t pol = l2_evict_last();  // every query tile of a chunk reads the same keys
   const uint64_t pol_q = l2_evict_first();  // queries are read once
   Ring qr, kr, vr;
-  int it;
+  int it, claims = 0;
   int4 itl;
-  while (pf_claim_item(p, ring, it, itl)) {
-    const PfItem w(p, it, itl);
+  int2 ikr;
+  while (pf_claim_item<CASC>(p, ring, it, itl, ikr, claims)) {
+    const PfItem<CASC> w(p, it, itl, ikr);
+    if (w.bad) {
+      if (lane == 0) atomicOr(p.status, NF_STATUS_BAD_SHARED);
+      continue;
+    }
     // the item's query rows, both halves (one copy per half and 64-element part)
     if (!mbar_wait(bar.q_empty(qr.st), qr.ph ^ 1, p.status)) return;
-    const int nq = w.n_half * NDH;
-    if (lane == 0) mbar_arrive_expect_tx(bar.q_full(qr.st), nq * 128 * 128);
-    __syncwarp();
-    if (lane < nq) {
-      const int h = lane / NDH, dh = lane - h * NDH;
-      const uint32_t dst = q_s + (qr.st * C::NH_ + h) * C::TILE + dh * 128 * 128;
-      const int row0 = w.tl.y + h * p.TT;
-      if constexpr (D_ == 64)
-        tma_load_3d(dst, tq, 0, w.kvh * p.G, row0, bar.q_full(qr.st), pol_q);
-      else
-        tma_load_4d(dst, tq, 0, dh, w.kvh * p.G, row0, bar.q_full(qr.st), pol_q);
+    const uint32_t q_full = bar.q_full(qr.st);
+    // block ids of key tile 0, requested before the query copies
+    const int* btrow = p.bt + (long long)w.tl.x * p.max_blocks;
+    int cur = pf_block_id(p, btrow, 0, w.nkeys, w.k0, lane);
+    if constexpr (CASC) {
+      // q may come from the launch before this one on the stream (a projection
+      // launched ahead with programmatic serialization): wait for it here,
+      // after the setup and the first records, before the first query copy
+      if (claims == 1) pdl_wait();
+      pf_gather_queries<D_>(p, w, tq, q_s + qr.st * C::NH_ * C::TILE, q_full, pol_q, lane);
+    } else {
+      const int nq = w.n_half * NDH;
+      if (lane == 0) mbar_arrive_expect_tx(q_full, nq * 128 * 128);
+      __syncwarp();
+      if (lane < nq) {
+        const int h = lane / NDH, dh = lane - h * NDH;
+        const uint32_t dst = q_s + (qr.st * C::NH_ + h) * C::TILE + dh * 128 * 128;
+        const int row0 = w.tl.y + h * p.TT;
+        if constexpr (D_ == 64)
+          tma_load_3d(dst, tq, 0, w.kvh * p.G, row0, q_full, pol_q);
+        else
+          tma_load_4d(dst, tq, 0, dh, w.kvh * p.G, row0, q_full, pol_q);
+      }
     }
     qr.next(C::QST);
-    const int* btrow = p.bt + (long long)w.tl.x * p.max_blocks;
-    int cur = pf_block_id(p, btrow, 0, w.nkeys, lane);
     for (int j = 0; j < w.nkt; ++j) {
       const int nb = min(8, (w.nkeys - j * 128 + 15) >> 4);
       if (!mbar_wait(bar.k_empty(kr.st), kr.ph ^ 1, p.status)) return;
-      pf_load_tile<D_>(p, tk, k_s + kr.st * C::TILE, bar.k_full(kr.st), cur, j, nb, w.kvh, pol, lane);
+      pf_load_tile<D_>(p, tk, k_s + kr.st * C::TILE, bar.k_full(kr.st), cur, j, nb, w.kvh, w.k0, pol, lane);
       kr.next(C::KST);
       if (!mbar_wait(bar.v_empty(vr.st), vr.ph ^ 1, p.status)) return;
-      pf_load_tile<D_>(p, tv, v_s + vr.st * C::TILE, bar.v_full(vr.st), cur, j, nb, w.kvh, pol, lane);
+      pf_load_tile<D_>(p, tv, v_s + vr.st * C::TILE, bar.v_full(vr.st), cur, j, nb, w.kvh, w.k0, pol, lane);
       vr.next(C::VST);
-      if (j + 1 < w.nkt) cur = pf_block_id(p, btrow, j + 1, w.nkeys, lane);
+      if (j + 1 < w.nkt) cur = pf_block_id(p, btrow, j + 1, w.nkeys, w.k0, lane);
     }
   }
 }
 
 // The MMA warp: every lane runs the loop and its waits; lane 0 issues the
 // MMAs and the commits that track them.
-template <int D_>
+template <int D_, bool CASC>
 __device__ void pf_mma(const PrefillParams& p, const PfBars& bar, uint32_t tmem, uint32_t q_s, uint32_t k_s,
                        uint32_t v_s, bool bf, PfItemRing& ring) {
   using C = PfCfg<D_>;
@@ -424,8 +542,10 @@ __device__ void pf_mma(const PrefillParams& p, const PfBars& bar, uint32_t tmem,
   };
   int it;
   int4 itl;
-  while (ring.next(it, itl, p.status)) {
-    const PfItem w(p, it, itl);
+  int2 ikr;
+  while (ring.next(it, itl, ikr, p.status)) {
+    const PfItem<CASC> w(p, it, itl, ikr);
+    if (w.bad) continue;
     int vprev = -1;  // V stage of tile j-1
     if (!mbar_wait(bar.q_full(qr.st), qr.ph, p.status)) return;
     for (int j = 0; j < w.nkt; ++j) {
@@ -478,7 +598,7 @@ __device__ void pf_mma(const PrefillParams& p, const PfBars& bar, uint32_t tmem,
   }
 }
 
-template <typename T, int D_>
+template <typename T, int D_, bool CASC>
 __device__ void pf_softmax(const PrefillParams& p, const PfBars& bar, uint32_t tmem, uint32_t v_s, int h,
                            PfItemRing& ring) {
   using C = PfCfg<D_>;
@@ -502,18 +622,34 @@ __device__ void pf_softmax(const PrefillParams& p, const PfBars& bar, uint32_t t
   Ring vr;  // V ring position of this CTA's current tile (every item advances it)
   int it;
   int4 itl;
-  while (ring.next(it, itl, p.status)) {
-    const PfItem w(p, it, itl);
-    if (h == 0 && w.tl.z > p.NH * p.TT && threadIdx.x == 128) atomicOr(p.status, NF_STATUS_BAD_TILE);
+  int2 ikr;
+  while (ring.next(it, itl, ikr, p.status)) {
+    const PfItem<CASC> w(p, it, itl, ikr);
+    if (w.bad) continue;
+    if (!CASC && h == 0 && w.tl.z > p.NH * p.TT && threadIdx.x == 128) atomicOr(p.status, NF_STATUS_BAD_TILE);
     const Ring vlast = vr.ahead(w.nkt - 1, C::VST);  // V stage of the item's last tile
     vr = vr.ahead(w.nkt, C::VST);
     const bool active = h < w.n_half;
     const int nkt = active ? w.nkt_h[h] : 0;
     // both warps of a quad take one turn per key tile of the item's longer half
     const int rounds = kTurns ? w.nkt_h[w.n_half - 1] : nkt;
-    const int tok = h * p.TT + row / G, hd = row % G;
-    const bool valid = tok < min(w.tl.z, p.NH * p.TT) && w.tl.y + tok < p.rows;
-    const int qpos = w.tl.w + tok;
+    const int tok = h * p.TT + row / G, hd = row % G;  // cascade: tok = the query's index in the group
+    const bool valid = CASC ? tok < w.tl.z : (tok < min(w.tl.z, p.NH * p.TT) && w.tl.y + tok < p.rows);
+    // the last visible key of the row, counted from the item's first key
+    const int qpos = CASC ? w.nkeys - 1 : w.tl.w + tok;
+    // cascade: the row's partial record, its three dependent loads issued now
+    // so that they complete while the item's tiles stream
+    float* rec = nullptr;
+    if (CASC && valid) {
+      const int item = __ldg(p.toks + 2 * (w.tl.y + tok));
+      const int n_items = min(__ldg(p.counts), p.max_items);
+      const int n_slots = min(__ldg(p.counts + 3), p.max_units);
+      const int slot = item >= 0 && item < n_items ? __ldg(p.items + 4 * item + 3) + w.tl.w : -1;
+      if (slot < 0 || slot >= n_slots)
+        atomicOr(p.status, NF_STATUS_UNIT_OVERFLOW);
+      else
+        rec = p.ws + ((long long)slot * p.Hq + (long long)w.kvh * G + hd) * (D_ + 4);
+    }
     float m = kPfNegInf, l = 0.f;
     for (int j = 0; j < rounds; ++j) {
       const bool has = j < nkt;
@@ -633,10 +769,29 @@ __device__ void pf_softmax(const PrefillParams& p, const PfBars& bar, uint32_t t
       if (lane == 0) mbar_arrive(bar.p_full(h));
     }
     if (!active) continue;
-    // epilogue: O_h / l for the valid rows
+    // epilogue: O_h / l for the valid rows (cascade: the row's split-K part record)
     if (!mbar_wait(bar.o_done(h), n_o & 1, p.status)) return;
     ++n_o;
     tc_fence_after();
+    if constexpr (CASC) {
+#pragma unroll
+      for (int c = 0; c < D_ / 32; ++c) {
+        uint32_t o[32];
+        tmem_ld32(o_addr + c * 32, o);
+        tmem_wait_ld();
+        tmem_reg_fence(o);
+        if (rec) {
+          float4* r4 = reinterpret_cast<float4*>(rec + c * 32);
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            __stcg(r4 + i, make_float4(__uint_as_float(o[4 * i]), __uint_as_float(o[4 * i + 1]),
+                                       __uint_as_float(o[4 * i + 2]), __uint_as_float(o[4 * i + 3])));
+        }
+      }
+      if (rec) __stcg(reinterpret_cast<float2*>(rec + D_), make_float2(m, l));
+      tc_fence_before();
+      continue;
+    }
     const float inv = l > 0.f ? 1.f / l : 0.f;
     T* dst = reinterpret_cast<T*>(p.out) + (long long)(w.tl.y + tok) * p.out_stride + (long long)(w.kvh * G + hd) * D_;
 #pragma unroll
@@ -668,7 +823,7 @@ __device__ void pf_softmax(const PrefillParams& p, const PfBars& bar, uint32_t t
   if (p.n_peers) __threadfence_system();
 }
 
-template <typename T, int D_>
+template <typename T, int D_, bool CASC>
 __global__ void __launch_bounds__(PfCfg<D_>::THREADS, PfCfg<D_>::MINB)
     prefill_attention_kernel(const PrefillParams p, const __grid_constant__ CUtensorMap tq,
                              const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv) {
@@ -678,6 +833,11 @@ __global__ void __launch_bounds__(PfCfg<D_>::THREADS, PfCfg<D_>::MINB)
   const uint32_t hdr = smem_u32(base);
   const PfBars bar(hdr);
   const int warp = threadIdx.x >> 5;
+  // cascade: the decode launch that follows may start as this grid's CTAs leave
+  if (CASC) pdl_launch_dependents();
+  // cascade: the first item of this CTA is item blockIdx.x; its task record is fetched during the setup
+  if (CASC && threadIdx.x == 32 && (int)blockIdx.x < p.n_tiles * p.Hkv)
+    asm volatile("prefetch.global.L1 [%0];" ::"l"(p.tasks + 8 * (blockIdx.x / p.Hkv)));
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::KST; ++s) {
       mbar_init(bar.k_full(s), 1);
@@ -714,29 +874,32 @@ __global__ void __launch_bounds__(PfCfg<D_>::THREADS, PfCfg<D_>::MINB)
   if (warp < 4) {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(C::REGS_CTRL));
     if (warp == 0)
-      pf_producer<D_>(p, &tq, &tk, &tv, bar, q_s, k_s, v_s, ring);
+      pf_producer<D_, CASC>(p, &tq, &tk, &tv, bar, q_s, k_s, v_s, ring);
     else if (warp == 1)
-      pf_mma<D_>(p, bar, tmem, q_s, k_s, v_s, std::is_same<T, __nv_bfloat16>::value, ring);
+      pf_mma<D_, CASC>(p, bar, tmem, q_s, k_s, v_s, std::is_same<T, __nv_bfloat16>::value, ring);
   } else {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(C::REGS_SOFTMAX));
-    pf_softmax<T, D_>(p, bar, tmem, v_s, (warp - 4) >> 2, ring);
+    pf_softmax<T, D_, CASC>(p, bar, tmem, v_s, (warp - 4) >> 2, ring);
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   if (warp == 1) tmem_dealloc(tmem, C::TMEM_COLS);
+  // cascade: the grid ends after the launch before it, so that a launch waiting for this grid sees that one's
+  // writes too
+  if (CASC && threadIdx.x == 0) pdl_wait();
   // every claim of this CTA is made; the last CTA out rewinds the queue for the next launch
-  if (threadIdx.x == 0 && atomicAdd(p.queue + 1, 1) == (int)gridDim.x - 1) {
+  if (!CASC && threadIdx.x == 0 && atomicAdd(p.queue + 1, 1) == (int)gridDim.x - 1) {
     atomicExch(p.queue, 0);
     atomicExch(p.queue + 1, 0);
   }
 }
 
-template <typename T, int D_>
+template <typename T, int D_, bool CASC = false>
 static int launch_prefill(const PrefillParams& p, const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                           int n_items, cudaStream_t st) {
   using C = PfCfg<D_>;
-  auto kern = prefill_attention_kernel<T, D_>;
+  auto kern = prefill_attention_kernel<T, D_, CASC>;
   cudaError_t e = prepare_launch(reinterpret_cast<const void*>(kern), (int)C::SMEM, C::THREADS, nullptr);
   if (e != cudaSuccess) return fail(NF_ECUDA, "nf_prefill_attention: smem attribute: %s", cudaGetErrorString(e));
   // setmaxnreg moves registers between warpgroups within the launch total:
@@ -752,8 +915,83 @@ static int launch_prefill(const PrefillParams& p, const CUtensorMap& tq, const C
                 "split needs %d", regs, C::LAUNCH_REGS);
   long long grid = n_items;
   if (grid > (long long)sm_count() * C::MINB) grid = (long long)sm_count() * C::MINB;
-  kern<<<(int)grid, C::THREADS, C::SMEM, st>>>(p, tq, tk, tv);
-  return check_launch("nf_prefill_attention");
+  if (!CASC) {
+    kern<<<(int)grid, C::THREADS, C::SMEM, st>>>(p, tq, tk, tv);
+    return check_launch("nf_prefill_attention");
+  }
+  // the cascade: programmatic stream serialization (the kernel waits for the
+  // launch before it ahead of its first read of q), plain stream order where
+  // the launch refuses the attribute
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3(C::THREADS);
+  cfg.dynamicSmemBytes = C::SMEM;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, kern, p, tq, tk, tv);
+  if (e != cudaSuccess) {
+    (void)cudaGetLastError();
+    cfg.numAttrs = 0;
+    e = cudaLaunchKernelEx(&cfg, kern, p, tq, tk, tv);
+  }
+  if (e != cudaSuccess) return fail(NF_ECUDA, "nf_cascade_attention: %s", cudaGetErrorString(e));
+  return check_launch("nf_cascade_attention");
+}
+
+// nf_cascade_attention on the tensor cores: 16-bit pools, head_dim 64/128,
+// 1/2/4/8 query heads per KV head, block size a multiple of 16; a task
+// holds up to 256 / G queries and any whole number of 16-key groups.
+int cascade_tensor_core(const CascTcArgs& a) {
+  if (a.dtype != NF_BF16 && a.dtype != NF_F16) return NF_EUNSUPPORTED;
+  if ((a.D != 64 && a.D != 128) || a.bs % 16) return NF_EUNSUPPORTED;
+  const int G = a.Hq / a.Hkv;
+  if (G != 1 && G != 2 && G != 4 && G != 8) return NF_EUNSUPPORTED;
+  if (a.n_tasks == 0) return ok();
+  // tq: boxes of one query row's G heads (the rows are gathered one copy per query)
+  CUtensorMap tq, tk, tv;
+  if (!encode_rows_map(&tq, a.q, a.dtype, a.D, a.Hq, a.q_rows, a.q_stride, G, 1) ||
+      !encode_pool_map(&tk, a.kp, a.dtype, a.D, a.Hkv, a.bs, a.num_blocks, 1, false) ||
+      !encode_pool_map(&tv, a.vp, a.dtype, a.D, a.Hkv, a.bs, a.num_blocks, 1, false))
+    return fail(NF_ECUDA, "nf_cascade_attention: tensor map encoding failed");
+  PrefillParams p = {};
+  p.out = nullptr;
+  p.q = static_cast<const char*>(a.q);
+  p.q_stride = a.q_stride;
+  p.rows = a.q_rows;
+  p.Hq = a.Hq;
+  p.Hkv = a.Hkv;
+  p.G = G;
+  p.TT = 128 / G;
+  p.NH = pf_halves(a.D);
+  p.bs = a.bs;
+  p.num_blocks = a.num_blocks;
+  p.bt = a.bt;
+  p.max_blocks = a.max_blocks;
+  p.n_tiles = a.n_tasks;
+  p.order = nullptr;
+  p.queue = nullptr;
+  p.scale_log2 = a.scale_log2;
+  p.status = a.status;
+  p.n_peers = 0;
+  p.tasks = a.tasks;
+  p.toks = a.toks;
+  p.n_toks = a.n_toks;
+  p.items = a.items;
+  p.counts = a.counts;
+  p.ws = a.ws;
+  p.max_items = a.max_items;
+  p.max_units = a.max_units;
+  const int n_items = a.n_tasks * a.Hkv;
+  cudaStream_t st = static_cast<cudaStream_t>(a.stream);
+  if (a.dtype == NF_BF16)
+    return a.D == 64 ? launch_prefill<__nv_bfloat16, 64, true>(p, tq, tk, tv, n_items, st)
+                     : launch_prefill<__nv_bfloat16, 128, true>(p, tq, tk, tv, n_items, st);
+  return a.D == 64 ? launch_prefill<__half, 64, true>(p, tq, tk, tv, n_items, st)
+                   : launch_prefill<__half, 128, true>(p, tq, tk, tv, n_items, st);
 }
 
 }  // namespace nf

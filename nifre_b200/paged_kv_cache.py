@@ -153,6 +153,7 @@ class PagedKVCache:
         # decode sequences that share leading blocks get those keys attended once per group (cascade)
         self.enable_cascade = True
         self._cascade_memo = None  # (batch key, grouping) of the last step planned
+        self._cascade_limit_memo = {}  # query heads per KV head -> cascade_limits()
         self.prefix_cache_max_entries = prefix_cache_max_entries
         self._num_blocks_override = num_blocks
         self.batch_size = 0
@@ -327,9 +328,13 @@ class PagedKVCache:
 
     # cascade over shared keys: at least this many shared keys and two sequences
     CASCADE_MIN_KEYS = 64
-    CASCADE_ROWS = 128  # query rows per nf_cascade_attention CTA
-    CASCADE_MAX_KEYS = 256  # keys per nf_cascade_attention task
-    CASCADE_WAVES = 2  # cascade CTAs per SM aimed for (two are resident at once)
+    # the mma.sync cascade kernel (group sizes the tensor-core path does not take): 128 query rows and at most
+    # 256 keys per task, two CTAs per SM aimed for
+    CASCADE_ROWS = 128
+    CASCADE_MAX_KEYS = 256
+    CASCADE_WAVES = 2
+    # the tensor-core path: one (task, KV head) item per SM aimed for, each at least this many keys long
+    CASCADE_TC_MIN_KEYS = 256
 
     def cascade_supported(self, q_heads: int | None) -> bool:
         """True when nf_cascade_attention serves this cache with q_heads query heads."""
@@ -337,6 +342,18 @@ class PagedKVCache:
             return False
         return (self.dtype in (torch.bfloat16, torch.float16) and self.head_dim in (64, 128)
                 and q_heads // self.n_heads <= self.CASCADE_ROWS and self.block_size % 16 == 0)
+
+    def cascade_limits(self, group: int) -> tuple[int, int, bool]:
+        """(query rows, keys) of the largest nf_cascade_attention task for ``group`` query heads per KV head,
+        and whether the tasks run on the tensor cores."""
+        memo = self._cascade_limit_memo
+        if group not in memo:
+            rows, keys = ctypes.c_int32(0), ctypes.c_int32(0)
+            _lib.check(_lib.load().nf_cascade_limits(_lib.dtype_code(self.dtype), group * self.n_heads, self.n_heads,
+                                                     self.head_dim, self.block_size, ctypes.byref(rows),
+                                                     ctypes.byref(keys)), "nf_cascade_limits")
+            memo[group] = (rows.value, keys.value, rows.value > self.CASCADE_ROWS)
+        return memo[group]
 
     def _cascade_groups(self, slots, q_lens, q_starts, ctx, dec, group: int, epochs=None):
         """Decode sequences that start with the same physical blocks, and the cascade work over those keys.
@@ -373,7 +390,8 @@ class PagedKVCache:
                 continue
             blocks = self.block_tables[int(slots[i])]._physical_blocks
             buckets.setdefault(blocks[0], []).append(i)
-        per_cta = self.CASCADE_ROWS // group
+        max_rows, max_keys, tensor_cores = self.cascade_limits(group)
+        per_cta = max_rows // group
         cuts = []  # (members, shared keys)
         for members in buckets.values():
             if len(members) < 2:
@@ -393,11 +411,14 @@ class PagedKVCache:
         tasks, toks = [], []
         if cuts:
             total = sum(p for _, p in cuts)
-            want = max(len(cuts), round(self.CASCADE_WAVES * self.sm_count / self.n_heads))
+            waves = 1 if tensor_cores else self.CASCADE_WAVES
+            want = max(len(cuts), round(waves * self.sm_count / self.n_heads))
             tok_off = np.cumsum(q_lens) - q_lens
             for members, p in cuts:
                 tiles = p // 16
-                nc = max(1, round(want * p / total), -(-p // self.CASCADE_MAX_KEYS))
+                nc = max(1, round(want * p / total), -(-p // max_keys))
+                if tensor_cores:  # a tensor-core item has a fixed cost: keep parts at least this long
+                    nc = max(1, min(nc, p // self.CASCADE_TC_MIN_KEYS))
                 nc = min(nc, tiles)
                 edges = [16 * (tiles * c // nc) for c in range(nc + 1)]
                 first = len(toks)
@@ -711,7 +732,7 @@ class PagedKVCache:
             if plan.n_casc_tasks:
                 # partials over the shared keys, merged by the decode launch with each query's own keys
                 _lib.check(lib.nf_cascade_attention(
-                    ws.data_ptr(), ws.numel(), qp, qs, kp, vp, self._dt_code,
+                    ws.data_ptr(), ws.numel(), qp, qs, q.shape[0], kp, vp, self._dt_code,
                     hq, self.n_heads, D, self.block_size, self.num_blocks, self._bt_ptr,
                     self.max_blocks_per_seq, plan.items.data_ptr(), plan.counts.data_ptr(), max_items,
                     plan.max_units, plan.casc_tasks.data_ptr(),

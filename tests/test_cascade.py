@@ -51,6 +51,7 @@ def test_cascade_groups_host():
     tables.append([4000, 4001])         # alone: no cascade
     ctx.append(20)
     c = _host_cache(tables, ctx, bs)
+    c.cascade_limits = lambda group: (128, 256, False)  # the mma.sync kernel's task sizes
     S = len(tables)
     slots = np.arange(S)
     q_lens = np.ones(S, dtype=np.int64)
@@ -86,6 +87,7 @@ def test_cascade_groups_host():
     assert max(t[2] for t in tasks8) == 16
     # a long shared run is cut into ranges of at most CASCADE_MAX_KEYS keys
     long_c = _host_cache([list(range(200)) + [900 + i] for i in range(4)], [200 * bs + 7] * 4, bs)
+    long_c.cascade_limits = c.cascade_limits
     lt = long_c._cascade_groups(np.arange(4), np.ones(4, np.int64), np.arange(4), np.full(4, 200 * bs + 7),
                                 np.ones(4, bool), 4)[2]
     assert len(lt) == 37 and max(t[5] - t[4] for t in lt) <= 256  # 37 ranges of 5-6 tiles
@@ -96,6 +98,33 @@ def test_cascade_groups_host():
     assert c._cascade_groups(slots, q_lens, q_starts, np.asarray(ctx) - 1000, dec, 8) is not again
     c.block_tables[3].epoch += 1
     assert c._cascade_groups(slots, q_lens, q_starts, np.asarray(ctx), dec, 8) is not again
+
+
+def test_cascade_limits_and_tensor_core_groups_host():
+    """nf_cascade_limits: 256 query rows and any key count on the tensor-core path (16-bit pools, D 64/128,
+    G in {1, 2, 4, 8}), 128 rows and 256 keys on the mma.sync kernel; tensor-core tasks aim at one item per
+    SM with at least CASCADE_TC_MIN_KEYS keys each."""
+    bs = 16
+    c = _host_cache([[0]], [1], bs)
+    assert c.cascade_limits(4) == (256, 1 << 30, True)
+    assert c.cascade_limits(8) == (256, 1 << 30, True)
+    assert c.cascade_limits(3) == (128, 256, False)
+    assert c.cascade_limits(16) == (128, 256, False)
+    # 70 sequences on a 2048-key prefix, G = 4: groups of at most 64; 148 SMs / 8 KV heads = 18 items wanted
+    tables = [list(range(128)) + [500 + i] for i in range(70)]
+    ctx = [128 * bs + 9] * 70
+    c = _host_cache(tables, ctx, bs)
+    S = len(tables)
+    shared, nparts, tasks, toks = c._cascade_groups(np.arange(S), np.ones(S, np.int64), np.arange(S),
+                                                    np.asarray(ctx), np.ones(S, bool), 4)
+    groups = sorted({(t[1], t[2]) for t in tasks})
+    assert [n for _, n in groups] == [64, 6]
+    assert shared.tolist() == [2048] * 70
+    for first, n in groups:
+        mine = [t for t in tasks if t[1] == first]
+        assert mine[0][4] == 0 and mine[-1][5] == 2048 and all(a[5] == b[4] for a, b in zip(mine, mine[1:]))
+        assert all(t[5] - t[4] >= c.CASCADE_TC_MIN_KEYS for t in mine)
+    assert len(tasks) == 16  # 9 parts each, at most 2048 / 256 = 8
 
 
 def _shared_prefix_cache(hq, hkv, D, prefixes, n_per, suffix, dtype, seed, tail_div=None):
@@ -128,7 +157,8 @@ def _shared_prefix_cache(hq, hkv, D, prefixes, n_per, suffix, dtype, seed, tail_
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("D,hq,hkv", [(64, 32, 8), (128, 32, 8), (64, 8, 8), (64, 16, 2)])
+@pytest.mark.parametrize("D,hq,hkv", [(64, 32, 8), (128, 32, 8), (64, 8, 8), (64, 16, 2),  # tensor cores
+                                       (64, 24, 8), (128, 12, 2)])  # G = 3 and 6: the mma.sync kernel
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 def test_cascade_decode_vs_oracle(D, hq, hkv, dtype):
     """A decode step over shared prefixes: cascade + decode merge equals the oracle per sequence."""
@@ -155,7 +185,8 @@ def test_cascade_decode_vs_oracle(D, hq, hkv, dtype):
 @pytest.mark.gpu
 def test_cascade_matches_plain_decode_and_many_groups():
     """Same step with and without the cascade (two caches built alike): outputs agree; 40 sequences on one
-    prefix with G = 4 make a group of 32 and one of 8; a long prefix gives several key ranges per group."""
+    prefix with G = 4 make one group (the tensor-core path takes 256 / G = 64 per group); a long prefix gives
+    several key ranges per group."""
     outs = []
     for casc in (True, False):
         cache, g = _shared_prefix_cache(32, 8, 64, [2048], 40, (1, 40), torch.bfloat16, seed=5)
@@ -165,7 +196,7 @@ def test_cascade_matches_plain_decode_and_many_groups():
         assert (plan.n_casc_tasks > 0) == casc
         if casc:
             tasks = plan.casc_tasks.view(-1, 8).cpu().numpy()
-            assert sorted({(int(t[1]), int(t[2])) for t in tasks}) == [(0, 32), (32, 8)]
+            assert sorted({(int(t[1]), int(t[2])) for t in tasks}) == [(0, 40)]
             assert plan.n_casc_tasks > 2
         q = torch.randn(B, 32 * 64, generator=g).to(torch.bfloat16).to(DEV)
         k = torch.randn(B, 8 * 64, generator=g).to(torch.bfloat16).to(DEV)
@@ -191,7 +222,7 @@ def test_cascade_bad_task_flagged():
     bad = torch.tensor([0, 0, 1000, 0, 0, 64, 0, 0], dtype=torch.int32, device=DEV)  # more queries than records
     q = torch.zeros(B, 32 * 64, dtype=torch.bfloat16, device=DEV)
     _lib.check(lib.nf_cascade_attention(
-        ws.data_ptr(), ws.numel(), q.data_ptr(), q.stride(0), cache.k[0].data_ptr(), cache.v[0].data_ptr(),
+        ws.data_ptr(), ws.numel(), q.data_ptr(), q.stride(0), q.shape[0], cache.k[0].data_ptr(), cache.v[0].data_ptr(),
         _lib.NF_BF16, 32, 8, 64, 16, cache.num_blocks, cache.bt_dev.data_ptr(), cache.max_blocks_per_seq,
         plan.items.data_ptr(), plan.counts.data_ptr(), B, plan.max_units, bad.data_ptr(), 1,
         plan.casc_toks.data_ptr(), plan.n_casc_toks, 0.125,
