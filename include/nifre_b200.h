@@ -155,10 +155,13 @@ int nf_selftest_umma(const void* A, const void* B, float* C, int32_t N, int32_t 
  * of cascade parts that nf_cascade_attention computes over them ({0, 0}:
  * none).  Such an item's parts 0..nc-1 are those cascade parts (partial
  * slots, no unit records); its units cover keys [shared, kv_len) as parts
- * nc, nc+1, ...
+ * nc, nc+1, ...; when one unit covers them all, that unit's record carries
+ * the part count negated, and the tensor-map decode kernel merges the
+ * cascade parts in that unit's epilogue.
  * counts[4]: counts[0] = n_tokens, counts[1] = number of units in the list,
- * counts[2] = 1 if some item has more than one part (the attention launch
- * then merges), counts[3] = number of partial slots (units + cascade parts).
+ * counts[2] = bit 0: some item has more than one part, bit 1: some item has
+ * more than one unit (the attention launch then merges at its end),
+ * counts[3] = number of partial slots (units + cascade parts).
  */
 int nf_pack_step(const int32_t* seqs, int32_t n_seqs,
                  const int32_t* patches, int32_t n_patches,
@@ -360,8 +363,9 @@ int nf_ipc_close(void* ptr, int64_t offset);
  * multiple of 16.  nf_cascade_limits gives the largest task: with 1, 2, 4
  * or 8 query heads per KV head (G) the tasks run on the tensor cores (the
  * prefill kernel's tcgen05 pipeline, one (task, KV head) item at a time per
- * CTA: up to 256 / G queries and any whole number of 16-key groups, q rows
- * 16-byte aligned); other group sizes use an mma.sync kernel (one CTA per
+ * CTA: up to 256 / G queries and any whole number of 16-key groups; q rows
+ * 16-byte aligned);
+ * other group sizes use an mma.sync kernel (one CTA per
  * task and KV head: up to 128 / G queries and 256 keys) launched with
  * programmatic stream serialization: the launch before it on the stream
  * must not write the shared blocks, q, items or counts (the step's KV

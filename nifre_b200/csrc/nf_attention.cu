@@ -115,7 +115,7 @@ __device__ __forceinline__ void loader_enter(const AttnParams& p, Loader& L, uns
   c.t0 = L.nb.x;
   c.t1 = L.nb.y;
   c.unit_base = L.nb.z;
-  c.nparts = L.nb.w;
+  c.nparts = abs(L.nb.w);  // negative: the item's only unit beside cascade parts (merged at the end here)
   L.t = c.t0;
   L.lb = c.t0 / p.bs;
   L.off = c.t0 - L.lb * p.bs;
@@ -652,7 +652,7 @@ __global__ void __launch_bounds__(256) paged_attention_kernel(const AttnParams p
   if constexpr (MMA) done = warp_mma<T, D_, MT>(p, ring, fifo, total);
   else done = warp_simt<T, DPL>(p, ring, ring_ptr, fifo, total);
   if ((threadIdx.x & 31) == 0 && done) atomicAdd(&cta_done, done);
-  finish_launch<T, 8>(p, &cta_done, total);
+  finish_launch<T, 8>(p, &cta_done, total, 1);
 }
 
 // ---------------------------------------------------------------- host plan

@@ -352,13 +352,17 @@ __device__ void tma_consumer(const AttnParams& p, unsigned char* base, int box_b
       c.t0 = r.t0;
       c.t1 = r.t1;
       c.unit_base = r.unit_base;
-      c.nparts = r.nsplits;
+      c.nparts = abs(r.nsplits);
       c.kvh = r.hg * p.HG + warp;
       c.part = r.part;
-      if (r.nsplits == 1)
+      if (c.nparts == 1) {
         mma_store_output<T, D_>(p, c, o, l0, l1);
-      else
+      } else {
+        // the part record also when this unit merges the item's cascade parts
+        // itself (nsplits < 0): a launch that merges at its end reads it
         mma_store_part<T, D_>(p, c, o, m0, m1, l0, l1);
+        if (r.nsplits < 0) mma_merge_cascade<T, D_>(p, c, o, m0, m1, l0, l1);
+      }
     }
   }
 }
@@ -389,7 +393,7 @@ __global__ void __launch_bounds__(kTmaMaxThreads, 1) paged_attention_tma_kernel(
   } else if ((threadIdx.x & 31) == 0) {
     cta_done = tma_producer<T, D_>(p, &tk, &tv, base, total, box_bytes, q_bytes);
   }
-  finish_launch<T, 8>(p, &cta_done, total);
+  finish_launch<T, 8>(p, &cta_done, total, 2);
 }
 
 // ---------------------------------------------------------------- host side

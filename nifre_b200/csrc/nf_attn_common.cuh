@@ -176,11 +176,15 @@ __device__ void merge_chunk(const AttnParams& p, const Work& c, int c0) {
 // The counts and each warp's first merge task's item records (the step's
 // pack wrote them before the launch) are requested before the wait, and
 // each task's successor's records before the task's parts, so that a merge
-// costs about one round trip once the wait ends.  The last CTA out resets
-// the queue and the counts for the next launch.  The wait needs every CTA
-// resident at once: the kernels are launched cooperatively.
+// costs about one round trip once the wait ends.  `merge_bits` selects the
+// pack's flags (counts[2]) that call for this merge: bit 0, an item with
+// several parts; bit 1, an item with several units (a kernel whose units
+// merge an item's cascade parts themselves when they are its only unit).
+// The last CTA out resets the queue and the counts for the next launch.  The
+// wait needs every CTA resident at once: the kernels are launched
+// cooperatively.
 template <typename T, int PB>
-__device__ void finish_launch(const AttnParams& p, int* cta_done, int total) {
+__device__ void finish_launch(const AttnParams& p, int* cta_done, int total, int merge_bits) {
   __shared__ int go;
   const int c_items = __ldg(p.counts), c_multi = __ldg(p.counts + 2), c_units = __ldg(p.counts + 3);
   const int groups = (p.G * (p.D >> 2) + 31) >> 5;
@@ -202,8 +206,7 @@ __device__ void finish_launch(const AttnParams& p, int* cta_done, int total) {
   int nx;
   records(task0, it, nx);
   __syncthreads();  // the CTA's output and part stores are issued
-  // set by the pack when an item has several parts
-  const bool merge = c_multi != 0 && !parts_refused(p);
+  const bool merge = (c_multi & merge_bits) != 0 && !parts_refused(p);
   if (threadIdx.x == 0) {
     __threadfence();
     const int mine = *cta_done;
@@ -317,6 +320,76 @@ __device__ __forceinline__ void mma_store_part(const AttnParams& p, const Work& 
       __stcg(wb + (n0 + 1) * DP + D_ + 1, l1);
     }
   }
+}
+
+// The output rows of an item whose only unit this is, beside nc = nparts - 1
+// cascade parts (slots unit_base .. unit_base + nc - 1, written by the
+// cascade launch before this one): the parts are merged into this unit's
+// running state (o, m, l; l summed over the lanes) in registers -- PB parts'
+// loads in flight at a time, rescaled as the maximum grows -- and the rows
+// written, with no wait for any other worker.
+template <typename T, int D_>
+__device__ __forceinline__ void mma_merge_cascade(const AttnParams& p, const Work& c, float (&o)[D_ / 16][4],
+                                                  float m0, float m1, float l0, float l1) {
+  constexpr int KS = D_ / 16;
+  constexpr int PB = D_ == 64 ? 4 : 2;
+  const int lane = threadIdx.x & 31;
+  const int n0 = 2 * (lane & 3), tq = lane >> 2;
+  const bool h0 = n0 < p.G, h1 = n0 + 1 < p.G;
+  const int DP = D_ + 4, nc = c.nparts - 1;
+  const float* wb = p.ws + ((long long)c.unit_base * p.Hq + c.kvh * p.G) * DP;
+  const long long ps = (long long)p.Hq * DP;  // between consecutive parts
+  float M0 = m0, M1 = m1;
+  for (int j = 0; j < nc; j += PB) {
+    float2 ml0[PB], ml1[PB];
+    float a[PB][KS][4];
+#pragma unroll
+    for (int u = 0; u < PB; ++u) {
+      const bool in = j + u < nc;
+      const float* w0 = wb + (j + u) * ps + n0 * DP;
+      const float* w1 = w0 + DP;
+      ml0[u] = in && h0 ? __ldcg(reinterpret_cast<const float2*>(w0 + D_)) : make_float2(kNegInf, 0.f);
+      ml1[u] = in && h1 ? __ldcg(reinterpret_cast<const float2*>(w1 + D_)) : make_float2(kNegInf, 0.f);
+#pragma unroll
+      for (int i = 0; i < KS; ++i) {
+        const int d = 16 * i + tq;
+        a[u][i][0] = in && h0 ? __ldcg(w0 + d) : 0.f;
+        a[u][i][2] = in && h0 ? __ldcg(w0 + d + 8) : 0.f;
+        a[u][i][1] = in && h1 ? __ldcg(w1 + d) : 0.f;
+        a[u][i][3] = in && h1 ? __ldcg(w1 + d + 8) : 0.f;
+      }
+    }
+    float nm0 = M0, nm1 = M1;
+#pragma unroll
+    for (int u = 0; u < PB; ++u) {
+      nm0 = fmaxf(nm0, ml0[u].x);
+      nm1 = fmaxf(nm1, ml1[u].x);
+    }
+    const float b0 = nm0 == kNegInf ? 0.f : nm0, b1 = nm1 == kNegInf ? 0.f : nm1;
+    const float s0 = ex2(M0 - b0), s1 = ex2(M1 - b1);  // 2^(-inf) = 0: a state that saw no key
+    l0 *= s0;
+    l1 *= s1;
+#pragma unroll
+    for (int i = 0; i < KS; ++i) {
+      o[i][0] *= s0; o[i][2] *= s0;
+      o[i][1] *= s1; o[i][3] *= s1;
+    }
+#pragma unroll
+    for (int u = 0; u < PB; ++u) {
+      const float w0 = ml0[u].x == kNegInf ? 0.f : ex2(ml0[u].x - b0);
+      const float w1 = ml1[u].x == kNegInf ? 0.f : ex2(ml1[u].x - b1);
+      l0 += ml0[u].y * w0;
+      l1 += ml1[u].y * w1;
+#pragma unroll
+      for (int i = 0; i < KS; ++i) {
+        o[i][0] += a[u][i][0] * w0; o[i][2] += a[u][i][2] * w0;
+        o[i][1] += a[u][i][1] * w1; o[i][3] += a[u][i][3] * w1;
+      }
+    }
+    M0 = nm0;
+    M1 = nm1;
+  }
+  mma_store_output<T, D_>(p, c, o, l0, l1);
 }
 
 // Output rows when the item has one part, else the part record (merged at

@@ -136,8 +136,8 @@ __global__ void __launch_bounds__(kPackThreads) pack_kernel(const PackParams p) 
     }
     p.bt[(long long)slot * p.max_blocks + lb] = phys;
   }
-  __shared__ int multi_sh;
-  if (tid == 0) multi_sh = 0;
+  __shared__ int multi_sh, cross_sh;
+  if (tid == 0) multi_sh = cross_sh = 0;
   // 2. query offsets: scan of q_len.
   for (int s = tid; s < p.n_seqs; s += kPackThreads) cu[s] = p.seqs[4 * s + 2];
   __syncthreads();
@@ -174,8 +174,10 @@ __global__ void __launch_bounds__(kPackThreads) pack_kernel(const PackParams p) 
     const int us = unit_size(p, s);
     int shared = 0, nc = 0;
     shared_of(p, s, kv_len, shared, nc);
-    it.w = nc + parts_of(kv_len - shared, us);  // number of parts; scanned below
+    const int own = parts_of(kv_len - shared, us);
+    it.w = nc + own;  // number of parts; scanned below
     if (it.w > 1) multi_sh = 1;
+    if (own > 1) cross_sh = 1;
     reinterpret_cast<int4*>(p.items)[t] = it;
   }
   __syncthreads();
@@ -233,7 +235,9 @@ __global__ void __launch_bounds__(kPackThreads) pack_kernel(const PackParams p) 
         if (u < p.max_units) {
           int4* rec = reinterpret_cast<int4*>(p.units) + 2 * u;
           rec[0] = make_int4(t, it.x, it.y, nc + j);
-          rec[1] = make_int4(shared + j * us, min(shared + (j + 1) * us, it.z), it.w, nc + n);
+          // n_parts is negative for an item whose only unit this is, beside cascade
+          // parts: that unit merges them itself
+          rec[1] = make_int4(shared + j * us, min(shared + (j + 1) * us, it.z), it.w, (n == 1 && nc > 0) ? -(nc + n) : nc + n);
         }
       }
     }
@@ -242,7 +246,9 @@ __global__ void __launch_bounds__(kPackThreads) pack_kernel(const PackParams p) 
     if (n_units > p.max_units) atomicOr(p.status, NF_STATUS_UNIT_OVERFLOW);
     p.counts[0] = T;
     p.counts[1] = min(n_list, p.max_units);
-    p.counts[2] = multi_sh;  // some item has more than one part: the attention launch merges
+    // bit 0: some item has more than one part; bit 1: some item has more than
+    // one unit (its parts come from several workers of the attention launch)
+    p.counts[2] = multi_sh | (cross_sh << 1);
     p.counts[3] = min(n_units, p.max_units);  // partial slots of all items, cascade parts included
   }
 }

@@ -335,6 +335,8 @@ class PagedKVCache:
     CASCADE_WAVES = 2
     # the tensor-core path: one (task, KV head) item per SM aimed for, each at least this many keys long
     CASCADE_TC_MIN_KEYS = 256
+    # own keys (in units of the step's split) up to which a cascade sequence's own keys are one decode unit
+    CASCADE_OWN_UNIT_MAX = 4
 
     def cascade_supported(self, q_heads: int | None) -> bool:
         """True when nf_cascade_attention serves this cache with q_heads query heads."""
@@ -352,7 +354,7 @@ class PagedKVCache:
             _lib.check(_lib.load().nf_cascade_limits(_lib.dtype_code(self.dtype), group * self.n_heads, self.n_heads,
                                                      self.head_dim, self.block_size, ctypes.byref(rows),
                                                      ctypes.byref(keys)), "nf_cascade_limits")
-            memo[group] = (rows.value, keys.value, rows.value > self.CASCADE_ROWS)
+            memo[group] = (rows.value, keys.value, keys.value > self.CASCADE_MAX_KEYS)
         return memo[group]
 
     def _cascade_groups(self, slots, q_lens, q_starts, ctx, dec, group: int, epochs=None):
@@ -513,6 +515,12 @@ class PagedKVCache:
         seq_split = np.zeros(S, dtype=np.int32)  # 0: the prefill kernel serves the sequence
         if dec.any():
             seq_split[dec] = (seq_unit_sizes(seq_keys[dec], split, self.decode_workers) if fine_tail else split)
+            # a decode sequence with cascade parts whose own keys fit in one unit of modest size gets that one
+            # unit: the decode kernel then merges the cascade parts in the unit's epilogue, and a step of such
+            # sequences needs no end-of-launch merge (enough of them keep the SMs busy)
+            one = dec & (shared > 0) & (q_lens == 1) & (seq_keys <= self.CASCADE_OWN_UNIT_MAX * split)
+            if one.sum() * 2 >= self.decode_workers:
+                seq_split[one] = (seq_keys[one] + 15) // 16 * 16
         item_split = np.repeat(seq_split.astype(np.int64), q_lens)
         n_units = int(((kv_dec + item_split[item_split > 0] - 1) // item_split[item_split > 0]).sum())
         n_casc = int(nparts.sum())  # partial slots of the cascade parts (q_len 1: one item per sequence)

@@ -210,6 +210,36 @@ def test_cascade_matches_plain_decode_and_many_groups():
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("n_per,suffix,cross", [(40, (1, 60), False), (60, (1, 700), True)])
+def test_cascade_single_own_unit_vs_oracle(n_per, suffix, cross):
+    """Enough decode sequences on shared prefixes that each one whose own keys fit in one unit gets one: the
+    decode kernel merges its cascade parts in that unit's epilogue (unit records with a negated part count).
+    Without longer sequences no item has several units and the launch skips its end-of-launch merge; with
+    some (cross) the merge runs too and also covers the single-unit items.  Oracle per sequence."""
+    cache, g = _shared_prefix_cache(32, 8, 64, [256, 512], n_per, suffix, torch.bfloat16, seed=11 + int(cross))
+    B = cache.batch_size
+    before = [cache.length(s) for s in range(B)]
+    plan = cache.plan(list(range(B)), [1] * B, list(range(B)), q_heads=32)
+    assert plan.n_casc_tasks > 0
+    units = plan.units.view(-1, 8)[:plan.decode_units].cpu().numpy()
+    single = units[:, 7] < 0
+    assert single.sum() >= 40
+    flags = int(plan.counts[2].item())
+    assert bool(flags & 2) == cross and flags & 1
+    q = torch.randn(B, 32 * 64, generator=g).to(torch.bfloat16).to(DEV)
+    k = torch.randn(B, 8 * 64, generator=g).to(torch.bfloat16).to(DEV)
+    cache.append_step(0, k, k, plan)
+    out = torch.zeros_like(q)
+    cache.attention_step(0, q, plan, out)
+    cache.check_status()
+    kp, vp = cache.k[0].cpu(), cache.v[0].cpu()
+    for b in range(B):
+        ref = attend_paged_fp32(q[b].view(1, 32, 64).cpu(), kp, vp, cache.block_tables[b].physical_blocks(),
+                                before[b] + 1, 4)
+        torch.testing.assert_close(out[b].view(32, 64).float().cpu(), ref[0], **TOL)
+
+
+@pytest.mark.gpu
 def test_cascade_bad_task_flagged():
     """A task naming more queries than there are records is flagged on the status word and writes nothing."""
     from nifre_b200 import _lib
