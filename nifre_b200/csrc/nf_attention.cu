@@ -115,7 +115,7 @@ __device__ __forceinline__ void loader_enter(const AttnParams& p, Loader& L, uns
   c.t0 = L.nb.x;
   c.t1 = L.nb.y;
   c.unit_base = L.nb.z;
-  c.nparts = abs(L.nb.w);  // negative: the item's only unit beside cascade parts (merged at the end here)
+  c.nparts = rec_parts(L.nb.w);
   L.t = c.t0;
   L.lb = c.t0 / p.bs;
   L.off = c.t0 - L.lb * p.bs;

@@ -352,16 +352,20 @@ __device__ void tma_consumer(const AttnParams& p, unsigned char* base, int box_b
       c.t0 = r.t0;
       c.t1 = r.t1;
       c.unit_base = r.unit_base;
-      c.nparts = abs(r.nsplits);
+      c.nparts = rec_parts(r.nsplits);
       c.kvh = r.hg * p.HG + warp;
       c.part = r.part;
+      const int units = rec_units(r.nsplits);
       if (c.nparts == 1) {
         mma_store_output<T, D_>(p, c, o, l0, l1);
       } else {
-        // the part record also when this unit merges the item's cascade parts
-        // itself (nsplits < 0): a launch that merges at its end reads it
+        // the part record (merged at the end of the launch), also for the
+        // item's only unit beside its cascade parts, which merges those now:
+        // a launch that also has items of several units merges every item
+        // with several parts at its end (stalling a consumer warp to merge
+        // many parts here would hold up its CTA's stream)
         mma_store_part<T, D_>(p, c, o, m0, m1, l0, l1);
-        if (r.nsplits < 0) mma_merge_cascade<T, D_>(p, c, o, m0, m1, l0, l1);
+        if (units == 1) mma_merge_parts<T, D_>(p, c, o, m0, m1, l0, l1);
       }
     }
   }
@@ -393,7 +397,7 @@ __global__ void __launch_bounds__(kTmaMaxThreads, 1) paged_attention_tma_kernel(
   } else if ((threadIdx.x & 31) == 0) {
     cta_done = tma_producer<T, D_>(p, &tk, &tv, base, total, box_bytes, q_bytes);
   }
-  finish_launch<T, 8>(p, &cta_done, total, 2);
+  finish_launch<T, 8>(p, &cta_done, total, 2);  // items of one unit merge in its epilogue
 }
 
 // ---------------------------------------------------------------- host side

@@ -322,21 +322,22 @@ __device__ __forceinline__ void mma_store_part(const AttnParams& p, const Work& 
   }
 }
 
-// The output rows of an item whose only unit this is, beside nc = nparts - 1
-// cascade parts (slots unit_base .. unit_base + nc - 1, written by the
-// cascade launch before this one): the parts are merged into this unit's
-// running state (o, m, l; l summed over the lanes) in registers -- PB parts'
-// loads in flight at a time, rescaled as the maximum grows -- and the rows
-// written, with no wait for any other worker.
+// The output rows of an item whose only unit this is, beside its cascade
+// parts: every other part of the item (slots unit_base .. unit_base +
+// nparts - 1 but this unit's own, c.part), written by the cascade launch
+// before this one, is merged into this unit's running state (o, m, l; l
+// summed over the lanes) in registers -- PB parts' loads in flight at a
+// time, rescaled as the maximum grows -- and the rows are written, with no
+// wait for any other worker.
 template <typename T, int D_>
-__device__ __forceinline__ void mma_merge_cascade(const AttnParams& p, const Work& c, float (&o)[D_ / 16][4],
-                                                  float m0, float m1, float l0, float l1) {
+__device__ __forceinline__ void mma_merge_parts(const AttnParams& p, const Work& c, float (&o)[D_ / 16][4],
+                                                float m0, float m1, float l0, float l1) {
   constexpr int KS = D_ / 16;
   constexpr int PB = D_ == 64 ? 4 : 2;
   const int lane = threadIdx.x & 31;
   const int n0 = 2 * (lane & 3), tq = lane >> 2;
   const bool h0 = n0 < p.G, h1 = n0 + 1 < p.G;
-  const int DP = D_ + 4, nc = c.nparts - 1;
+  const int DP = D_ + 4, nc = c.nparts - 1;  // the other parts
   const float* wb = p.ws + ((long long)c.unit_base * p.Hq + c.kvh * p.G) * DP;
   const long long ps = (long long)p.Hq * DP;  // between consecutive parts
   float M0 = m0, M1 = m1;
@@ -346,7 +347,8 @@ __device__ __forceinline__ void mma_merge_cascade(const AttnParams& p, const Wor
 #pragma unroll
     for (int u = 0; u < PB; ++u) {
       const bool in = j + u < nc;
-      const float* w0 = wb + (j + u) * ps + n0 * DP;
+      const int part = j + u < c.part ? j + u : j + u + 1;  // skipping this unit's own
+      const float* w0 = wb + part * ps + n0 * DP;
       const float* w1 = w0 + DP;
       ml0[u] = in && h0 ? __ldcg(reinterpret_cast<const float2*>(w0 + D_)) : make_float2(kNegInf, 0.f);
       ml1[u] = in && h1 ? __ldcg(reinterpret_cast<const float2*>(w1 + D_)) : make_float2(kNegInf, 0.f);

@@ -92,6 +92,13 @@ __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepc
 // the caller then leaves its loops, so no kernel can spin forever.
 constexpr long long kWaitLimitCycles = 4000000000LL;
 
+// Split-K unit records (nf_pack_step) carry an item's part count in the low
+// 16 bits of their last field and its unit count in the high bits; more
+// parts than this per item are flagged (NF_STATUS_UNIT_OVERFLOW).
+constexpr int kMaxParts = (1 << 15) - 1;
+__device__ __forceinline__ int rec_parts(int w) { return w & 0xffff; }
+__device__ __forceinline__ int rec_units(int w) { return w >> 16; }
+
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* status,
                                           long long limit = kWaitLimitCycles) {
   if (mbar_try_wait(bar, parity)) return true;

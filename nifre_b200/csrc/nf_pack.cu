@@ -136,8 +136,8 @@ __global__ void __launch_bounds__(kPackThreads) pack_kernel(const PackParams p) 
     }
     p.bt[(long long)slot * p.max_blocks + lb] = phys;
   }
-  __shared__ int multi_sh, cross_sh;
-  if (tid == 0) multi_sh = cross_sh = 0;
+  __shared__ int multi_sh, cross_sh, max_parts_sh;
+  if (tid == 0) multi_sh = cross_sh = max_parts_sh = 0;
   // 2. query offsets: scan of q_len.
   for (int s = tid; s < p.n_seqs; s += kPackThreads) cu[s] = p.seqs[4 * s + 2];
   __syncthreads();
@@ -178,6 +178,7 @@ __global__ void __launch_bounds__(kPackThreads) pack_kernel(const PackParams p) 
     it.w = nc + own;  // number of parts; scanned below
     if (it.w > 1) multi_sh = 1;
     if (own > 1) cross_sh = 1;
+    if (it.w > kMaxParts) atomicMax(&max_parts_sh, it.w);
     reinterpret_cast<int4*>(p.items)[t] = it;
   }
   __syncthreads();
@@ -235,15 +236,17 @@ __global__ void __launch_bounds__(kPackThreads) pack_kernel(const PackParams p) 
         if (u < p.max_units) {
           int4* rec = reinterpret_cast<int4*>(p.units) + 2 * u;
           rec[0] = make_int4(t, it.x, it.y, nc + j);
-          // n_parts is negative for an item whose only unit this is, beside cascade
-          // parts: that unit merges them itself
-          rec[1] = make_int4(shared + j * us, min(shared + (j + 1) * us, it.z), it.w, (n == 1 && nc > 0) ? -(nc + n) : nc + n);
+          // low 16 bits: the item's parts; high: its units (the parts that are
+          // not cascade parts), so that the last unit to finish can merge
+          rec[1] = make_int4(shared + j * us, min(shared + (j + 1) * us, it.z), it.w,
+                             (min(n, kMaxParts) << 16) | min(nc + n, kMaxParts));
         }
       }
     }
   }
   if (tid == 0) {
     if (n_units > p.max_units) atomicOr(p.status, NF_STATUS_UNIT_OVERFLOW);
+    if (max_parts_sh > kMaxParts) atomicOr(p.status, NF_STATUS_UNIT_OVERFLOW);
     p.counts[0] = T;
     p.counts[1] = min(n_list, p.max_units);
     // bit 0: some item has more than one part; bit 1: some item has more than

@@ -213,16 +213,16 @@ def test_cascade_matches_plain_decode_and_many_groups():
 @pytest.mark.parametrize("n_per,suffix,cross", [(40, (1, 60), False), (60, (1, 700), True)])
 def test_cascade_single_own_unit_vs_oracle(n_per, suffix, cross):
     """Enough decode sequences on shared prefixes that each one whose own keys fit in one unit gets one: the
-    decode kernel merges its cascade parts in that unit's epilogue (unit records with a negated part count).
-    Without longer sequences no item has several units and the launch skips its end-of-launch merge; with
-    some (cross) the merge runs too and also covers the single-unit items.  Oracle per sequence."""
+    decode kernel merges its cascade parts in that unit's epilogue (unit records: parts in the low 16 bits of
+    the last field, units in the high bits).  With longer sequences too (cross), their items have several
+    units, and the last of them to finish merges every part.  Oracle per sequence."""
     cache, g = _shared_prefix_cache(32, 8, 64, [256, 512], n_per, suffix, torch.bfloat16, seed=11 + int(cross))
     B = cache.batch_size
     before = [cache.length(s) for s in range(B)]
     plan = cache.plan(list(range(B)), [1] * B, list(range(B)), q_heads=32)
     assert plan.n_casc_tasks > 0
     units = plan.units.view(-1, 8)[:plan.decode_units].cpu().numpy()
-    single = units[:, 7] < 0
+    single = ((units[:, 7] >> 16) == 1) & ((units[:, 7] & 0xFFFF) > 1)
     assert single.sum() >= 40
     flags = int(plan.counts[2].item())
     assert bool(flags & 2) == cross and flags & 1

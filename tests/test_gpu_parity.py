@@ -145,7 +145,8 @@ def test_decode_vs_oracle(dtype, D, Hq, Hkv, split):
 
 
 def test_pack_unit_list():
-    """Every key range of every item appears once with its part index; the units of
+    """Every key range of every item appears once with its part index; the last field holds the item's
+    part count (low 16 bits) and unit count (high bits; the same here: no cascade parts); the units of
     sequences at the step's split come first, then the short-unit tail, each in item order."""
     import numpy as np
     rng = np.random.default_rng(3)
@@ -166,7 +167,7 @@ def test_pack_unit_list():
     assert (items[:, 3] == np.concatenate([[0], np.cumsum(nsp)[:-1]])).all()  # unit_base
     seen = set()
     for t, slot, q_row, part, k0, k1, ub, n in units.tolist():
-        assert (slot, q_row, ub, n) == (t, t, items[t, 3], nsp[t])
+        assert (slot, q_row, ub, n & 0xFFFF, n >> 16) == (t, t, items[t, 3], nsp[t], nsp[t])
         assert k0 == part * us[t] and k1 == min(k0 + us[t], kv[t])
         seen.add((t, part))
     assert seen == {(t, j) for t in range(B) for j in range(nsp[t])}
