@@ -381,6 +381,10 @@ __global__ void __launch_bounds__(kTmaMaxThreads, 1) paged_attention_tma_kernel(
   const int warp = threadIdx.x >> 5;
   const int box_bytes = p.HG * 16 * D_ * 2;
   const int q_bytes = p.HG * p.G * D_ * 2;
+  if (threadIdx.x == 32 * p.HG) {  // the producer
+    tma_prefetch_map(&tk);
+    tma_prefetch_map(&tv);
+  }
   if (threadIdx.x == 0) {
     for (int s = 0; s < p.stages; ++s) {
       mbar_init(smem_u32(base) + 8 * s, 1);

@@ -835,9 +835,15 @@ __global__ void __launch_bounds__(PfCfg<D_>::THREADS, PfCfg<D_>::MINB)
   const int warp = threadIdx.x >> 5;
   // cascade: the decode launch that follows may start as this grid's CTAs leave
   if (CASC) pdl_launch_dependents();
-  // cascade: the first item of this CTA is item blockIdx.x; its task record is fetched during the setup
-  if (CASC && threadIdx.x == 32 && (int)blockIdx.x < p.n_tiles * p.Hkv)
-    asm volatile("prefetch.global.L1 [%0];" ::"l"(p.tasks + 8 * (blockIdx.x / p.Hkv)));
+  // the tensor maps' descriptors, and (cascade: the first item of this CTA is
+  // item blockIdx.x) its task record, are fetched during the setup
+  if (threadIdx.x == 32) {
+    tma_prefetch_map(&tk);
+    tma_prefetch_map(&tv);
+    tma_prefetch_map(&tq);
+    if (CASC && (int)blockIdx.x < p.n_tiles * p.Hkv)
+      asm volatile("prefetch.global.L1 [%0];" ::"l"(p.tasks + 8 * (blockIdx.x / p.Hkv)));
+  }
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::KST; ++s) {
       mbar_init(bar.k_full(s), 1);

@@ -71,6 +71,10 @@ __global__ void __launch_bounds__(192, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int m0 = blockIdx.x * kQkvBM, n0 = blockIdx.y * kQkvBN;
   const int nk = (p.K + 63) >> 6;
+  if (threadIdx.x == 32) {
+    tma_prefetch_map(&tx);
+    tma_prefetch_map(&tw);
+  }
   if (threadIdx.x == 0) {
     for (int s = 0; s < kQkvStages; ++s) {
       mbar_init(full(s), 1);

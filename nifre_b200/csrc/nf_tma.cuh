@@ -24,6 +24,13 @@ __device__ __forceinline__ uint64_t l2_evict_last() {
   return pol;
 }
 
+// Starts the fetch of a tensor map (a __grid_constant__ kernel parameter)
+// into the tensor-copy unit's descriptor cache, so that the first copy
+// through it does not wait for the descriptor.
+__device__ __forceinline__ void tma_prefetch_map(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int c0, int c1, uint32_t bar,
                                             uint64_t pol) {
   asm volatile(
