@@ -3,11 +3,15 @@
 // When sequences of a step start with the same physical blocks (prompt
 // prefixes imported from the prefix index, jyotilakra92/nifre
 // src/inference/prefix_cache.py:33-81 and paged_kv_cache.py:87-105), the
-// split-K decode kernel would stream those blocks once per sequence.  Here a
-// CTA takes the queries of up to 128 / G of those sequences for one KV head
-// (G query heads each: up to 128 query rows) and one range of the shared
-// keys (at most 256), stages its K and V in shared memory once, and
-// computes for every row the partial softmax state over that range: the
+// split-K decode kernel would stream those blocks once per sequence.  With
+// 1, 2, 4 or 8 query heads per KV head (G) the tasks run on the tensor cores,
+// in the cascade mode of the prefill kernel (nf_prefill.cu,
+// cascade_tensor_core); this file holds the entry point, the task limits
+// and, for other group sizes, an mma.sync kernel: a CTA takes the queries of
+// up to 128 / G of those sequences for one KV head (G query heads each: up
+// to 128 query rows) and one range of the shared keys (at most 256), stages
+// its K and V in shared memory once, and computes for every row the partial
+// softmax state over that range: the
 // unnormalised sum of 2^(s - m) v, its maximum m and its weight l, with s
 // the score times scale * log2(e) -- the same partial record the decode
 // kernel writes for a key range of an item, in the item's partial slot
