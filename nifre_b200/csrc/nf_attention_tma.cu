@@ -356,8 +356,13 @@ __device__ void tma_consumer(const AttnParams& p, unsigned char* base, int box_b
       c.kvh = r.hg * p.HG + warp;
       c.part = r.part;
       const int units = rec_units(r.nsplits);
+      // output staging of this warp (a gathered output: 16-byte stores to the peers)
+      const uint32_t stage = p.stage_out ? hdr + p.stage_out + warp * p.G * D_ * 2 : 0u;
       if (c.nparts == 1) {
-        mma_store_output<T, D_>(p, c, o, l0, l1);
+        if (stage)
+          mma_store_output_staged<T, D_>(p, c, o, l0, l1, stage);
+        else
+          mma_store_output<T, D_>(p, c, o, l0, l1);
       } else {
         // the part record (merged at the end of the launch), also for the
         // item's only unit beside its cascade parts, which merges those now:
@@ -365,14 +370,17 @@ __device__ void tma_consumer(const AttnParams& p, unsigned char* base, int box_b
         // with several parts at its end (stalling a consumer warp to merge
         // many parts here would hold up its CTA's stream)
         mma_store_part<T, D_>(p, c, o, m0, m1, l0, l1);
-        if (units == 1) mma_merge_parts<T, D_>(p, c, o, m0, m1, l0, l1);
+        if (units == 1) mma_merge_parts<T, D_>(p, c, o, m0, m1, l0, l1, stage);
       }
     }
   }
 }
 
-template <typename T, int D_>
-__global__ void __launch_bounds__(kTmaMaxThreads, 1) paged_attention_tma_kernel(const AttnParams p,
+// ONE_HEAD: the build for CTAs of one KV head (a pool sharded down to one
+// KV head per GPU): 64 threads and registers capped so that the eight CTAs
+// per SM the launch sizes its shared memory for are resident at once.
+template <typename T, int D_, bool ONE_HEAD = false>
+__global__ void __launch_bounds__(ONE_HEAD ? 64 : kTmaMaxThreads, ONE_HEAD ? 8 : 1) paged_attention_tma_kernel(const AttnParams p,
                                                                   const __grid_constant__ CUtensorMap tk,
                                                                   const __grid_constant__ CUtensorMap tv) {
   extern __shared__ unsigned char smem_raw[];
@@ -565,9 +573,15 @@ int launch_attention_tma(AttnParams p, int dtype, long long want, cudaStream_t s
   const int HB = p.D * 2;
   const int box = hg * 16 * HB, qb = hg * p.G * HB;
   const int stage = ((2 * box + qb + 1023) / 1024) * 1024;
-  // per CTA: 1 KB reserved by the system, the header, 1 KB of alignment slack
-  // and the static shared memory of finish_launch
-  const int budget = 228 * 1024 / ctas - 1024 - kTmaHeader - 1024 - 256;
+  // a gathered output whose rows (here and on every peer) allow 16-byte
+  // stores: each consumer warp stages its G x D output block in shared
+  // memory and stores it in 16-byte pieces
+  bool al16 = p.n_peers > 0 && (reinterpret_cast<uintptr_t>(p.out) & 15) == 0 && (p.out_stride * 2) % 16 == 0;
+  for (int r = 0; r < p.n_peers; ++r) al16 = al16 && (reinterpret_cast<uintptr_t>(p.peer_out[r]) & 15) == 0;
+  const int stage_out = al16 ? (hg * p.G * p.D * 2 + 127) / 128 * 128 : 0;
+  // per CTA: 1 KB reserved by the system, the header, 1 KB of alignment slack,
+  // the static shared memory of finish_launch and the output staging
+  const int budget = 228 * 1024 / ctas - 1024 - kTmaHeader - 1024 - 256 - stage_out;
   int stages = budget / stage;
   if (stages > kTmaMaxStages) stages = kTmaMaxStages;
   if (stages < 2) return NF_EUNSUPPORTED;
@@ -583,11 +597,17 @@ int launch_attention_tma(AttnParams p, int dtype, long long want, cudaStream_t s
   p.stage_bytes = stage;
   p.swz = permuted ? 1 : 0;  // reused as "one box covers all heads of the group"
   p.W = hg;
-  const int smem = kTmaHeader + stages * stage + 1024;  // + alignment slack
+  p.stage_out = stage_out ? kTmaHeader + stages * stage : 0;
+  const int smem = kTmaHeader + stages * stage + stage_out + 1024;  // + alignment slack
   auto kern = (dtype == NF_BF16) ? (p.D == 64 ? paged_attention_tma_kernel<__nv_bfloat16, 64>
                                               : paged_attention_tma_kernel<__nv_bfloat16, 128>)
                                  : (p.D == 64 ? paged_attention_tma_kernel<__half, 64>
                                               : paged_attention_tma_kernel<__half, 128>);
+  if (hg == 1)
+    kern = (dtype == NF_BF16) ? (p.D == 64 ? paged_attention_tma_kernel<__nv_bfloat16, 64, true>
+                                           : paged_attention_tma_kernel<__nv_bfloat16, 128, true>)
+                              : (p.D == 64 ? paged_attention_tma_kernel<__half, 64, true>
+                                           : paged_attention_tma_kernel<__half, 128, true>);
   int per_sm = 1;
   const int threads = (hg + 1) * 32;
   cudaError_t e = prepare_launch(reinterpret_cast<const void*>(kern), smem, threads, &per_sm);

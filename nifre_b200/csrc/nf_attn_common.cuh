@@ -32,6 +32,7 @@ struct AttnParams {
   int W, stages, head_bytes, stage_bytes, swz, tile, bs16, q_smem;
   int HG, n_hg;  // tensor-map path: KV heads per CTA and head groups
   int vec_out;         // 1: out rows and strides allow 8-byte (16-bit types) / 16-byte (float) stores
+  int stage_out;       // tensor-map path: byte offset of the consumer warps' output staging (0: none)
   int pdl;             // 1: may be launched with programmatic stream serialization
   int own_parts_only;  // 1: the workspace holds only this launch's parts (no cascade parts to merge)
   // Gathered output over several GPUs: every output row is also stored at
@@ -288,6 +289,46 @@ __device__ __forceinline__ void mma_store_output(const AttnParams& p, const Work
   }
 }
 
+// Normalised output rows (the item has one part) staged in shared memory:
+// the warp's G x D block of the output row (contiguous: the KV head's query
+// heads) is written to its staging area, then copied out in 16-byte stores,
+// one per lane and destination -- over NVLink to a gathered output's peers
+// a 16-byte store carries eight times what a 2-byte one does.
+template <typename T, int D_>
+__device__ __forceinline__ void mma_store_output_staged(const AttnParams& p, const Work& c, float (&o)[D_ / 16][4],
+                                                        float l0, float l1, uint32_t stage) {
+  constexpr int KS = D_ / 16;
+  const int lane = threadIdx.x & 31;
+  const int n0 = 2 * (lane & 3), tq = lane >> 2;
+  const bool h0 = n0 < p.G, h1 = n0 + 1 < p.G;
+  const float i0 = l0 > 0.f ? 1.f / l0 : 0.f, i1 = l1 > 0.f ? 1.f / l1 : 0.f;
+  auto st16 = [](uint32_t a, T v) {
+    asm volatile("st.shared.b16 [%0], %1;" ::"r"(a), "h"(*reinterpret_cast<unsigned short*>(&v)) : "memory");
+  };
+#pragma unroll
+  for (int i = 0; i < KS; ++i) {
+    const int d = 16 * i + tq;
+    if (h0) {
+      st16(stage + (n0 * D_ + d) * 2, Elem<T>::from_f(o[i][0] * i0));
+      st16(stage + (n0 * D_ + d + 8) * 2, Elem<T>::from_f(o[i][2] * i0));
+    }
+    if (h1) {
+      st16(stage + ((n0 + 1) * D_ + d) * 2, Elem<T>::from_f(o[i][1] * i1));
+      st16(stage + ((n0 + 1) * D_ + d + 8) * 2, Elem<T>::from_f(o[i][3] * i1));
+    }
+  }
+  __syncwarp();
+  const long long ob = (long long)c.q_row * p.out_stride + (long long)(c.kvh * p.G) * D_;
+  for (int ch = lane; ch < p.G * D_ / 8; ch += 32) {
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "r"(stage + ch * 16));
+    *reinterpret_cast<uint4*>(reinterpret_cast<T*>(p.out) + ob + ch * 8) = v;
+    for (int r = 0; r < p.n_peers; ++r) *reinterpret_cast<uint4*>(reinterpret_cast<T*>(p.peer_out[r]) + ob + ch * 8) = v;
+  }
+  __syncwarp();  // the staging area is free for the warp's next output
+}
+
 // The unit's split-K part record (acc, m, l) in the workspace.
 template <typename T, int D_>
 __device__ __forceinline__ void mma_store_part(const AttnParams& p, const Work& c, float (&o)[D_ / 16][4], float m0,
@@ -331,7 +372,7 @@ __device__ __forceinline__ void mma_store_part(const AttnParams& p, const Work& 
 // wait for any other worker.
 template <typename T, int D_>
 __device__ __forceinline__ void mma_merge_parts(const AttnParams& p, const Work& c, float (&o)[D_ / 16][4],
-                                                float m0, float m1, float l0, float l1) {
+                                                float m0, float m1, float l0, float l1, uint32_t stage) {
   constexpr int KS = D_ / 16;
   constexpr int PB = D_ == 64 ? 4 : 2;
   const int lane = threadIdx.x & 31;
@@ -391,7 +432,10 @@ __device__ __forceinline__ void mma_merge_parts(const AttnParams& p, const Work&
     M0 = nm0;
     M1 = nm1;
   }
-  mma_store_output<T, D_>(p, c, o, l0, l1);
+  if (stage)
+    mma_store_output_staged<T, D_>(p, c, o, l0, l1, stage);
+  else
+    mma_store_output<T, D_>(p, c, o, l0, l1);
 }
 
 // Output rows when the item has one part, else the part record (merged at
