@@ -764,8 +764,12 @@ def _run_decode_timed(steps, warmup, e2e_steps, cache, B, ctx, world, rank, loca
     def out_of(layer):
         return ex.out(ex.slot_for(layer, cache.steps_closed, L), B) if ex is not None else out_loc[layer]
 
-    def step(rec_layer=-1):
-        p = cache.plan(slots, ones, rows, q_heads=hq)
+    def step(rec_layer=-1, fixed=False):
+        p = cache.plan(slots, ones, rows, q_heads=hq, fixed_layout=fixed)
+        layers(p, rec_layer)
+        return p
+
+    def layers(p, rec_layer=-1):
         for layer in range(L):
             o = out_of(layer)
             cache.append_step(layer, k_all[layer], v_all[layer], p)
@@ -778,10 +782,39 @@ def _run_decode_timed(steps, warmup, e2e_steps, cache, B, ctx, world, rank, loca
             if record:
                 e1.record(stream)
                 att_events.append((e0, e1, p))
+
+    # The timed steps: each plans on the host (one pack launch) and replays a CUDA graph of its layers' append
+    # and attention launches, captured once per plan layout and exchange-buffer parity (the exchange's epoch
+    # lives on the device, so replays exchange afresh).  A new layout runs eagerly once, then is captured.
+    graphs, seen = {}, set()
+
+    def graph_step():
+        p = cache.plan(slots, ones, rows, q_heads=hq, fixed_layout=True)
+        key = (p.layout_key, cache.steps_closed % 2)
+        g = graphs.get(key)
+        if g is not None:
+            g.replay()
+            cache._close(p)  # the host bookkeeping the captured layers did when they ran
+            return p
+        if key not in seen:
+            seen.add(key)
+            layers(p)
+            return p
+        g = torch.cuda.CUDAGraph()
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(stream)
+        with torch.cuda.stream(side):
+            with torch.cuda.graph(g, stream=side):
+                layers(p)
+        stream.wait_stream(side)
+        graphs[key] = g
+        g.replay()  # the capture launched nothing: run this step
         return p
 
+    for _ in range(4):  # the graphs of both parities captured before the warm-up steps
+        graph_step()
     for _ in range(warmup):
-        step()
+        graph_step()
     torch.cuda.synchronize()
     cache.check_status()
     if world > 1:
@@ -793,15 +826,19 @@ def _run_decode_timed(steps, warmup, e2e_steps, cache, B, ctx, world, rank, loca
     e_start = torch.cuda.Event(enable_timing=True)
     e_end = torch.cuda.Event(enable_timing=True)
     e_start.record(stream)
-    # the attention kernel is timed by events around one layer per step, a
-    # different layer each step: events between every pair of kernels would
-    # add a drain per event to the step
     for s in range(steps):
-        step(rec_layer=s % L)
+        graph_step()
     e_end.record(stream)
     torch.cuda.synchronize()
     clk = clocks.stop()
     ms = _max_over_ranks(e_start.elapsed_time(e_end), dev, dist)
+    cache.check_status()
+    # the attention launches issued from the host one layer at a time, as the step's eager form runs them:
+    # events around one layer per step, a different layer each step (events between every pair of kernels
+    # would add a drain per event to the step)
+    for s in range(min(L, 8)):
+        step(rec_layer=s % L, fixed=True)
+    torch.cuda.synchronize()
     cache.check_status()
     # attention kernel: algorithmic bytes per launch / event duration
     att_ms = [a.elapsed_time(b) for a, b, _ in att_events]
@@ -829,38 +866,35 @@ def _run_decode_timed(steps, warmup, e2e_steps, cache, B, ctx, world, rank, loca
     ok = _max_over_ranks(0.0 if ok else 1.0, dev, dist) == 0.0
 
     # the attention launches without the host: the last step's per-layer calls (cascade + decode when the plan
-    # has cascade tasks) captured in a CUDA graph and replayed, so that host enqueue gaps are not counted and the
-    # launches overlap as programmatic serialization lets them (one GPU: the exchange's epochs are per call)
-    graph_replay = None
-    if world == 1:
-        kv = int(p.kv_lens.sum())
-        nblk = int(((p.kv_lens + bs - 1) // bs).sum())
-        g_bytes = (kv - shared) * hkv * D * 2 * 2 + 2 * B * hq * D * 2 + 4 * nblk + 16 * B
-        side = torch.cuda.Stream(dev)
-        side.wait_stream(stream)
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.stream(side):
-            with torch.cuda.graph(graph, stream=side):
-                for layer in range(L):
-                    cache.attention_step(layer, q_all[layer], p, out_of(layer))
-        torch.cuda.synchronize()
-        for _ in range(3):
-            graph.replay()
-        n_rep = 20
-        ga, gb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        ga.record(stream)
-        for _ in range(n_rep):
-            graph.replay()
-        gb.record(stream)
-        torch.cuda.synchronize()
-        cache.check_status()
-        g_us = ga.elapsed_time(gb) * 1e3 / (n_rep * L)
-        graph_replay = {"us_per_layer": g_us, "achieved": g_bytes / (g_us * 1e-6) / 1e9,
-                        "frac": g_bytes / (g_us * 1e-6) / 1e9 / peak, "replays": n_rep,
-                        "launches_per_layer": 2 if p.n_casc_tasks else 1,
-                        "what": "attention of one layer (cascade + decode launches when the step has cascade "
-                                "tasks) from CUDA-graph replays of one step's layers, back to back"}
-        del graph
+    # has cascade tasks; with the exchange over N GPUs) captured in a CUDA graph and replayed back to back, so
+    # that host enqueue gaps are not counted and the launches overlap as programmatic serialization lets them
+    kv = int(p.kv_lens.sum())
+    nblk = int(((p.kv_lens + bs - 1) // bs).sum())
+    g_bytes = (kv - shared) * hkv * D * 2 * 2 + 2 * B * hq * D * 2 + 4 * nblk + 16 * B
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(stream)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(side):
+        with torch.cuda.graph(graph, stream=side):
+            for layer in range(L):
+                cache.attention_step(layer, q_all[layer], p, out_of(layer), exchange=ex)
+    torch.cuda.synchronize()
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    n_rep = 20
+    ga, gb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ga.record(stream)
+    for _ in range(n_rep):
+        graph.replay()
+    gb.record(stream)
+    torch.cuda.synchronize()
+    cache.check_status()
+    g_us = _max_over_ranks(ga.elapsed_time(gb), dev, dist) * 1e3 / (n_rep * L)
+    g_achieved = g_bytes / (g_us * 1e-6) / 1e9
+    del graph
 
     # e2e through the public drop-in API with host buffers: every step uploads its q/k/v from pinned host
     # memory (one copy per tensor, all layers) and downloads its attention outputs (one copy); uploads and
@@ -964,27 +998,35 @@ def _run_decode_timed(steps, warmup, e2e_steps, cache, B, ctx, world, rank, loca
                            f"U[{CFG['suffix_lo']},{CFG['suffix_hi']}] suffix + step"),
                    "parallelism": (f"kv-head shard x{world}; outputs gathered by the attention kernels' peer "
                                    "stores over NVLink (no collective library call)" if world > 1 else "single GPU"),
-                   "method": ("all layers run every step" if L == L_model else
-                              f"{L} resident layer(s) run per step; tok/s and ms_per_step scaled to "
-                              f"{L_model} layers at the measured per-layer time"),
+                   "method": (("all layers run every step" if L == L_model else
+                               f"{L} resident layer(s) run per step; tok/s and ms_per_step scaled to "
+                               f"{L_model} layers at the measured per-layer time") +
+                              "; a step = plan + pack on the host, then one replay of a CUDA graph of the layers' "
+                              "append and attention launches (captured per plan layout)"),
                    "l2": ("inputs larger than L2 (each layer reads a distinct pool of >=300 MB)"
                           if not shared else
                           "each layer reads a distinct pool; shared prefix blocks (16 MB per layer) are read by "
                           "every sequence that imported them: the roofline counts them once (unique bytes)")},
-        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                     "frac": achieved / peak,
+        "roofline": {"bound": "hbm", "achieved": g_achieved, "peak": peak, "unit": "GB/s",
+                     "frac": g_achieved / peak,
                      "traffic": (CFG["traffic_ratio"] * sum(att_bytes) / len(att_bytes)
                                  if CFG.get("traffic_ratio") else None),
                      "traffic_source": CFG.get("traffic_source"),
                      "kernel": "nf_paged_attention",
                      "kernel_path": {0: "per-warp cp.async", 1: "tensor map, one copy per block",
                                      2: "tensor map, one copy per head"}.get(att_path, str(att_path)),
-                     "peak_source": peak_kind, "avg_launch_us": att_avg_ms * 1e3,
-                     "bytes_per_launch": sum(att_bytes) / len(att_bytes),
+                     "peak_source": peak_kind, "avg_launch_us": g_us,
+                     "bytes_per_launch": g_bytes,
+                     "timing": ("CUDA events around 20 replays of a CUDA graph of one step's per-layer attention "
+                                "calls (cascade + decode launches when the step has cascade tasks; the exchange "
+                                "over N GPUs), divided by the layers; max over ranks"),
+                     "launches_per_layer": 2 if p.n_casc_tasks else 1,
+                     "eager": {"avg_launch_us": att_avg_ms * 1e3, "achieved": achieved, "frac": achieved / peak,
+                               "what": "events around one layer's attention call per step, the calls issued from "
+                                       "the host one layer at a time"},
                      **({"bytes": "unique (shared prefix blocks once)",
-                         "achieved_logical": (sum(logical_bytes) / len(logical_bytes)) / (att_avg_ms * 1e-3) / 1e9}
-                        if shared else {}),
-                     **({"graph_replay": graph_replay} if graph_replay else {})},
+                         "achieved_logical": (sum(logical_bytes) / len(logical_bytes)) / (g_us * 1e-6) / 1e9}
+                        if shared else {})},
         "parity": {"rows_checked": len(pick) * world, "max_abs_err": worst, "within_tol": ok,
                    "against": "float32 torch attention over the pool, last layer of one extra step",
                    "tol": "rtol 2e-2, atol 2e-2"},

@@ -73,7 +73,12 @@ extern "C" {
  * process by nf_ipc_open.  flags[r] is rank r's flag array (int32[n_ranks],
  * zero when allocated, mapped likewise; flags[rank] is this GPU's own).
  * epoch numbers the exchanges: the same value on every rank for the same
- * call, increasing from 1.  n_ranks == 1 means no exchange.
+ * call, increasing from 1.  With epoch_counter (device int32, zero when
+ * allocated, one per rank) the epoch is kept on the device instead: the
+ * launch that signals adds one to *epoch_counter and uses the result, so
+ * that a captured CUDA graph replays with a fresh epoch each time (every
+ * rank must make the same exchanges in the same order; epoch is then
+ * ignored).  n_ranks == 1 means no exchange.
  */
 #define NF_MAX_RANKS 8
 typedef struct NfGather {
@@ -83,6 +88,7 @@ typedef struct NfGather {
   int32_t pad;
   void* peer_out[NF_MAX_RANKS - 1];
   int32_t* flags[NF_MAX_RANKS];
+  int32_t* epoch_counter;
 } NfGather;
 
 /* Message of the last failed call on this thread ("" if none). */

@@ -45,7 +45,7 @@ class NfGather(ctypes.Structure):
     """struct NfGather of include/nifre_b200.h: a gathered output over the ranks of one node."""
     _fields_ = [("n_ranks", ctypes.c_int32), ("rank", ctypes.c_int32), ("epoch", ctypes.c_int32),
                 ("pad", ctypes.c_int32), ("peer_out", ctypes.c_void_p * (MAX_RANKS - 1)),
-                ("flags", ctypes.c_void_p * MAX_RANKS)]
+                ("flags", ctypes.c_void_p * MAX_RANKS), ("epoch_counter", ctypes.c_void_p)]
 
 
 _G = ctypes.POINTER(NfGather)

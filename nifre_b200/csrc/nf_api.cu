@@ -106,6 +106,6 @@ size_t dtype_size(int dtype) {
 
 extern "C" const char* nf_last_error(void) { return nf::g_err; }
 
-extern "C" int nf_abi_version(void) { return 13; }
+extern "C" int nf_abi_version(void) { return 14; }
 
 extern "C" int nf_last_attention_path(void) { return nf::g_attention_path; }

@@ -852,6 +852,7 @@ static int prepare_attention(void* out, int64_t out_row_stride, const void* q, i
   p.n_ranks = 1;
   p.rank = 0;
   p.epoch = 0;
+  p.epoch_counter = nullptr;
   return ok();
 }
 
@@ -876,6 +877,7 @@ static int apply_gather(AttnParams& p, const NfGather* g, size_t es) {
   p.n_ranks = g->n_ranks;
   p.rank = g->rank;
   p.epoch = g->epoch;
+  p.epoch_counter = g->epoch_counter;
   return ok();
 }
 

@@ -41,6 +41,7 @@ struct AttnParams {
   // rank's entry of every rank's flag array to epoch and waits until all
   // ranks have set theirs (n_ranks > 1).
   int n_peers, n_ranks, rank, epoch;
+  int* epoch_counter;  // device epoch (NfGather.epoch_counter), or null: epoch
   char* peer_out[kMaxRanks - 1];
   int* rank_flags[kMaxRanks];
 };
@@ -257,7 +258,8 @@ __device__ void finish_launch(const AttnParams& p, int* cta_done, int total, int
     // the last CTA out: this rank's rows are in every rank's buffer; signal
     // the peers and wait for theirs, so that the launch ends with the whole
     // gathered output in place on this GPU
-    if (p.n_ranks > 1) exchange_signal_wait(p.rank_flags, p.n_ranks, p.rank, p.epoch, p.status);
+    if (p.n_ranks > 1)
+      exchange_signal_wait(p.rank_flags, p.n_ranks, p.rank, p.epoch, p.status, kWaitLimitCycles, p.epoch_counter);
   }
 }
 

@@ -151,7 +151,12 @@ __device__ __forceinline__ int ld_acquire_sys(const int* addr) {
 // (epochs compared modulo 2^32).  Returns false (NF_STATUS_WAIT_TIMEOUT set)
 // if the limit runs out.
 __device__ __forceinline__ bool exchange_signal_wait(int* const* rank_flags, int n_ranks, int rank, int epoch,
-                                                     int* status, long long limit = kWaitLimitCycles) {
+                                                     int* status, long long limit = kWaitLimitCycles,
+                                                     int* epoch_counter = nullptr) {
+  if (epoch_counter) {  // the epoch kept on the device: this call's is the next one
+    epoch = *reinterpret_cast<volatile int*>(epoch_counter) + 1;
+    *reinterpret_cast<volatile int*>(epoch_counter) = epoch;
+  }
   __threadfence_system();
   for (int r = 0; r < n_ranks; ++r) st_release_sys(rank_flags[r] + rank, epoch);
   const int* mine = rank_flags[rank];

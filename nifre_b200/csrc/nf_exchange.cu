@@ -20,7 +20,7 @@ namespace nf {
 __global__ void exchange_barrier_kernel(NfGather g, int* status) {
   int* flags[kMaxRanks];
   for (int r = 0; r < g.n_ranks; ++r) flags[r] = g.flags[r];
-  exchange_signal_wait(flags, g.n_ranks, g.rank, g.epoch, status);
+  exchange_signal_wait(flags, g.n_ranks, g.rank, g.epoch, status, kWaitLimitCycles, g.epoch_counter);
 }
 
 static PFN_cuMemGetAddressRange_v3020 range_fn() {

@@ -94,6 +94,9 @@ class PeerExchange:
         self.width = shard.world * shard.q_heads * shard.head_dim
         self.buffers = torch.zeros(slots, max_rows, self.width, dtype=dtype, device=device)
         self.flags = torch.zeros(shard.world, dtype=torch.int32, device=device)
+        # the exchange number, kept on the device: the signalling launch advances it, so that a CUDA graph of
+        # exchanging launches replays with fresh epochs
+        self.epoch_dev = torch.zeros(1, dtype=torch.int32, device=device)
         torch.cuda.synchronize(device)
         lib = _lib.load()
         mine = []
@@ -153,6 +156,7 @@ class PeerExchange:
             g.peer_out[i] = base + off
         for r, f in enumerate(self.peer_flags):
             g.flags[r] = f
+        g.epoch_counter = self.epoch_dev.data_ptr()
         return g
 
     def close(self) -> None:

@@ -13,6 +13,8 @@ replacing attention + an NCCL all-gather.  Checked on every rank:
   (rtol = atol = 2e-2, the bf16 tolerance) -- the reference's attention
   (attention.py:106-152) with grouped-query heads expanded;
 * both ranks end with bit-identical gathered buffers;
+* a CUDA graph of an exchanging decode launch, replayed three times, gives
+  the eager launch's gathered rows (the exchange's epoch lives on the device);
 * a rank that skips an exchange makes the other rank's kernel give up after
   its time limit with NF_STATUS_WAIT_TIMEOUT set (a wait nothing satisfies;
   nothing faults), after which the context still answers.
@@ -127,6 +129,30 @@ def _worker(rank, port, out_q):
         res["mixed"] = run_step([14] + dec[:6], [96] + [1] * 6, 1)       # one chunk on the prefill kernel
         res["prefill_only"] = run_step([15], [64], 2)                     # stand-alone barrier
         res["second_decode"] = run_step(dec, [1] * 14, 0)                 # buffer 0 again, next epoch
+        # a CUDA graph of an exchanging launch: the epoch lives on the device, so replays exchange afresh
+        T = 14
+        qg = torch.randn(T, Hq * D, generator=g).to(torch.bfloat16)
+        kg = torch.randn(T, Hkv * D, generator=g).to(torch.bfloat16)
+        pg = cache.plan(dec, [1] * T, list(range(T)), q_heads=hq)
+        cache.append_step(0, kg[:, kvc].contiguous().to(dev), kg[:, kvc].contiguous().to(dev), pg)
+        qd = qg[:, qc].contiguous().to(dev)
+        og = ex.out(2, T)
+        cache.attention_step(0, qd, pg, og, exchange=ex)
+        torch.cuda.synchronize(dev)
+        ref = ex.gathered(2, T).clone()
+        ex.gathered(2, T).zero_()
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(side):
+            with torch.cuda.graph(graph, stream=side):
+                cache.attention_step(0, qd, pg, og, exchange=ex)
+        for _ in range(3):
+            graph.replay()
+        torch.cuda.synchronize(dev)
+        cache.check_status()
+        res["graph_equal"] = bool(torch.equal(ex.gathered(2, T), ref))
+        del graph
         # failure detection: rank 1 leaves one exchange out; rank 0's kernel gives up after its limit
         if rank == 1:
             run_step(dec, [1] * 14, 1, skip=True)
@@ -172,5 +198,6 @@ def test_sharded_gathered_output_two_gpus():
     r0 = next(r for r in results if r["rank"] == 0)
     for key in ("decode", "mixed", "prefill_only", "second_decode"):
         assert r0[key] is not None and r0[key] < 2e-2
+    assert all(r["graph_equal"] for r in results)
     assert r0["timeout_status"] & _lib.NF_STATUS_WAIT_TIMEOUT
     assert r0["context_ok"]

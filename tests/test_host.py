@@ -199,7 +199,7 @@ def test_library_exports_every_declared_symbol():
     for s in syms:
         assert hasattr(lib, s), s
     assert set(_lib.EXPORTS) <= set(syms)
-    assert _lib.load().nf_abi_version() == 13
+    assert _lib.load().nf_abi_version() == 14
 
 
 def test_workspace_sizing_and_argument_errors():
