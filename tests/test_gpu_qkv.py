@@ -81,6 +81,49 @@ def test_qkv_append_vs_float32(dtype, hq, hkv, d, kdim, bias):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("rows", [1, 33, 64, 100, 128])
+@pytest.mark.parametrize("hq,hkv,d,kdim,bias", [(32, 8, 64, 2048, False), (2, 1, 64, 256, True),
+                                                 (8, 2, 128, 1024, True)])
+def test_qkv_few_rows_vs_float32(dtype, rows, hq, hkv, d, kdim, bias):
+    """Decode-sized steps (1 to 128 rows, one 128-row tile with its zero-filled tail): q and the pool rows
+    against the float32 product, one rounding (rtol = atol = 1e-2), and bit-equal to the same rows written
+    into a dense buffer (the scatter); (2, 1, 64): output tiles on both sides of the k/v boundary."""
+    from nifre_b200 import _lib
+    lens = [1] * rows  # decode rows
+    cache, plan, g = _step(hq, hkv, d, lens, dtype, seed=rows + kdim)
+    T, nq, nkv = rows, hq * d, hkv * d
+    x = torch.randn(T, kdim, generator=g).to(dtype).to(DEV)
+    w = (torch.randn(nq + 2 * nkv, kdim, generator=g) / kdim ** 0.5).to(dtype).to(DEV)
+    b = torch.randn(nq + 2 * nkv, generator=g).to(dtype).to(DEV) if bias else None
+    q = torch.empty(T, nq, dtype=dtype, device=DEV)
+    cache.project_append_step(0, x, w, b, plan, q)
+    torch.cuda.synchronize()
+    cache.check_status()
+    ref = x.float() @ w.float().T + (b.float() if bias else 0.0)
+    tol = dict(rtol=1e-2, atol=1e-2)
+    torch.testing.assert_close(q.float(), ref[:, :nq], **tol)
+    slots = plan.slot_mapping.long()
+    kp, vp = cache.k[0].view(-1, nkv), cache.v[0].view(-1, nkv)
+    torch.testing.assert_close(kp[slots].float(), ref[:, nq:nq + nkv], **tol)
+    torch.testing.assert_close(vp[slots].float(), ref[:, nq + nkv:], **tol)
+    dense_k = torch.zeros(T, nkv, dtype=dtype, device=DEV)
+    dense_v = torch.zeros_like(dense_k)
+    q2 = torch.empty_like(q)
+    ident = torch.arange(T, dtype=torch.int32, device=DEV)
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    lib = _lib.load()
+    _lib.check(lib.nf_qkv_append(x.data_ptr(), kdim, T, w.data_ptr(), b.data_ptr() if bias else None, kdim, nq, nkv,
+                                 q2.data_ptr(), nq, dense_k.data_ptr(), dense_v.data_ptr(), T, _lib.dtype_code(dtype),
+                                 ident.data_ptr(), None, 0, None, status.data_ptr(),
+                                 _lib.stream_handle(torch.device(DEV))), "nf_qkv_append")
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    assert torch.equal(q2, q)
+    assert torch.equal(kp[slots], dense_k) and torch.equal(vp[slots], dense_v)
+
+
+@pytest.mark.gpu
 def test_qkv_append_advances_pos_on_last_layer_only():
     lens = [3, 1, 20]
     cache, plan, g = _step(8, 2, 64, lens, torch.bfloat16, seed=1, layers=2)
