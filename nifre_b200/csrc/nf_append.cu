@@ -62,6 +62,7 @@ template <> struct Vec8<__nv_bfloat16> : Vec8Half<__nv_bfloat16> {};
 template <typename T>
 __global__ void append_copy_kernel(const AppendParams p) {
   pdl_launch_dependents();
+  pdl_wait();  // the rows may come from the launch before this one
   constexpr int V = 16 / sizeof(T);
   const int chunks = p.row_elems / V;
   const long long total = (long long)p.n_tokens * 2 * chunks;
@@ -91,6 +92,7 @@ __global__ void append_copy_kernel(const AppendParams p) {
 template <typename Ts, typename Td>
 __global__ void append_convert_kernel(const AppendParams p) {
   pdl_launch_dependents();
+  pdl_wait();  // the rows may come from the launch before this one
   const int chunks = p.row_elems / 8;
   const long long total = (long long)p.n_tokens * 2 * chunks;
   for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < total;
@@ -120,6 +122,7 @@ __global__ void append_convert_kernel(const AppendParams p) {
 template <typename Ts, typename Td>
 __global__ void append_scalar_kernel(const AppendParams p) {
   pdl_launch_dependents();
+  pdl_wait();  // the rows may come from the launch before this one
   const long long total = (long long)p.n_tokens * 2 * p.row_elems;
   for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < total;
        idx += (long long)gridDim.x * blockDim.x) {
@@ -142,6 +145,29 @@ __global__ void append_scalar_kernel(const AppendParams p) {
   }
 }
 
+// The append kernels launch with programmatic stream serialization: a grid
+// may start while the launch before it on the stream (the previous layer's
+// attention) finishes, and waits for it (griddepcontrol.wait) before reading
+// anything, so its launch and start-up overlap that kernel's tail.  Plain
+// stream order where the launch refuses the attribute.
+template <typename K>
+static void launch_pdl(K kern, long long blocks, int threads, cudaStream_t st, const AppendParams& p) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)blocks);
+  cfg.blockDim = dim3(threads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, kern, p) != cudaSuccess) {
+    (void)cudaGetLastError();
+    kern<<<(unsigned)blocks, threads, 0, st>>>(p);
+  }
+}
+
 template <typename Ts, typename Td>
 static void launch_append(const AppendParams& p, bool vec_ok, cudaStream_t st) {
   const int threads = 256;
@@ -151,15 +177,15 @@ static void launch_append(const AppendParams& p, bool vec_ok, cudaStream_t st) {
   if (blocks > cap) blocks = cap;
   if (blocks < 1) blocks = 1;
   if (!vec_ok) {
-    append_scalar_kernel<Ts, Td><<<(int)blocks, threads, 0, st>>>(p);
+    launch_pdl(append_scalar_kernel<Ts, Td>, blocks, threads, st, p);
   } else if (sizeof(Ts) == sizeof(Td) && std::is_same<Ts, Td>::value) {
     const long long vwork = (long long)p.n_tokens * 2 * (p.row_elems * sizeof(Td) / 16);
     long long vb = (vwork + threads - 1) / threads;
     if (vb > cap) vb = cap;
     if (vb < 1) vb = 1;
-    append_copy_kernel<Td><<<(int)vb, threads, 0, st>>>(p);
+    launch_pdl(append_copy_kernel<Td>, vb, threads, st, p);
   } else {
-    append_convert_kernel<Ts, Td><<<(int)blocks, threads, 0, st>>>(p);
+    launch_pdl(append_convert_kernel<Ts, Td>, blocks, threads, st, p);
   }
 }
 

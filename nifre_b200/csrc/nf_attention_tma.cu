@@ -389,6 +389,9 @@ __global__ void __launch_bounds__(ONE_HEAD ? 64 : kTmaMaxThreads, ONE_HEAD ? 8 :
   const int warp = threadIdx.x >> 5;
   const int box_bytes = p.HG * 16 * D_ * 2;
   const int q_bytes = p.HG * p.G * D_ * 2;
+  // the launch after this one (the next layer's KV append) may start as this
+  // grid's CTAs leave; it waits for this grid before it reads or writes anything
+  pdl_launch_dependents();
   if (threadIdx.x == 32 * p.HG) {  // the producer
     tma_prefetch_map(&tk);
     tma_prefetch_map(&tv);
