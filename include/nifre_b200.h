@@ -166,7 +166,8 @@ int nf_selftest_umma(const void* A, const void* B, float* C, int32_t N, int32_t 
  * cascade parts in that unit's epilogue.
  * counts[4]: counts[0] = n_tokens, counts[1] = number of units in the list,
  * counts[2] = bit 0: some item has more than one part, bit 1: some item has
- * more than one unit (the attention launch then merges at its end),
+ * more than one unit (the attention launch then merges at its end), bits 2
+ * and up: the first item with units (the items before it have none),
  * counts[3] = number of partial slots (units + cascade parts).
  */
 int nf_pack_step(const int32_t* seqs, int32_t n_seqs,

@@ -189,6 +189,8 @@ template <typename T, int PB>
 __device__ void finish_launch(const AttnParams& p, int* cta_done, int total, int merge_bits) {
   __shared__ int go;
   const int c_items = __ldg(p.counts), c_multi = __ldg(p.counts + 2), c_units = __ldg(p.counts + 3);
+  // items before the first one with units (a step's prefill rows) have no parts: the tasks start after them
+  const int t_first = max(0, c_multi >> 2);
   const int groups = (p.G * (p.D >> 2) + 31) >> 5;
   const int stride = gridDim.x * (blockDim.x >> 5);
   const int task0 = (threadIdx.x >> 5) * gridDim.x + blockIdx.x;
@@ -196,7 +198,7 @@ __device__ void finish_launch(const AttnParams& p, int* cta_done, int total, int
   // records of a task's item t and the unit base of item t + 1 (within the buffers; checked against the counts
   // when used)
   auto records = [&](int task, int4& it, int& nx) {
-    const int t = task / groups / p.Hkv;
+    const int t = t_first + task / groups / p.Hkv;
     it = make_int4(0, 0, 0, -1);
     nx = 0;
     if (t < p.max_items) {
@@ -221,11 +223,11 @@ __device__ void finish_launch(const AttnParams& p, int* cta_done, int total, int
   if (go && merge) {
     const int n_items = min(c_items, p.max_items);
     const int n_units = min(c_units, p.max_units);  // partial slots, cascade parts included
-    const int tasks = n_items * p.Hkv * groups;
+    const int tasks = max(0, n_items - t_first) * p.Hkv * groups;
     // tasks dealt round-robin over the CTAs so that every SM takes a share
     for (int task = task0; task < tasks; task += stride) {
       const int pair = task / groups, grp = task - pair * groups;
-      const int t = pair / p.Hkv;
+      const int tl = pair / p.Hkv, t = t_first + tl;
       const int next = t + 1 < n_items ? nx : n_units;
       const int4 cur = it;
       if (task + stride < tasks) records(task + stride, it, nx);
@@ -240,7 +242,7 @@ __device__ void finish_launch(const AttnParams& p, int* cta_done, int total, int
       c.t0 = c.t1 = 0;
       c.unit_base = cur.w;
       c.nparts = nparts;
-      c.kvh = pair - t * p.Hkv;
+      c.kvh = pair - tl * p.Hkv;
       c.part = 0;
       merge_chunk<T, PB>(p, c, grp * 32);
     }

@@ -136,8 +136,11 @@ __global__ void __launch_bounds__(kPackThreads) pack_kernel(const PackParams p) 
     }
     p.bt[(long long)slot * p.max_blocks + lb] = phys;
   }
-  __shared__ int multi_sh, cross_sh, max_parts_sh;
-  if (tid == 0) multi_sh = cross_sh = max_parts_sh = 0;
+  __shared__ int multi_sh, cross_sh, max_parts_sh, first_sh;
+  if (tid == 0) {
+    multi_sh = cross_sh = max_parts_sh = 0;
+    first_sh = 1 << 29;
+  }
   // 2. query offsets: scan of q_len.
   for (int s = tid; s < p.n_seqs; s += kPackThreads) cu[s] = p.seqs[4 * s + 2];
   __syncthreads();
@@ -178,6 +181,7 @@ __global__ void __launch_bounds__(kPackThreads) pack_kernel(const PackParams p) 
     it.w = nc + own;  // number of parts; scanned below
     if (it.w > 1) multi_sh = 1;
     if (own > 1) cross_sh = 1;
+    if (us > 0) atomicMin(&first_sh, t);
     if (it.w > kMaxParts) atomicMax(&max_parts_sh, it.w);
     reinterpret_cast<int4*>(p.items)[t] = it;
   }
@@ -250,8 +254,10 @@ __global__ void __launch_bounds__(kPackThreads) pack_kernel(const PackParams p) 
     p.counts[0] = T;
     p.counts[1] = min(n_list, p.max_units);
     // bit 0: some item has more than one part; bit 1: some item has more than
-    // one unit (its parts come from several workers of the attention launch)
-    p.counts[2] = multi_sh | (cross_sh << 1);
+    // one unit (its parts come from several workers of the attention launch);
+    // from bit 2: the first item with units (the rows before it are the
+    // prefill kernel's), where the end-of-launch merge starts looking
+    p.counts[2] = multi_sh | (cross_sh << 1) | (min(first_sh, T) << 2);
     p.counts[3] = min(n_units, p.max_units);  // partial slots of all items, cascade parts included
   }
 }
