@@ -158,6 +158,7 @@ def _shared_prefix_cache(hq, hkv, D, prefixes, n_per, suffix, dtype, seed, tail_
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("D,hq,hkv", [(64, 32, 8), (128, 32, 8), (64, 8, 8), (64, 16, 2),  # tensor cores
+                                       (64, 4, 1), (128, 4, 1),  # one KV head (an 8-way shard): one-head decode
                                        (64, 24, 8), (128, 12, 2)])  # G = 3 and 6: the mma.sync kernel
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 def test_cascade_decode_vs_oracle(D, hq, hkv, dtype):
