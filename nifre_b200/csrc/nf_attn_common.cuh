@@ -247,11 +247,17 @@ __device__ void finish_launch(const AttnParams& p, int* cta_done, int total, int
       merge_chunk<T, PB>(p, c, grp * 32);
     }
   }
-  // a gathered output: every thread's stores, to this GPU and to its peers,
-  // are made visible system-wide before the CTA counts itself done
-  if (p.n_ranks > 1) __threadfence_system();
+  // a gathered output: the CTA's stores, to this GPU and to its peers, are
+  // ordered before the CTA counts itself done by the CTA barrier and a
+  // device-scope fence of the counting thread; the last CTA out observes
+  // every count and fences at system scope before it signals the peers
+  // (exchange_signal_wait), and as fences are cumulative that release covers
+  // the stores of every CTA of the grid.  One system-scope fence per launch:
+  // a fence in every CTA cost 7 us per two-GPU launch.
   __syncthreads();
+  if (threadIdx.x == 0 && p.n_ranks > 1) __threadfence();
   if (threadIdx.x == 0 && atomicAdd(p.queue + 3, 1) == (int)gridDim.x - 1) {
+    __threadfence();
     p.queue[0] = 0;
     p.queue[1] = 0;
     p.queue[2] = 0;
