@@ -144,6 +144,35 @@ def test_decode_vs_oracle(dtype, D, Hq, Hkv, split):
     cache.check_status()
 
 
+def test_pack_first_item_with_units_and_mixed_merge():
+    """counts[2] carries, from bit 2, the first item with split-K units: a mixed step's prefill rows (listed
+    first, served by the prefill kernel) have none, so the decode launch's end-of-launch merge starts after
+    them.  The step's decode rows (several parts each) still match the oracle."""
+    import numpy as np
+    from oracle.attention import attend_paged_fp32
+    ctx = [300, 0, 700, 900, 1500]
+    cache, g = _random_cache(32, 8, 64, 16, [c if c else 16 for c in ctx], torch.bfloat16, seed=21, room=64)
+    q_lens = [40, 24, 1, 1, 1]  # two prefill rows (>= 16 new tokens), then three decodes
+    B, T = len(q_lens), sum(q_lens)
+    before = [cache.length(s) for s in range(B)]
+    starts = np.cumsum([0] + q_lens[:-1]).tolist()
+    plan = cache.plan(list(range(B)), q_lens, starts, q_heads=32, split=128)
+    assert plan.n_tiles > 0
+    flags = int(plan.counts[2].item())
+    assert flags >> 2 == 64 and flags & 2  # items 0..63 are the prefill rows'; the decodes have several units
+    q = torch.randn(T, 32 * 64, generator=g).to(torch.bfloat16).to(DEV)
+    k = torch.randn(T, 8 * 64, generator=g).to(torch.bfloat16).to(DEV)
+    cache.append_step(0, k, k, plan)
+    out = torch.zeros_like(q)
+    cache.attention_step(0, q, plan, out)
+    cache.check_status()
+    kp, vp = cache.k[0].cpu(), cache.v[0].cpu()
+    for b in (2, 3, 4):
+        ref = attend_paged_fp32(q[starts[b]].view(1, 32, 64).cpu(), kp, vp, cache.block_tables[b].physical_blocks(),
+                                before[b] + 1, 4)
+        torch.testing.assert_close(out[starts[b]].view(32, 64).float().cpu(), ref[0], rtol=2e-2, atol=2e-2)
+
+
 def test_pack_unit_list():
     """Every key range of every item appears once with its part index; the last field holds the item's
     part count (low 16 bits) and unit count (high bits; the same here: no cascade parts); the units of
