@@ -161,9 +161,11 @@ int nf_selftest_umma(const void* A, const void* B, float* C, int32_t N, int32_t 
  * of cascade parts that nf_cascade_attention computes over them ({0, 0}:
  * none).  Such an item's parts 0..nc-1 are those cascade parts (partial
  * slots, no unit records); its units cover keys [shared, kv_len) as parts
- * nc, nc+1, ...; when one unit covers them all, that unit's record carries
- * the part count negated, and the tensor-map decode kernel merges the
- * cascade parts in that unit's epilogue.
+ * nc, nc+1, ...  A unit record's last field holds its item's part count
+ * (low 16 bits, at most 32767: more is flagged NF_STATUS_UNIT_OVERFLOW) and
+ * unit count (high bits); when one unit covers an item's own keys, the
+ * tensor-map decode kernel merges the item's cascade parts in that unit's
+ * epilogue.
  * counts[4]: counts[0] = n_tokens, counts[1] = number of units in the list,
  * counts[2] = bit 0: some item has more than one part, bit 1: some item has
  * more than one unit (the attention launch then merges at its end), bits 2
